@@ -1,0 +1,4 @@
+// Address-space switch for host compilation of the reference kernels.
+#undef threadgroup
+#define threadgroup
+#include_next "objectives.metal.h"

@@ -1,0 +1,175 @@
+"""ctypes bindings to the CPU checkers under oracle/ (test infrastructure).
+
+liboracle.so is the C restatement of the reference's training semantics;
+_ref/libxgbref.so holds the reference's own serial kernel functions compiled
+for the host. Tests use both only to check results; the product never loads
+either library.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ORACLE_DIR = os.path.join(ROOT, "oracle")
+
+SPLIT_DTYPE = np.dtype([
+    ("gain", "<f4"), ("threshold", "<f4"), ("applied_parent_weight", "<f4"), ("left_h", "<f4"),
+    ("applied_parent_hessian", "<f4"), ("right_h", "<f4"), ("feature", "<i4"),
+    ("default_left", "<u4"), ("left_weight", "<f4"), ("right_weight", "<f4"), ("total_g", "<f4"),
+    ("total_h", "<f4"), ("split_type", "<u4"), ("category_begin", "<u4"),
+    ("category_count", "<u4"), ("parent_weight", "<f4"), ("left_sum_g", "<i8"),
+    ("left_sum_h", "<i8"), ("right_sum_g", "<i8"), ("right_sum_h", "<i8")])
+assert SPLIT_DTYPE.itemsize == 96
+
+NODE_DTYPE = np.dtype([
+    ("left", "<i4"), ("right", "<i4"), ("feature", "<i4"), ("parent", "<i4"),
+    ("threshold", "<f4"), ("leaf", "<f4"), ("cover", "<f4"), ("gain", "<f4"),
+    ("default_left", "<u4"), ("split_bin", "<i4")])
+assert NODE_DTYPE.itemsize == 40
+
+MISSING = 0xFFFFFFFF
+
+_P = ctypes.c_void_p
+_U32 = ctypes.c_uint32
+_F = ctypes.c_float
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data_as(_P)
+
+
+def _load(path):
+    if not os.path.exists(path):
+        return None
+    return ctypes.CDLL(path)
+
+
+def build():
+    """Build the checkers in place (the reference harness only where the
+    reference checkout exists)."""
+    import subprocess
+    subprocess.run(["make", "-s", "-C", ORACLE_DIR], check=True)
+
+
+class _Lib:
+    def __init__(self, lib, prefix):
+        self.lib = lib
+        self.p = prefix
+
+    def fn(self, name, restype=None):
+        f = getattr(self.lib, self.p + name)
+        f.restype = restype
+        return f
+
+
+class Checker:
+    """Common interface over the oracle and the reference harness."""
+
+    def __init__(self, kind):
+        if kind == "oracle":
+            lib = _load(os.path.join(ORACLE_DIR, "liboracle.so"))
+            prefix = "orc_"
+        else:
+            lib = _load(os.path.join(ORACLE_DIR, "_ref", "libxgbref.so"))
+            prefix = "xgbref_"
+        if lib is None:
+            raise FileNotFoundError(kind)
+        self.kind = kind
+        self._l = _Lib(lib, prefix)
+
+    def sketch_cuts(self, X, max_bin, weights=None):
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        rows, cols = X.shape
+        stride = max(1, min(max_bin, rows))
+        cuts = np.zeros((cols, stride), np.float32)
+        counts = np.zeros(cols, np.uint32)
+        minima = np.zeros(cols, np.float32)
+        w = None if weights is None else np.ascontiguousarray(weights, dtype=np.float32)
+        got = self._l.fn("sketch_cuts", ctypes.c_int)(
+            _ptr(X), _U32(rows), _U32(cols), _ptr(w), _U32(max_bin), _ptr(cuts), _ptr(counts),
+            _ptr(minima))
+        assert got == stride
+        return cuts, counts, minima
+
+    def quantize(self, X, cuts, counts):
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        rows, cols = X.shape
+        out = np.zeros((rows, cols), np.uint32)
+        self._l.fn("quantize")(_ptr(X), _U32(rows), _U32(cols), _ptr(cuts), _U32(cuts.shape[1]),
+                               _ptr(counts), _ptr(out))
+        return out
+
+    def gradient_scales(self, pairs):
+        pairs = np.ascontiguousarray(pairs, dtype=np.float32)
+        rows, groups = pairs.shape[0], pairs.shape[1]
+        scales = np.zeros((groups, 2), np.float32)
+        self._l.fn("gradient_scales")(_ptr(pairs), _U32(rows), _U32(groups), _ptr(scales))
+        return scales
+
+    def quantize_gradients(self, pairs, scales):
+        pairs = np.ascontiguousarray(pairs, dtype=np.float32)
+        rows, groups = pairs.shape[0], pairs.shape[1]
+        q = np.zeros((rows, groups, 2), np.int64)
+        self._l.fn("quantize_gradients")(_ptr(pairs), _U32(rows), _U32(groups),
+                                         _ptr(np.ascontiguousarray(scales, np.float32)), _ptr(q))
+        return q
+
+    def evaluate_splits(self, hist, scale, cuts, counts, minima, params, use_parent_sums,
+                        node_sums):
+        nodes, cols, b1, _ = hist.shape
+        out = np.zeros(nodes * cols, SPLIT_DTYPE)
+        self._l.fn("evaluate_splits")(
+            _ptr(np.ascontiguousarray(hist, np.int64)), _U32(nodes), _U32(cols), _U32(b1 - 1),
+            _ptr(np.ascontiguousarray(scale, np.float32)), _ptr(cuts), _ptr(counts), _ptr(minima),
+            _F(params["reg_lambda"]), _F(params["reg_alpha"]), _F(params["min_child_weight"]),
+            _F(params["max_delta_step"]), _U32(use_parent_sums),
+            _ptr(np.ascontiguousarray(node_sums, np.int64)), _ptr(out))
+        return out.reshape(nodes, cols)
+
+    def select_splits(self, candidates, scale, params):
+        nodes, cols = candidates.shape
+        best = np.zeros(nodes, SPLIT_DTYPE)
+        self._l.fn("select_splits")(
+            _ptr(np.ascontiguousarray(candidates)), _U32(nodes), _U32(cols),
+            _ptr(np.ascontiguousarray(scale, np.float32)), _F(params["reg_lambda"]),
+            _F(params["reg_alpha"]), _F(params["max_delta_step"]), _ptr(best))
+        return best
+
+    def grow_tree(self, bins, q, scale, cuts, counts, minima, params):
+        rows, cols = bins.shape
+        cap = (2 << params["max_depth"]) - 1
+        nodes = np.zeros(cap, NODE_DTYPE)
+        leaf = np.zeros(rows, np.float32)
+        args = [_ptr(np.ascontiguousarray(bins, np.uint32)), _U32(rows), _U32(cols),
+                _ptr(np.ascontiguousarray(q, np.int64)), _ptr(np.ascontiguousarray(scale, np.float32)),
+                _ptr(cuts), _U32(cuts.shape[1]), _ptr(counts), _ptr(minima)]
+        if self.kind == "oracle":
+            tp = (ctypes.c_uint32 * 1)(params["max_depth"])
+            buf = np.array([params["max_depth"]], np.uint32).tobytes() + np.array(
+                [params["eta"], params["reg_lambda"], params["reg_alpha"],
+                 params["min_child_weight"], params["max_delta_step"], params["min_split_loss"]],
+                np.float32).tobytes()
+            tpb = ctypes.create_string_buffer(buf, len(buf))
+            del tp
+            n = self._l.fn("grow_tree", ctypes.c_int)(*args, tpb, _ptr(nodes), _U32(cap), _ptr(leaf))
+        else:
+            n = self._l.fn("grow_tree", ctypes.c_int)(
+                *args, _U32(params["max_depth"]), _F(params["eta"]), _F(params["reg_lambda"]),
+                _F(params["reg_alpha"]), _F(params["min_child_weight"]),
+                _F(params["max_delta_step"]), _F(params["min_split_loss"]), _ptr(nodes), _U32(cap),
+                _ptr(leaf))
+        assert n > 0, n
+        return nodes[:n], leaf
+
+
+def oracle():
+    return Checker("oracle")
+
+
+def reference():
+    return Checker("reference")
+
+
+def have_reference():
+    return os.path.exists(os.path.join(ORACLE_DIR, "_ref", "libxgbref.so"))
