@@ -1,0 +1,50 @@
+/*
+ * B200 extensions of the C ABI. They have upstream-style conventions (0 / -1
+ * and XGBGetLastError) and plain pointers and sizes.
+ */
+#ifndef XGB_B200_EXTENSIONS_H_
+#define XGB_B200_EXTENSIONS_H_
+
+#include "xgboost/c_api.h"
+
+/* Hex encoding of an NCCL unique id, to be shared with every rank before
+ * XGCommunicatorInit. Replaces the tracker of upstream's collective module
+ * (python-package/xgboost/collective.py in the reference). */
+XGB_DLL int XGBBNcclUniqueId(char const** out);
+/* Selects the CUDA device of the calling thread. */
+XGB_DLL int XGBBSetDevice(int device);
+/* Waits for all work on the current device. */
+XGB_DLL int XGBBSynchronize(void);
+/* Quantises a matrix now (QuantileDMatrix), with the cuts of `ref` when it is
+ * not NULL. Replaces XGQuantileDMatrixCreateFromCallback
+ * (include/xgboost/c_api.h:535) for in-memory data. */
+XGB_DLL int XGDMatrixQuantise(DMatrixHandle handle, int max_bin, DMatrixHandle ref);
+/* JSON {"hist_ms", "hist_launches", "rounds"}: CUDA-event time of the
+ * histogram kernels when the booster has cuda_profile=1. Replaces
+ * XGBoosterMetalProfile (include/metalgb/c_api.h:8-12). */
+XGB_DLL int XGBoosterGetCudaProfile(BoosterHandle handle, char const** out);
+
+/* Kernel-level entry points used by the parity tests (host buffers in, host
+ * buffers out). */
+/* Cuts (cuts[f * min(max_bin, rows) + i]), counts, minima and row-major bins
+ * (0xffffffff = missing) of X [rows][cols]: the reference's
+ * Matrix::quantize (src/data.cpp:1210-1306). */
+XGB_DLL int XGBBQuantizeHost(const float* X, bst_ulong rows, bst_ulong cols, uint32_t max_bin,
+                             float* cuts, uint32_t* counts, float* minima, uint32_t* bins);
+/* Gradient pairs [groups][rows][2] and power-of-two scales [groups][2]: the
+ * reference's gradients + gradient_partial_sums + gradient_scales
+ * (kernels/boost.metal:553-601, kernels/gradient_quantization.metal.h:1-67). */
+XGB_DLL int XGBBGradientsHost(int objective, const float* margins, const float* labels,
+                              const float* weights, bst_ulong rows, uint32_t groups,
+                              float scale_pos_weight, float* pairs, float* scales);
+/* `rounds` rounds of training; trees back to back as 48-byte node records
+ * {left, right, parent, feature, split_bin, default_left, threshold, leaf,
+ * cover, gain, base_weight, flags}, tree sizes, and the final training
+ * margins [rows][groups]. The reference's Learner::update loop
+ * (src/learner.cpp:632-985). */
+XGB_DLL int XGBBTrainHost(const float* X, bst_ulong rows, bst_ulong cols, const float* labels,
+                          const float* weights, char const* params_json, uint32_t rounds,
+                          void* nodes, bst_ulong node_capacity, uint32_t* tree_sizes,
+                          float* margins);
+
+#endif /* XGB_B200_EXTENSIONS_H_ */

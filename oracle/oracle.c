@@ -198,6 +198,9 @@ static void feature_cuts(const float* X, uint32_t rows, uint32_t cols, uint32_t 
     float w = unit ? 1.0f : weights[r];
     nonmissing += !isnan(v);
     if (isnan(v) || (f32_bits(w) & 0x7fffffffu) == 0) continue;
+    /* [ours] -0 reads as +0, so a summary never depends on which signed zero
+     * came first (the reference keeps the first one's sign). */
+    if (v == 0.0f) v = 0.0f;
     ++elements;
     if (!nruns || !(v == previous)) {
       runs[nruns].v = v;

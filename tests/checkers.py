@@ -173,3 +173,75 @@ def reference():
 
 def have_reference():
     return os.path.exists(os.path.join(ORACLE_DIR, "_ref", "libxgbref.so"))
+
+
+# --- whole-run training through the oracle -----------------------------------
+
+class _TreeParams(ctypes.Structure):
+    _fields_ = [("max_depth", ctypes.c_uint32), ("eta", ctypes.c_float),
+                ("reg_lambda", ctypes.c_float), ("reg_alpha", ctypes.c_float),
+                ("min_child_weight", ctypes.c_float), ("max_delta_step", ctypes.c_float),
+                ("min_split_loss", ctypes.c_float)]
+
+
+class _TrainParams(ctypes.Structure):
+    _fields_ = [("objective", ctypes.c_int), ("num_class", ctypes.c_uint32),
+                ("max_bin", ctypes.c_uint32), ("rounds", ctypes.c_uint32),
+                ("scale_pos_weight", ctypes.c_float), ("has_base_score", ctypes.c_int),
+                ("base_score", ctypes.c_float), ("tree", _TreeParams)]
+
+
+OBJECTIVES = {"reg:squarederror": 0, "binary:logistic": 1, "multi:softprob": 3}
+
+
+def train_params(params):
+    """Full parameter set with the upstream defaults (the Booster's own)."""
+    p = {"objective": "reg:squarederror", "max_depth": 6, "eta": 0.3, "reg_lambda": 1.0,
+         "reg_alpha": 0.0, "min_child_weight": 1.0, "max_delta_step": 0.0,
+         "min_split_loss": 0.0, "max_bin": 256, "scale_pos_weight": 1.0, "num_class": 0}
+    p.update(params)
+    return p
+
+
+def oracle_train(X, y, params, rounds, weights=None):
+    """Returns (list of per-tree NODE_DTYPE arrays, margins [rows, groups], base margins)."""
+    p = train_params(params)
+    X = np.ascontiguousarray(X, np.float32)
+    y = np.ascontiguousarray(y, np.float32)
+    rows, cols = X.shape
+    obj = OBJECTIVES[p["objective"]]
+    groups = int(p["num_class"]) if obj == 3 else 1
+    tp = _TrainParams(obj, int(p["num_class"]), int(p["max_bin"]), int(rounds),
+                      float(p["scale_pos_weight"]), int("base_score" in p),
+                      float(p.get("base_score", 0.0)),
+                      _TreeParams(int(p["max_depth"]), float(p["eta"]), float(p["reg_lambda"]),
+                                  float(p["reg_alpha"]), float(p["min_child_weight"]),
+                                  float(p["max_delta_step"]), float(p["min_split_loss"])))
+    cap = rounds * groups * ((2 << int(p["max_depth"])) - 1)
+    nodes = np.zeros(cap, NODE_DTYPE)
+    sizes = np.zeros(rounds * groups, np.uint32)
+    margins = np.zeros((rows, groups), np.float32)
+    base = np.zeros(groups, np.float32)
+    w = None if weights is None else np.ascontiguousarray(weights, np.float32)
+    lib = oracle()._l.lib
+    lib.orc_train.restype = ctypes.c_int64
+    n = lib.orc_train(_ptr(X), _U32(rows), _U32(cols), _ptr(y), _ptr(w), ctypes.byref(tp),
+                      _ptr(nodes), ctypes.c_uint64(cap), _ptr(sizes), _ptr(margins), _ptr(base))
+    assert n >= 0, n
+    trees, off = [], 0
+    for s in sizes:
+        trees.append(nodes[off:off + s])
+        off += int(s)
+    return trees, margins, base
+
+
+def oracle_gradients(objective, margins, labels, weights=None, scale_pos_weight=1.0):
+    margins = np.ascontiguousarray(margins, np.float32)
+    rows, groups = margins.shape
+    pairs = np.zeros((rows, groups, 2), np.float32)
+    lib = oracle()._l.lib
+    lib.orc_gradients(ctypes.c_int(OBJECTIVES[objective]), _ptr(margins),
+                      _ptr(np.ascontiguousarray(labels, np.float32)),
+                      _ptr(None if weights is None else np.ascontiguousarray(weights, np.float32)),
+                      _U32(rows), _U32(groups), _F(scale_pos_weight), _ptr(pairs))
+    return pairs

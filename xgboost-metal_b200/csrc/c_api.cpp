@@ -1,0 +1,620 @@
+// The drop-in C ABI: the upstream XGBoost entry points of the training and
+// prediction path (restated by signature in include/xgboost/c_api.h), plus the
+// B200 extensions of include/xgb_b200.h. Every entry returns 0 on success and
+// -1 on failure with a thread-local message for XGBGetLastError, and output
+// pointers stay valid until the next call on the same thread (the reference's
+// convention, src/c_api.cpp:16-40).
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "comm.h"
+#include "json.h"
+#include "learner.h"
+#include "sketch.h"
+#include "xgb_b200.h"
+#include "xgboost/c_api.h"
+
+namespace {
+using xgbb::Error;
+using xgbb::Json;
+using xgbb::require;
+
+thread_local std::string last_error;
+struct Results {
+  std::string str;
+  std::vector<float> floats;
+  std::vector<bst_ulong> shape;
+  std::vector<std::string> strings;
+  std::vector<const char*> ptrs;
+};
+thread_local Results results;
+void (*log_callback)(const char*) = nullptr;
+
+template <class F>
+int guarded(F&& f) noexcept {
+  try {
+    f();
+    return 0;
+  } catch (const std::exception& e) {
+    last_error = e.what();
+  } catch (...) {
+    last_error = "unknown error";
+  }
+  return -1;
+}
+
+using DMatrixPtr = std::shared_ptr<xgbb::DMatrix>;
+DMatrixPtr& dmat(DMatrixHandle h) {
+  require(h != nullptr, "DMatrix handle is null.");
+  return *static_cast<DMatrixPtr*>(h);
+}
+xgbb::Booster& booster(BoosterHandle h) {
+  require(h != nullptr, "Booster handle is null.");
+  return *static_cast<xgbb::Booster*>(h);
+}
+
+void ensure_device() {
+  int n = 0;
+  const cudaError_t e = cudaGetDeviceCount(&n);
+  require(e == cudaSuccess && n > 0, "No CUDA device is available; this library trains on CUDA GPUs only.");
+}
+
+// A NumPy __array_interface__ (or its JSON encoding): pointer, shape, dtype.
+struct ArrayView {
+  const char* ptr = nullptr;
+  std::vector<uint64_t> shape;
+  std::vector<int64_t> strides;  // bytes; empty = C contiguous
+  char kind = 'f';
+  int itemsize = 4;
+};
+
+ArrayView parse_array(const std::string& text) {
+  Json j = Json::parse(text);
+  if (j.kind == Json::Array) {
+    require(j.arr.size() == 1, "Only one array per interface is supported.");
+    j = j.arr[0];
+  }
+  ArrayView a;
+  const Json& data = j.at("data");
+  require(data.kind == Json::Array && !data.arr.empty(), "array interface 'data' must be [ptr, readonly]");
+  a.ptr = reinterpret_cast<const char*>(uintptr_t(data.arr[0].as_u64()));
+  for (auto& s : j.at("shape").arr) a.shape.push_back(s.as_u64());
+  const std::string type = j.at("typestr").str;
+  require(type.size() >= 3, "bad typestr");
+  require(type[0] != '>', "Big-endian arrays are not supported.");
+  a.kind = type[1];
+  a.itemsize = std::stoi(type.substr(2));
+  if (auto* st = j.find("strides"); st && st->kind == Json::Array)
+    for (auto& s : st->arr) a.strides.push_back(s.as_i64());
+  return a;
+}
+
+double read_element(const ArrayView& a, const char* p) {
+  switch (a.kind) {
+    case 'f':
+      if (a.itemsize == 4) { float v; std::memcpy(&v, p, 4); return v; }
+      if (a.itemsize == 8) { double v; std::memcpy(&v, p, 8); return v; }
+      if (a.itemsize == 2) {
+        uint16_t h; std::memcpy(&h, p, 2);
+        const uint32_t sign = uint32_t(h & 0x8000u) << 16, e = (h >> 10) & 31, m = h & 0x3ffu;
+        uint32_t out;
+        if (e == 31) out = sign | 0x7f800000u | (m << 13);
+        else if (e) out = sign | ((e + 112) << 23) | (m << 13);
+        else if (!m) out = sign;
+        else { int sh = __builtin_clz(m) - 21; out = sign | (uint32_t(113 - sh) << 23) | (((m << sh) & 0x3ffu) << 13); }
+        float v; std::memcpy(&v, &out, 4); return v;
+      }
+      break;
+    case 'i':
+      if (a.itemsize == 1) return *reinterpret_cast<const int8_t*>(p);
+      if (a.itemsize == 2) { int16_t v; std::memcpy(&v, p, 2); return v; }
+      if (a.itemsize == 4) { int32_t v; std::memcpy(&v, p, 4); return v; }
+      if (a.itemsize == 8) { int64_t v; std::memcpy(&v, p, 8); return double(v); }
+      break;
+    case 'u':
+      if (a.itemsize == 1) return *reinterpret_cast<const uint8_t*>(p);
+      if (a.itemsize == 2) { uint16_t v; std::memcpy(&v, p, 2); return v; }
+      if (a.itemsize == 4) { uint32_t v; std::memcpy(&v, p, 4); return v; }
+      if (a.itemsize == 8) { uint64_t v; std::memcpy(&v, p, 8); return double(v); }
+      break;
+    case 'b':
+      return *reinterpret_cast<const uint8_t*>(p) ? 1.0 : 0.0;
+  }
+  throw Error("Unsupported array dtype.");
+}
+
+// Copies a 1-D or 2-D array to float32, row-major.
+std::vector<float> to_floats(const ArrayView& a, uint64_t& rows, uint64_t& cols) {
+  rows = a.shape.empty() ? 0 : a.shape[0];
+  cols = a.shape.size() > 1 ? a.shape[1] : 1;
+  std::vector<float> out(size_t(rows) * cols);
+  const int64_t s0 = a.strides.size() > 0 ? a.strides[0] : int64_t(cols) * a.itemsize;
+  const int64_t s1 = a.strides.size() > 1 ? a.strides[1] : a.itemsize;
+  if (a.kind == 'f' && a.itemsize == 4 && s1 == 4 && s0 == int64_t(cols) * 4) {
+    if (!out.empty()) std::memcpy(out.data(), a.ptr, out.size() * 4);
+    return out;
+  }
+  for (uint64_t r = 0; r < rows; ++r)
+    for (uint64_t c = 0; c < cols; ++c)
+      out[size_t(r) * cols + c] = float(read_element(a, a.ptr + int64_t(r) * s0 + int64_t(c) * s1));
+  return out;
+}
+
+// Missing sentinel -> NaN; any other infinity is an error (src/data.cpp:433).
+void normalise(std::vector<float>& v, float missing, bool& has_missing) {
+  has_missing = false;
+  const bool nan_missing = std::isnan(missing);
+  for (float& x : v) {
+    if (nan_missing ? std::isnan(x) : (x == missing)) {
+      x = NAN;
+      has_missing = true;
+    } else if (std::isnan(x)) {
+      has_missing = true;
+    } else {
+      require(!std::isinf(x), "Input data contains infinity or a value too large for float32.");
+    }
+  }
+}
+
+float config_missing(const char* config) {
+  if (!config || !*config) return NAN;
+  Json c = Json::parse(config);
+  if (auto* m = c.find("missing"); m && m->kind == Json::Number) return float(m->num);
+  return NAN;
+}
+
+DMatrixHandle new_dmatrix(std::vector<float>&& values, uint64_t rows, uint64_t cols, float missing) {
+  require(rows < (1ull << 32) && cols < (1ull << 31), "Matrix exceeds the 32-bit row index range.");
+  auto d = std::make_shared<xgbb::DMatrix>();
+  d->rows = uint32_t(rows);
+  d->cols = uint32_t(cols);
+  d->data = std::move(values);
+  normalise(d->data, missing, d->has_missing);
+  return new DMatrixPtr(std::move(d));
+}
+
+void set_info(xgbb::DMatrix& d, const std::string& field, std::vector<float> v) {
+  if (field == "label") {
+    for (float x : v) require(std::isfinite(x), "Label contains NaN, infinity or a value too large.");
+    d.labels = std::move(v);
+  } else if (field == "weight") {
+    for (float x : v) require(std::isfinite(x) && x >= 0, "Weights must be finite and nonnegative.");
+    d.weights = std::move(v);
+  } else if (field == "base_margin") {
+    d.base_margin = std::move(v);
+  } else {
+    throw Error("Unknown or unsupported metadata field: " + field);
+  }
+  ++d.generation;
+}
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Library
+// ---------------------------------------------------------------------------
+XGB_DLL void XGBoostVersion(int* major, int* minor, int* patch) {
+  if (major) *major = 3;
+  if (minor) *minor = 5;
+  if (patch) *patch = 0;
+}
+
+XGB_DLL const char* XGBGetLastError() { return last_error.c_str(); }
+
+XGB_DLL int XGBRegisterLogCallback(void (*callback)(const char*)) {
+  log_callback = callback;
+  return 0;
+}
+
+XGB_DLL int XGBuildInfo(char const** out) {
+  return guarded([&] {
+    int runtime = 0;
+    cudaRuntimeGetVersion(&runtime);
+    results.str = std::string("{\"USE_CUDA\":true,\"USE_NCCL\":true,\"USE_OPENMP\":false,") +
+                  "\"BUILTIN_PREFETCH_PRESENT\":false,\"DEBUG\":false,\"USE_FEDERATED\":false," +
+                  "\"USE_RMM\":false,\"CUDA_VERSION\":[" + std::to_string(runtime / 1000) + "," +
+                  std::to_string((runtime % 1000) / 10) + "],\"DEVICE\":\"B200 sm_100a\"}";
+    *out = results.str.c_str();
+  });
+}
+
+XGB_DLL int XGBSetGlobalConfig(char const* config) {
+  return guarded([&] { (void)Json::parse(config ? config : "{}"); });
+}
+
+XGB_DLL int XGBGetGlobalConfig(char const** out) {
+  return guarded([&] {
+    results.str = "{\"verbosity\":1,\"use_rmm\":false,\"nthread\":0}";
+    *out = results.str.c_str();
+  });
+}
+
+// ---------------------------------------------------------------------------
+// DMatrix
+// ---------------------------------------------------------------------------
+XGB_DLL int XGDMatrixCreateFromDense(char const* data, char const* config, DMatrixHandle* out) {
+  return guarded([&] {
+    ArrayView a = parse_array(data);
+    require(a.shape.size() == 2, "Dense input must be 2-dimensional.");
+    uint64_t rows, cols;
+    auto v = to_floats(a, rows, cols);
+    *out = new_dmatrix(std::move(v), rows, cols, config_missing(config));
+  });
+}
+
+XGB_DLL int XGDMatrixCreateFromMat(const float* data, bst_ulong nrow, bst_ulong ncol, float missing,
+                                   DMatrixHandle* out) {
+  return guarded([&] {
+    std::vector<float> v(data, data + nrow * ncol);
+    *out = new_dmatrix(std::move(v), nrow, ncol, missing);
+  });
+}
+
+// CSR input is densified: an absent entry is a missing value, exactly as the
+// reference's CSR histogram treats it (missing = node total - present bins).
+XGB_DLL int XGDMatrixCreateFromCSR(char const* indptr, char const* indices, char const* data,
+                                   bst_ulong ncol, char const* config, DMatrixHandle* out) {
+  return guarded([&] {
+    ArrayView p = parse_array(indptr), i = parse_array(indices), v = parse_array(data);
+    uint64_t pr, pc, ir, ic, vr, vc;
+    auto ptr = to_floats(p, pr, pc);
+    auto idx = to_floats(i, ir, ic);
+    auto val = to_floats(v, vr, vc);
+    require(pr >= 1, "CSR indptr must have at least one entry.");
+    const uint64_t rows = pr - 1;
+    uint64_t cols = ncol;
+    for (float c : idx) cols = std::max<uint64_t>(cols, uint64_t(c) + 1);
+    std::vector<float> dense(size_t(rows) * cols, NAN);
+    const float missing = config_missing(config);
+    for (uint64_t r = 0; r < rows; ++r)
+      for (uint64_t k = uint64_t(ptr[r]); k < uint64_t(ptr[r + 1]); ++k) {
+        const float x = val[k];
+        dense[size_t(r) * cols + uint64_t(idx[k])] = (std::isnan(missing) ? false : x == missing) ? NAN : x;
+      }
+    *out = new_dmatrix(std::move(dense), rows, cols, NAN);
+  });
+}
+
+XGB_DLL int XGDMatrixFree(DMatrixHandle handle) {
+  return guarded([&] {
+    require(handle != nullptr, "DMatrix handle is null.");
+    delete static_cast<DMatrixPtr*>(handle);
+  });
+}
+
+XGB_DLL int XGDMatrixSetFloatInfo(DMatrixHandle handle, const char* field, const float* array,
+                                  bst_ulong len) {
+  return guarded([&] { set_info(*dmat(handle), field, std::vector<float>(array, array + len)); });
+}
+
+XGB_DLL int XGDMatrixSetInfoFromInterface(DMatrixHandle handle, char const* field, char const* data) {
+  return guarded([&] {
+    ArrayView a = parse_array(data);
+    uint64_t r, c;
+    set_info(*dmat(handle), field, to_floats(a, r, c));
+  });
+}
+
+XGB_DLL int XGDMatrixGetFloatInfo(const DMatrixHandle handle, const char* field, bst_ulong* out_len,
+                                  const float** out_dptr) {
+  return guarded([&] {
+    auto& d = *dmat(handle);
+    const std::string f = field;
+    const std::vector<float>* v = f == "label" ? &d.labels : f == "weight" ? &d.weights
+                                  : f == "base_margin" ? &d.base_margin : nullptr;
+    require(v != nullptr, "Unknown metadata field: " + f);
+    results.floats = *v;
+    *out_len = results.floats.size();
+    *out_dptr = results.floats.data();
+  });
+}
+
+XGB_DLL int XGDMatrixNumRow(DMatrixHandle handle, bst_ulong* out) {
+  return guarded([&] { *out = dmat(handle)->rows; });
+}
+XGB_DLL int XGDMatrixNumCol(DMatrixHandle handle, bst_ulong* out) {
+  return guarded([&] { *out = dmat(handle)->cols; });
+}
+XGB_DLL int XGDMatrixNumNonMissing(DMatrixHandle handle, bst_ulong* out) {
+  return guarded([&] {
+    uint64_t n = 0;
+    for (float x : dmat(handle)->data) n += !std::isnan(x);
+    *out = n;
+  });
+}
+
+// ---------------------------------------------------------------------------
+// Booster
+// ---------------------------------------------------------------------------
+XGB_DLL int XGBoosterCreate(const DMatrixHandle dmats[], bst_ulong len, BoosterHandle* out) {
+  return guarded([&] {
+    ensure_device();
+    std::vector<DMatrixPtr> cache;
+    for (bst_ulong i = 0; i < len; ++i) cache.push_back(dmat(dmats[i]));
+    *out = new xgbb::Booster(std::move(cache));
+  });
+}
+
+XGB_DLL int XGBoosterFree(BoosterHandle handle) {
+  return guarded([&] { delete &booster(handle); });
+}
+
+XGB_DLL int XGBoosterSetParam(BoosterHandle handle, const char* name, const char* value) {
+  return guarded([&] { booster(handle).set_param(name, value ? value : ""); });
+}
+
+XGB_DLL int XGBoosterSetParams(BoosterHandle handle, char const* config) {
+  return guarded([&] {
+    Json c = Json::parse(config);
+    for (auto& kv : c.obj)
+      booster(handle).set_param(kv.first, kv.second.kind == Json::String ? kv.second.str : kv.second.dump());
+  });
+}
+
+XGB_DLL int XGBoosterBoostedRounds(BoosterHandle handle, int* out) {
+  return guarded([&] { *out = int(booster(handle).boosted_rounds()); });
+}
+
+XGB_DLL int XGBoosterGetNumFeature(BoosterHandle handle, bst_ulong* out) {
+  return guarded([&] { *out = booster(handle).num_feature(); });
+}
+
+XGB_DLL int XGBoosterUpdateOneIter(BoosterHandle handle, int iter, DMatrixHandle dtrain) {
+  return guarded([&] { booster(handle).update(dmat(dtrain), iter); });
+}
+
+XGB_DLL int XGBoosterPredictFromDMatrix(BoosterHandle handle, DMatrixHandle dm, char const* config,
+                                        bst_ulong const** out_shape, bst_ulong* out_dim,
+                                        float const** out_result) {
+  return guarded([&] {
+    Json c = Json::parse(config && *config ? config : "{}");
+    int type = 0;
+    if (auto* t = c.find("type")) type = int(t->num);
+    require(type == 0 || type == 1, "Only value (type 0) and margin (type 1) predictions are implemented.");
+    uint32_t begin = 0, end = 0;
+    if (auto* b = c.find("iteration_begin")) begin = uint32_t(b->num);
+    if (auto* e = c.find("iteration_end")) end = uint32_t(e->num);
+    bool training = false;
+    if (auto* t = c.find("training")) training = t->truthy();
+    bool strict = false;
+    if (auto* s = c.find("strict_shape")) strict = s->truthy();
+    std::vector<uint64_t> shape;
+    results.floats = booster(handle).predict(dmat(dm), type == 1, begin, end, training, shape);
+    if (strict && shape.size() == 1) shape.push_back(1);
+    results.shape.assign(shape.begin(), shape.end());
+    *out_shape = results.shape.data();
+    *out_dim = results.shape.size();
+    *out_result = results.floats.data();
+  });
+}
+
+// Legacy upstream predict entry (older include/xgboost/c_api.h; absent from the
+// reference's header, whose predict entries are c_api.h:1207-1339): bit 0 of
+// option_mask selects margins; ntree_limit counts rounds (0 = all).
+XGB_DLL int XGBoosterPredict(BoosterHandle handle, DMatrixHandle dm, int option_mask,
+                             unsigned ntree_limit, int training, bst_ulong* out_len,
+                             const float** out_result) {
+  return guarded([&] {
+    std::vector<uint64_t> shape;
+    results.floats = booster(handle).predict(dmat(dm), (option_mask & 1) != 0, 0, ntree_limit,
+                                             training != 0, shape);
+    *out_len = results.floats.size();
+    *out_result = results.floats.data();
+  });
+}
+
+XGB_DLL int XGBoosterSetAttr(BoosterHandle handle, const char* key, const char* value) {
+  return guarded([&] {
+    auto& b = booster(handle);
+    if (value) b.attrs[key] = value;
+    else b.attrs.erase(key);
+  });
+}
+
+XGB_DLL int XGBoosterGetAttr(BoosterHandle handle, const char* key, const char** out, int* success) {
+  return guarded([&] {
+    auto& b = booster(handle);
+    auto it = b.attrs.find(key);
+    *success = it != b.attrs.end();
+    if (*success) {
+      results.str = it->second;
+      *out = results.str.c_str();
+    } else {
+      *out = nullptr;
+    }
+  });
+}
+
+XGB_DLL int XGBoosterGetAttrNames(BoosterHandle handle, bst_ulong* out_len, const char*** out) {
+  return guarded([&] {
+    auto& b = booster(handle);
+    results.strings.clear();
+    for (auto& kv : b.attrs) results.strings.push_back(kv.first);
+    results.ptrs.clear();
+    for (auto& s : results.strings) results.ptrs.push_back(s.c_str());
+    *out_len = results.ptrs.size();
+    *out = results.ptrs.data();
+  });
+}
+
+XGB_DLL int XGBoosterSetStrFeatureInfo(BoosterHandle handle, const char* field,
+                                       const char** features, const bst_ulong size) {
+  return guarded([&] {
+    std::vector<std::string> v;
+    for (bst_ulong i = 0; i < size; ++i) v.emplace_back(features[i]);
+    booster(handle).feature_info[field] = std::move(v);
+  });
+}
+
+XGB_DLL int XGBoosterGetStrFeatureInfo(BoosterHandle handle, const char* field, bst_ulong* len,
+                                       const char*** out_features) {
+  return guarded([&] {
+    auto& fi = booster(handle).feature_info;
+    auto it = fi.find(field);
+    results.strings = it == fi.end() ? std::vector<std::string>{} : it->second;
+    results.ptrs.clear();
+    for (auto& s : results.strings) results.ptrs.push_back(s.c_str());
+    *len = results.ptrs.size();
+    *out_features = results.ptrs.data();
+  });
+}
+
+XGB_DLL int XGBoosterSaveJsonConfig(BoosterHandle handle, bst_ulong* out_len, char const** out_str) {
+  return guarded([&] {
+    results.str = booster(handle).config_json();
+    *out_len = results.str.size();
+    *out_str = results.str.c_str();
+  });
+}
+
+// ---------------------------------------------------------------------------
+// Collective (row-sharded training over NCCL)
+// ---------------------------------------------------------------------------
+XGB_DLL int XGCommunicatorInit(char const* config) {
+  return guarded([&] {
+    Json c = Json::parse(config && *config ? config : "{}");
+    int rank = 0, world = 1, device = 0;
+    if (auto* r = c.find("rank")) rank = int(r->num);
+    if (auto* w = c.find("world_size")) world = int(w->num);
+    if (auto* d = c.find("device")) device = int(d->num);
+    std::string id;
+    if (auto* i = c.find("nccl_unique_id")) id = i->str;
+    xgbb::Comm::get().init(rank, world, id, device);
+  });
+}
+
+XGB_DLL int XGCommunicatorFinalize(void) {
+  return guarded([&] { xgbb::Comm::get().finalize(); });
+}
+
+XGB_DLL int XGCommunicatorGetRank(void) { return xgbb::Comm::get().rank(); }
+XGB_DLL int XGCommunicatorGetWorldSize(void) { return xgbb::Comm::get().world(); }
+
+// ---------------------------------------------------------------------------
+// B200 extensions (include/xgb_b200.h)
+// ---------------------------------------------------------------------------
+XGB_DLL int XGBBNcclUniqueId(char const** out) {
+  return guarded([&] {
+    results.str = xgbb::nccl_unique_id_hex();
+    *out = results.str.c_str();
+  });
+}
+
+XGB_DLL int XGBBSetDevice(int device) {
+  return guarded([&] { XGBB_CUDA(cudaSetDevice(device)); });
+}
+
+XGB_DLL int XGBBSynchronize(void) {
+  return guarded([&] { XGBB_CUDA(cudaDeviceSynchronize()); });
+}
+
+XGB_DLL int XGDMatrixQuantise(DMatrixHandle handle, int max_bin, DMatrixHandle ref) {
+  return guarded([&] {
+    ensure_device();
+    auto& d = *dmat(handle);
+    const xgbb::DMatrix* r = ref ? dmat(ref).get() : nullptr;
+    d.quantise(uint32_t(max_bin), r, nullptr, 0);
+    XGBB_CUDA(cudaStreamSynchronize(nullptr));
+  });
+}
+
+XGB_DLL int XGBoosterGetCudaProfile(BoosterHandle handle, char const** out) {
+  return guarded([&] {
+    auto& p = booster(handle).profile;
+    results.str = "{\"hist_ms\":" + std::to_string(p.hist_ms) +
+                  ",\"hist_launches\":" + std::to_string(p.hist_launches) +
+                  ",\"rounds\":" + std::to_string(p.rounds) + "}";
+    *out = results.str.c_str();
+  });
+}
+
+// Test entry: product cuts (host sketch) and GPU bins, decoded to row-major
+// uint32 with 0xffffffff for missing. cuts must hold cols * min(max_bin, rows).
+XGB_DLL int XGBBQuantizeHost(const float* X, bst_ulong rows, bst_ulong cols, uint32_t max_bin,
+                             float* cuts, uint32_t* counts, float* minima, uint32_t* bins) {
+  return guarded([&] {
+    ensure_device();
+    auto h = new_dmatrix(std::vector<float>(X, X + rows * cols), rows, cols, NAN);
+    std::unique_ptr<DMatrixPtr> owner(static_cast<DMatrixPtr*>(h));
+    auto& d = **owner;
+    d.quantise(max_bin, nullptr, nullptr, 0);
+    XGBB_CUDA(cudaDeviceSynchronize());
+    const auto& c = *d.cuts;
+    std::memcpy(cuts, c.values.data(), c.values.size() * 4);
+    std::memcpy(counts, c.counts.data(), c.counts.size() * 4);
+    std::memcpy(minima, c.minima.data(), c.minima.size() * 4);
+    const size_t n = size_t(rows) * d.ell.stride;
+    std::vector<uint8_t> raw(n * d.ell.bytes_per_code);
+    if (n) XGBB_CUDA(cudaMemcpy(raw.data(), d.codes.get(), raw.size(), cudaMemcpyDeviceToHost));
+    for (uint64_t r = 0; r < rows; ++r)
+      for (uint64_t f = 0; f < cols; ++f) {
+        const size_t i = size_t(r) * d.ell.stride + f;
+        const uint32_t code = d.ell.bytes_per_code == 1 ? raw[i] : reinterpret_cast<uint16_t*>(raw.data())[i];
+        bins[size_t(r) * cols + f] = code == d.ell.missing ? 0xffffffffu : code;
+      }
+  });
+}
+
+// Test entry: gradient pairs [groups][rows] and scales [groups][2] for margins
+// [rows][groups] through the product's gradient and exact-scale kernels.
+XGB_DLL int XGBBGradientsHost(int objective, const float* margins, const float* labels,
+                              const float* weights, bst_ulong rows, uint32_t groups,
+                              float scale_pos_weight, float* pairs, float* scales) {
+  return guarded([&] {
+    ensure_device();
+    xgbb::DeviceBuffer dm(std::max<size_t>(rows * groups, 1) * 4), dl(std::max<size_t>(rows, 1) * 4),
+        dw(weights ? rows * 4 : 0), dp(std::max<size_t>(rows * groups, 1) * 8),
+        mass(groups * 2 * sizeof(xgbb::MassAccum)), ds(groups * 8);
+    XGBB_CUDA(cudaMemcpy(dm.get(), margins, rows * groups * 4, cudaMemcpyHostToDevice));
+    XGBB_CUDA(cudaMemcpy(dl.get(), labels, rows * 4, cudaMemcpyHostToDevice));
+    if (weights) XGBB_CUDA(cudaMemcpy(dw.get(), weights, rows * 4, cudaMemcpyHostToDevice));
+    XGBB_CUDA(cudaMemset(mass.get(), 0, mass.size()));
+    auto* m = mass.as<xgbb::MassAccum>();
+    auto* p = dp.as<float2>();
+    xgbb::launch_gradients(objective, dm.as<float>(), dl.as<float>(), weights ? dw.as<float>() : nullptr,
+                           uint32_t(rows), groups, scale_pos_weight, p, m, nullptr);
+    xgbb::launch_mass_window(p, uint32_t(rows), groups, m, nullptr);
+    xgbb::launch_scales(p, uint32_t(rows), groups, m, ds.as<float2>(), rows, true, nullptr);
+    xgbb::launch_mass_exact(p, uint32_t(rows), groups, m, nullptr);
+    xgbb::launch_scales_exact(groups, m, ds.as<float2>(), nullptr);
+    XGBB_CUDA(cudaDeviceSynchronize());
+    XGBB_CUDA(cudaMemcpy(pairs, dp.get(), rows * groups * 8, cudaMemcpyDeviceToHost));
+    XGBB_CUDA(cudaMemcpy(scales, ds.get(), groups * 8, cudaMemcpyDeviceToHost));
+  });
+}
+
+// Test entry: a whole training run through DMatrix + Booster, with the trees
+// written back to back as DevNode records (48 bytes each).
+XGB_DLL int XGBBTrainHost(const float* X, bst_ulong rows, bst_ulong cols, const float* labels,
+                          const float* weights, char const* params_json, uint32_t rounds,
+                          void* nodes, bst_ulong node_capacity, uint32_t* tree_sizes,
+                          float* margins) {
+  return guarded([&] {
+    ensure_device();
+    auto h = new_dmatrix(std::vector<float>(X, X + rows * cols), rows, cols, NAN);
+    std::unique_ptr<DMatrixPtr> owner(static_cast<DMatrixPtr*>(h));
+    DMatrixPtr d = *owner;
+    set_info(*d, "label", std::vector<float>(labels, labels + rows));
+    if (weights) set_info(*d, "weight", std::vector<float>(weights, weights + rows));
+    xgbb::Booster b({d});
+    Json p = Json::parse(params_json && *params_json ? params_json : "{}");
+    for (auto& kv : p.obj) b.set_param(kv.first, kv.second.kind == Json::String ? kv.second.str : kv.second.dump());
+    for (uint32_t r = 0; r < rounds; ++r) b.update(d, int(r));
+    const auto& trees = b.trees();
+    size_t used = 0;
+    for (size_t t = 0; t < trees.size(); ++t) {
+      require(used + trees[t].nodes.size() <= node_capacity, "node buffer too small");
+      std::memcpy(static_cast<xgbb::DevNode*>(nodes) + used, trees[t].nodes.data(),
+                  trees[t].nodes.size() * sizeof(xgbb::DevNode));
+      tree_sizes[t] = uint32_t(trees[t].nodes.size());
+      used += trees[t].nodes.size();
+    }
+    std::vector<uint64_t> shape;
+    auto m = b.predict(d, true, 0, 0, true, shape);
+    std::memcpy(margins, m.data(), m.size() * 4);
+  });
+}

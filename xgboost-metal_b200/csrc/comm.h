@@ -1,0 +1,38 @@
+// Row-sharded training across GPUs: one process per GPU, one NCCL
+// communicator per process. Every rank holds a contiguous shard of the rows;
+// integer histograms, child row counts and the exact gradient masses are
+// summed over ranks, so each rank takes the same decisions as one GPU would.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+
+namespace xgbb {
+
+class Comm {
+ public:
+  static Comm& get();
+  // `id_hex` is an NCCL unique id produced by nccl_unique_id_hex() on one rank
+  // and shared with the others out of band.
+  void init(int rank, int world, const std::string& id_hex, int device);
+  void finalize();
+  bool active() const { return world_ > 1; }
+  int rank() const { return rank_; }
+  int world() const { return world_; }
+  void sum_u64(void* buf, size_t count, cudaStream_t s);
+  void sum_u32(void* buf, size_t count, cudaStream_t s);
+  void max_u32(void* buf, size_t count, cudaStream_t s);
+  void sum_f64(void* buf, size_t count, cudaStream_t s);
+  void broadcast(void* buf, size_t bytes, int root, cudaStream_t s);
+  void barrier(cudaStream_t s);
+
+ private:
+  int rank_ = 0, world_ = 1;
+  void* comm_ = nullptr;
+};
+
+std::string nccl_unique_id_hex();
+
+}  // namespace xgbb

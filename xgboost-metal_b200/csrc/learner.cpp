@@ -1,0 +1,567 @@
+// Booster and DMatrix runtime (host C++20). Mirrors the reference learner's
+// round structure (tabulai/xgboost-metal src/learner.cpp:632-985): gradients
+// for every output group, exact fixed-point scales, one depthwise tree per
+// group (all trees of a round use the round's starting margins), margins
+// advanced by the new trees.
+#include "learner.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <sstream>
+
+#include "comm.h"
+#include "json.h"
+#include "sketch.h"
+
+namespace xgbb {
+
+// ---------------------------------------------------------------------------
+// Cuts / DMatrix
+// ---------------------------------------------------------------------------
+void Cuts::upload() {
+  d_values.resize(std::max<size_t>(values.size(), 1) * sizeof(float));
+  d_counts.resize(std::max<size_t>(counts.size(), 1) * sizeof(uint32_t));
+  d_minima.resize(std::max<size_t>(minima.size(), 1) * sizeof(float));
+  if (!values.empty())
+    XGBB_CUDA(cudaMemcpy(d_values.get(), values.data(), values.size() * 4, cudaMemcpyHostToDevice));
+  if (!counts.empty())
+    XGBB_CUDA(cudaMemcpy(d_counts.get(), counts.data(), counts.size() * 4, cudaMemcpyHostToDevice));
+  if (!minima.empty())
+    XGBB_CUDA(cudaMemcpy(d_minima.get(), minima.data(), minima.size() * 4, cudaMemcpyHostToDevice));
+}
+
+const float* DMatrix::device_data(cudaStream_t stream) {
+  const size_t bytes = size_t(rows) * cols * sizeof(float);
+  if (!d_data && bytes) {
+    d_data.resize(bytes);
+    XGBB_CUDA(cudaMemcpyAsync(d_data.get(), data.data(), bytes, cudaMemcpyHostToDevice, stream));
+  }
+  return d_data.as<float>();
+}
+
+void DMatrix::upload_info(cudaStream_t stream) {
+  if (uploaded_generation == generation) return;
+  require(labels.size() == rows || labels.empty(), "Label length must equal the number of rows.");
+  d_labels.resize(std::max<size_t>(labels.size(), 1) * 4);
+  if (!labels.empty())
+    XGBB_CUDA(cudaMemcpyAsync(d_labels.get(), labels.data(), labels.size() * 4,
+                              cudaMemcpyHostToDevice, stream));
+  if (!weights.empty()) {
+    d_weights.resize(weights.size() * 4);
+    XGBB_CUDA(cudaMemcpyAsync(d_weights.get(), weights.data(), weights.size() * 4,
+                              cudaMemcpyHostToDevice, stream));
+  } else {
+    d_weights.release();
+  }
+  uploaded_generation = generation;
+}
+
+void DMatrix::set_cuts(std::shared_ptr<Cuts> c, cudaStream_t stream) {
+  require(c->cols == cols, "Quantile reference does not match the feature count.");
+  uint32_t max_count = 0;
+  for (uint32_t v : c->counts) max_count = std::max(max_count, v);
+  const bool narrow = max_count <= 255 || (!has_missing && max_count <= 256);
+  ell = Ellpack{};
+  ell.rows = rows;
+  ell.cols = cols;
+  ell.bytes_per_code = narrow ? 1 : 2;
+  ell.missing = narrow ? 0xffu : 0xffffu;
+  const uint32_t align = 16 / ell.bytes_per_code;
+  ell.stride = std::max(align, (cols + align - 1) / align * align);
+  ell.bins = c->stride;
+  ell.cuts = c->d_values.as<float>();
+  ell.counts = c->d_counts.as<uint32_t>();
+  ell.minima = c->d_minima.as<float>();
+  const size_t bytes = size_t(rows) * ell.stride * ell.bytes_per_code;
+  codes.resize(std::max<size_t>(bytes, 16));
+  if (rows) {
+    const float* X = device_data(stream);
+    launch_quantize(X, rows, cols, ell.cuts, ell.counts, ell.bins, codes.get(), ell.stride,
+                    ell.bytes_per_code, ell.missing, stream);
+  }
+  ell.codes = codes.get();
+  cuts = std::move(c);
+}
+
+void DMatrix::quantise(uint32_t mb, const DMatrix* ref, cudaStream_t stream, int threads) {
+  if (quantised() && max_bin == mb) return;
+  require(mb >= 2, "max_bin must be at least 2.");
+  require(mb <= kMaxBins, "max_bin above 256 is not supported by the CUDA histogram kernels.");
+  std::shared_ptr<Cuts> c;
+  if (ref) {
+    require(ref->cuts && ref->max_bin == mb, "Quantile reference does not match max_bin.");
+    c = ref->cuts;
+  } else {
+    c = std::make_shared<Cuts>();
+    c->cols = cols;
+    c->max_bin = mb;
+    c->stride = cut_stride(rows, mb);
+    c->values.assign(size_t(cols) * c->stride, 0.0f);
+    c->counts.assign(cols, 0);
+    c->minima.assign(cols, -INFINITY);
+    sketch_cuts(data.data(), rows, cols, weights.empty() ? nullptr : weights.data(), mb,
+                c->values.data(), c->counts.data(), c->minima.data(), threads);
+    c->upload();
+  }
+  max_bin = mb;
+  set_cuts(std::move(c), stream);
+}
+
+// ---------------------------------------------------------------------------
+// Training state for one matrix.
+// ---------------------------------------------------------------------------
+struct Booster::TrainState {
+  std::weak_ptr<DMatrix> owner;
+  DMatrix* d = nullptr;
+  uint32_t rows = 0, groups = 1, margin_rounds = 0;
+  DeviceBuffer margins, pairs, mass, scales;
+  DeviceBuffer state, ids[2], sums[2], seg_begin[2], seg_count[2], parent_slot, built_left,
+      tile_offset, ptile_offset, cursor_l, cursor_r, counts_local, counts_global, mode, slot_leaf,
+      keys[2], cand, nodes, built, bank[2], rows_buf[2];
+  TreeWorkspace ws{};
+  HistConfig hc{};
+  std::vector<cudaGraphExec_t> graphs;
+  DevNode* host_nodes = nullptr;   // pinned [groups][capacity]
+  DriverState* host_state = nullptr;  // pinned [groups]
+  uint32_t capacity = 0;
+  std::vector<cudaEvent_t> events;  // profiling: [groups][levels][2]
+  ~TrainState() {
+    for (auto g : graphs)
+      if (g) cudaGraphExecDestroy(g);
+    for (auto e : events) cudaEventDestroy(e);
+    if (host_nodes) cudaFreeHost(host_nodes);
+    if (host_state) cudaFreeHost(host_state);
+  }
+};
+
+Booster::Booster(std::vector<std::shared_ptr<DMatrix>> cache) {
+  for (auto& d : cache) cache_.push_back(d);
+  XGBB_CUDA(cudaGetDevice(&device_));
+  XGBB_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+}
+
+Booster::~Booster() {
+  state_.reset();
+  if (stream_) cudaStreamDestroy(stream_);
+}
+
+void Booster::set_param(const std::string& key, const std::string& value) {
+  static const std::map<std::string, std::string> alias = {
+      {"eta", "learning_rate"}, {"lambda", "reg_lambda"}, {"alpha", "reg_alpha"},
+      {"gamma", "min_split_loss"}};
+  auto it = alias.find(key);
+  params_[it == alias.end() ? key : it->second] = value;
+  configured_ = false;
+}
+
+std::string Booster::get_param(const std::string& key, const std::string& def) const {
+  auto it = params_.find(key);
+  return it == params_.end() ? def : it->second;
+}
+
+namespace {
+float number(const std::map<std::string, std::string>& p, const std::string& k, float def) {
+  auto it = p.find(k);
+  if (it == p.end() || it->second.empty()) return def;
+  return std::stof(it->second);
+}
+long integer(const std::map<std::string, std::string>& p, const std::string& k, long def) {
+  auto it = p.find(k);
+  if (it == p.end() || it->second.empty()) return def;
+  return std::lround(std::stod(it->second));
+}
+}  // namespace
+
+void Booster::configure() {
+  if (configured_) return;
+  static const std::map<std::string, int> objectives = {
+      {"reg:squarederror", kSquaredError}, {"reg:linear", kSquaredError},
+      {"binary:logistic", kLogistic},       {"reg:logistic", kLogistic},
+      {"binary:logitraw", kLogitRaw},       {"multi:softprob", kSoftprob},
+      {"multi:softmax", kSoftmax}};
+  const std::string obj = get_param("objective", "reg:squarederror");
+  auto it = objectives.find(obj);
+  require(it != objectives.end(), "Objective is not implemented by the CUDA backend: " + obj);
+  const int new_objective = it->second;
+  require(!initialized_ || new_objective == objective_, "The objective cannot change after training starts.");
+  objective_ = new_objective;
+  const std::string device = get_param("device", "cuda");
+  require(device == "cuda" || device == "gpu" || device.rfind("cuda:", 0) == 0,
+          "This build trains on CUDA devices only; device must be 'cuda', 'cuda:N' or 'gpu'.");
+  const std::string method = get_param("tree_method", "hist");
+  require(method == "hist" || method == "auto" || method == "gpu_hist",
+          "CUDA tree training requires tree_method='hist' or 'auto'.");
+  require(get_param("booster", "gbtree") == "gbtree", "Only the gbtree booster is implemented.");
+  require(get_param("grow_policy", "depthwise") == "depthwise", "Only grow_policy='depthwise' is implemented.");
+  require(number(params_, "subsample", 1) == 1.0f, "subsample < 1 is not implemented by the CUDA backend.");
+  for (auto k : {"colsample_bytree", "colsample_bylevel", "colsample_bynode"})
+    require(number(params_, k, 1) == 1.0f, std::string(k) + " < 1 is not implemented by the CUDA backend.");
+  require(integer(params_, "num_parallel_tree", 1) == 1, "num_parallel_tree > 1 is not implemented.");
+  require(integer(params_, "max_leaves", 0) == 0, "max_leaves is not implemented.");
+  for (auto k : {"monotone_constraints", "interaction_constraints"}) {
+    auto v = get_param(k, "");
+    require(v.empty() || v == "()" || v == "[]", std::string(k) + " are not implemented.");
+  }
+  tp_.max_depth = uint32_t(integer(params_, "max_depth", 6));
+  require(tp_.max_depth >= 1 && tp_.max_depth <= kMaxDepth,
+          "max_depth must be in [1, 10] for the CUDA depthwise driver.");
+  tp_.eta = number(params_, "learning_rate", 0.3f);
+  tp_.reg_lambda = number(params_, "reg_lambda", 1.0f);
+  tp_.reg_alpha = number(params_, "reg_alpha", 0.0f);
+  tp_.min_split_loss = number(params_, "min_split_loss", 0.0f);
+  tp_.min_child_weight = number(params_, "min_child_weight", 1.0f);
+  tp_.max_delta_step = number(params_, "max_delta_step", 0.0f);
+  for (float v : {tp_.reg_lambda, tp_.reg_alpha, tp_.min_split_loss, tp_.min_child_weight,
+                  tp_.max_delta_step, tp_.eta})
+    require(v >= 0 && std::isfinite(v), "Tree parameters must be finite and nonnegative.");
+  spw_ = number(params_, "scale_pos_weight", 1.0f);
+  const uint32_t mb = uint32_t(integer(params_, "max_bin", 256));
+  require(!initialized_ || mb == max_bin_ || trees_.empty(), "max_bin cannot change after training starts.");
+  max_bin_ = mb;
+  if (objective_ == kSoftprob || objective_ == kSoftmax) {
+    const long nc = integer(params_, "num_class", 0);
+    require(nc >= 2, "Multiclass requires num_class >= 2.");
+    require(!initialized_ || uint32_t(nc) == groups_, "num_class cannot change after training starts.");
+    groups_ = uint32_t(nc);
+  } else {
+    groups_ = 1;
+  }
+  profiling = integer(params_, "cuda_profile", 0) != 0;
+  configured_ = true;
+  if (state_) state_.reset();  // parameters are baked into captured graphs
+}
+
+void Booster::initialize(DMatrix& d) {
+  require(d.cols > 0, "Data must contain at least one feature.");
+  num_feature_ = d.cols;
+  base_score_.assign(groups_, 0.5f);
+  const auto bs = params_.find("base_score");
+  if (bs != params_.end()) {
+    base_score_.assign(groups_, std::stof(bs->second));
+  } else {
+    d.upload_info(stream_);
+    const uint32_t chunks = (d.rows + 1023) / 1024;
+    DeviceBuffer sums(std::max<uint32_t>(chunks, 1) * 2 * sizeof(double));
+    std::vector<double> host(size_t(chunks) * 2);
+    for (uint32_t k = 0; k < groups_; ++k) {
+      launch_base_chunks(objective_, d.d_labels.as<float>(), d.d_weights.as<float>(), d.rows, k,
+                         spw_, sums.as<double>(), stream_);
+      if (chunks)
+        XGBB_CUDA(cudaMemcpyAsync(host.data(), sums.get(), host.size() * 8, cudaMemcpyDeviceToHost, stream_));
+      XGBB_CUDA(cudaStreamSynchronize(stream_));
+      double sy = 0, sw = 0;
+      for (uint32_t c = 0; c < chunks; ++c) {
+        sy = sy + host[2 * c];
+        sw = sw + host[2 * c + 1];
+      }
+      base_score_[k] = sw > 0 ? float(sy / sw) : (objective_ == kSquaredError && d.rows == 0 ? 0.0f : 0.5f);
+    }
+  }
+  // Scores to margins (src/objectives.cpp:17-31; the multiclass intercept of
+  // kernels/boost.metal:404-420).
+  base_margin_ = base_score_;
+  if ((objective_ == kSoftprob || objective_ == kSoftmax) && bs == params_.end()) {
+    float mean = 0;
+    for (uint32_t j = 0; j < groups_; ++j) mean += std::log(std::max(base_score_[j], 1.0e-6f));
+    for (uint32_t k = 0; k < groups_; ++k)
+      base_margin_[k] = std::log(std::max(base_score_[k], 1.0e-6f)) - mean / float(groups_);
+    base_score_ = base_margin_;
+  } else if (objective_ == kLogistic) {
+    for (uint32_t k = 0; k < groups_; ++k) {
+      require(base_score_[k] >= 0 && base_score_[k] <= 1, "base_score must be in [0,1] for logistic loss.");
+      const float v = std::min(std::max(base_score_[k], 1.0e-6f), 1.0f - 1.0e-6f);
+      base_margin_[k] = -std::log(1.0f / v - 1.0f);
+    }
+  }
+  initialized_ = true;
+}
+
+Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp) {
+  DMatrix& d = *dp;
+  if (state_ && state_->d == &d && !state_->owner.expired()) return *state_;
+  state_.reset();
+  auto ts = std::make_unique<TrainState>();
+  ts->owner = dp;
+  ts->d = &d;
+  ts->rows = d.rows;
+  ts->groups = groups_;
+  const uint32_t n = d.rows, G = groups_, C = d.cols, D = tp_.max_depth;
+  const Ellpack& e = d.ell;
+  ts->margins.resize(std::max<size_t>(size_t(n) * G, 1) * 4);
+  ts->pairs.resize(std::max<size_t>(size_t(n) * G, 1) * 8);
+  ts->mass.resize(size_t(G) * 2 * sizeof(MassAccum));
+  ts->scales.resize(size_t(G) * sizeof(float2));
+  ts->state.resize(sizeof(DriverState));
+  for (int i = 0; i < 2; ++i) {
+    ts->ids[i].resize(kMaxFrontier * 4);
+    ts->sums[i].resize(kMaxFrontier * 16);
+    ts->seg_begin[i].resize(kMaxFrontier * 4);
+    ts->seg_count[i].resize(kMaxFrontier * 4);
+    ts->keys[i].resize(kMaxFrontier * 8);
+    ts->rows_buf[i].resize(std::max<size_t>(n, 1) * 4);
+  }
+  ts->parent_slot.resize(kMaxFrontier * 4);
+  ts->built_left.resize(kMaxFrontier * 4);
+  ts->tile_offset.resize((kMaxFrontier + 1) * 4);
+  ts->ptile_offset.resize((kMaxFrontier + 1) * 4);
+  ts->cursor_l.resize(kMaxFrontier * 4);
+  ts->cursor_r.resize(kMaxFrontier * 4);
+  ts->counts_local.resize(kMaxFrontier * 8);
+  ts->counts_global.resize(kMaxFrontier * 8);
+  ts->mode.resize(kMaxFrontier * 4);
+  ts->slot_leaf.resize(kMaxFrontier * 8);
+  const size_t node_bytes = hist_node_bytes(e);
+  const uint32_t max_slots = max_slots_at(D - 1);
+  ts->cand.resize(size_t(max_slots) * C * sizeof(DevSplit));
+  ts->capacity = (2u << D) - 1;
+  ts->nodes.resize(size_t(ts->capacity) * sizeof(DevNode));
+  ts->built.resize(size_t(max_pairs_at(D - 1)) * node_bytes);
+  const uint32_t bank_slots = D >= 2 ? max_slots_at(D - 2) : 1u;
+  ts->bank[0].resize(size_t(bank_slots) * node_bytes);
+  ts->bank[1].resize(size_t(bank_slots) * node_bytes);
+  XGBB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ts->host_nodes),
+                           size_t(G) * ts->capacity * sizeof(DevNode)));
+  XGBB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ts->host_state), size_t(G) * sizeof(DriverState)));
+
+  TreeWorkspace& ws = ts->ws;
+  ws.state = ts->state.as<DriverState>();
+  for (int i = 0; i < 2; ++i) {
+    ws.ids[i] = ts->ids[i].as<uint32_t>();
+    ws.sums[i] = ts->sums[i].as<long long>();
+    ws.seg_begin[i] = ts->seg_begin[i].as<uint32_t>();
+    ws.seg_count[i] = ts->seg_count[i].as<uint32_t>();
+    ws.keys[i] = ts->keys[i].as<unsigned long long>();
+    ws.bank[i] = ts->bank[i].as<longlong2>();
+    ws.rows[i] = ts->rows_buf[i].as<uint32_t>();
+  }
+  ws.parent_slot = ts->parent_slot.as<uint32_t>();
+  ws.built_left = ts->built_left.as<uint32_t>();
+  ws.tile_offset = ts->tile_offset.as<uint32_t>();
+  ws.ptile_offset = ts->ptile_offset.as<uint32_t>();
+  ws.cursor_l = ts->cursor_l.as<uint32_t>();
+  ws.cursor_r = ts->cursor_r.as<uint32_t>();
+  ws.counts_local = ts->counts_local.as<uint32_t>();
+  ws.counts_global = Comm::get().active() ? ts->counts_global.as<uint32_t>() : ws.counts_local;
+  ws.mode = ts->mode.as<uint32_t>();
+  ws.slot_leaf = ts->slot_leaf.as<float>();
+  ws.cand = ts->cand.as<DevSplit>();
+  ws.nodes = ts->nodes.as<DevNode>();
+  ws.built = ts->built.as<longlong2>();
+  ws.node_capacity = ts->capacity;
+  ts->hc = hist_config(e, objective_ == kSquaredError && d.weights.empty());
+  ts->graphs.assign(G, nullptr);
+  if (profiling) {
+    ts->events.resize(size_t(G) * D * 2);
+    for (auto& ev : ts->events) XGBB_CUDA(cudaEventCreate(&ev));
+  }
+  // Margins start from the base margins plus every tree already in the model.
+  d.upload_info(stream_);
+  DeviceBuffer base(G * 4);
+  XGBB_CUDA(cudaMemcpyAsync(base.get(), base_margin_.data(), G * 4, cudaMemcpyHostToDevice, stream_));
+  if (trees_.empty()) {
+    launch_fill_margins(ts->margins.as<float>(), base.as<float>(), n, G, stream_);
+  } else {
+    std::vector<uint64_t> shape;
+    auto m = predict(dp, true, 0, 0, false, shape);
+    XGBB_CUDA(cudaMemcpyAsync(ts->margins.get(), m.data(), m.size() * 4, cudaMemcpyHostToDevice, stream_));
+  }
+  XGBB_CUDA(cudaStreamSynchronize(stream_));
+  ts->margin_rounds = rounds_;
+  state_ = std::move(ts);
+  return *state_;
+}
+
+void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s) {
+  DMatrix& d = *ts.d;
+  Comm& comm = Comm::get();
+  TreeLaunch tl{};
+  tl.ell = d.ell;
+  tl.params = tp_;
+  tl.pairs = ts.pairs.as<float2>() + size_t(g) * ts.rows;
+  tl.scale = ts.scales.as<float2>() + g;
+  tl.margins = ts.margins.as<float>();
+  tl.groups = ts.groups;
+  tl.group = g;
+  tl.unit_hessian = objective_ == kSquaredError && d.weights.empty();
+  tl.feature_group = ts.hc.feature_group;
+  tl.hist_smem = ts.hc.smem;
+  tl.hist_threads = ts.hc.threads;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device_);
+  tl.hist_blocks = sms * 2;
+  tl.eval_blocks = sms * 8;
+  tl.part_blocks = sms * 8;
+  const TreeWorkspace& ws = ts.ws;
+  const uint32_t D = tp_.max_depth;
+  const size_t node_bytes = hist_node_bytes(d.ell);
+  tree_init(ws, tl, s);
+  for (uint32_t depth = 0; depth < D; ++depth) {
+    if (profiling) XGBB_CUDA(cudaEventRecord(ts.events[(size_t(g) * D + depth) * 2], s));
+    tree_level_hist(ws, tl, depth, s);
+    if (profiling) XGBB_CUDA(cudaEventRecord(ts.events[(size_t(g) * D + depth) * 2 + 1], s));
+    comm.sum_u64(ws.built, size_t(max_pairs_at(depth)) * node_bytes / 8, s);
+    tree_level_eval(ws, tl, depth, s);
+    tree_level_control(ws, tl, depth, s);
+    tree_level_partition(ws, tl, depth, s);
+    if (depth + 1 < D) {
+      tree_level_counts(ws, depth, s);
+      if (comm.active()) {
+        XGBB_CUDA(cudaMemcpyAsync(ws.counts_global, ws.counts_local, kMaxFrontier * 8,
+                                  cudaMemcpyDeviceToDevice, s));
+        comm.sum_u32(ws.counts_global, kMaxFrontier * 2, s);
+      }
+      tree_level_plan(ws, tl, depth + 1, s);
+    }
+  }
+  XGBB_CUDA(cudaMemcpyAsync(ts.host_nodes + size_t(g) * ts.capacity, ws.nodes,
+                            size_t(ts.capacity) * sizeof(DevNode), cudaMemcpyDeviceToHost, s));
+  XGBB_CUDA(cudaMemcpyAsync(ts.host_state + g, ws.state, sizeof(DriverState),
+                            cudaMemcpyDeviceToHost, s));
+}
+
+void Booster::run_round(TrainState& ts) {
+  DMatrix& d = *ts.d;
+  const uint32_t n = ts.rows, G = ts.groups;
+  d.upload_info(stream_);
+  MassAccum* mass = ts.mass.as<MassAccum>();
+  float2* pairs = ts.pairs.as<float2>();
+  XGBB_CUDA(cudaMemsetAsync(mass, 0, size_t(G) * 2 * sizeof(MassAccum), stream_));
+  launch_gradients(objective_, ts.margins.as<float>(), d.d_labels.as<float>(),
+                   d.d_weights.as<float>(), n, G, spw_, pairs, mass, stream_);
+  launch_mass_window(pairs, n, G, mass, stream_);
+  launch_scales(pairs, n, G, mass, ts.scales.as<float2>(), n, true, stream_);
+  launch_mass_exact(pairs, n, G, mass, stream_);
+  launch_scales_exact(G, mass, ts.scales.as<float2>(), stream_);
+  const bool use_graph = integer(params_, "cuda_graph", 1) != 0;
+  for (uint32_t g = 0; g < G; ++g) {
+    if (use_graph) {
+      if (!ts.graphs[g]) {
+        // Kernel attributes are set on first use, outside any capture.
+        record_tree_launches(ts, g, stream_);
+        XGBB_CUDA(cudaStreamSynchronize(stream_));
+        cudaGraph_t graph;
+        XGBB_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+        // The eager tree above already trained this group; replaying it would
+        // train the same tree twice, so the graph is only captured here.
+        record_tree_launches(ts, g, stream_);
+        XGBB_CUDA(cudaStreamEndCapture(stream_, &graph));
+        XGBB_CUDA(cudaGraphInstantiate(&ts.graphs[g], graph, 0));
+        XGBB_CUDA(cudaGraphDestroy(graph));
+      } else {
+        XGBB_CUDA(cudaGraphLaunch(ts.graphs[g], stream_));
+      }
+    } else {
+      record_tree_launches(ts, g, stream_);
+    }
+  }
+  XGBB_CUDA(cudaStreamSynchronize(stream_));
+  for (uint32_t g = 0; g < G; ++g) {
+    const DriverState st = ts.host_state[g];
+    require(!st.error, "GPU tree driver produced an invalid tree.");
+    require(st.node_count >= 1 && st.node_count <= ts.capacity, "GPU tree driver node count out of range.");
+    HostTree t;
+    t.group = g;
+    const DevNode* src = ts.host_nodes + size_t(g) * ts.capacity;
+    t.nodes.assign(src, src + st.node_count);
+    trees_.push_back(std::move(t));
+  }
+  if (profiling) {
+    const uint32_t D = tp_.max_depth;
+    for (uint32_t g = 0; g < G; ++g)
+      for (uint32_t depth = 0; depth < D; ++depth) {
+        float ms = 0;
+        XGBB_CUDA(cudaEventElapsedTime(&ms, ts.events[(size_t(g) * D + depth) * 2],
+                                       ts.events[(size_t(g) * D + depth) * 2 + 1]));
+        profile.hist_ms += ms;
+        ++profile.hist_launches;
+      }
+  }
+  ++profile.rounds;
+  ++rounds_;
+  ts.margin_rounds = rounds_;
+}
+
+void Booster::update(const std::shared_ptr<DMatrix>& d, int) {
+  XGBB_CUDA(cudaSetDevice(device_));
+  configure();
+  d->upload_info(stream_);
+  require(d->labels.size() == d->rows, "Labels must be provided for training.");
+  if (!initialized_) initialize(*d);
+  require(d->cols == num_feature_, "Number of columns does not match the trained model.");
+  if (!d->quantised() || d->max_bin != max_bin_)
+    d->quantise(max_bin_, nullptr, stream_, int(integer(params_, "nthread", 0)));
+  TrainState& ts = train_state(d);
+  run_round(ts);
+}
+
+void Booster::sync() { XGBB_CUDA(cudaStreamSynchronize(stream_)); }
+
+std::vector<float> Booster::predict(const std::shared_ptr<DMatrix>& dp, bool output_margin,
+                                    uint32_t begin, uint32_t end, bool, std::vector<uint64_t>& shape) {
+  XGBB_CUDA(cudaSetDevice(device_));
+  configure();
+  DMatrix& d = *dp;
+  const uint32_t G = initialized_ ? groups_ : std::max<uint32_t>(groups_, 1);
+  require(!initialized_ || d.cols == num_feature_ || d.rows == 0, "Feature shape mismatch.");
+  if (end == 0 || end > rounds_) end = rounds_;
+  std::vector<float> out(size_t(d.rows) * G);
+  std::vector<float> base = initialized_ ? base_margin_ : std::vector<float>(G, 0.5f);
+  if (d.rows) {
+    DeviceBuffer dout(out.size() * 4), dbase(G * 4);
+    XGBB_CUDA(cudaMemcpyAsync(dbase.get(), base.data(), G * 4, cudaMemcpyHostToDevice, stream_));
+    const bool cached = state_ && state_->d == &d && begin == 0 && end == rounds_ &&
+                        state_->margin_rounds == rounds_;
+    if (cached) {
+      XGBB_CUDA(cudaMemcpyAsync(dout.get(), state_->margins.get(), out.size() * 4,
+                                cudaMemcpyDeviceToDevice, stream_));
+    } else {
+      std::vector<DevNode> all;
+      std::vector<uint32_t> tb, tg;
+      for (size_t t = size_t(begin) * G; t < size_t(end) * G && t < trees_.size(); ++t) {
+        tb.push_back(uint32_t(all.size()));
+        tg.push_back(trees_[t].group);
+        all.insert(all.end(), trees_[t].nodes.begin(), trees_[t].nodes.end());
+      }
+      DeviceBuffer dn(std::max<size_t>(all.size(), 1) * sizeof(DevNode)),
+          db(std::max<size_t>(tb.size(), 1) * 4), dg(std::max<size_t>(tg.size(), 1) * 4);
+      if (!all.empty()) {
+        XGBB_CUDA(cudaMemcpyAsync(dn.get(), all.data(), all.size() * sizeof(DevNode), cudaMemcpyHostToDevice, stream_));
+        XGBB_CUDA(cudaMemcpyAsync(db.get(), tb.data(), tb.size() * 4, cudaMemcpyHostToDevice, stream_));
+        XGBB_CUDA(cudaMemcpyAsync(dg.get(), tg.data(), tg.size() * 4, cudaMemcpyHostToDevice, stream_));
+      }
+      launch_predict(d.device_data(stream_), d.rows, d.cols, dn.as<DevNode>(), db.as<uint32_t>(),
+                     dg.as<uint32_t>(), uint32_t(tb.size()), dbase.as<float>(), G, dout.as<float>(),
+                     stream_);
+    }
+    if (!output_margin) launch_transform(objective_, dout.as<float>(), d.rows, G, stream_);
+    XGBB_CUDA(cudaMemcpyAsync(out.data(), dout.get(), out.size() * 4, cudaMemcpyDeviceToHost, stream_));
+    XGBB_CUDA(cudaStreamSynchronize(stream_));
+  }
+  if (!output_margin && objective_ == kSoftmax) {
+    std::vector<float> labels(d.rows);
+    for (uint32_t r = 0; r < d.rows; ++r) labels[r] = out[size_t(r) * G];
+    shape = {d.rows};
+    return labels;
+  }
+  if (G > 1) shape = {d.rows, G};
+  else shape = {d.rows};
+  return out;
+}
+
+std::string Booster::config_json() const {
+  Json root;
+  root.kind = Json::Object;
+  Json learner;
+  learner.kind = Json::Object;
+  for (auto& kv : params_) {
+    Json v;
+    v.kind = Json::String;
+    v.str = kv.second;
+    learner.obj.emplace_back(kv.first, v);
+  }
+  root.obj.emplace_back("learner", learner);
+  return root.dump();
+}
+
+}  // namespace xgbb

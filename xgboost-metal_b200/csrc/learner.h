@@ -1,0 +1,144 @@
+// Host runtime: DMatrix (data + quantised ELLPACK in HBM) and Booster (model,
+// parameters, per-matrix training state), driving the CUDA kernels.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common.h"
+#include "tree.h"
+
+namespace xgbb {
+
+// Owning device allocation.
+class DeviceBuffer {
+ public:
+  DeviceBuffer() = default;
+  explicit DeviceBuffer(size_t bytes) { resize(bytes); }
+  DeviceBuffer(const DeviceBuffer&) = delete;
+  DeviceBuffer& operator=(const DeviceBuffer&) = delete;
+  DeviceBuffer(DeviceBuffer&& o) noexcept : p_(o.p_), n_(o.n_) { o.p_ = nullptr; o.n_ = 0; }
+  DeviceBuffer& operator=(DeviceBuffer&& o) noexcept {
+    release();
+    p_ = o.p_; n_ = o.n_; o.p_ = nullptr; o.n_ = 0;
+    return *this;
+  }
+  ~DeviceBuffer() { release(); }
+  void resize(size_t bytes) {
+    if (bytes <= n_ && p_) return;
+    release();
+    if (bytes) XGBB_CUDA(cudaMalloc(&p_, bytes));
+    n_ = bytes;
+  }
+  void release() {
+    if (p_) cudaFree(p_);
+    p_ = nullptr;
+    n_ = 0;
+  }
+  template <class T> T* as() const { return static_cast<T*>(p_); }
+  void* get() const { return p_; }
+  size_t size() const { return n_; }
+  explicit operator bool() const { return p_ != nullptr; }
+
+ private:
+  void* p_ = nullptr;
+  size_t n_ = 0;
+};
+
+// Cut values shared by every matrix quantised with them.
+struct Cuts {
+  uint32_t cols = 0, stride = 0, max_bin = 0;
+  std::vector<float> values, minima;
+  std::vector<uint32_t> counts;
+  DeviceBuffer d_values, d_counts, d_minima;
+  void upload();
+};
+
+class DMatrix {
+ public:
+  uint32_t rows = 0, cols = 0;
+  std::vector<float> data;  // row-major, NaN = missing
+  std::vector<float> labels, weights, base_margin;
+  bool has_missing = false;
+
+  // Quantised form.
+  std::shared_ptr<Cuts> cuts;
+  DeviceBuffer codes;
+  Ellpack ell;
+  uint32_t max_bin = 0;
+  bool quantised() const { return bool(cuts) && (codes || rows == 0); }
+  void quantise(uint32_t max_bin, const DMatrix* ref, cudaStream_t stream, int threads);
+  void set_cuts(std::shared_ptr<Cuts> c, cudaStream_t stream);
+
+  // Device copies on demand.
+  DeviceBuffer d_data, d_labels, d_weights;
+  uint64_t generation = 0, labels_generation = 0;
+  const float* device_data(cudaStream_t stream);
+  void upload_info(cudaStream_t stream);
+  size_t uploaded_labels = 0;
+  uint64_t uploaded_generation = ~0ull;
+};
+
+struct HostTree {
+  std::vector<DevNode> nodes;
+  uint32_t group = 0;
+};
+
+struct Profile {
+  double hist_ms = 0, total_ms = 0;
+  double hist_bytes = 0;
+  uint64_t hist_launches = 0, kernel_launches = 0, rounds = 0;
+};
+
+class Booster {
+ public:
+  explicit Booster(std::vector<std::shared_ptr<DMatrix>> cache);
+  ~Booster();
+  void set_param(const std::string& key, const std::string& value);
+  std::string get_param(const std::string& key, const std::string& def) const;
+  void update(const std::shared_ptr<DMatrix>& d, int iteration);
+  // Returns values [rows][groups] (margins if output_margin).
+  std::vector<float> predict(const std::shared_ptr<DMatrix>& d, bool output_margin,
+                             uint32_t iter_begin, uint32_t iter_end, bool training,
+                             std::vector<uint64_t>& shape);
+  uint32_t boosted_rounds() const { return rounds_; }
+  uint32_t num_feature() const { return num_feature_; }
+  uint32_t groups() const { return groups_; }
+  const std::vector<HostTree>& trees() { sync(); return trees_; }
+  std::string save_json();
+  void load_json(const std::string& text);
+  std::string config_json() const;
+  std::map<std::string, std::string> attrs;
+  std::map<std::string, std::vector<std::string>> feature_info;
+  Profile profile;
+  bool profiling = false;
+  void sync();
+
+ private:
+  struct TrainState;
+  void configure();
+  void initialize(DMatrix& d);
+  TrainState& train_state(const std::shared_ptr<DMatrix>& d);
+  void run_round(TrainState& ts);
+  void record_tree_launches(TrainState& ts, uint32_t group, cudaStream_t stream);
+  void materialize();
+
+  std::map<std::string, std::string> params_;
+  std::vector<std::weak_ptr<DMatrix>> cache_;
+  bool configured_ = false, initialized_ = false;
+  int objective_ = kSquaredError;
+  uint32_t groups_ = 1, num_feature_ = 0, rounds_ = 0, max_bin_ = 256;
+  TreeParams tp_{};
+  float spw_ = 1.0f;
+  std::vector<float> base_score_, base_margin_;
+  std::vector<HostTree> trees_;
+  cudaStream_t stream_ = nullptr;
+  int device_ = 0;
+  std::unique_ptr<TrainState> state_;
+};
+
+}  // namespace xgbb

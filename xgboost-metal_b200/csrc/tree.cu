@@ -1,0 +1,1344 @@
+// CUDA kernels of the histogram tree trainer (sm_100a).
+//
+// Reference semantics (tabulai/xgboost-metal) that each kernel reproduces:
+//   quantize_kernel      kernels/boost.metal:461-499 (bin = #cuts <= x, capped)
+//   gradient_kernel      kernels/boost.metal:553-601
+//   mass_*/scales        kernels/gradient_quantization.metal.h:1-67
+//   hist_kernel          kernels/boost.metal:700-733, histogram_missing.metal.h
+//   eval_kernel          kernels/boost.metal:902-1005 (+ subtraction :780-794)
+//   control_kernel       kernels/boost.metal:1245-1265, tree_driver.metal.h:28-94,
+//                        src/tree.cpp:1663-1717 (node table replay)
+//   partition_kernel     kernels/boost.metal:1325-1329, 1383-1389, 1738-1765
+//   base_chunk_kernel    kernels/boost.metal:356-420
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "device_math.cuh"
+#include "tree.h"
+
+namespace xgbb {
+namespace {
+
+constexpr int kWarp = 32;
+
+__device__ __forceinline__ unsigned long long shfl_u64(unsigned long long v, int src) {
+  return __shfl_sync(0xffffffffu, v, src);
+}
+
+// Inclusive warp scan of 64-bit integers (wrap-around).
+__device__ __forceinline__ unsigned long long warp_scan_u64(unsigned long long v, int lane) {
+#pragma unroll
+  for (int d = 1; d < kWarp; d <<= 1) {
+    unsigned long long o = __shfl_up_sync(0xffffffffu, v, d);
+    if (lane >= d) v += o;
+  }
+  return v;
+}
+
+// Exclusive block scan for <= 1024 threads; returns the total in *total.
+__device__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* total) {
+  __shared__ uint32_t warp_sums[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t x = v;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    uint32_t o = __shfl_up_sync(0xffffffffu, x, d);
+    if (lane >= d) x += o;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = (blockDim.x + 31) >> 5;
+    uint32_t w = lane < nw ? warp_sums[lane] : 0;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      uint32_t o = __shfl_up_sync(0xffffffffu, w, d);
+      if (lane >= d) w += o;
+    }
+    warp_sums[lane] = w;
+  }
+  __syncthreads();
+  const uint32_t before = warp ? warp_sums[warp - 1] : 0;
+  *total = warp_sums[((blockDim.x + 31) >> 5) - 1];
+  __syncthreads();
+  return before + x - v;
+}
+
+// ---------------------------------------------------------------------------
+// Binning.
+// ---------------------------------------------------------------------------
+template <typename CodeT>
+__global__ void quantize_kernel(const float* __restrict__ X, uint32_t rows, uint32_t cols,
+                                const float* __restrict__ cuts, const uint32_t* __restrict__ counts,
+                                uint32_t bins, CodeT* __restrict__ codes, uint32_t stride,
+                                uint32_t missing) {
+  const uint64_t total = uint64_t(rows) * stride;
+  for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < total;
+       i += uint64_t(gridDim.x) * blockDim.x) {
+    const uint32_t r = uint32_t(i / stride), c = uint32_t(i % stride);
+    uint32_t code = missing;
+    if (c < cols) {
+      const float v = X[size_t(r) * cols + c];
+      const uint32_t count = counts[c];
+      if (!isnan(v) && count) {
+        const float* fc = cuts + size_t(c) * bins;
+        uint32_t lo = 0, hi = count;
+        while (lo < hi) {
+          const uint32_t mid = (lo + hi) >> 1;
+          if (v >= __ldg(fc + mid)) lo = mid + 1;
+          else hi = mid;
+        }
+        code = lo < count - 1 ? lo : count - 1;
+      }
+    }
+    codes[i] = CodeT(code);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Gradients and exact power-of-two scales.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float2 gradient_pair(int objective, const float* __restrict__ margins,
+                                                float label, float weight, uint32_t row,
+                                                uint32_t groups, uint32_t k, float spw) {
+  const float pred = margins[size_t(row) * groups + k];
+  float w = weight, g = __fsub_rn(pred, label), h = 1.0f;
+  if (objective == kLogistic || objective == kLogitRaw) {
+    const float prob = __fdiv_rn(1.0f, __fadd_rn(1.0f, det_expf(-pred)));
+    w = __fmul_rn(w, label == 1.0f ? spw : 1.0f);
+    g = __fsub_rn(prob, label);
+    h = fmaxf(__fmul_rn(prob, __fsub_rn(1.0f, prob)), 1.0e-16f);
+  } else if (objective == kSoftprob || objective == kSoftmax) {
+    float mx = 0x1p-126f;
+    for (uint32_t j = 0; j < groups; ++j) mx = fmaxf(mx, margins[size_t(row) * groups + j]);
+    double denom = 0.0;
+    for (uint32_t j = 0; j < groups; ++j)
+      denom = __dadd_rn(denom, (double)det_expf(__fsub_rn(margins[size_t(row) * groups + j], mx)));
+    const float prob = __double2float_rn(__ddiv_rn((double)det_expf(__fsub_rn(pred, mx)), denom));
+    g = __fsub_rn(prob, uint32_t(label) == k ? 1.0f : 0.0f);
+    return make_float2(__fmul_rn(g, w), fmaxf(__fmul_rn(fabsf(g), w), 1.0e-16f));
+  }
+  return make_float2(__fmul_rn(g, w), __fmul_rn(h, w));
+}
+
+// Gradient pairs [group][row]; per (group, part) the largest magnitude.
+__global__ void gradient_kernel(int objective, const float* __restrict__ margins,
+                                const float* __restrict__ labels, const float* __restrict__ weights,
+                                uint32_t rows, uint32_t groups, float spw, float2* __restrict__ pairs,
+                                MassAccum* __restrict__ mass) {
+  const uint32_t k = blockIdx.y;
+  uint32_t mg = 0, mh = 0;
+  for (uint32_t r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
+    const float2 p = gradient_pair(objective, margins, labels[r], weights ? weights[r] : 1.0f, r,
+                                   groups, k, spw);
+    pairs[size_t(k) * rows + r] = p;
+    mg = max(mg, __float_as_uint(p.x) & 0x7fffffffu);
+    mh = max(mh, __float_as_uint(p.y) & 0x7fffffffu);
+  }
+  mg = __reduce_max_sync(0xffffffffu, mg);
+  mh = __reduce_max_sync(0xffffffffu, mh);
+  if ((threadIdx.x & 31) == 0) {
+    if (mg) atomicMax(&mass[k * 2].max_bits, mg);
+    if (mh) atomicMax(&mass[k * 2 + 1].max_bits, mh);
+  }
+}
+
+// Windowed exact sum: every magnitude is m * 2^s in units of 2^-149
+// (m < 2^24); terms are accumulated as floor(m * 2^(s - L)) in 128 bits with
+// L = max(s_max - 72, 0), so the sum of at most 2^32 terms cannot overflow.
+__device__ __forceinline__ uint32_t window_shift(uint32_t max_bits) {
+  const uint32_t e = max_bits >> 23;
+  const uint32_t smax = e ? e - 1 : 0;
+  return smax > 72 ? smax - 72 : 0;
+}
+
+__device__ __forceinline__ void add_term(uint32_t bits, uint32_t L, unsigned long long& lo,
+                                         unsigned long long& hi) {
+  const uint32_t e = (bits >> 23) & 255;
+  const unsigned long long m = (bits & 0x7fffffu) | (e ? 0x800000u : 0u);
+  const int s = int(e ? e - 1 : 0) - int(L);
+  unsigned long long tlo, thi;
+  if (s >= 64) {
+    tlo = 0;
+    thi = m << (s - 64);
+  } else if (s >= 0) {
+    tlo = m << s;
+    thi = s ? (m >> (64 - s)) : 0;
+  } else {
+    tlo = (-s) >= 24 ? 0 : (m >> (-s));
+    thi = 0;
+  }
+  const unsigned long long nlo = lo + tlo;
+  hi += thi + (nlo < lo ? 1 : 0);
+  lo = nlo;
+}
+
+__device__ __forceinline__ void atomic_add_u128(unsigned long long* lo, unsigned long long* hi,
+                                                unsigned long long vlo, unsigned long long vhi) {
+  const unsigned long long old = atomicAdd(lo, vlo);
+  const unsigned long long carry = (old + vlo < old) ? 1ull : 0ull;
+  if (vhi + carry) atomicAdd(hi, vhi + carry);
+}
+
+__global__ void mass_window_kernel(const float2* __restrict__ pairs, uint32_t rows,
+                                   MassAccum* __restrict__ mass) {
+  const uint32_t k = blockIdx.y;
+  const uint32_t Lg = window_shift(mass[k * 2].max_bits);
+  const uint32_t Lh = window_shift(mass[k * 2 + 1].max_bits);
+  unsigned long long glo = 0, ghi = 0, hlo = 0, hhi = 0;
+  const float2* p = pairs + size_t(k) * rows;
+  for (uint32_t r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
+    const float2 v = p[r];
+    add_term(__float_as_uint(v.x) & 0x7fffffffu, Lg, glo, ghi);
+    add_term(__float_as_uint(v.y) & 0x7fffffffu, Lh, hlo, hhi);
+  }
+  // Warp reduction of the 128-bit sums.
+#pragma unroll
+  for (int d = 16; d; d >>= 1) {
+    unsigned long long a = __shfl_down_sync(0xffffffffu, glo, d),
+                       b = __shfl_down_sync(0xffffffffu, ghi, d);
+    unsigned long long n = glo + a;
+    ghi += b + (n < glo);
+    glo = n;
+    a = __shfl_down_sync(0xffffffffu, hlo, d);
+    b = __shfl_down_sync(0xffffffffu, hhi, d);
+    n = hlo + a;
+    hhi += b + (n < hlo);
+    hlo = n;
+  }
+  if ((threadIdx.x & 31) == 0) {
+    if (glo | ghi) atomic_add_u128(&mass[k * 2].lo, &mass[k * 2].hi, glo, ghi);
+    if (hlo | hhi) atomic_add_u128(&mass[k * 2 + 1].lo, &mass[k * 2 + 1].hi, hlo, hhi);
+  }
+}
+
+__device__ __forceinline__ int bitlen128(unsigned long long lo, unsigned long long hi) {
+  return hi ? 128 - __clzll(hi) : (lo ? 64 - __clzll(lo) : 0);
+}
+
+__device__ __forceinline__ float scale_for(int bitlen_mass) {
+  const int e = bitlen_mass - 149 > 0 ? bitlen_mass - 149 : 0;
+  return __uint_as_float(uint32_t(62 - e + 127) << 23);
+}
+
+// One thread per (group, part). The windowed sum A satisfies
+// A * 2^L <= M < (A + n) * 2^L, so bitlen(M) = bitlen(A) + L whenever
+// A + n <= 2^bitlen(A); otherwise the exact fallback decides.
+__global__ void scales_kernel(MassAccum* mass, float2* scales, uint32_t groups,
+                              unsigned long long rows_total) {
+  const uint32_t i = threadIdx.x;
+  if (i >= groups * 2) return;
+  MassAccum& m = mass[i];
+  const uint32_t L = window_shift(m.max_bits);
+  const int bl = bitlen128(m.lo, m.hi);
+  bool decided = true;
+  if (L && bl) {
+    // A + n <= 2^bl ?
+    const unsigned long long lo = m.lo + rows_total, hi = m.hi + (m.lo + rows_total < m.lo ? 1 : 0);
+    const int bl2 = bitlen128(lo, hi);
+    const bool power_of_two = __popcll(lo) + __popcll(hi) == 1;
+    decided = bl2 == bl || (bl2 == bl + 1 && power_of_two);
+  }
+  m.fallback = decided ? 0u : 1u;
+  if (decided) {
+    const float s = scale_for(bl ? bl + int(L) : 0);
+    reinterpret_cast<float*>(scales)[i] = s;
+  }
+}
+
+// Exact fallback: 32-bit limb sums of m * 2^s (each addend < 2^32, so 64-bit
+// limb sums cannot overflow for fewer than 2^32 rows), carried afterwards.
+__global__ void mass_exact_kernel(const float2* __restrict__ pairs, uint32_t rows,
+                                  MassAccum* __restrict__ mass) {
+  const uint32_t k = blockIdx.y;
+  const bool need_g = mass[k * 2].fallback, need_h = mass[k * 2 + 1].fallback;
+  if (!need_g && !need_h) return;
+  __shared__ unsigned long long limbs[2][11];
+  if (threadIdx.x < 22) (&limbs[0][0])[threadIdx.x] = 0;
+  __syncthreads();
+  const float2* p = pairs + size_t(k) * rows;
+  for (uint32_t r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
+    const float2 v = p[r];
+    for (int part = 0; part < 2; ++part) {
+      if (!(part ? need_h : need_g)) continue;
+      const uint32_t bits = __float_as_uint(part ? v.y : v.x) & 0x7fffffffu;
+      const uint32_t e = bits >> 23;
+      const unsigned long long m = (bits & 0x7fffffu) | (e ? 0x800000u : 0u);
+      const uint32_t s = e ? e - 1 : 0, w = s / 32, b = s % 32;
+      const unsigned long long t = m << b;
+      if (t & 0xffffffffull) atomicAdd(&limbs[part][w], t & 0xffffffffull);
+      if (t >> 32) atomicAdd(&limbs[part][w + 1], t >> 32);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < 20) {
+    const int part = threadIdx.x / 10, w = threadIdx.x % 10;
+    if (limbs[part][w]) atomicAdd(&mass[k * 2 + part].exact[w], limbs[part][w]);
+  }
+}
+
+__global__ void scales_exact_kernel(MassAccum* mass, float2* scales, uint32_t groups) {
+  const uint32_t i = threadIdx.x;
+  if (i >= groups * 2 || !mass[i].fallback) return;
+  uint32_t limb[10];
+  unsigned long long carry = 0;
+  for (int w = 0; w < 10; ++w) {
+    const unsigned long long s = mass[i].exact[w] + carry;
+    limb[w] = uint32_t(s);
+    carry = s >> 32;
+  }
+  int bl = 0;
+  for (int w = 9; w >= 0; --w)
+    if (limb[w]) {
+      bl = w * 32 + 32 - __clz(limb[w]);
+      break;
+    }
+  reinterpret_cast<float*>(scales)[i] = scale_for(bl);
+}
+
+// ---------------------------------------------------------------------------
+// Base score: fixed-order binary64 sums of y*w and w over 1024-row chunks.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kBaseChunk = 1024;
+
+__global__ void base_chunk_kernel(int objective, const float* __restrict__ labels,
+                                  const float* __restrict__ weights, uint32_t rows, uint32_t k,
+                                  float spw, double* __restrict__ chunk_sums) {
+  __shared__ double sy[kBaseChunk], sw[kBaseChunk];
+  const uint32_t base = blockIdx.x * kBaseChunk;
+  for (uint32_t i = threadIdx.x; i < kBaseChunk; i += blockDim.x) {
+    const uint32_t r = base + i;
+    double yw = 0.0, ww = 0.0;
+    if (r < rows) {
+      float y = labels[r], w = weights ? weights[r] : 1.0f;
+      if (objective == kLogistic || objective == kLogitRaw) w = __fmul_rn(w, y == 1.0f ? spw : 1.0f);
+      if (objective == kSoftprob || objective == kSoftmax) y = uint32_t(y) == k ? 1.0f : 0.0f;
+      yw = __dmul_rn((double)y, (double)w);
+      ww = (double)w;
+    }
+    sy[i] = yw;
+    sw[i] = ww;
+  }
+  __syncthreads();
+  for (uint32_t h = kBaseChunk / 2; h; h >>= 1) {
+    for (uint32_t i = threadIdx.x; i < h; i += blockDim.x) {
+      sy[i] = __dadd_rn(sy[i], sy[i + h]);
+      sw[i] = __dadd_rn(sw[i], sw[i + h]);
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    chunk_sums[blockIdx.x * 2] = sy[0];
+    chunk_sums[blockIdx.x * 2 + 1] = sw[0];
+  }
+}
+
+__global__ void fill_margins_kernel(float* margins, const float* base, uint32_t rows,
+                                    uint32_t groups) {
+  const uint64_t total = uint64_t(rows) * groups;
+  for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < total;
+       i += uint64_t(gridDim.x) * blockDim.x)
+    margins[i] = base[i % groups];
+}
+
+// ---------------------------------------------------------------------------
+// Tree driver kernels.
+// ---------------------------------------------------------------------------
+struct HistArgs {
+  Ellpack e;
+  const float2* pairs;
+  const float2* scale;
+  const uint32_t* rows;
+  const DriverState* state;
+  const uint32_t* tile_offset;
+  const uint32_t* built_left;
+  const uint32_t* seg_begin;
+  const uint32_t* seg_count;
+  longlong2* built;
+  uint32_t fg, ngroups;
+};
+
+// Histograms of the built child of every node pair (or of the root). Each CTA
+// walks a contiguous run of (feature group, pair, row tile) work items,
+// accumulating exact int64 sums in shared memory, and flushes them with
+// global 64-bit atomics when the (group, pair) changes.
+template <typename CodeT, bool kUnitH, bool kRoot>
+__global__ void __launch_bounds__(512) hist_kernel(HistArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const DriverState st = *a.state;
+  if (!st.frontier || !st.total_tiles) return;
+  const uint32_t B = a.e.bins, B1 = B + 1, C = a.e.cols;
+  const uint32_t npairs = kRoot ? 1u : st.pairs;
+  const uint32_t total_tiles = st.total_tiles;
+  const uint64_t items = uint64_t(total_tiles) * a.ngroups;
+  const uint64_t per = (items + gridDim.x - 1) / gridDim.x;
+  uint64_t it = blockIdx.x * per;
+  const uint64_t end = min(items, it + per);
+  if (it >= end) return;
+  unsigned long long* sg = reinterpret_cast<unsigned long long*>(smem);
+  unsigned int* sc = reinterpret_cast<unsigned int*>(smem + size_t(a.fg) * B1 * 8);
+  unsigned long long* sh = reinterpret_cast<unsigned long long*>(smem + size_t(a.fg) * B1 * 8);
+  const float2 s = *a.scale;
+  const long long qh_unit = __float2ll_rn(s.y);
+  const CodeT* __restrict__ codes = static_cast<const CodeT*>(a.e.codes);
+  const uint32_t stride = a.e.stride;
+  const uint32_t miss = a.e.missing;
+  constexpr uint32_t kPerVec = 16 / sizeof(CodeT);
+
+  int64_t cur_group = -1, cur_pair = -1;
+  auto zero = [&](uint32_t nf) {
+    const uint32_t n = nf * B1;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+      sg[i] = 0;
+      if (kUnitH) sc[i] = 0;
+      else sh[i] = 0;
+    }
+  };
+  auto flush = [&](uint32_t group, uint32_t pair) {
+    const uint32_t f0 = group * a.fg, nf = min(a.fg, C - f0);
+    longlong2* dst = a.built + (size_t(pair) * C + f0) * B1;
+    const uint32_t n = nf * B1;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+      const unsigned long long g = sg[i];
+      const unsigned long long h = kUnitH ? (unsigned long long)sc[i] * (unsigned long long)qh_unit : sh[i];
+      if (g | (kUnitH ? (unsigned long long)sc[i] : h)) {
+        atomicAdd(reinterpret_cast<unsigned long long*>(&dst[i].x), g);
+        atomicAdd(reinterpret_cast<unsigned long long*>(&dst[i].y), h);
+      }
+    }
+  };
+
+  for (; it < end; ++it) {
+    const uint32_t group = uint32_t(it / total_tiles), t = uint32_t(it % total_tiles);
+    uint32_t pair = 0;
+    if (!kRoot) {
+      uint32_t lo = 0, hi = npairs;
+      while (hi - lo > 1) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (a.tile_offset[mid] <= t) lo = mid;
+        else hi = mid;
+      }
+      pair = lo;
+    }
+    if (int64_t(group) != cur_group || int64_t(pair) != cur_pair) {
+      if (cur_group >= 0) {
+        __syncthreads();
+        flush(uint32_t(cur_group), uint32_t(cur_pair));
+      }
+      __syncthreads();
+      zero(min(a.fg, C - group * a.fg));
+      __syncthreads();
+      cur_group = group;
+      cur_pair = pair;
+    }
+    const uint32_t slot = kRoot ? 0u : 2u * pair + (a.built_left[pair] ? 0u : 1u);
+    const uint32_t seg0 = a.seg_begin[slot], segn = a.seg_count[slot];
+    const uint32_t begin = seg0 + (t - (kRoot ? 0u : a.tile_offset[pair])) * kTileRows;
+    const uint32_t cnt = min(kTileRows, seg0 + segn - begin);
+    const uint32_t f0 = group * a.fg, nf = min(a.fg, C - f0);
+    const uint32_t nvec = (nf + kPerVec - 1) / kPerVec;
+    for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) {
+      const uint32_t row = kRoot ? begin + i : __ldg(a.rows + begin + i);
+      const float2 gp = __ldg(a.pairs + row);
+      const unsigned long long qg = (unsigned long long)__float2ll_rn(__fmul_rn(gp.x, s.x));
+      const unsigned long long qh =
+          kUnitH ? 0ull : (unsigned long long)__float2ll_rn(__fmul_rn(gp.y, s.y));
+      const uint4* rp = reinterpret_cast<const uint4*>(codes + size_t(row) * stride + f0);
+      for (uint32_t v = 0; v < nvec; ++v) {
+        const uint4 w = __ldg(rp + v);
+        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (uint32_t j = 0; j < kPerVec; ++j) {
+          const uint32_t f = v * kPerVec + j;
+          if (f < nf) {
+            uint32_t code;
+            if (sizeof(CodeT) == 1) code = (words[j >> 2] >> ((j & 3) * 8)) & 0xffu;
+            else code = (words[j >> 1] >> ((j & 1) * 16)) & 0xffffu;
+            const uint32_t bin = code == miss ? B : code;
+            atomicAdd(&sg[f * B1 + bin], qg);
+            if (kUnitH) atomicAdd(&sc[f * B1 + bin], 1u);
+            else atomicAdd(&sh[f * B1 + bin], qh);
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  flush(uint32_t(cur_group), uint32_t(cur_pair));
+}
+
+struct EvalArgs {
+  Ellpack e;
+  SplitMath m;
+  const float2* scale;
+  const DriverState* state;
+  uint32_t depth;
+  const longlong2* built;
+  const longlong2* prev_bank;
+  longlong2* bank;
+  const uint32_t* parent_slot;
+  const uint32_t* built_left;
+  const long long* sums;
+  DevSplit* cand;
+  unsigned long long* keys;
+  bool write_bank;
+};
+
+struct Candidate {
+  float gain, lw, rw, threshold;
+  uint32_t order;
+  int32_t split_bin;
+  uint32_t default_left;
+  double LH, RH;
+  long long lg, lh, rg, rh;
+};
+
+// One warp per (node, feature): the node's histogram (the built child, or the
+// parent minus the built sibling), a warp-shuffle prefix scan over the bins,
+// forward candidates (missing right) and, when the node has missing rows,
+// backward candidates (missing left), each scored in binary64 with the
+// reference's rounding points; the best candidate by (gain, scan order).
+__global__ void __launch_bounds__(256) eval_kernel(EvalArgs a) {
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t nslots = a.state->frontier;
+  const uint32_t C = a.e.cols, B = a.e.bins, B1 = B + 1;
+  const uint64_t total = uint64_t(nslots) * C;
+  const uint64_t nwarps = uint64_t(gridDim.x) * (blockDim.x >> 5);
+  const float2 sc = *a.scale;
+  int eg, eh;
+  frexpf(sc.x, &eg);
+  frexpf(sc.y, &eh);
+  const double inv_g = ldexp(1.0, -(eg - 1)), inv_h = ldexp(1.0, -(eh - 1));
+  for (uint64_t w = blockIdx.x * uint64_t(blockDim.x >> 5) + (threadIdx.x >> 5); w < total; w += nwarps) {
+    const uint32_t slot = uint32_t(w / C), f = uint32_t(w % C);
+    const longlong2* bptr;
+    const longlong2* pptr = nullptr;
+    if (a.depth == 0) {
+      bptr = a.built + size_t(f) * B1;
+    } else {
+      const uint32_t p = slot >> 1;
+      const uint32_t built_side = a.built_left[p] ? 0u : 1u;
+      bptr = a.built + (size_t(p) * C + f) * B1;
+      if ((slot & 1u) != built_side) pptr = a.prev_bank + (size_t(a.parent_slot[p]) * C + f) * B1;
+    }
+    // Lane `lane` holds bins [8 lane, 8 lane + 8).
+    long long vg[8], vh[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t b = lane * 8 + j;
+      long long g = 0, h = 0;
+      if (b < B) {
+        const longlong2 x = bptr[b];
+        g = x.x;
+        h = x.y;
+        if (pptr) {
+          const longlong2 y = pptr[b];
+          g = (long long)((unsigned long long)y.x - (unsigned long long)g);
+          h = (long long)((unsigned long long)y.y - (unsigned long long)h);
+        }
+      }
+      vg[j] = g;
+      vh[j] = h;
+    }
+    long long missg, missh;
+    {
+      const longlong2 x = bptr[B];
+      missg = x.x;
+      missh = x.y;
+      if (pptr) {
+        const longlong2 y = pptr[B];
+        missg = (long long)((unsigned long long)y.x - (unsigned long long)missg);
+        missh = (long long)((unsigned long long)y.y - (unsigned long long)missh);
+      }
+    }
+    if (a.write_bank) {
+      longlong2* dst = a.bank + (size_t(slot) * C + f) * B1;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t b = lane * 8 + j;
+        if (b < B) dst[b] = make_longlong2(vg[j], vh[j]);
+      }
+      if (lane == 0) dst[B] = make_longlong2(missg, missh);
+    }
+    // Lane-local inclusive prefix, then the warp scan of lane totals.
+    unsigned long long pg[8], ph[8];
+    unsigned long long accg = 0, acch = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      accg += (unsigned long long)vg[j];
+      acch += (unsigned long long)vh[j];
+      pg[j] = accg;
+      ph[j] = acch;
+    }
+    const unsigned long long incg = warp_scan_u64(accg, lane), inch = warp_scan_u64(acch, lane);
+    const unsigned long long exg = incg - accg, exh = inch - acch;
+    const unsigned long long Pg = shfl_u64(incg, 31), Ph = shfl_u64(inch, 31);
+    unsigned long long Tg, Th;
+    if (a.depth == 0) {
+      Tg = Pg + (unsigned long long)missg;
+      Th = Ph + (unsigned long long)missh;
+    } else {
+      Tg = (unsigned long long)a.sums[slot * 2];
+      Th = (unsigned long long)a.sums[slot * 2 + 1];
+    }
+    const unsigned long long Mg = Tg - Pg, Mh = Th - Ph;
+    const double TG = stat_value((long long)Tg, inv_g), TH = stat_value((long long)Th, inv_h);
+    const float wparent = leaf_weight(TG, TH, a.m);
+    const float parent_gain = node_gain(TG, TH, wparent, a.m);
+    const uint32_t count = a.e.counts[f];
+    const float* fc = a.e.cuts + size_t(f) * B;
+
+    Candidate best;
+    best.gain = -CUDART_INF_F;
+    best.order = 0xffffffffu;
+    auto consider = [&](unsigned long long lg, unsigned long long lh, unsigned long long rg,
+                        unsigned long long rh, uint32_t order, float threshold, int32_t sbin,
+                        uint32_t dl) {
+      const double LG = stat_value((long long)lg, inv_g), LH = stat_value((long long)lh, inv_h);
+      const double RG = stat_value((long long)rg, inv_g), RH = stat_value((long long)rh, inv_h);
+      if (!valid_hessian(LH, a.m) || !valid_hessian(RH, a.m)) return;
+      const float lw = leaf_weight(LG, LH, a.m), rw = leaf_weight(RG, RH, a.m);
+      const float gain =
+          __fsub_rn(__fadd_rn(node_gain(LG, LH, lw, a.m), node_gain(RG, RH, rw, a.m)), parent_gain);
+      if (!(gain > -CUDART_INF_F)) return;
+      if (gain > best.gain || (gain == best.gain && order < best.order)) {
+        best.gain = gain;
+        best.order = order;
+        best.lw = lw;
+        best.rw = rw;
+        best.threshold = threshold;
+        best.split_bin = sbin;
+        best.default_left = dl;
+        best.LH = LH;
+        best.RH = RH;
+        best.lg = (long long)lg;
+        best.lh = (long long)lh;
+        best.rg = (long long)rg;
+        best.rh = (long long)rh;
+      }
+    };
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t b = lane * 8 + j;
+      if (b < count) {
+        const unsigned long long Lg = exg + pg[j], Lh = exh + ph[j];
+        consider(Lg, Lh, Tg - Lg, Th - Lh, b, fc[b], int32_t(b), 0u);
+      }
+    }
+    if (Mg != 0 || Mh != 0) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t b = lane * 8 + j;
+        if (b < count) {
+          const unsigned long long Rg = Pg - (exg + pg[j] - (unsigned long long)vg[j]);
+          const unsigned long long Rh = Ph - (exh + ph[j] - (unsigned long long)vh[j]);
+          consider(Tg - Rg, Th - Rh, Rg, Rh, count + (count - 1 - b),
+                   b == 0 ? a.e.minima[f] : fc[b - 1], int32_t(b) - 1, 1u);
+        }
+      }
+    }
+    // Warp argmax by (gain, order).
+    float bg = best.gain;
+    uint32_t bo = best.order, bl = lane;
+#pragma unroll
+    for (int d = 16; d; d >>= 1) {
+      const float og = __shfl_xor_sync(0xffffffffu, bg, d);
+      const uint32_t oo = __shfl_xor_sync(0xffffffffu, bo, d);
+      const uint32_t ol = __shfl_xor_sync(0xffffffffu, bl, d);
+      const bool take = (og > bg) || (og == bg && oo < bo) || (og == bg && oo == bo && ol < bl);
+      if (take) {
+        bg = og;
+        bo = oo;
+        bl = ol;
+      }
+    }
+    const bool any = bg > -CUDART_INF_F;
+    if ((any && lane == bl) || (!any && lane == 0)) {
+      DevSplit r;
+      r.total_g = __double2float_rn(TG);
+      r.total_h = __double2float_rn(TH);
+      r.parent_weight = wparent;
+      r.applied_parent_weight = 0.0f;
+      r.applied_parent_hessian = 0.0f;
+      r.pad = 0;
+      if (any) {
+        r.gain = best.gain;
+        r.threshold = best.threshold;
+        r.feature = int32_t(f);
+        r.split_bin = best.split_bin;
+        r.default_left = best.default_left;
+        r.left_weight = best.lw;
+        r.right_weight = best.rw;
+        r.left_h = __double2float_rn(best.LH);
+        r.right_h = __double2float_rn(best.RH);
+        r.order = best.order;
+        r.left_g = best.lg;
+        r.left_hs = best.lh;
+        r.right_g = best.rg;
+        r.right_hs = best.rh;
+      } else {
+        r.gain = -CUDART_INF_F;
+        r.threshold = 0.0f;
+        r.feature = -1;
+        r.split_bin = -1;
+        r.default_left = 0;
+        r.left_weight = wparent;
+        r.right_weight = wparent;
+        r.left_h = 0.0f;
+        r.right_h = 0.0f;
+        r.order = 0xffffffffu;
+        r.left_g = r.left_hs = r.right_g = r.right_hs = 0;
+      }
+      a.cand[size_t(slot) * C + f] = r;
+      const unsigned long long key =
+          ((unsigned long long)gain_key(r.gain) << 32) | (0xffffffffu - f);
+      atomicMax(a.keys + slot, key);
+    }
+  }
+}
+
+struct ControlArgs {
+  Ellpack e;
+  TreeParams tp;
+  SplitMath m;
+  const float2* scale;
+  DriverState* state;
+  uint32_t depth;
+  const uint32_t* ids;
+  const long long* sums;
+  const uint32_t* seg_begin;
+  const uint32_t* seg_count;
+  const DevSplit* cand;
+  const unsigned long long* keys;
+  unsigned long long* next_keys;
+  uint32_t* next_ids;
+  long long* next_sums;
+  uint32_t* parent_slot;
+  uint32_t* mode;
+  float* slot_leaf;
+  uint32_t* cursor_l;
+  uint32_t* cursor_r;
+  uint32_t* ptile_offset;
+  DevNode* nodes;
+  uint32_t node_capacity;
+};
+
+// Per-node selection (first feature with the largest gain), the reference's
+// expansion rule and node numbering, the node table and the next frontier.
+__global__ void __launch_bounds__(1024) control_kernel(ControlArgs a) {
+  __shared__ uint32_t s_node_count, s_error;
+  const uint32_t n = a.state->frontier;
+  const uint32_t s = threadIdx.x;
+  if (threadIdx.x == 0) {
+    s_node_count = a.state->node_count;
+    s_error = a.state->error;
+  }
+  __syncthreads();
+  DevSplit best{};
+  uint32_t expand = 0;
+  if (s < n && !s_error) {
+    const unsigned long long key = a.keys[s];
+    const uint32_t f = 0xffffffffu - uint32_t(key & 0xffffffffu);
+    best = a.cand[size_t(s) * a.e.cols + (f < a.e.cols ? f : 0u)];
+    if (best.feature >= 0) {
+      const float2 sc = *a.scale;
+      int eg, eh;
+      frexpf(sc.x, &eg);
+      frexpf(sc.y, &eh);
+      const double inv_g = ldexp(1.0, -(eg - 1)), inv_h = ldexp(1.0, -(eh - 1));
+      const double G = __dadd_rn(stat_value(best.left_g, inv_g), stat_value(best.right_g, inv_g));
+      const double H = __dadd_rn(stat_value(best.left_hs, inv_h), stat_value(best.right_hs, inv_h));
+      double value = 0.0;
+      if (H > 0.0) {
+        const double t = fabs(G) <= a.m.alpha ? 0.0 : (G < 0.0 ? __dadd_rn(G, a.m.alpha) : __dsub_rn(G, a.m.alpha));
+        value = __ddiv_rn(-t, __dadd_rn(H, a.m.lambda));
+        const double limit = fabs((double)a.tp.max_delta_step);
+        if (limit != 0.0 && fabs(value) > limit) value = copysign(limit, value);
+      }
+      best.applied_parent_weight = __double2float_rn(value);
+      best.applied_parent_hessian = __double2float_rn(H);
+    }
+    expand = best.feature >= 0 && best.gain > 1.0e-6f && best.gain >= a.tp.min_split_loss;
+  }
+  uint32_t total_expand;
+  const uint32_t sel = block_exclusive_scan(expand, &total_expand);
+  const uint32_t node_count = s_node_count;
+  const bool overflow = node_count + 2ull * total_expand > a.node_capacity;
+  const bool terminal = a.depth + 1 >= a.tp.max_depth;
+  const float eta = a.tp.eta;
+  if (s < n && !s_error && !overflow) {
+    const uint32_t id = a.ids[s];
+    DevNode node = a.nodes[id];
+    node.flags |= 1u;
+    node.cover = best.total_h;
+    if (id == 0) {
+      node.leaf = __fmul_rn(best.parent_weight, eta);
+      node.base_weight = best.parent_weight;
+    }
+    if (expand) {
+      const uint32_t left = node_count + 2 * sel;
+      node.left = int32_t(left);
+      node.right = int32_t(left + 1);
+      node.feature = best.feature;
+      node.split_bin = best.split_bin;
+      node.default_left = best.default_left;
+      node.threshold = best.threshold;
+      node.gain = best.gain;
+      node.cover = best.applied_parent_hessian;
+      node.base_weight = best.applied_parent_weight;
+      node.flags |= 2u;
+      const float ll = __fmul_rn(best.left_weight, eta), rl = __fmul_rn(best.right_weight, eta);
+      DevNode c{};
+      c.left = c.right = c.feature = -1;
+      c.split_bin = -1;
+      c.parent = int32_t(id);
+      c.leaf = ll;
+      c.cover = best.left_h;
+      c.base_weight = ll;
+      a.nodes[left] = c;
+      c.leaf = rl;
+      c.cover = best.right_h;
+      c.base_weight = rl;
+      a.nodes[left + 1] = c;
+      a.mode[s] = terminal ? 2u : 1u;
+      a.slot_leaf[2 * s] = ll;
+      a.slot_leaf[2 * s + 1] = rl;
+      if (!terminal) {
+        a.next_ids[2 * sel] = left;
+        a.next_ids[2 * sel + 1] = left + 1;
+        a.next_sums[4 * sel] = best.left_g;
+        a.next_sums[4 * sel + 1] = best.left_hs;
+        a.next_sums[4 * sel + 2] = best.right_g;
+        a.next_sums[4 * sel + 3] = best.right_hs;
+        a.parent_slot[sel] = s;
+        a.next_keys[2 * sel] = 0;
+        a.next_keys[2 * sel + 1] = 0;
+      }
+    } else {
+      a.mode[s] = 0u;
+      a.slot_leaf[2 * s] = node.leaf;
+    }
+    a.nodes[id] = node;
+    a.cursor_l[s] = a.seg_begin[s];
+    a.cursor_r[s] = a.seg_begin[s] + a.seg_count[s];
+  }
+  const uint32_t tiles = (s < n) ? (a.seg_count[s] + kTileRows - 1) / kTileRows : 0u;
+  uint32_t total_tiles;
+  const uint32_t off = block_exclusive_scan(tiles, &total_tiles);
+  if (s < n) a.ptile_offset[s] = off;
+  if (threadIdx.x == 0) {
+    if (s_error || overflow) {
+      a.state->error = s_error ? s_error : kErrCapacity;
+      a.state->pad0 = 0;
+      a.state->pad1 = 0;
+    } else {
+      a.state->node_count = node_count + 2 * total_expand;
+      a.state->pad0 = total_tiles;                        // partition tiles
+      a.state->pad1 = terminal ? 0u : 2u * total_expand;  // next frontier
+    }
+    a.ptile_offset[n] = total_tiles;
+  }
+}
+
+struct PartArgs {
+  Ellpack e;
+  const DriverState* state;
+  const uint32_t* ids;
+  const DevNode* nodes;
+  const uint32_t* seg_begin;
+  const uint32_t* seg_count;
+  const uint32_t* ptile_offset;
+  const uint32_t* mode;
+  const float* slot_leaf;
+  const uint32_t* rows;
+  uint32_t* rows_next;
+  uint32_t* cursor_l;
+  uint32_t* cursor_r;
+  float* margins;
+  uint32_t groups, group;
+  bool root;
+};
+
+// Rows of every frontier node: nodes that stop add their leaf to the row's
+// margin, nodes split at the last level add the child leaf, other split nodes
+// scatter their rows to the two children (left block from the segment start,
+// right block from the segment end).
+template <typename CodeT>
+__global__ void __launch_bounds__(256) partition_kernel(PartArgs a) {
+  const DriverState st = *a.state;
+  if (!st.frontier || st.error) return;
+  const uint32_t n = st.frontier, ptiles = st.pad0;
+  const CodeT* __restrict__ codes = static_cast<const CodeT*>(a.e.codes);
+  const uint32_t lane = threadIdx.x & 31;
+  for (uint32_t t = blockIdx.x; t < ptiles; t += gridDim.x) {
+    uint32_t lo = 0, hi = n;
+    while (hi - lo > 1) {
+      const uint32_t mid = (lo + hi) >> 1;
+      if (a.ptile_offset[mid] <= t) lo = mid;
+      else hi = mid;
+    }
+    const uint32_t s = lo;
+    const uint32_t seg0 = a.seg_begin[s], segn = a.seg_count[s];
+    const uint32_t begin = seg0 + (t - a.ptile_offset[s]) * kTileRows;
+    const uint32_t cnt = min(kTileRows, seg0 + segn - begin);
+    const uint32_t md = a.mode[s];
+    const DevNode node = a.nodes[a.ids[s]];
+    const float leaf_l = a.slot_leaf[2 * s], leaf_r = a.slot_leaf[2 * s + 1];
+    const uint32_t rounded = (cnt + 31) & ~31u;
+    for (uint32_t i = threadIdx.x; i < rounded; i += blockDim.x) {
+      const bool valid = i < cnt;
+      const uint32_t row = valid ? (a.root ? begin + i : a.rows[begin + i]) : 0u;
+      if (md == 0) {
+        if (valid) {
+          float* m = a.margins + size_t(row) * a.groups + a.group;
+          *m = __fadd_rn(*m, leaf_l);
+        }
+        continue;
+      }
+      bool left = false;
+      if (valid) {
+        const uint32_t code = codes[size_t(row) * a.e.stride + uint32_t(node.feature)];
+        left = code == a.e.missing ? node.default_left != 0u : int32_t(code) <= node.split_bin;
+      }
+      if (md == 2) {
+        if (valid) {
+          float* m = a.margins + size_t(row) * a.groups + a.group;
+          *m = __fadd_rn(*m, left ? leaf_l : leaf_r);
+        }
+        continue;
+      }
+      const uint32_t lmask = __ballot_sync(0xffffffffu, valid && left);
+      const uint32_t rmask = __ballot_sync(0xffffffffu, valid && !left);
+      uint32_t lbase = 0, rbase = 0;
+      if (lane == 0) {
+        if (lmask) lbase = atomicAdd(a.cursor_l + s, __popc(lmask));
+        if (rmask) rbase = atomicSub(a.cursor_r + s, __popc(rmask)) - __popc(rmask);
+      }
+      lbase = __shfl_sync(0xffffffffu, lbase, 0);
+      rbase = __shfl_sync(0xffffffffu, rbase, 0);
+      const uint32_t below = (1u << lane) - 1u;
+      if (valid) {
+        if (left) a.rows_next[lbase + __popc(lmask & below)] = row;
+        else a.rows_next[rbase + __popc(rmask & below)] = row;
+      }
+    }
+  }
+}
+
+// Local child counts of split nodes, [slot][left, right].
+__global__ void counts_kernel(const DriverState* state, const uint32_t* seg_begin,
+                              const uint32_t* seg_count, const uint32_t* mode,
+                              const uint32_t* cursor_l, uint32_t* counts) {
+  const uint32_t n = state->frontier;
+  for (uint32_t s = threadIdx.x; s < kMaxFrontier; s += blockDim.x) {
+    uint32_t l = 0, r = 0;
+    if (s < n && mode[s] == 1u) {
+      l = cursor_l[s] - seg_begin[s];
+      r = seg_count[s] - l;
+    }
+    counts[2 * s] = l;
+    counts[2 * s + 1] = r;
+  }
+}
+
+struct PlanArgs {
+  DriverState* state;
+  uint32_t next_depth;
+  const uint32_t* parent_slot;
+  const uint32_t* seg_begin_cur;
+  const uint32_t* counts_local;
+  const uint32_t* counts_global;
+  uint32_t* seg_begin;
+  uint32_t* seg_count;
+  uint32_t* built_left;
+  uint32_t* tile_offset;
+};
+
+// Next level: child segments, the smaller child of each pair to build (by
+// the counts over all ranks; ties build the left child,
+// kernels/boost.metal:672) and the row tiles of the built children.
+__global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
+  const DriverState st = *a.state;
+  const uint32_t next = st.error ? 0u : st.pad1;
+  const uint32_t pairs = next / 2;
+  const uint32_t p = threadIdx.x;
+  uint32_t tiles = 0;
+  if (p < pairs) {
+    const uint32_t s = a.parent_slot[p];
+    const uint32_t begin = a.seg_begin_cur[s];
+    const uint32_t nl = a.counts_local[2 * s], nr = a.counts_local[2 * s + 1];
+    const uint32_t gl = a.counts_global[2 * s], gr = a.counts_global[2 * s + 1];
+    a.seg_begin[2 * p] = begin;
+    a.seg_count[2 * p] = nl;
+    a.seg_begin[2 * p + 1] = begin + nl;
+    a.seg_count[2 * p + 1] = nr;
+    const bool bl = gl <= gr;
+    a.built_left[p] = bl ? 1u : 0u;
+    tiles = ((bl ? nl : nr) + kTileRows - 1) / kTileRows;
+  }
+  uint32_t total;
+  const uint32_t off = block_exclusive_scan(tiles, &total);
+  if (p < pairs) a.tile_offset[p] = off;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    a.tile_offset[pairs] = total;
+    a.state->frontier = next;
+    a.state->depth = a.next_depth;
+    a.state->pairs = pairs;
+    a.state->total_tiles = total;
+  }
+}
+
+__global__ void init_tree_kernel(DriverState* state, uint32_t rows, uint32_t* ids,
+                                 long long* sums, uint32_t* seg_begin, uint32_t* seg_count,
+                                 uint32_t* tile_offset, uint32_t* built_left,
+                                 unsigned long long* keys, DevNode* nodes) {
+  const uint32_t tiles = (rows + kTileRows - 1) / kTileRows;
+  DriverState s{};
+  s.node_count = 1;
+  s.frontier = 1;
+  s.pairs = 1;
+  s.total_tiles = tiles;
+  *state = s;
+  ids[0] = 0;
+  sums[0] = 0;
+  sums[1] = 0;
+  seg_begin[0] = 0;
+  seg_count[0] = rows;
+  tile_offset[0] = 0;
+  tile_offset[1] = tiles;
+  built_left[0] = 1;
+  keys[0] = 0;
+  DevNode root{};
+  root.left = root.right = root.parent = root.feature = -1;
+  root.split_bin = -1;
+  nodes[0] = root;
+}
+
+// ---------------------------------------------------------------------------
+// Prediction from raw features (x < threshold goes left, NaN takes the
+// default direction; kernels/boost.metal:1325-1329, 1738-1765).
+// ---------------------------------------------------------------------------
+__global__ void predict_kernel(const float* __restrict__ X, uint32_t rows, uint32_t cols,
+                               const DevNode* __restrict__ nodes, const uint32_t* tree_begin,
+                               const uint32_t* tree_group, uint32_t trees, const float* base,
+                               uint32_t groups, float* out) {
+  for (uint32_t r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
+    const float* x = X + size_t(r) * cols;
+    for (uint32_t k = 0; k < groups; ++k) {
+      float sum = base[k];
+      for (uint32_t t = 0; t < trees; ++t) {
+        if (tree_group[t] != k) continue;
+        const DevNode* tn = nodes + tree_begin[t];
+        int32_t n = 0;
+        while (tn[n].left >= 0) {
+          const float v = x[tn[n].feature];
+          const bool left = isnan(v) ? tn[n].default_left != 0u : v < tn[n].threshold;
+          n = left ? tn[n].left : tn[n].right;
+        }
+        sum = __fadd_rn(sum, tn[n].leaf);
+      }
+      out[size_t(r) * groups + k] = sum;
+    }
+  }
+}
+
+// Output transforms (kernels/boost.metal:1855-1885) with det_expf.
+__global__ void transform_kernel(int objective, float* v, uint32_t rows, uint32_t groups) {
+  for (uint32_t r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
+    float* x = v + size_t(r) * groups;
+    if (objective == kSoftprob) {
+      float mx = -CUDART_INF_F, denom = 0.0f;
+      for (uint32_t k = 0; k < groups; ++k) mx = fmaxf(mx, x[k]);
+      for (uint32_t k = 0; k < groups; ++k) denom = __fadd_rn(denom, det_expf(__fsub_rn(x[k], mx)));
+      for (uint32_t k = 0; k < groups; ++k) x[k] = __fdiv_rn(det_expf(__fsub_rn(x[k], mx)), denom);
+    } else if (objective == kSoftmax) {
+      uint32_t best = 0;
+      for (uint32_t k = 1; k < groups; ++k)
+        if (x[k] > x[best]) best = k;
+      x[0] = float(best);
+    } else if (objective == kLogistic) {
+      for (uint32_t k = 0; k < groups; ++k)
+        x[k] = __fdiv_rn(1.0f, __fadd_rn(1.0f, det_expf(-x[k])));
+    }
+  }
+}
+
+int grid_for(uint64_t work, int threads, int cap = 148 * 16) {
+  const uint64_t blocks = (work + threads - 1) / threads;
+  return int(std::max<uint64_t>(1, std::min<uint64_t>(blocks, uint64_t(cap))));
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Launchers.
+// ---------------------------------------------------------------------------
+void launch_quantize(const float* X, uint32_t rows, uint32_t cols, const float* cuts,
+                     const uint32_t* counts, uint32_t bins, void* codes, uint32_t stride,
+                     uint32_t bytes_per_code, uint32_t missing, cudaStream_t stream) {
+  const uint64_t total = uint64_t(rows) * stride;
+  if (!total) return;
+  const int threads = 256, blocks = grid_for(total, threads, 148 * 32);
+  if (bytes_per_code == 1)
+    quantize_kernel<uint8_t><<<blocks, threads, 0, stream>>>(
+        X, rows, cols, cuts, counts, bins, static_cast<uint8_t*>(codes), stride, missing);
+  else
+    quantize_kernel<uint16_t><<<blocks, threads, 0, stream>>>(
+        X, rows, cols, cuts, counts, bins, static_cast<uint16_t*>(codes), stride, missing);
+  XGBB_CUDA(cudaGetLastError());
+}
+
+void launch_gradients(int objective, const float* margins, const float* labels,
+                      const float* weights, uint32_t rows, uint32_t groups, float spw,
+                      float2* pairs, MassAccum* mass, cudaStream_t stream) {
+  if (!rows) return;
+  const int threads = 256;
+  dim3 grid(grid_for(rows, threads, 148 * 4), groups);
+  gradient_kernel<<<grid, threads, 0, stream>>>(objective, margins, labels, weights, rows, groups,
+                                                spw, pairs, mass);
+  XGBB_CUDA(cudaGetLastError());
+}
+
+void launch_mass_window(const float2* pairs, uint32_t rows, uint32_t groups, MassAccum* mass,
+                        cudaStream_t stream) {
+  if (!rows) return;
+  const int threads = 256;
+  dim3 grid(grid_for(rows, threads, 148 * 4), groups);
+  mass_window_kernel<<<grid, threads, 0, stream>>>(pairs, rows, mass);
+  XGBB_CUDA(cudaGetLastError());
+}
+
+void launch_scales(const float2*, uint32_t, uint32_t groups, MassAccum* mass, float2* scales,
+                   unsigned long long rows_total, bool, cudaStream_t stream) {
+  scales_kernel<<<1, 64 * ((2 * groups + 63) / 64), 0, stream>>>(mass, scales, groups, rows_total);
+  XGBB_CUDA(cudaGetLastError());
+}
+
+void launch_mass_exact(const float2* pairs, uint32_t rows, uint32_t groups, MassAccum* mass,
+                       cudaStream_t stream) {
+  if (!rows) return;
+  const int threads = 256;
+  dim3 grid(grid_for(rows, threads, 148 * 4), groups);
+  mass_exact_kernel<<<grid, threads, 0, stream>>>(pairs, rows, mass);
+  XGBB_CUDA(cudaGetLastError());
+}
+
+void launch_scales_exact(uint32_t groups, MassAccum* mass, float2* scales, cudaStream_t stream) {
+  scales_exact_kernel<<<1, 64 * ((2 * groups + 63) / 64), 0, stream>>>(mass, scales, groups);
+  XGBB_CUDA(cudaGetLastError());
+}
+
+void launch_base_chunks(int objective, const float* labels, const float* weights, uint32_t rows,
+                        uint32_t group, float spw, double* chunk_sums, cudaStream_t stream) {
+  const uint32_t chunks = (rows + kBaseChunk - 1) / kBaseChunk;
+  if (!chunks) return;
+  base_chunk_kernel<<<chunks, 512, 0, stream>>>(objective, labels, weights, rows, group, spw,
+                                                chunk_sums);
+  XGBB_CUDA(cudaGetLastError());
+}
+
+void launch_fill_margins(float* margins, const float* base, uint32_t rows, uint32_t groups,
+                         cudaStream_t stream) {
+  const uint64_t total = uint64_t(rows) * groups;
+  if (!total) return;
+  fill_margins_kernel<<<grid_for(total, 256), 256, 0, stream>>>(margins, base, rows, groups);
+  XGBB_CUDA(cudaGetLastError());
+}
+
+HistConfig hist_config(const Ellpack& e, bool unit_hessian) {
+  const size_t per_feature = size_t(e.bins + 1) * (unit_hessian ? 12 : 16);
+  const size_t budget = 110 * 1024;  // two CTAs per SM
+  const uint32_t align = e.bytes_per_code == 1 ? 16 : 8;
+  uint32_t fg = uint32_t(budget / per_feature);
+  fg = std::max(align, fg / align * align);
+  fg = std::min<uint32_t>(fg, (e.cols + align - 1) / align * align);
+  HistConfig c;
+  c.feature_group = fg;
+  c.smem = per_feature * fg;
+  c.threads = 512;
+  return c;
+}
+
+namespace {
+template <typename CodeT, bool kUnit, bool kRoot>
+void launch_hist_t(const HistArgs& args, int blocks, int threads, size_t smem, cudaStream_t stream) {
+  auto kernel = hist_kernel<CodeT, kUnit, kRoot>;
+  static bool configured = false;
+  if (!configured) {
+    XGBB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    configured = true;
+  }
+  kernel<<<blocks, threads, smem, stream>>>(args);
+}
+}  // namespace
+
+void tree_init(const TreeWorkspace& ws, const TreeLaunch& tl, cudaStream_t stream) {
+  init_tree_kernel<<<1, 1, 0, stream>>>(ws.state, tl.ell.rows, ws.ids[0], ws.sums[0],
+                                        ws.seg_begin[0], ws.seg_count[0], ws.tile_offset,
+                                        ws.built_left, ws.keys[0], ws.nodes);
+  XGBB_CUDA(cudaGetLastError());
+}
+
+void tree_level_hist(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t depth,
+                     cudaStream_t stream) {
+  const size_t bytes = size_t(max_pairs_at(depth)) * hist_node_bytes(tl.ell);
+  XGBB_CUDA(cudaMemsetAsync(ws.built, 0, bytes, stream));
+  HistArgs a;
+  a.e = tl.ell;
+  a.pairs = tl.pairs;
+  a.scale = tl.scale;
+  a.rows = ws.rows[depth & 1];
+  a.state = ws.state;
+  a.tile_offset = ws.tile_offset;
+  a.built_left = ws.built_left;
+  a.seg_begin = ws.seg_begin[depth & 1];
+  a.seg_count = ws.seg_count[depth & 1];
+  a.built = ws.built;
+  a.fg = tl.feature_group;
+  a.ngroups = (tl.ell.cols + tl.feature_group - 1) / tl.feature_group;
+  const bool root = depth == 0;
+  const bool u8 = tl.ell.bytes_per_code == 1;
+  const int b = tl.hist_blocks, t = tl.hist_threads;
+  const size_t sm = tl.hist_smem;
+#define XGBB_HIST(C, U, R) launch_hist_t<C, U, R>(a, b, t, sm, stream)
+  if (u8) {
+    if (tl.unit_hessian) { if (root) XGBB_HIST(uint8_t, true, true); else XGBB_HIST(uint8_t, true, false); }
+    else { if (root) XGBB_HIST(uint8_t, false, true); else XGBB_HIST(uint8_t, false, false); }
+  } else {
+    if (tl.unit_hessian) { if (root) XGBB_HIST(uint16_t, true, true); else XGBB_HIST(uint16_t, true, false); }
+    else { if (root) XGBB_HIST(uint16_t, false, true); else XGBB_HIST(uint16_t, false, false); }
+  }
+#undef XGBB_HIST
+  XGBB_CUDA(cudaGetLastError());
+}
+
+static SplitMath split_math(const TreeParams& p) {
+  SplitMath m;
+  m.lambda = (double)p.reg_lambda;
+  m.alpha = fabs((double)p.reg_alpha);
+  m.alpha2 = (double)p.reg_alpha + (double)p.reg_alpha;
+  m.min_child = (double)fabsf(p.min_child_weight);
+  m.max_delta = fabsf(p.max_delta_step);
+  return m;
+}
+
+void tree_level_eval(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t depth,
+                     cudaStream_t stream) {
+  EvalArgs a;
+  a.e = tl.ell;
+  a.m = split_math(tl.params);
+  a.scale = tl.scale;
+  a.state = ws.state;
+  a.depth = depth;
+  a.built = ws.built;
+  a.prev_bank = ws.bank[(depth + 1) & 1];
+  a.bank = ws.bank[depth & 1];
+  a.parent_slot = ws.parent_slot;
+  a.built_left = ws.built_left;
+  a.sums = ws.sums[depth & 1];
+  a.cand = ws.cand;
+  a.keys = ws.keys[depth & 1];
+  a.write_bank = depth + 1 < tl.params.max_depth;
+  eval_kernel<<<tl.eval_blocks, 256, 0, stream>>>(a);
+  XGBB_CUDA(cudaGetLastError());
+}
+
+void tree_level_control(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t depth,
+                        cudaStream_t stream) {
+  ControlArgs a;
+  a.e = tl.ell;
+  a.tp = tl.params;
+  a.m = split_math(tl.params);
+  a.scale = tl.scale;
+  a.state = ws.state;
+  a.depth = depth;
+  a.ids = ws.ids[depth & 1];
+  a.sums = ws.sums[depth & 1];
+  a.seg_begin = ws.seg_begin[depth & 1];
+  a.seg_count = ws.seg_count[depth & 1];
+  a.cand = ws.cand;
+  a.keys = ws.keys[depth & 1];
+  a.next_keys = ws.keys[(depth + 1) & 1];
+  a.next_ids = ws.ids[(depth + 1) & 1];
+  a.next_sums = ws.sums[(depth + 1) & 1];
+  a.parent_slot = ws.parent_slot;
+  a.mode = ws.mode;
+  a.slot_leaf = ws.slot_leaf;
+  a.cursor_l = ws.cursor_l;
+  a.cursor_r = ws.cursor_r;
+  a.ptile_offset = ws.ptile_offset;
+  a.nodes = ws.nodes;
+  a.node_capacity = ws.node_capacity;
+  control_kernel<<<1, 1024, 0, stream>>>(a);
+  XGBB_CUDA(cudaGetLastError());
+}
+
+void tree_level_partition(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t depth,
+                          cudaStream_t stream) {
+  PartArgs a;
+  a.e = tl.ell;
+  a.state = ws.state;
+  a.ids = ws.ids[depth & 1];
+  a.nodes = ws.nodes;
+  a.seg_begin = ws.seg_begin[depth & 1];
+  a.seg_count = ws.seg_count[depth & 1];
+  a.ptile_offset = ws.ptile_offset;
+  a.mode = ws.mode;
+  a.slot_leaf = ws.slot_leaf;
+  a.rows = ws.rows[depth & 1];
+  a.rows_next = ws.rows[(depth + 1) & 1];
+  a.cursor_l = ws.cursor_l;
+  a.cursor_r = ws.cursor_r;
+  a.margins = tl.margins;
+  a.groups = tl.groups;
+  a.group = tl.group;
+  a.root = depth == 0;
+  if (tl.ell.bytes_per_code == 1)
+    partition_kernel<uint8_t><<<tl.part_blocks, 256, 0, stream>>>(a);
+  else
+    partition_kernel<uint16_t><<<tl.part_blocks, 256, 0, stream>>>(a);
+  XGBB_CUDA(cudaGetLastError());
+}
+
+void tree_level_counts(const TreeWorkspace& ws, uint32_t depth, cudaStream_t stream) {
+  counts_kernel<<<1, 512, 0, stream>>>(ws.state, ws.seg_begin[depth & 1], ws.seg_count[depth & 1],
+                                       ws.mode, ws.cursor_l, ws.counts_local);
+  XGBB_CUDA(cudaGetLastError());
+}
+
+void tree_level_plan(const TreeWorkspace& ws, const TreeLaunch&, uint32_t next_depth,
+                     cudaStream_t stream) {
+  PlanArgs a;
+  a.state = ws.state;
+  a.next_depth = next_depth;
+  a.parent_slot = ws.parent_slot;
+  a.seg_begin_cur = ws.seg_begin[(next_depth + 1) & 1];
+  a.counts_local = ws.counts_local;
+  a.counts_global = ws.counts_global;
+  a.seg_begin = ws.seg_begin[next_depth & 1];
+  a.seg_count = ws.seg_count[next_depth & 1];
+  a.built_left = ws.built_left;
+  a.tile_offset = ws.tile_offset;
+  plan_kernel<<<1, 1024, 0, stream>>>(a);
+  XGBB_CUDA(cudaGetLastError());
+}
+
+void launch_predict(const float* X, uint32_t rows, uint32_t cols, const DevNode* nodes,
+                    const uint32_t* tree_begin, const uint32_t* tree_group, uint32_t trees,
+                    const float* base, uint32_t groups, float* out, cudaStream_t stream) {
+  if (!rows) return;
+  predict_kernel<<<grid_for(rows, 128), 128, 0, stream>>>(X, rows, cols, nodes, tree_begin,
+                                                         tree_group, trees, base, groups, out);
+  XGBB_CUDA(cudaGetLastError());
+}
+
+void launch_transform(int objective, float* v, uint32_t rows, uint32_t groups,
+                      cudaStream_t stream) {
+  if (!rows) return;
+  transform_kernel<<<grid_for(rows, 128), 128, 0, stream>>>(objective, v, rows, groups);
+  XGBB_CUDA(cudaGetLastError());
+}
+
+}  // namespace xgbb

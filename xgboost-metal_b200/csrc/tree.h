@@ -1,0 +1,129 @@
+// Device workspaces and launch entry points of the histogram tree trainer.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "common.h"
+
+namespace xgbb {
+
+// Quantised feature matrix in HBM: row-major ELLPACK, one code per
+// (row, feature), uint8 or uint16, `missing` = the type's maximum code.
+// Each row is padded to `stride` codes (a multiple of 16 bytes) with missing.
+struct Ellpack {
+  const void* codes = nullptr;
+  uint32_t rows = 0, cols = 0, stride = 0;  // stride in codes
+  uint32_t bytes_per_code = 1;              // 1 or 2
+  uint32_t missing = 0xff;
+  uint32_t bins = 0;                        // cut stride B (histogram has B + 1 bins)
+  const float* cuts = nullptr;              // [cols][bins]
+  const uint32_t* counts = nullptr;         // [cols]
+  const float* minima = nullptr;            // [cols]
+};
+
+// Exact magnitude accumulators for the gradient scales of one (group, part).
+struct MassAccum {
+  unsigned int max_bits;       // max |value| bits (exponent is what matters)
+  unsigned int fallback;       // 1 when the windowed sum cannot decide the exponent
+  unsigned long long lo, hi;   // 128-bit windowed sum
+  unsigned long long exact[10];// exact 320-bit sum in 32-bit limbs (fallback path)
+};
+
+// Everything one tree needs on the device; pointers are fixed for a booster,
+// so the launch sequence can be captured once as a CUDA graph and replayed.
+struct TreeWorkspace {
+  DriverState* state;
+  uint32_t* ids[2];
+  long long* sums[2];        // [slot][2]
+  uint32_t* seg_begin[2];
+  uint32_t* seg_count[2];
+  uint32_t* parent_slot;     // next-level pair -> parent slot
+  uint32_t* built_left;      // pair -> 1 when the left child is built
+  uint32_t* tile_offset;     // [pairs + 1] tiles of built children (exclusive scan)
+  uint32_t* ptile_offset;    // [frontier + 1] tiles of all frontier nodes
+  uint32_t* cursor_l;        // partition cursors per slot
+  uint32_t* cursor_r;
+  uint32_t* counts_local;    // [slot][2] left/right child counts of this rank
+  uint32_t* counts_global;   // [slot][2] summed over ranks (== local on one GPU)
+  uint32_t* mode;            // per slot: 0 retire, 1 split, 2 terminal split
+  float* slot_leaf;          // [slot][2]
+  unsigned long long* keys[2];  // best (gain, feature) key per slot
+  DevSplit* cand;            // [kMaxFrontier][cols]
+  DevNode* nodes;            // [node_capacity]
+  longlong2* built;          // [pairs][cols][bins + 1]
+  longlong2* bank[2];        // [slots][cols][bins + 1]
+  uint32_t* rows[2];         // row ids per level (level 0 uses the identity)
+  uint32_t node_capacity;
+};
+
+struct TreeLaunch {
+  Ellpack ell;
+  TreeParams params;
+  const float2* pairs;       // gradient pairs of this group [rows]
+  const float2* scale;       // power-of-two scales of this group
+  float* margins;            // [rows][groups]
+  uint32_t groups, group;
+  bool unit_hessian;
+  int hist_blocks, hist_threads, eval_blocks, part_blocks;
+  uint32_t feature_group;    // features per histogram CTA
+  size_t hist_smem;
+};
+
+// Launch helpers (tree.cu). All are asynchronous on `stream`.
+void launch_quantize(const float* X, uint32_t rows, uint32_t cols, const float* cuts,
+                     const uint32_t* counts, uint32_t bins, void* codes, uint32_t stride,
+                     uint32_t bytes_per_code, uint32_t missing, cudaStream_t stream);
+void launch_gradients(int objective, const float* margins, const float* labels,
+                      const float* weights, uint32_t rows, uint32_t groups, float scale_pos_weight,
+                      float2* pairs, MassAccum* mass, cudaStream_t stream);
+void launch_mass_window(const float2* pairs, uint32_t rows, uint32_t groups, MassAccum* mass,
+                        cudaStream_t stream);
+// Reduces per-rank accumulators (already summed across ranks if sharded) to
+// scales; runs the exact fallback when needed. rows_total = rows over ranks.
+void launch_scales(const float2* pairs, uint32_t rows, uint32_t groups, MassAccum* mass,
+                   float2* scales, unsigned long long rows_total, bool may_fallback,
+                   cudaStream_t stream);
+void launch_mass_exact(const float2* pairs, uint32_t rows, uint32_t groups, MassAccum* mass,
+                       cudaStream_t stream);
+void launch_scales_exact(uint32_t groups, MassAccum* mass, float2* scales, cudaStream_t stream);
+void launch_base_chunks(int objective, const float* labels, const float* weights, uint32_t rows,
+                        uint32_t group, float scale_pos_weight, double* chunk_sums,
+                        cudaStream_t stream);
+void launch_fill_margins(float* margins, const float* base, uint32_t rows, uint32_t groups,
+                         cudaStream_t stream);
+
+struct HistConfig {
+  uint32_t feature_group;
+  size_t smem;
+  int threads;
+};
+HistConfig hist_config(const Ellpack& ell, bool unit_hessian);
+
+void tree_init(const TreeWorkspace& ws, const TreeLaunch& tl, cudaStream_t stream);
+void tree_level_hist(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t depth,
+                     cudaStream_t stream);
+void tree_level_eval(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t depth,
+                     cudaStream_t stream);
+void tree_level_control(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t depth,
+                        cudaStream_t stream);
+void tree_level_partition(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t depth,
+                          cudaStream_t stream);
+void tree_level_counts(const TreeWorkspace& ws, uint32_t depth, cudaStream_t stream);
+void tree_level_plan(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t next_depth,
+                     cudaStream_t stream);
+
+// Bytes of one node's histogram and the largest pair / slot counts at a depth.
+inline size_t hist_node_bytes(const Ellpack& e) {
+  return size_t(e.cols) * (e.bins + 1) * sizeof(longlong2);
+}
+inline uint32_t max_pairs_at(uint32_t depth) { return depth ? (1u << (depth - 1)) : 1u; }
+inline uint32_t max_slots_at(uint32_t depth) { return 1u << depth; }
+
+void launch_predict(const float* X, uint32_t rows, uint32_t cols, const DevNode* nodes,
+                    const uint32_t* tree_begin, const uint32_t* tree_group, uint32_t trees,
+                    const float* base_margin, uint32_t groups, float* out, cudaStream_t stream);
+void launch_transform(int objective, float* values, uint32_t rows, uint32_t groups,
+                      cudaStream_t stream);
+
+}  // namespace xgbb

@@ -1,0 +1,127 @@
+"""Scikit-learn estimators (python-package/xgboost/sklearn.py in the
+reference): XGBRegressor and XGBClassifier over train()."""
+import numpy as np
+
+from .core import DMatrix, XGBoostError
+from .training import train
+
+__all__ = ["XGBModel", "XGBRegressor", "XGBClassifier"]
+
+_PARAM_NAMES = (
+    "max_depth", "max_leaves", "max_bin", "grow_policy", "learning_rate", "verbosity",
+    "objective", "booster", "tree_method", "n_jobs", "gamma", "min_child_weight",
+    "max_delta_step", "subsample", "sampling_method", "colsample_bytree", "colsample_bylevel",
+    "colsample_bynode", "reg_alpha", "reg_lambda", "scale_pos_weight", "base_score",
+    "random_state", "missing", "num_parallel_tree", "monotone_constraints",
+    "interaction_constraints", "importance_type", "device", "validate_parameters",
+    "enable_categorical", "feature_types", "max_cat_to_onehot", "max_cat_threshold",
+    "multi_strategy", "eval_metric", "early_stopping_rounds", "callbacks")
+
+
+class XGBModel:
+    def __init__(self, *, n_estimators=100, objective=None, **kwargs):
+        self.n_estimators = n_estimators
+        self.objective = objective
+        for k in _PARAM_NAMES:
+            if k != "objective":
+                setattr(self, k, kwargs.pop(k, None))
+        self.kwargs = kwargs
+        self._Booster = None
+
+    def get_params(self, deep=True):
+        out = {"n_estimators": self.n_estimators, "objective": self.objective}
+        for k in _PARAM_NAMES:
+            if k != "objective":
+                out[k] = getattr(self, k)
+        out.update(self.kwargs)
+        return out
+
+    def set_params(self, **params):
+        for k, v in params.items():
+            if k in _PARAM_NAMES or k in ("n_estimators", "objective"):
+                setattr(self, k, v)
+            else:
+                self.kwargs[k] = v
+        return self
+
+    def get_xgb_params(self):
+        skip = {"n_estimators", "missing", "n_jobs", "random_state", "importance_type",
+                "enable_categorical", "feature_types", "early_stopping_rounds", "callbacks",
+                "eval_metric"}
+        params = {k: v for k, v in self.get_params().items() if v is not None and k not in skip}
+        if self.random_state is not None:
+            params["seed"] = self.random_state
+        params.setdefault("device", "cuda")
+        params.setdefault("tree_method", "hist")
+        return params
+
+    def get_booster(self):
+        if self._Booster is None:
+            raise XGBoostError("need to call fit or load_model beforehand")
+        return self._Booster
+
+    def _fit(self, X, y, sample_weight, eval_set, verbose, params):
+        dtrain = DMatrix(X, y, weight=sample_weight,
+                         missing=np.nan if self.missing is None else self.missing)
+        evals = []
+        for i, (ex, ey) in enumerate(eval_set or []):
+            evals.append((DMatrix(ex, ey), "validation_%d" % i))
+        self.evals_result_ = {}
+        if self.eval_metric is not None:
+            params["eval_metric"] = self.eval_metric
+        self._Booster = train(params, dtrain, self.n_estimators, evals=evals,
+                              evals_result=self.evals_result_, verbose_eval=bool(verbose))
+        self.n_features_in_ = dtrain.num_col()
+        return self
+
+    def predict(self, X, output_margin=False, validate_features=True, base_margin=None,
+                iteration_range=None):
+        dm = DMatrix(X, missing=np.nan if self.missing is None else self.missing,
+                     base_margin=base_margin)
+        return self.get_booster().predict(dm, output_margin=output_margin,
+                                          iteration_range=iteration_range or (0, 0))
+
+
+class XGBRegressor(XGBModel):
+    def __init__(self, *, objective="reg:squarederror", **kwargs):
+        super().__init__(objective=objective, **kwargs)
+
+    def fit(self, X, y, *, sample_weight=None, base_margin=None, eval_set=None, verbose=True,
+            xgb_model=None, sample_weight_eval_set=None, base_margin_eval_set=None,
+            feature_weights=None):
+        return self._fit(X, y, sample_weight, eval_set, verbose, self.get_xgb_params())
+
+
+class XGBClassifier(XGBModel):
+    def __init__(self, *, objective="binary:logistic", **kwargs):
+        super().__init__(objective=objective, **kwargs)
+
+    def fit(self, X, y, *, sample_weight=None, base_margin=None, eval_set=None, verbose=True,
+            xgb_model=None, sample_weight_eval_set=None, base_margin_eval_set=None,
+            feature_weights=None):
+        y = np.asarray(y)
+        self.classes_ = np.unique(y)
+        self.n_classes_ = len(self.classes_)
+        encoded = np.searchsorted(self.classes_, y).astype(np.float32)
+        params = self.get_xgb_params()
+        if self.n_classes_ > 2:
+            if params.get("objective", "").startswith("binary:"):
+                params["objective"] = "multi:softprob"
+            params["num_class"] = self.n_classes_
+        eval_set = [(ex, np.searchsorted(self.classes_, np.asarray(ey)).astype(np.float32))
+                    for ex, ey in (eval_set or [])]
+        return self._fit(X, encoded, sample_weight, eval_set, verbose, params)
+
+    def predict_proba(self, X, validate_features=True, base_margin=None, iteration_range=None):
+        p = super().predict(X, base_margin=base_margin, iteration_range=iteration_range)
+        if p.ndim == 1:
+            return np.stack([1 - p, p], axis=1)
+        return p
+
+    def predict(self, X, output_margin=False, validate_features=True, base_margin=None,
+                iteration_range=None):
+        if output_margin:
+            return super().predict(X, output_margin=True, base_margin=base_margin,
+                                   iteration_range=iteration_range)
+        p = self.predict_proba(X, base_margin=base_margin, iteration_range=iteration_range)
+        return self.classes_[np.argmax(p, axis=1)]
