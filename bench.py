@@ -1,0 +1,428 @@
+#!/usr/bin/env python
+"""Benchmark: train ms per 100 rounds (and histogram-build HBM GB/s) of the
+CUDA trainer on the BASELINE.json workload, at 1..8 GPUs of one node.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c4|c2|c1|c0]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (one rank per GPU)
+    python bench.py --impl reference ...                     (CPU reference arm)
+
+A step is one boosting round. Data are synthetic and seeded per 1M-row chunk,
+generated on the GPU, so every GPU count trains on the same rows (strong
+scaling: the total row count is fixed and rows are sharded contiguously).
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "xgboost-metal_b200"))
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+
+METRIC = "train ms per 100 rounds (histogram build in roofline GB/s)"
+UNIT = "ms/100 rounds"
+
+WORKLOADS = {
+    # the 1/2/4/8-GPU workload.
+    "c4": dict(rows=50_000_000, cols=128, nan=0.05, objective="binary:logistic", max_depth=10,
+               eta=0.1, labels="logistic"),
+    # the 10x-vs-CPU workload.
+    "c2": dict(rows=262_144, cols=64, nan=0.0, objective="reg:squarederror", max_depth=8,
+               eta=0.3, labels="linear"),
+    "c1": dict(rows=100_000, cols=32, nan=0.15, objective="reg:squarederror", max_depth=6,
+               eta=0.3, labels="linear"),
+    "c0": dict(rows=100_000, cols=32, nan=0.0, objective="reg:squarederror", max_depth=6,
+               eta=0.3, labels="linear"),
+}
+CHUNK = 1_000_000
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ---------------------------------------------------------------------------
+# Synthetic data (GPU, seeded per chunk)
+# ---------------------------------------------------------------------------
+def gen_chunk(wl, c, device):
+    """Rows [c*CHUNK, min((c+1)*CHUNK, rows)) of workload `wl`, on the GPU."""
+    import torch
+    spec = WORKLOADS[wl]
+    begin = c * CHUNK
+    n = min(CHUNK, spec["rows"] - begin)
+    cols = spec["cols"]
+    g = torch.Generator(device=device)
+    g.manual_seed(1337 * 1000003 + c)
+    X = torch.randn(n, cols, generator=g, device=device, dtype=torch.float32)
+    mask = torch.rand(n, cols, generator=g, device=device) < spec["nan"] if spec["nan"] else None
+    g2 = torch.Generator(device=device)
+    g2.manual_seed(1340 * 1000003 + c)
+    if spec["labels"] == "logistic":
+        w = torch.from_numpy(np.random.default_rng(1339).normal(0, 0.1, cols).astype(np.float32)).to(device)
+        Xz = X if mask is None else X.masked_fill(mask, 0.0)
+        logits = Xz @ w + 0.5 * Xz[:, 0] * Xz[:, 1]
+        y = (torch.rand(n, generator=g2, device=device) < torch.sigmoid(logits)).float()
+    else:
+        w = torch.from_numpy(np.random.default_rng(1338).normal(size=cols).astype(np.float32)).to(device)
+        y = X @ w + 0.1 * torch.randn(n, generator=g2, device=device)
+    if mask is not None:
+        X = X.masked_fill(mask, float("nan"))
+    return X, y
+
+
+def gen_rows(wl, begin, end, device, pin=True):
+    """Host (pinned) copies of global rows [begin, end)."""
+    import torch
+    cols = WORKLOADS[wl]["cols"]
+    n = end - begin
+    Xh = torch.empty((n, cols), dtype=torch.float32, pin_memory=pin)
+    yh = torch.empty((n,), dtype=torch.float32, pin_memory=pin)
+    c = begin // CHUNK
+    while c * CHUNK < end:
+        X, y = gen_chunk(wl, c, device)
+        lo, hi = max(begin, c * CHUNK), min(end, c * CHUNK + X.shape[0])
+        Xh[lo - begin:hi - begin].copy_(X[lo - c * CHUNK:hi - c * CHUNK])
+        yh[lo - begin:hi - begin].copy_(y[lo - c * CHUNK:hi - c * CHUNK])
+        del X, y
+        c += 1
+    torch.cuda.synchronize(device)
+    return Xh.numpy(), yh.numpy()
+
+
+def params_for(wl):
+    s = WORKLOADS[wl]
+    return {"objective": s["objective"], "max_depth": s["max_depth"], "eta": s["eta"],
+            "max_bin": 256, "tree_method": "hist", "device": "cuda", "seed": 42,
+            "reg_lambda": 1.0}
+
+
+# ---------------------------------------------------------------------------
+# Clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[4:8]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(max(mx)),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# Distributed plumbing (one process per GPU)
+# ---------------------------------------------------------------------------
+class Dist:
+    def __init__(self):
+        self.rank = int(os.environ.get("RANK", 0))
+        self.world = int(os.environ.get("WORLD_SIZE", 1))
+        self.local = int(os.environ.get("LOCAL_RANK", 0))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+            dist.init_process_group("gloo", timeout=datetime.timedelta(minutes=15))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, v):
+        if not self.pg:
+            return v
+        import torch
+        t = torch.tensor([float(v)], dtype=torch.float64)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def bcast(self, obj):
+        if not self.pg:
+            return obj
+        box = [obj]
+        self.pg.broadcast_object_list(box, src=0)
+        return box[0]
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+def shard(rows, rank, world):
+    return rows * rank // world, rows * (rank + 1) // world
+
+
+def launches_per_round(depth, groups):
+    # gradients, window, scales, exact, exact scales; per tree: init, 4 per
+    # level (histogram, evaluation, control, partition), 2 per non-last level
+    # (counts, plan).
+    return 5 + groups * (1 + 4 * depth + 2 * (depth - 1))
+
+
+# ---------------------------------------------------------------------------
+# CPU baselines
+# ---------------------------------------------------------------------------
+def cpu_oracle_baseline(wl, device):
+    """The single-threaded oracle on a bounded sample; per-round cost from the
+    difference of 2-round and 0-round runs, scaled by rows to the workload."""
+    import checkers as C
+    spec = WORKLOADS[wl]
+    rows = min(spec["rows"], 100_000 if wl == "c4" else spec["rows"])
+    X, y = gen_rows(wl, 0, rows, device, pin=False)
+    p = C.train_params(dict(objective=spec["objective"], max_depth=spec["max_depth"],
+                            eta=spec["eta"]))
+    t = time.perf_counter()
+    C.oracle_train(X, y, p, 0)
+    t0 = time.perf_counter() - t
+    t = time.perf_counter()
+    C.oracle_train(X, y, p, 2)
+    t2 = time.perf_counter() - t
+    per_round = max(t2 - t0, 1e-9) / 2
+    value = per_round * 1000 * 100 * spec["rows"] / rows
+    return {"value": value, "unit": UNIT, "cores": 1, "kind": "port",
+            "sample": "oracle (single-threaded C) on the first %d rows, 2 rounds minus setup, "
+                      "scaled by rows to %d rows and to 100 rounds" % (rows, spec["rows"])}
+
+
+def reference_arm(args, wl, device):
+    """The reference's own serial split/driver/predict functions (oracle/_ref),
+    on a bounded sample per step, scaled to the workload."""
+    import checkers as C
+    spec = WORKLOADS[wl]
+    rows = min(spec["rows"], 50_000 if wl == "c4" else spec["rows"])
+    X, y = gen_rows(wl, 0, rows, device, pin=False)
+    kind = "reference" if C.have_reference() else "port"
+    chk = C.reference() if kind == "reference" else C.oracle()
+    o = C.oracle()
+    cuts, counts, minima = o.sketch_cuts(X, 256)
+    bins = o.quantize(X, cuts, counts)
+    margins = np.zeros((rows, 1), np.float32)
+    tp = dict(max_depth=spec["max_depth"], eta=spec["eta"], reg_lambda=1.0, reg_alpha=0.0,
+              min_child_weight=1.0, max_delta_step=0.0, min_split_loss=0.0)
+    times = []
+    for step in range(args.warmup + args.steps):
+        t = time.perf_counter()
+        pairs = C.oracle_gradients(spec["objective"], margins, y)
+        scale = chk.gradient_scales(pairs)
+        q = chk.quantize_gradients(pairs, scale)[:, 0, :]
+        _, leaf = chk.grow_tree(bins, q, scale[0], cuts, counts, minima, tp)
+        margins[:, 0] += leaf
+        if step >= args.warmup:
+            times.append(time.perf_counter() - t)
+    per_round = float(np.mean(times))
+    value = per_round * 1000 * 100 * spec["rows"] / rows
+    sample = ("%s per-round tree on the first %d rows (%d timed steps), scaled by rows to %d "
+              "and to 100 rounds" % ("oracle/_ref reference functions" if kind == "reference"
+                                     else "oracle port", rows, args.steps, spec["rows"]))
+    return {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": value / 100,
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "int64",
+            "data": "synthetic", "config": {"workload": wl, "rows": spec["rows"], "cols": spec["cols"],
+                                            "max_depth": spec["max_depth"]},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": 1, "kind": kind, "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def measured_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def ncu_traffic(wl):
+    """Per-launch DRAM bytes of the histogram kernel from the committed ncu
+    summary, scaled to one average launch of this workload, or None."""
+    path = os.path.join(ROOT, "profiles", "hist_traffic_%s.json" % wl)
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return None
+
+
+# ---------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="c4", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="override the row count (small profiling cases only; not a bench line)")
+    args = ap.parse_args()
+    assert args.warmup >= 3, "at least 3 warm-up rounds"
+    dist = Dist()
+    wl = args.workload
+    if args.rows:
+        WORKLOADS[wl] = dict(WORKLOADS[wl], rows=args.rows)
+    spec = WORKLOADS[wl]
+    import torch
+    device = torch.device("cuda", dist.local)
+    torch.cuda.set_device(device)
+
+    if args.impl == "reference":
+        if dist.rank == 0:
+            print(json.dumps(reference_arm(args, wl, device)), flush=True)
+        dist.close()
+        return
+
+    import xgboost as xgb
+    from xgboost import core
+    core.set_device(dist.local)
+    if dist.world > 1:
+        uid = dist.bcast(xgb.collective.nccl_unique_id() if dist.rank == 0 else None)
+        xgb.collective.init(rank=dist.rank, world_size=dist.world, nccl_unique_id=uid,
+                            device=dist.local)
+
+    begin, end = shard(spec["rows"], dist.rank, dist.world)
+    t = time.perf_counter()
+    Xh, yh = gen_rows(wl, begin, end, device)
+    sample = min(spec["rows"], CHUNK)
+    if wl == "c4":
+        Xs, _ = gen_rows(wl, 0, sample, device, pin=False)
+        ref = xgb.QuantileDMatrix(Xs, max_bin=256)
+    log("rank %d: rows [%d, %d) generated in %.1fs" % (dist.rank, begin, end, time.perf_counter() - t))
+    params = params_for(wl)
+    K, W = args.steps, args.warmup
+    groups = 1
+
+    # End to end: host buffers in, quantisation (H2D + binning) and K rounds
+    # through the public API; every round reads its trees back to the host.
+    dist.barrier()
+    core.synchronize()
+    t0 = time.perf_counter()
+    if wl == "c4":
+        dtrain = xgb.QuantileDMatrix(Xh, label=yh, ref=ref, max_bin=256)
+    else:
+        dtrain = xgb.DMatrix(Xh, label=yh)
+    bst = xgb.train(params, dtrain, K)
+    core.synchronize()
+    e2e_ms = dist.max((time.perf_counter() - t0) * 1000)
+    del bst
+
+    # Device-resident: a fresh booster on the quantised matrix, W warm-up
+    # rounds, then K rounds between CUDA events on the booster's stream.
+    bst = xgb.Booster(dict(params, cuda_profile=1), [dtrain])
+    for i in range(W):
+        bst.update(dtrain, i)
+    dist.barrier()
+    core.synchronize()
+    bst.reset_cuda_profile()
+    with ClockSampler(dist.local) as clocks:
+        bst.record_event(0)
+        for i in range(K):
+            bst.update(dtrain, W + i)
+        bst.record_event(1)
+        dev_ms = bst.event_elapsed(0, 1)
+        core.synchronize()
+    dev_ms = dist.max(dev_ms)
+    prof = bst.cuda_profile()
+    value = dev_ms * 100.0 / K
+
+    peak, peak_kind = measured_peak()
+    hist_gbs = prof["hist_bytes"] / prof["hist_ms"] / 1e6 if prof["hist_ms"] > 0 else 0.0
+    traffic = ncu_traffic(wl)
+    roofline = {"bound": "hbm", "achieved": round(hist_gbs, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(hist_gbs / peak, 4), "peak_kind": peak_kind,
+                "traffic": traffic["dram_bytes_per_launch"] if traffic else None,
+                "kernel": "hist_kernel",
+                "algorithmic_bytes_per_launch": prof["hist_bytes"] / max(prof["hist_launches"], 1),
+                "avg_launch_ms": prof["hist_ms"] / max(prof["hist_launches"], 1),
+                "launches": prof["hist_launches"],
+                "hist_ms_per_round": prof["hist_ms"] / K}
+
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_oracle_baseline(wl, device)
+
+    bytes_per_code = 2 if (spec["nan"] > 0) else 1
+    x_bytes = Xh.nbytes + yh.nbytes
+    node_table = groups * ((2 << spec["max_depth"]) - 1) * 48 + 32 + 2 * 10 * 12
+    out = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": dist.world,
+        "steps": K, "warmup": W, "ms_per_step": round(dev_ms / K, 4), "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int64",
+        "data": "synthetic (seeded per 1M-row chunk, generated on the GPU)",
+        "config": {"workload": wl + ("-rows%d" % args.rows if args.rows else ""),
+                   "rows": spec["rows"], "cols": spec["cols"],
+                   "objective": spec["objective"], "max_depth": spec["max_depth"],
+                   "max_bin": 256, "eta": spec["eta"], "nan_fraction": spec["nan"],
+                   "bins": "uint%d ELLPACK" % (8 * bytes_per_code),
+                   "parallelism": "row-shard dp%d" % dist.world,
+                   "cuts": ("from the first %d rows (QuantileDMatrix ref), identical on every rank"
+                            % sample) if wl == "c4" else "sketch of the full matrix",
+                   "l2": "inputs larger than L2 (quantised matrix %.1f GB)"
+                         % (spec["rows"] * spec["cols"] * bytes_per_code / 1e9)},
+        "roofline": roofline,
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e_ms * 100.0 / K, 3), "unit": UNIT,
+                "h2d_bytes_per_step": int(x_bytes / K), "d2h_bytes_per_step": node_table,
+                "note": "xgb.train(QuantileDMatrix/DMatrix from pinned host arrays) for K rounds, "
+                        "wall clock, max over ranks; H2D of the matrix amortised over K rounds"},
+        "gpu_launches": launches_per_round(spec["max_depth"], groups) * K,
+        "clocks": clocks.summary(),
+    }
+    if dist.rank == 0:
+        print(json.dumps(out), flush=True)
+    if dist.world > 1:
+        xgb.collective.finalize()
+    dist.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -19,10 +19,16 @@ XGB_DLL int XGBBSynchronize(void);
  * not NULL. Replaces XGQuantileDMatrixCreateFromCallback
  * (include/xgboost/c_api.h:535) for in-memory data. */
 XGB_DLL int XGDMatrixQuantise(DMatrixHandle handle, int max_bin, DMatrixHandle ref);
-/* JSON {"hist_ms", "hist_launches", "rounds"}: CUDA-event time of the
+/* JSON {"hist_ms", "hist_bytes", "hist_launches", "rounds"}: CUDA-event time of the
  * histogram kernels when the booster has cuda_profile=1. Replaces
  * XGBoosterMetalProfile (include/metalgb/c_api.h:8-12). */
 XGB_DLL int XGBoosterGetCudaProfile(BoosterHandle handle, char const** out);
+/* Clears the counters of XGBoosterGetCudaProfile. */
+XGB_DLL int XGBoosterResetCudaProfile(BoosterHandle handle);
+/* Records CUDA event `slot` (0..63) on the booster's stream, and the device
+ * time between two recorded events; used to time whole rounds. */
+XGB_DLL int XGBoosterRecordEvent(BoosterHandle handle, int slot);
+XGB_DLL int XGBoosterEventElapsed(BoosterHandle handle, int a, int b, float* ms);
 
 /* Kernel-level entry points used by the parity tests (host buffers in, host
  * buffers out). */

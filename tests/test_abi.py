@@ -67,8 +67,10 @@ def test_errors_are_reported_not_raised_through_the_abi():
     import xgboost as xgb
     X = np.ones((3, 2), np.float32)
     X[0, 0] = np.inf
+    # A non-NaN missing sentinel takes the copying path, validated on the host
+    # at construction; zero-copy input is validated when it reaches the GPU.
     with pytest.raises(xgb.XGBoostError, match="infinity"):
-        xgb.DMatrix(X)
+        xgb.DMatrix(X, missing=-999.0)
     with pytest.raises(xgb.XGBoostError, match="Label"):
         xgb.DMatrix(np.ones((2, 2), np.float32), label=[np.nan, 1])
     lib = ctypes.CDLL(LIB)

@@ -184,3 +184,12 @@ def test_c2_full_size_matches_oracle():
     trees_p, margins_p = P.train(X, y, {k: v for k, v in params.items() if k != "num_class"}, 3)
     assert_same_trees(trees_p, trees_o)
     np.testing.assert_array_equal(bits(margins_p), bits(margins_o))
+
+
+def test_zero_copy_infinity_is_reported_on_first_use():
+    import xgboost as xgb
+    X = np.ones((64, 3), np.float32)
+    X[5, 1] = np.inf
+    d = xgb.DMatrix(X, label=np.zeros(64, np.float32))
+    with pytest.raises(xgb.XGBoostError, match="infinity"):
+        xgb.train({"device": "cuda"}, d, 1)

@@ -173,8 +173,24 @@ DMatrixHandle new_dmatrix(std::vector<float>&& values, uint64_t rows, uint64_t c
   auto d = std::make_shared<xgbb::DMatrix>();
   d->rows = uint32_t(rows);
   d->cols = uint32_t(cols);
-  d->data = std::move(values);
-  normalise(d->data, missing, d->has_missing);
+  d->owned = std::move(values);
+  normalise(d->owned, missing, d->has_missing);
+  d->host = d->owned.data();
+  d->validated = true;
+  return new DMatrixPtr(std::move(d));
+}
+
+// Zero-copy: the matrix reads the caller's float32 C-contiguous buffer, which
+// must stay alive and unchanged while the matrix exists (the reference wraps
+// caller memory the same way, src/runtime.mm:100-130). Validation (NaN = missing,
+// no infinities) happens on the GPU when the data is first uploaded.
+DMatrixHandle borrowed_dmatrix(const float* data, uint64_t rows, uint64_t cols) {
+  require(rows < (1ull << 32) && cols < (1ull << 31), "Matrix exceeds the 32-bit row index range.");
+  auto d = std::make_shared<xgbb::DMatrix>();
+  d->rows = uint32_t(rows);
+  d->cols = uint32_t(cols);
+  d->host = data;
+  d->validated = false;
   return new DMatrixPtr(std::move(d));
 }
 
@@ -240,9 +256,21 @@ XGB_DLL int XGDMatrixCreateFromDense(char const* data, char const* config, DMatr
   return guarded([&] {
     ArrayView a = parse_array(data);
     require(a.shape.size() == 2, "Dense input must be 2-dimensional.");
+    bool zero_copy = false;
+    if (config && *config) {
+      Json c = Json::parse(config);
+      if (auto* z = c.find("zero_copy")) zero_copy = z->truthy();
+    }
+    const float missing = config_missing(config);
+    const bool contiguous = a.strides.empty() ||
+                            (a.strides.size() == 2 && a.strides[1] == 4 && a.strides[0] == int64_t(a.shape[1]) * 4);
+    if (zero_copy && a.kind == 'f' && a.itemsize == 4 && contiguous && std::isnan(missing)) {
+      *out = borrowed_dmatrix(reinterpret_cast<const float*>(a.ptr), a.shape[0], a.shape[1]);
+      return;
+    }
     uint64_t rows, cols;
     auto v = to_floats(a, rows, cols);
-    *out = new_dmatrix(std::move(v), rows, cols, config_missing(config));
+    *out = new_dmatrix(std::move(v), rows, cols, missing);
   });
 }
 
@@ -322,7 +350,8 @@ XGB_DLL int XGDMatrixNumCol(DMatrixHandle handle, bst_ulong* out) {
 XGB_DLL int XGDMatrixNumNonMissing(DMatrixHandle handle, bst_ulong* out) {
   return guarded([&] {
     uint64_t n = 0;
-    for (float x : dmat(handle)->data) n += !std::isnan(x);
+    auto& d = *dmat(handle);
+    for (size_t i = 0; i < size_t(d.rows) * d.cols; ++i) n += !std::isnan(d.host[i]);
     *out = n;
   });
 }
@@ -526,10 +555,23 @@ XGB_DLL int XGBoosterGetCudaProfile(BoosterHandle handle, char const** out) {
   return guarded([&] {
     auto& p = booster(handle).profile;
     results.str = "{\"hist_ms\":" + std::to_string(p.hist_ms) +
+                  ",\"hist_bytes\":" + std::to_string(p.hist_bytes) +
                   ",\"hist_launches\":" + std::to_string(p.hist_launches) +
                   ",\"rounds\":" + std::to_string(p.rounds) + "}";
     *out = results.str.c_str();
   });
+}
+
+XGB_DLL int XGBoosterRecordEvent(BoosterHandle handle, int slot) {
+  return guarded([&] { booster(handle).record_event(slot); });
+}
+
+XGB_DLL int XGBoosterEventElapsed(BoosterHandle handle, int a, int b, float* ms) {
+  return guarded([&] { *ms = booster(handle).elapsed_ms(a, b); });
+}
+
+XGB_DLL int XGBoosterResetCudaProfile(BoosterHandle handle) {
+  return guarded([&] { booster(handle).profile = xgbb::Profile{}; });
 }
 
 // Test entry: product cuts (host sketch) and GPU bins, decoded to row-major
@@ -568,12 +610,12 @@ XGB_DLL int XGBBGradientsHost(int objective, const float* margins, const float* 
     ensure_device();
     xgbb::DeviceBuffer dm(std::max<size_t>(rows * groups, 1) * 4), dl(std::max<size_t>(rows, 1) * 4),
         dw(weights ? rows * 4 : 0), dp(std::max<size_t>(rows * groups, 1) * 8),
-        mass(groups * 2 * sizeof(xgbb::MassAccum)), ds(groups * 8);
+        mass(xgbb::mass_bytes(groups)), ds(groups * 8);
     XGBB_CUDA(cudaMemcpy(dm.get(), margins, rows * groups * 4, cudaMemcpyHostToDevice));
     XGBB_CUDA(cudaMemcpy(dl.get(), labels, rows * 4, cudaMemcpyHostToDevice));
     if (weights) XGBB_CUDA(cudaMemcpy(dw.get(), weights, rows * 4, cudaMemcpyHostToDevice));
     XGBB_CUDA(cudaMemset(mass.get(), 0, mass.size()));
-    auto* m = mass.as<xgbb::MassAccum>();
+    const xgbb::MassAccum m = xgbb::mass_view(mass.get(), groups);
     auto* p = dp.as<float2>();
     xgbb::launch_gradients(objective, dm.as<float>(), dl.as<float>(), weights ? dw.as<float>() : nullptr,
                            uint32_t(rows), groups, scale_pos_weight, p, m, nullptr);

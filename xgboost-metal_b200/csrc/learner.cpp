@@ -35,7 +35,23 @@ const float* DMatrix::device_data(cudaStream_t stream) {
   const size_t bytes = size_t(rows) * cols * sizeof(float);
   if (!d_data && bytes) {
     d_data.resize(bytes);
-    XGBB_CUDA(cudaMemcpyAsync(d_data.get(), data.data(), bytes, cudaMemcpyHostToDevice, stream));
+    XGBB_CUDA(cudaMemcpyAsync(d_data.get(), host, bytes, cudaMemcpyHostToDevice, stream));
+    if (!validated) {
+      // Zero-copy input is checked on the device: NaN marks missing values,
+      // any infinity is an error (src/data.cpp:433).
+      DeviceBuffer flags(8);
+      unsigned int h[2] = {0, 0};
+      XGBB_CUDA(cudaMemsetAsync(flags.get(), 0, 8, stream));
+      launch_validate(d_data.as<float>(), uint64_t(rows) * cols, flags.as<unsigned int>(), stream);
+      XGBB_CUDA(cudaMemcpyAsync(h, flags.get(), 8, cudaMemcpyDeviceToHost, stream));
+      XGBB_CUDA(cudaStreamSynchronize(stream));
+      if (h[1]) {
+        d_data.release();
+        throw Error("Input data contains infinity or a value too large for float32.");
+      }
+      has_missing = h[0] != 0;
+      validated = true;
+    }
   }
   return d_data.as<float>();
 }
@@ -59,6 +75,8 @@ void DMatrix::upload_info(cudaStream_t stream) {
 
 void DMatrix::set_cuts(std::shared_ptr<Cuts> c, cudaStream_t stream) {
   require(c->cols == cols, "Quantile reference does not match the feature count.");
+  // Uploading also settles has_missing for zero-copy input.
+  const float* X = rows ? device_data(stream) : nullptr;
   uint32_t max_count = 0;
   for (uint32_t v : c->counts) max_count = std::max(max_count, v);
   const bool narrow = max_count <= 255 || (!has_missing && max_count <= 256);
@@ -66,7 +84,9 @@ void DMatrix::set_cuts(std::shared_ptr<Cuts> c, cudaStream_t stream) {
   ell.rows = rows;
   ell.cols = cols;
   ell.bytes_per_code = narrow ? 1 : 2;
-  ell.missing = narrow ? 0xffu : 0xffffu;
+  // With 256 bins and no missing value every uint8 code is a bin, so the
+  // missing code is one no stored code can equal.
+  ell.missing = narrow ? (max_count <= 255 ? 0xffu : 0x100u) : 0xffffu;
   const uint32_t align = 16 / ell.bytes_per_code;
   ell.stride = std::max(align, (cols + align - 1) / align * align);
   ell.bins = c->stride;
@@ -76,7 +96,6 @@ void DMatrix::set_cuts(std::shared_ptr<Cuts> c, cudaStream_t stream) {
   const size_t bytes = size_t(rows) * ell.stride * ell.bytes_per_code;
   codes.resize(std::max<size_t>(bytes, 16));
   if (rows) {
-    const float* X = device_data(stream);
     launch_quantize(X, rows, cols, ell.cuts, ell.counts, ell.bins, codes.get(), ell.stride,
                     ell.bytes_per_code, ell.missing, stream);
   }
@@ -100,7 +119,7 @@ void DMatrix::quantise(uint32_t mb, const DMatrix* ref, cudaStream_t stream, int
     c->values.assign(size_t(cols) * c->stride, 0.0f);
     c->counts.assign(cols, 0);
     c->minima.assign(cols, -INFINITY);
-    sketch_cuts(data.data(), rows, cols, weights.empty() ? nullptr : weights.data(), mb,
+    sketch_cuts(host, rows, cols, weights.empty() ? nullptr : weights.data(), mb,
                 c->values.data(), c->counts.data(), c->minima.data(), threads);
     c->upload();
   }
@@ -115,15 +134,18 @@ struct Booster::TrainState {
   std::weak_ptr<DMatrix> owner;
   DMatrix* d = nullptr;
   uint32_t rows = 0, groups = 1, margin_rounds = 0;
+  unsigned long long rows_total = 0;  // rows over all ranks
   DeviceBuffer margins, pairs, mass, scales;
   DeviceBuffer state, ids[2], sums[2], seg_begin[2], seg_count[2], parent_slot, built_left,
       tile_offset, ptile_offset, cursor_l, cursor_r, counts_local, counts_global, mode, slot_leaf,
-      keys[2], cand, nodes, built, bank[2], rows_buf[2];
+      keys[2], cand, nodes, built, bank[2], rows_buf[2], level_rows, level_nodes;
   TreeWorkspace ws{};
   HistConfig hc{};
   std::vector<cudaGraphExec_t> graphs;
   DevNode* host_nodes = nullptr;   // pinned [groups][capacity]
   DriverState* host_state = nullptr;  // pinned [groups]
+  unsigned long long* host_level_rows = nullptr;  // pinned [groups][kMaxDepth]
+  uint32_t* host_level_nodes = nullptr;           // pinned [groups][kMaxDepth]
   uint32_t capacity = 0;
   std::vector<cudaEvent_t> events;  // profiling: [groups][levels][2]
   ~TrainState() {
@@ -132,6 +154,8 @@ struct Booster::TrainState {
     for (auto e : events) cudaEventDestroy(e);
     if (host_nodes) cudaFreeHost(host_nodes);
     if (host_state) cudaFreeHost(host_state);
+    if (host_level_rows) cudaFreeHost(host_level_rows);
+    if (host_level_nodes) cudaFreeHost(host_level_nodes);
   }
 };
 
@@ -143,6 +167,8 @@ Booster::Booster(std::vector<std::shared_ptr<DMatrix>> cache) {
 
 Booster::~Booster() {
   state_.reset();
+  for (auto e : user_events_)
+    if (e) cudaEventDestroy(e);
   if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -241,12 +267,59 @@ void Booster::initialize(DMatrix& d) {
     base_score_.assign(groups_, std::stof(bs->second));
   } else {
     d.upload_info(stream_);
-    const uint32_t chunks = (d.rows + 1023) / 1024;
+    // The intercept is a fixed-order sum over the rows of every rank: with
+    // rows sharded, each rank gathers all labels (and weights) first, so the
+    // result does not depend on the number of GPUs.
+    Comm& comm = Comm::get();
+    const float* labels = d.d_labels.as<float>();
+    const float* weights = d.d_weights.as<float>();
+    uint64_t total = d.rows;
+    DeviceBuffer all_labels, all_weights;
+    if (comm.active()) {
+      const int world = comm.world(), rank = comm.rank();
+      DeviceBuffer counts(size_t(world) * 8);
+      std::vector<unsigned long long> hc(world, 0);
+      hc[rank] = d.rows;
+      XGBB_CUDA(cudaMemcpyAsync(counts.get(), hc.data(), world * 8, cudaMemcpyHostToDevice, stream_));
+      comm.sum_u64(counts.get(), world, stream_);
+      XGBB_CUDA(cudaMemcpyAsync(hc.data(), counts.get(), world * 8, cudaMemcpyDeviceToHost, stream_));
+      XGBB_CUDA(cudaStreamSynchronize(stream_));
+      unsigned long long w_flag = d.weights.empty() ? 0 : 1;
+      {
+        DeviceBuffer f(8);
+        XGBB_CUDA(cudaMemcpyAsync(f.get(), &w_flag, 8, cudaMemcpyHostToDevice, stream_));
+        comm.sum_u64(f.get(), 1, stream_);
+        XGBB_CUDA(cudaMemcpyAsync(&w_flag, f.get(), 8, cudaMemcpyDeviceToHost, stream_));
+        XGBB_CUDA(cudaStreamSynchronize(stream_));
+      }
+      require(w_flag == 0 || w_flag == uint64_t(world), "Either every rank or no rank must set weights.");
+      total = 0;
+      std::vector<uint64_t> offset(world);
+      for (int r = 0; r < world; ++r) {
+        offset[r] = total;
+        total += hc[r];
+      }
+      require(total < (1ull << 32), "Too many rows over all ranks.");
+      all_labels.resize(std::max<uint64_t>(total, 1) * 4);
+      if (w_flag) all_weights.resize(std::max<uint64_t>(total, 1) * 4);
+      XGBB_CUDA(cudaMemcpyAsync(all_labels.as<float>() + offset[rank], labels, size_t(d.rows) * 4,
+                                cudaMemcpyDeviceToDevice, stream_));
+      if (w_flag)
+        XGBB_CUDA(cudaMemcpyAsync(all_weights.as<float>() + offset[rank], weights, size_t(d.rows) * 4,
+                                  cudaMemcpyDeviceToDevice, stream_));
+      for (int r = 0; r < world; ++r) {
+        comm.broadcast(all_labels.as<float>() + offset[r], hc[r] * 4, r, stream_);
+        if (w_flag) comm.broadcast(all_weights.as<float>() + offset[r], hc[r] * 4, r, stream_);
+      }
+      labels = all_labels.as<float>();
+      weights = w_flag ? all_weights.as<float>() : nullptr;
+    }
+    const uint32_t chunks = uint32_t((total + 1023) / 1024);
     DeviceBuffer sums(std::max<uint32_t>(chunks, 1) * 2 * sizeof(double));
     std::vector<double> host(size_t(chunks) * 2);
     for (uint32_t k = 0; k < groups_; ++k) {
-      launch_base_chunks(objective_, d.d_labels.as<float>(), d.d_weights.as<float>(), d.rows, k,
-                         spw_, sums.as<double>(), stream_);
+      launch_base_chunks(objective_, labels, weights, uint32_t(total), k, spw_, sums.as<double>(),
+                         stream_);
       if (chunks)
         XGBB_CUDA(cudaMemcpyAsync(host.data(), sums.get(), host.size() * 8, cudaMemcpyDeviceToHost, stream_));
       XGBB_CUDA(cudaStreamSynchronize(stream_));
@@ -255,7 +328,7 @@ void Booster::initialize(DMatrix& d) {
         sy = sy + host[2 * c];
         sw = sw + host[2 * c + 1];
       }
-      base_score_[k] = sw > 0 ? float(sy / sw) : (objective_ == kSquaredError && d.rows == 0 ? 0.0f : 0.5f);
+      base_score_[k] = sw > 0 ? float(sy / sw) : (objective_ == kSquaredError && total == 0 ? 0.0f : 0.5f);
     }
   }
   // Scores to margins (src/objectives.cpp:17-31; the multiclass intercept of
@@ -286,11 +359,19 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp) {
   ts->d = &d;
   ts->rows = d.rows;
   ts->groups = groups_;
+  ts->rows_total = d.rows;
+  if (Comm::get().active()) {
+    DeviceBuffer n(8);
+    XGBB_CUDA(cudaMemcpyAsync(n.get(), &ts->rows_total, 8, cudaMemcpyHostToDevice, stream_));
+    Comm::get().sum_u64(n.get(), 1, stream_);
+    XGBB_CUDA(cudaMemcpyAsync(&ts->rows_total, n.get(), 8, cudaMemcpyDeviceToHost, stream_));
+    XGBB_CUDA(cudaStreamSynchronize(stream_));
+  }
   const uint32_t n = d.rows, G = groups_, C = d.cols, D = tp_.max_depth;
   const Ellpack& e = d.ell;
   ts->margins.resize(std::max<size_t>(size_t(n) * G, 1) * 4);
   ts->pairs.resize(std::max<size_t>(size_t(n) * G, 1) * 8);
-  ts->mass.resize(size_t(G) * 2 * sizeof(MassAccum));
+  ts->mass.resize(mass_bytes(G));
   ts->scales.resize(size_t(G) * sizeof(float2));
   ts->state.resize(sizeof(DriverState));
   for (int i = 0; i < 2; ++i) {
@@ -323,6 +404,10 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp) {
   XGBB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ts->host_nodes),
                            size_t(G) * ts->capacity * sizeof(DevNode)));
   XGBB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ts->host_state), size_t(G) * sizeof(DriverState)));
+  XGBB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ts->host_level_rows), size_t(G) * kMaxDepth * 8));
+  XGBB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ts->host_level_nodes), size_t(G) * kMaxDepth * 4));
+  ts->level_rows.resize(kMaxDepth * 8);
+  ts->level_nodes.resize(kMaxDepth * 4);
 
   TreeWorkspace& ws = ts->ws;
   ws.state = ts->state.as<DriverState>();
@@ -349,6 +434,8 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp) {
   ws.nodes = ts->nodes.as<DevNode>();
   ws.built = ts->built.as<longlong2>();
   ws.node_capacity = ts->capacity;
+  ws.level_rows = ts->level_rows.as<unsigned long long>();
+  ws.level_nodes = ts->level_nodes.as<uint32_t>();
   ts->hc = hist_config(e, objective_ == kSquaredError && d.weights.empty());
   ts->graphs.assign(G, nullptr);
   if (profiling) {
@@ -418,20 +505,34 @@ void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s) {
                             size_t(ts.capacity) * sizeof(DevNode), cudaMemcpyDeviceToHost, s));
   XGBB_CUDA(cudaMemcpyAsync(ts.host_state + g, ws.state, sizeof(DriverState),
                             cudaMemcpyDeviceToHost, s));
+  XGBB_CUDA(cudaMemcpyAsync(ts.host_level_rows + size_t(g) * kMaxDepth, ws.level_rows,
+                            kMaxDepth * 8, cudaMemcpyDeviceToHost, s));
+  XGBB_CUDA(cudaMemcpyAsync(ts.host_level_nodes + size_t(g) * kMaxDepth, ws.level_nodes,
+                            kMaxDepth * 4, cudaMemcpyDeviceToHost, s));
 }
 
 void Booster::run_round(TrainState& ts) {
   DMatrix& d = *ts.d;
   const uint32_t n = ts.rows, G = ts.groups;
   d.upload_info(stream_);
-  MassAccum* mass = ts.mass.as<MassAccum>();
+  const MassAccum mass = mass_view(ts.mass.get(), G);
   float2* pairs = ts.pairs.as<float2>();
-  XGBB_CUDA(cudaMemsetAsync(mass, 0, size_t(G) * 2 * sizeof(MassAccum), stream_));
+  Comm& comm = Comm::get();
+  // Exact gradient masses are summed over ranks, so every rank derives the
+  // same power-of-two scales as a single GPU holding all rows would.
+  XGBB_CUDA(cudaMemsetAsync(ts.mass.get(), 0, mass_bytes(G), stream_));
   launch_gradients(objective_, ts.margins.as<float>(), d.d_labels.as<float>(),
                    d.d_weights.as<float>(), n, G, spw_, pairs, mass, stream_);
+  comm.max_u32(mass.max_bits, 2 * G, stream_);
   launch_mass_window(pairs, n, G, mass, stream_);
-  launch_scales(pairs, n, G, mass, ts.scales.as<float2>(), n, true, stream_);
+  if (comm.active()) {
+    launch_window_to_limbs(mass, G, stream_);
+    comm.sum_u64(mass.limbs, 8 * size_t(G), stream_);
+    launch_limbs_to_window(mass, G, stream_);
+  }
+  launch_scales(pairs, n, G, mass, ts.scales.as<float2>(), ts.rows_total, true, stream_);
   launch_mass_exact(pairs, n, G, mass, stream_);
+  comm.sum_u64(mass.exact, 20 * size_t(G), stream_);
   launch_scales_exact(G, mass, ts.scales.as<float2>(), stream_);
   const bool use_graph = integer(params_, "cuda_graph", 1) != 0;
   for (uint32_t g = 0; g < G; ++g) {
@@ -467,13 +568,23 @@ void Booster::run_round(TrainState& ts) {
     trees_.push_back(std::move(t));
   }
   if (profiling) {
+    // Algorithmic bytes of a histogram launch: per row the feature codes, the
+    // float gradient pair and (below the root) the row id; per built node the
+    // int64 histogram written.
     const uint32_t D = tp_.max_depth;
+    const Ellpack& e = d.ell;
+    const double row_bytes = double(e.cols) * e.bytes_per_code + 8.0;
+    const double node_bytes = double(hist_node_bytes(e));
     for (uint32_t g = 0; g < G; ++g)
       for (uint32_t depth = 0; depth < D; ++depth) {
         float ms = 0;
         XGBB_CUDA(cudaEventElapsedTime(&ms, ts.events[(size_t(g) * D + depth) * 2],
                                        ts.events[(size_t(g) * D + depth) * 2 + 1]));
+        const double rows = double(ts.host_level_rows[size_t(g) * kMaxDepth + depth]);
+        const double nodes = double(ts.host_level_nodes[size_t(g) * kMaxDepth + depth]);
+        if (nodes == 0) continue;
         profile.hist_ms += ms;
+        profile.hist_bytes += rows * (row_bytes + (depth ? 4.0 : 0.0)) + nodes * node_bytes;
         ++profile.hist_launches;
       }
   }
@@ -496,6 +607,22 @@ void Booster::update(const std::shared_ptr<DMatrix>& d, int) {
 }
 
 void Booster::sync() { XGBB_CUDA(cudaStreamSynchronize(stream_)); }
+
+void Booster::record_event(int slot) {
+  require(slot >= 0 && slot < 64, "event slot out of range");
+  if (user_events_.size() <= size_t(slot)) user_events_.resize(size_t(slot) + 1, nullptr);
+  if (!user_events_[slot]) XGBB_CUDA(cudaEventCreate(&user_events_[slot]));
+  XGBB_CUDA(cudaEventRecord(user_events_[slot], stream_));
+}
+
+float Booster::elapsed_ms(int a, int b) {
+  require(a >= 0 && b >= 0 && size_t(a) < user_events_.size() && size_t(b) < user_events_.size() &&
+              user_events_[a] && user_events_[b], "event not recorded");
+  XGBB_CUDA(cudaEventSynchronize(user_events_[b]));
+  float ms = 0;
+  XGBB_CUDA(cudaEventElapsedTime(&ms, user_events_[a], user_events_[b]));
+  return ms;
+}
 
 std::vector<float> Booster::predict(const std::shared_ptr<DMatrix>& dp, bool output_margin,
                                     uint32_t begin, uint32_t end, bool, std::vector<uint64_t>& shape) {

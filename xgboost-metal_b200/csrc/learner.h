@@ -61,7 +61,11 @@ struct Cuts {
 class DMatrix {
  public:
   uint32_t rows = 0, cols = 0;
-  std::vector<float> data;  // row-major, NaN = missing
+  // Row-major values, NaN = missing: either `owned`, or a caller buffer that
+  // the caller keeps alive and unchanged (zero-copy ingestion).
+  std::vector<float> owned;
+  const float* host = nullptr;
+  bool validated = false;
   std::vector<float> labels, weights, base_margin;
   bool has_missing = false;
 
@@ -117,6 +121,9 @@ class Booster {
   Profile profile;
   bool profiling = false;
   void sync();
+  // CUDA events on the booster's stream, for timing whole rounds on the device.
+  void record_event(int slot);
+  float elapsed_ms(int a, int b);
 
  private:
   struct TrainState;
@@ -139,6 +146,7 @@ class Booster {
   cudaStream_t stream_ = nullptr;
   int device_ = 0;
   std::unique_ptr<TrainState> state_;
+  std::vector<cudaEvent_t> user_events_;
 };
 
 }  // namespace xgbb

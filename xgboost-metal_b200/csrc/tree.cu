@@ -96,6 +96,29 @@ __global__ void quantize_kernel(const float* __restrict__ X, uint32_t rows, uint
   }
 }
 
+__global__ void validate_kernel(const float4* __restrict__ X4, const float* __restrict__ X,
+                                uint64_t n, unsigned int* flags) {
+  unsigned int nan = 0, inf = 0;
+  const uint64_t n4 = X4 ? n / 4 : 0;
+  for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < n4;
+       i += uint64_t(gridDim.x) * blockDim.x) {
+    const float4 v = X4[i];
+    nan |= isnan(v.x) | isnan(v.y) | isnan(v.z) | isnan(v.w);
+    inf |= isinf(v.x) | isinf(v.y) | isinf(v.z) | isinf(v.w);
+  }
+  for (uint64_t i = n4 * 4 + blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < n;
+       i += uint64_t(gridDim.x) * blockDim.x) {
+    nan |= isnan(X[i]);
+    inf |= isinf(X[i]);
+  }
+  nan = __reduce_or_sync(0xffffffffu, nan);
+  inf = __reduce_or_sync(0xffffffffu, inf);
+  if ((threadIdx.x & 31) == 0) {
+    if (nan) atomicOr(flags, 1u);
+    if (inf) atomicOr(flags + 1, 1u);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Gradients and exact power-of-two scales.
 // ---------------------------------------------------------------------------
@@ -126,7 +149,7 @@ __device__ __forceinline__ float2 gradient_pair(int objective, const float* __re
 __global__ void gradient_kernel(int objective, const float* __restrict__ margins,
                                 const float* __restrict__ labels, const float* __restrict__ weights,
                                 uint32_t rows, uint32_t groups, float spw, float2* __restrict__ pairs,
-                                MassAccum* __restrict__ mass) {
+                                MassAccum mass) {
   const uint32_t k = blockIdx.y;
   uint32_t mg = 0, mh = 0;
   for (uint32_t r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
@@ -139,8 +162,8 @@ __global__ void gradient_kernel(int objective, const float* __restrict__ margins
   mg = __reduce_max_sync(0xffffffffu, mg);
   mh = __reduce_max_sync(0xffffffffu, mh);
   if ((threadIdx.x & 31) == 0) {
-    if (mg) atomicMax(&mass[k * 2].max_bits, mg);
-    if (mh) atomicMax(&mass[k * 2 + 1].max_bits, mh);
+    if (mg) atomicMax(mass.max_bits + k * 2, mg);
+    if (mh) atomicMax(mass.max_bits + k * 2 + 1, mh);
   }
 }
 
@@ -182,10 +205,10 @@ __device__ __forceinline__ void atomic_add_u128(unsigned long long* lo, unsigned
 }
 
 __global__ void mass_window_kernel(const float2* __restrict__ pairs, uint32_t rows,
-                                   MassAccum* __restrict__ mass) {
+                                   MassAccum mass) {
   const uint32_t k = blockIdx.y;
-  const uint32_t Lg = window_shift(mass[k * 2].max_bits);
-  const uint32_t Lh = window_shift(mass[k * 2 + 1].max_bits);
+  const uint32_t Lg = window_shift(mass.max_bits[k * 2]);
+  const uint32_t Lh = window_shift(mass.max_bits[k * 2 + 1]);
   unsigned long long glo = 0, ghi = 0, hlo = 0, hhi = 0;
   const float2* p = pairs + size_t(k) * rows;
   for (uint32_t r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
@@ -208,8 +231,8 @@ __global__ void mass_window_kernel(const float2* __restrict__ pairs, uint32_t ro
     hlo = n;
   }
   if ((threadIdx.x & 31) == 0) {
-    if (glo | ghi) atomic_add_u128(&mass[k * 2].lo, &mass[k * 2].hi, glo, ghi);
-    if (hlo | hhi) atomic_add_u128(&mass[k * 2 + 1].lo, &mass[k * 2 + 1].hi, hlo, hhi);
+    if (glo | ghi) atomic_add_u128(mass.window + k * 4, mass.window + k * 4 + 1, glo, ghi);
+    if (hlo | hhi) atomic_add_u128(mass.window + k * 4 + 2, mass.window + k * 4 + 3, hlo, hhi);
   }
 }
 
@@ -225,22 +248,22 @@ __device__ __forceinline__ float scale_for(int bitlen_mass) {
 // One thread per (group, part). The windowed sum A satisfies
 // A * 2^L <= M < (A + n) * 2^L, so bitlen(M) = bitlen(A) + L whenever
 // A + n <= 2^bitlen(A); otherwise the exact fallback decides.
-__global__ void scales_kernel(MassAccum* mass, float2* scales, uint32_t groups,
+__global__ void scales_kernel(MassAccum mass, float2* scales, uint32_t groups,
                               unsigned long long rows_total) {
   const uint32_t i = threadIdx.x;
   if (i >= groups * 2) return;
-  MassAccum& m = mass[i];
-  const uint32_t L = window_shift(m.max_bits);
-  const int bl = bitlen128(m.lo, m.hi);
+  const unsigned long long A_lo = mass.window[2 * i], A_hi = mass.window[2 * i + 1];
+  const uint32_t L = window_shift(mass.max_bits[i]);
+  const int bl = bitlen128(A_lo, A_hi);
   bool decided = true;
   if (L && bl) {
     // A + n <= 2^bl ?
-    const unsigned long long lo = m.lo + rows_total, hi = m.hi + (m.lo + rows_total < m.lo ? 1 : 0);
+    const unsigned long long lo = A_lo + rows_total, hi = A_hi + (A_lo + rows_total < A_lo ? 1 : 0);
     const int bl2 = bitlen128(lo, hi);
     const bool power_of_two = __popcll(lo) + __popcll(hi) == 1;
     decided = bl2 == bl || (bl2 == bl + 1 && power_of_two);
   }
-  m.fallback = decided ? 0u : 1u;
+  mass.fallback[i] = decided ? 0u : 1u;
   if (decided) {
     const float s = scale_for(bl ? bl + int(L) : 0);
     reinterpret_cast<float*>(scales)[i] = s;
@@ -250,9 +273,9 @@ __global__ void scales_kernel(MassAccum* mass, float2* scales, uint32_t groups,
 // Exact fallback: 32-bit limb sums of m * 2^s (each addend < 2^32, so 64-bit
 // limb sums cannot overflow for fewer than 2^32 rows), carried afterwards.
 __global__ void mass_exact_kernel(const float2* __restrict__ pairs, uint32_t rows,
-                                  MassAccum* __restrict__ mass) {
+                                  MassAccum mass) {
   const uint32_t k = blockIdx.y;
-  const bool need_g = mass[k * 2].fallback, need_h = mass[k * 2 + 1].fallback;
+  const bool need_g = mass.fallback[k * 2], need_h = mass.fallback[k * 2 + 1];
   if (!need_g && !need_h) return;
   __shared__ unsigned long long limbs[2][11];
   if (threadIdx.x < 22) (&limbs[0][0])[threadIdx.x] = 0;
@@ -274,17 +297,17 @@ __global__ void mass_exact_kernel(const float2* __restrict__ pairs, uint32_t row
   __syncthreads();
   if (threadIdx.x < 20) {
     const int part = threadIdx.x / 10, w = threadIdx.x % 10;
-    if (limbs[part][w]) atomicAdd(&mass[k * 2 + part].exact[w], limbs[part][w]);
+    if (limbs[part][w]) atomicAdd(mass.exact + (k * 2 + part) * 10 + w, limbs[part][w]);
   }
 }
 
-__global__ void scales_exact_kernel(MassAccum* mass, float2* scales, uint32_t groups) {
+__global__ void scales_exact_kernel(MassAccum mass, float2* scales, uint32_t groups) {
   const uint32_t i = threadIdx.x;
-  if (i >= groups * 2 || !mass[i].fallback) return;
+  if (i >= groups * 2 || !mass.fallback[i]) return;
   uint32_t limb[10];
   unsigned long long carry = 0;
   for (int w = 0; w < 10; ++w) {
-    const unsigned long long s = mass[i].exact[w] + carry;
+    const unsigned long long s = mass.exact[i * 10 + w] + carry;
     limb[w] = uint32_t(s);
     carry = s >> 32;
   }
@@ -944,6 +967,8 @@ __global__ void counts_kernel(const DriverState* state, const uint32_t* seg_begi
 
 struct PlanArgs {
   DriverState* state;
+  unsigned long long* level_rows;
+  uint32_t* level_nodes;
   uint32_t next_depth;
   const uint32_t* parent_slot;
   const uint32_t* seg_begin_cur;
@@ -976,12 +1001,14 @@ __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
     const bool bl = gl <= gr;
     a.built_left[p] = bl ? 1u : 0u;
     tiles = ((bl ? nl : nr) + kTileRows - 1) / kTileRows;
+    if (a.next_depth < kMaxDepth) atomicAdd(a.level_rows + a.next_depth, (unsigned long long)(bl ? nl : nr));
   }
   uint32_t total;
   const uint32_t off = block_exclusive_scan(tiles, &total);
   if (p < pairs) a.tile_offset[p] = off;
   __syncthreads();
   if (threadIdx.x == 0) {
+    if (a.next_depth < kMaxDepth) a.level_nodes[a.next_depth] = pairs;
     a.tile_offset[pairs] = total;
     a.state->frontier = next;
     a.state->depth = a.next_depth;
@@ -993,7 +1020,14 @@ __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
 __global__ void init_tree_kernel(DriverState* state, uint32_t rows, uint32_t* ids,
                                  long long* sums, uint32_t* seg_begin, uint32_t* seg_count,
                                  uint32_t* tile_offset, uint32_t* built_left,
-                                 unsigned long long* keys, DevNode* nodes) {
+                                 unsigned long long* keys, DevNode* nodes,
+                                 unsigned long long* level_rows, uint32_t* level_nodes) {
+  for (uint32_t d = 0; d < kMaxDepth; ++d) {
+    level_rows[d] = 0;
+    level_nodes[d] = 0;
+  }
+  level_rows[0] = rows;
+  level_nodes[0] = 1;
   const uint32_t tiles = (rows + kTileRows - 1) / kTileRows;
   DriverState s{};
   s.node_count = 1;
@@ -1065,6 +1099,29 @@ __global__ void transform_kernel(int objective, float* v, uint32_t rows, uint32_
   }
 }
 
+__global__ void window_to_limbs_kernel(MassAccum m, uint32_t n) {
+  const uint32_t i = threadIdx.x;
+  if (i >= n) return;
+  const unsigned long long lo = m.window[2 * i], hi = m.window[2 * i + 1];
+  m.limbs[4 * i] = lo & 0xffffffffull;
+  m.limbs[4 * i + 1] = lo >> 32;
+  m.limbs[4 * i + 2] = hi & 0xffffffffull;
+  m.limbs[4 * i + 3] = hi >> 32;
+}
+
+__global__ void limbs_to_window_kernel(MassAccum m, uint32_t n) {
+  const uint32_t i = threadIdx.x;
+  if (i >= n) return;
+  unsigned long long carry = 0, w[4];
+  for (int k = 0; k < 4; ++k) {
+    const unsigned long long s = m.limbs[4 * i + k] + carry;
+    w[k] = s & 0xffffffffull;
+    carry = s >> 32;
+  }
+  m.window[2 * i] = w[0] | (w[1] << 32);
+  m.window[2 * i + 1] = w[2] | (w[3] << 32);
+}
+
 int grid_for(uint64_t work, int threads, int cap = 148 * 16) {
   const uint64_t blocks = (work + threads - 1) / threads;
   return int(std::max<uint64_t>(1, std::min<uint64_t>(blocks, uint64_t(cap))));
@@ -1075,6 +1132,28 @@ int grid_for(uint64_t work, int threads, int cap = 148 * 16) {
 // ---------------------------------------------------------------------------
 // Launchers.
 // ---------------------------------------------------------------------------
+MassAccum mass_view(void* base, uint32_t groups) {
+  char* p = static_cast<char*>(base);
+  const size_t n = size_t(groups) * 2;
+  MassAccum m;
+  m.window = reinterpret_cast<unsigned long long*>(p);
+  m.limbs = m.window + 2 * n;
+  m.exact = m.limbs + 4 * n;
+  m.max_bits = reinterpret_cast<unsigned int*>(m.exact + 10 * n);
+  m.fallback = m.max_bits + n;
+  return m;
+}
+
+void launch_window_to_limbs(MassAccum m, uint32_t groups, cudaStream_t stream) {
+  window_to_limbs_kernel<<<1, 64 * ((2 * groups + 63) / 64), 0, stream>>>(m, 2 * groups);
+  XGBB_CUDA(cudaGetLastError());
+}
+
+void launch_limbs_to_window(MassAccum m, uint32_t groups, cudaStream_t stream) {
+  limbs_to_window_kernel<<<1, 64 * ((2 * groups + 63) / 64), 0, stream>>>(m, 2 * groups);
+  XGBB_CUDA(cudaGetLastError());
+}
+
 void launch_quantize(const float* X, uint32_t rows, uint32_t cols, const float* cuts,
                      const uint32_t* counts, uint32_t bins, void* codes, uint32_t stride,
                      uint32_t bytes_per_code, uint32_t missing, cudaStream_t stream) {
@@ -1090,9 +1169,17 @@ void launch_quantize(const float* X, uint32_t rows, uint32_t cols, const float* 
   XGBB_CUDA(cudaGetLastError());
 }
 
+void launch_validate(const float* X, uint64_t n, unsigned int* flags, cudaStream_t stream) {
+  if (!n) return;
+  const bool aligned = (reinterpret_cast<uintptr_t>(X) & 15) == 0;
+  validate_kernel<<<grid_for(n / 4 + 1, 256, 148 * 8), 256, 0, stream>>>(
+      aligned ? reinterpret_cast<const float4*>(X) : nullptr, X, n, flags);
+  XGBB_CUDA(cudaGetLastError());
+}
+
 void launch_gradients(int objective, const float* margins, const float* labels,
                       const float* weights, uint32_t rows, uint32_t groups, float spw,
-                      float2* pairs, MassAccum* mass, cudaStream_t stream) {
+                      float2* pairs, MassAccum mass, cudaStream_t stream) {
   if (!rows) return;
   const int threads = 256;
   dim3 grid(grid_for(rows, threads, 148 * 4), groups);
@@ -1101,7 +1188,7 @@ void launch_gradients(int objective, const float* margins, const float* labels,
   XGBB_CUDA(cudaGetLastError());
 }
 
-void launch_mass_window(const float2* pairs, uint32_t rows, uint32_t groups, MassAccum* mass,
+void launch_mass_window(const float2* pairs, uint32_t rows, uint32_t groups, MassAccum mass,
                         cudaStream_t stream) {
   if (!rows) return;
   const int threads = 256;
@@ -1110,13 +1197,13 @@ void launch_mass_window(const float2* pairs, uint32_t rows, uint32_t groups, Mas
   XGBB_CUDA(cudaGetLastError());
 }
 
-void launch_scales(const float2*, uint32_t, uint32_t groups, MassAccum* mass, float2* scales,
+void launch_scales(const float2*, uint32_t, uint32_t groups, MassAccum mass, float2* scales,
                    unsigned long long rows_total, bool, cudaStream_t stream) {
   scales_kernel<<<1, 64 * ((2 * groups + 63) / 64), 0, stream>>>(mass, scales, groups, rows_total);
   XGBB_CUDA(cudaGetLastError());
 }
 
-void launch_mass_exact(const float2* pairs, uint32_t rows, uint32_t groups, MassAccum* mass,
+void launch_mass_exact(const float2* pairs, uint32_t rows, uint32_t groups, MassAccum mass,
                        cudaStream_t stream) {
   if (!rows) return;
   const int threads = 256;
@@ -1125,7 +1212,7 @@ void launch_mass_exact(const float2* pairs, uint32_t rows, uint32_t groups, Mass
   XGBB_CUDA(cudaGetLastError());
 }
 
-void launch_scales_exact(uint32_t groups, MassAccum* mass, float2* scales, cudaStream_t stream) {
+void launch_scales_exact(uint32_t groups, MassAccum mass, float2* scales, cudaStream_t stream) {
   scales_exact_kernel<<<1, 64 * ((2 * groups + 63) / 64), 0, stream>>>(mass, scales, groups);
   XGBB_CUDA(cudaGetLastError());
 }
@@ -1177,7 +1264,8 @@ void launch_hist_t(const HistArgs& args, int blocks, int threads, size_t smem, c
 void tree_init(const TreeWorkspace& ws, const TreeLaunch& tl, cudaStream_t stream) {
   init_tree_kernel<<<1, 1, 0, stream>>>(ws.state, tl.ell.rows, ws.ids[0], ws.sums[0],
                                         ws.seg_begin[0], ws.seg_count[0], ws.tile_offset,
-                                        ws.built_left, ws.keys[0], ws.nodes);
+                                        ws.built_left, ws.keys[0], ws.nodes, ws.level_rows,
+                                        ws.level_nodes);
   XGBB_CUDA(cudaGetLastError());
 }
 
@@ -1312,6 +1400,8 @@ void tree_level_plan(const TreeWorkspace& ws, const TreeLaunch&, uint32_t next_d
                      cudaStream_t stream) {
   PlanArgs a;
   a.state = ws.state;
+  a.level_rows = ws.level_rows;
+  a.level_nodes = ws.level_nodes;
   a.next_depth = next_depth;
   a.parent_slot = ws.parent_slot;
   a.seg_begin_cur = ws.seg_begin[(next_depth + 1) & 1];

@@ -9,7 +9,8 @@
 namespace xgbb {
 
 // Quantised feature matrix in HBM: row-major ELLPACK, one code per
-// (row, feature), uint8 or uint16, `missing` = the type's maximum code.
+// (row, feature), uint8 or uint16. `missing` is the type's maximum code, or
+// 0x100 for uint8 codes when all 256 codes are bins (no missing value).
 // Each row is padded to `stride` codes (a multiple of 16 bytes) with missing.
 struct Ellpack {
   const void* codes = nullptr;
@@ -22,13 +23,22 @@ struct Ellpack {
   const float* minima = nullptr;            // [cols]
 };
 
-// Exact magnitude accumulators for the gradient scales of one (group, part).
+// Exact magnitude accumulators for the gradient scales, one entry per
+// (group, part) with part 0 = g, 1 = h; separate arrays so that each can be
+// reduced over ranks with one NCCL call.
 struct MassAccum {
-  unsigned int max_bits;       // max |value| bits (exponent is what matters)
-  unsigned int fallback;       // 1 when the windowed sum cannot decide the exponent
-  unsigned long long lo, hi;   // 128-bit windowed sum
-  unsigned long long exact[10];// exact 320-bit sum in 32-bit limbs (fallback path)
+  unsigned int* max_bits;         // [2G] max |value| bits (max over ranks)
+  unsigned int* fallback;         // [2G] 1 when the windowed sum cannot decide
+  unsigned long long* window;     // [2G][2] 128-bit windowed sum (lo, hi)
+  unsigned long long* limbs;      // [2G][4] the windowed sum as 32-bit limbs (sum over ranks)
+  unsigned long long* exact;      // [2G][10] 32-bit limb sums of the exact magnitude
 };
+// Bytes of the accumulators for `groups` output groups (one allocation).
+inline size_t mass_bytes(uint32_t groups) { return size_t(groups) * 2 * (4 + 4 + 16 + 32 + 80); }
+MassAccum mass_view(void* base, uint32_t groups);
+// Cross-rank transport of the windowed sums: window -> limbs and back.
+void launch_window_to_limbs(MassAccum m, uint32_t groups, cudaStream_t stream);
+void launch_limbs_to_window(MassAccum m, uint32_t groups, cudaStream_t stream);
 
 // Everything one tree needs on the device; pointers are fixed for a booster,
 // so the launch sequence can be captured once as a CUDA graph and replayed.
@@ -55,6 +65,8 @@ struct TreeWorkspace {
   longlong2* bank[2];        // [slots][cols][bins + 1]
   uint32_t* rows[2];         // row ids per level (level 0 uses the identity)
   uint32_t node_capacity;
+  unsigned long long* level_rows;  // [kMaxDepth] rows in built nodes per level
+  uint32_t* level_nodes;           // [kMaxDepth] built nodes per level
 };
 
 struct TreeLaunch {
@@ -74,19 +86,21 @@ struct TreeLaunch {
 void launch_quantize(const float* X, uint32_t rows, uint32_t cols, const float* cuts,
                      const uint32_t* counts, uint32_t bins, void* codes, uint32_t stride,
                      uint32_t bytes_per_code, uint32_t missing, cudaStream_t stream);
+// flags[0] |= any NaN, flags[1] |= any infinity over n values.
+void launch_validate(const float* X, uint64_t n, unsigned int* flags, cudaStream_t stream);
 void launch_gradients(int objective, const float* margins, const float* labels,
                       const float* weights, uint32_t rows, uint32_t groups, float scale_pos_weight,
-                      float2* pairs, MassAccum* mass, cudaStream_t stream);
-void launch_mass_window(const float2* pairs, uint32_t rows, uint32_t groups, MassAccum* mass,
+                      float2* pairs, MassAccum mass, cudaStream_t stream);
+void launch_mass_window(const float2* pairs, uint32_t rows, uint32_t groups, MassAccum mass,
                         cudaStream_t stream);
 // Reduces per-rank accumulators (already summed across ranks if sharded) to
 // scales; runs the exact fallback when needed. rows_total = rows over ranks.
-void launch_scales(const float2* pairs, uint32_t rows, uint32_t groups, MassAccum* mass,
+void launch_scales(const float2* pairs, uint32_t rows, uint32_t groups, MassAccum mass,
                    float2* scales, unsigned long long rows_total, bool may_fallback,
                    cudaStream_t stream);
-void launch_mass_exact(const float2* pairs, uint32_t rows, uint32_t groups, MassAccum* mass,
+void launch_mass_exact(const float2* pairs, uint32_t rows, uint32_t groups, MassAccum mass,
                        cudaStream_t stream);
-void launch_scales_exact(uint32_t groups, MassAccum* mass, float2* scales, cudaStream_t stream);
+void launch_scales_exact(uint32_t groups, MassAccum mass, float2* scales, cudaStream_t stream);
 void launch_base_chunks(int objective, const float* labels, const float* weights, uint32_t rows,
                         uint32_t group, float scale_pos_weight, double* chunk_sums,
                         cudaStream_t stream);

@@ -94,19 +94,23 @@ class DMatrix:
             raise XGBoostError("Ranking groups are not implemented by the CUDA backend.")
         self.handle = ctypes.c_void_p()
         miss = np.nan if missing is None else float(missing)
-        config = json.dumps({"missing": None if np.isnan(miss) else miss, "nthread": nthread or 0})
+        config = {"missing": None if np.isnan(miss) else miss, "nthread": nthread or 0}
         if _is_scipy_csr(data):
             csr = data
             _check_call(_LIB.XGDMatrixCreateFromCSR(
                 _c_str(_array_interface(csr.indptr)), _c_str(_array_interface(csr.indices)),
                 _c_str(_array_interface(np.asarray(csr.data, dtype=np.float32))),
-                c_bst_ulong(csr.shape[1]), _c_str(config), ctypes.byref(self.handle)))
+                c_bst_ulong(csr.shape[1]), _c_str(json.dumps(config)), ctypes.byref(self.handle)))
         else:
             arr = _to_2d_float(data)
-            self._data_ref = arr
+            # A C-contiguous float32 array with NaN as the missing value is
+            # read in place (no host copy); this object keeps it alive. It must
+            # not be modified while the DMatrix exists.
+            if arr.dtype == np.float32 and arr.flags.c_contiguous and np.isnan(miss):
+                config["zero_copy"] = True
+                self._data_ref = arr
             _check_call(_LIB.XGDMatrixCreateFromDense(
-                _c_str(_array_interface(arr)), _c_str(config), ctypes.byref(self.handle)))
-            self._data_ref = None
+                _c_str(_array_interface(arr)), _c_str(json.dumps(config)), ctypes.byref(self.handle)))
         self.feature_names = list(feature_names) if feature_names is not None else (
             [str(c) for c in data.columns] if hasattr(data, "columns") else None)
         self.feature_types = feature_types
@@ -302,6 +306,20 @@ class Booster:
         out = ctypes.c_char_p()
         _check_call(_LIB.XGBoosterGetCudaProfile(self.handle, ctypes.byref(out)))
         return json.loads(out.value.decode())
+
+    def reset_cuda_profile(self):
+        _check_call(_LIB.XGBoosterResetCudaProfile(self.handle))
+
+    def record_event(self, slot):
+        """Records CUDA event `slot` on the booster's stream (device timing)."""
+        _check_call(_LIB.XGBoosterRecordEvent(self.handle, ctypes.c_int(int(slot))))
+
+    def event_elapsed(self, a, b):
+        """Device milliseconds between two recorded events."""
+        ms = ctypes.c_float()
+        _check_call(_LIB.XGBoosterEventElapsed(self.handle, ctypes.c_int(a), ctypes.c_int(b),
+                                               ctypes.byref(ms)))
+        return ms.value
 
     def copy(self):
         raise XGBoostError("Booster copies are not implemented by the CUDA backend yet.")
