@@ -213,65 +213,99 @@ def launches_per_round(depth, groups):
 # ---------------------------------------------------------------------------
 # CPU baselines
 # ---------------------------------------------------------------------------
+def _fit_to_full(samples, full_rows):
+    """Per-round seconds at `full_rows` from (rows, seconds) samples: a + b*rows
+    by least squares (the split search is a per-node cost, the histograms and
+    partitions a per-row cost)."""
+    r = np.array([s[0] for s in samples], np.float64)
+    t = np.array([s[1] for s in samples], np.float64)
+    if len(set(r.tolist())) == 1:
+        return float(t.mean()) * full_rows / r[0]
+    b, a = np.polyfit(r, t, 1)
+    return float(a + b * full_rows)
+
+
+def _sample_sizes(wl):
+    rows = WORKLOADS[wl]["rows"]
+    if rows <= 300_000:
+        return [rows]
+    return [25_000, 100_000]
+
+
 def cpu_oracle_baseline(wl, device):
-    """The single-threaded oracle on a bounded sample; per-round cost from the
-    difference of 2-round and 0-round runs, scaled by rows to the workload."""
+    """The single-threaded oracle on bounded samples: per-round cost as the
+    difference of 2-round and 0-round runs, fitted over two sample sizes and
+    evaluated at the workload's rows."""
     import checkers as C
     spec = WORKLOADS[wl]
-    rows = min(spec["rows"], 100_000 if wl == "c4" else spec["rows"])
-    X, y = gen_rows(wl, 0, rows, device, pin=False)
     p = C.train_params(dict(objective=spec["objective"], max_depth=spec["max_depth"],
                             eta=spec["eta"]))
-    t = time.perf_counter()
-    C.oracle_train(X, y, p, 0)
-    t0 = time.perf_counter() - t
-    t = time.perf_counter()
-    C.oracle_train(X, y, p, 2)
-    t2 = time.perf_counter() - t
-    per_round = max(t2 - t0, 1e-9) / 2
-    value = per_round * 1000 * 100 * spec["rows"] / rows
-    return {"value": value, "unit": UNIT, "cores": 1, "kind": "port",
-            "sample": "oracle (single-threaded C) on the first %d rows, 2 rounds minus setup, "
-                      "scaled by rows to %d rows and to 100 rounds" % (rows, spec["rows"])}
+    samples = []
+    for rows in _sample_sizes(wl):
+        X, y = gen_rows(wl, 0, rows, device, pin=False)
+        t = time.perf_counter()
+        C.oracle_train(X, y, p, 0)
+        t0 = time.perf_counter() - t
+        t = time.perf_counter()
+        C.oracle_train(X, y, p, 2)
+        t2 = time.perf_counter() - t
+        samples.append((rows, max(t2 - t0, 1e-9) / 2))
+    per_round = _fit_to_full(samples, spec["rows"])
+    value = per_round * 1000 * 100
+    return {"value": round(value, 1), "unit": UNIT, "cores": 1, "kind": "port",
+            "sample": "oracle (single-threaded C): per-round seconds %s on the first rows, "
+                      "linear fit in rows evaluated at %d rows, x100 rounds"
+                      % (", ".join("%d rows %.3fs" % s for s in samples), spec["rows"])}
 
 
 def reference_arm(args, wl, device):
-    """The reference's own serial split/driver/predict functions (oracle/_ref),
-    on a bounded sample per step, scaled to the workload."""
+    """The reference's own serial split/driver/predict functions (oracle/_ref,
+    every host thread), one boosting round per step on bounded samples
+    (alternating two sizes), fitted in rows to the workload."""
     import checkers as C
     spec = WORKLOADS[wl]
-    rows = min(spec["rows"], 50_000 if wl == "c4" else spec["rows"])
-    X, y = gen_rows(wl, 0, rows, device, pin=False)
     kind = "reference" if C.have_reference() else "port"
     chk = C.reference() if kind == "reference" else C.oracle()
     o = C.oracle()
-    cuts, counts, minima = o.sketch_cuts(X, 256)
-    bins = o.quantize(X, cuts, counts)
-    margins = np.zeros((rows, 1), np.float32)
+    sizes = _sample_sizes(wl) if spec["rows"] <= 300_000 else [10_000, 40_000]
+    setups = []
+    for rows in sizes:
+        X, y = gen_rows(wl, 0, rows, device, pin=False)
+        cuts, counts, minima = o.sketch_cuts(X, 256)
+        setups.append(dict(rows=rows, y=y, bins=o.quantize(X, cuts, counts), cuts=cuts,
+                           counts=counts, minima=minima, margins=np.zeros((rows, 1), np.float32)))
     tp = dict(max_depth=spec["max_depth"], eta=spec["eta"], reg_lambda=1.0, reg_alpha=0.0,
               min_child_weight=1.0, max_delta_step=0.0, min_split_loss=0.0)
-    times = []
+    samples = []
     for step in range(args.warmup + args.steps):
+        st = setups[step % len(setups)]
         t = time.perf_counter()
-        pairs = C.oracle_gradients(spec["objective"], margins, y)
+        pairs = C.oracle_gradients(spec["objective"], st["margins"], st["y"])
         scale = chk.gradient_scales(pairs)
         q = chk.quantize_gradients(pairs, scale)[:, 0, :]
-        _, leaf = chk.grow_tree(bins, q, scale[0], cuts, counts, minima, tp)
-        margins[:, 0] += leaf
+        _, leaf = chk.grow_tree(st["bins"], q, scale[0], st["cuts"], st["counts"], st["minima"], tp)
+        st["margins"][:, 0] += leaf
         if step >= args.warmup:
-            times.append(time.perf_counter() - t)
-    per_round = float(np.mean(times))
-    value = per_round * 1000 * 100 * spec["rows"] / rows
-    sample = ("%s per-round tree on the first %d rows (%d timed steps), scaled by rows to %d "
-              "and to 100 rounds" % ("oracle/_ref reference functions" if kind == "reference"
-                                     else "oracle port", rows, args.steps, spec["rows"]))
-    return {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": value / 100,
-            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "int64",
-            "data": "synthetic", "config": {"workload": wl, "rows": spec["rows"], "cols": spec["cols"],
-                                            "max_depth": spec["max_depth"]},
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": 1, "kind": kind, "sample": sample},
-            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            samples.append((st["rows"], time.perf_counter() - t))
+    per_round = _fit_to_full(samples, spec["rows"])
+    value = per_round * 1000 * 100
+    cores = os.cpu_count() if kind == "reference" else 1
+    sample = ("%s, one round per step on the first %s rows (%d timed steps, means %s), linear "
+              "fit in rows evaluated at %d rows, x100 rounds"
+              % ("reference kernel functions compiled for the host (oracle/_ref)" if kind == "reference"
+                 else "oracle port", "/".join(str(x) for x in sizes), args.steps,
+                 ", ".join("%.3fs" % np.mean([t for r, t in samples if r == x]) for x in sizes),
+                 spec["rows"]))
+    return {"impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": UNIT,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(value / 100, 3), "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int64", "data": "synthetic",
+            "config": {"workload": wl, "rows": spec["rows"], "cols": spec["cols"],
+                       "max_depth": spec["max_depth"], "objective": spec["objective"]},
+            "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": cores, "kind": kind,
+                             "sample": sample},
+            "e2e": {"value": round(value, 1), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
 
 
 def measured_peak():

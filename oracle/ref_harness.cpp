@@ -18,6 +18,9 @@
 //   tree_driver_apply        kernels/tree_driver.metal.h:28-94
 //   split_left               kernels/boost.metal:1325-1329
 //   predict                  kernels/boost.metal:1738-1765
+#include <thread>  // before the shim, whose `thread` address-space macro it must not see
+using host_thread = std::thread;
+
 #include "metal_shim.hpp"
 #include "metalgb/shared.h"
 using namespace metalgb;
@@ -41,6 +44,25 @@ u32 sketch_budget(u32 bins, u32 count) {
 }
 
 u32 round_up(u32 v, u32 m) { return (v + m - 1) / m * m; }
+
+// Runs body(i) for i in [0, n) on every host thread. The reference runs these
+// loops as independent GPU threads (one per (node, feature) or per row tile),
+// so their order does not matter; the bench's CPU arm uses all host cores.
+template <class F>
+void parallel_for(u32 n, F body) {
+  u32 threads = std::max(1u, host_thread::hardware_concurrency());
+  threads = std::min(threads, std::max(1u, n));
+  if (threads == 1) {
+    for (u32 i = 0; i < n; ++i) body(i);
+    return;
+  }
+  std::vector<host_thread> pool;
+  for (u32 t = 0; t < threads; ++t)
+    pool.emplace_back([=, &body] {
+      for (u32 i = t; i < n; i += threads) body(i);
+    });
+  for (auto& th : pool) th.join();
+}
 
 // Cuts for one numeric feature, following Matrix::make_quantile_cuts
 // (src/quantile.cpp:22-213) with the serial summary, reduction and cut
@@ -207,12 +229,18 @@ void xgbref_evaluate_splits(const int64_t* hist, uint32_t nodes, uint32_t cols, 
   p.max_cat_to_onehot = 4; p.max_cat_threshold = 64; p.sort_stride = 1; p.has_categorical = 0;
   p.use_parent_sums = use_parent_sums;
   float2 s(scale[0], scale[1]);
-  for (u32 n = 0; n < nodes; ++n)
-    for (u32 f = 0; f < cols; ++f)
-      evaluate_splits<>(reinterpret_cast<const uint*>(hist), &s, cuts, counts, minima, monotone.data(),
-                        bounds.data(), allowed.data(), reinterpret_cast<Split*>(out), categorical.data(),
-                        dummy2, dummy_u, dummy_cat, reinterpret_cast<const long2*>(node_sums), p,
-                        uint2(f, n));
+  parallel_for(nodes * cols, [&](u32 i) {
+    const u32 n = i / cols, f = i % cols;
+    float2 local_dummy[1] = {float2(0)};
+    uint local_u[1] = {0}, local_cat[1] = {0};
+    evaluate_splits<>(reinterpret_cast<const uint*>(hist), &s, cuts, counts, minima, monotone.data(),
+                      bounds.data(), allowed.data(), reinterpret_cast<Split*>(out), categorical.data(),
+                      local_dummy, local_u, local_cat, reinterpret_cast<const long2*>(node_sums), p,
+                      uint2(f, n));
+  });
+  (void)dummy2;
+  (void)dummy_u;
+  (void)dummy_cat;
 }
 
 void xgbref_select_splits(const void* candidates, uint32_t nodes, uint32_t cols, const float* scale,
@@ -281,14 +309,17 @@ int xgbref_grow_tree(const uint32_t* bins, uint32_t rows, uint32_t cols, const i
       seg_count[s] = u32(segments[s].size());
       seg_offset[s] = offset;
       offset += seg_count[s];
-      for (u32 r : segments[s])
-        for (u32 f = 0; f < cols; ++f) {
+    }
+    // Exact int64 sums, one feature per task.
+    parallel_for(cols, [&](u32 f) {
+      for (u32 s = 0; s < nodes; ++s)
+        for (u32 r : segments[s]) {
           u32 b = bins[std::size_t(r) * cols + f];
           std::size_t cell = ((std::size_t(s) * cols + f) * (B + 1) + (b == 0xffffffffu ? B : b)) * 2;
           hist[cell] = int64_t(uint64_t(hist[cell]) + uint64_t(q[std::size_t(r) * 2]));
           hist[cell + 1] = int64_t(uint64_t(hist[cell + 1]) + uint64_t(q[std::size_t(r) * 2 + 1]));
         }
-    }
+    });
     std::vector<Split> candidates(std::size_t(nodes) * cols), best(nodes);
     xgbref_evaluate_splits(hist.data(), nodes, cols, B, scale, cuts, counts, minima, reg_lambda,
                            reg_alpha, min_child_weight, max_delta_step, depth != 0,

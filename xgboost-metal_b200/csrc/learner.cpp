@@ -84,9 +84,14 @@ void DMatrix::set_cuts(std::shared_ptr<Cuts> c, cudaStream_t stream) {
   ell.rows = rows;
   ell.cols = cols;
   ell.bytes_per_code = narrow ? 1 : 2;
-  // With 256 bins and no missing value every uint8 code is a bin, so the
-  // missing code is one no stored code can equal.
-  ell.missing = narrow ? (max_count <= 255 ? 0xffu : 0x100u) : 0xffffu;
+  // The missing code is the cut stride B (the histogram's missing bin) when it
+  // fits the code type; with uint8 codes and B = 256 it is 255 (a missing
+  // value then implies at most 255 bins), and with 256 bins and no missing
+  // value it is 0x100, which no stored code can equal.
+  const uint32_t B = c->stride;
+  if (!narrow) ell.missing = B;
+  else if (B <= 255) ell.missing = B;
+  else ell.missing = max_count <= 255 ? 0xffu : 0x100u;
   const uint32_t align = 16 / ell.bytes_per_code;
   ell.stride = std::max(align, (cols + align - 1) / align * align);
   ell.bins = c->stride;
@@ -459,7 +464,13 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp) {
   return *state_;
 }
 
-void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s) {
+void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s, bool capturing) {
+  // Inside a capture the profiling events become external event-record nodes,
+  // recorded again at every launch of the graph.
+  auto mark = [&](cudaEvent_t ev) {
+    if (capturing) XGBB_CUDA(cudaEventRecordWithFlags(ev, s, cudaEventRecordExternal));
+    else XGBB_CUDA(cudaEventRecord(ev, s));
+  };
   DMatrix& d = *ts.d;
   Comm& comm = Comm::get();
   TreeLaunch tl{};
@@ -467,6 +478,7 @@ void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s) {
   tl.params = tp_;
   tl.pairs = ts.pairs.as<float2>() + size_t(g) * ts.rows;
   tl.scale = ts.scales.as<float2>() + g;
+  tl.max_bits = mass_view(ts.mass.get(), ts.groups).max_bits + 2 * g;
   tl.margins = ts.margins.as<float>();
   tl.groups = ts.groups;
   tl.group = g;
@@ -476,7 +488,7 @@ void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s) {
   tl.hist_threads = ts.hc.threads;
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device_);
-  tl.hist_blocks = sms * 2;
+  tl.hist_blocks = sms;
   tl.eval_blocks = sms * 8;
   tl.part_blocks = sms * 8;
   const TreeWorkspace& ws = ts.ws;
@@ -484,9 +496,9 @@ void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s) {
   const size_t node_bytes = hist_node_bytes(d.ell);
   tree_init(ws, tl, s);
   for (uint32_t depth = 0; depth < D; ++depth) {
-    if (profiling) XGBB_CUDA(cudaEventRecord(ts.events[(size_t(g) * D + depth) * 2], s));
+    if (profiling) mark(ts.events[(size_t(g) * D + depth) * 2]);
     tree_level_hist(ws, tl, depth, s);
-    if (profiling) XGBB_CUDA(cudaEventRecord(ts.events[(size_t(g) * D + depth) * 2 + 1], s));
+    if (profiling) mark(ts.events[(size_t(g) * D + depth) * 2 + 1]);
     comm.sum_u64(ws.built, size_t(max_pairs_at(depth)) * node_bytes / 8, s);
     tree_level_eval(ws, tl, depth, s);
     tree_level_control(ws, tl, depth, s);
@@ -535,17 +547,19 @@ void Booster::run_round(TrainState& ts) {
   comm.sum_u64(mass.exact, 20 * size_t(G), stream_);
   launch_scales_exact(G, mass, ts.scales.as<float2>(), stream_);
   const bool use_graph = integer(params_, "cuda_graph", 1) != 0;
+  bool captured = false;
   for (uint32_t g = 0; g < G; ++g) {
     if (use_graph) {
       if (!ts.graphs[g]) {
         // Kernel attributes are set on first use, outside any capture.
-        record_tree_launches(ts, g, stream_);
+        record_tree_launches(ts, g, stream_, false);
         XGBB_CUDA(cudaStreamSynchronize(stream_));
         cudaGraph_t graph;
         XGBB_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
         // The eager tree above already trained this group; replaying it would
         // train the same tree twice, so the graph is only captured here.
-        record_tree_launches(ts, g, stream_);
+        record_tree_launches(ts, g, stream_, true);
+        captured = true;
         XGBB_CUDA(cudaStreamEndCapture(stream_, &graph));
         XGBB_CUDA(cudaGraphInstantiate(&ts.graphs[g], graph, 0));
         XGBB_CUDA(cudaGraphDestroy(graph));
@@ -553,7 +567,7 @@ void Booster::run_round(TrainState& ts) {
         XGBB_CUDA(cudaGraphLaunch(ts.graphs[g], stream_));
       }
     } else {
-      record_tree_launches(ts, g, stream_);
+      record_tree_launches(ts, g, stream_, false);
     }
   }
   XGBB_CUDA(cudaStreamSynchronize(stream_));
@@ -567,7 +581,7 @@ void Booster::run_round(TrainState& ts) {
     t.nodes.assign(src, src + st.node_count);
     trees_.push_back(std::move(t));
   }
-  if (profiling) {
+  if (profiling && !captured) {
     // Algorithmic bytes of a histogram launch: per row the feature codes, the
     // float gradient pair and (below the root) the row id; per built node the
     // int64 histogram written.

@@ -131,7 +131,7 @@ class Booster {
   void initialize(DMatrix& d);
   TrainState& train_state(const std::shared_ptr<DMatrix>& d);
   void run_round(TrainState& ts);
-  void record_tree_launches(TrainState& ts, uint32_t group, cudaStream_t stream);
+  void record_tree_launches(TrainState& ts, uint32_t group, cudaStream_t stream, bool capturing);
   void materialize();
 
   std::map<std::string, std::string> params_;

@@ -372,6 +372,7 @@ struct HistArgs {
   Ellpack e;
   const float2* pairs;
   const float2* scale;
+  const unsigned int* max_bits;  // largest |g| and |h| bits of this group (float bits)
   const uint32_t* rows;
   const DriverState* state;
   const uint32_t* tile_offset;
@@ -379,19 +380,56 @@ struct HistArgs {
   const uint32_t* seg_begin;
   const uint32_t* seg_count;
   longlong2* built;
-  uint32_t fg, ngroups;
+  uint32_t ngroups;
 };
 
-// Histograms of the built child of every node pair (or of the root). Each CTA
-// walks a contiguous run of (feature group, pair, row tile) work items,
-// accumulating exact int64 sums in shared memory, and flushes them with
-// global 64-bit atomics when the (group, pair) changes.
+constexpr int kHistWarps = 32;          // 1024 threads, one CTA per SM
+constexpr uint32_t kHistLanes = 32;     // features per CTA: lane = feature
+
+// Width of the limbs of one value type: three signed 32-bit limbs of L bits
+// hold the CTA's exact int64 per-bin sums. L >= 17 keeps the top limb (bits
+// >= 2L of a sum below 2^63) inside int32; L >= bitlen(max|q|)/3 keeps every
+// single value inside three limbs.
+__device__ __forceinline__ uint32_t limb_width(unsigned int max_bits, float scale) {
+  const float mv = __uint_as_float(max_bits & 0x7fffffffu);
+  const long long qm = __float2ll_rn(__fmul_rn(mv, scale));
+  const unsigned long long a = (unsigned long long)(qm < 0 ? -qm : qm);
+  const uint32_t bl = a ? 64u - __clzll(a) : 0u;
+  const uint32_t L = (bl + 2) / 3;
+  return L < 17 ? 17u : (L > 21 ? 21u : L);
+}
+
+__device__ __forceinline__ long long combine_limbs(const int* base, uint32_t plane, uint32_t L) {
+  const unsigned long long v = (unsigned long long)(long long)base[0] +
+                               ((unsigned long long)(long long)base[plane] << L) +
+                               ((unsigned long long)(long long)base[2 * plane] << (2 * L));
+  return (long long)v;
+}
+
+// Histograms of the built child of every node pair (or of the root).
+//
+// One CTA per SM walks a contiguous run of (feature group, pair, row tile)
+// work items. Lane f of every warp owns feature f0 + f, so the 32 lanes of an
+// atomic touch 32 consecutive words ([bin][32] layout): no bank conflicts.
+// Exact int64 sums live in three signed 32-bit limbs per value (shared-memory
+// atomics are 32-bit), carried between limbs every 2^(31-L) rows, and are
+// recombined and flushed with 64-bit global atomics when the (group, pair)
+// changes.
 template <typename CodeT, bool kUnitH, bool kRoot>
-__global__ void __launch_bounds__(512) hist_kernel(HistArgs a) {
-  extern __shared__ __align__(16) unsigned char smem[];
+__global__ void __launch_bounds__(1024, 1) hist_kernel(HistArgs a) {
+  extern __shared__ __align__(16) int smem[];
   const DriverState st = *a.state;
   if (!st.frontier || !st.total_tiles) return;
   const uint32_t B = a.e.bins, B1 = B + 1, C = a.e.cols;
+  const uint32_t plane = B1 * kHistLanes;  // ints per limb array
+  int* lg = smem;                           // g limbs: 3 planes
+  int* lh = smem + 3 * plane;               // h limbs: 3 planes, or counts (unit hessian)
+  const uint32_t nplanes = kUnitH ? 4 : 6;
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // Per-warp staging of the 32 rows of a batch: (g0, g1, g2, h0 | count) and (h1, h2).
+  int4* stage4 = reinterpret_cast<int4*>(smem + nplanes * plane) + warp * 32;
+  int2* stage2 = reinterpret_cast<int2*>(reinterpret_cast<int4*>(smem + nplanes * plane) + kHistWarps * 32) +
+                 warp * 32;
   const uint32_t npairs = kRoot ? 1u : st.pairs;
   const uint32_t total_tiles = st.total_tiles;
   const uint64_t items = uint64_t(total_tiles) * a.ngroups;
@@ -399,39 +437,82 @@ __global__ void __launch_bounds__(512) hist_kernel(HistArgs a) {
   uint64_t it = blockIdx.x * per;
   const uint64_t end = min(items, it + per);
   if (it >= end) return;
-  unsigned long long* sg = reinterpret_cast<unsigned long long*>(smem);
-  unsigned int* sc = reinterpret_cast<unsigned int*>(smem + size_t(a.fg) * B1 * 8);
-  unsigned long long* sh = reinterpret_cast<unsigned long long*>(smem + size_t(a.fg) * B1 * 8);
   const float2 s = *a.scale;
+  const uint32_t Lg = limb_width(a.max_bits[0], s.x);
+  const uint32_t Lh = kUnitH ? 17u : limb_width(a.max_bits[1], s.y);
+  const uint32_t Lmax = Lg > Lh ? Lg : Lh;
+  const uint32_t norm_rows = (1u << (31 - Lmax)) - 1;  // rows allowed between carries
+  // Every warp takes one batch of `batch` rows per sub-chunk; 21-bit limbs
+  // carry every 1023 rows, so their sub-chunks are half as long.
+  const uint32_t batch = Lmax >= 21 ? 16u : 32u;
+  const uint32_t sub_rows = batch * kHistWarps;
   const long long qh_unit = __float2ll_rn(s.y);
   const CodeT* __restrict__ codes = static_cast<const CodeT*>(a.e.codes);
   const uint32_t stride = a.e.stride;
-  const uint32_t miss = a.e.missing;
-  constexpr uint32_t kPerVec = 16 / sizeof(CodeT);
+  // The missing code is also its shared-memory slot; it is flushed to bin B.
+  const uint32_t miss_slot = a.e.missing;
 
-  int64_t cur_group = -1, cur_pair = -1;
-  auto zero = [&](uint32_t nf) {
-    const uint32_t n = nf * B1;
-    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
-      sg[i] = 0;
-      if (kUnitH) sc[i] = 0;
-      else sh[i] = 0;
-    }
-  };
-  auto flush = [&](uint32_t group, uint32_t pair) {
-    const uint32_t f0 = group * a.fg, nf = min(a.fg, C - f0);
-    longlong2* dst = a.built + (size_t(pair) * C + f0) * B1;
-    const uint32_t n = nf * B1;
-    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
-      const unsigned long long g = sg[i];
-      const unsigned long long h = kUnitH ? (unsigned long long)sc[i] * (unsigned long long)qh_unit : sh[i];
-      if (g | (kUnitH ? (unsigned long long)sc[i] : h)) {
-        atomicAdd(reinterpret_cast<unsigned long long*>(&dst[i].x), g);
-        atomicAdd(reinterpret_cast<unsigned long long*>(&dst[i].y), h);
+  for (uint32_t i = threadIdx.x; i < nplanes * plane; i += blockDim.x) smem[i] = 0;
+  __syncthreads();
+
+  auto normalise = [&]() {
+    for (uint32_t i = threadIdx.x; i < plane; i += blockDim.x) {
+#pragma unroll
+      for (int v = 0; v < (kUnitH ? 1 : 2); ++v) {
+        int* b = (v ? lh : lg) + i;
+        const uint32_t L = v ? Lh : Lg;
+        int x0 = b[0];
+        const int c0 = x0 >> L;  // arithmetic shift: floor division by 2^L
+        x0 -= c0 * (1 << L);
+        int x1 = b[plane] + c0;
+        const int c1 = x1 >> L;
+        x1 -= c1 * (1 << L);
+        b[0] = x0;
+        b[plane] = x1;
+        b[2 * plane] += c1;
       }
     }
   };
+  auto flush = [&](uint32_t group, uint32_t pair) {
+    const uint32_t f0 = group * kHistLanes;
+    for (uint32_t i = threadIdx.x; i < plane; i += blockDim.x) {
+      const uint32_t slot = i / kHistLanes, f = f0 + (i % kHistLanes);
+      const uint32_t bin = slot == miss_slot ? B : slot;
+      const long long g = combine_limbs(lg + i, plane, Lg);
+      long long h;
+      if (kUnitH) h = (long long)((unsigned long long)(unsigned)lh[i] * (unsigned long long)qh_unit);
+      else h = combine_limbs(lh + i, plane, Lh);
+      const bool any = kUnitH ? (g != 0 || lh[i] != 0) : (g != 0 || h != 0);
+      if (any && f < C) {
+        longlong2* dst = a.built + (size_t(pair) * C + f) * B1 + bin;
+        atomicAdd(reinterpret_cast<unsigned long long*>(&dst->x), (unsigned long long)g);
+        atomicAdd(reinterpret_cast<unsigned long long*>(&dst->y), (unsigned long long)h);
+      }
+      lg[i] = 0;
+      lg[i + plane] = 0;
+      lg[i + 2 * plane] = 0;
+      lh[i] = 0;
+      if (!kUnitH) {
+        lh[i + plane] = 0;
+        lh[i + 2 * plane] = 0;
+      }
+    }
+  };
+  auto split = [](long long q, uint32_t L, int& c0, int& c1, int& c2) {
+    const bool neg = q < 0;
+    const unsigned long long m = (unsigned long long)(neg ? -q : q), mask = (1ull << L) - 1;
+    c0 = int(m & mask);
+    c1 = int((m >> L) & mask);
+    c2 = int(m >> (2 * L));
+    if (neg) {
+      c0 = -c0;
+      c1 = -c1;
+      c2 = -c2;
+    }
+  };
 
+  int64_t cur_group = -1, cur_pair = -1;
+  uint32_t since = 0;  // rows added since the last carry
   for (; it < end; ++it) {
     const uint32_t group = uint32_t(it / total_tiles), t = uint32_t(it % total_tiles);
     uint32_t pair = 0;
@@ -448,10 +529,9 @@ __global__ void __launch_bounds__(512) hist_kernel(HistArgs a) {
       if (cur_group >= 0) {
         __syncthreads();
         flush(uint32_t(cur_group), uint32_t(cur_pair));
+        __syncthreads();
+        since = 0;
       }
-      __syncthreads();
-      zero(min(a.fg, C - group * a.fg));
-      __syncthreads();
       cur_group = group;
       cur_pair = pair;
     }
@@ -459,31 +539,60 @@ __global__ void __launch_bounds__(512) hist_kernel(HistArgs a) {
     const uint32_t seg0 = a.seg_begin[slot], segn = a.seg_count[slot];
     const uint32_t begin = seg0 + (t - (kRoot ? 0u : a.tile_offset[pair])) * kTileRows;
     const uint32_t cnt = min(kTileRows, seg0 + segn - begin);
-    const uint32_t f0 = group * a.fg, nf = min(a.fg, C - f0);
-    const uint32_t nvec = (nf + kPerVec - 1) / kPerVec;
-    for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) {
-      const uint32_t row = kRoot ? begin + i : __ldg(a.rows + begin + i);
-      const float2 gp = __ldg(a.pairs + row);
-      const unsigned long long qg = (unsigned long long)__float2ll_rn(__fmul_rn(gp.x, s.x));
-      const unsigned long long qh =
-          kUnitH ? 0ull : (unsigned long long)__float2ll_rn(__fmul_rn(gp.y, s.y));
-      const uint4* rp = reinterpret_cast<const uint4*>(codes + size_t(row) * stride + f0);
-      for (uint32_t v = 0; v < nvec; ++v) {
-        const uint4 w = __ldg(rp + v);
-        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+    const uint32_t f = group * kHistLanes + lane;
+    // Lanes past the last feature run the same instructions on code 0: they
+    // only touch their own column, which is never flushed.
+    const bool active = f < C;
+    for (uint32_t sub = 0; sub < cnt; sub += sub_rows) {
+      const uint32_t nsub = min(sub_rows, cnt - sub);
+      const uint32_t base = warp * batch;
+      const uint32_t nrows = base < nsub ? min(batch, nsub - base) : 0u;
+      if (nrows) {
+        // Lane i: row i of the batch, its gradient pair split into limbs once.
+        const bool mine = lane < nrows;
+        const uint32_t my_row =
+            mine ? (kRoot ? begin + sub + base + lane : __ldg(a.rows + begin + sub + base + lane)) : 0u;
+        int g0 = 0, g1 = 0, g2 = 0, h0 = 0, h1 = 0, h2 = 0;
+        if (mine) {
+          const float2 gp = __ldg(a.pairs + my_row);
+          split(__float2ll_rn(__fmul_rn(gp.x, s.x)), Lg, g0, g1, g2);
+          if (kUnitH) h0 = 1;
+          else split(__float2ll_rn(__fmul_rn(gp.y, s.y)), Lh, h0, h1, h2);
+        }
+        stage4[lane] = make_int4(g0, g1, g2, h0);
+        if (!kUnitH) stage2[lane] = make_int2(h1, h2);
+        __syncwarp();
+        // Rows past nrows carry zero limbs and code 0: their adds are no-ops.
+        for (uint32_t j0 = 0; j0 < nrows; j0 += 8) {
+          uint32_t code[8];
 #pragma unroll
-        for (uint32_t j = 0; j < kPerVec; ++j) {
-          const uint32_t f = v * kPerVec + j;
-          if (f < nf) {
-            uint32_t code;
-            if (sizeof(CodeT) == 1) code = (words[j >> 2] >> ((j & 3) * 8)) & 0xffu;
-            else code = (words[j >> 1] >> ((j & 1) * 16)) & 0xffffu;
-            const uint32_t bin = code == miss ? B : code;
-            atomicAdd(&sg[f * B1 + bin], qg);
-            if (kUnitH) atomicAdd(&sc[f * B1 + bin], 1u);
-            else atomicAdd(&sh[f * B1 + bin], qh);
+          for (int u = 0; u < 8; ++u) {
+            const uint32_t r = __shfl_sync(0xffffffffu, my_row, j0 + u);
+            code[u] = (active && j0 + u < nrows) ? uint32_t(__ldg(codes + size_t(r) * stride + f)) : 0u;
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const uint32_t idx = code[u] * kHistLanes + lane;
+            const int4 q4 = stage4[j0 + u];
+            atomicAdd(lg + idx, q4.x);
+            atomicAdd(lg + idx + plane, q4.y);
+            atomicAdd(lg + idx + 2 * plane, q4.z);
+            atomicAdd(lh + idx, q4.w);
+            if (!kUnitH) {
+              const int2 q2 = stage2[j0 + u];
+              atomicAdd(lh + idx + plane, q2.x);
+              atomicAdd(lh + idx + 2 * plane, q2.y);
+            }
           }
         }
+        __syncwarp();
+      }
+      since += nsub;
+      if (since + sub_rows > norm_rows) {
+        __syncthreads();
+        normalise();
+        __syncthreads();
+        since = 0;
       }
     }
   }
@@ -886,14 +995,18 @@ struct PartArgs {
 // Rows of every frontier node: nodes that stop add their leaf to the row's
 // margin, nodes split at the last level add the child leaf, other split nodes
 // scatter their rows to the two children (left block from the segment start,
-// right block from the segment end).
+// right block from the segment end). Each thread takes 8 consecutive rows of
+// a 2048-row tile; one block-wide scan and one cursor reservation per tile.
+constexpr uint32_t kPartThreads = 256;
+constexpr uint32_t kPartPerThread = kTileRows / kPartThreads;
+
 template <typename CodeT>
-__global__ void __launch_bounds__(256) partition_kernel(PartArgs a) {
+__global__ void __launch_bounds__(kPartThreads) partition_kernel(PartArgs a) {
+  __shared__ uint32_t s_base[2];
   const DriverState st = *a.state;
   if (!st.frontier || st.error) return;
   const uint32_t n = st.frontier, ptiles = st.pad0;
   const CodeT* __restrict__ codes = static_cast<const CodeT*>(a.e.codes);
-  const uint32_t lane = threadIdx.x & 31;
   for (uint32_t t = blockIdx.x; t < ptiles; t += gridDim.x) {
     uint32_t lo = 0, hi = n;
     while (hi - lo > 1) {
@@ -908,44 +1021,51 @@ __global__ void __launch_bounds__(256) partition_kernel(PartArgs a) {
     const uint32_t md = a.mode[s];
     const DevNode node = a.nodes[a.ids[s]];
     const float leaf_l = a.slot_leaf[2 * s], leaf_r = a.slot_leaf[2 * s + 1];
-    const uint32_t rounded = (cnt + 31) & ~31u;
-    for (uint32_t i = threadIdx.x; i < rounded; i += blockDim.x) {
-      const bool valid = i < cnt;
-      const uint32_t row = valid ? (a.root ? begin + i : a.rows[begin + i]) : 0u;
+    const uint32_t first = threadIdx.x * kPartPerThread;
+    uint32_t rows[kPartPerThread];
+    uint32_t left_mask = 0, nl = 0, nr = 0;
+#pragma unroll
+    for (uint32_t k = 0; k < kPartPerThread; ++k) {
+      const uint32_t i = first + k;
+      rows[k] = i < cnt ? (a.root ? begin + i : a.rows[begin + i]) : 0u;
+    }
+#pragma unroll
+    for (uint32_t k = 0; k < kPartPerThread; ++k) {
+      if (first + k >= cnt) continue;
+      const uint32_t row = rows[k];
       if (md == 0) {
-        if (valid) {
-          float* m = a.margins + size_t(row) * a.groups + a.group;
-          *m = __fadd_rn(*m, leaf_l);
-        }
+        float* m = a.margins + size_t(row) * a.groups + a.group;
+        *m = __fadd_rn(*m, leaf_l);
         continue;
       }
-      bool left = false;
-      if (valid) {
-        const uint32_t code = codes[size_t(row) * a.e.stride + uint32_t(node.feature)];
-        left = code == a.e.missing ? node.default_left != 0u : int32_t(code) <= node.split_bin;
-      }
+      const uint32_t code = codes[size_t(row) * a.e.stride + uint32_t(node.feature)];
+      const bool left = code == a.e.missing ? node.default_left != 0u : int32_t(code) <= node.split_bin;
       if (md == 2) {
-        if (valid) {
-          float* m = a.margins + size_t(row) * a.groups + a.group;
-          *m = __fadd_rn(*m, left ? leaf_l : leaf_r);
-        }
-        continue;
-      }
-      const uint32_t lmask = __ballot_sync(0xffffffffu, valid && left);
-      const uint32_t rmask = __ballot_sync(0xffffffffu, valid && !left);
-      uint32_t lbase = 0, rbase = 0;
-      if (lane == 0) {
-        if (lmask) lbase = atomicAdd(a.cursor_l + s, __popc(lmask));
-        if (rmask) rbase = atomicSub(a.cursor_r + s, __popc(rmask)) - __popc(rmask);
-      }
-      lbase = __shfl_sync(0xffffffffu, lbase, 0);
-      rbase = __shfl_sync(0xffffffffu, rbase, 0);
-      const uint32_t below = (1u << lane) - 1u;
-      if (valid) {
-        if (left) a.rows_next[lbase + __popc(lmask & below)] = row;
-        else a.rows_next[rbase + __popc(rmask & below)] = row;
+        float* m = a.margins + size_t(row) * a.groups + a.group;
+        *m = __fadd_rn(*m, left ? leaf_l : leaf_r);
+      } else {
+        left_mask |= uint32_t(left) << k;
+        nl += left;
+        nr += !left;
       }
     }
+    if (md != 1) continue;  // uniform across the block
+    uint32_t total;
+    const uint32_t off = block_exclusive_scan(nl | (nr << 16), &total);
+    if (threadIdx.x == 0) {
+      const uint32_t tl = total & 0xffffu, tr = total >> 16;
+      s_base[0] = tl ? atomicAdd(a.cursor_l + s, tl) : 0u;
+      s_base[1] = tr ? atomicSub(a.cursor_r + s, tr) - tr : 0u;
+    }
+    __syncthreads();
+    uint32_t lpos = s_base[0] + (off & 0xffffu), rpos = s_base[1] + (off >> 16);
+#pragma unroll
+    for (uint32_t k = 0; k < kPartPerThread; ++k) {
+      if (first + k >= cnt) continue;
+      if ((left_mask >> k) & 1u) a.rows_next[lpos++] = rows[k];
+      else a.rows_next[rpos++] = rows[k];
+    }
+    __syncthreads();
   }
 }
 
@@ -1235,16 +1355,11 @@ void launch_fill_margins(float* margins, const float* base, uint32_t rows, uint3
 }
 
 HistConfig hist_config(const Ellpack& e, bool unit_hessian) {
-  const size_t per_feature = size_t(e.bins + 1) * (unit_hessian ? 12 : 16);
-  const size_t budget = 110 * 1024;  // two CTAs per SM
-  const uint32_t align = e.bytes_per_code == 1 ? 16 : 8;
-  uint32_t fg = uint32_t(budget / per_feature);
-  fg = std::max(align, fg / align * align);
-  fg = std::min<uint32_t>(fg, (e.cols + align - 1) / align * align);
   HistConfig c;
-  c.feature_group = fg;
-  c.smem = per_feature * fg;
-  c.threads = 512;
+  c.feature_group = kHistLanes;
+  c.smem = size_t(unit_hessian ? 4 : 6) * (e.bins + 1) * kHistLanes * sizeof(int) +
+           size_t(kHistWarps) * 32 * (sizeof(int4) + (unit_hessian ? 0 : sizeof(int2)));
+  c.threads = kHistWarps * 32;
   return c;
 }
 
@@ -1254,7 +1369,7 @@ void launch_hist_t(const HistArgs& args, int blocks, int threads, size_t smem, c
   auto kernel = hist_kernel<CodeT, kUnit, kRoot>;
   static bool configured = false;
   if (!configured) {
-    XGBB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    XGBB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
     configured = true;
   }
   kernel<<<blocks, threads, smem, stream>>>(args);
@@ -1284,8 +1399,8 @@ void tree_level_hist(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t dep
   a.seg_begin = ws.seg_begin[depth & 1];
   a.seg_count = ws.seg_count[depth & 1];
   a.built = ws.built;
-  a.fg = tl.feature_group;
-  a.ngroups = (tl.ell.cols + tl.feature_group - 1) / tl.feature_group;
+  a.max_bits = tl.max_bits;
+  a.ngroups = (tl.ell.cols + kHistLanes - 1) / kHistLanes;
   const bool root = depth == 0;
   const bool u8 = tl.ell.bytes_per_code == 1;
   const int b = tl.hist_blocks, t = tl.hist_threads;
@@ -1384,9 +1499,9 @@ void tree_level_partition(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_
   a.group = tl.group;
   a.root = depth == 0;
   if (tl.ell.bytes_per_code == 1)
-    partition_kernel<uint8_t><<<tl.part_blocks, 256, 0, stream>>>(a);
+    partition_kernel<uint8_t><<<tl.part_blocks, kPartThreads, 0, stream>>>(a);
   else
-    partition_kernel<uint16_t><<<tl.part_blocks, 256, 0, stream>>>(a);
+    partition_kernel<uint16_t><<<tl.part_blocks, kPartThreads, 0, stream>>>(a);
   XGBB_CUDA(cudaGetLastError());
 }
 

@@ -9,9 +9,11 @@
 namespace xgbb {
 
 // Quantised feature matrix in HBM: row-major ELLPACK, one code per
-// (row, feature), uint8 or uint16. `missing` is the type's maximum code, or
-// 0x100 for uint8 codes when all 256 codes are bins (no missing value).
-// Each row is padded to `stride` codes (a multiple of 16 bytes) with missing.
+// (row, feature), uint8 or uint16. `missing` is the code of a missing value:
+// the cut stride B (the histogram's missing bin) when it fits, else 255 for
+// uint8 codes with B = 256, or 0x100 when all 256 uint8 codes are bins and no
+// value is missing. Each row is padded to `stride` codes (a multiple of 16
+// bytes).
 struct Ellpack {
   const void* codes = nullptr;
   uint32_t rows = 0, cols = 0, stride = 0;  // stride in codes
@@ -74,6 +76,7 @@ struct TreeLaunch {
   TreeParams params;
   const float2* pairs;       // gradient pairs of this group [rows]
   const float2* scale;       // power-of-two scales of this group
+  const unsigned int* max_bits;  // largest |g|, |h| of this group (float bits)
   float* margins;            // [rows][groups]
   uint32_t groups, group;
   bool unit_hessian;
