@@ -359,6 +359,8 @@ def main():
     from xgboost import core
     core.set_device(dist.local)
     if dist.world > 1:
+        # One node: NCCL bootstrap on loopback; data moves over NVLink.
+        os.environ.setdefault("NCCL_SOCKET_IFNAME", "lo")
         uid = dist.bcast(xgb.collective.nccl_unique_id() if dist.rank == 0 else None)
         xgb.collective.init(rank=dist.rank, world_size=dist.world, nccl_unique_id=uid,
                             device=dist.local)

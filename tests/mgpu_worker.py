@@ -1,0 +1,61 @@
+"""One rank of the row-sharded training check (launched by test_multi_gpu.py
+under torch.distributed.run, one process per GPU): trains on its contiguous
+row shard with cuts from the full matrix and writes the full-matrix margins."""
+import json
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(os.path.dirname(HERE), "xgboost-metal_b200"))
+
+import torch  # noqa: E402  (first, so its NCCL is the process's NCCL)
+import torch.distributed as dist  # noqa: E402
+
+import xgboost as xgb  # noqa: E402
+from xgboost import core  # noqa: E402
+
+
+def data(objective):
+    rng = np.random.default_rng(2026)
+    n, c = 30000, 12
+    X = rng.normal(size=(n, c)).astype(np.float32)
+    X[rng.random(X.shape) < 0.08] = np.nan
+    z = np.nan_to_num(X) @ rng.normal(size=c)
+    if objective == "binary:logistic":
+        y = (rng.random(n) < 1 / (1 + np.exp(-z))).astype(np.float32)
+    else:
+        y = (z + rng.normal(size=n)).astype(np.float32)
+    return X, y
+
+
+def main():
+    import faulthandler
+    faulthandler.dump_traceback_later(int(os.environ.get("XGBB_WORKER_TIMEOUT", "240")), exit=True)
+    out_dir, objective = sys.argv[1], sys.argv[2]
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("gloo")
+    core.set_device(local)
+    box = [xgb.collective.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    xgb.collective.init(rank=rank, world_size=world, nccl_unique_id=box[0], device=local)
+    X, y = data(objective)
+    lo, hi = len(y) * rank // world, len(y) * (rank + 1) // world
+    ref = xgb.QuantileDMatrix(X, max_bin=64)
+    shard = xgb.QuantileDMatrix(X[lo:hi], label=y[lo:hi], ref=ref, max_bin=64)
+    params = {"objective": objective, "max_depth": 6, "eta": 0.3, "max_bin": 64,
+              "device": "cuda", "tree_method": "hist",
+              "cuda_graph": int(os.environ.get("XGBB_WORKER_GRAPH", "1"))}
+    bst = xgb.train(params, shard, 6)
+    margins = bst.predict(xgb.DMatrix(X), output_margin=True)
+    np.save(os.path.join(out_dir, "margins_%d.npy" % rank), margins)
+    xgb.collective.finalize()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

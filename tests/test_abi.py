@@ -91,3 +91,15 @@ def test_no_gpu_means_a_clear_error_not_a_fallback():
     d = xgb.DMatrix(np.ones((4, 2), np.float32), label=[0, 1, 0, 1])
     with pytest.raises(xgb.XGBoostError, match="CUDA"):
         xgb.train({"tree_method": "hist", "device": "cuda"}, d, 1)
+
+
+def test_nccl_is_not_a_load_time_dependency():
+    # NCCL is opened only when a communicator is created, so importing the
+    # library never pins an NCCL build into the process.
+    import subprocess
+    out = subprocess.run(["ldd", LIB], capture_output=True, text=True).stdout
+    assert "libnccl" not in out
+    code = ("import sys; sys.path.insert(0, %r); import xgboost; import torch; print('ok')"
+            % os.path.join(ROOT, "xgboost-metal_b200"))
+    res = subprocess.run([__import__("sys").executable, "-c", code], capture_output=True, text=True)
+    assert res.stdout.strip().endswith("ok"), res.stderr[-2000:]

@@ -1,0 +1,43 @@
+"""Row-sharded training over NCCL, one process per GPU: every rank's model
+equals the single-GPU model (checked against the oracle on all rows, bit for
+bit). Needs two or more GPUs; skipped otherwise."""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+import checkers as C
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def gpu_count():
+    try:
+        import torch
+        return torch.cuda.device_count()
+    except Exception:  # pragma: no cover
+        return 0
+
+
+@pytest.mark.skipif(gpu_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("objective", ["reg:squarederror", "binary:logistic"])
+def test_two_ranks_match_the_oracle(tmp_path, objective):
+    sys.path.insert(0, HERE)
+    import mgpu_worker
+    # One node: NCCL's bootstrap sockets on loopback, no NVLink multicast.
+    env = dict(os.environ, MASTER_ADDR="127.0.0.1", NCCL_NVLS_ENABLE="0", NCCL_SOCKET_IFNAME="lo")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", "--master-port=29533",
+           os.path.join(HERE, "mgpu_worker.py"), str(tmp_path), objective]
+    proc = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=420)
+    assert proc.returncode == 0, proc.stderr[-3000:]
+    X, y = mgpu_worker.data(objective)
+    params = C.train_params(dict(objective=objective, max_depth=6, eta=0.3, max_bin=64))
+    _, margins, _ = C.oracle_train(X, y, params, 6)
+    for r in range(2):
+        got = np.load(os.path.join(tmp_path, "margins_%d.npy" % r))
+        np.testing.assert_array_equal(got.view(np.uint32), margins[:, 0].view(np.uint32))

@@ -50,7 +50,7 @@ def build(force=False):
         objs = list(ex.map(_compile, sources()))
     if os.path.exists(LIB) and all(os.path.getmtime(LIB) >= os.path.getmtime(o) for o in objs):
         return LIB
-    cmd = [NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", LIB] + objs + ["-lnccl"]
+    cmd = [NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", LIB] + objs + ["-ldl"]
     subprocess.run(cmd, check=True)
     return LIB
 

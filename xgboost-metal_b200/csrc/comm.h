@@ -7,6 +7,8 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <functional>
+#include <map>
 #include <string>
 
 namespace xgbb {
@@ -27,10 +29,15 @@ class Comm {
   void sum_f64(void* buf, size_t count, cudaStream_t s);
   void broadcast(void* buf, size_t bytes, int root, cudaStream_t s);
   void barrier(cudaStream_t s);
+  // Work that must be released before the communicator is destroyed: CUDA
+  // graphs holding NCCL calls would otherwise keep ncclCommDestroy waiting.
+  void add_release_hook(const void* owner, std::function<void()> fn);
+  void remove_release_hook(const void* owner);
 
  private:
   int rank_ = 0, world_ = 1;
   void* comm_ = nullptr;
+  std::map<const void*, std::function<void()>> hooks_;
 };
 
 std::string nccl_unique_id_hex();

@@ -171,6 +171,7 @@ Booster::Booster(std::vector<std::shared_ptr<DMatrix>> cache) {
 }
 
 Booster::~Booster() {
+  Comm::get().remove_release_hook(this);
   state_.reset();
   for (auto e : user_events_)
     if (e) cudaEventDestroy(e);
@@ -461,6 +462,14 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp) {
   XGBB_CUDA(cudaStreamSynchronize(stream_));
   ts->margin_rounds = rounds_;
   state_ = std::move(ts);
+  if (Comm::get().active()) {
+    // Sharded training captures NCCL calls in its graphs; the communicator
+    // drops this state (graphs included) before it is destroyed.
+    Comm::get().add_release_hook(this, [this] {
+      if (state_) cudaStreamSynchronize(stream_);
+      state_.reset();
+    });
+  }
   return *state_;
 }
 
@@ -484,6 +493,7 @@ void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s, b
   tl.group = g;
   tl.unit_hessian = objective_ == kSquaredError && d.weights.empty();
   tl.feature_group = ts.hc.feature_group;
+  tl.min_limbs = uint32_t(integer(params_, "cuda_hist_limbs", 0));
   tl.hist_smem = ts.hc.smem;
   tl.hist_threads = ts.hc.threads;
   int sms = 148;

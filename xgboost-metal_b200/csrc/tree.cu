@@ -381,22 +381,31 @@ struct HistArgs {
   const uint32_t* seg_count;
   longlong2* built;
   uint32_t ngroups;
+  uint32_t min_limbs;  // 3 forces three-limb accumulation (tuning; results unchanged)
 };
 
 constexpr int kHistWarps = 32;          // 1024 threads, one CTA per SM
 constexpr uint32_t kHistLanes = 32;     // features per CTA: lane = feature
 
-// Width of the limbs of one value type: three signed 32-bit limbs of L bits
-// hold the CTA's exact int64 per-bin sums. L >= 17 keeps the top limb (bits
-// >= 2L of a sum below 2^63) inside int32; L >= bitlen(max|q|)/3 keeps every
-// single value inside three limbs.
-__device__ __forceinline__ uint32_t limb_width(unsigned int max_bits, float scale) {
+// Limbs of one value type: three signed 32-bit limbs of L bits hold the
+// CTA's exact int64 per-bin sums. L >= 17 keeps the top limb (bits >= 2L of a
+// sum below 2^63) inside int32. When every |q| of the round has at most 2L
+// bits (L <= 21), the top limb only receives carries and values touch two
+// limbs; otherwise L >= bitlen/3 and values touch three.
+struct LimbPlan {
+  uint32_t L, n;
+};
+__device__ __forceinline__ LimbPlan limb_plan(unsigned int max_bits, float scale) {
   const float mv = __uint_as_float(max_bits & 0x7fffffffu);
   const long long qm = __float2ll_rn(__fmul_rn(mv, scale));
   const unsigned long long a = (unsigned long long)(qm < 0 ? -qm : qm);
   const uint32_t bl = a ? 64u - __clzll(a) : 0u;
+  if (bl <= 42) {
+    const uint32_t L = (bl + 1) / 2;
+    return {L < 17 ? 17u : L, 2u};
+  }
   const uint32_t L = (bl + 2) / 3;
-  return L < 17 ? 17u : (L > 21 ? 21u : L);
+  return {L > 21 ? 21u : L, 3u};
 }
 
 __device__ __forceinline__ long long combine_limbs(const int* base, uint32_t plane, uint32_t L) {
@@ -415,11 +424,9 @@ __device__ __forceinline__ long long combine_limbs(const int* base, uint32_t pla
 // atomics are 32-bit), carried between limbs every 2^(31-L) rows, and are
 // recombined and flushed with 64-bit global atomics when the (group, pair)
 // changes.
-template <typename CodeT, bool kUnitH, bool kRoot>
-__global__ void __launch_bounds__(1024, 1) hist_kernel(HistArgs a) {
-  extern __shared__ __align__(16) int smem[];
-  const DriverState st = *a.state;
-  if (!st.frontier || !st.total_tiles) return;
+template <typename CodeT, bool kUnitH, bool kRoot, int NG, int NH>
+__device__ __forceinline__ void hist_body(const HistArgs& a, int* smem, const DriverState& st,
+                                          uint32_t Lg, uint32_t Lh) {
   const uint32_t B = a.e.bins, B1 = B + 1, C = a.e.cols;
   const uint32_t plane = B1 * kHistLanes;  // ints per limb array
   int* lg = smem;                           // g limbs: 3 planes
@@ -438,8 +445,6 @@ __global__ void __launch_bounds__(1024, 1) hist_kernel(HistArgs a) {
   const uint64_t end = min(items, it + per);
   if (it >= end) return;
   const float2 s = *a.scale;
-  const uint32_t Lg = limb_width(a.max_bits[0], s.x);
-  const uint32_t Lh = kUnitH ? 17u : limb_width(a.max_bits[1], s.y);
   const uint32_t Lmax = Lg > Lh ? Lg : Lh;
   const uint32_t norm_rows = (1u << (31 - Lmax)) - 1;  // rows allowed between carries
   // Every warp takes one batch of `batch` rows per sub-chunk; 21-bit limbs
@@ -576,12 +581,12 @@ __global__ void __launch_bounds__(1024, 1) hist_kernel(HistArgs a) {
             const int4 q4 = stage4[j0 + u];
             atomicAdd(lg + idx, q4.x);
             atomicAdd(lg + idx + plane, q4.y);
-            atomicAdd(lg + idx + 2 * plane, q4.z);
+            if (NG == 3) atomicAdd(lg + idx + 2 * plane, q4.z);
             atomicAdd(lh + idx, q4.w);
             if (!kUnitH) {
               const int2 q2 = stage2[j0 + u];
               atomicAdd(lh + idx + plane, q2.x);
-              atomicAdd(lh + idx + 2 * plane, q2.y);
+              if (NH == 3) atomicAdd(lh + idx + 2 * plane, q2.y);
             }
           }
         }
@@ -598,6 +603,25 @@ __global__ void __launch_bounds__(1024, 1) hist_kernel(HistArgs a) {
   }
   __syncthreads();
   flush(uint32_t(cur_group), uint32_t(cur_pair));
+}
+
+template <typename CodeT, bool kUnitH, bool kRoot>
+__global__ void __launch_bounds__(1024, 1) hist_kernel(HistArgs a) {
+  extern __shared__ __align__(16) int smem[];
+  const DriverState st = *a.state;
+  if (!st.frontier || !st.total_tiles) return;
+  const float2 s = *a.scale;
+  LimbPlan pg = limb_plan(a.max_bits[0], s.x);
+  LimbPlan ph = kUnitH ? LimbPlan{17u, 2u} : limb_plan(a.max_bits[1], s.y);
+  if (a.min_limbs >= 3) {
+    // Three limbs of L = max(17, bitlen / 3) bits hold any value of the round.
+    if (pg.n == 2) pg = LimbPlan{(pg.L * 2 + 2) / 3 < 17 ? 17u : (pg.L * 2 + 2) / 3, 3u};
+    if (!kUnitH && ph.n == 2) ph = LimbPlan{(ph.L * 2 + 2) / 3 < 17 ? 17u : (ph.L * 2 + 2) / 3, 3u};
+  }
+  if (pg.n == 2 && ph.n == 2) hist_body<CodeT, kUnitH, kRoot, 2, 2>(a, smem, st, pg.L, ph.L);
+  else if (pg.n == 2) hist_body<CodeT, kUnitH, kRoot, 2, 3>(a, smem, st, pg.L, ph.L);
+  else if (ph.n == 2) hist_body<CodeT, kUnitH, kRoot, 3, 2>(a, smem, st, pg.L, ph.L);
+  else hist_body<CodeT, kUnitH, kRoot, 3, 3>(a, smem, st, pg.L, ph.L);
 }
 
 struct EvalArgs {
@@ -1400,6 +1424,7 @@ void tree_level_hist(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t dep
   a.seg_count = ws.seg_count[depth & 1];
   a.built = ws.built;
   a.max_bits = tl.max_bits;
+  a.min_limbs = tl.min_limbs;
   a.ngroups = (tl.ell.cols + kHistLanes - 1) / kHistLanes;
   const bool root = depth == 0;
   const bool u8 = tl.ell.bytes_per_code == 1;

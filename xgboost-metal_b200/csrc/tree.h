@@ -82,6 +82,7 @@ struct TreeLaunch {
   bool unit_hessian;
   int hist_blocks, hist_threads, eval_blocks, part_blocks;
   uint32_t feature_group;    // features per histogram CTA
+  uint32_t min_limbs;        // 3 forces three-limb histogram accumulation
   size_t hist_smem;
 };
 
