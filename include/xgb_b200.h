@@ -43,6 +43,28 @@ XGB_DLL int XGBBQuantizeHost(const float* X, bst_ulong rows, bst_ulong cols, uin
 XGB_DLL int XGBBGradientsHost(int objective, const float* margins, const float* labels,
                               const float* weights, bst_ulong rows, uint32_t groups,
                               float scale_pos_weight, float* pairs, float* scales);
+/* No counterpart in the reference. Device-pointer variant of
+ * XGBBGradientsHost that allocates no device memory: margins [rows][groups],
+ * labels [rows], weights [rows] or NULL, pairs [groups][rows][2] and scales
+ * [groups][2] are caller-owned device buffers, and the scale accumulators live
+ * in one fixed 17,408-byte device array of the library, cleared on `stream`
+ * (a cudaStream_t, NULL = default stream) at the start of every call. Work is
+ * enqueued on `stream` and not waited for.
+ * Limit: 1 <= groups <= 64 and 1 <= rows < 2^32; other sizes are rejected with
+ * an error before anything is enqueued.
+ * For callers that cannot allocate: a custom-objective loop stepping beside
+ * training on its own stream, where cudaMalloc/cudaFree would synchronise the
+ * device and stall the other streams, and a process whose device memory is
+ * already claimed by a pool allocator, where a per-call allocation can fail
+ * mid-run.
+ * Calls that can overlap on one device (different streams or unordered host
+ * threads) race on the shared array; calls on one stream are safe. The first
+ * call on each device looks up the array's address (cudaGetSymbolAddress) and
+ * should come before any stream capture on that device. */
+XGB_DLL int XGBBGradientsDeviceNoAlloc(int objective, const float* margins, const float* labels,
+                                       const float* weights, bst_ulong rows, uint32_t groups,
+                                       float scale_pos_weight, float* pairs, float* scales,
+                                       void* stream);
 /* `rounds` rounds of training; trees back to back as 48-byte node records
  * {left, right, parent, feature, split_bin, default_left, threshold, leaf,
  * cover, gain, base_weight, flags}, tree sizes, and the final training

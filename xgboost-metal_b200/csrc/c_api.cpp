@@ -629,6 +629,20 @@ XGB_DLL int XGBBGradientsHost(int objective, const float* margins, const float* 
   });
 }
 
+// Device-pointer variant of XGBBGradientsHost that allocates nothing: the
+// scale accumulators live in a fixed device array (at most 64 groups) and
+// everything is enqueued on `stream` without waiting for it.
+XGB_DLL int XGBBGradientsDeviceNoAlloc(int objective, const float* margins, const float* labels,
+                                       const float* weights, bst_ulong rows, uint32_t groups,
+                                       float scale_pos_weight, float* pairs, float* scales,
+                                       void* stream) {
+  return guarded([&] {
+    xgbb::gradients_no_alloc(objective, margins, labels, weights, rows, groups, scale_pos_weight,
+                             reinterpret_cast<float2*>(pairs), reinterpret_cast<float2*>(scales),
+                             static_cast<cudaStream_t>(stream));
+  });
+}
+
 // Test entry: a whole training run through DMatrix + Booster, with the trees
 // written back to back as DevNode records (48 bytes each).
 XGB_DLL int XGBBTrainHost(const float* X, bst_ulong rows, bst_ulong cols, const float* labels,

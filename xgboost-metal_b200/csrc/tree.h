@@ -105,6 +105,12 @@ void launch_scales(const float2* pairs, uint32_t rows, uint32_t groups, MassAccu
 void launch_mass_exact(const float2* pairs, uint32_t rows, uint32_t groups, MassAccum mass,
                        cudaStream_t stream);
 void launch_scales_exact(uint32_t groups, MassAccum mass, float2* scales, cudaStream_t stream);
+// Gradient pairs and scales into caller-owned device buffers with the scale
+// accumulators in a fixed array of the library (no device allocation; at most
+// 64 groups; calls that overlap on one device race). Defined in noalloc.cu.
+void gradients_no_alloc(int objective, const float* margins, const float* labels,
+                        const float* weights, uint64_t rows, uint32_t groups,
+                        float scale_pos_weight, float2* pairs, float2* scales, cudaStream_t stream);
 void launch_base_chunks(int objective, const float* labels, const float* weights, uint32_t rows,
                         uint32_t group, float scale_pos_weight, double* chunk_sums,
                         cudaStream_t stream);
