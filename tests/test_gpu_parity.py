@@ -193,3 +193,31 @@ def test_zero_copy_infinity_is_reported_on_first_use():
     d = xgb.DMatrix(X, label=np.zeros(64, np.float32))
     with pytest.raises(xgb.XGBoostError, match="infinity"):
         xgb.train({"device": "cuda"}, d, 1)
+
+
+# Millions of rows with gradients of similar magnitude keep every |q| of a
+# round within 42 bits (scale = 2^62 / 2^bitlen(sum |v|)), which selects the
+# staged two-limb histogram path; smaller cases run the three-limb path.
+def test_two_limb_logistic_u16_partial_group_matches_oracle():
+    rows, cols = 3_000_000, 40
+    rng = np.random.default_rng(5)
+    X = rng.normal(size=(rows, cols)).astype(np.float32)
+    X[rng.random(X.shape) < 0.05] = np.nan
+    y = (np.nan_to_num(X[:, 0]) + 0.5 * rng.normal(size=rows) > 0).astype(np.float32)
+    params = C.train_params(dict(objective="binary:logistic", max_depth=6, eta=0.3))
+    trees_o, margins_o, _ = C.oracle_train(X, y, params, 3)
+    trees_p, margins_p = P.train(X, y, {k: v for k, v in params.items() if k != "num_class"}, 3)
+    assert_same_trees(trees_p, trees_o)
+    np.testing.assert_array_equal(bits(margins_p), bits(margins_o))
+
+
+def test_two_limb_unit_hessian_u8_matches_oracle():
+    rows, cols = 3_000_000, 20
+    rng = np.random.default_rng(6)
+    X = rng.normal(size=(rows, cols)).astype(np.float32)
+    y = np.where(X[:, 1] + 0.3 * rng.normal(size=rows) > 0, 1.0, -1.0).astype(np.float32)
+    params = C.train_params(dict(max_depth=5, eta=0.3, max_bin=64))
+    trees_o, margins_o, _ = C.oracle_train(X, y, params, 3)
+    trees_p, margins_p = P.train(X, y, {k: v for k, v in params.items() if k != "num_class"}, 3)
+    assert_same_trees(trees_p, trees_o)
+    np.testing.assert_array_equal(bits(margins_p), bits(margins_o))

@@ -143,7 +143,7 @@ struct Booster::TrainState {
   DeviceBuffer margins, pairs, mass, scales;
   DeviceBuffer state, ids[2], sums[2], seg_begin[2], seg_count[2], parent_slot, built_left,
       tile_offset, ptile_offset, cursor_l, cursor_r, counts_local, counts_global, mode, slot_leaf,
-      keys[2], cand, nodes, built, bank[2], rows_buf[2], level_rows, level_nodes;
+      keys[2], cand, nodes, built, bank[2], rows_buf[2], level_rows, level_nodes, hist_top;
   TreeWorkspace ws{};
   HistConfig hc{};
   std::vector<cudaGraphExec_t> graphs;
@@ -443,6 +443,12 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp) {
   ws.level_rows = ts->level_rows.as<unsigned long long>();
   ws.level_nodes = ts->level_nodes.as<uint32_t>();
   ts->hc = hist_config(e, objective_ == kSquaredError && d.weights.empty());
+  {
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device_);
+    ts->hist_top.resize(size_t(sms) * ts->hc.top_ints * sizeof(int));
+    ws.hist_top = ts->hist_top.as<int>();
+  }
   ts->graphs.assign(G, nullptr);
   if (profiling) {
     ts->events.resize(size_t(G) * D * 2);

@@ -380,12 +380,39 @@ struct HistArgs {
   const uint32_t* seg_begin;
   const uint32_t* seg_count;
   longlong2* built;
+  int* top;            // [grid][2][kPlaneWords] carries out of limb 1 (staged path)
   uint32_t ngroups;
   uint32_t min_limbs;  // 3 forces three-limb accumulation (tuning; results unchanged)
 };
 
 constexpr int kHistWarps = 32;          // 1024 threads, one CTA per SM
 constexpr uint32_t kHistLanes = 32;     // features per CTA: lane = feature
+
+// The (feature group, tile) items of one CTA. When the SMs split evenly
+// over the feature groups, the CTAs of all groups get the same tile ranges:
+// they run in step over the same rows, so the two 64-byte halves of a row's
+// 128-byte line are requested together and DRAM serves each line once
+// (DRAM reads 128-byte lines even for 64-byte requests). Otherwise the items
+// are split into equal contiguous runs.
+__device__ __forceinline__ void hist_item_range(uint32_t total_tiles, uint32_t ngroups, uint64_t& it,
+                                                uint64_t& end) {
+  const uint32_t grid = gridDim.x, b = blockIdx.x;
+  const uint32_t per_group = grid / ngroups;
+  if (per_group >= 1 && uint64_t(per_group) * ngroups * 8 >= uint64_t(grid) * 7) {
+    if (b >= per_group * ngroups) {
+      it = end = 0;
+      return;
+    }
+    const uint32_t g = b / per_group, k = b % per_group;
+    it = uint64_t(g) * total_tiles + uint64_t(k) * total_tiles / per_group;
+    end = uint64_t(g) * total_tiles + uint64_t(k + 1) * total_tiles / per_group;
+    return;
+  }
+  const uint64_t items = uint64_t(total_tiles) * ngroups;
+  const uint64_t per = (items + grid - 1) / grid;
+  it = b * per;
+  end = min(items, it + per);
+}
 
 // Limbs of one value type: three signed 32-bit limbs of L bits hold the
 // CTA's exact int64 per-bin sums. L >= 17 keeps the top limb (bits >= 2L of a
@@ -439,10 +466,8 @@ __device__ __forceinline__ void hist_body(const HistArgs& a, int* smem, const Dr
                  warp * 32;
   const uint32_t npairs = kRoot ? 1u : st.pairs;
   const uint32_t total_tiles = st.total_tiles;
-  const uint64_t items = uint64_t(total_tiles) * a.ngroups;
-  const uint64_t per = (items + gridDim.x - 1) / gridDim.x;
-  uint64_t it = blockIdx.x * per;
-  const uint64_t end = min(items, it + per);
+  uint64_t it, end;
+  hist_item_range(total_tiles, a.ngroups, it, end);
   if (it >= end) return;
   const float2 s = *a.scale;
   const uint32_t Lmax = Lg > Lh ? Lg : Lh;
@@ -605,6 +630,349 @@ __device__ __forceinline__ void hist_body(const HistArgs& a, int* smem, const Dr
   flush(uint32_t(cur_group), uint32_t(cur_pair));
 }
 
+// ---------------------------------------------------------------------------
+// Staged two-limb histogram (every |q| of the round has at most 2L bits).
+//
+// Same ownership as hist_body (one CTA per SM, lane = feature, contiguous run
+// of (feature group, tile) items), but the global reads leave the critical
+// path: each warp copies the 32-feature code slice and the gradient pair of
+// its next 16 rows into shared memory with cp.async while it accumulates the
+// current 16, and the row ids two steps ahead are loaded into a register. The
+// inner loop is then one shared load of the code, one broadcast load of the
+// row's limbs and 3-4 shared atomics at compile-time plane offsets. Limb 1
+// carries into a CTA-private int32 array in global memory (L2-resident), so
+// only the four (three) atomically-updated planes live in shared memory.
+constexpr uint32_t kSlots = 257;                       // bins 0..255 + missing slot (<= 256)
+constexpr uint32_t kPlaneWords = kSlots * kHistLanes;  // ints per plane
+constexpr uint32_t kStageRows = 16;                    // rows per warp per step
+constexpr uint32_t kStepRows = kStageRows * kHistWarps;  // rows per CTA per step
+
+template <typename CodeT>
+struct __align__(16) HistStage {
+  CodeT codes[kStageRows][kHistLanes];
+  float2 pairs[kStageRows];
+  int4 limbs[kStageRows];
+};
+
+template <typename CodeT, bool kUnitH>
+constexpr size_t hist2_smem() {
+  return size_t(kUnitH ? 3 : 4) * kPlaneWords * sizeof(int) +
+         size_t(kHistWarps) * 2 * sizeof(HistStage<CodeT>);
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+__device__ __forceinline__ void red_shared(uint32_t addr, int v) {
+  asm volatile("red.shared.add.s32 [%0], %1;\n" ::"r"(addr), "r"(v) : "memory");
+}
+
+// One step of one warp: up to kStageRows rows of one item.
+struct HistStep {
+  uint32_t valid;    // 0 past the CTA's last item
+  uint32_t group, pair;
+  uint32_t row0;     // root: first row id; else index of the first row in the id list
+  uint32_t n;        // rows of this warp (0..kStageRows)
+  uint32_t cta_rows; // rows of the whole CTA in this step
+};
+
+template <bool kRoot>
+struct HistCursor {
+  uint64_t it, end;
+  uint32_t k;        // step within the item
+  uint32_t group, pair, begin, cnt;
+  uint32_t total_tiles;
+  uint32_t t_lo, t_hi;   // tiles of `pair`: [t_lo, t_hi)
+  uint32_t seg0, segn;   // rows of the built child of `pair`
+
+  __device__ __forceinline__ void load_pair(const HistArgs& a) {
+    if (kRoot) {
+      t_lo = 0;
+      t_hi = total_tiles;
+      seg0 = __ldg(a.seg_begin);
+      segn = __ldg(a.seg_count);
+      return;
+    }
+    t_lo = __ldg(a.tile_offset + pair);
+    t_hi = __ldg(a.tile_offset + pair + 1);
+    const uint32_t slot = 2u * pair + (__ldg(a.built_left + pair) ? 0u : 1u);
+    seg0 = __ldg(a.seg_begin + slot);
+    segn = __ldg(a.seg_count + slot);
+  }
+  // Full lookup (binary search over the pairs' tile offsets).
+  __device__ __forceinline__ void resolve(const HistArgs& a, uint32_t npairs) {
+    group = uint32_t(it / total_tiles);
+    const uint32_t t = uint32_t(it % total_tiles);
+    pair = 0;
+    if (!kRoot) {
+      uint32_t lo = 0, hi = npairs;
+      while (hi - lo > 1) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (__ldg(a.tile_offset + mid) <= t) lo = mid;
+        else hi = mid;
+      }
+      pair = lo;
+    }
+    load_pair(a);
+    locate(t);
+  }
+  __device__ __forceinline__ void locate(uint32_t t) {
+    begin = seg0 + (t - t_lo) * kTileRows;
+    cnt = min(kTileRows, seg0 + segn - begin);
+  }
+  __device__ __forceinline__ HistStep step(uint32_t warp) const {
+    HistStep s;
+    s.valid = it < end;
+    s.group = group;
+    s.pair = pair;
+    const uint32_t off = k * kStepRows;
+    s.cta_rows = s.valid ? min(kStepRows, cnt - off) : 0u;
+    const uint32_t w0 = off + warp * kStageRows;
+    s.n = (s.valid && w0 < cnt) ? min(kStageRows, cnt - w0) : 0u;
+    s.row0 = begin + w0;
+    return s;
+  }
+  // Next step; the pair advances incrementally (items of a CTA are in tile
+  // order), so only a change of feature group needs the full lookup.
+  __device__ __forceinline__ void advance(const HistArgs& a, uint32_t npairs) {
+    if (it >= end) return;
+    if ((k + 1) * kStepRows < cnt) {
+      ++k;
+      return;
+    }
+    k = 0;
+    if (++it >= end) return;
+    const uint32_t g = uint32_t(it / total_tiles), t = uint32_t(it % total_tiles);
+    if (g != group) {
+      resolve(a, npairs);
+      return;
+    }
+    if (!kRoot && t >= t_hi) {
+      do {
+        ++pair;
+        t_lo = t_hi;
+        t_hi = __ldg(a.tile_offset + pair + 1);
+      } while (t >= t_hi);
+      const uint32_t slot = 2u * pair + (__ldg(a.built_left + pair) ? 0u : 1u);
+      seg0 = __ldg(a.seg_begin + slot);
+      segn = __ldg(a.seg_count + slot);
+    }
+    locate(t);
+  }
+};
+
+template <typename CodeT, bool kUnitH, bool kRoot>
+__device__ __forceinline__ void hist_body2(const HistArgs& a, int* smem, const DriverState& st,
+                                           uint32_t Lg, uint32_t Lh) {
+  constexpr uint32_t kPlanes = kUnitH ? 3 : 4;  // g0, g1, h0 | count, h1
+  constexpr uint32_t kPlaneBytes = kPlaneWords * sizeof(int);
+  constexpr uint32_t kSlice = kHistLanes * sizeof(CodeT);  // bytes of a row's group slice
+  const uint32_t B = a.e.bins, B1 = B + 1, C = a.e.cols;
+  const uint32_t words = B1 * kHistLanes;
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t npairs = kRoot ? 1u : st.pairs;
+  HistCursor<kRoot> cur;
+  hist_item_range(st.total_tiles, a.ngroups, cur.it, cur.end);
+  cur.k = 0;
+  cur.total_tiles = st.total_tiles;
+  if (cur.it >= cur.end) return;
+  cur.resolve(a, npairs);
+
+  HistStage<CodeT>* stage = reinterpret_cast<HistStage<CodeT>*>(smem + kPlanes * kPlaneWords) + warp * 2;
+  int* topg = a.top + size_t(blockIdx.x) * 2 * kPlaneWords;
+  int* toph = topg + kPlaneWords;
+  const float2 sc = *a.scale;
+  const long long qh_unit = __float2ll_rn(sc.y);
+  const uint32_t Lmax = kUnitH ? Lg : (Lg > Lh ? Lg : Lh);
+  const uint32_t norm_rows = (1u << (31 - Lmax)) - 1;
+  const unsigned char* codes = static_cast<const unsigned char*>(a.e.codes);
+  const size_t row_bytes = size_t(a.e.stride) * sizeof(CodeT);
+  const uint32_t miss_slot = a.e.missing;
+
+  for (uint32_t i = threadIdx.x; i < kPlanes * kPlaneWords; i += blockDim.x) smem[i] = 0;
+  {
+    int* sz = reinterpret_cast<int*>(stage - warp * 2);
+    const uint32_t n = kHistWarps * 2 * sizeof(HistStage<CodeT>) / sizeof(int);
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) sz[i] = 0;
+  }
+  for (uint32_t i = threadIdx.x; i < 2 * kPlaneWords; i += blockDim.x) topg[i] = 0;
+  __syncthreads();
+
+  // Copies of one step's code slices and gradient pairs into stage buffer
+  // `buf`; `id` holds the row id of lane j's row (non-root).
+  auto issue = [&](const HistStep& s, uint32_t id, uint32_t buf) {
+    if (!s.n) return;
+    HistStage<CodeT>& dst = stage[buf];
+    const uint32_t fvalid = min(kHistLanes, C - s.group * kHistLanes);
+    const uint32_t chunks = (fvalid * sizeof(CodeT) + 15) / 16;  // 16-byte pieces of the slice
+    constexpr uint32_t kParts = kSlice / 16;                      // 4 (u16) or 2 (u8)
+    constexpr uint32_t kRowsPerPass = 32 / kParts;
+    const uint32_t part = lane % kParts;
+    const size_t col_bytes = size_t(s.group) * kSlice + part * 16;
+#pragma unroll
+    for (uint32_t pass = 0; pass < kStageRows / kRowsPerPass; ++pass) {
+      const uint32_t r = pass * kRowsPerPass + lane / kParts;
+      const uint32_t rid = kRoot ? s.row0 + r : __shfl_sync(0xffffffffu, id, r);
+      if (r < s.n && part < chunks)
+        cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(&dst.codes[r][0])) + part * 16,
+                   codes + size_t(rid) * row_bytes + col_bytes);
+    }
+    if (lane < s.n) {
+      const uint32_t rid = kRoot ? s.row0 + lane : id;
+      cp_async8(static_cast<uint32_t>(__cvta_generic_to_shared(&dst.pairs[lane])), a.pairs + rid);
+    }
+  };
+  auto load_ids = [&](const HistStep& s) -> uint32_t {
+    if (kRoot) return 0u;
+    return lane < s.n ? __ldg(a.rows + s.row0 + lane) : 0u;
+  };
+  auto split2 = [](long long q, uint32_t L, int& c0, int& c1) {
+    const bool neg = q < 0;
+    const unsigned long long m = (unsigned long long)(neg ? -q : q);
+    c0 = int(m & ((1ull << L) - 1));
+    c1 = int(m >> L);
+    if (neg) {
+      c0 = -c0;
+      c1 = -c1;
+    }
+  };
+  auto carry = [&](int* p0, int* p1, int* top, uint32_t i, uint32_t L) {
+    int x0 = p0[i];
+    const int c0 = x0 >> L;
+    x0 -= c0 * (1 << L);
+    int x1 = p1[i] + c0;
+    const int c1 = x1 >> L;
+    x1 -= c1 * (1 << L);
+    p0[i] = x0;
+    p1[i] = x1;
+    if (c1) top[i] += c1;
+  };
+  auto normalise = [&]() {
+    for (uint32_t i = threadIdx.x; i < words; i += blockDim.x) {
+      carry(smem, smem + kPlaneWords, topg, i, Lg);
+      if (!kUnitH) carry(smem + 2 * kPlaneWords, smem + 3 * kPlaneWords, toph, i, Lh);
+    }
+  };
+  auto flush = [&](uint32_t group, uint32_t pair) {
+    const uint32_t f0 = group * kHistLanes;
+    int* p0 = smem;
+    int* p1 = smem + kPlaneWords;
+    int* p2 = smem + 2 * kPlaneWords;
+    int* p3 = smem + 3 * kPlaneWords;
+    for (uint32_t i = threadIdx.x; i < words; i += blockDim.x) {
+      const uint32_t slot = i / kHistLanes, f = f0 + (i % kHistLanes);
+      const uint32_t bin = slot == miss_slot ? B : slot;
+      const long long g = (long long)((unsigned long long)(long long)p0[i] +
+                                      ((unsigned long long)(long long)p1[i] << Lg) +
+                                      ((unsigned long long)(long long)topg[i] << (2 * Lg)));
+      long long h;
+      bool any;
+      if (kUnitH) {
+        h = (long long)((unsigned long long)(unsigned)p2[i] * (unsigned long long)qh_unit);
+        any = g != 0 || p2[i] != 0;
+      } else {
+        h = (long long)((unsigned long long)(long long)p2[i] +
+                        ((unsigned long long)(long long)p3[i] << Lh) +
+                        ((unsigned long long)(long long)toph[i] << (2 * Lh)));
+        any = g != 0 || h != 0;
+      }
+      if (any && f < C) {
+        longlong2* dst = a.built + (size_t(pair) * C + f) * B1 + bin;
+        atomicAdd(reinterpret_cast<unsigned long long*>(&dst->x), (unsigned long long)g);
+        atomicAdd(reinterpret_cast<unsigned long long*>(&dst->y), (unsigned long long)h);
+      }
+      p0[i] = 0;
+      p1[i] = 0;
+      p2[i] = 0;
+      if (!kUnitH) p3[i] = 0;
+      topg[i] = 0;
+      if (!kUnitH) toph[i] = 0;
+    }
+  };
+
+  // Three-deep pipeline: s0 accumulates, s1's copies are in flight, s2's row
+  // ids are being loaded.
+  HistStep s0 = cur.step(warp);
+  cur.advance(a, npairs);
+  HistStep s1 = cur.step(warp);
+  cur.advance(a, npairs);
+  HistStep s2 = cur.step(warp);
+  uint32_t id = load_ids(s0);
+  issue(s0, id, 0);
+  cp_async_commit();
+  id = load_ids(s1);
+  uint32_t buf = 0;
+  int64_t cur_group = -1, cur_pair = -1;
+  uint32_t since = 0;
+  const uint32_t plane0 = static_cast<uint32_t>(__cvta_generic_to_shared(smem)) + lane * 4;
+
+  while (s0.valid) {
+    if (int64_t(s0.group) != cur_group || int64_t(s0.pair) != cur_pair) {
+      if (cur_group >= 0) {
+        __syncthreads();
+        flush(uint32_t(cur_group), uint32_t(cur_pair));
+        __syncthreads();
+        since = 0;
+      }
+      cur_group = s0.group;
+      cur_pair = s0.pair;
+    }
+    if (since + s0.cta_rows > norm_rows) {
+      __syncthreads();
+      normalise();
+      __syncthreads();
+      since = 0;
+    }
+    cp_async_wait_all();
+    __syncwarp();
+    HistStage<CodeT>& st0 = stage[buf];
+    if (lane < kStageRows) {
+      int g0 = 0, g1 = 0, h0 = 0, h1 = 0;
+      if (lane < s0.n) {
+        const float2 gp = st0.pairs[lane];
+        split2(__float2ll_rn(__fmul_rn(gp.x, sc.x)), Lg, g0, g1);
+        if (kUnitH) h0 = 1;
+        else split2(__float2ll_rn(__fmul_rn(gp.y, sc.y)), Lh, h0, h1);
+      }
+      st0.limbs[lane] = make_int4(g0, g1, h0, h1);
+    }
+    __syncwarp();
+    issue(s1, id, buf ^ 1);
+    cp_async_commit();
+    id = load_ids(s2);
+    // Rows past n carry zero limbs (their stale codes are valid slots).
+    const uint32_t nr = (s0.n + 7) & ~7u;
+    const CodeT* cc = &st0.codes[0][lane];
+    for (uint32_t j0 = 0; j0 < nr; j0 += 8) {
+#pragma unroll
+      for (uint32_t u = 0; u < 8; ++u) {
+        const uint32_t code = cc[(j0 + u) * kHistLanes];
+        const int4 q = st0.limbs[j0 + u];
+        const uint32_t addr = plane0 + code * (kHistLanes * 4);
+        red_shared(addr, q.x);
+        red_shared(addr + kPlaneBytes, q.y);
+        red_shared(addr + 2 * kPlaneBytes, q.z);
+        if (!kUnitH) red_shared(addr + 3 * kPlaneBytes, q.w);
+      }
+    }
+    __syncwarp();
+    since += s0.cta_rows;
+    s0 = s1;
+    s1 = s2;
+    cur.advance(a, npairs);
+    s2 = cur.step(warp);
+    buf ^= 1;
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  flush(uint32_t(cur_group), uint32_t(cur_pair));
+}
+
 template <typename CodeT, bool kUnitH, bool kRoot>
 __global__ void __launch_bounds__(1024, 1) hist_kernel(HistArgs a) {
   extern __shared__ __align__(16) int smem[];
@@ -618,7 +986,8 @@ __global__ void __launch_bounds__(1024, 1) hist_kernel(HistArgs a) {
     if (pg.n == 2) pg = LimbPlan{(pg.L * 2 + 2) / 3 < 17 ? 17u : (pg.L * 2 + 2) / 3, 3u};
     if (!kUnitH && ph.n == 2) ph = LimbPlan{(ph.L * 2 + 2) / 3 < 17 ? 17u : (ph.L * 2 + 2) / 3, 3u};
   }
-  if (pg.n == 2 && ph.n == 2) hist_body<CodeT, kUnitH, kRoot, 2, 2>(a, smem, st, pg.L, ph.L);
+  if (a.top && pg.n == 2 && (kUnitH || ph.n == 2)) hist_body2<CodeT, kUnitH, kRoot>(a, smem, st, pg.L, ph.L);
+  else if (pg.n == 2 && ph.n == 2) hist_body<CodeT, kUnitH, kRoot, 2, 2>(a, smem, st, pg.L, ph.L);
   else if (pg.n == 2) hist_body<CodeT, kUnitH, kRoot, 2, 3>(a, smem, st, pg.L, ph.L);
   else if (ph.n == 2) hist_body<CodeT, kUnitH, kRoot, 3, 2>(a, smem, st, pg.L, ph.L);
   else hist_body<CodeT, kUnitH, kRoot, 3, 3>(a, smem, st, pg.L, ph.L);
@@ -1383,6 +1752,12 @@ HistConfig hist_config(const Ellpack& e, bool unit_hessian) {
   c.feature_group = kHistLanes;
   c.smem = size_t(unit_hessian ? 4 : 6) * (e.bins + 1) * kHistLanes * sizeof(int) +
            size_t(kHistWarps) * 32 * (sizeof(int4) + (unit_hessian ? 0 : sizeof(int2)));
+  // The staged two-limb path needs its fixed 257-slot planes and stage buffers.
+  const size_t staged = e.bytes_per_code == 1
+                            ? (unit_hessian ? hist2_smem<uint8_t, true>() : hist2_smem<uint8_t, false>())
+                            : (unit_hessian ? hist2_smem<uint16_t, true>() : hist2_smem<uint16_t, false>());
+  if (e.bins + 1 <= kSlots) c.smem = std::max(c.smem, staged);
+  c.top_ints = size_t(2) * kPlaneWords;
   c.threads = kHistWarps * 32;
   return c;
 }
@@ -1423,6 +1798,7 @@ void tree_level_hist(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t dep
   a.seg_begin = ws.seg_begin[depth & 1];
   a.seg_count = ws.seg_count[depth & 1];
   a.built = ws.built;
+  a.top = tl.ell.bins + 1 <= kSlots ? ws.hist_top : nullptr;
   a.max_bits = tl.max_bits;
   a.min_limbs = tl.min_limbs;
   a.ngroups = (tl.ell.cols + kHistLanes - 1) / kHistLanes;
