@@ -204,10 +204,11 @@ def shard(rows, rank, world):
 
 
 def launches_per_round(depth, groups):
-    # gradients, window, scales, exact, exact scales; per tree: init, 4 per
-    # level (histogram, evaluation, control, partition), 2 per non-last level
-    # (counts, plan).
-    return 5 + groups * (1 + 4 * depth + 2 * (depth - 1))
+    # gradients, window, scales, exact, exact scales; per tree: init, root
+    # limbs, 5 per level (three-limb and staged histogram kernels, one of
+    # which exits at once; evaluation, control, partition), 2 per non-last
+    # level (counts, plan).
+    return 5 + groups * (2 + 5 * depth + 2 * (depth - 1))
 
 
 # ---------------------------------------------------------------------------
@@ -420,7 +421,9 @@ def main():
                 "algorithmic_bytes_per_launch": prof["hist_bytes"] / max(prof["hist_launches"], 1),
                 "avg_launch_ms": prof["hist_ms"] / max(prof["hist_launches"], 1),
                 "launches": prof["hist_launches"],
-                "hist_ms_per_round": prof["hist_ms"] / K}
+                "hist_ms_per_round": prof["hist_ms"] / K,
+                "per_level_ms_mrows": [[round(ms / K, 3), round(rows / K / 1e6, 3)]
+                                       for ms, rows, _ in prof.get("levels", []) if rows]}
 
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:

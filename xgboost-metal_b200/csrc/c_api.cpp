@@ -557,7 +557,13 @@ XGB_DLL int XGBoosterGetCudaProfile(BoosterHandle handle, char const** out) {
     results.str = "{\"hist_ms\":" + std::to_string(p.hist_ms) +
                   ",\"hist_bytes\":" + std::to_string(p.hist_bytes) +
                   ",\"hist_launches\":" + std::to_string(p.hist_launches) +
-                  ",\"rounds\":" + std::to_string(p.rounds) + "}";
+                  ",\"rounds\":" + std::to_string(p.rounds) + ",\"levels\":[";
+    for (uint32_t d = 0; d < xgbb::kMaxDepth; ++d) {
+      if (d) results.str += ",";
+      results.str += "[" + std::to_string(p.level_ms[d]) + "," + std::to_string(p.level_rows[d]) + "," +
+                     std::to_string(p.level_nodes[d]) + "]";
+    }
+    results.str += "]}";
     *out = results.str.c_str();
   });
 }

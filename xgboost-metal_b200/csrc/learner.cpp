@@ -143,7 +143,7 @@ struct Booster::TrainState {
   DeviceBuffer margins, pairs, mass, scales;
   DeviceBuffer state, ids[2], sums[2], seg_begin[2], seg_count[2], parent_slot, built_left,
       tile_offset, ptile_offset, cursor_l, cursor_r, counts_local, counts_global, mode, slot_leaf,
-      keys[2], cand, nodes, built, bank[2], rows_buf[2], level_rows, level_nodes, hist_top;
+      keys[2], cand, nodes, built, bank[2], rows_buf[2], level_rows, level_nodes, ord[2], limbs_root;
   TreeWorkspace ws{};
   HistConfig hc{};
   std::vector<cudaGraphExec_t> graphs;
@@ -387,7 +387,9 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp) {
     ts->seg_count[i].resize(kMaxFrontier * 4);
     ts->keys[i].resize(kMaxFrontier * 8);
     ts->rows_buf[i].resize(std::max<size_t>(n, 1) * 4);
+    ts->ord[i].resize(std::max<size_t>(n, 1) * 16);
   }
+  ts->limbs_root.resize(std::max<size_t>(n, 1) * 16);
   ts->parent_slot.resize(kMaxFrontier * 4);
   ts->built_left.resize(kMaxFrontier * 4);
   ts->tile_offset.resize((kMaxFrontier + 1) * 4);
@@ -425,6 +427,7 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp) {
     ws.keys[i] = ts->keys[i].as<unsigned long long>();
     ws.bank[i] = ts->bank[i].as<longlong2>();
     ws.rows[i] = ts->rows_buf[i].as<uint32_t>();
+    ws.ord[i] = ts->ord[i].get();
   }
   ws.parent_slot = ts->parent_slot.as<uint32_t>();
   ws.built_left = ts->built_left.as<uint32_t>();
@@ -442,13 +445,8 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp) {
   ws.node_capacity = ts->capacity;
   ws.level_rows = ts->level_rows.as<unsigned long long>();
   ws.level_nodes = ts->level_nodes.as<uint32_t>();
+  ws.limbs_root = ts->limbs_root.as<int4>();
   ts->hc = hist_config(e, objective_ == kSquaredError && d.weights.empty());
-  {
-    int sms = 148;
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device_);
-    ts->hist_top.resize(size_t(sms) * ts->hc.top_ints * sizeof(int));
-    ws.hist_top = ts->hist_top.as<int>();
-  }
   ts->graphs.assign(G, nullptr);
   if (profiling) {
     ts->events.resize(size_t(G) * D * 2);
@@ -616,6 +614,9 @@ void Booster::run_round(TrainState& ts) {
         profile.hist_ms += ms;
         profile.hist_bytes += rows * (row_bytes + (depth ? 4.0 : 0.0)) + nodes * node_bytes;
         ++profile.hist_launches;
+        profile.level_ms[depth] += ms;
+        profile.level_rows[depth] += rows;
+        profile.level_nodes[depth] += nodes;
       }
   }
   ++profile.rounds;

@@ -96,6 +96,8 @@ struct Profile {
   double hist_ms = 0, total_ms = 0;
   double hist_bytes = 0;
   uint64_t hist_launches = 0, kernel_launches = 0, rounds = 0;
+  // Per tree level: histogram time, rows in built nodes, built nodes.
+  double level_ms[kMaxDepth] = {}, level_rows[kMaxDepth] = {}, level_nodes[kMaxDepth] = {};
 };
 
 class Booster {

@@ -370,7 +370,8 @@ __global__ void fill_margins_kernel(float* margins, const float* base, uint32_t 
 // ---------------------------------------------------------------------------
 struct HistArgs {
   Ellpack e;
-  const float2* pairs;
+  const float2* pairs;   // gradient pairs in the order of the level's row list (three-limb kernel)
+  const int4* limbs;     // balanced two-limb values in that order (staged kernel)
   const float2* scale;
   const unsigned int* max_bits;  // largest |g| and |h| bits of this group (float bits)
   const uint32_t* rows;
@@ -380,7 +381,7 @@ struct HistArgs {
   const uint32_t* seg_begin;
   const uint32_t* seg_count;
   longlong2* built;
-  int* top;            // [grid][2][kPlaneWords] carries out of limb 1 (staged path)
+  bool staged;         // the staged two-limb kernel may take this level (bins + 1 <= 257)
   uint32_t ngroups;
   uint32_t min_limbs;  // 3 forces three-limb accumulation (tuning; results unchanged)
 };
@@ -421,6 +422,7 @@ __device__ __forceinline__ void hist_item_range(uint32_t total_tiles, uint32_t n
 // limbs; otherwise L >= bitlen/3 and values touch three.
 struct LimbPlan {
   uint32_t L, n;
+  uint32_t bits;  // bit length of the largest |q| of the round
 };
 __device__ __forceinline__ LimbPlan limb_plan(unsigned int max_bits, float scale) {
   const float mv = __uint_as_float(max_bits & 0x7fffffffu);
@@ -429,10 +431,10 @@ __device__ __forceinline__ LimbPlan limb_plan(unsigned int max_bits, float scale
   const uint32_t bl = a ? 64u - __clzll(a) : 0u;
   if (bl <= 42) {
     const uint32_t L = (bl + 1) / 2;
-    return {L < 17 ? 17u : L, 2u};
+    return {L < 17 ? 17u : L, 2u, bl};
   }
   const uint32_t L = (bl + 2) / 3;
-  return {L > 21 ? 21u : L, 3u};
+  return {L > 21 ? 21u : L, 3u, bl};
 }
 
 __device__ __forceinline__ long long combine_limbs(const int* base, uint32_t plane, uint32_t L) {
@@ -471,7 +473,9 @@ __device__ __forceinline__ void hist_body(const HistArgs& a, int* smem, const Dr
   if (it >= end) return;
   const float2 s = *a.scale;
   const uint32_t Lmax = Lg > Lh ? Lg : Lh;
-  const uint32_t norm_rows = (1u << (31 - Lmax)) - 1;  // rows allowed between carries
+  // Rows allowed between carries: a word below 2^L plus n values below 2^L, and
+  // the carry that normalise() adds to limb 1, stay inside int32.
+  const uint32_t norm_rows = (1u << (31 - Lmax)) - 2;
   // Every warp takes one batch of `batch` rows per sub-chunk; 21-bit limbs
   // carry every 1023 rows, so their sub-chunks are half as long.
   const uint32_t batch = Lmax >= 21 ? 16u : 32u;
@@ -584,7 +588,7 @@ __device__ __forceinline__ void hist_body(const HistArgs& a, int* smem, const Dr
             mine ? (kRoot ? begin + sub + base + lane : __ldg(a.rows + begin + sub + base + lane)) : 0u;
         int g0 = 0, g1 = 0, g2 = 0, h0 = 0, h1 = 0, h2 = 0;
         if (mine) {
-          const float2 gp = __ldg(a.pairs + my_row);
+          const float2 gp = __ldg(a.pairs + begin + sub + base + lane);
           split(__float2ll_rn(__fmul_rn(gp.x, s.x)), Lg, g0, g1, g2);
           if (kUnitH) h0 = 1;
           else split(__float2ll_rn(__fmul_rn(gp.y, s.y)), Lh, h0, h1, h2);
@@ -633,31 +637,36 @@ __device__ __forceinline__ void hist_body(const HistArgs& a, int* smem, const Dr
 // ---------------------------------------------------------------------------
 // Staged two-limb histogram (every |q| of the round has at most 2L bits).
 //
-// Same ownership as hist_body (one CTA per SM, lane = feature, contiguous run
-// of (feature group, tile) items), but the global reads leave the critical
-// path: each warp copies the 32-feature code slice and the gradient pair of
-// its next 16 rows into shared memory with cp.async while it accumulates the
-// current 16, and the row ids two steps ahead are loaded into a register. The
-// inner loop is then one shared load of the code, one broadcast load of the
-// row's limbs and 3-4 shared atomics at compile-time plane offsets. Limb 1
-// carries into a CTA-private int32 array in global memory (L2-resident), so
-// only the four (three) atomically-updated planes live in shared memory.
+// Same ownership as hist_body (one CTA per SM, lane = feature, tile-ordered
+// items), with 16 warps. The global reads leave the critical path: each warp
+// copies the 32-feature code slice and the precomputed limbs of each of its
+// 32-row steps into one of two shared-memory stage buffers with cp.async, one
+// step ahead of the step it accumulates, and loads the row ids one step
+// ahead of the copies. The inner loop is one shared load of the code, one
+// broadcast load of the row's limbs and 3-4 shared atomics at compile-time
+// plane offsets. The carries out of limb 1 stay in registers (each thread
+// owns fixed words of the planes), so normalisation and flush touch only
+// shared memory and registers.
 constexpr uint32_t kSlots = 257;                       // bins 0..255 + missing slot (<= 256)
 constexpr uint32_t kPlaneWords = kSlots * kHistLanes;  // ints per plane
-constexpr uint32_t kStageRows = 16;                    // rows per warp per step
-constexpr uint32_t kStepRows = kStageRows * kHistWarps;  // rows per CTA per step
+constexpr uint32_t kH2Warps = 16;
+constexpr uint32_t kH2Threads = kH2Warps * 32;
+constexpr uint32_t kStageRows = 32;                    // rows per warp per step
+constexpr uint32_t kStepRows = kStageRows * kH2Warps;  // rows per CTA per step
+constexpr uint32_t kStageBufs = 2;                     // one step of copies in flight
+constexpr uint32_t kOwn2 = (kPlaneWords / 2 + kH2Threads - 1) / kH2Threads;  // word pairs per thread
+static_assert(kPlaneWords % 2 == 0, "planes hold whole word pairs");
 
 template <typename CodeT>
 struct __align__(16) HistStage {
   CodeT codes[kStageRows][kHistLanes];
-  float2 pairs[kStageRows];
   int4 limbs[kStageRows];
 };
 
 template <typename CodeT, bool kUnitH>
 constexpr size_t hist2_smem() {
   return size_t(kUnitH ? 3 : 4) * kPlaneWords * sizeof(int) +
-         size_t(kHistWarps) * 2 * sizeof(HistStage<CodeT>);
+         size_t(kH2Warps) * kStageBufs * sizeof(HistStage<CodeT>);
 }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
@@ -667,19 +676,77 @@ __device__ __forceinline__ void cp_async8(uint32_t dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(dst), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
 __device__ __forceinline__ void red_shared(uint32_t addr, int v) {
   asm volatile("red.shared.add.s32 [%0], %1;\n" ::"r"(addr), "r"(v) : "memory");
 }
 
-// One step of one warp: up to kStageRows rows of one item.
+// Limb plans of a round; the staged kernel takes the rounds whose values all
+// fit two limbs, the three-limb kernel the others. The histogram, limb and
+// partition kernels make the same choice from the same inputs.
+__device__ __forceinline__ bool plan_round(const float2* scale, const unsigned int* max_bits,
+                                           uint32_t min_limbs, bool staged, bool unit_h, LimbPlan& pg,
+                                           LimbPlan& ph) {
+  const float2 s = *scale;
+  pg = limb_plan(max_bits[0], s.x);
+  ph = unit_h ? LimbPlan{17u, 2u, 1u} : limb_plan(max_bits[1], s.y);
+  if (min_limbs >= 3) {
+    // Three limbs of L = max(17, bitlen / 3) bits hold any value of the round.
+    if (pg.n == 2) pg = LimbPlan{(pg.L * 2 + 2) / 3 < 17 ? 17u : (pg.L * 2 + 2) / 3, 3u, pg.bits};
+    if (!unit_h && ph.n == 2) ph = LimbPlan{(ph.L * 2 + 2) / 3 < 17 ? 17u : (ph.L * 2 + 2) / 3, 3u, ph.bits};
+  }
+  return staged && pg.n == 2 && ph.n == 2;
+}
+__device__ __forceinline__ bool plan_round(const HistArgs& a, bool unit_h, LimbPlan& pg, LimbPlan& ph) {
+  return plan_round(a.scale, a.max_bits, a.min_limbs, a.staged, unit_h, pg, ph);
+}
+
+// Balanced two-limb split of q: l0 in [-2^(L-1), 2^(L-1)), l1 = (q - l0) / 2^L.
+__device__ __forceinline__ void split_balanced(long long q, uint32_t L, int& l0, int& l1) {
+  const long long half = 1ll << (L - 1);
+  l0 = int(((q + half) & ((1ll << L) - 1)) - half);
+  l1 = int((q - l0) >> L);  // exact: q - l0 is a multiple of 2^L
+}
+// (g0, g1, h0, h1) of one row, or (g0, g1, 1, 0) with unit hessians.
+__device__ __forceinline__ int4 row_limbs(float2 gp, float2 sc, uint32_t Lg, uint32_t Lh, bool unit_h) {
+  int4 v;
+  split_balanced(__float2ll_rn(__fmul_rn(gp.x, sc.x)), Lg, v.x, v.y);
+  if (unit_h) {
+    v.z = 1;
+    v.w = 0;
+  } else {
+    split_balanced(__float2ll_rn(__fmul_rn(gp.y, sc.y)), Lh, v.z, v.w);
+  }
+  return v;
+}
+
+// Limbs of every row (row order) for the root level of a staged round.
+__global__ void limbs_kernel(const float2* __restrict__ pairs, uint32_t rows, const float2* scale,
+                             const unsigned int* max_bits, uint32_t min_limbs, bool staged, bool unit_h,
+                             int4* __restrict__ out) {
+  LimbPlan pg, ph;
+  if (!plan_round(scale, max_bits, min_limbs, staged, unit_h, pg, ph)) return;
+  const float2 sc = *scale;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < rows; i += gridDim.x * blockDim.x)
+    out[i] = row_limbs(__ldg(pairs + i), sc, pg.L, ph.L, unit_h);
+}
+
+// One step of one warp: up to kStageRows rows of one item, packed into three
+// registers (group < 2^22, pair < 2^10, rows of the CTA <= kStepRows).
 struct HistStep {
-  uint32_t valid;    // 0 past the CTA's last item
-  uint32_t group, pair;
-  uint32_t row0;     // root: first row id; else index of the first row in the id list
-  uint32_t n;        // rows of this warp (0..kStageRows)
-  uint32_t cta_rows; // rows of the whole CTA in this step
+  uint32_t gp;    // group << 10 | pair
+  uint32_t row0;  // root: first row id; else index of the first row in the row list
+  uint32_t meta;  // valid << 31 | cta_rows << 8 | n
+  __device__ __forceinline__ bool valid() const { return meta >> 31; }
+  __device__ __forceinline__ uint32_t n() const { return meta & 0xffu; }
+  __device__ __forceinline__ uint32_t cta_rows() const { return (meta >> 8) & 0xffffu; }
+  __device__ __forceinline__ uint32_t group() const { return gp >> 10; }
+  __device__ __forceinline__ uint32_t pair() const { return gp & 0x3ffu; }
 };
+static_assert(kMaxFrontier / 2 <= 0x400u && kStepRows <= 0xffffu && kStageRows <= 0xffu, "HistStep packing");
 
 template <bool kRoot>
 struct HistCursor {
@@ -727,13 +794,13 @@ struct HistCursor {
   }
   __device__ __forceinline__ HistStep step(uint32_t warp) const {
     HistStep s;
-    s.valid = it < end;
-    s.group = group;
-    s.pair = pair;
+    const bool valid = it < end;
+    s.gp = group << 10 | pair;
     const uint32_t off = k * kStepRows;
-    s.cta_rows = s.valid ? min(kStepRows, cnt - off) : 0u;
+    const uint32_t cta_rows = valid ? min(kStepRows, cnt - off) : 0u;
     const uint32_t w0 = off + warp * kStageRows;
-    s.n = (s.valid && w0 < cnt) ? min(kStageRows, cnt - w0) : 0u;
+    const uint32_t n = (valid && w0 < cnt) ? min(kStageRows, cnt - w0) : 0u;
+    s.meta = uint32_t(valid) << 31 | cta_rows << 8 | n;
     s.row0 = begin + w0;
     return s;
   }
@@ -767,8 +834,13 @@ struct HistCursor {
 };
 
 template <typename CodeT, bool kUnitH, bool kRoot>
-__device__ __forceinline__ void hist_body2(const HistArgs& a, int* smem, const DriverState& st,
-                                           uint32_t Lg, uint32_t Lh) {
+__global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
+  extern __shared__ __align__(16) int smem[];
+  const DriverState st = *a.state;
+  if (!st.frontier || !st.total_tiles) return;
+  LimbPlan pg, ph;
+  if (!plan_round(a, kUnitH, pg, ph)) return;  // the three-limb kernel builds this level
+  const uint32_t Lg = pg.L, Lh = ph.L;
   constexpr uint32_t kPlanes = kUnitH ? 3 : 4;  // g0, g1, h0 | count, h1
   constexpr uint32_t kPlaneBytes = kPlaneWords * sizeof(int);
   constexpr uint32_t kSlice = kHistLanes * sizeof(CodeT);  // bytes of a row's group slice
@@ -783,120 +855,140 @@ __device__ __forceinline__ void hist_body2(const HistArgs& a, int* smem, const D
   if (cur.it >= cur.end) return;
   cur.resolve(a, npairs);
 
-  HistStage<CodeT>* stage = reinterpret_cast<HistStage<CodeT>*>(smem + kPlanes * kPlaneWords) + warp * 2;
-  int* topg = a.top + size_t(blockIdx.x) * 2 * kPlaneWords;
-  int* toph = topg + kPlaneWords;
+  HistStage<CodeT>* stage = reinterpret_cast<HistStage<CodeT>*>(smem + kPlanes * kPlaneWords) + warp * kStageBufs;
   const float2 sc = *a.scale;
   const long long qh_unit = __float2ll_rn(sc.y);
+  // Limbs are balanced: l0 in [-2^(L-1), 2^(L-1)), l1 = (q - l0) / 2^L, so
+  // |l1| <= 2^(L-1) as well when |q| < 2^(2L-1). A word starts below 2^L
+  // after a carry and may take `norm_rows` more rows before int32 overflows.
   const uint32_t Lmax = kUnitH ? Lg : (Lg > Lh ? Lg : Lh);
-  const uint32_t norm_rows = (1u << (31 - Lmax)) - 1;
+  const uint32_t per_row_bits =
+      (pg.bits + 1 <= 2 * Lg && (kUnitH || ph.bits + 1 <= 2 * Lh)) ? Lmax - 1 : Lmax;
+  const uint32_t norm_rows = uint32_t((0x7fffffffull - (1ull << Lmax)) >> per_row_bits);
   const unsigned char* codes = static_cast<const unsigned char*>(a.e.codes);
   const size_t row_bytes = size_t(a.e.stride) * sizeof(CodeT);
   const uint32_t miss_slot = a.e.missing;
 
   for (uint32_t i = threadIdx.x; i < kPlanes * kPlaneWords; i += blockDim.x) smem[i] = 0;
   {
-    int* sz = reinterpret_cast<int*>(stage - warp * 2);
-    const uint32_t n = kHistWarps * 2 * sizeof(HistStage<CodeT>) / sizeof(int);
+    int* sz = reinterpret_cast<int*>(stage - warp * kStageBufs);
+    const uint32_t n = kH2Warps * kStageBufs * sizeof(HistStage<CodeT>) / sizeof(int);
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) sz[i] = 0;
   }
-  for (uint32_t i = threadIdx.x; i < 2 * kPlaneWords; i += blockDim.x) topg[i] = 0;
   __syncthreads();
+
+  // Carries out of limb 1 of the word pairs tid + k * kH2Threads.
+  int2 tg[kOwn2], th[kOwn2];
+#pragma unroll
+  for (uint32_t k = 0; k < kOwn2; ++k) tg[k] = th[k] = make_int2(0, 0);
 
   // Copies of one step's code slices and gradient pairs into stage buffer
   // `buf`; `id` holds the row id of lane j's row (non-root).
   auto issue = [&](const HistStep& s, uint32_t id, uint32_t buf) {
-    if (!s.n) return;
+    if (!s.n()) return;
     HistStage<CodeT>& dst = stage[buf];
-    const uint32_t fvalid = min(kHistLanes, C - s.group * kHistLanes);
+    const uint32_t fvalid = min(kHistLanes, C - s.group() * kHistLanes);
     const uint32_t chunks = (fvalid * sizeof(CodeT) + 15) / 16;  // 16-byte pieces of the slice
     constexpr uint32_t kParts = kSlice / 16;                      // 4 (u16) or 2 (u8)
     constexpr uint32_t kRowsPerPass = 32 / kParts;
     const uint32_t part = lane % kParts;
-    const size_t col_bytes = size_t(s.group) * kSlice + part * 16;
+    const size_t col_bytes = size_t(s.group()) * kSlice + part * 16;
 #pragma unroll
     for (uint32_t pass = 0; pass < kStageRows / kRowsPerPass; ++pass) {
       const uint32_t r = pass * kRowsPerPass + lane / kParts;
       const uint32_t rid = kRoot ? s.row0 + r : __shfl_sync(0xffffffffu, id, r);
-      if (r < s.n && part < chunks)
+      if (r < s.n() && part < chunks)
         cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(&dst.codes[r][0])) + part * 16,
                    codes + size_t(rid) * row_bytes + col_bytes);
     }
-    if (lane < s.n) {
-      const uint32_t rid = kRoot ? s.row0 + lane : id;
-      cp_async8(static_cast<uint32_t>(__cvta_generic_to_shared(&dst.pairs[lane])), a.pairs + rid);
-    }
+    // Limb slots past n up to the next multiple of 8 are read by the
+    // unrolled loop: they hold zeros, so their stale codes add nothing.
+    if (lane < s.n())
+      cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(&dst.limbs[lane])), a.limbs + s.row0 + lane);
+    else if (lane < ((s.n() + 7) & ~7u))
+      dst.limbs[lane] = make_int4(0, 0, 0, 0);
   };
   auto load_ids = [&](const HistStep& s) -> uint32_t {
     if (kRoot) return 0u;
-    return lane < s.n ? __ldg(a.rows + s.row0 + lane) : 0u;
+    return lane < s.n() ? __ldg(a.rows + s.row0 + lane) : 0u;
   };
-  auto split2 = [](long long q, uint32_t L, int& c0, int& c1) {
-    const bool neg = q < 0;
-    const unsigned long long m = (unsigned long long)(neg ? -q : q);
-    c0 = int(m & ((1ull << L) - 1));
-    c1 = int(m >> L);
-    if (neg) {
-      c0 = -c0;
-      c1 = -c1;
-    }
-  };
-  auto carry = [&](int* p0, int* p1, int* top, uint32_t i, uint32_t L) {
-    int x0 = p0[i];
-    const int c0 = x0 >> L;
+  auto carry1 = [](int& x0, int& x1, int& top, uint32_t L) {
+    const int c0 = x0 >> L;  // arithmetic shift: floor division by 2^L
     x0 -= c0 * (1 << L);
-    int x1 = p1[i] + c0;
+    x1 += c0;
     const int c1 = x1 >> L;
     x1 -= c1 * (1 << L);
-    p0[i] = x0;
-    p1[i] = x1;
-    if (c1) top[i] += c1;
+    top += c1;
+  };
+  auto carry = [&](int* p0, int* p1, int2& top, uint32_t L) {
+    int2 x0 = *reinterpret_cast<int2*>(p0), x1 = *reinterpret_cast<int2*>(p1);
+    carry1(x0.x, x1.x, top.x, L);
+    carry1(x0.y, x1.y, top.y, L);
+    *reinterpret_cast<int2*>(p0) = x0;
+    *reinterpret_cast<int2*>(p1) = x1;
   };
   auto normalise = [&]() {
-    for (uint32_t i = threadIdx.x; i < words; i += blockDim.x) {
-      carry(smem, smem + kPlaneWords, topg, i, Lg);
-      if (!kUnitH) carry(smem + 2 * kPlaneWords, smem + 3 * kPlaneWords, toph, i, Lh);
+    __syncthreads();
+#pragma unroll
+    for (uint32_t k = 0; k < kOwn2; ++k) {
+      const uint32_t i = 2 * (threadIdx.x + k * kH2Threads);
+      if (i < words) {
+        carry(smem + i, smem + kPlaneWords + i, tg[k], Lg);
+        if (!kUnitH) carry(smem + 2 * kPlaneWords + i, smem + 3 * kPlaneWords + i, th[k], Lh);
+      }
     }
+    __syncthreads();
   };
   auto flush = [&](uint32_t group, uint32_t pair) {
+    __syncthreads();
     const uint32_t f0 = group * kHistLanes;
     int* p0 = smem;
     int* p1 = smem + kPlaneWords;
     int* p2 = smem + 2 * kPlaneWords;
     int* p3 = smem + 3 * kPlaneWords;
-    for (uint32_t i = threadIdx.x; i < words; i += blockDim.x) {
-      const uint32_t slot = i / kHistLanes, f = f0 + (i % kHistLanes);
-      const uint32_t bin = slot == miss_slot ? B : slot;
-      const long long g = (long long)((unsigned long long)(long long)p0[i] +
-                                      ((unsigned long long)(long long)p1[i] << Lg) +
-                                      ((unsigned long long)(long long)topg[i] << (2 * Lg)));
-      long long h;
-      bool any;
-      if (kUnitH) {
-        h = (long long)((unsigned long long)(unsigned)p2[i] * (unsigned long long)qh_unit);
-        any = g != 0 || p2[i] != 0;
-      } else {
-        h = (long long)((unsigned long long)(long long)p2[i] +
-                        ((unsigned long long)(long long)p3[i] << Lh) +
-                        ((unsigned long long)(long long)toph[i] << (2 * Lh)));
-        any = g != 0 || h != 0;
+#pragma unroll
+    for (uint32_t k = 0; k < kOwn2; ++k) {
+      const uint32_t i0 = 2 * (threadIdx.x + k * kH2Threads);
+      if (i0 < words) {
+#pragma unroll
+        for (uint32_t e = 0; e < 2; ++e) {
+          const uint32_t i = i0 + e;
+          const int topg = e ? tg[k].y : tg[k].x, toph = e ? th[k].y : th[k].x;
+          const uint32_t slot = i / kHistLanes, f = f0 + (i % kHistLanes);
+          const uint32_t bin = slot == miss_slot ? B : slot;
+          const long long g = (long long)((unsigned long long)(long long)p0[i] +
+                                          ((unsigned long long)(long long)p1[i] << Lg) +
+                                          ((unsigned long long)(long long)topg << (2 * Lg)));
+          long long h;
+          bool any;
+          if (kUnitH) {
+            h = (long long)((unsigned long long)(unsigned)p2[i] * (unsigned long long)qh_unit);
+            any = g != 0 || p2[i] != 0;
+          } else {
+            h = (long long)((unsigned long long)(long long)p2[i] +
+                            ((unsigned long long)(long long)p3[i] << Lh) +
+                            ((unsigned long long)(long long)toph << (2 * Lh)));
+            any = g != 0 || h != 0;
+          }
+          if (any && f < C) {
+            longlong2* dst = a.built + (size_t(pair) * C + f) * B1 + bin;
+            atomicAdd(reinterpret_cast<unsigned long long*>(&dst->x), (unsigned long long)g);
+            atomicAdd(reinterpret_cast<unsigned long long*>(&dst->y), (unsigned long long)h);
+          }
+        }
+        *reinterpret_cast<int2*>(p0 + i0) = make_int2(0, 0);
+        *reinterpret_cast<int2*>(p1 + i0) = make_int2(0, 0);
+        *reinterpret_cast<int2*>(p2 + i0) = make_int2(0, 0);
+        if (!kUnitH) *reinterpret_cast<int2*>(p3 + i0) = make_int2(0, 0);
       }
-      if (any && f < C) {
-        longlong2* dst = a.built + (size_t(pair) * C + f) * B1 + bin;
-        atomicAdd(reinterpret_cast<unsigned long long*>(&dst->x), (unsigned long long)g);
-        atomicAdd(reinterpret_cast<unsigned long long*>(&dst->y), (unsigned long long)h);
-      }
-      p0[i] = 0;
-      p1[i] = 0;
-      p2[i] = 0;
-      if (!kUnitH) p3[i] = 0;
-      topg[i] = 0;
-      if (!kUnitH) toph[i] = 0;
+      tg[k] = make_int2(0, 0);
+      th[k] = make_int2(0, 0);
     }
+    __syncthreads();
   };
 
-  // Three-deep pipeline: s0 accumulates, s1's copies are in flight, s2's row
-  // ids are being loaded.
+  // Pipeline: s0 accumulates, the copies of s1 are in flight, the row ids of
+  // s2 are being loaded.
   HistStep s0 = cur.step(warp);
   cur.advance(a, npairs);
   HistStep s1 = cur.step(warp);
@@ -911,42 +1003,26 @@ __device__ __forceinline__ void hist_body2(const HistArgs& a, int* smem, const D
   uint32_t since = 0;
   const uint32_t plane0 = static_cast<uint32_t>(__cvta_generic_to_shared(smem)) + lane * 4;
 
-  while (s0.valid) {
-    if (int64_t(s0.group) != cur_group || int64_t(s0.pair) != cur_pair) {
+  while (s0.valid()) {
+    if (int64_t(s0.group()) != cur_group || int64_t(s0.pair()) != cur_pair) {
       if (cur_group >= 0) {
-        __syncthreads();
         flush(uint32_t(cur_group), uint32_t(cur_pair));
-        __syncthreads();
         since = 0;
       }
-      cur_group = s0.group;
-      cur_pair = s0.pair;
+      cur_group = s0.group();
+      cur_pair = s0.pair();
     }
-    if (since + s0.cta_rows > norm_rows) {
-      __syncthreads();
+    if (since + s0.cta_rows() > norm_rows) {
       normalise();
-      __syncthreads();
       since = 0;
     }
-    cp_async_wait_all();
-    __syncwarp();
-    HistStage<CodeT>& st0 = stage[buf];
-    if (lane < kStageRows) {
-      int g0 = 0, g1 = 0, h0 = 0, h1 = 0;
-      if (lane < s0.n) {
-        const float2 gp = st0.pairs[lane];
-        split2(__float2ll_rn(__fmul_rn(gp.x, sc.x)), Lg, g0, g1);
-        if (kUnitH) h0 = 1;
-        else split2(__float2ll_rn(__fmul_rn(gp.y, sc.y)), Lh, h0, h1);
-      }
-      st0.limbs[lane] = make_int4(g0, g1, h0, h1);
-    }
+    cp_async_wait<0>();  // this step's copies
     __syncwarp();
     issue(s1, id, buf ^ 1);
     cp_async_commit();
     id = load_ids(s2);
-    // Rows past n carry zero limbs (their stale codes are valid slots).
-    const uint32_t nr = (s0.n + 7) & ~7u;
+    HistStage<CodeT>& st0 = stage[buf];
+    const uint32_t nr = (s0.n() + 7) & ~7u;
     const CodeT* cc = &st0.codes[0][lane];
     for (uint32_t j0 = 0; j0 < nr; j0 += 8) {
 #pragma unroll
@@ -961,15 +1037,14 @@ __device__ __forceinline__ void hist_body2(const HistArgs& a, int* smem, const D
       }
     }
     __syncwarp();
-    since += s0.cta_rows;
+    since += s0.cta_rows();
     s0 = s1;
     s1 = s2;
     cur.advance(a, npairs);
     s2 = cur.step(warp);
     buf ^= 1;
   }
-  cp_async_wait_all();
-  __syncthreads();
+  cp_async_wait<0>();
   flush(uint32_t(cur_group), uint32_t(cur_pair));
 }
 
@@ -978,16 +1053,9 @@ __global__ void __launch_bounds__(1024, 1) hist_kernel(HistArgs a) {
   extern __shared__ __align__(16) int smem[];
   const DriverState st = *a.state;
   if (!st.frontier || !st.total_tiles) return;
-  const float2 s = *a.scale;
-  LimbPlan pg = limb_plan(a.max_bits[0], s.x);
-  LimbPlan ph = kUnitH ? LimbPlan{17u, 2u} : limb_plan(a.max_bits[1], s.y);
-  if (a.min_limbs >= 3) {
-    // Three limbs of L = max(17, bitlen / 3) bits hold any value of the round.
-    if (pg.n == 2) pg = LimbPlan{(pg.L * 2 + 2) / 3 < 17 ? 17u : (pg.L * 2 + 2) / 3, 3u};
-    if (!kUnitH && ph.n == 2) ph = LimbPlan{(ph.L * 2 + 2) / 3 < 17 ? 17u : (ph.L * 2 + 2) / 3, 3u};
-  }
-  if (a.top && pg.n == 2 && (kUnitH || ph.n == 2)) hist_body2<CodeT, kUnitH, kRoot>(a, smem, st, pg.L, ph.L);
-  else if (pg.n == 2 && ph.n == 2) hist_body<CodeT, kUnitH, kRoot, 2, 2>(a, smem, st, pg.L, ph.L);
+  LimbPlan pg, ph;
+  if (plan_round(a, kUnitH, pg, ph)) return;  // the staged kernel builds this level
+  if (pg.n == 2 && ph.n == 2) hist_body<CodeT, kUnitH, kRoot, 2, 2>(a, smem, st, pg.L, ph.L);
   else if (pg.n == 2) hist_body<CodeT, kUnitH, kRoot, 2, 3>(a, smem, st, pg.L, ph.L);
   else if (ph.n == 2) hist_body<CodeT, kUnitH, kRoot, 3, 2>(a, smem, st, pg.L, ph.L);
   else hist_body<CodeT, kUnitH, kRoot, 3, 3>(a, smem, st, pg.L, ph.L);
@@ -1378,6 +1446,14 @@ struct PartArgs {
   const float* slot_leaf;
   const uint32_t* rows;
   uint32_t* rows_next;
+  const float2* pairs;       // gradient pairs in the order of `rows` (three-limb rounds)
+  float2* pairs_next;        // ... and of `rows_next`
+  const int4* limbs;         // two-limb values in the order of `rows` (staged rounds)
+  int4* limbs_next;          // ... and of `rows_next`
+  const float2* scale;       // the round's limb plan (as the histogram kernels make it)
+  const unsigned int* max_bits;
+  uint32_t min_limbs;
+  bool staged, unit_h;
   uint32_t* cursor_l;
   uint32_t* cursor_r;
   float* margins;
@@ -1387,19 +1463,26 @@ struct PartArgs {
 
 // Rows of every frontier node: nodes that stop add their leaf to the row's
 // margin, nodes split at the last level add the child leaf, other split nodes
-// scatter their rows to the two children (left block from the segment start,
-// right block from the segment end). Each thread takes 8 consecutive rows of
-// a 2048-row tile; one block-wide scan and one cursor reservation per tile.
+// move their rows, each with its gradient pair, to the two children (left
+// block from the segment start, right block from the segment end), so that
+// the next level reads both in row-list order. A warp owns 256 consecutive
+// rows of a 2048-row tile, lane-strided so that reads and writes coalesce;
+// ranks come from warp ballots, and one cursor reservation is made per tile.
 constexpr uint32_t kPartThreads = 256;
-constexpr uint32_t kPartPerThread = kTileRows / kPartThreads;
+constexpr uint32_t kPartWarps = kPartThreads / 32;
+constexpr uint32_t kPartIter = kTileRows / kPartThreads;  // rows per lane
 
 template <typename CodeT>
 __global__ void __launch_bounds__(kPartThreads) partition_kernel(PartArgs a) {
-  __shared__ uint32_t s_base[2];
+  __shared__ uint32_t s_off[kPartWarps][2];
   const DriverState st = *a.state;
   if (!st.frontier || st.error) return;
   const uint32_t n = st.frontier, ptiles = st.pad0;
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t lt_mask = (1u << lane) - 1u;
   const CodeT* __restrict__ codes = static_cast<const CodeT*>(a.e.codes);
+  LimbPlan pg, ph;
+  const bool two_limb = plan_round(a.scale, a.max_bits, a.min_limbs, a.staged, a.unit_h, pg, ph);
   for (uint32_t t = blockIdx.x; t < ptiles; t += gridDim.x) {
     uint32_t lo = 0, hi = n;
     while (hi - lo > 1) {
@@ -1414,17 +1497,19 @@ __global__ void __launch_bounds__(kPartThreads) partition_kernel(PartArgs a) {
     const uint32_t md = a.mode[s];
     const DevNode node = a.nodes[a.ids[s]];
     const float leaf_l = a.slot_leaf[2 * s], leaf_r = a.slot_leaf[2 * s + 1];
-    const uint32_t first = threadIdx.x * kPartPerThread;
-    uint32_t rows[kPartPerThread];
-    uint32_t left_mask = 0, nl = 0, nr = 0;
+    const uint32_t w0 = warp * (kTileRows / kPartWarps);
+    uint32_t rows[kPartIter];
+    uint32_t left_bits = 0, valid_bits = 0;
 #pragma unroll
-    for (uint32_t k = 0; k < kPartPerThread; ++k) {
-      const uint32_t i = first + k;
-      rows[k] = i < cnt ? (a.root ? begin + i : a.rows[begin + i]) : 0u;
+    for (uint32_t k = 0; k < kPartIter; ++k) {
+      const uint32_t i = w0 + k * 32 + lane;
+      const bool valid = i < cnt;
+      rows[k] = valid ? (a.root ? begin + i : a.rows[begin + i]) : 0u;
+      valid_bits |= uint32_t(valid) << k;
     }
 #pragma unroll
-    for (uint32_t k = 0; k < kPartPerThread; ++k) {
-      if (first + k >= cnt) continue;
+    for (uint32_t k = 0; k < kPartIter; ++k) {
+      if (!((valid_bits >> k) & 1u)) continue;
       const uint32_t row = rows[k];
       if (md == 0) {
         float* m = a.margins + size_t(row) * a.groups + a.group;
@@ -1437,26 +1522,56 @@ __global__ void __launch_bounds__(kPartThreads) partition_kernel(PartArgs a) {
         float* m = a.margins + size_t(row) * a.groups + a.group;
         *m = __fadd_rn(*m, left ? leaf_l : leaf_r);
       } else {
-        left_mask |= uint32_t(left) << k;
-        nl += left;
-        nr += !left;
+        left_bits |= uint32_t(left) << k;
       }
     }
     if (md != 1) continue;  // uniform across the block
-    uint32_t total;
-    const uint32_t off = block_exclusive_scan(nl | (nr << 16), &total);
-    if (threadIdx.x == 0) {
-      const uint32_t tl = total & 0xffffu, tr = total >> 16;
-      s_base[0] = tl ? atomicAdd(a.cursor_l + s, tl) : 0u;
-      s_base[1] = tr ? atomicSub(a.cursor_r + s, tr) - tr : 0u;
+    // Per-warp totals, then warp offsets within the tile and the tile's
+    // positions in the two child blocks.
+    uint32_t nl = 0, nr = 0;
+#pragma unroll
+    for (uint32_t k = 0; k < kPartIter; ++k) {
+      const bool valid = (valid_bits >> k) & 1u, left = (left_bits >> k) & 1u;
+      nl += __popc(__ballot_sync(0xffffffffu, valid && left));
+      nr += __popc(__ballot_sync(0xffffffffu, valid && !left));
+    }
+    if (lane == 0) {
+      s_off[warp][0] = nl;
+      s_off[warp][1] = nr;
     }
     __syncthreads();
-    uint32_t lpos = s_base[0] + (off & 0xffffu), rpos = s_base[1] + (off >> 16);
+    if (threadIdx.x == 0) {
+      uint32_t tl = 0, tr = 0;
+      for (uint32_t w = 0; w < kPartWarps; ++w) {
+        const uint32_t l = s_off[w][0], r = s_off[w][1];
+        s_off[w][0] = tl;
+        s_off[w][1] = tr;
+        tl += l;
+        tr += r;
+      }
+      const uint32_t lb = tl ? atomicAdd(a.cursor_l + s, tl) : 0u;
+      const uint32_t rb = tr ? atomicSub(a.cursor_r + s, tr) - tr : 0u;
+      for (uint32_t w = 0; w < kPartWarps; ++w) {
+        s_off[w][0] += lb;
+        s_off[w][1] += rb;
+      }
+    }
+    __syncthreads();
+    uint32_t lpos = s_off[warp][0], rpos = s_off[warp][1];
 #pragma unroll
-    for (uint32_t k = 0; k < kPartPerThread; ++k) {
-      if (first + k >= cnt) continue;
-      if ((left_mask >> k) & 1u) a.rows_next[lpos++] = rows[k];
-      else a.rows_next[rpos++] = rows[k];
+    for (uint32_t k = 0; k < kPartIter; ++k) {
+      const bool valid = (valid_bits >> k) & 1u, left = (left_bits >> k) & 1u;
+      const uint32_t bl = __ballot_sync(0xffffffffu, valid && left);
+      const uint32_t br = __ballot_sync(0xffffffffu, valid && !left);
+      if (valid) {
+        const uint32_t pos = left ? lpos + __popc(bl & lt_mask) : rpos + __popc(br & lt_mask);
+        a.rows_next[pos] = rows[k];
+        const uint32_t src = begin + w0 + k * 32 + lane;
+        if (two_limb) a.limbs_next[pos] = __ldg(a.limbs + src);
+        else a.pairs_next[pos] = __ldg(a.pairs + src);
+      }
+      lpos += __popc(bl);
+      rpos += __popc(br);
     }
     __syncthreads();
   }
@@ -1752,12 +1867,6 @@ HistConfig hist_config(const Ellpack& e, bool unit_hessian) {
   c.feature_group = kHistLanes;
   c.smem = size_t(unit_hessian ? 4 : 6) * (e.bins + 1) * kHistLanes * sizeof(int) +
            size_t(kHistWarps) * 32 * (sizeof(int4) + (unit_hessian ? 0 : sizeof(int2)));
-  // The staged two-limb path needs its fixed 257-slot planes and stage buffers.
-  const size_t staged = e.bytes_per_code == 1
-                            ? (unit_hessian ? hist2_smem<uint8_t, true>() : hist2_smem<uint8_t, false>())
-                            : (unit_hessian ? hist2_smem<uint16_t, true>() : hist2_smem<uint16_t, false>());
-  if (e.bins + 1 <= kSlots) c.smem = std::max(c.smem, staged);
-  c.top_ints = size_t(2) * kPlaneWords;
   c.threads = kHistWarps * 32;
   return c;
 }
@@ -1772,6 +1881,19 @@ void launch_hist_t(const HistArgs& args, int blocks, int threads, size_t smem, c
     configured = true;
   }
   kernel<<<blocks, threads, smem, stream>>>(args);
+  if (args.staged) {
+    // The staged kernel exits at once when the round needs three limbs (and
+    // the three-limb kernel exits when it does not); the choice is made on the
+    // device from the round's gradient magnitudes.
+    auto staged = hist2_kernel<CodeT, kUnit, kRoot>;
+    constexpr size_t smem2 = hist2_smem<CodeT, kUnit>();
+    static bool configured2 = false;
+    if (!configured2) {
+      XGBB_CUDA(cudaFuncSetAttribute(staged, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem2)));
+      configured2 = true;
+    }
+    staged<<<blocks, kH2Threads, smem2, stream>>>(args);
+  }
 }
 }  // namespace
 
@@ -1781,6 +1903,13 @@ void tree_init(const TreeWorkspace& ws, const TreeLaunch& tl, cudaStream_t strea
                                         ws.built_left, ws.keys[0], ws.nodes, ws.level_rows,
                                         ws.level_nodes);
   XGBB_CUDA(cudaGetLastError());
+  if (tl.ell.bins + 1 <= kSlots && tl.ell.rows) {
+    // Root limbs for a staged round (the kernel exits when the round needs
+    // three limbs).
+    limbs_kernel<<<grid_for(tl.ell.rows, 256, 148 * 8), 256, 0, stream>>>(
+        tl.pairs, tl.ell.rows, tl.scale, tl.max_bits, tl.min_limbs, true, tl.unit_hessian, ws.limbs_root);
+    XGBB_CUDA(cudaGetLastError());
+  }
 }
 
 void tree_level_hist(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t depth,
@@ -1789,7 +1918,8 @@ void tree_level_hist(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t dep
   XGBB_CUDA(cudaMemsetAsync(ws.built, 0, bytes, stream));
   HistArgs a;
   a.e = tl.ell;
-  a.pairs = tl.pairs;
+  a.pairs = depth == 0 ? tl.pairs : static_cast<const float2*>(ws.ord[depth & 1]);
+  a.limbs = depth == 0 ? ws.limbs_root : static_cast<const int4*>(ws.ord[depth & 1]);
   a.scale = tl.scale;
   a.rows = ws.rows[depth & 1];
   a.state = ws.state;
@@ -1798,7 +1928,7 @@ void tree_level_hist(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t dep
   a.seg_begin = ws.seg_begin[depth & 1];
   a.seg_count = ws.seg_count[depth & 1];
   a.built = ws.built;
-  a.top = tl.ell.bins + 1 <= kSlots ? ws.hist_top : nullptr;
+  a.staged = tl.ell.bins + 1 <= kSlots;
   a.max_bits = tl.max_bits;
   a.min_limbs = tl.min_limbs;
   a.ngroups = (tl.ell.cols + kHistLanes - 1) / kHistLanes;
@@ -1893,6 +2023,15 @@ void tree_level_partition(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_
   a.slot_leaf = ws.slot_leaf;
   a.rows = ws.rows[depth & 1];
   a.rows_next = ws.rows[(depth + 1) & 1];
+  a.pairs = depth == 0 ? tl.pairs : static_cast<const float2*>(ws.ord[depth & 1]);
+  a.pairs_next = static_cast<float2*>(ws.ord[(depth + 1) & 1]);
+  a.limbs = depth == 0 ? ws.limbs_root : static_cast<const int4*>(ws.ord[depth & 1]);
+  a.limbs_next = static_cast<int4*>(ws.ord[(depth + 1) & 1]);
+  a.scale = tl.scale;
+  a.max_bits = tl.max_bits;
+  a.min_limbs = tl.min_limbs;
+  a.staged = tl.ell.bins + 1 <= kSlots;
+  a.unit_h = tl.unit_hessian;
   a.cursor_l = ws.cursor_l;
   a.cursor_r = ws.cursor_r;
   a.margins = tl.margins;

@@ -66,7 +66,9 @@ struct TreeWorkspace {
   longlong2* built;          // [pairs][cols][bins + 1]
   longlong2* bank[2];        // [slots][cols][bins + 1]
   uint32_t* rows[2];         // row ids per level (level 0 uses the identity)
-  int* hist_top;             // [hist CTAs][HistConfig::top_ints] carry scratch
+  void* ord[2];              // per row of rows[] (level >= 1): float2 gradient pair
+                             // (three-limb rounds) or int4 limbs (staged rounds)
+  int4* limbs_root;          // int4 limbs in row order (level 0 of staged rounds)
   uint32_t node_capacity;
   unsigned long long* level_rows;  // [kMaxDepth] rows in built nodes per level
   uint32_t* level_nodes;           // [kMaxDepth] built nodes per level
@@ -122,7 +124,6 @@ struct HistConfig {
   uint32_t feature_group;
   size_t smem;
   int threads;
-  size_t top_ints;  // per-CTA carry scratch of the staged path (ints)
 };
 HistConfig hist_config(const Ellpack& ell, bool unit_hessian);
 
