@@ -105,6 +105,20 @@ void DMatrix::set_cuts(std::shared_ptr<Cuts> c, cudaStream_t stream) {
                     ell.bytes_per_code, ell.missing, stream);
   }
   ell.codes = codes.get();
+  // A feature-major copy lets the partition read a node's split feature from
+  // a dense column; it is made when it leaves a quarter of the device free.
+  codes_fm.release();
+  ell.codes_fm = nullptr;
+  if (rows && cols) {
+    const size_t fm_bytes = size_t(rows) * cols * ell.bytes_per_code;
+    size_t free_b = 0, total_b = 0;
+    if (cudaMemGetInfo(&free_b, &total_b) == cudaSuccess && fm_bytes + total_b / 4 <= free_b) {
+      codes_fm.resize(fm_bytes);
+      launch_transpose_codes(codes.get(), rows, cols, ell.stride, ell.bytes_per_code, codes_fm.get(),
+                             stream);
+      ell.codes_fm = codes_fm.get();
+    }
+  }
   cuts = std::move(c);
 }
 
@@ -477,6 +491,30 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp) {
   return *state_;
 }
 
+namespace {
+// The device's choice of histogram kernel for group g's tree, restated on the
+// host for the profile: two limbs when every |q| of the round has at most 42
+// bits (the staged kernel), three otherwise.
+bool staged_round(const unsigned int* max_bits, const float2* scales, uint32_t g, const Ellpack& e,
+                  bool unit_h, uint32_t min_limbs) {
+  if (e.bins + 1 > 257 || min_limbs >= 3) return false;
+  unsigned int bits[2];
+  float2 scale;
+  XGBB_CUDA(cudaMemcpy(bits, max_bits + 2 * g, sizeof bits, cudaMemcpyDeviceToHost));
+  XGBB_CUDA(cudaMemcpy(&scale, scales + g, sizeof scale, cudaMemcpyDeviceToHost));
+  auto two_limbs = [](unsigned int b, float sc) {
+    float mv;
+    const unsigned int m = b & 0x7fffffffu;
+    std::memcpy(&mv, &m, 4);
+    const long long q = std::llrint(mv * sc);
+    const unsigned long long a = (unsigned long long)(q < 0 ? -q : q);
+    const int bl = a ? 64 - __builtin_clzll(a) : 0;
+    return bl <= 42;
+  };
+  return two_limbs(bits[0], scale.x) && (unit_h || two_limbs(bits[1], scale.y));
+}
+}  // namespace
+
 void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s, bool capturing) {
   // Inside a capture the profiling events become external event-record nodes,
   // recorded again at every launch of the graph.
@@ -601,9 +639,16 @@ void Booster::run_round(TrainState& ts) {
     // int64 histogram written.
     const uint32_t D = tp_.max_depth;
     const Ellpack& e = d.ell;
-    const double row_bytes = double(e.cols) * e.bytes_per_code + 8.0;
     const double node_bytes = double(hist_node_bytes(e));
-    for (uint32_t g = 0; g < G; ++g)
+    const bool unit_h = objective_ == kSquaredError && d.weights.empty();
+    const uint32_t min_limbs = uint32_t(integer(params_, "cuda_hist_limbs", 0));
+    for (uint32_t g = 0; g < G; ++g) {
+      // Per row the histogram reads its codes, its gradient values (the
+      // int64-exact two-limb values, 16 bytes, on the staged path; the float
+      // pair, 8 bytes, on the three-limb path) and below the root its row id.
+      const bool staged = staged_round(mass_view(ts.mass.get(), ts.groups).max_bits,
+                                       ts.scales.as<float2>(), g, e, unit_h, min_limbs);
+      const double row_bytes = double(e.cols) * e.bytes_per_code + (staged ? 16.0 : 8.0);
       for (uint32_t depth = 0; depth < D; ++depth) {
         float ms = 0;
         XGBB_CUDA(cudaEventElapsedTime(&ms, ts.events[(size_t(g) * D + depth) * 2],
@@ -618,6 +663,7 @@ void Booster::run_round(TrainState& ts) {
         profile.level_rows[depth] += rows;
         profile.level_nodes[depth] += nodes;
       }
+    }
   }
   ++profile.rounds;
   ++rounds_;

@@ -72,6 +72,7 @@ class DMatrix {
   // Quantised form.
   std::shared_ptr<Cuts> cuts;
   DeviceBuffer codes;
+  DeviceBuffer codes_fm;  // feature-major copy for the partition, when memory allows
   Ellpack ell;
   uint32_t max_bin = 0;
   bool quantised() const { return bool(cuts) && (codes || rows == 0); }

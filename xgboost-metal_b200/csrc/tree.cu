@@ -96,6 +96,31 @@ __global__ void quantize_kernel(const float* __restrict__ X, uint32_t rows, uint
   }
 }
 
+// Feature-major copy of the codes, [cols][rows], for the partition: the rows
+// of a node then read their split feature from a dense column (64x64 tiles
+// through shared memory, both sides coalesced).
+template <typename CodeT>
+__global__ void __launch_bounds__(256) transpose_codes_kernel(const CodeT* __restrict__ codes, uint32_t rows,
+                                                              uint32_t cols, uint32_t stride,
+                                                              CodeT* __restrict__ fm) {
+  __shared__ CodeT tile[64][65];
+  const uint32_t ctiles = (cols + 63) / 64;
+  const uint64_t tiles = uint64_t((rows + 63) / 64) * ctiles;
+  for (uint64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const uint32_t r0 = uint32_t(t / ctiles) * 64, c0 = uint32_t(t % ctiles) * 64;
+    for (uint32_t i = threadIdx.x; i < 64 * 64; i += blockDim.x) {
+      const uint32_t r = i / 64, c = i % 64;
+      if (r0 + r < rows && c0 + c < cols) tile[r][c] = codes[size_t(r0 + r) * stride + c0 + c];
+    }
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < 64 * 64; i += blockDim.x) {
+      const uint32_t c = i / 64, r = i % 64;
+      if (r0 + r < rows && c0 + c < cols) fm[size_t(c0 + c) * rows + r0 + r] = tile[r][c];
+    }
+    __syncthreads();
+  }
+}
+
 __global__ void validate_kernel(const float4* __restrict__ X4, const float* __restrict__ X,
                                 uint64_t n, unsigned int* flags) {
   unsigned int nan = 0, inf = 0;
@@ -1481,6 +1506,7 @@ __global__ void __launch_bounds__(kPartThreads) partition_kernel(PartArgs a) {
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t lt_mask = (1u << lane) - 1u;
   const CodeT* __restrict__ codes = static_cast<const CodeT*>(a.e.codes);
+  const CodeT* __restrict__ fm = static_cast<const CodeT*>(a.e.codes_fm);
   LimbPlan pg, ph;
   const bool two_limb = plan_round(a.scale, a.max_bits, a.min_limbs, a.staged, a.unit_h, pg, ph);
   for (uint32_t t = blockIdx.x; t < ptiles; t += gridDim.x) {
@@ -1516,7 +1542,8 @@ __global__ void __launch_bounds__(kPartThreads) partition_kernel(PartArgs a) {
         *m = __fadd_rn(*m, leaf_l);
         continue;
       }
-      const uint32_t code = codes[size_t(row) * a.e.stride + uint32_t(node.feature)];
+      const uint32_t code = fm ? fm[size_t(node.feature) * a.e.rows + row]
+                               : codes[size_t(row) * a.e.stride + uint32_t(node.feature)];
       const bool left = code == a.e.missing ? node.default_left != 0u : int32_t(code) <= node.split_bin;
       if (md == 2) {
         float* m = a.margins + size_t(row) * a.groups + a.group;
@@ -1779,6 +1806,20 @@ void launch_window_to_limbs(MassAccum m, uint32_t groups, cudaStream_t stream) {
 
 void launch_limbs_to_window(MassAccum m, uint32_t groups, cudaStream_t stream) {
   limbs_to_window_kernel<<<1, 64 * ((2 * groups + 63) / 64), 0, stream>>>(m, 2 * groups);
+  XGBB_CUDA(cudaGetLastError());
+}
+
+void launch_transpose_codes(const void* codes, uint32_t rows, uint32_t cols, uint32_t stride,
+                            uint32_t bytes_per_code, void* fm, cudaStream_t stream) {
+  const uint64_t tiles = uint64_t((rows + 63) / 64) * ((cols + 63) / 64);
+  if (!tiles) return;
+  const int blocks = grid_for(tiles, 1, 148 * 16);
+  if (bytes_per_code == 1)
+    transpose_codes_kernel<uint8_t><<<blocks, 256, 0, stream>>>(
+        static_cast<const uint8_t*>(codes), rows, cols, stride, static_cast<uint8_t*>(fm));
+  else
+    transpose_codes_kernel<uint16_t><<<blocks, 256, 0, stream>>>(
+        static_cast<const uint16_t*>(codes), rows, cols, stride, static_cast<uint16_t*>(fm));
   XGBB_CUDA(cudaGetLastError());
 }
 

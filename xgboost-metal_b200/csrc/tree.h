@@ -16,6 +16,7 @@ namespace xgbb {
 // bytes).
 struct Ellpack {
   const void* codes = nullptr;
+  const void* codes_fm = nullptr;           // optional feature-major copy [cols][rows]
   uint32_t rows = 0, cols = 0, stride = 0;  // stride in codes
   uint32_t bytes_per_code = 1;              // 1 or 2
   uint32_t missing = 0xff;
@@ -90,6 +91,8 @@ struct TreeLaunch {
 };
 
 // Launch helpers (tree.cu). All are asynchronous on `stream`.
+void launch_transpose_codes(const void* codes, uint32_t rows, uint32_t cols, uint32_t stride,
+                            uint32_t bytes_per_code, void* fm, cudaStream_t stream);
 void launch_quantize(const float* X, uint32_t rows, uint32_t cols, const float* cuts,
                      const uint32_t* counts, uint32_t bins, void* codes, uint32_t stride,
                      uint32_t bytes_per_code, uint32_t missing, cudaStream_t stream);
