@@ -38,6 +38,10 @@ WORKLOADS = {
                eta=0.3, labels="linear"),
     "c0": dict(rows=100_000, cols=32, nan=0.0, objective="reg:squarederror", max_depth=6,
                eta=0.3, labels="linear"),
+    # 10-class softprob on integer-valued images (<= 256 distinct
+    # values per feature, ~80 % zeros, no missing), a synthetic stand-in.
+    "c3": dict(rows=1_000_000, cols=784, nan=0.0, objective="multi:softprob", max_depth=6,
+               eta=0.3, labels="classes", num_class=10),
 }
 CHUNK = 1_000_000
 
@@ -49,6 +53,26 @@ def log(*a):
 # ---------------------------------------------------------------------------
 # Synthetic data (GPU, seeded per chunk)
 # ---------------------------------------------------------------------------
+def gen_classes_chunk(spec, begin, n, device):
+    """Rows of the class-pattern workload: class patterns P[k] ~ U(0, 255) per
+    pixel (seed 7), cells below the 80th percentile of P[k] are 0, the rest
+    clip(Poisson(P[k]), 0, 255); row i has class (i mod K) under a fixed
+    shuffle (seed 8)."""
+    import torch
+    K, cols, rows = spec["num_class"], spec["cols"], spec["rows"]
+    P = np.random.default_rng(7).uniform(0, 255, size=(K, cols)).astype(np.float32)
+    thr = np.quantile(P, 0.8, axis=1, keepdims=True).astype(np.float32)
+    labels = (np.arange(rows) % K)[np.random.default_rng(8).permutation(rows)][begin:begin + n]
+    Pd = torch.from_numpy(P).to(device)
+    keep = torch.from_numpy(P >= thr).to(device)
+    lab = torch.from_numpy(labels.astype(np.int64)).to(device)
+    g = torch.Generator(device=device)
+    g.manual_seed(1341 * 1000003 + begin // CHUNK)
+    X = torch.poisson(Pd[lab], generator=g).clamp_(0, 255)
+    X = torch.where(keep[lab], X, torch.zeros_like(X))
+    return X, lab.float()
+
+
 def gen_chunk(wl, c, device):
     """Rows [c*CHUNK, min((c+1)*CHUNK, rows)) of workload `wl`, on the GPU."""
     import torch
@@ -56,6 +80,8 @@ def gen_chunk(wl, c, device):
     begin = c * CHUNK
     n = min(CHUNK, spec["rows"] - begin)
     cols = spec["cols"]
+    if spec["labels"] == "classes":
+        return gen_classes_chunk(spec, begin, n, device)
     g = torch.Generator(device=device)
     g.manual_seed(1337 * 1000003 + c)
     X = torch.randn(n, cols, generator=g, device=device, dtype=torch.float32)
@@ -96,9 +122,16 @@ def gen_rows(wl, begin, end, device, pin=True):
 
 def params_for(wl):
     s = WORKLOADS[wl]
-    return {"objective": s["objective"], "max_depth": s["max_depth"], "eta": s["eta"],
-            "max_bin": 256, "tree_method": "hist", "device": "cuda", "seed": 42,
-            "reg_lambda": 1.0}
+    p = {"objective": s["objective"], "max_depth": s["max_depth"], "eta": s["eta"],
+         "max_bin": 256, "tree_method": "hist", "device": "cuda", "seed": 42,
+         "reg_lambda": 1.0}
+    if "num_class" in s:
+        p["num_class"] = s["num_class"]
+    return p
+
+
+def groups_of(wl):
+    return int(WORKLOADS[wl].get("num_class", 1))
 
 
 # ---------------------------------------------------------------------------
@@ -227,9 +260,12 @@ def _fit_to_full(samples, full_rows):
 
 
 def _sample_sizes(wl):
-    rows = WORKLOADS[wl]["rows"]
+    spec = WORKLOADS[wl]
+    rows = spec["rows"]
     if rows <= 300_000:
         return [rows]
+    if spec["cols"] * spec.get("num_class", 1) > 1000:
+        return [4_000, 16_000]   # wide multi-class rows: keep the CPU sample to seconds
     return [25_000, 100_000]
 
 
@@ -239,8 +275,9 @@ def cpu_oracle_baseline(wl, device):
     evaluated at the workload's rows."""
     import checkers as C
     spec = WORKLOADS[wl]
+    extra = {"num_class": spec["num_class"]} if "num_class" in spec else {}
     p = C.train_params(dict(objective=spec["objective"], max_depth=spec["max_depth"],
-                            eta=spec["eta"]))
+                            eta=spec["eta"], **extra))
     samples = []
     for rows in _sample_sizes(wl):
         X, y = gen_rows(wl, 0, rows, device, pin=False)
@@ -268,13 +305,15 @@ def reference_arm(args, wl, device):
     kind = "reference" if C.have_reference() else "port"
     chk = C.reference() if kind == "reference" else C.oracle()
     o = C.oracle()
-    sizes = _sample_sizes(wl) if spec["rows"] <= 300_000 else [10_000, 40_000]
+    sizes = _sample_sizes(wl) if spec["rows"] <= 300_000 else (
+        [2_000, 8_000] if spec["cols"] * spec.get("num_class", 1) > 1000 else [10_000, 40_000])
     setups = []
     for rows in sizes:
         X, y = gen_rows(wl, 0, rows, device, pin=False)
         cuts, counts, minima = o.sketch_cuts(X, 256)
         setups.append(dict(rows=rows, y=y, bins=o.quantize(X, cuts, counts), cuts=cuts,
-                           counts=counts, minima=minima, margins=np.zeros((rows, 1), np.float32)))
+                           counts=counts, minima=minima,
+                           margins=np.zeros((rows, groups_of(wl)), np.float32)))
     tp = dict(max_depth=spec["max_depth"], eta=spec["eta"], reg_lambda=1.0, reg_alpha=0.0,
               min_child_weight=1.0, max_delta_step=0.0, min_split_loss=0.0)
     samples = []
@@ -283,9 +322,11 @@ def reference_arm(args, wl, device):
         t = time.perf_counter()
         pairs = C.oracle_gradients(spec["objective"], st["margins"], st["y"])
         scale = chk.gradient_scales(pairs)
-        q = chk.quantize_gradients(pairs, scale)[:, 0, :]
-        _, leaf = chk.grow_tree(st["bins"], q, scale[0], st["cuts"], st["counts"], st["minima"], tp)
-        st["margins"][:, 0] += leaf
+        q_all = chk.quantize_gradients(pairs, scale)
+        for grp in range(groups_of(wl)):   # one tree per class
+            _, leaf = chk.grow_tree(st["bins"], q_all[:, grp, :], scale[grp], st["cuts"], st["counts"],
+                                    st["minima"], tp)
+            st["margins"][:, grp] += leaf
         if step >= args.warmup:
             samples.append((st["rows"], time.perf_counter() - t))
     per_round = _fit_to_full(samples, spec["rows"])
@@ -376,7 +417,7 @@ def main():
     log("rank %d: rows [%d, %d) generated in %.1fs" % (dist.rank, begin, end, time.perf_counter() - t))
     params = params_for(wl)
     K, W = args.steps, args.warmup
-    groups = 1
+    groups = groups_of(wl)
 
     # End to end: host buffers in, quantisation (H2D + binning) and K rounds
     # through the public API; every round reads its trees back to the host.

@@ -705,8 +705,12 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
+// Shared-memory add without a compiler memory barrier: the accumulation
+// loop's loads read the stage buffers, which these adds never touch, so the
+// compiler may hoist the next rows' loads above them. Every other access to
+// the planes is separated from the adds by a CTA barrier.
 __device__ __forceinline__ void red_shared(uint32_t addr, int v) {
-  asm volatile("red.shared.add.s32 [%0], %1;\n" ::"r"(addr), "r"(v) : "memory");
+  asm volatile("red.shared.add.s32 [%0], %1;\n" ::"r"(addr), "r"(v));
 }
 
 // Limb plans of a round; the staged kernel takes the rounds whose values all
