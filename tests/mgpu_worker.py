@@ -17,9 +17,9 @@ import xgboost as xgb  # noqa: E402
 from xgboost import core  # noqa: E402
 
 
-def data(objective):
+def data(objective, c=12):
     rng = np.random.default_rng(2026)
-    n, c = 30000, 12
+    n = 30000
     X = rng.normal(size=(n, c)).astype(np.float32)
     X[rng.random(X.shape) < 0.08] = np.nan
     z = np.nan_to_num(X) @ rng.normal(size=c)
@@ -34,6 +34,7 @@ def main():
     import faulthandler
     faulthandler.dump_traceback_later(int(os.environ.get("XGBB_WORKER_TIMEOUT", "240")), exit=True)
     out_dir, objective = sys.argv[1], sys.argv[2]
+    cols = int(sys.argv[3]) if len(sys.argv) > 3 else 12
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
@@ -42,7 +43,7 @@ def main():
     box = [xgb.collective.nccl_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(box, src=0)
     xgb.collective.init(rank=rank, world_size=world, nccl_unique_id=box[0], device=local)
-    X, y = data(objective)
+    X, y = data(objective, cols)
     lo, hi = len(y) * rank // world, len(y) * (rank + 1) // world
     ref = xgb.QuantileDMatrix(X, max_bin=64)
     shard = xgb.QuantileDMatrix(X[lo:hi], label=y[lo:hi], ref=ref, max_bin=64)

@@ -24,18 +24,20 @@ def gpu_count():
 
 
 @pytest.mark.skipif(gpu_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("objective", ["reg:squarederror", "binary:logistic"])
-def test_two_ranks_match_the_oracle(tmp_path, objective):
+@pytest.mark.parametrize("objective,cols", [("reg:squarederror", 12), ("binary:logistic", 13)])
+def test_two_ranks_match_the_oracle(tmp_path, objective, cols):
+    """13 features over 2 ranks: the padded feature of the reduce-scatter
+    layout and an uneven split of the split search."""
     sys.path.insert(0, HERE)
     import mgpu_worker
     # One node: NCCL's bootstrap sockets on loopback, no NVLink multicast.
     env = dict(os.environ, MASTER_ADDR="127.0.0.1", NCCL_NVLS_ENABLE="0", NCCL_SOCKET_IFNAME="lo")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
            "--master-addr=127.0.0.1", "--master-port=29533",
-           os.path.join(HERE, "mgpu_worker.py"), str(tmp_path), objective]
+           os.path.join(HERE, "mgpu_worker.py"), str(tmp_path), objective, str(cols)]
     proc = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=420)
     assert proc.returncode == 0, proc.stderr[-3000:]
-    X, y = mgpu_worker.data(objective)
+    X, y = mgpu_worker.data(objective, cols)
     params = C.train_params(dict(objective=objective, max_depth=6, eta=0.3, max_bin=64))
     _, margins, _ = C.oracle_train(X, y, params, 6)
     for r in range(2):

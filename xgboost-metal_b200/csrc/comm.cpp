@@ -27,6 +27,9 @@ struct NcclApi {
                              cudaStream_t) = nullptr;
   ncclResult_t (*broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t,
                             cudaStream_t) = nullptr;
+  ncclResult_t (*reduce_scatter)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                                 cudaStream_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
 };
 
@@ -52,6 +55,8 @@ const NcclApi& nccl() {
     api.destroy = reinterpret_cast<decltype(api.destroy)>(sym("ncclCommDestroy"));
     api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(sym("ncclAllReduce"));
     api.broadcast = reinterpret_cast<decltype(api.broadcast)>(sym("ncclBroadcast"));
+    api.reduce_scatter = reinterpret_cast<decltype(api.reduce_scatter)>(sym("ncclReduceScatter"));
+    api.all_gather = reinterpret_cast<decltype(api.all_gather)>(sym("ncclAllGather"));
     api.error_string = reinterpret_cast<decltype(api.error_string)>(sym("ncclGetErrorString"));
   });
   require(failure.empty(), failure);
@@ -154,6 +159,17 @@ void Comm::broadcast(void* buf, size_t bytes, int root, cudaStream_t s) {
   if (!active() || !bytes) return;
   trace(rank_, "broadcast", bytes);
   XGBB_NCCL(nccl().broadcast(buf, buf, bytes, ncclUint8, root, as_comm(comm_), s));
+}
+void Comm::reduce_scatter_u64(void* buf, size_t count, cudaStream_t s) {
+  if (!active() || !count) return;
+  trace(rank_, "reduce_scatter_u64", count);
+  auto* b = static_cast<unsigned long long*>(buf);
+  XGBB_NCCL(nccl().reduce_scatter(b, b + size_t(rank_) * count, count, ncclUint64, ncclSum, as_comm(comm_), s));
+}
+void Comm::all_gather(const void* send, void* recv, size_t bytes, cudaStream_t s) {
+  if (!active() || !bytes) return;
+  trace(rank_, "all_gather", bytes);
+  XGBB_NCCL(nccl().all_gather(send, recv, bytes, ncclUint8, as_comm(comm_), s));
 }
 void Comm::barrier(cudaStream_t s) {
   if (!active()) return;

@@ -28,6 +28,11 @@ class Comm {
   void max_u32(void* buf, size_t count, cudaStream_t s);
   void sum_f64(void* buf, size_t count, cudaStream_t s);
   void broadcast(void* buf, size_t bytes, int root, cudaStream_t s);
+  // In-place reduce-scatter of uint64 sums: `buf` holds world() chunks of
+  // `count` words; this rank's chunk (at rank() * count) receives the sums.
+  void reduce_scatter_u64(void* buf, size_t count, cudaStream_t s);
+  // `bytes` from every rank, concatenated in rank order into `recv`.
+  void all_gather(const void* send, void* recv, size_t bytes, cudaStream_t s);
   void barrier(cudaStream_t s);
   // Work that must be released before the communicator is destroyed: CUDA
   // graphs holding NCCL calls would otherwise keep ncclCommDestroy waiting.

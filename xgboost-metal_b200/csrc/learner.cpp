@@ -154,7 +154,8 @@ struct Booster::TrainState {
   DMatrix* d = nullptr;
   uint32_t rows = 0, groups = 1, margin_rounds = 0;
   unsigned long long rows_total = 0;  // rows over all ranks
-  DeviceBuffer margins, pairs, mass, scales;
+  DeviceBuffer margins, pairs, mass, scales, best_mine, best_all;
+  uint32_t cols_pad = 0;
   DeviceBuffer state, ids[2], sums[2], seg_begin[2], seg_count[2], parent_slot, built_left,
       tile_offset, ptile_offset, cursor_l, cursor_r, counts_local, counts_global, mode, slot_leaf,
       keys[2], cand, nodes, built, bank[2], rows_buf[2], level_rows, level_nodes, ord[2], limbs_root;
@@ -419,7 +420,16 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp) {
   ts->cand.resize(size_t(max_slots) * C * sizeof(DevSplit));
   ts->capacity = (2u << D) - 1;
   ts->nodes.resize(size_t(ts->capacity) * sizeof(DevNode));
-  ts->built.resize(size_t(max_pairs_at(D - 1)) * node_bytes);
+  // The built histograms are feature-major, [cols_pad][pairs][bins + 1], with
+  // the features padded to a multiple of the ranks so that a reduce-scatter
+  // hands every rank whole features.
+  const uint32_t world = uint32_t(Comm::get().world());
+  ts->cols_pad = (C + world - 1) / world * world;
+  ts->built.resize(size_t(max_pairs_at(D - 1)) * hist_node_bytes(e, ts->cols_pad));
+  if (world > 1) {
+    ts->best_mine.resize(size_t(kMaxFrontier) * best_record_bytes());
+    ts->best_all.resize(size_t(world) * kMaxFrontier * best_record_bytes());
+  }
   const uint32_t bank_slots = D >= 2 ? max_slots_at(D - 2) : 1u;
   ts->bank[0].resize(size_t(bank_slots) * node_bytes);
   ts->bank[1].resize(size_t(bank_slots) * node_bytes);
@@ -545,14 +555,26 @@ void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s, b
   tl.part_blocks = sms * 8;
   const TreeWorkspace& ws = ts.ws;
   const uint32_t D = tp_.max_depth;
-  const size_t node_bytes = hist_node_bytes(d.ell);
+  // Each rank evaluates the splits of its own feature range; one GPU evaluates
+  // them all.
+  const uint32_t world = uint32_t(comm.world()), rank = uint32_t(comm.rank());
+  tl.cols_pad = ts.cols_pad;
+  const uint32_t per_rank = ts.cols_pad / world;
+  tl.f_lo = std::min(rank * per_rank, d.ell.cols);
+  tl.f_hi = std::min((rank + 1) * per_rank, d.ell.cols);
   tree_init(ws, tl, s);
   for (uint32_t depth = 0; depth < D; ++depth) {
     if (profiling) mark(ts.events[(size_t(g) * D + depth) * 2]);
     tree_level_hist(ws, tl, depth, s);
     if (profiling) mark(ts.events[(size_t(g) * D + depth) * 2 + 1]);
-    comm.sum_u64(ws.built, size_t(max_pairs_at(depth)) * node_bytes / 8, s);
+    // Sum the built histograms over ranks, each rank receiving its features.
+    comm.reduce_scatter_u64(ws.built, size_t(per_rank) * max_pairs_at(depth) * (d.ell.bins + 1) * 2, s);
     tree_level_eval(ws, tl, depth, s);
+    if (comm.active()) {
+      tree_level_pack_best(ws, tl, depth, ts.best_mine.get(), s);
+      comm.all_gather(ts.best_mine.get(), ts.best_all.get(), size_t(kMaxFrontier) * best_record_bytes(), s);
+      tree_level_merge_best(ws, tl, depth, ts.best_all.get(), world, s);
+    }
     tree_level_control(ws, tl, depth, s);
     tree_level_partition(ws, tl, depth, s);
     if (depth + 1 < D) {

@@ -405,7 +405,8 @@ struct HistArgs {
   const uint32_t* built_left;
   const uint32_t* seg_begin;
   const uint32_t* seg_count;
-  longlong2* built;
+  longlong2* built;      // [cols_pad][pair_stride][bins + 1]
+  uint32_t pair_stride;  // pairs of this level in the built layout
   bool staged;         // the staged two-limb kernel may take this level (bins + 1 <= 257)
   uint32_t ngroups;
   uint32_t min_limbs;  // 3 forces three-limb accumulation (tuning; results unchanged)
@@ -543,7 +544,7 @@ __device__ __forceinline__ void hist_body(const HistArgs& a, int* smem, const Dr
       else h = combine_limbs(lh + i, plane, Lh);
       const bool any = kUnitH ? (g != 0 || lh[i] != 0) : (g != 0 || h != 0);
       if (any && f < C) {
-        longlong2* dst = a.built + (size_t(pair) * C + f) * B1 + bin;
+        longlong2* dst = a.built + (size_t(f) * a.pair_stride + pair) * B1 + bin;
         atomicAdd(reinterpret_cast<unsigned long long*>(&dst->x), (unsigned long long)g);
         atomicAdd(reinterpret_cast<unsigned long long*>(&dst->y), (unsigned long long)h);
       }
@@ -1000,7 +1001,7 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
             any = g != 0 || h != 0;
           }
           if (any && f < C) {
-            longlong2* dst = a.built + (size_t(pair) * C + f) * B1 + bin;
+            longlong2* dst = a.built + (size_t(f) * a.pair_stride + pair) * B1 + bin;
             atomicAdd(reinterpret_cast<unsigned long long*>(&dst->x), (unsigned long long)g);
             atomicAdd(reinterpret_cast<unsigned long long*>(&dst->y), (unsigned long long)h);
           }
@@ -1096,7 +1097,9 @@ struct EvalArgs {
   const float2* scale;
   const DriverState* state;
   uint32_t depth;
-  const longlong2* built;
+  const longlong2* built;    // [cols_pad][pair_stride][bins + 1]
+  uint32_t pair_stride;
+  uint32_t f_lo, f_hi;       // features this rank evaluates
   const longlong2* prev_bank;
   longlong2* bank;
   const uint32_t* parent_slot;
@@ -1125,7 +1128,8 @@ __global__ void __launch_bounds__(256) eval_kernel(EvalArgs a) {
   const uint32_t lane = threadIdx.x & 31;
   const uint32_t nslots = a.state->frontier;
   const uint32_t C = a.e.cols, B = a.e.bins, B1 = B + 1;
-  const uint64_t total = uint64_t(nslots) * C;
+  const uint32_t nf = a.f_hi > a.f_lo ? a.f_hi - a.f_lo : 0u;
+  const uint64_t total = uint64_t(nslots) * nf;
   const uint64_t nwarps = uint64_t(gridDim.x) * (blockDim.x >> 5);
   const float2 sc = *a.scale;
   int eg, eh;
@@ -1133,7 +1137,7 @@ __global__ void __launch_bounds__(256) eval_kernel(EvalArgs a) {
   frexpf(sc.y, &eh);
   const double inv_g = ldexp(1.0, -(eg - 1)), inv_h = ldexp(1.0, -(eh - 1));
   for (uint64_t w = blockIdx.x * uint64_t(blockDim.x >> 5) + (threadIdx.x >> 5); w < total; w += nwarps) {
-    const uint32_t slot = uint32_t(w / C), f = uint32_t(w % C);
+    const uint32_t slot = uint32_t(w / nf), f = a.f_lo + uint32_t(w % nf);
     const longlong2* bptr;
     const longlong2* pptr = nullptr;
     if (a.depth == 0) {
@@ -1141,7 +1145,7 @@ __global__ void __launch_bounds__(256) eval_kernel(EvalArgs a) {
     } else {
       const uint32_t p = slot >> 1;
       const uint32_t built_side = a.built_left[p] ? 0u : 1u;
-      bptr = a.built + (size_t(p) * C + f) * B1;
+      bptr = a.built + (size_t(f) * a.pair_stride + p) * B1;
       if ((slot & 1u) != built_side) pptr = a.prev_bank + (size_t(a.parent_slot[p]) * C + f) * B1;
     }
     // Lane `lane` holds bins [8 lane, 8 lane + 8).
@@ -1460,6 +1464,46 @@ __global__ void __launch_bounds__(1024) control_kernel(ControlArgs a) {
       a.state->pad1 = terminal ? 0u : 2u * total_expand;  // next frontier
     }
     a.ptile_offset[n] = total_tiles;
+  }
+}
+
+// Distributed split search: every rank evaluates its own feature range, then
+// the best candidate of each slot (key + record) is gathered from all ranks
+// and the overall best written where control_kernel reads it, so every rank
+// selects the same split as one GPU evaluating every feature would.
+struct BestRecord {
+  unsigned long long key;
+  DevSplit split;
+};
+
+__global__ void pack_best_kernel(const unsigned long long* keys, const DevSplit* cand, uint32_t cols,
+                                 BestRecord* out) {
+  for (uint32_t s = threadIdx.x; s < kMaxFrontier; s += blockDim.x) {
+    BestRecord r;
+    r.key = keys[s];
+    const uint32_t f = 0xffffffffu - uint32_t(r.key & 0xffffffffu);
+    if (r.key && f < cols) r.split = cand[size_t(s) * cols + f];
+    else r = BestRecord{};
+    out[s] = r;
+  }
+}
+
+__global__ void merge_best_kernel(const DriverState* state, const BestRecord* all, uint32_t ranks,
+                                  uint32_t cols, unsigned long long* keys, DevSplit* cand) {
+  const uint32_t n = state->frontier;
+  for (uint32_t s = threadIdx.x; s < n; s += blockDim.x) {
+    uint32_t best = 0;
+    unsigned long long key = all[s].key;
+    for (uint32_t r = 1; r < ranks; ++r) {
+      const unsigned long long k = all[size_t(r) * kMaxFrontier + s].key;
+      if (k > key) {
+        key = k;
+        best = r;
+      }
+    }
+    keys[s] = key;
+    const uint32_t f = 0xffffffffu - uint32_t(key & 0xffffffffu);
+    if (key && f < cols) cand[size_t(s) * cols + f] = all[size_t(best) * kMaxFrontier + s].split;
   }
 }
 
@@ -1959,7 +2003,7 @@ void tree_init(const TreeWorkspace& ws, const TreeLaunch& tl, cudaStream_t strea
 
 void tree_level_hist(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t depth,
                      cudaStream_t stream) {
-  const size_t bytes = size_t(max_pairs_at(depth)) * hist_node_bytes(tl.ell);
+  const size_t bytes = size_t(max_pairs_at(depth)) * hist_node_bytes(tl.ell, tl.cols_pad);
   XGBB_CUDA(cudaMemsetAsync(ws.built, 0, bytes, stream));
   HistArgs a;
   a.e = tl.ell;
@@ -1973,6 +2017,7 @@ void tree_level_hist(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t dep
   a.seg_begin = ws.seg_begin[depth & 1];
   a.seg_count = ws.seg_count[depth & 1];
   a.built = ws.built;
+  a.pair_stride = max_pairs_at(depth);
   a.staged = tl.ell.bins + 1 <= kSlots;
   a.max_bits = tl.max_bits;
   a.min_limbs = tl.min_limbs;
@@ -2012,6 +2057,9 @@ void tree_level_eval(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t dep
   a.state = ws.state;
   a.depth = depth;
   a.built = ws.built;
+  a.pair_stride = max_pairs_at(depth);
+  a.f_lo = tl.f_lo;
+  a.f_hi = tl.f_hi;
   a.prev_bank = ws.bank[(depth + 1) & 1];
   a.bank = ws.bank[depth & 1];
   a.parent_slot = ws.parent_slot;
@@ -2023,6 +2071,22 @@ void tree_level_eval(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t dep
   eval_kernel<<<tl.eval_blocks, 256, 0, stream>>>(a);
   XGBB_CUDA(cudaGetLastError());
 }
+
+void tree_level_pack_best(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t depth, void* out,
+                          cudaStream_t stream) {
+  pack_best_kernel<<<1, 512, 0, stream>>>(ws.keys[depth & 1], ws.cand, tl.ell.cols,
+                                          static_cast<BestRecord*>(out));
+  XGBB_CUDA(cudaGetLastError());
+}
+
+void tree_level_merge_best(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t depth,
+                           const void* all, uint32_t ranks, cudaStream_t stream) {
+  merge_best_kernel<<<1, 512, 0, stream>>>(ws.state, static_cast<const BestRecord*>(all), ranks,
+                                           tl.ell.cols, ws.keys[depth & 1], ws.cand);
+  XGBB_CUDA(cudaGetLastError());
+}
+
+size_t best_record_bytes() { return sizeof(BestRecord); }
 
 void tree_level_control(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t depth,
                         cudaStream_t stream) {

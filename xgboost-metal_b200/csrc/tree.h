@@ -88,6 +88,8 @@ struct TreeLaunch {
   uint32_t feature_group;    // features per histogram CTA
   uint32_t min_limbs;        // 3 forces three-limb histogram accumulation
   size_t hist_smem;
+  uint32_t cols_pad;         // features in the built layout (a multiple of the ranks)
+  uint32_t f_lo, f_hi;       // features whose splits this rank evaluates
 };
 
 // Launch helpers (tree.cu). All are asynchronous on `stream`.
@@ -135,6 +137,14 @@ void tree_level_hist(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t dep
                      cudaStream_t stream);
 void tree_level_eval(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t depth,
                      cudaStream_t stream);
+// Multi-GPU split search: this rank's best candidate per slot into `out`
+// ([kMaxFrontier] records of best_record_bytes()), and the best of all ranks'
+// records ([ranks][kMaxFrontier]) back into the keys and candidates.
+void tree_level_pack_best(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t depth, void* out,
+                          cudaStream_t stream);
+void tree_level_merge_best(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t depth,
+                           const void* all, uint32_t ranks, cudaStream_t stream);
+size_t best_record_bytes();
 void tree_level_control(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t depth,
                         cudaStream_t stream);
 void tree_level_partition(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t depth,
@@ -146,6 +156,11 @@ void tree_level_plan(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t nex
 // Bytes of one node's histogram and the largest pair / slot counts at a depth.
 inline size_t hist_node_bytes(const Ellpack& e) {
   return size_t(e.cols) * (e.bins + 1) * sizeof(longlong2);
+}
+// Bytes of one node's histogram in the built buffer, whose feature count is
+// padded to a multiple of the ranks (each rank receives whole features).
+inline size_t hist_node_bytes(const Ellpack& e, uint32_t cols_pad) {
+  return size_t(cols_pad) * (e.bins + 1) * sizeof(longlong2);
 }
 inline uint32_t max_pairs_at(uint32_t depth) { return depth ? (1u << (depth - 1)) : 1u; }
 inline uint32_t max_slots_at(uint32_t depth) { return 1u << depth; }
