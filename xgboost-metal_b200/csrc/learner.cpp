@@ -73,36 +73,112 @@ void DMatrix::upload_info(cudaStream_t stream) {
   uploaded_generation = generation;
 }
 
-void DMatrix::set_cuts(std::shared_ptr<Cuts> c, cudaStream_t stream) {
-  require(c->cols == cols, "Quantile reference does not match the feature count.");
-  // Uploading also settles has_missing for zero-copy input.
-  const float* X = rows ? device_data(stream) : nullptr;
-  uint32_t max_count = 0;
-  for (uint32_t v : c->counts) max_count = std::max(max_count, v);
-  const bool narrow = max_count <= 255 || (!has_missing && max_count <= 256);
-  ell = Ellpack{};
-  ell.rows = rows;
-  ell.cols = cols;
+namespace {
+// Missing code and row stride of the ELLPACK for a code width: the missing
+// code is the cut stride B (the histogram's missing bin) when it fits the
+// code type; with uint8 codes and B = 256 it is 255 (a missing value then
+// implies at most 255 bins), and with 256 bins and no missing value it is
+// 0x100, which no stored code can equal.
+void code_layout(Ellpack& ell, uint32_t cols, uint32_t B, uint32_t max_count, bool narrow) {
   ell.bytes_per_code = narrow ? 1 : 2;
-  // The missing code is the cut stride B (the histogram's missing bin) when it
-  // fits the code type; with uint8 codes and B = 256 it is 255 (a missing
-  // value then implies at most 255 bins), and with 256 bins and no missing
-  // value it is 0x100, which no stored code can equal.
-  const uint32_t B = c->stride;
   if (!narrow) ell.missing = B;
   else if (B <= 255) ell.missing = B;
   else ell.missing = max_count <= 255 ? 0xffu : 0x100u;
   const uint32_t align = 16 / ell.bytes_per_code;
   ell.stride = std::max(align, (cols + align - 1) / align * align);
+}
+}  // namespace
+
+void DMatrix::set_cuts(std::shared_ptr<Cuts> c, cudaStream_t stream) {
+  require(c->cols == cols, "Quantile reference does not match the feature count.");
+  uint32_t max_count = 0;
+  for (uint32_t v : c->counts) max_count = std::max(max_count, v);
+  const uint32_t B = c->stride;
+  ell = Ellpack{};
+  ell.rows = rows;
+  ell.cols = cols;
   ell.bins = c->stride;
   ell.cuts = c->d_values.as<float>();
   ell.counts = c->d_counts.as<uint32_t>();
   ell.minima = c->d_minima.as<float>();
-  const size_t bytes = size_t(rows) * ell.stride * ell.bytes_per_code;
-  codes.resize(std::max<size_t>(bytes, 16));
-  if (rows) {
-    launch_quantize(X, rows, cols, ell.cuts, ell.counts, ell.bins, codes.get(), ell.stride,
+  // uint8 codes whenever every feature's codes, missing included, fit 256
+  // symbols. Whether a value is missing is only known once the data has been
+  // read, so with exactly 256 bins an unread matrix is quantised to uint16
+  // and narrowed afterwards if it holds no missing value.
+  const bool decided = max_count <= 255 || validated || bool(d_data);
+  bool narrow = max_count <= 255 || (!has_missing && max_count <= 256);
+  if (!decided) narrow = false;
+  code_layout(ell, cols, B, max_count, narrow);
+  codes.resize(std::max<size_t>(size_t(rows) * ell.stride * ell.bytes_per_code, 16));
+  if (rows && d_data) {
+    launch_quantize(d_data.as<float>(), rows, cols, ell.cuts, ell.counts, ell.bins, codes.get(), ell.stride,
                     ell.bytes_per_code, ell.missing, stream);
+  } else if (rows) {
+    // Stream the host matrix through two staging buffers: the copy of one
+    // chunk overlaps the validation and quantisation of the other, and the
+    // raw values never occupy the device as a whole.
+    const size_t row_bytes = size_t(cols) * sizeof(float);
+    const uint32_t chunk = uint32_t(std::max<size_t>(1, std::min<size_t>(rows, (256ull << 20) / row_bytes)));
+    DeviceBuffer stage[2], flags(8);
+    stage[0].resize(size_t(chunk) * row_bytes);
+    stage[1].resize(size_t(chunk) * row_bytes);
+    XGBB_CUDA(cudaMemsetAsync(flags.get(), 0, 8, stream));
+    cudaStream_t cs;
+    XGBB_CUDA(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
+    cudaEvent_t copied[2], consumed[2];
+    for (int b = 0; b < 2; ++b) {
+      XGBB_CUDA(cudaEventCreateWithFlags(&copied[b], cudaEventDisableTiming));
+      XGBB_CUDA(cudaEventCreateWithFlags(&consumed[b], cudaEventDisableTiming));
+    }
+    // The copy stream must not start before the flags are cleared and the
+    // previous users of `stream` are done with the staging memory.
+    XGBB_CUDA(cudaEventRecord(consumed[0], stream));
+    XGBB_CUDA(cudaStreamWaitEvent(cs, consumed[0], 0));
+    const size_t code_row = size_t(ell.stride) * ell.bytes_per_code;
+    uint32_t i = 0;
+    for (uint32_t r0 = 0; r0 < rows; r0 += chunk, ++i) {
+      const uint32_t n = std::min(chunk, rows - r0);
+      const int b = int(i & 1);
+      if (i >= 2) XGBB_CUDA(cudaStreamWaitEvent(cs, consumed[b], 0));
+      XGBB_CUDA(cudaMemcpyAsync(stage[b].get(), host + size_t(r0) * cols, size_t(n) * row_bytes,
+                                cudaMemcpyHostToDevice, cs));
+      XGBB_CUDA(cudaEventRecord(copied[b], cs));
+      XGBB_CUDA(cudaStreamWaitEvent(stream, copied[b], 0));
+      if (!validated)
+        launch_validate(stage[b].as<float>(), uint64_t(n) * cols, flags.as<unsigned int>(), stream);
+      launch_quantize(stage[b].as<float>(), n, cols, ell.cuts, ell.counts, ell.bins,
+                      static_cast<char*>(codes.get()) + size_t(r0) * code_row, ell.stride,
+                      ell.bytes_per_code, ell.missing, stream);
+      XGBB_CUDA(cudaEventRecord(consumed[b], stream));
+    }
+    unsigned int h[2] = {0, 0};
+    if (!validated) XGBB_CUDA(cudaMemcpyAsync(h, flags.get(), 8, cudaMemcpyDeviceToHost, stream));
+    XGBB_CUDA(cudaStreamSynchronize(stream));
+    for (int b = 0; b < 2; ++b) {
+      cudaEventDestroy(copied[b]);
+      cudaEventDestroy(consumed[b]);
+    }
+    cudaStreamDestroy(cs);
+    if (!validated) {
+      // Zero-copy input is checked on the device: NaN marks missing values,
+      // any infinity is an error (src/data.cpp:433).
+      if (h[1]) {
+        codes.release();
+        throw Error("Input data contains infinity or a value too large for float32.");
+      }
+      has_missing = h[0] != 0;
+      validated = true;
+    }
+    if (!decided && !has_missing) {
+      // 256 bins and no missing value: every code is a bin below 256.
+      Ellpack n8 = ell;
+      code_layout(n8, cols, B, max_count, true);
+      DeviceBuffer c8(std::max<size_t>(size_t(rows) * n8.stride, 16));
+      launch_narrow_codes(codes.get(), rows, cols, ell.stride, n8.stride, n8.missing, c8.get(), stream);
+      XGBB_CUDA(cudaStreamSynchronize(stream));
+      codes = std::move(c8);
+      ell = n8;
+    }
   }
   ell.codes = codes.get();
   // A feature-major copy lets the partition read a node's split feature from

@@ -121,6 +121,18 @@ __global__ void __launch_bounds__(256) transpose_codes_kernel(const CodeT* __res
   }
 }
 
+// uint16 codes [rows][s16] to uint8 codes [rows][s8] (every code below 256);
+// padding columns take `pad`.
+__global__ void narrow_codes_kernel(const uint16_t* __restrict__ src, uint32_t rows, uint32_t cols,
+                                    uint32_t s16, uint32_t s8, uint8_t pad, uint8_t* __restrict__ dst) {
+  const uint64_t total = uint64_t(rows) * s8;
+  for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < total;
+       i += uint64_t(gridDim.x) * blockDim.x) {
+    const uint32_t r = uint32_t(i / s8), c = uint32_t(i % s8);
+    dst[i] = c < cols ? uint8_t(src[size_t(r) * s16 + c]) : pad;
+  }
+}
+
 __global__ void validate_kernel(const float4* __restrict__ X4, const float* __restrict__ X,
                                 uint64_t n, unsigned int* flags) {
   unsigned int nan = 0, inf = 0;
@@ -1883,6 +1895,15 @@ void launch_quantize(const float* X, uint32_t rows, uint32_t cols, const float* 
   else
     quantize_kernel<uint16_t><<<blocks, threads, 0, stream>>>(
         X, rows, cols, cuts, counts, bins, static_cast<uint16_t*>(codes), stride, missing);
+  XGBB_CUDA(cudaGetLastError());
+}
+
+void launch_narrow_codes(const void* src, uint32_t rows, uint32_t cols, uint32_t s16, uint32_t s8,
+                         uint32_t pad, void* dst, cudaStream_t stream) {
+  const uint64_t total = uint64_t(rows) * s8;
+  if (!total) return;
+  narrow_codes_kernel<<<grid_for(total, 256, 148 * 16), 256, 0, stream>>>(
+      static_cast<const uint16_t*>(src), rows, cols, s16, s8, uint8_t(pad), static_cast<uint8_t*>(dst));
   XGBB_CUDA(cudaGetLastError());
 }
 

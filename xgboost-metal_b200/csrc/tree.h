@@ -93,6 +93,8 @@ struct TreeLaunch {
 };
 
 // Launch helpers (tree.cu). All are asynchronous on `stream`.
+void launch_narrow_codes(const void* src, uint32_t rows, uint32_t cols, uint32_t s16, uint32_t s8,
+                         uint32_t pad, void* dst, cudaStream_t stream);
 void launch_transpose_codes(const void* codes, uint32_t rows, uint32_t cols, uint32_t stride,
                             uint32_t bytes_per_code, void* fm, cudaStream_t stream);
 void launch_quantize(const float* X, uint32_t rows, uint32_t cols, const float* cuts,

@@ -122,7 +122,8 @@ class DMatrix:
             self.set_base_margin(base_margin)
 
     def __del__(self):
-        if getattr(self, "handle", None) is not None and self.handle.value:
+        # At interpreter exit the module globals may already be gone.
+        if _LIB is not None and getattr(self, "handle", None) is not None and self.handle.value:
             _LIB.XGDMatrixFree(self.handle)
             self.handle = None
 
@@ -216,7 +217,7 @@ class Booster:
             raise XGBoostError("Model loading is not implemented by the CUDA backend yet.")
 
     def __del__(self):
-        if getattr(self, "handle", None) is not None and self.handle.value:
+        if _LIB is not None and getattr(self, "handle", None) is not None and self.handle.value:
             _LIB.XGBoosterFree(self.handle)
             self.handle = None
 
