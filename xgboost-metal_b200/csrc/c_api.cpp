@@ -553,6 +553,7 @@ XGB_DLL int XGDMatrixQuantise(DMatrixHandle handle, int max_bin, DMatrixHandle r
 
 XGB_DLL int XGBoosterGetCudaProfile(BoosterHandle handle, char const** out) {
   return guarded([&] {
+    booster(handle).finish_pending();  // the last round's profile figures
     auto& p = booster(handle).profile;
     results.str = "{\"hist_ms\":" + std::to_string(p.hist_ms) +
                   ",\"hist_bytes\":" + std::to_string(p.hist_bytes) +
@@ -577,7 +578,10 @@ XGB_DLL int XGBoosterEventElapsed(BoosterHandle handle, int a, int b, float* ms)
 }
 
 XGB_DLL int XGBoosterResetCudaProfile(BoosterHandle handle) {
-  return guarded([&] { booster(handle).profile = xgbb::Profile{}; });
+  return guarded([&] {
+    booster(handle).finish_pending();  // a pending round belongs to the counts being cleared
+    booster(handle).profile = xgbb::Profile{};
+  });
 }
 
 // Test entry: product cuts (host sketch) and GPU bins, decoded to row-major

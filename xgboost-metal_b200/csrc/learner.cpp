@@ -238,20 +238,29 @@ struct Booster::TrainState {
   TreeWorkspace ws{};
   HistConfig hc{};
   std::vector<cudaGraphExec_t> graphs;
-  DevNode* host_nodes = nullptr;   // pinned [groups][capacity]
-  DriverState* host_state = nullptr;  // pinned [groups]
-  unsigned long long* host_level_rows = nullptr;  // pinned [groups][kMaxDepth]
-  uint32_t* host_level_nodes = nullptr;           // pinned [groups][kMaxDepth]
+  // Host copies of each round's trees, two sets: a round's copies land in
+  // set (round & 1) while the host reads the previous round's set.
+  DevNode* host_nodes[2] = {};                       // pinned [groups][capacity]
+  DriverState* host_state[2] = {};                   // pinned [groups]
+  unsigned long long* host_level_rows[2] = {};       // pinned [groups][kMaxDepth]
+  uint32_t* host_level_nodes[2] = {};                // pinned [groups][kMaxDepth]
+  cudaEvent_t copied[2] = {};                        // the set's copies are complete
+  int pending = -1;        // set of a launched round not yet turned into trees
+  bool pending_captured = false;
+  uint32_t parity = 0;
   uint32_t capacity = 0;
   std::vector<cudaEvent_t> events;  // profiling: [groups][levels][2]
   ~TrainState() {
     for (auto g : graphs)
       if (g) cudaGraphExecDestroy(g);
     for (auto e : events) cudaEventDestroy(e);
-    if (host_nodes) cudaFreeHost(host_nodes);
-    if (host_state) cudaFreeHost(host_state);
-    if (host_level_rows) cudaFreeHost(host_level_rows);
-    if (host_level_nodes) cudaFreeHost(host_level_nodes);
+    for (int b = 0; b < 2; ++b) {
+      if (copied[b]) cudaEventDestroy(copied[b]);
+      if (host_nodes[b]) cudaFreeHost(host_nodes[b]);
+      if (host_state[b]) cudaFreeHost(host_state[b]);
+      if (host_level_rows[b]) cudaFreeHost(host_level_rows[b]);
+      if (host_level_nodes[b]) cudaFreeHost(host_level_nodes[b]);
+    }
   }
 };
 
@@ -263,6 +272,8 @@ Booster::Booster(std::vector<std::shared_ptr<DMatrix>> cache) {
 
 Booster::~Booster() {
   Comm::get().remove_release_hook(this);
+  // Copies into pinned buffers may still be in flight.
+  if (stream_) cudaStreamSynchronize(stream_);
   state_.reset();
   for (auto e : user_events_)
     if (e) cudaEventDestroy(e);
@@ -450,6 +461,10 @@ void Booster::initialize(DMatrix& d) {
 Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp) {
   DMatrix& d = *dp;
   if (state_ && state_->d == &d && !state_->owner.expired()) return *state_;
+  if (state_) {
+    finish_pending();
+    XGBB_CUDA(cudaStreamSynchronize(stream_));
+  }
   state_.reset();
   auto ts = std::make_unique<TrainState>();
   ts->owner = dp;
@@ -509,11 +524,14 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp) {
   const uint32_t bank_slots = D >= 2 ? max_slots_at(D - 2) : 1u;
   ts->bank[0].resize(size_t(bank_slots) * node_bytes);
   ts->bank[1].resize(size_t(bank_slots) * node_bytes);
-  XGBB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ts->host_nodes),
-                           size_t(G) * ts->capacity * sizeof(DevNode)));
-  XGBB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ts->host_state), size_t(G) * sizeof(DriverState)));
-  XGBB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ts->host_level_rows), size_t(G) * kMaxDepth * 8));
-  XGBB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ts->host_level_nodes), size_t(G) * kMaxDepth * 4));
+  for (int b = 0; b < 2; ++b) {
+    XGBB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ts->host_nodes[b]),
+                             size_t(G) * ts->capacity * sizeof(DevNode)));
+    XGBB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ts->host_state[b]), size_t(G) * sizeof(DriverState)));
+    XGBB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ts->host_level_rows[b]), size_t(G) * kMaxDepth * 8));
+    XGBB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ts->host_level_nodes[b]), size_t(G) * kMaxDepth * 4));
+    XGBB_CUDA(cudaEventCreateWithFlags(&ts->copied[b], cudaEventDisableTiming));
+  }
   ts->level_rows.resize(kMaxDepth * 8);
   ts->level_nodes.resize(kMaxDepth * 4);
 
@@ -547,9 +565,12 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp) {
   ws.level_nodes = ts->level_nodes.as<uint32_t>();
   ws.limbs_root = ts->limbs_root.as<int4>();
   ts->hc = hist_config(e, objective_ == kSquaredError && d.weights.empty());
-  ts->graphs.assign(G, nullptr);
+  // One graph per group and round parity: the two differ only in the
+  // profiling events they record, so a round's events are read after the
+  // next round has been enqueued.
+  ts->graphs.assign(size_t(G) * 2, nullptr);
   if (profiling) {
-    ts->events.resize(size_t(G) * D * 2);
+    ts->events.resize(size_t(2) * G * D * 2);
     for (auto& ev : ts->events) XGBB_CUDA(cudaEventCreate(&ev));
   }
   // Margins start from the base margins plus every tree already in the model.
@@ -570,7 +591,14 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp) {
     // Sharded training captures NCCL calls in its graphs; the communicator
     // drops this state (graphs included) before it is destroyed.
     Comm::get().add_release_hook(this, [this] {
-      if (state_) cudaStreamSynchronize(stream_);
+      if (state_) {
+        cudaStreamSynchronize(stream_);
+        try {
+          finish_pending();
+        } catch (const std::exception&) {
+          // The communicator is going away; a failed round has no model to keep.
+        }
+      }
       state_.reset();
     });
   }
@@ -601,7 +629,8 @@ bool staged_round(const unsigned int* max_bits, const float2* scales, uint32_t g
 }
 }  // namespace
 
-void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s, bool capturing) {
+void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s, bool capturing,
+                                   uint32_t parity) {
   // Inside a capture the profiling events become external event-record nodes,
   // recorded again at every launch of the graph.
   auto mark = [&](cudaEvent_t ev) {
@@ -640,9 +669,9 @@ void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s, b
   tl.f_hi = std::min((rank + 1) * per_rank, d.ell.cols);
   tree_init(ws, tl, s);
   for (uint32_t depth = 0; depth < D; ++depth) {
-    if (profiling) mark(ts.events[(size_t(g) * D + depth) * 2]);
+    if (profiling) mark(ts.events[((size_t(parity) * ts.groups + g) * D + depth) * 2]);
     tree_level_hist(ws, tl, depth, s);
-    if (profiling) mark(ts.events[(size_t(g) * D + depth) * 2 + 1]);
+    if (profiling) mark(ts.events[((size_t(parity) * ts.groups + g) * D + depth) * 2 + 1]);
     // Sum the built histograms over ranks, each rank receiving its features.
     comm.reduce_scatter_u64(ws.built, size_t(per_rank) * max_pairs_at(depth) * (d.ell.bins + 1) * 2, s);
     tree_level_eval(ws, tl, depth, s);
@@ -663,14 +692,21 @@ void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s, b
       tree_level_plan(ws, tl, depth + 1, s);
     }
   }
-  XGBB_CUDA(cudaMemcpyAsync(ts.host_nodes + size_t(g) * ts.capacity, ws.nodes,
-                            size_t(ts.capacity) * sizeof(DevNode), cudaMemcpyDeviceToHost, s));
-  XGBB_CUDA(cudaMemcpyAsync(ts.host_state + g, ws.state, sizeof(DriverState),
+}
+
+// Group g's tree (node table, driver state, level statistics) into host set
+// `b`, ordered after the tree on the stream; the next group reuses the device
+// buffers.
+static void copy_tree_out(const TreeWorkspace& ws, uint32_t capacity, uint32_t g, DevNode* nodes,
+                          DriverState* state, unsigned long long* level_rows, uint32_t* level_nodes,
+                          cudaStream_t s) {
+  XGBB_CUDA(cudaMemcpyAsync(nodes + size_t(g) * capacity, ws.nodes, size_t(capacity) * sizeof(DevNode),
                             cudaMemcpyDeviceToHost, s));
-  XGBB_CUDA(cudaMemcpyAsync(ts.host_level_rows + size_t(g) * kMaxDepth, ws.level_rows,
-                            kMaxDepth * 8, cudaMemcpyDeviceToHost, s));
-  XGBB_CUDA(cudaMemcpyAsync(ts.host_level_nodes + size_t(g) * kMaxDepth, ws.level_nodes,
-                            kMaxDepth * 4, cudaMemcpyDeviceToHost, s));
+  XGBB_CUDA(cudaMemcpyAsync(state + g, ws.state, sizeof(DriverState), cudaMemcpyDeviceToHost, s));
+  XGBB_CUDA(cudaMemcpyAsync(level_rows + size_t(g) * kMaxDepth, ws.level_rows, kMaxDepth * 8,
+                            cudaMemcpyDeviceToHost, s));
+  XGBB_CUDA(cudaMemcpyAsync(level_nodes + size_t(g) * kMaxDepth, ws.level_nodes, kMaxDepth * 4,
+                            cudaMemcpyDeviceToHost, s));
 }
 
 void Booster::run_round(TrainState& ts) {
@@ -698,36 +734,61 @@ void Booster::run_round(TrainState& ts) {
   launch_scales_exact(G, mass, ts.scales.as<float2>(), stream_);
   const bool use_graph = integer(params_, "cuda_graph", 1) != 0;
   bool captured = false;
+  const uint32_t b = ts.parity;
   for (uint32_t g = 0; g < G; ++g) {
     if (use_graph) {
-      if (!ts.graphs[g]) {
+      cudaGraphExec_t& exec = ts.graphs[size_t(g) * 2 + b];
+      if (!exec) {
         // Kernel attributes are set on first use, outside any capture.
-        record_tree_launches(ts, g, stream_, false);
+        record_tree_launches(ts, g, stream_, false, b);
         XGBB_CUDA(cudaStreamSynchronize(stream_));
-        cudaGraph_t graph;
-        XGBB_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
         // The eager tree above already trained this group; replaying it would
-        // train the same tree twice, so the graph is only captured here.
-        record_tree_launches(ts, g, stream_, true);
+        // train the same tree twice, so the graphs of both parities are only
+        // captured here.
+        for (uint32_t p = 0; p < 2; ++p) {
+          cudaGraph_t graph;
+          XGBB_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+          record_tree_launches(ts, g, stream_, true, p);
+          XGBB_CUDA(cudaStreamEndCapture(stream_, &graph));
+          XGBB_CUDA(cudaGraphInstantiate(&ts.graphs[size_t(g) * 2 + p], graph, 0));
+          XGBB_CUDA(cudaGraphDestroy(graph));
+        }
         captured = true;
-        XGBB_CUDA(cudaStreamEndCapture(stream_, &graph));
-        XGBB_CUDA(cudaGraphInstantiate(&ts.graphs[g], graph, 0));
-        XGBB_CUDA(cudaGraphDestroy(graph));
       } else {
-        XGBB_CUDA(cudaGraphLaunch(ts.graphs[g], stream_));
+        XGBB_CUDA(cudaGraphLaunch(exec, stream_));
       }
     } else {
-      record_tree_launches(ts, g, stream_, false);
+      record_tree_launches(ts, g, stream_, false, b);
     }
+    copy_tree_out(ts.ws, ts.capacity, g, ts.host_nodes[b], ts.host_state[b], ts.host_level_rows[b],
+                  ts.host_level_nodes[b], stream_);
   }
-  XGBB_CUDA(cudaStreamSynchronize(stream_));
+  XGBB_CUDA(cudaEventRecord(ts.copied[b], stream_));
+  ++rounds_;
+  ts.margin_rounds = rounds_;
+  ts.parity ^= 1u;
+  // The round runs on while the host turns the previous round into trees.
+  finish_round(ts);
+  ts.pending = int(b);
+  ts.pending_captured = captured;
+}
+
+// Turns the pending round's host copies into trees (and profile figures).
+void Booster::finish_round(TrainState& ts) {
+  if (ts.pending < 0) return;
+  const int b = ts.pending;
+  const bool captured = ts.pending_captured;
+  ts.pending = -1;
+  XGBB_CUDA(cudaEventSynchronize(ts.copied[b]));
+  DMatrix& d = *ts.d;
+  const uint32_t G = ts.groups;
   for (uint32_t g = 0; g < G; ++g) {
-    const DriverState st = ts.host_state[g];
+    const DriverState st = ts.host_state[b][g];
     require(!st.error, "GPU tree driver produced an invalid tree.");
     require(st.node_count >= 1 && st.node_count <= ts.capacity, "GPU tree driver node count out of range.");
     HostTree t;
     t.group = g;
-    const DevNode* src = ts.host_nodes + size_t(g) * ts.capacity;
+    const DevNode* src = ts.host_nodes[b] + size_t(g) * ts.capacity;
     t.nodes.assign(src, src + st.node_count);
     trees_.push_back(std::move(t));
   }
@@ -749,10 +810,10 @@ void Booster::run_round(TrainState& ts) {
       const double row_bytes = double(e.cols) * e.bytes_per_code + (staged ? 16.0 : 8.0);
       for (uint32_t depth = 0; depth < D; ++depth) {
         float ms = 0;
-        XGBB_CUDA(cudaEventElapsedTime(&ms, ts.events[(size_t(g) * D + depth) * 2],
-                                       ts.events[(size_t(g) * D + depth) * 2 + 1]));
-        const double rows = double(ts.host_level_rows[size_t(g) * kMaxDepth + depth]);
-        const double nodes = double(ts.host_level_nodes[size_t(g) * kMaxDepth + depth]);
+        const size_t e = ((size_t(b) * G + g) * D + depth) * 2;
+        XGBB_CUDA(cudaEventElapsedTime(&ms, ts.events[e], ts.events[e + 1]));
+        const double rows = double(ts.host_level_rows[b][size_t(g) * kMaxDepth + depth]);
+        const double nodes = double(ts.host_level_nodes[b][size_t(g) * kMaxDepth + depth]);
         if (nodes == 0) continue;
         profile.hist_ms += ms;
         profile.hist_bytes += rows * (row_bytes + (depth ? 4.0 : 0.0)) + nodes * node_bytes;
@@ -764,8 +825,10 @@ void Booster::run_round(TrainState& ts) {
     }
   }
   ++profile.rounds;
-  ++rounds_;
-  ts.margin_rounds = rounds_;
+}
+
+void Booster::finish_pending() {
+  if (state_) finish_round(*state_);
 }
 
 void Booster::update(const std::shared_ptr<DMatrix>& d, int) {
@@ -781,7 +844,10 @@ void Booster::update(const std::shared_ptr<DMatrix>& d, int) {
   run_round(ts);
 }
 
-void Booster::sync() { XGBB_CUDA(cudaStreamSynchronize(stream_)); }
+void Booster::sync() {
+  XGBB_CUDA(cudaStreamSynchronize(stream_));
+  finish_pending();
+}
 
 void Booster::record_event(int slot) {
   require(slot >= 0 && slot < 64, "event slot out of range");
@@ -803,6 +869,7 @@ std::vector<float> Booster::predict(const std::shared_ptr<DMatrix>& dp, bool out
                                     uint32_t begin, uint32_t end, bool, std::vector<uint64_t>& shape) {
   XGBB_CUDA(cudaSetDevice(device_));
   configure();
+  finish_pending();
   DMatrix& d = *dp;
   const uint32_t G = initialized_ ? groups_ : std::max<uint32_t>(groups_, 1);
   require(!initialized_ || d.cols == num_feature_ || d.rows == 0, "Feature shape mismatch.");

@@ -116,6 +116,9 @@ class Booster {
   uint32_t num_feature() const { return num_feature_; }
   uint32_t groups() const { return groups_; }
   const std::vector<HostTree>& trees() { sync(); return trees_; }
+  // A round returns once it is enqueued; its trees reach trees_ when the next
+  // round is enqueued or when anything reads the model (this call).
+  void finish_pending();
   std::string save_json();
   void load_json(const std::string& text);
   std::string config_json() const;
@@ -134,7 +137,9 @@ class Booster {
   void initialize(DMatrix& d);
   TrainState& train_state(const std::shared_ptr<DMatrix>& d);
   void run_round(TrainState& ts);
-  void record_tree_launches(TrainState& ts, uint32_t group, cudaStream_t stream, bool capturing);
+  void finish_round(TrainState& ts);
+  void record_tree_launches(TrainState& ts, uint32_t group, cudaStream_t stream, bool capturing,
+                            uint32_t parity);
   void materialize();
 
   std::map<std::string, std::string> params_;
