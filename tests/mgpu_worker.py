@@ -30,11 +30,35 @@ def data(objective, c=12):
     return X, y
 
 
+def leave_after_two_rounds(params, shard, rank, world):
+    """The last rank leaves between rounds, its work finished and nothing in
+    flight; the others must end a later round with an error (after the
+    communicator's 15 s limit) instead of waiting for it forever."""
+    bst = xgb.Booster(params, [shard])
+    for i in range(2):
+        bst.update(shard, i)
+    core.synchronize()
+    if rank == world - 1:
+        print("rank %d leaves after 2 rounds" % rank, flush=True)
+        os._exit(0)
+    try:
+        for i in range(2, 8):
+            bst.update(shard, i)
+        core.synchronize()
+    except xgb.core.XGBoostError as e:
+        # After an aborted communicator the process exits at once.
+        print("rank %d raised: %s" % (rank, e), flush=True)
+        os._exit(3)
+    print("rank %d: no error" % rank, flush=True)
+    os._exit(1)
+
+
 def main():
     import faulthandler
     faulthandler.dump_traceback_later(int(os.environ.get("XGBB_WORKER_TIMEOUT", "240")), exit=True)
     out_dir, objective = sys.argv[1], sys.argv[2]
     cols = int(sys.argv[3]) if len(sys.argv) > 3 else 12
+    mode = sys.argv[4] if len(sys.argv) > 4 else "train"
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
@@ -42,7 +66,8 @@ def main():
     core.set_device(local)
     box = [xgb.collective.nccl_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(box, src=0)
-    xgb.collective.init(rank=rank, world_size=world, nccl_unique_id=box[0], device=local)
+    xgb.collective.init(rank=rank, world_size=world, nccl_unique_id=box[0], device=local,
+                        timeout=15.0 if mode == "leave" else None)
     X, y = data(objective, cols)
     lo, hi = len(y) * rank // world, len(y) * (rank + 1) // world
     ref = xgb.QuantileDMatrix(X, max_bin=64)
@@ -50,6 +75,9 @@ def main():
     params = {"objective": objective, "max_depth": 6, "eta": 0.3, "max_bin": 64,
               "device": "cuda", "tree_method": "hist",
               "cuda_graph": int(os.environ.get("XGBB_WORKER_GRAPH", "1"))}
+    if mode == "leave":
+        leave_after_two_rounds(params, shard, rank, world)
+        return
     bst = xgb.train(params, shard, 6)
     margins = bst.predict(xgb.DMatrix(X), output_margin=True)
     np.save(os.path.join(out_dir, "margins_%d.npy" % rank), margins)

@@ -43,3 +43,21 @@ def test_two_ranks_match_the_oracle(tmp_path, objective, cols):
     for r in range(2):
         got = np.load(os.path.join(tmp_path, "margins_%d.npy" % r))
         np.testing.assert_array_equal(got.view(np.uint32), margins[:, 0].view(np.uint32))
+
+
+@pytest.mark.skipif(gpu_count() < 2, reason="needs two GPUs")
+def test_rank_that_leaves_ends_the_others_with_an_error(tmp_path):
+    """Failure detection without a GPU fault: rank 1 leaves between rounds
+    with nothing in flight. Rank 0's next round cannot complete its
+    collectives; after the communicator's 15 s limit the communicator is
+    aborted and the round raises XGBoostError (rank 0 then exits with 3)."""
+    env = dict(os.environ, MASTER_ADDR="127.0.0.1", NCCL_NVLS_ENABLE="0", NCCL_SOCKET_IFNAME="lo")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", "--master-port=29535",
+           os.path.join(HERE, "mgpu_worker.py"), str(tmp_path), "reg:squarederror", "12", "leave"]
+    proc = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
+    out = proc.stdout + proc.stderr
+    assert "rank 1 leaves after 2 rounds" in out, out[-3000:]
+    assert "rank 0 raised:" in out, out[-3000:]
+    assert "did not complete within" in out or "NCCL error" in out, out[-3000:]
+    assert proc.returncode != 0

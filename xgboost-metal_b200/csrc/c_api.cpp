@@ -512,6 +512,9 @@ XGB_DLL int XGCommunicatorInit(char const* config) {
     if (auto* d = c.find("device")) device = int(d->num);
     std::string id;
     if (auto* i = c.find("nccl_unique_id")) id = i->str;
+    // Seconds a collective may wait for the other ranks before the
+    // communicator is aborted and the waiting call fails.
+    if (auto* t = c.find("timeout")) xgbb::Comm::get().set_timeout(t->num);
     xgbb::Comm::get().init(rank, world, id, device);
   });
 }
@@ -538,7 +541,7 @@ XGB_DLL int XGBBSetDevice(int device) {
 }
 
 XGB_DLL int XGBBSynchronize(void) {
-  return guarded([&] { XGBB_CUDA(cudaDeviceSynchronize()); });
+  return guarded([&] { xgbb::Comm::get().wait_device("device synchronisation"); });
 }
 
 XGB_DLL int XGDMatrixQuantise(DMatrixHandle handle, int max_bin, DMatrixHandle ref) {

@@ -4,6 +4,7 @@
 // summed over ranks, so each rank takes the same decisions as one GPU would.
 #pragma once
 #include <cuda_runtime.h>
+#include <nccl.h>
 
 #include <cstddef>
 #include <cstdint>
@@ -38,10 +39,23 @@ class Comm {
   // graphs holding NCCL calls would otherwise keep ncclCommDestroy waiting.
   void add_release_hook(const void* owner, std::function<void()> fn);
   void remove_release_hook(const void* owner);
+  // Host waits for stream work that contains collectives (the event recorded
+  // after it) and for the whole device, bounded by the timeout: on an NCCL
+  // error or the timeout the communicator is aborted and an Error raised.
+  void wait(cudaEvent_t ev, const char* what);
+  void wait_device(const char* what);
+  void set_timeout(double seconds);
+  bool failed() const { return failed_; }
 
  private:
+  void settle(const char* what);
+  void call(ncclResult_t r, const char* what);
+  void abort_detached();
+  [[noreturn]] void fail(const std::string& what);
   int rank_ = 0, world_ = 1;
   void* comm_ = nullptr;
+  bool failed_ = false;
+  double timeout_s_ = 600.0;
   std::map<const void*, std::function<void()>> hooks_;
 };
 

@@ -272,11 +272,19 @@ Booster::Booster(std::vector<std::shared_ptr<DMatrix>> cache) {
 
 Booster::~Booster() {
   Comm::get().remove_release_hook(this);
+  if (Comm::get().failed()) {
+    // Kernels of an aborted communicator may still use this state; waiting
+    // for them or freeing under them could block, so it is left to the
+    // process exit that must follow such a failure.
+    (void)state_.release();
+    return;
+  }
   // Copies into pinned buffers may still be in flight.
   if (stream_) cudaStreamSynchronize(stream_);
   state_.reset();
   for (auto e : user_events_)
     if (e) cudaEventDestroy(e);
+  if (wait_event_) cudaEventDestroy(wait_event_);
   if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -591,6 +599,10 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp) {
     // Sharded training captures NCCL calls in its graphs; the communicator
     // drops this state (graphs included) before it is destroyed.
     Comm::get().add_release_hook(this, [this] {
+      if (Comm::get().failed()) {
+        (void)state_.release();  // see ~Booster
+        return;
+      }
       if (state_) {
         cudaStreamSynchronize(stream_);
         try {
@@ -710,6 +722,12 @@ static void copy_tree_out(const TreeWorkspace& ws, uint32_t capacity, uint32_t g
 }
 
 void Booster::run_round(TrainState& ts) {
+  // With collectives on the stream, the previous round must have completed
+  // before new NCCL calls are enqueued: an enqueue behind a collective that
+  // can no longer complete (a rank failed or left) could block inside NCCL,
+  // out of reach of the communicator's time limit.
+  if (Comm::get().active() && ts.pending >= 0)
+    Comm::get().wait(ts.copied[ts.pending], "the previous training round");
   DMatrix& d = *ts.d;
   const uint32_t n = ts.rows, G = ts.groups;
   d.upload_info(stream_);
@@ -741,7 +759,7 @@ void Booster::run_round(TrainState& ts) {
       if (!exec) {
         // Kernel attributes are set on first use, outside any capture.
         record_tree_launches(ts, g, stream_, false, b);
-        XGBB_CUDA(cudaStreamSynchronize(stream_));
+        wait_stream("the first tree of a group");
         // The eager tree above already trained this group; replaying it would
         // train the same tree twice, so the graphs of both parities are only
         // captured here.
@@ -779,7 +797,7 @@ void Booster::finish_round(TrainState& ts) {
   const int b = ts.pending;
   const bool captured = ts.pending_captured;
   ts.pending = -1;
-  XGBB_CUDA(cudaEventSynchronize(ts.copied[b]));
+  Comm::get().wait(ts.copied[b], "a training round");
   DMatrix& d = *ts.d;
   const uint32_t G = ts.groups;
   for (uint32_t g = 0; g < G; ++g) {
@@ -845,8 +863,16 @@ void Booster::update(const std::shared_ptr<DMatrix>& d, int) {
 }
 
 void Booster::sync() {
-  XGBB_CUDA(cudaStreamSynchronize(stream_));
+  wait_stream("the booster's work");
   finish_pending();
+}
+
+// Waits for everything enqueued on the booster's stream, through the
+// communicator's bounded wait when the stream carries collectives.
+void Booster::wait_stream(const char* what) {
+  if (!wait_event_) XGBB_CUDA(cudaEventCreateWithFlags(&wait_event_, cudaEventDisableTiming));
+  XGBB_CUDA(cudaEventRecord(wait_event_, stream_));
+  Comm::get().wait(wait_event_, what);
 }
 
 void Booster::record_event(int slot) {

@@ -138,6 +138,7 @@ class Booster {
   TrainState& train_state(const std::shared_ptr<DMatrix>& d);
   void run_round(TrainState& ts);
   void finish_round(TrainState& ts);
+  void wait_stream(const char* what);
   void record_tree_launches(TrainState& ts, uint32_t group, cudaStream_t stream, bool capturing,
                             uint32_t parity);
   void materialize();
@@ -155,6 +156,7 @@ class Booster {
   int device_ = 0;
   std::unique_ptr<TrainState> state_;
   std::vector<cudaEvent_t> user_events_;
+  cudaEvent_t wait_event_ = nullptr;
 };
 
 }  // namespace xgbb

@@ -30,6 +30,10 @@ def init(**args):
     cfg = {"rank": int(args.get("rank", 0)), "world_size": int(args.get("world_size", 1)),
            "device": int(args.get("device", 0)),
            "nccl_unique_id": args.get("nccl_unique_id", "")}
+    # Seconds a collective may wait for the other ranks before the
+    # communicator is aborted and the waiting call raises XGBoostError.
+    if args.get("timeout") is not None:
+        cfg["timeout"] = float(args["timeout"])
     _check_call(_LIB.XGCommunicatorInit(_c_str(json.dumps(cfg))))
 
 
