@@ -92,6 +92,15 @@ XGB_DLL int XGBoosterPredictFromDMatrix(BoosterHandle handle, DMatrixHandle dmat
 XGB_DLL int XGBoosterPredict(BoosterHandle handle, DMatrixHandle dmat, int option_mask,
                              unsigned ntree_limit, int training, bst_ulong* out_len,
                              const float** out_result);
+/* include/xgboost/c_api.h:1378. Loads a JSON or UBJSON model file (upstream XGBoost's schema). */
+XGB_DLL int XGBoosterLoadModel(BoosterHandle handle, const char* fname);
+/* include/xgboost/c_api.h:1387. JSON when the name ends in ".json", else UBJSON. */
+XGB_DLL int XGBoosterSaveModel(BoosterHandle handle, const char* fname);
+/* include/xgboost/c_api.h:1396. */
+XGB_DLL int XGBoosterLoadModelFromBuffer(BoosterHandle handle, const void* buf, bst_ulong len);
+/* include/xgboost/c_api.h:1414. config: {"format": "json" | "ubj"} (default "ubj"). */
+XGB_DLL int XGBoosterSaveModelToBuffer(BoosterHandle handle, char const* config, bst_ulong* out_len,
+                                       char const** out_dptr);
 /* include/xgboost/c_api.h:1451 */
 XGB_DLL int XGBoosterSaveJsonConfig(BoosterHandle handle, bst_ulong* out_len, char const** out_str);
 /* include/xgboost/c_api.h:1548 */

@@ -6,7 +6,9 @@
 // convention, src/c_api.cpp:16-40).
 #include <cuda_runtime.h>
 
+#include <cctype>
 #include <cmath>
+#include <cstdio>
 #include <cstring>
 #include <memory>
 #include <string>
@@ -361,7 +363,6 @@ XGB_DLL int XGDMatrixNumNonMissing(DMatrixHandle handle, bst_ulong* out) {
 // ---------------------------------------------------------------------------
 XGB_DLL int XGBoosterCreate(const DMatrixHandle dmats[], bst_ulong len, BoosterHandle* out) {
   return guarded([&] {
-    ensure_device();
     std::vector<DMatrixPtr> cache;
     for (bst_ulong i = 0; i < len; ++i) cache.push_back(dmat(dmats[i]));
     *out = new xgbb::Booster(std::move(cache));
@@ -490,6 +491,73 @@ XGB_DLL int XGBoosterGetStrFeatureInfo(BoosterHandle handle, const char* field, 
     *len = results.ptrs.size();
     *out_features = results.ptrs.data();
   });
+}
+
+// Model files (src/c_api.cpp:521-538 in the reference): JSON text, or
+// Universal Binary JSON, the same document in binary form.
+namespace {
+std::string model_bytes(xgbb::Booster& b, const std::string& format) {
+  xgbb::require(format == "json" || format == "ubj", "Model format must be 'json' or 'ubj': " + format);
+  std::string text = b.save_json();
+  return format == "json" ? text : xgbb::Json::parse(text).dump_ubj();
+}
+void load_model_bytes(xgbb::Booster& b, const void* data, size_t size) {
+  const char* p = static_cast<const char*>(data);
+  size_t i = 0;
+  while (i < size && std::isspace(static_cast<unsigned char>(p[i]))) ++i;
+  xgbb::require(i < size, "The model buffer is empty.");
+  // Both open with '{': JSON text continues with a quote, blank or '}', a
+  // UBJSON object with the marker of its first key's length.
+  const char next = i + 1 < size ? p[i + 1] : '}';
+  const bool text = p[i] == '{' && (next == '"' || next == '}' || std::isspace(static_cast<unsigned char>(next)));
+  if (text) b.load_json(std::string(p, size));
+  else b.load_json(xgbb::Json::parse_ubj(p, size).dump());
+}
+}  // namespace
+
+XGB_DLL int XGBoosterSaveModel(BoosterHandle handle, const char* fname) {
+  return guarded([&] {
+    const std::string path = fname ? fname : "";
+    const bool json = path.size() >= 5 && path.compare(path.size() - 5, 5, ".json") == 0;
+    const std::string bytes = model_bytes(booster(handle), json ? "json" : "ubj");
+    std::FILE* f = std::fopen(path.c_str(), "wb");
+    xgbb::require(f != nullptr, "Cannot write model: " + path);
+    const size_t wrote = std::fwrite(bytes.data(), 1, bytes.size(), f);
+    const bool closed = std::fclose(f) == 0;
+    xgbb::require(wrote == bytes.size() && closed, "Failed to write model: " + path);
+  });
+}
+
+XGB_DLL int XGBoosterLoadModel(BoosterHandle handle, const char* fname) {
+  return guarded([&] {
+    const std::string path = fname ? fname : "";
+    std::FILE* f = std::fopen(path.c_str(), "rb");
+    xgbb::require(f != nullptr, "Cannot read model file: " + path);
+    std::string bytes;
+    char buf[1 << 16];
+    size_t n;
+    while ((n = std::fread(buf, 1, sizeof buf, f)) > 0) bytes.append(buf, n);
+    std::fclose(f);
+    load_model_bytes(booster(handle), bytes.data(), bytes.size());
+  });
+}
+
+XGB_DLL int XGBoosterSaveModelToBuffer(BoosterHandle handle, char const* config, bst_ulong* out_len,
+                                       char const** out_dptr) {
+  return guarded([&] {
+    std::string format = "ubj";
+    if (config && *config) {
+      Json c = Json::parse(config);
+      if (auto* f = c.find("format")) format = f->str;
+    }
+    results.str = model_bytes(booster(handle), format);
+    *out_len = results.str.size();
+    *out_dptr = results.str.data();
+  });
+}
+
+XGB_DLL int XGBoosterLoadModelFromBuffer(BoosterHandle handle, const void* buf, bst_ulong len) {
+  return guarded([&] { load_model_bytes(booster(handle), buf, size_t(len)); });
 }
 
 XGB_DLL int XGBoosterSaveJsonConfig(BoosterHandle handle, bst_ulong* out_len, char const** out_str) {

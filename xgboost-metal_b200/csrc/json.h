@@ -45,6 +45,11 @@ struct Json {
 
   static Json parse(const std::string& text);
   std::string dump() const;
+  // Universal Binary JSON (the binary model format of upstream XGBoost):
+  // numeric arrays are written as typed arrays (float32 when any element is
+  // fractional, else int32/int64); typed and untyped containers are read.
+  std::string dump_ubj() const;
+  static Json parse_ubj(const void* data, size_t size);
 };
 
 }  // namespace xgbb

@@ -7,6 +7,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
 #include <cstring>
 #include <sstream>
 
@@ -266,8 +267,21 @@ struct Booster::TrainState {
 
 Booster::Booster(std::vector<std::shared_ptr<DMatrix>> cache) {
   for (auto& d : cache) cache_.push_back(d);
-  XGBB_CUDA(cudaGetDevice(&device_));
-  XGBB_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+  // The device current at creation trains this booster. Without a GPU a
+  // booster still loads, saves and describes models; training and
+  // prediction then fail with a clear error.
+  int n = 0;
+  if (cudaGetDeviceCount(&n) == cudaSuccess && n > 0) {
+    XGBB_CUDA(cudaGetDevice(&device_));
+    XGBB_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+  } else {
+    cudaGetLastError();
+  }
+}
+
+void Booster::gpu() {
+  require(stream_ != nullptr, "No CUDA device is available; this library trains on CUDA GPUs only.");
+  XGBB_CUDA(cudaSetDevice(device_));
 }
 
 Booster::~Booster() {
@@ -850,7 +864,7 @@ void Booster::finish_pending() {
 }
 
 void Booster::update(const std::shared_ptr<DMatrix>& d, int) {
-  XGBB_CUDA(cudaSetDevice(device_));
+  gpu();
   configure();
   d->upload_info(stream_);
   require(d->labels.size() == d->rows, "Labels must be provided for training.");
@@ -863,7 +877,7 @@ void Booster::update(const std::shared_ptr<DMatrix>& d, int) {
 }
 
 void Booster::sync() {
-  wait_stream("the booster's work");
+  if (stream_) wait_stream("the booster's work");
   finish_pending();
 }
 
@@ -876,6 +890,7 @@ void Booster::wait_stream(const char* what) {
 }
 
 void Booster::record_event(int slot) {
+  gpu();
   require(slot >= 0 && slot < 64, "event slot out of range");
   if (user_events_.size() <= size_t(slot)) user_events_.resize(size_t(slot) + 1, nullptr);
   if (!user_events_[slot]) XGBB_CUDA(cudaEventCreate(&user_events_[slot]));
@@ -893,7 +908,7 @@ float Booster::elapsed_ms(int a, int b) {
 
 std::vector<float> Booster::predict(const std::shared_ptr<DMatrix>& dp, bool output_margin,
                                     uint32_t begin, uint32_t end, bool, std::vector<uint64_t>& shape) {
-  XGBB_CUDA(cudaSetDevice(device_));
+  gpu();
   configure();
   finish_pending();
   DMatrix& d = *dp;
@@ -942,6 +957,292 @@ std::vector<float> Booster::predict(const std::shared_ptr<DMatrix>& dp, bool out
   if (G > 1) shape = {d.rows, G};
   else shape = {d.rows};
   return out;
+}
+
+// ---------------------------------------------------------------------------
+// Model files: upstream XGBoost's JSON model schema (the one the reference
+// writes, src/model.cpp:28-78, and reads, src/model.cpp:79-240): per tree the
+// node arrays, with leaves as split_conditions, and the learner's base score,
+// objective and feature count.
+// ---------------------------------------------------------------------------
+namespace {
+Json jnum(const std::string& text) {
+  Json v;
+  v.kind = Json::Number;
+  v.str = text;
+  v.num = std::strtod(text.c_str(), nullptr);
+  return v;
+}
+Json jnum(int64_t x) { return jnum(std::to_string(x)); }
+// The shortest decimal that reads back as the same float32.
+Json jfloat(float x) {
+  if (!std::isfinite(x)) x = 0.0f;
+  char buf[32];
+  for (int digits = 6; digits <= 9; ++digits) {
+    std::snprintf(buf, sizeof buf, "%.*g", digits, double(x));
+    if (std::strtof(buf, nullptr) == x) break;
+  }
+  return jnum(buf);
+}
+Json jstr(const std::string& x) {
+  Json v;
+  v.kind = Json::String;
+  v.str = x;
+  return v;
+}
+Json jarr() {
+  Json v;
+  v.kind = Json::Array;
+  return v;
+}
+Json jobj() {
+  Json v;
+  v.kind = Json::Object;
+  return v;
+}
+float jf(const Json& v) {
+  if (v.kind == Json::String) return std::strtof(v.str.c_str(), nullptr);
+  require(v.kind == Json::Number, "Model contains a non-numeric value.");
+  return std::strtof(v.str.c_str(), nullptr);
+}
+int64_t ji(const Json& v) {
+  if (v.kind == Json::String) return std::stoll(v.str);
+  if (v.kind == Json::Bool) return v.b ? 1 : 0;
+  require(v.kind == Json::Number, "Model contains a non-numeric value.");
+  return int64_t(v.num);
+}
+const char* objective_name(int objective) {
+  switch (objective) {
+    case kLogistic: return "binary:logistic";
+    case kLogitRaw: return "binary:logitraw";
+    case kSoftprob: return "multi:softprob";
+    case kSoftmax: return "multi:softmax";
+    default: return "reg:squarederror";
+  }
+}
+}  // namespace
+
+std::string Booster::save_json() {
+  sync();
+  configure();
+  const uint32_t G = groups_;
+  Json trees = jarr(), info = jarr(), indptr = jarr();
+  for (size_t t = 0; t < trees_.size(); ++t) {
+    const HostTree& tree = trees_[t];
+    Json left = jarr(), right = jarr(), parents = jarr(), idx = jarr(), cond = jarr(), dl = jarr(),
+         gain = jarr(), hess = jarr(), bw = jarr(), stype = jarr();
+    for (size_t i = 0; i < tree.nodes.size(); ++i) {
+      const DevNode& n = tree.nodes[i];
+      const bool leaf = n.left < 0;
+      left.arr.push_back(jnum(leaf ? -1 : n.left));
+      right.arr.push_back(jnum(leaf ? -1 : n.right));
+      parents.arr.push_back(jnum(i == 0 ? 2147483647 : n.parent));
+      idx.arr.push_back(jnum(leaf ? 0 : n.feature));
+      cond.arr.push_back(jfloat(leaf ? n.leaf : n.threshold));
+      dl.arr.push_back(jnum(leaf ? 0 : int64_t(n.default_left != 0)));
+      gain.arr.push_back(jfloat(leaf ? 0.0f : n.gain));
+      hess.arr.push_back(jfloat(n.cover));
+      bw.arr.push_back(jfloat(n.base_weight));
+      stype.arr.push_back(jnum(0));
+    }
+    Json tp = jobj();
+    tp.obj.emplace_back("num_deleted", jstr("0"));
+    tp.obj.emplace_back("num_feature", jstr(std::to_string(num_feature_)));
+    tp.obj.emplace_back("num_nodes", jstr(std::to_string(tree.nodes.size())));
+    tp.obj.emplace_back("size_leaf_vector", jstr("1"));
+    Json tj = jobj();
+    tj.obj.emplace_back("base_weights", bw);
+    for (const char* empty : {"categories", "categories_nodes", "categories_segments", "categories_sizes"})
+      tj.obj.emplace_back(empty, jarr());
+    tj.obj.emplace_back("default_left", dl);
+    tj.obj.emplace_back("id", jnum(int64_t(t)));
+    tj.obj.emplace_back("left_children", left);
+    tj.obj.emplace_back("loss_changes", gain);
+    tj.obj.emplace_back("parents", parents);
+    tj.obj.emplace_back("right_children", right);
+    tj.obj.emplace_back("split_conditions", cond);
+    tj.obj.emplace_back("split_indices", idx);
+    tj.obj.emplace_back("split_type", stype);
+    tj.obj.emplace_back("sum_hessian", hess);
+    tj.obj.emplace_back("tree_param", tp);
+    trees.arr.push_back(tj);
+    info.arr.push_back(jnum(tree.group));
+  }
+  for (size_t r = 0; r <= trees_.size() / std::max<uint32_t>(G, 1); ++r) indptr.arr.push_back(jnum(int64_t(r * G)));
+  Json gbp = jobj();
+  gbp.obj.emplace_back("num_parallel_tree", jstr("1"));
+  gbp.obj.emplace_back("num_trees", jstr(std::to_string(trees_.size())));
+  Json model = jobj();
+  model.obj.emplace_back("gbtree_model_param", gbp);
+  model.obj.emplace_back("iteration_indptr", indptr);
+  model.obj.emplace_back("tree_info", info);
+  model.obj.emplace_back("trees", trees);
+  Json gb = jobj();
+  gb.obj.emplace_back("model", model);
+  gb.obj.emplace_back("name", jstr("gbtree"));
+  std::string bs = "[";
+  const std::vector<float> scores = initialized_ ? base_score_ : std::vector<float>(G, 0.5f);
+  for (size_t k = 0; k < scores.size(); ++k) {
+    if (k) bs += ",";
+    bs += jfloat(scores[k]).str;
+  }
+  bs += "]";
+  const bool multi = objective_ == kSoftprob || objective_ == kSoftmax;
+  Json mp = jobj();
+  mp.obj.emplace_back("base_score", jstr(bs));
+  mp.obj.emplace_back("boost_from_average", jstr(params_.count("base_score") ? "0" : "1"));
+  mp.obj.emplace_back("num_class", jstr(multi ? std::to_string(G) : "0"));
+  mp.obj.emplace_back("num_feature", jstr(std::to_string(num_feature_)));
+  mp.obj.emplace_back("num_target", jstr("1"));
+  Json obj = jobj();
+  obj.obj.emplace_back("name", jstr(objective_name(objective_)));
+  if (multi) {
+    Json smp = jobj();
+    smp.obj.emplace_back("num_class", jstr(std::to_string(G)));
+    obj.obj.emplace_back("softmax_multiclass_param", smp);
+  } else {
+    Json rlp = jobj();
+    rlp.obj.emplace_back("scale_pos_weight", jstr(jfloat(spw_).str));
+    obj.obj.emplace_back("reg_loss_param", rlp);
+  }
+  Json attributes = jobj();
+  for (auto& kv : attrs) attributes.obj.emplace_back(kv.first, jstr(kv.second));
+  Json names = jarr(), types = jarr();
+  if (auto it = feature_info.find("feature_name"); it != feature_info.end())
+    for (auto& x : it->second) names.arr.push_back(jstr(x));
+  if (auto it = feature_info.find("feature_type"); it != feature_info.end())
+    for (auto& x : it->second) types.arr.push_back(jstr(x));
+  Json learner = jobj();
+  learner.obj.emplace_back("attributes", attributes);
+  learner.obj.emplace_back("feature_names", names);
+  learner.obj.emplace_back("feature_types", types);
+  learner.obj.emplace_back("gradient_booster", gb);
+  learner.obj.emplace_back("learner_model_param", mp);
+  learner.obj.emplace_back("objective", obj);
+  Json version = jarr();
+  for (int v : {3, 5, 0}) version.arr.push_back(jnum(v));
+  Json root = jobj();
+  root.obj.emplace_back("learner", learner);
+  root.obj.emplace_back("version", version);
+  return root.dump();
+}
+
+void Booster::load_json(const std::string& text) {
+  sync();
+  const Json root = Json::parse(text);
+  const Json& learner = root.at("learner");
+  const Json& gb = learner.at("gradient_booster");
+  require(gb.at("name").str == "gbtree", "Only gbtree models are supported: " + gb.at("name").str);
+  const Json& mp = learner.at("learner_model_param");
+  const std::string objective = learner.at("objective").at("name").str;
+  const uint32_t nf = uint32_t(ji(mp.at("num_feature")));
+  const uint32_t nc = uint32_t(ji(mp.at("num_class")));
+  require(!mp.find("num_target") || ji(mp.at("num_target")) <= 1, "Multi-target models are not supported.");
+  // Objective and class count decide the output groups, as in training.
+  std::map<std::string, std::string> params = params_;
+  params["objective"] = objective;
+  if (nc > 1) params["num_class"] = std::to_string(nc);
+  else params.erase("num_class");
+  if (const Json* o = learner.at("objective").find("reg_loss_param"))
+    if (const Json* w = o->find("scale_pos_weight")) params["scale_pos_weight"] = w->str;
+  params_ = params;
+  configured_ = false;
+  configure();
+  const uint32_t G = groups_;
+  // Base score: a number, or an array written as a string.
+  std::vector<float> scores;
+  const Json& bsj = mp.at("base_score");
+  if (bsj.kind == Json::String && !bsj.str.empty() && bsj.str[0] == '[') {
+    for (const Json& v : Json::parse(bsj.str).arr) scores.push_back(jf(v));
+  } else {
+    scores.push_back(jf(bsj));
+  }
+  if (scores.size() == 1) scores.resize(G, scores[0]);
+  require(scores.size() == G, "Invalid base_score shape in model.");
+  const Json& model = gb.at("model");
+  const Json& trees = model.at("trees");
+  const Json& info = model.at("tree_info");
+  require(info.arr.size() == trees.arr.size(), "Invalid tree_info length.");
+  require(ji(model.at("gbtree_model_param").at("num_parallel_tree")) == 1, "num_parallel_tree > 1 is not supported.");
+  require(trees.arr.size() % G == 0, "Invalid model tree count.");
+  std::vector<HostTree> loaded;
+  for (size_t t = 0; t < trees.arr.size(); ++t) {
+    const Json& tj = trees.arr[t];
+    const size_t n = size_t(ji(tj.at("tree_param").at("num_nodes")));
+    require(n >= 1, "A tree must have a root node.");
+    require(ji(tj.at("tree_param").at("size_leaf_vector")) <= 1, "Vector-leaf trees are not supported.");
+    for (const char* f : {"left_children", "right_children", "parents", "split_indices", "split_conditions",
+                          "default_left", "loss_changes", "sum_hessian"})
+      require(tj.at(f).arr.size() == n, "Inconsistent node-array length in model.");
+    if (const Json* st = tj.find("split_type"))
+      for (const Json& v : st->arr) require(ji(v) == 0, "Categorical splits are not supported.");
+    HostTree tree;
+    tree.group = uint32_t(ji(info.arr[t]));
+    require(tree.group < G, "Tree output group is out of range.");
+    const Json* bw = tj.find("base_weights");
+    tree.nodes.resize(n);
+    for (size_t i = 0; i < n; ++i) {
+      DevNode& d = tree.nodes[i];
+      d = DevNode{};
+      d.left = int32_t(ji(tj.at("left_children").arr[i]));
+      d.right = int32_t(ji(tj.at("right_children").arr[i]));
+      d.parent = i == 0 ? -1 : int32_t(ji(tj.at("parents").arr[i]));
+      const bool leaf = d.left < 0;
+      d.feature = leaf ? -1 : int32_t(ji(tj.at("split_indices").arr[i]));
+      d.split_bin = -1;
+      d.default_left = leaf ? 0u : uint32_t(ji(tj.at("default_left").arr[i]) != 0);
+      const float c = jf(tj.at("split_conditions").arr[i]);
+      d.threshold = leaf ? 0.0f : c;
+      d.leaf = leaf ? c : 0.0f;
+      d.cover = jf(tj.at("sum_hessian").arr[i]);
+      d.gain = jf(tj.at("loss_changes").arr[i]);
+      d.base_weight = bw && bw->arr.size() == n ? jf(bw->arr[i]) : d.leaf;
+      d.flags = leaf ? 1u : 3u;
+      if (leaf) {
+        require(d.right < 0, "Invalid leaf in model.");
+      } else {
+        require(d.right >= 0 && size_t(d.left) < n && size_t(d.right) < n && d.left != int32_t(i) &&
+                    d.right != int32_t(i) && d.feature >= 0 && uint32_t(d.feature) < nf,
+                "Model contains an out-of-range tree index.");
+      }
+    }
+    // Every node reachable once from the root, depth bounded.
+    std::vector<uint8_t> seen(n, 0);
+    std::vector<std::pair<int32_t, uint32_t>> stack{{0, 0}};
+    while (!stack.empty()) {
+      auto [id, depth] = stack.back();
+      stack.pop_back();
+      require(depth <= 1024 && !seen[size_t(id)], "Model contains a cyclic or excessively deep tree.");
+      seen[size_t(id)] = 1;
+      if (tree.nodes[size_t(id)].left >= 0) {
+        stack.push_back({tree.nodes[size_t(id)].left, depth + 1});
+        stack.push_back({tree.nodes[size_t(id)].right, depth + 1});
+      }
+    }
+    loaded.push_back(std::move(tree));
+  }
+  // The model replaces this booster's model; its training state is dropped.
+  state_.reset();
+  trees_ = std::move(loaded);
+  rounds_ = uint32_t(trees_.size() / G);
+  num_feature_ = nf;
+  base_score_ = scores;
+  base_margin_ = scores;
+  if (objective_ == kLogistic) {
+    for (uint32_t k = 0; k < G; ++k) {
+      const float v = std::min(std::max(base_score_[k], 1.0e-6f), 1.0f - 1.0e-6f);
+      base_margin_[k] = -std::log(1.0f / v - 1.0f);
+    }
+  }
+  initialized_ = true;
+  attrs.clear();
+  if (const Json* a = learner.find("attributes"))
+    for (auto& kv : a->obj) attrs[kv.first] = kv.second.str;
+  feature_info.clear();
+  if (const Json* f = learner.find("feature_names"); f && !f->arr.empty())
+    for (const Json& x : f->arr) feature_info["feature_name"].push_back(x.str);
+  if (const Json* f = learner.find("feature_types"); f && !f->arr.empty())
+    for (const Json& x : f->arr) feature_info["feature_type"].push_back(x.str);
 }
 
 std::string Booster::config_json() const {

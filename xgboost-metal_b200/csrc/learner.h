@@ -138,6 +138,7 @@ class Booster {
   TrainState& train_state(const std::shared_ptr<DMatrix>& d);
   void run_round(TrainState& ts);
   void finish_round(TrainState& ts);
+  void gpu();  // makes the booster's device current; fails without a GPU
   void wait_stream(const char* what);
   void record_tree_launches(TrainState& ts, uint32_t group, cudaStream_t stream, bool capturing,
                             uint32_t parity);

@@ -214,7 +214,7 @@ class Booster:
                 continue
             self.set_param(k, v)
         if model_file is not None:
-            raise XGBoostError("Model loading is not implemented by the CUDA backend yet.")
+            self.load_model(model_file)
 
     def __del__(self):
         if _LIB is not None and getattr(self, "handle", None) is not None and self.handle.value:
@@ -322,8 +322,51 @@ class Booster:
                                                ctypes.byref(ms)))
         return ms.value
 
+    # -- model files (python-package/xgboost/core.py save_model / load_model /
+    # save_raw in the reference): upstream XGBoost's JSON schema, as text or
+    # as Universal Binary JSON.
+    def save_model(self, fname):
+        """Saves the model: JSON when the file name ends in ".json", else UBJSON."""
+        _check_call(_LIB.XGBoosterSaveModel(self.handle, _c_str(os.fspath(fname))))
+
+    def save_raw(self, raw_format="ubj"):
+        """The model as bytes ("json" or "ubj")."""
+        length = c_bst_ulong()
+        out = ctypes.c_char_p()
+        _check_call(_LIB.XGBoosterSaveModelToBuffer(
+            self.handle, _c_str(json.dumps({"format": raw_format})), ctypes.byref(length),
+            ctypes.byref(out)))
+        return bytearray(ctypes.string_at(out, length.value))
+
+    def load_model(self, fname):
+        """Loads a model from a file name or from the bytes of save_raw."""
+        if isinstance(fname, (bytes, bytearray, memoryview)):
+            buf = bytes(fname)
+            _check_call(_LIB.XGBoosterLoadModelFromBuffer(self.handle, ctypes.c_char_p(buf),
+                                                          c_bst_ulong(len(buf))))
+        else:
+            _check_call(_LIB.XGBoosterLoadModel(self.handle, _c_str(os.fspath(fname))))
+
+    def __getstate__(self):
+        return {"raw": bytes(self.save_raw("ubj")), "feature_names": self.feature_names,
+                "feature_types": self.feature_types}
+
+    def __setstate__(self, state):
+        self.handle = ctypes.c_void_p()
+        _check_call(_LIB.XGBoosterCreate(None, c_bst_ulong(0), ctypes.byref(self.handle)))
+        self._cache = []
+        self.feature_names = state.get("feature_names")
+        self.feature_types = state.get("feature_types")
+        self.load_model(state["raw"])
+
     def copy(self):
-        raise XGBoostError("Booster copies are not implemented by the CUDA backend yet.")
+        return Booster(model_file=self.save_raw("ubj"))
+
+    def __copy__(self):
+        return self.copy()
+
+    def __deepcopy__(self, memo):
+        return self.copy()
 
 
 def synchronize():

@@ -1,8 +1,10 @@
 """Scikit-learn estimators (python-package/xgboost/sklearn.py in the
 reference): XGBRegressor and XGBClassifier over train()."""
+import json
+
 import numpy as np
 
-from .core import DMatrix, XGBoostError
+from .core import Booster, DMatrix, XGBoostError
 from .training import train
 
 __all__ = ["XGBModel", "XGBRegressor", "XGBClassifier"]
@@ -59,6 +61,31 @@ class XGBModel:
         if self._Booster is None:
             raise XGBoostError("need to call fit or load_model beforehand")
         return self._Booster
+
+    # Model files (python-package/xgboost/sklearn.py save_model / load_model):
+    # the estimator's own attributes travel in the model's "scikit_learn"
+    # attribute.
+    def save_model(self, fname):
+        meta = {"n_features_in_": getattr(self, "n_features_in_", None)}
+        if hasattr(self, "classes_"):
+            meta["classes_"] = np.asarray(self.classes_).tolist()
+            meta["n_classes_"] = int(self.n_classes_)
+        booster = self.get_booster()
+        booster.set_attr(scikit_learn=json.dumps(meta))
+        booster.save_model(fname)
+        booster.set_attr(scikit_learn=None)
+
+    def load_model(self, fname):
+        self._Booster = Booster(model_file=fname)
+        meta = self._Booster.attr("scikit_learn")
+        if meta:
+            meta = json.loads(meta)
+            if meta.get("n_features_in_") is not None:
+                self.n_features_in_ = meta["n_features_in_"]
+            if "classes_" in meta:
+                self.classes_ = np.asarray(meta["classes_"])
+                self.n_classes_ = meta["n_classes_"]
+            self._Booster.set_attr(scikit_learn=None)
 
     def _fit(self, X, y, sample_weight, eval_set, verbose, params):
         dtrain = DMatrix(X, y, weight=sample_weight,
