@@ -5,7 +5,11 @@
 //   gradient_kernel      kernels/boost.metal:553-601
 //   mass_*/scales        kernels/gradient_quantization.metal.h:1-67
 //   hist_kernel          kernels/boost.metal:700-733, histogram_missing.metal.h
-//   eval_kernel          kernels/boost.metal:902-1005 (+ subtraction :780-794)
+//   hist2_kernel         the same sums, staged two-limb form (limbs_kernel
+//                        forms each row's values once per tree)
+//   eval_kernel          kernels/boost.metal:902-1005 (+ subtraction :780-794);
+//                        pack_best / merge_best select across ranks
+//   transpose_codes_kernel, narrow_codes_kernel: layouts of the same codes
 //   control_kernel       kernels/boost.metal:1245-1265, tree_driver.metal.h:28-94,
 //                        src/tree.cpp:1663-1717 (node table replay)
 //   partition_kernel     kernels/boost.metal:1325-1329, 1383-1389, 1738-1765
