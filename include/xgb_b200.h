@@ -37,6 +37,12 @@ XGB_DLL int XGBoosterEventElapsed(BoosterHandle handle, int a, int b, float* ms)
  * Matrix::quantize (src/data.cpp:1210-1306). */
 XGB_DLL int XGBBQuantizeHost(const float* X, bst_ulong rows, bst_ulong cols, uint32_t max_bin,
                              float* cuts, uint32_t* counts, float* minima, uint32_t* bins);
+/* Cuts (cuts[f * min(max_bin, rows) + i]), counts and minima of X [rows][cols]
+ * from the host sketch alone, with `threads` workers (0 = all cores): the
+ * reference's Matrix::make_quantile_cuts (src/quantile.cpp:22-213). Needs no
+ * GPU. */
+XGB_DLL int XGBBSketchHost(const float* X, bst_ulong rows, bst_ulong cols, const float* weights,
+                           uint32_t max_bin, int threads, float* cuts, uint32_t* counts, float* minima);
 /* Gradient pairs [groups][rows][2] and power-of-two scales [groups][2]: the
  * reference's gradients + gradient_partial_sums + gradient_scales
  * (kernels/boost.metal:553-601, kernels/gradient_quantization.metal.h:1-67). */

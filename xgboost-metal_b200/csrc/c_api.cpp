@@ -682,6 +682,16 @@ XGB_DLL int XGBBQuantizeHost(const float* X, bst_ulong rows, bst_ulong cols, uin
   });
 }
 
+// Test entry: the host quantile sketch on its own (no device needed).
+XGB_DLL int XGBBSketchHost(const float* X, bst_ulong rows, bst_ulong cols, const float* weights,
+                           uint32_t max_bin, int threads, float* cuts, uint32_t* counts, float* minima) {
+  return guarded([&] {
+    xgbb::require(rows < (1ull << 32) && cols < (1ull << 32), "matrix too large");
+    xgbb::require(max_bin >= 2 && max_bin <= xgbb::kMaxBins, "max_bin must be in [2, 256]");
+    xgbb::sketch_cuts(X, uint32_t(rows), uint32_t(cols), weights, max_bin, cuts, counts, minima, threads);
+  });
+}
+
 // Test entry: gradient pairs [groups][rows] and scales [groups][2] for margins
 // [rows][groups] through the product's gradient and exact-scale kernels.
 XGB_DLL int XGBBGradientsHost(int objective, const float* margins, const float* labels,
