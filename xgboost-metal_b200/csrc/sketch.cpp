@@ -10,12 +10,15 @@
 // queries otherwise, then max + (|max| + 1e-5)). Entries are plain IEEE
 // binary32 with gradual underflow; -0 is read as +0, and ties keep row order.
 //
-// This first version runs on the host, one feature per worker thread; the
-// cuts it produces decide every bin, so they are compared exactly against the
-// checker in the tests.
+// It runs on the host. Workers take blocks of features: one sequential pass
+// over the rows copies a block's columns into contiguous buffers (each cache
+// line of the row-major matrix is read once per block, not once per
+// feature), then each column is summarised. The cuts decide every bin, so
+// they are compared exactly against the checker in the tests.
 #include "sketch.h"
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstring>
 #include <thread>
@@ -40,6 +43,43 @@ uint32_t budget_for(uint32_t bins, uint32_t count) {
     if ((uint64_t{1} << level) * limit >= count) return uint32_t(limit);
   }
   return count;
+}
+
+// Stable sort of runs by value: an LSD radix sort on order-preserving keys
+// (the sign bit flipped for positives, all bits for negatives), which orders
+// every non-NaN float as `<` does (-0 never occurs: it is read as +0) and
+// keeps equal values in their input order, as std::stable_sort would. Passes
+// in which every key has the same digit are skipped.
+inline uint32_t order_key(float v) {
+  uint32_t b;
+  std::memcpy(&b, &v, 4);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+void sort_runs(Run* a, size_t n, std::vector<Run>& tmp, std::vector<uint32_t>& keys,
+               std::vector<uint32_t>& keys_tmp) {
+  if (n < 2) return;
+  tmp.resize(n);
+  keys.resize(n);
+  keys_tmp.resize(n);
+  for (size_t i = 0; i < n; ++i) keys[i] = order_key(a[i].v);
+  Run* src = a;
+  Run* dst = tmp.data();
+  uint32_t* ks = keys.data();
+  uint32_t* kd = keys_tmp.data();
+  for (int shift = 0; shift < 32; shift += 8) {
+    uint32_t hist[257] = {0};
+    for (size_t i = 0; i < n; ++i) ++hist[((ks[i] >> shift) & 0xffu) + 1];
+    if (hist[((ks[0] >> shift) & 0xffu) + 1] == n) continue;  // one digit: order unchanged
+    for (int d = 0; d < 256; ++d) hist[d + 1] += hist[d];
+    for (size_t i = 0; i < n; ++i) {
+      const uint32_t pos = hist[(ks[i] >> shift) & 0xffu]++;
+      dst[pos] = src[i];
+      kd[pos] = ks[i];
+    }
+    std::swap(src, dst);
+    std::swap(ks, kd);
+  }
+  if (src != a) std::copy(src, src + n, a);
 }
 
 inline float lower_next(const Entry& e) { return e.rmin + e.wmin; }
@@ -136,15 +176,16 @@ uint64_t bits64(double v) {
   return b;
 }
 
-void one_feature(const float* X, uint32_t rows, uint32_t cols, uint32_t f, const float* weights,
-                 uint32_t max_bin, float* out, uint32_t* count_out, float* minimum) {
+// One feature's cuts from its column `col` (contiguous, `rows` values).
+void one_feature(const float* col, uint32_t rows, const float* weights, uint32_t max_bin, float* out,
+                 uint32_t* count_out, float* minimum) {
   const bool unit = weights == nullptr;
   std::vector<Run> runs;
   runs.reserve(rows);
   uint32_t elements = 0, nonmissing = 0;
   float previous = 0;
   for (uint32_t r = 0; r < rows; ++r) {
-    float v = X[size_t(r) * cols + f];
+    float v = col[r];
     const float w = unit ? 1.0f : weights[r];
     nonmissing += !std::isnan(v);
     uint32_t wb;
@@ -172,11 +213,13 @@ void one_feature(const float* X, uint32_t rows, uint32_t cols, uint32_t f, const
   std::vector<Entry> resident(size_t(limit) * levels), current(2 * size_t(limit) + 1),
       scratch(2 * size_t(limit) + 1), summary(capacity + 1);
   uint32_t counts[64] = {0};
+  std::vector<Run> sort_tmp;
+  std::vector<uint32_t> sort_keys, sort_keys_tmp;
   for (uint32_t batch = 0; batch < nbatch; ++batch) {
     const uint64_t begin = batch * capacity;
     const uint32_t size = uint32_t(std::min<uint64_t>(capacity, nruns - begin));
     Run* src = runs.data() + begin;
-    std::stable_sort(src, src + size, [](const Run& a, const Run& b) { return a.v < b.v; });
+    sort_runs(src, size, sort_tmp, sort_keys, sort_keys_tmp);
     uint32_t n = 0;
     float total = 0;
     for (uint32_t i = 0; i < size;) {
@@ -260,12 +303,27 @@ void sketch_cuts(const float* X, uint32_t rows, uint32_t cols, const float* weig
   std::fill(cuts, cuts + size_t(cols) * stride, 0.0f);
   if (threads <= 0) threads = int(std::max(1u, std::thread::hardware_concurrency()));
   threads = int(std::min<uint32_t>(uint32_t(threads), std::max(1u, cols)));
+  // Blocks of up to 16 features (one 64-byte line of a row), fewer when there
+  // are few features per worker, handed out by a shared counter.
+  const uint32_t block = std::max(1u, std::min(16u, cols / uint32_t(threads)));
+  const uint32_t nblocks = (cols + block - 1) / block;
+  std::atomic<uint32_t> next{0};
   std::vector<std::thread> pool;
   for (int t = 0; t < threads; ++t)
-    pool.emplace_back([=] {
-      for (uint32_t f = uint32_t(t); f < cols; f += uint32_t(threads))
-        one_feature(X, rows, cols, f, weights, max_bin, cuts + size_t(f) * stride, counts + f,
-                    minima + f);
+    pool.emplace_back([&] {
+      std::vector<float> buf(size_t(block) * rows);
+      for (uint32_t b = next++; b < nblocks; b = next++) {
+        const uint32_t f0 = b * block, nf = std::min(block, cols - f0);
+        for (uint32_t r = 0; r < rows; ++r) {
+          const float* row = X + size_t(r) * cols + f0;
+          for (uint32_t j = 0; j < nf; ++j) buf[size_t(j) * rows + r] = row[j];
+        }
+        for (uint32_t j = 0; j < nf; ++j) {
+          const uint32_t f = f0 + j;
+          one_feature(buf.data() + size_t(j) * rows, rows, weights, max_bin, cuts + size_t(f) * stride,
+                      counts + f, minima + f);
+        }
+      }
     });
   for (auto& th : pool) th.join();
 }
