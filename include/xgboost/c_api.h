@@ -24,6 +24,29 @@
 typedef uint64_t bst_ulong;
 typedef void* DMatrixHandle;
 typedef void* BoosterHandle;
+/* include/xgboost/c_api.h:371-474: the caller's batch iterator. */
+typedef void* DataIterHandle;
+typedef int XGDMatrixCallbackNext(DataIterHandle iter);
+typedef void DataIterResetCallback(DataIterHandle handle);
+
+/* include/xgboost/c_api.h:1865-1875: a strided 1-D or 2-D host buffer.
+ * dtype_code: 1 f32, 2 f64, 3 f16, 4 bf16, 5 i8, 6 i16, 7 i32, 8 i64, 9 u8,
+ * 10 u16, 11 u32, 12 u64, 13 bool bytes, 14 LSB-first bits (one column).
+ * flags: bit 0 C-contiguous (strides ignored), bit 1 zero copy preferred,
+ * bit 2 strides[0] = first bit of a bit buffer. mask_mode (one entry per
+ * row, from mask_bit_offset): 0 none, 1 LSB-first valid bits, 2 nonzero
+ * bytes valid, 3 nonzero bytes invalid; invalid rows read as missing. */
+typedef struct {
+  const void* data;
+  uint64_t shape[2];
+  int64_t strides[2];
+  uint32_t ndim;
+  uint32_t dtype_code;
+  const void* mask_data;
+  int64_t mask_bit_offset;
+  uint32_t mask_mode;
+  uint32_t flags;
+} XGBufferDescriptor;
 
 /* --- library ------------------------------------------------------------ */
 /* include/xgboost/c_api.h:68 */
@@ -65,6 +88,30 @@ XGB_DLL int XGDMatrixNumRow(DMatrixHandle handle, bst_ulong* out);
 XGB_DLL int XGDMatrixNumCol(DMatrixHandle handle, bst_ulong* out);
 /* include/xgboost/c_api.h:919 */
 XGB_DLL int XGDMatrixNumNonMissing(DMatrixHandle handle, bst_ulong* out);
+/* include/xgboost/c_api.h:1877 (src/c_api.cpp:838-844). */
+XGB_DLL int XGDMatrixCreateFromBufferDescriptor(XGBufferDescriptor const* desc, float missing,
+                                                DMatrixHandle* out);
+/* include/xgboost/c_api.h:1881: fields as XGDMatrixSetInfoFromInterface. */
+XGB_DLL int XGDMatrixSetInfoFromBufferDescriptor(DMatrixHandle handle, char const* field,
+                                                 XGBufferDescriptor const* desc);
+/* include/xgboost/c_api.h:460: the batch holder filled by an iterator's next(). */
+XGB_DLL int XGProxyDMatrixCreate(DMatrixHandle* out);
+/* include/xgboost/c_api.h:622 */
+XGB_DLL int XGProxyDMatrixSetDataDense(DMatrixHandle handle, char const* data);
+/* include/xgboost/c_api.h:635 */
+XGB_DLL int XGProxyDMatrixSetDataCSR(DMatrixHandle handle, char const* indptr, char const* indices,
+                                     char const* data, bst_ulong ncol);
+/* include/xgboost/c_api.h:499 (src/c_api.cpp:140-157, 222-224): batches
+ * concatenated on the host; config {"missing"}. */
+XGB_DLL int XGDMatrixCreateFromCallback(DataIterHandle iter, DMatrixHandle proxy,
+                                        DataIterResetCallback* reset, XGDMatrixCallbackNext* next,
+                                        char const* config, DMatrixHandle* out);
+/* include/xgboost/c_api.h:535 (src/c_api.cpp:225-239): as above, then
+ * quantised on the GPU with the cuts of `ref` (a DMatrix handle) when given;
+ * config {"missing", "max_bin"}. */
+XGB_DLL int XGQuantileDMatrixCreateFromCallback(DataIterHandle iter, DMatrixHandle proxy, DataIterHandle ref,
+                                                DataIterResetCallback* reset, XGDMatrixCallbackNext* next,
+                                                char const* config, DMatrixHandle* out);
 
 /* --- Booster -------------------------------------------------------------- */
 /* include/xgboost/c_api.h:996 (src/c_api.cpp:442-452) */
@@ -92,6 +139,18 @@ XGB_DLL int XGBoosterPredictFromDMatrix(BoosterHandle handle, DMatrixHandle dmat
 XGB_DLL int XGBoosterPredict(BoosterHandle handle, DMatrixHandle dmat, int option_mask,
                              unsigned ntree_limit, int training, bst_ulong* out_len,
                              const float** out_result);
+/* include/xgboost/c_api.h:1234 (src/c_api.cpp:510-512): in-place prediction
+ * from a dense __array_interface__; config as XGBoosterPredictFromDMatrix plus
+ * "missing"; base margins from the proxy `m` when not NULL. */
+XGB_DLL int XGBoosterPredictFromDense(BoosterHandle handle, char const* values, char const* config,
+                                      DMatrixHandle m, bst_ulong const** out_shape, bst_ulong* out_dim,
+                                      const float** out_result);
+/* include/xgboost/c_api.h:1020: releases the training state; the model stays. */
+XGB_DLL int XGBoosterReset(BoosterHandle handle);
+/* include/xgboost/c_api.h:1035 (src/c_api.cpp:503-506): rounds begin, begin+step,
+ * ... < end (end 0 = all) as a new booster; -2 when out of range. */
+XGB_DLL int XGBoosterSlice(BoosterHandle handle, int begin_layer, int end_layer, int step,
+                           BoosterHandle* out);
 /* include/xgboost/c_api.h:1378. Loads a JSON or UBJSON model file (upstream XGBoost's schema). */
 XGB_DLL int XGBoosterLoadModel(BoosterHandle handle, const char* fname);
 /* include/xgboost/c_api.h:1387. JSON when the name ends in ".json", else UBJSON. */
@@ -103,6 +162,32 @@ XGB_DLL int XGBoosterSaveModelToBuffer(BoosterHandle handle, char const* config,
                                        char const** out_dptr);
 /* include/xgboost/c_api.h:1451 */
 XGB_DLL int XGBoosterSaveJsonConfig(BoosterHandle handle, bst_ulong* out_len, char const** out_str);
+/* include/xgboost/c_api.h:1461 (src/model.cpp:287-333). */
+XGB_DLL int XGBoosterLoadJsonConfig(BoosterHandle handle, char const* config);
+/* include/xgboost/c_api.h:1426: {"Config", "Model"} as UBJSON (pickling). */
+XGB_DLL int XGBoosterSerializeToBuffer(BoosterHandle handle, bst_ulong* out_len, char const** out_dptr);
+/* include/xgboost/c_api.h:1437 */
+XGB_DLL int XGBoosterUnserializeFromBuffer(BoosterHandle handle, const void* buf, bst_ulong len);
+/* include/xgboost/c_api.h:1473: text dump. */
+XGB_DLL int XGBoosterDumpModel(BoosterHandle handle, const char* fmap, int with_stats, bst_ulong* out_len,
+                               const char*** out_dump_array);
+/* include/xgboost/c_api.h:1486 (src/model.cpp:334-429): format "text", "json"
+ * or "dot"; fmap must be empty. */
+XGB_DLL int XGBoosterDumpModelEx(BoosterHandle handle, const char* fmap, int with_stats, const char* format,
+                                 bst_ulong* out_len, const char*** out_dump_array);
+/* include/xgboost/c_api.h:1501 */
+XGB_DLL int XGBoosterDumpModelWithFeatures(BoosterHandle handle, int fnum, const char** fname,
+                                           const char** ftype, int with_stats, bst_ulong* out_len,
+                                           const char*** out_models);
+/* include/xgboost/c_api.h:1517 */
+XGB_DLL int XGBoosterDumpModelExWithFeatures(BoosterHandle handle, int fnum, const char** fname,
+                                             const char** ftype, int with_stats, const char* format,
+                                             bst_ulong* out_len, const char*** out_models);
+/* include/xgboost/c_api.h:1633 (src/c_api.cpp:590-620): config
+ * {"importance_type", "feature_names"}; features used by a split only. */
+XGB_DLL int XGBoosterFeatureScore(BoosterHandle handle, const char* config, bst_ulong* out_n_features,
+                                  char const*** out_features, bst_ulong* out_dim,
+                                  bst_ulong const** out_shape, float const** out_scores);
 /* include/xgboost/c_api.h:1548 */
 XGB_DLL int XGBoosterGetAttr(BoosterHandle handle, const char* key, const char** out, int* success);
 /* include/xgboost/c_api.h:1558 */

@@ -17,6 +17,7 @@
 #include "comm.h"
 #include "json.h"
 #include "learner.h"
+#include "model_dump.h"
 #include "sketch.h"
 #include "xgb_b200.h"
 #include "xgboost/c_api.h"
@@ -126,6 +127,11 @@ double read_element(const ArrayView& a, const char* p) {
       break;
     case 'b':
       return *reinterpret_cast<const uint8_t*>(p) ? 1.0 : 0.0;
+    case 'B': {  // bfloat16: the upper half of a float32
+      uint16_t h; std::memcpy(&h, p, 2);
+      const uint32_t bits = uint32_t(h) << 16;
+      float v; std::memcpy(&v, &bits, 4); return v;
+    }
   }
   throw Error("Unsupported array dtype.");
 }
@@ -194,6 +200,89 @@ DMatrixHandle borrowed_dmatrix(const float* data, uint64_t rows, uint64_t cols) 
   d->host = data;
   d->validated = false;
   return new DMatrixPtr(std::move(d));
+}
+
+// XGBufferDescriptor (include/xgboost/c_api.h): a strided 1-D or 2-D buffer
+// of dtype_code 1 f32, 2 f64, 3 f16, 4 bf16, 5-8 i8..i64, 9-12 u8..u64,
+// 13 bool bytes, 14 LSB-first bits; flags bit 0 = C-contiguous (strides
+// ignored), bit 1 = zero copy preferred, bit 2 = strides[0] is the bit offset
+// of a bit buffer; an optional per-row validity mask (mask_mode 1 LSB-first
+// bits, 2 nonzero bytes = valid, 3 nonzero bytes = invalid). Rows masked
+// invalid read as missing. The reference's spec_from_descriptor and
+// ingest_strided_typed (src/c_api.cpp:657-690, kernels/boost.metal:256-306).
+struct DescriptorView {
+  const XGBufferDescriptor* d;
+  uint64_t rows = 0, cols = 0;
+  int64_t stride_r = 0, stride_c = 0, bit0 = 0;
+  ArrayView elem;
+};
+
+DescriptorView view_descriptor(const XGBufferDescriptor* d, bool two_d) {
+  require(d != nullptr, "Null buffer descriptor.");
+  if (two_d) require(d->ndim == 2, "Feature data must be two dimensional.");
+  else require(d->ndim == 1 || d->ndim == 2, "Buffer descriptor must be 1D or 2D.");
+  require(d->shape[0] <= 0xffffffffull && (d->ndim == 1 || d->shape[1] <= 0xffffffffull),
+          "Matrix dimension exceeds the 32-bit row or feature index range.");
+  require(d->dtype_code >= 1 && d->dtype_code <= 14, "Unsupported buffer dtype code.");
+  require(d->mask_mode <= 3, "Invalid buffer mask mode.");
+  static const char kinds[] = {0, 'f', 'f', 'f', 'B', 'i', 'i', 'i', 'i', 'u', 'u', 'u', 'u', 'b', 't'};
+  static const int widths[] = {0, 4, 8, 2, 2, 1, 2, 4, 8, 1, 2, 4, 8, 1, 0};
+  DescriptorView v{d};
+  v.rows = d->shape[0];
+  v.cols = d->ndim == 2 ? d->shape[1] : 1;
+  v.elem.kind = kinds[d->dtype_code];
+  v.elem.itemsize = widths[d->dtype_code];
+  const int64_t w = v.elem.itemsize;
+  if (d->dtype_code == 14) {
+    require(v.cols == 1, "Bit-packed boolean buffers must be 1D or single-column.");
+    v.bit0 = (d->flags & 4u) ? d->strides[0] : 0;
+    require(v.bit0 >= 0, "Invalid negative bit offset.");
+  } else if (d->flags & 1u) {
+    v.stride_c = d->ndim == 2 ? w : 0;
+    v.stride_r = d->ndim == 2 ? int64_t(v.cols) * w : w;
+  } else {
+    v.stride_r = d->strides[0];
+    v.stride_c = d->ndim == 2 ? d->strides[1] : 0;
+  }
+  if (v.rows * v.cols > 0) {
+    require(d->data != nullptr, "Null data pointer for a nonempty buffer.");
+    if (d->mask_mode != 0) {
+      require(d->mask_data != nullptr, "Null validity mask for a nonempty buffer.");
+      require(d->mask_bit_offset >= 0, "Invalid negative mask offset.");
+    }
+  }
+  return v;
+}
+
+bool descriptor_c_contiguous_f32(const DescriptorView& v) {
+  return v.d->dtype_code == 1 && v.d->mask_mode == 0 &&
+         (v.cols == 1 || v.stride_c == 4) && (v.rows <= 1 || v.stride_r == int64_t(v.cols) * 4);
+}
+
+std::vector<float> descriptor_floats(const DescriptorView& v) {
+  std::vector<float> out(size_t(v.rows * v.cols));
+  const char* base = static_cast<const char*>(v.d->data);
+  const auto* mask = static_cast<const uint8_t*>(v.d->mask_data);
+  const uint64_t moff = uint64_t(v.d->mask_bit_offset);
+  for (uint64_t r = 0; r < v.rows; ++r) {
+    bool valid = true;
+    if (v.d->mask_mode == 1) valid = (mask[(r + moff) >> 3] >> ((r + moff) & 7)) & 1u;
+    else if (v.d->mask_mode == 2) valid = mask[r + moff] != 0;
+    else if (v.d->mask_mode == 3) valid = mask[r + moff] == 0;
+    for (uint64_t c = 0; c < v.cols; ++c) {
+      float x = NAN;
+      if (valid) {
+        if (v.elem.kind == 't') {
+          const uint64_t bit = uint64_t(v.bit0) + r;
+          x = float((reinterpret_cast<const uint8_t*>(base)[bit >> 3] >> (bit & 7)) & 1u);
+        } else {
+          x = float(read_element(v.elem, base + int64_t(r) * v.stride_r + int64_t(c) * v.stride_c));
+        }
+      }
+      out[size_t(r * v.cols + c)] = x;
+    }
+  }
+  return out;
 }
 
 void set_info(xgbb::DMatrix& d, const std::string& field, std::vector<float> v) {
@@ -358,6 +447,150 @@ XGB_DLL int XGDMatrixNumNonMissing(DMatrixHandle handle, bst_ulong* out) {
   });
 }
 
+XGB_DLL int XGDMatrixCreateFromBufferDescriptor(XGBufferDescriptor const* desc, float missing,
+                                                DMatrixHandle* out) {
+  return guarded([&] {
+    require(out != nullptr, "Null output handle.");
+    const DescriptorView v = view_descriptor(desc, true);
+    // A float32 C-contiguous buffer offered for zero copy, with NaN as the
+    // missing value, is read in place.
+    if ((desc->flags & 2u) && descriptor_c_contiguous_f32(v) && std::isnan(missing)) {
+      *out = borrowed_dmatrix(static_cast<const float*>(desc->data), v.rows, v.cols);
+      return;
+    }
+    *out = new_dmatrix(descriptor_floats(v), v.rows, v.cols, missing);
+  });
+}
+
+XGB_DLL int XGDMatrixSetInfoFromBufferDescriptor(DMatrixHandle handle, char const* field,
+                                                 XGBufferDescriptor const* desc) {
+  return guarded([&] {
+    require(field != nullptr, "Null field name.");
+    set_info(*dmat(handle), field, descriptor_floats(view_descriptor(desc, false)));
+  });
+}
+
+// Streaming construction (the reference's from_iterator, src/c_api.cpp:140-157):
+// the caller's `next` callback fills the proxy with one batch at a time through
+// XGProxyDMatrixSetData* and XGDMatrixSetInfoFromInterface; the batches are
+// concatenated on the host into one matrix.
+XGB_DLL int XGProxyDMatrixCreate(DMatrixHandle* out) {
+  return guarded([&] {
+    require(out != nullptr, "Null output handle.");
+    *out = new DMatrixPtr(std::make_shared<xgbb::DMatrix>());
+  });
+}
+
+namespace {
+// Replaces the proxy's data and keeps its labels, weights and margins.
+void replace_proxy_data(DMatrixHandle proxy, DMatrixHandle fresh) {
+  DMatrixPtr& slot = dmat(proxy);
+  DMatrixPtr value = dmat(fresh);
+  delete static_cast<DMatrixPtr*>(fresh);
+  value->labels = std::move(slot->labels);
+  value->weights = std::move(slot->weights);
+  value->base_margin = std::move(slot->base_margin);
+  ++value->generation;
+  slot = std::move(value);
+}
+
+DMatrixPtr from_iterator(DataIterHandle iter, DMatrixHandle proxy, DataIterResetCallback* reset,
+                         XGDMatrixCallbackNext* next, const char* config) {
+  require(reset != nullptr && next != nullptr && proxy != nullptr, "Iterator callbacks and proxy must be provided.");
+  const float missing = config_missing(config);
+  std::vector<float> values, labels, weights, margins;
+  uint64_t rows = 0, cols = 0;
+  bool first = true;
+  int has_labels = -1, has_weights = -1, has_margins = -1;
+  reset(iter);
+  while (true) {
+    const int status = next(iter);
+    require(status >= 0, "Data iterator callback failed.");
+    if (!status) break;
+    const xgbb::DMatrix& b = *dmat(proxy);
+    require(b.host != nullptr || b.rows == 0, "A batch of the iterator has no data.");
+    if (first) cols = b.cols;
+    require(b.cols == cols, "Every batch must have the same number of features.");
+    // Every nonempty batch carries a field or none does.
+    auto append = [&](std::vector<float>& dst, int& present, const std::vector<float>& src, const char* name) {
+      if (b.rows == 0) return;
+      const int has = src.empty() ? 0 : 1;
+      if (present < 0) present = has;
+      require(present == has, std::string("Batches disagree on whether they carry ") + name + ".");
+      dst.insert(dst.end(), src.begin(), src.end());
+    };
+    append(labels, has_labels, b.labels, "labels");
+    append(weights, has_weights, b.weights, "weights");
+    append(margins, has_margins, b.base_margin, "base margins");
+    values.insert(values.end(), b.host, b.host + size_t(b.rows) * b.cols);
+    rows += b.rows;
+    first = false;
+  }
+  reset(iter);
+  require(cols > 0, "The iterator produced no feature data.");
+  DMatrixPtr out = dmat(new_dmatrix(std::move(values), rows, cols, missing));
+  if (!labels.empty()) set_info(*out, "label", std::move(labels));
+  if (!weights.empty()) set_info(*out, "weight", std::move(weights));
+  if (!margins.empty()) set_info(*out, "base_margin", std::move(margins));
+  return out;
+}
+}  // namespace
+
+XGB_DLL int XGProxyDMatrixSetDataDense(DMatrixHandle handle, char const* data) {
+  return guarded([&] {
+    require(data != nullptr, "Null array interface.");
+    ArrayView a = parse_array(data);
+    require(a.shape.size() == 2, "Dense input must be 2-dimensional.");
+    uint64_t rows, cols;
+    auto v = to_floats(a, rows, cols);
+    replace_proxy_data(handle, new_dmatrix(std::move(v), rows, cols, NAN));
+  });
+}
+
+XGB_DLL int XGProxyDMatrixSetDataCSR(DMatrixHandle handle, char const* indptr, char const* indices,
+                                     char const* data, bst_ulong ncol) {
+  return guarded([&] {
+    DMatrixHandle fresh = nullptr;
+    require(XGDMatrixCreateFromCSR(indptr, indices, data, ncol, nullptr, &fresh) == 0, last_error);
+    replace_proxy_data(handle, fresh);
+  });
+}
+
+XGB_DLL int XGDMatrixCreateFromCallback(DataIterHandle iter, DMatrixHandle proxy, DataIterResetCallback* reset,
+                                        XGDMatrixCallbackNext* next, char const* config, DMatrixHandle* out) {
+  return guarded([&] {
+    require(out != nullptr, "Null output handle.");
+    *out = new DMatrixPtr(from_iterator(iter, proxy, reset, next, config));
+  });
+}
+
+// The batches are concatenated, then quantised on the GPU with `ref`'s cuts
+// when `ref` (a DMatrix handle) is given (src/c_api.cpp:225-239 in the
+// reference). config: {"missing", "max_bin" (default 256)}.
+XGB_DLL int XGQuantileDMatrixCreateFromCallback(DataIterHandle iter, DMatrixHandle proxy, DataIterHandle ref,
+                                                DataIterResetCallback* reset, XGDMatrixCallbackNext* next,
+                                                char const* config, DMatrixHandle* out) {
+  return guarded([&] {
+    require(out != nullptr, "Null output handle.");
+    uint32_t bins = 256;
+    if (config && *config) {
+      const Json c = Json::parse(config);
+      if (const Json* m = c.find("max_bin"); m && m->kind != Json::Null) {
+        require(m->kind == Json::Number && m->num == std::floor(m->num), "max_bin must be an integer.");
+        require(m->num >= 2 && m->num <= 2147483647.0, "max_bin must be in [2, 2147483647].");
+        bins = uint32_t(m->num);
+      }
+    }
+    DMatrixPtr m = from_iterator(iter, proxy, reset, next, config);
+    ensure_device();
+    xgbb::DMatrix* r = ref ? dmat(ref).get() : nullptr;
+    if (r && !r->quantised()) r->quantise(bins, nullptr, nullptr, 0);
+    m->quantise(bins, r, nullptr, 0);
+    XGBB_CUDA(cudaStreamSynchronize(nullptr));
+    *out = new DMatrixPtr(std::move(m));
+  });
+}
+
 // ---------------------------------------------------------------------------
 // Booster
 // ---------------------------------------------------------------------------
@@ -397,28 +630,56 @@ XGB_DLL int XGBoosterUpdateOneIter(BoosterHandle handle, int iter, DMatrixHandle
   return guarded([&] { booster(handle).update(dmat(dtrain), iter); });
 }
 
+namespace {
+// Prediction config: {"type": 0 value | 1 margin, "iteration_begin",
+// "iteration_end", "training", "strict_shape"} (src/c_api.cpp:507 in the
+// reference).
+void predict_output(xgbb::Booster& bst, const DMatrixPtr& d, const char* config, bst_ulong const** out_shape,
+                    bst_ulong* out_dim, float const** out_result) {
+  Json c = Json::parse(config && *config ? config : "{}");
+  int type = 0;
+  if (auto* t = c.find("type")) type = int(t->num);
+  require(type == 0 || type == 1, "Only value (type 0) and margin (type 1) predictions are implemented.");
+  uint32_t begin = 0, end = 0;
+  if (auto* b = c.find("iteration_begin")) begin = uint32_t(b->num);
+  if (auto* e = c.find("iteration_end")) end = uint32_t(e->num);
+  bool training = false;
+  if (auto* t = c.find("training")) training = t->truthy();
+  bool strict = false;
+  if (auto* s = c.find("strict_shape")) strict = s->truthy();
+  std::vector<uint64_t> shape;
+  results.floats = bst.predict(d, type == 1, begin, end, training, shape);
+  if (strict && shape.size() == 1) shape.push_back(1);
+  results.shape.assign(shape.begin(), shape.end());
+  *out_shape = results.shape.data();
+  *out_dim = results.shape.size();
+  *out_result = results.floats.data();
+}
+}  // namespace
+
 XGB_DLL int XGBoosterPredictFromDMatrix(BoosterHandle handle, DMatrixHandle dm, char const* config,
                                         bst_ulong const** out_shape, bst_ulong* out_dim,
                                         float const** out_result) {
+  return guarded([&] { predict_output(booster(handle), dmat(dm), config, out_shape, out_dim, out_result); });
+}
+
+// In-place prediction from a dense __array_interface__ (src/c_api.cpp:510-512
+// in the reference): config adds "missing"; base margins come from the proxy
+// `m` when it is given.
+XGB_DLL int XGBoosterPredictFromDense(BoosterHandle handle, char const* values, char const* config,
+                                      DMatrixHandle m, bst_ulong const** out_shape, bst_ulong* out_dim,
+                                      const float** out_result) {
   return guarded([&] {
-    Json c = Json::parse(config && *config ? config : "{}");
-    int type = 0;
-    if (auto* t = c.find("type")) type = int(t->num);
-    require(type == 0 || type == 1, "Only value (type 0) and margin (type 1) predictions are implemented.");
-    uint32_t begin = 0, end = 0;
-    if (auto* b = c.find("iteration_begin")) begin = uint32_t(b->num);
-    if (auto* e = c.find("iteration_end")) end = uint32_t(e->num);
-    bool training = false;
-    if (auto* t = c.find("training")) training = t->truthy();
-    bool strict = false;
-    if (auto* s = c.find("strict_shape")) strict = s->truthy();
-    std::vector<uint64_t> shape;
-    results.floats = booster(handle).predict(dmat(dm), type == 1, begin, end, training, shape);
-    if (strict && shape.size() == 1) shape.push_back(1);
-    results.shape.assign(shape.begin(), shape.end());
-    *out_shape = results.shape.data();
-    *out_dim = results.shape.size();
-    *out_result = results.floats.data();
+    require(values != nullptr, "Null array interface.");
+    ArrayView a = parse_array(values);
+    require(a.shape.size() == 2, "Dense input must be 2-dimensional.");
+    uint64_t rows, cols;
+    auto v = to_floats(a, rows, cols);
+    auto* handle_d = static_cast<DMatrixPtr*>(new_dmatrix(std::move(v), rows, cols, config_missing(config)));
+    DMatrixPtr d = std::move(*handle_d);
+    delete handle_d;
+    if (m) d->base_margin = dmat(m)->base_margin;
+    predict_output(booster(handle), d, config, out_shape, out_dim, out_result);
   });
 }
 
@@ -474,9 +735,22 @@ XGB_DLL int XGBoosterGetAttrNames(BoosterHandle handle, bst_ulong* out_len, cons
 XGB_DLL int XGBoosterSetStrFeatureInfo(BoosterHandle handle, const char* field,
                                        const char** features, const bst_ulong size) {
   return guarded([&] {
+    const std::string f = field ? field : "";
+    require(f == "feature_name" || f == "feature_type", "Unknown feature info field: " + f);
     std::vector<std::string> v;
-    for (bst_ulong i = 0; i < size; ++i) v.emplace_back(features[i]);
-    booster(handle).feature_info[field] = std::move(v);
+    for (bst_ulong i = 0; i < size; ++i) {
+      require(features && features[i], "Null feature metadata.");
+      v.emplace_back(features[i]);
+      if (f == "feature_type")
+        require(v.back() == "q" || v.back() == "c" || v.back() == "int" || v.back() == "float" || v.back() == "i",
+                "Invalid feature type: " + v.back());
+    }
+    auto& b = booster(handle);
+    // A model that knows its width checks the list against it
+    // (src/c_api.cpp:119-128 in the reference).
+    require(v.empty() || b.num_feature() == 0 || v.size() == b.num_feature(),
+            "Feature metadata length must match the number of features.");
+    b.feature_info[f] = std::move(v);
   });
 }
 
@@ -565,6 +839,144 @@ XGB_DLL int XGBoosterSaveJsonConfig(BoosterHandle handle, bst_ulong* out_len, ch
     results.str = booster(handle).config_json();
     *out_len = results.str.size();
     *out_str = results.str.c_str();
+  });
+}
+
+XGB_DLL int XGBoosterLoadJsonConfig(BoosterHandle handle, char const* config) {
+  return guarded([&] {
+    require(config != nullptr, "Null configuration.");
+    booster(handle).load_config(config);
+  });
+}
+
+// The whole booster for pickling: {"Config": ..., "Model": ...} as UBJSON
+// (src/c_api.cpp:541-546 in the reference).
+XGB_DLL int XGBoosterSerializeToBuffer(BoosterHandle handle, bst_ulong* out_len, char const** out_dptr) {
+  return guarded([&] {
+    auto& b = booster(handle);
+    Json state;
+    state.kind = Json::Object;
+    state.obj.emplace_back("Config", Json::parse(b.config_json()));
+    state.obj.emplace_back("Model", Json::parse(b.save_json()));
+    results.str = state.dump_ubj();
+    *out_len = results.str.size();
+    *out_dptr = results.str.data();
+  });
+}
+
+XGB_DLL int XGBoosterUnserializeFromBuffer(BoosterHandle handle, const void* buf, bst_ulong len) {
+  return guarded([&] {
+    require(buf != nullptr || len == 0, "Null buffer.");
+    const Json state = Json::parse_ubj(buf, size_t(len));
+    auto& b = booster(handle);
+    b.load_json(state.at("Model").dump());
+    b.load_config(state.at("Config").dump());
+  });
+}
+
+XGB_DLL int XGBoosterReset(BoosterHandle handle) {
+  return guarded([&] { booster(handle).reset_training(); });
+}
+
+// -2 marks an out-of-range layer index (src/c_api.cpp:503-506 in the reference).
+XGB_DLL int XGBoosterSlice(BoosterHandle handle, int begin_layer, int end_layer, int step,
+                           BoosterHandle* out) {
+  const int status = guarded([&] {
+    require(out != nullptr, "Null output handle.");
+    *out = booster(handle).slice(begin_layer, end_layer, step).release();
+  });
+  return status != 0 && last_error.find("out of range") != std::string::npos ? -2 : status;
+}
+
+namespace {
+void string_output(std::vector<std::string> strings, bst_ulong* len, char const*** out) {
+  results.strings = std::move(strings);
+  results.ptrs.clear();
+  for (auto& s : results.strings) results.ptrs.push_back(s.c_str());
+  *len = results.ptrs.size();
+  *out = results.ptrs.data();
+}
+
+std::vector<std::string> feature_field(xgbb::Booster& b, const char* field) {
+  auto it = b.feature_info.find(field);
+  return it == b.feature_info.end() ? std::vector<std::string>{} : it->second;
+}
+
+std::vector<std::string> checked_features(const char** values, bst_ulong len, uint32_t cols, bool types) {
+  require(len == 0 || cols == 0 || len == cols, "Feature metadata length must match the number of features.");
+  std::vector<std::string> out;
+  for (bst_ulong i = 0; i < len; ++i) {
+    require(values && values[i], "Null feature metadata.");
+    std::string v = values[i];
+    if (types)
+      require(v == "q" || v == "c" || v == "int" || v == "float" || v == "i", "Invalid feature type: " + v);
+    out.push_back(std::move(v));
+  }
+  return out;
+}
+}  // namespace
+
+XGB_DLL int XGBoosterDumpModelEx(BoosterHandle handle, const char* fmap, int with_stats, const char* format,
+                                 bst_ulong* out_len, const char*** out_dump_array) {
+  return guarded([&] {
+    require(!fmap || !*fmap, "Feature-map files have not been implemented yet.");
+    auto& b = booster(handle);
+    const auto& trees = b.trees();
+    string_output(xgbb::dump_trees(trees, feature_field(b, "feature_name"), feature_field(b, "feature_type"),
+                                   format ? format : "text", with_stats != 0),
+                  out_len, out_dump_array);
+  });
+}
+
+XGB_DLL int XGBoosterDumpModel(BoosterHandle handle, const char* fmap, int with_stats, bst_ulong* out_len,
+                               const char*** out_dump_array) {
+  return XGBoosterDumpModelEx(handle, fmap, with_stats, "text", out_len, out_dump_array);
+}
+
+XGB_DLL int XGBoosterDumpModelExWithFeatures(BoosterHandle handle, int fnum, const char** fname,
+                                             const char** ftype, int with_stats, const char* format,
+                                             bst_ulong* out_len, const char*** out_models) {
+  return guarded([&] {
+    auto& b = booster(handle);
+    require(fnum >= 0, "Negative feature count.");
+    const auto& trees = b.trees();
+    const auto names = checked_features(fname, bst_ulong(fnum), b.num_feature(), false);
+    const auto types = checked_features(ftype, bst_ulong(fnum), b.num_feature(), true);
+    string_output(xgbb::dump_trees(trees, names, types, format ? format : "text", with_stats != 0), out_len,
+                  out_models);
+  });
+}
+
+XGB_DLL int XGBoosterDumpModelWithFeatures(BoosterHandle handle, int fnum, const char** fname,
+                                           const char** ftype, int with_stats, bst_ulong* out_len,
+                                           const char*** out_models) {
+  return XGBoosterDumpModelExWithFeatures(handle, fnum, fname, ftype, with_stats, "text", out_len, out_models);
+}
+
+// config: {"importance_type": "weight" | "gain" | "cover" | "total_gain" |
+// "total_cover", "feature_names": [...] or null}. Only features used by a split
+// are listed; scores have shape [n_features].
+XGB_DLL int XGBoosterFeatureScore(BoosterHandle handle, const char* config, bst_ulong* out_n_features,
+                                  char const*** out_features, bst_ulong* out_dim,
+                                  bst_ulong const** out_shape, float const** out_scores) {
+  return guarded([&] {
+    auto& b = booster(handle);
+    const Json c = Json::parse(config && *config ? config : "{}");
+    std::string kind = "weight";
+    if (const Json* k = c.find("importance_type"); k && k->kind == Json::String) kind = k->str;
+    std::vector<std::string> names = feature_field(b, "feature_name");
+    if (const Json* f = c.find("feature_names"); f && f->kind == Json::Array) {
+      names.clear();
+      for (const Json& x : f->arr) names.push_back(x.str);
+    }
+    const auto& trees = b.trees();
+    xgbb::FeatureScores s = xgbb::feature_scores(trees, b.num_feature(), names, kind);
+    results.floats = std::move(s.scores);
+    string_output(std::move(s.names), out_n_features, out_features);
+    results.shape.assign(1, *out_n_features);
+    *out_dim = 1;
+    *out_shape = results.shape.data();
+    *out_scores = results.floats.data();
   });
 }
 

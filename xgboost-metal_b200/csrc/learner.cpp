@@ -373,7 +373,10 @@ void Booster::configure() {
     require(v >= 0 && std::isfinite(v), "Tree parameters must be finite and nonnegative.");
   spw_ = number(params_, "scale_pos_weight", 1.0f);
   const uint32_t mb = uint32_t(integer(params_, "max_bin", 256));
-  require(!initialized_ || mb == max_bin_ || trees_.empty(), "max_bin cannot change after training starts.");
+  // A loaded (or reset) model has no quantised training state yet, so its
+  // continued training may pick any max_bin.
+  require(!initialized_ || mb == max_bin_ || trees_.empty() || !state_,
+          "max_bin cannot change after training starts.");
   max_bin_ = mb;
   if (objective_ == kSoftprob || objective_ == kSoftmax) {
     const long nc = integer(params_, "num_class", 0);
@@ -1022,6 +1025,44 @@ const char* objective_name(int objective) {
 }
 }  // namespace
 
+// learner_model_param of the model file: base scores as a bracketed list,
+// class and feature counts (src/model.cpp:28-60).
+Json Booster::model_param_json() const {
+  const uint32_t G = groups_;
+  std::string bs = "[";
+  const std::vector<float> scores = initialized_ ? base_score_ : std::vector<float>(G, 0.5f);
+  for (size_t k = 0; k < scores.size(); ++k) {
+    if (k) bs += ",";
+    bs += jfloat(scores[k]).str;
+  }
+  bs += "]";
+  const bool multi = objective_ == kSoftprob || objective_ == kSoftmax;
+  Json mp = jobj();
+  mp.obj.emplace_back("base_score", jstr(bs));
+  mp.obj.emplace_back("boost_from_average", jstr(params_.count("base_score") ? "0" : "1"));
+  mp.obj.emplace_back("num_class", jstr(multi ? std::to_string(G) : "0"));
+  mp.obj.emplace_back("num_feature", jstr(std::to_string(num_feature_)));
+  mp.obj.emplace_back("num_target", jstr("1"));
+  return mp;
+}
+
+// The objective's name and parameters, shared by the model and the config.
+Json Booster::objective_json() const {
+  const bool multi = objective_ == kSoftprob || objective_ == kSoftmax;
+  Json obj = jobj();
+  obj.obj.emplace_back("name", jstr(objective_name(objective_)));
+  if (multi) {
+    Json smp = jobj();
+    smp.obj.emplace_back("num_class", jstr(std::to_string(groups_)));
+    obj.obj.emplace_back("softmax_multiclass_param", smp);
+  } else {
+    Json rlp = jobj();
+    rlp.obj.emplace_back("scale_pos_weight", jstr(jfloat(spw_).str));
+    obj.obj.emplace_back("reg_loss_param", rlp);
+  }
+  return obj;
+}
+
 std::string Booster::save_json() {
   sync();
   configure();
@@ -1080,31 +1121,8 @@ std::string Booster::save_json() {
   Json gb = jobj();
   gb.obj.emplace_back("model", model);
   gb.obj.emplace_back("name", jstr("gbtree"));
-  std::string bs = "[";
-  const std::vector<float> scores = initialized_ ? base_score_ : std::vector<float>(G, 0.5f);
-  for (size_t k = 0; k < scores.size(); ++k) {
-    if (k) bs += ",";
-    bs += jfloat(scores[k]).str;
-  }
-  bs += "]";
-  const bool multi = objective_ == kSoftprob || objective_ == kSoftmax;
-  Json mp = jobj();
-  mp.obj.emplace_back("base_score", jstr(bs));
-  mp.obj.emplace_back("boost_from_average", jstr(params_.count("base_score") ? "0" : "1"));
-  mp.obj.emplace_back("num_class", jstr(multi ? std::to_string(G) : "0"));
-  mp.obj.emplace_back("num_feature", jstr(std::to_string(num_feature_)));
-  mp.obj.emplace_back("num_target", jstr("1"));
-  Json obj = jobj();
-  obj.obj.emplace_back("name", jstr(objective_name(objective_)));
-  if (multi) {
-    Json smp = jobj();
-    smp.obj.emplace_back("num_class", jstr(std::to_string(G)));
-    obj.obj.emplace_back("softmax_multiclass_param", smp);
-  } else {
-    Json rlp = jobj();
-    rlp.obj.emplace_back("scale_pos_weight", jstr(jfloat(spw_).str));
-    obj.obj.emplace_back("reg_loss_param", rlp);
-  }
+  const Json mp = model_param_json();
+  const Json obj = objective_json();
   Json attributes = jobj();
   for (auto& kv : attrs) attributes.obj.emplace_back(kv.first, jstr(kv.second));
   Json names = jarr(), types = jarr();
@@ -1245,19 +1263,198 @@ void Booster::load_json(const std::string& text) {
     for (const Json& x : f->arr) feature_info["feature_type"].push_back(x.str);
 }
 
-std::string Booster::config_json() const {
-  Json root;
-  root.kind = Json::Object;
-  Json learner;
-  learner.kind = Json::Object;
-  for (auto& kv : params_) {
-    Json v;
-    v.kind = Json::String;
-    v.str = kv.second;
-    learner.obj.emplace_back(kv.first, v);
+// The training configuration in upstream XGBoost's layout (the reference's
+// Learner::config, src/model.cpp:245-286): generic, model, train, booster,
+// metric and objective sections, every value a string.
+std::string Booster::config_json() {
+  sync();
+  configure();
+  auto str = [&](const char* key, const std::string& def) { return jstr(get_param(key, def)); };
+  static const std::pair<const char*, const char*> tree_defaults[] = {
+      {"colsample_bylevel", "1"}, {"colsample_bynode", "1"}, {"colsample_bytree", "1"},
+      {"grow_policy", "depthwise"}, {"interaction_constraints", ""}, {"learning_rate", "0.300000012"},
+      {"max_bin", "256"}, {"max_cat_threshold", "64"}, {"max_cat_to_onehot", "4"},
+      {"max_delta_step", "0"}, {"max_depth", "6"}, {"max_leaves", "0"}, {"min_child_weight", "1"},
+      {"min_split_loss", "0"}, {"monotone_constraints", "()"}, {"refresh_leaf", "1"},
+      {"reg_alpha", "0"}, {"reg_lambda", "1"}, {"sampling_method", "uniform"},
+      {"sparse_threshold", "0.2"}, {"subsample", "1"}};
+  std::map<std::string, Json> train;
+  for (auto& kv : tree_defaults) train[kv.first] = str(kv.first, kv.second);
+  train["eta"] = train["learning_rate"];
+  train["lambda"] = train["reg_lambda"];
+  train["alpha"] = train["reg_alpha"];
+  train["gamma"] = train["min_split_loss"];
+  Json ttp = jobj();
+  for (auto& kv : train) ttp.obj.emplace_back(kv.first, kv.second);
+
+  const std::string updater = "grow_gpu_hist";
+  Json gtp = jobj();
+  gtp.obj.emplace_back("process_type", jstr("default"));
+  gtp.obj.emplace_back("tree_method", str("tree_method", "hist"));
+  gtp.obj.emplace_back("updater", jstr(updater));
+  gtp.obj.emplace_back("updater_seq", jstr(updater));
+  Json gmp = jobj();
+  gmp.obj.emplace_back("num_parallel_tree", str("num_parallel_tree", "1"));
+  gmp.obj.emplace_back("num_trees", jstr(std::to_string(trees_.size())));
+  Json htp = jobj();
+  htp.obj.emplace_back("debug_synchronize", jstr("0"));
+  htp.obj.emplace_back("max_cached_hist_node", str("max_cached_hist_node", "18446744073709551615"));
+  Json up = jobj();
+  up.obj.emplace_back("hist_train_param", htp);
+  up.obj.emplace_back("name", jstr(updater));
+  Json updaters = jarr();
+  updaters.arr.push_back(up);
+  Json specified;
+  specified.kind = Json::Bool;
+  specified.b = params_.count("updater") != 0;
+  Json gb = jobj();
+  gb.obj.emplace_back("gbtree_model_param", gmp);
+  gb.obj.emplace_back("gbtree_train_param", gtp);
+  gb.obj.emplace_back("name", jstr("gbtree"));
+  gb.obj.emplace_back("specified_updater", specified);
+  gb.obj.emplace_back("tree_train_param", ttp);
+  gb.obj.emplace_back("updater", updaters);
+
+  Json gp = jobj();
+  gp.obj.emplace_back("device", jstr("cuda:" + std::to_string(device_)));
+  gp.obj.emplace_back("n_jobs", str("nthread", "0"));
+  gp.obj.emplace_back("nthread", str("nthread", "0"));
+  gp.obj.emplace_back("random_state", str("seed", "0"));
+  gp.obj.emplace_back("seed", str("seed", "0"));
+  gp.obj.emplace_back("seed_per_iteration", str("seed_per_iteration", "0"));
+  gp.obj.emplace_back("validate_parameters", jstr("1"));
+
+  const bool multi = objective_ == kSoftprob || objective_ == kSoftmax;
+  Json ltp = jobj();
+  ltp.obj.emplace_back("base_score", str("base_score", "[]"));
+  ltp.obj.emplace_back("boost_from_average", jstr(params_.count("base_score") ? "0" : "1"));
+  ltp.obj.emplace_back("booster", jstr("gbtree"));
+  ltp.obj.emplace_back("disable_default_eval_metric", str("disable_default_eval_metric", "0"));
+  ltp.obj.emplace_back("multi_strategy", str("multi_strategy", "one_output_per_tree"));
+  ltp.obj.emplace_back("num_class", jstr(multi ? std::to_string(groups_) : "0"));
+  ltp.obj.emplace_back("num_target", jstr("1"));
+  ltp.obj.emplace_back("objective", jstr(objective_name(objective_)));
+
+  Json metrics = jarr();
+  const std::string em = get_param("eval_metric", "");
+  for (size_t b = 0; b < em.size();) {
+    size_t e = em.find(',', b);
+    if (e == std::string::npos) e = em.size();
+    if (e > b) {
+      Json m = jobj();
+      m.obj.emplace_back("name", jstr(em.substr(b, e - b)));
+      metrics.arr.push_back(m);
+    }
+    b = e + 1;
   }
+
+  Json learner = jobj();
+  learner.obj.emplace_back("generic_param", gp);
+  learner.obj.emplace_back("gradient_booster", gb);
+  learner.obj.emplace_back("learner_model_param", model_param_json());
+  learner.obj.emplace_back("learner_train_param", ltp);
+  learner.obj.emplace_back("metrics", metrics);
+  learner.obj.emplace_back("objective", objective_json());
+  Json version = jarr();
+  for (int v : {3, 5, 0}) version.arr.push_back(jnum(v));
+  Json root = jobj();
   root.obj.emplace_back("learner", learner);
+  root.obj.emplace_back("version", version);
   return root.dump();
+}
+
+// Restores the parameters of config_json (the reference's Learner::load_config,
+// src/model.cpp:287-333); the model itself is untouched.
+void Booster::load_config(const std::string& text) {
+  sync();
+  const Json root = Json::parse(text);
+  const Json& learner = root.at("learner");
+  auto value = [](const Json& v) { return v.kind == Json::String ? v.str : v.dump(); };
+  std::map<std::string, std::string> params = params_;
+  auto put = [&](const std::string& key, const std::string& v) {
+    static const std::map<std::string, std::string> alias = {
+        {"eta", "learning_rate"}, {"lambda", "reg_lambda"}, {"alpha", "reg_alpha"}, {"gamma", "min_split_loss"}};
+    auto it = alias.find(key);
+    params[it == alias.end() ? key : it->second] = v;
+  };
+  const Json& objective = learner.at("objective");
+  put("objective", objective.at("name").str);
+  for (auto& kv : objective.obj)
+    if (kv.second.kind == Json::Object)
+      for (auto& p : kv.second.obj) put(p.first, value(p.second));
+  if (const Json* gp = learner.find("generic_param"))
+    for (auto& kv : gp->obj)
+      if (kv.first != "device" && kv.first != "rng_state" && kv.first != "n_jobs" && kv.first != "random_state")
+        put(kv.first, value(kv.second));
+  if (const Json* gb = learner.find("gradient_booster")) {
+    const std::string name = gb->find("name") ? gb->at("name").str : "gbtree";
+    require(name == "gbtree", "Only the gbtree booster is implemented: " + name);
+    if (const Json* t = gb->find("gbtree_train_param"))
+      if (const Json* m = t->find("tree_method")) put("tree_method", value(*m));
+    if (const Json* t = gb->find("tree_train_param"))
+      for (auto& kv : t->obj) put(kv.first, value(kv.second));
+    if (const Json* m = gb->find("gbtree_model_param"))
+      if (const Json* n = m->find("num_parallel_tree")) put("num_parallel_tree", value(*n));
+  }
+  if (const Json* ltp = learner.find("learner_train_param"))
+    for (auto& kv : ltp->obj) {
+      if (kv.first == "base_score" && value(kv.second) == "[]") continue;
+      // Derived flags, not parameters of this build.
+      if (kv.first == "boost_from_average" || kv.first == "num_target") continue;
+      if (kv.first == "num_class" && value(kv.second) == "0") {
+        params.erase("num_class");
+        continue;
+      }
+      put(kv.first, value(kv.second));
+    }
+  if (const Json* ms = learner.find("metrics")) {
+    std::string em;
+    for (const Json& m : ms->arr) {
+      if (!em.empty()) em += ",";
+      em += m.at("name").str;
+    }
+    if (em.empty()) params.erase("eval_metric");
+    else params["eval_metric"] = em;
+  }
+  params_ = std::move(params);
+  configured_ = false;
+}
+
+// A new booster holding the rounds begin, begin+step, ... < end of this one
+// (end 0 = all rounds), with the same parameters and attributes except
+// best_iteration and best_score (the reference's Learner::slice,
+// src/model.cpp:430-459).
+std::unique_ptr<Booster> Booster::slice(int begin, int end, int step) {
+  sync();
+  configure();
+  require(step > 0 && begin >= 0, "Invalid model slice.");
+  if (end == 0) end = int(rounds_);
+  require(end <= int(rounds_) && begin < end, "Model slice index out of range.");
+  auto out = std::make_unique<Booster>(std::vector<std::shared_ptr<DMatrix>>{});
+  out->params_ = params_;
+  out->configure();
+  out->num_feature_ = num_feature_;
+  out->max_bin_ = max_bin_;
+  out->base_score_ = base_score_;
+  out->base_margin_ = base_margin_;
+  out->initialized_ = initialized_;
+  out->attrs = attrs;
+  out->attrs.erase("best_iteration");
+  out->attrs.erase("best_score");
+  out->feature_info = feature_info;
+  const uint32_t G = groups_;
+  for (int r = begin; r < end; r += step) {
+    for (uint32_t g = 0; g < G; ++g) out->trees_.push_back(trees_[size_t(r) * G + g]);
+    ++out->rounds_;
+  }
+  return out;
+}
+
+// Drops the per-matrix training state (device buffers, captured graphs); the
+// model stays. Training again rebuilds it.
+void Booster::reset_training() {
+  sync();
+  state_.reset();
 }
 
 }  // namespace xgbb

@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "common.h"
+#include "json.h"
 #include "tree.h"
 
 namespace xgbb {
@@ -121,7 +122,13 @@ class Booster {
   void finish_pending();
   std::string save_json();
   void load_json(const std::string& text);
-  std::string config_json() const;
+  // Training configuration (upstream layout) and its inverse.
+  std::string config_json();
+  void load_config(const std::string& text);
+  // Rounds begin, begin+step, ... < end (0 = all) as a new booster.
+  std::unique_ptr<Booster> slice(int begin, int end, int step);
+  // Releases the training state of every matrix; the model stays.
+  void reset_training();
   std::map<std::string, std::string> attrs;
   std::map<std::string, std::vector<std::string>> feature_info;
   Profile profile;
@@ -143,6 +150,8 @@ class Booster {
   void record_tree_launches(TrainState& ts, uint32_t group, cudaStream_t stream, bool capturing,
                             uint32_t parity);
   void materialize();
+  Json model_param_json() const;
+  Json objective_json() const;
 
   std::map<std::string, std::string> params_;
   std::vector<std::weak_ptr<DMatrix>> cache_;

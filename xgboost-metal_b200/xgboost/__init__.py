@@ -2,11 +2,11 @@
 device="cuda") on hand-written sm_100a CUDA kernels, behind the upstream
 XGBoost Python API and C ABI."""
 from . import collective
-from .core import Booster, DMatrix, QuantileDMatrix, XGBoostError, build_info, synchronize
+from .core import Booster, DataIter, DMatrix, QuantileDMatrix, XGBoostError, build_info, synchronize
 from .sklearn import XGBClassifier, XGBModel, XGBRegressor
 from .training import train
 
 __version__ = "3.5.0-dev"
 
-__all__ = ["Booster", "DMatrix", "QuantileDMatrix", "XGBoostError", "XGBModel", "XGBRegressor",
+__all__ = ["Booster", "DataIter", "DMatrix", "QuantileDMatrix", "XGBoostError", "XGBModel", "XGBRegressor",
            "XGBClassifier", "train", "build_info", "collective", "synchronize"]

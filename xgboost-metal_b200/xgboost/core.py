@@ -8,11 +8,12 @@ libpath.find_lib_path does (python-package/xgboost/libpath.py:27-58).
 """
 import ctypes
 import json
+import math
 import os
 
 import numpy as np
 
-__all__ = ["DMatrix", "QuantileDMatrix", "Booster", "XGBoostError", "build_info"]
+__all__ = ["DMatrix", "QuantileDMatrix", "DataIter", "Booster", "XGBoostError", "build_info"]
 
 
 class XGBoostError(ValueError):
@@ -82,9 +83,115 @@ def _to_2d_float(data):
     return arr
 
 
+_NEXT_CALLBACK = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p)
+_RESET_CALLBACK = ctypes.CFUNCTYPE(None, ctypes.c_void_p)
+
+
+class DataIter:
+    """Batches for DMatrix / QuantileDMatrix (python-package/xgboost/core.py
+    DataIter): subclasses define reset() and next(input_data), where next
+    calls input_data(data=..., label=..., weight=..., base_margin=...) once
+    per batch and returns False after the last one. The batches are
+    concatenated on the host before quantisation."""
+
+    def __init__(self, cache_prefix=None, release_data=True, *, on_host=True,
+                 min_cache_page_bytes=None):
+        self.cache_prefix = cache_prefix
+        self._release = release_data
+        self._exception = None
+        self._proxy = None
+        self._batch = None
+        self._feature_names = None
+        self._feature_types = None
+
+    def reset(self):
+        raise NotImplementedError()
+
+    def next(self, input_data):
+        raise NotImplementedError()
+
+    # An exception inside a ctypes callback cannot cross the C frames: it is
+    # kept, the iteration stops, and it is raised after the C call returns.
+    def _handle_exception(self, fn, default):
+        if self._exception is not None:
+            return default
+        try:
+            return fn()
+        except Exception as e:  # noqa: BLE001
+            self._exception = e
+        return default
+
+    def reraise(self):
+        self._batch = None
+        if self._exception is not None:
+            exc, self._exception = self._exception, None
+            raise exc
+
+    def _reset_wrapper(self, _this):
+        if self._release:
+            self._batch = None
+        self._handle_exception(self.reset, None)
+
+    def _input_data(self, *, data, label=None, weight=None, base_margin=None, feature_names=None,
+                    feature_types=None, **kwargs):
+        proxy = self._proxy
+        if _is_scipy_csr(data):
+            values = np.asarray(data.data, dtype=np.float32)
+            keep = (data.indptr, data.indices, values)
+            _check_call(_LIB.XGProxyDMatrixSetDataCSR(
+                proxy, _c_str(_array_interface(data.indptr)), _c_str(_array_interface(data.indices)),
+                _c_str(_array_interface(values)), c_bst_ulong(data.shape[1])))
+        else:
+            arr = _to_2d_float(data)
+            keep = (arr,)
+            _check_call(_LIB.XGProxyDMatrixSetDataDense(proxy, _c_str(_array_interface(arr))))
+        # Every field is written for every batch (empty when absent), so no
+        # field of an earlier batch survives into this one.
+        for field, values in (("label", label), ("weight", weight), ("base_margin", base_margin)):
+            v = np.zeros(0, np.float32) if values is None else \
+                np.ascontiguousarray(np.asarray(values, dtype=np.float32).reshape(-1))
+            keep = keep + (v,)
+            _check_call(_LIB.XGDMatrixSetInfoFromInterface(proxy, _c_str(field),
+                                                           _c_str(_array_interface(v))))
+        if feature_names is not None:
+            self._feature_names = list(feature_names)
+        elif hasattr(data, "columns"):
+            self._feature_names = [str(c) for c in data.columns]
+        if feature_types is not None:
+            self._feature_types = list(feature_types)
+        self._batch = keep
+
+    def _next_wrapper(self, _this):
+        return self._handle_exception(lambda: int(bool(self.next(self._input_data))), 0)
+
+    def _create(self, config, ref=None, quantile=False):
+        """Runs the iterator through the C callbacks and returns the handle."""
+        proxy = ctypes.c_void_p()
+        _check_call(_LIB.XGProxyDMatrixCreate(ctypes.byref(proxy)))
+        self._proxy = proxy
+        reset = _RESET_CALLBACK(self._reset_wrapper)
+        nxt = _NEXT_CALLBACK(self._next_wrapper)
+        handle = ctypes.c_void_p()
+        try:
+            if quantile:
+                ret = _LIB.XGQuantileDMatrixCreateFromCallback(
+                    None, proxy, ref, reset, nxt, _c_str(json.dumps(config)), ctypes.byref(handle))
+            else:
+                ret = _LIB.XGDMatrixCreateFromCallback(
+                    None, proxy, reset, nxt, _c_str(json.dumps(config)), ctypes.byref(handle))
+            self.reraise()
+            _check_call(ret)
+        finally:
+            _LIB.XGDMatrixFree(proxy)
+            self._proxy = None
+            self._batch = None
+        return handle
+
+
 class DMatrix:
     """Data matrix (python-package/xgboost/core.py DMatrix). Quantisation is
-    lazy: it happens on the first training round, as in the reference."""
+    lazy: it happens on the first training round, as in the reference. A
+    DataIter is read batch by batch and concatenated."""
 
     def __init__(self, data, label=None, *, weight=None, base_margin=None, missing=None,
                  silent=False, feature_names=None, feature_types=None, nthread=None,
@@ -95,6 +202,12 @@ class DMatrix:
         self.handle = ctypes.c_void_p()
         miss = np.nan if missing is None else float(missing)
         config = {"missing": None if np.isnan(miss) else miss, "nthread": nthread or 0}
+        if isinstance(data, DataIter):
+            self.handle = data._create(config)
+            self.feature_names = list(feature_names) if feature_names is not None else \
+                data._feature_names
+            self.feature_types = feature_types if feature_types is not None else data._feature_types
+            return
         if _is_scipy_csr(data):
             csr = data
             _check_call(_LIB.XGDMatrixCreateFromCSR(
@@ -184,10 +297,22 @@ class QuantileDMatrix(DMatrix):
                  max_bin=None, ref=None, group=None, qid=None, label_lower_bound=None,
                  label_upper_bound=None, feature_weights=None, enable_categorical=False,
                  max_quantile_batches=None, data_split_mode=None):
+        self.max_bin = 256 if max_bin is None else int(max_bin)
+        if isinstance(data, DataIter):
+            if group is not None or qid is not None:
+                raise XGBoostError("Ranking groups are not implemented by the CUDA backend.")
+            miss = np.nan if missing is None else float(missing)
+            config = {"missing": None if np.isnan(miss) else miss, "nthread": nthread or 0,
+                      "max_bin": self.max_bin}
+            self.handle = data._create(config, ref.handle if ref is not None else None,
+                                       quantile=True)
+            self.feature_names = list(feature_names) if feature_names is not None else \
+                data._feature_names
+            self.feature_types = feature_types if feature_types is not None else data._feature_types
+            return
         super().__init__(data, label, weight=weight, base_margin=base_margin, missing=missing,
                          feature_names=feature_names, feature_types=feature_types, nthread=nthread,
                          group=group, qid=qid)
-        self.max_bin = 256 if max_bin is None else int(max_bin)
         _check_call(_LIB.XGDMatrixQuantise(self.handle, ctypes.c_int(self.max_bin),
                                            ref.handle if ref is not None else None))
 
@@ -202,8 +327,9 @@ class Booster:
         self.handle = ctypes.c_void_p()
         _check_call(_LIB.XGBoosterCreate(arr, c_bst_ulong(len(cache)), ctypes.byref(self.handle)))
         self._cache = cache
-        self.feature_names = cache[0].feature_names if cache else None
-        self.feature_types = None
+        if cache:
+            self.feature_names = cache[0].feature_names
+            self.feature_types = cache[0].feature_types
         params = params or {}
         if isinstance(params, dict):
             items = list(params.items())
@@ -220,6 +346,43 @@ class Booster:
         if _LIB is not None and getattr(self, "handle", None) is not None and self.handle.value:
             _LIB.XGBoosterFree(self.handle)
             self.handle = None
+
+    # Feature names and types live in the native booster, so that model files,
+    # dumps and importance scores carry them (python-package/xgboost/core.py
+    # Booster.feature_names).
+    def _get_feature_info(self, field):
+        length = c_bst_ulong()
+        sarr = ctypes.POINTER(ctypes.c_char_p)()
+        _check_call(_LIB.XGBoosterGetStrFeatureInfo(self.handle, _c_str(field), ctypes.byref(length),
+                                                    ctypes.byref(sarr)))
+        values = [sarr[i].decode() for i in range(length.value)]
+        return values if values else None
+
+    def _set_feature_info(self, field, values):
+        if values is None:
+            _check_call(_LIB.XGBoosterSetStrFeatureInfo(self.handle, _c_str(field), None,
+                                                        c_bst_ulong(0)))
+            return
+        values = [str(v) for v in values]
+        arr = (ctypes.c_char_p * len(values))(*[v.encode() for v in values])
+        _check_call(_LIB.XGBoosterSetStrFeatureInfo(self.handle, _c_str(field), arr,
+                                                    c_bst_ulong(len(values))))
+
+    @property
+    def feature_names(self):
+        return self._get_feature_info("feature_name")
+
+    @feature_names.setter
+    def feature_names(self, names):
+        self._set_feature_info("feature_name", names)
+
+    @property
+    def feature_types(self):
+        return self._get_feature_info("feature_type")
+
+    @feature_types.setter
+    def feature_types(self, types):
+        self._set_feature_info("feature_type", types)
 
     def set_param(self, params, value=None):
         if isinstance(params, dict):
@@ -273,9 +436,43 @@ class Booster:
 
     def inplace_predict(self, data, iteration_range=(0, 0), predict_type="value", missing=np.nan,
                         validate_features=True, base_margin=None, strict_shape=False):
-        dm = DMatrix(data, missing=missing, base_margin=base_margin)
-        return self.predict(dm, output_margin=predict_type == "margin",
-                            iteration_range=iteration_range, strict_shape=strict_shape)
+        """Prediction straight from an array (XGBoosterPredictFromDense); CSR
+        input goes through a DMatrix."""
+        if predict_type not in ("value", "margin"):
+            raise XGBoostError("predict_type must be 'value' or 'margin'.")
+        if _is_scipy_csr(data):
+            dm = DMatrix(data, missing=missing, base_margin=base_margin)
+            return self.predict(dm, output_margin=predict_type == "margin",
+                                iteration_range=iteration_range, strict_shape=strict_shape)
+        arr = _to_2d_float(data)
+        miss = float(missing) if missing is not None else np.nan
+        config = json.dumps({"type": 1 if predict_type == "margin" else 0, "training": False,
+                             "iteration_begin": int(iteration_range[0]),
+                             "iteration_end": int(iteration_range[1]),
+                             "strict_shape": bool(strict_shape),
+                             "missing": None if np.isnan(miss) else miss})
+        proxy = None
+        if base_margin is not None:
+            proxy = ctypes.c_void_p()
+            _check_call(_LIB.XGProxyDMatrixCreate(ctypes.byref(proxy)))
+        try:
+            if proxy is not None:
+                bm = np.ascontiguousarray(np.asarray(base_margin, dtype=np.float32).reshape(-1))
+                _check_call(_LIB.XGDMatrixSetInfoFromInterface(proxy, _c_str("base_margin"),
+                                                               _c_str(_array_interface(bm))))
+            shape = ctypes.POINTER(c_bst_ulong)()
+            dims = c_bst_ulong()
+            result = ctypes.POINTER(ctypes.c_float)()
+            _check_call(_LIB.XGBoosterPredictFromDense(
+                self.handle, _c_str(_array_interface(arr)), _c_str(config), proxy,
+                ctypes.byref(shape), ctypes.byref(dims), ctypes.byref(result)))
+            dims_t = tuple(shape[i] for i in range(dims.value))
+            n = int(np.prod(dims_t)) if dims_t else 0
+            return np.ctypeslib.as_array(result, shape=(n,)).copy().reshape(dims_t) if n else \
+                np.zeros(dims_t, np.float32)
+        finally:
+            if proxy is not None:
+                _LIB.XGDMatrixFree(proxy)
 
     def attr(self, key):
         out = ctypes.c_char_p()
@@ -347,17 +544,36 @@ class Booster:
         else:
             _check_call(_LIB.XGBoosterLoadModel(self.handle, _c_str(os.fspath(fname))))
 
+    # Pickling keeps the model and the training configuration
+    # (XGBoosterSerializeToBuffer: {"Config", "Model"} as UBJSON).
     def __getstate__(self):
-        return {"raw": bytes(self.save_raw("ubj")), "feature_names": self.feature_names,
-                "feature_types": self.feature_types}
+        length = c_bst_ulong()
+        out = ctypes.c_char_p()
+        _check_call(_LIB.XGBoosterSerializeToBuffer(self.handle, ctypes.byref(length),
+                                                    ctypes.byref(out)))
+        state = {k: v for k, v in self.__dict__.items() if k not in ("handle", "_cache")}
+        state["handle"] = bytes(ctypes.string_at(out, length.value))
+        return state
 
     def __setstate__(self, state):
-        self.handle = ctypes.c_void_p()
-        _check_call(_LIB.XGBoosterCreate(None, c_bst_ulong(0), ctypes.byref(self.handle)))
+        state = dict(state)
+        buf = state.pop("handle")
+        handle = ctypes.c_void_p()
+        _check_call(_LIB.XGBoosterCreate(None, c_bst_ulong(0), ctypes.byref(handle)))
+        _check_call(_LIB.XGBoosterUnserializeFromBuffer(handle, ctypes.c_char_p(buf),
+                                                        c_bst_ulong(len(buf))))
+        self.__dict__.update(state)
+        self.handle = handle
         self._cache = []
-        self.feature_names = state.get("feature_names")
-        self.feature_types = state.get("feature_types")
-        self.load_model(state["raw"])
+
+    def load_config(self, config):
+        """Restores the parameters written by save_config."""
+        _check_call(_LIB.XGBoosterLoadJsonConfig(self.handle, _c_str(config)))
+
+    def reset(self):
+        """Releases the training state on the device; the model stays."""
+        _check_call(_LIB.XGBoosterReset(self.handle))
+        return self
 
     def copy(self):
         return Booster(model_file=self.save_raw("ubj"))
@@ -367,6 +583,132 @@ class Booster:
 
     def __deepcopy__(self, memo):
         return self.copy()
+
+    # -- slicing (python-package/xgboost/core.py Booster.__getitem__) --------
+    def __getitem__(self, val):
+        """A booster of the rounds selected by an int or a slice; the
+        best_iteration and best_score attributes are dropped."""
+        if isinstance(val, (int, np.integer)) and not isinstance(val, bool):
+            val = slice(int(val), int(val) + 1)
+        if val is Ellipsis:
+            val = slice(0, 0)
+        if isinstance(val, tuple):
+            raise ValueError("Only supports slicing through 1 dimension.")
+        if not isinstance(val, slice):
+            raise TypeError("Expected an int, a slice or an ellipsis, got %s" % type(val).__name__)
+        start = 0 if val.start is None or val.start is Ellipsis else val.start
+        stop = 0 if val.stop is None or val.stop is Ellipsis else val.stop
+        if val.stop is not None and val.stop is not Ellipsis and stop < start:
+            raise ValueError("Invalid slice", val)
+        step = 1 if val.step is None else val.step
+        handle = ctypes.c_void_p()
+        status = _LIB.XGBoosterSlice(self.handle, ctypes.c_int(start), ctypes.c_int(stop),
+                                     ctypes.c_int(step), ctypes.byref(handle))
+        if status == -2:
+            raise IndexError("Layer index out of range")
+        _check_call(status)
+        sliced = Booster.__new__(Booster)
+        sliced.handle = handle
+        sliced._cache = []
+        return sliced
+
+    def __iter__(self):
+        for i in range(self.num_boosted_rounds()):
+            yield self[i]
+
+    # -- model inspection (python-package/xgboost/core.py get_dump,
+    # dump_model, get_score, get_fscore, trees_to_dataframe) ----------------
+    def get_dump(self, fmap="", with_stats=False, dump_format="text"):
+        """One string per tree: "text", "json" or "dot"."""
+        length = c_bst_ulong()
+        sarr = ctypes.POINTER(ctypes.c_char_p)()
+        _check_call(_LIB.XGBoosterDumpModelEx(self.handle, _c_str(os.fspath(fmap)),
+                                              ctypes.c_int(int(with_stats)), _c_str(dump_format),
+                                              ctypes.byref(length), ctypes.byref(sarr)))
+        return [sarr[i].decode() for i in range(length.value)]
+
+    def dump_model(self, fout, fmap="", with_stats=False, dump_format="text"):
+        """Writes get_dump to a file name or an open text file."""
+        close = isinstance(fout, (str, os.PathLike))
+        f = open(os.fspath(os.path.expanduser(fout)), "w", encoding="utf-8") if close else fout
+        try:
+            trees = self.get_dump(fmap, with_stats, dump_format)
+            if dump_format == "json":
+                f.write("[\n")
+                f.write(",\n".join(trees))
+                f.write("\n]")
+            else:
+                for i, tree in enumerate(trees):
+                    f.write("booster[%d]:\n" % i)
+                    f.write(tree)
+        finally:
+            if close:
+                f.close()
+
+    def get_score(self, fmap="", importance_type="weight"):
+        """Importance of each feature used by a split: "weight", "gain",
+        "cover", "total_gain" or "total_cover"."""
+        features = ctypes.POINTER(ctypes.c_char_p)()
+        scores = ctypes.POINTER(ctypes.c_float)()
+        n = c_bst_ulong()
+        dim = c_bst_ulong()
+        shape = ctypes.POINTER(c_bst_ulong)()
+        config = json.dumps({"importance_type": importance_type, "feature_map": os.fspath(fmap)})
+        _check_call(_LIB.XGBoosterFeatureScore(self.handle, _c_str(config), ctypes.byref(n),
+                                               ctypes.byref(features), ctypes.byref(dim),
+                                               ctypes.byref(shape), ctypes.byref(scores)))
+        return {features[i].decode(): float(scores[i]) for i in range(n.value)}
+
+    def get_fscore(self, fmap=""):
+        return self.get_score(fmap, importance_type="weight")
+
+    def trees_to_dataframe(self, fmap=""):
+        """One row per node: Tree, Target, Node, ID, Feature, Split, Yes, No,
+        Missing, Gain (leaf value for leaves), Cover, Category."""
+        from pandas import DataFrame
+        model = json.loads(self.save_raw(raw_format="json"))
+        gbm = model["learner"]["gradient_booster"]
+        trees = gbm["model"]["trees"]
+        tree_info = gbm["model"]["tree_info"]
+        fnames = dict(enumerate(self.feature_names or []))
+        ftypes = dict(enumerate(self.feature_types or []))
+        cols = {k: [] for k in ("Tree", "Target", "Node", "ID", "Feature", "Split", "Yes", "No",
+                                "Missing", "Gain", "Cover", "Category")}
+
+        def row(**kw):
+            for k in cols:
+                cols[k].append(kw.get(k))
+
+        for tid, tree in enumerate(trees):
+            left, right = tree["left_children"], tree["right_children"]
+            target = int(tree_info[tid])
+            stack = [0]
+            while stack:
+                nid = stack.pop()
+                if left[nid] == -1:
+                    row(Tree=tid, Target=target, Node=nid, ID="%d-%d" % (tid, nid), Feature="Leaf",
+                        Gain=float(tree["split_conditions"][nid]), Cover=tree["sum_hessian"][nid])
+                    continue
+                stack.append(left[nid])
+                stack.append(right[nid])
+                fidx = tree["split_indices"][nid]
+                dft = left[nid] if tree["default_left"][nid] else right[nid]
+                yes, no = left[nid], right[nid]
+                split = tree["split_conditions"][nid]
+                if ftypes.get(fidx, "q") == "i":
+                    yes, no = (right[nid] if tree["default_left"][nid] else left[nid]), dft
+                    split = None
+                elif ftypes.get(fidx, "q") == "int":
+                    split = float(math.ceil(split))
+                row(Tree=tid, Target=target, Node=nid, ID="%d-%d" % (tid, nid),
+                    Feature=fnames.get(fidx, "f%d" % fidx), Split=split, Yes="%d-%d" % (tid, yes),
+                    No="%d-%d" % (tid, no), Missing="%d-%d" % (tid, dft),
+                    Gain=tree["loss_changes"][nid], Cover=tree["sum_hessian"][nid])
+        df = DataFrame(cols).astype({"Tree": "Int64", "Target": "Int64", "Node": "Int64",
+                                     "ID": "string", "Feature": "string", "Split": "Float64",
+                                     "Yes": "string", "No": "string", "Missing": "string",
+                                     "Gain": "Float64", "Cover": "Float64"})
+        return df.sort_values(["Tree", "Node", "Target"]).reset_index(drop=True)
 
 
 def synchronize():

@@ -62,6 +62,20 @@ class XGBModel:
             raise XGBoostError("need to call fit or load_model beforehand")
         return self._Booster
 
+    @property
+    def feature_importances_(self):
+        """Importance per input feature (importance_type, default "gain"),
+        normalised to sum to one; unused features score zero."""
+        b = self.get_booster()
+        score = b.get_score(importance_type=self.importance_type or "gain")
+        names = b.feature_names or ["f%d" % i for i in range(self.n_features_in_)]
+        values = np.array([score.get(f, 0.0) for f in names], dtype=np.float32)
+        total = values.sum()
+        return values if total == 0 else values / total
+
+    def evals_result(self):
+        return self.evals_result_
+
     # Model files (python-package/xgboost/sklearn.py save_model / load_model):
     # the estimator's own attributes travel in the model's "scikit_learn"
     # attribute.
