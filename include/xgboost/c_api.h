@@ -128,6 +128,14 @@ XGB_DLL int XGBoosterSetParams(BoosterHandle handle, char const* config);
 XGB_DLL int XGBoosterGetNumFeature(BoosterHandle handle, bst_ulong* out);
 /* include/xgboost/c_api.h:1095 (src/c_api.cpp:484): one boosting round on the GPU. */
 XGB_DLL int XGBoosterUpdateOneIter(BoosterHandle handle, int iter, DMatrixHandle dtrain);
+/* include/xgboost/c_api.h:1121 (src/c_api.cpp:485-487): one round from a custom
+ * objective; grad and hess are __array_interface__ JSON of shape (rows,) or
+ * (rows, groups), finite. Without base_score the intercept is 0.5. */
+XGB_DLL int XGBoosterTrainOneIter(BoosterHandle handle, DMatrixHandle dtrain, int iter, char const* grad,
+                                  char const* hess);
+/* include/xgboost/c_api.h:1103: the same from flat float arrays of len = rows * groups. */
+XGB_DLL int XGBoosterBoostOneIter(BoosterHandle handle, DMatrixHandle dtrain, float* grad, float* hess,
+                                  bst_ulong len);
 /* include/xgboost/c_api.h:1207 (src/c_api.cpp:507): config {"type": 0 value | 1 margin,
  * "training", "iteration_begin", "iteration_end", "strict_shape"}. */
 XGB_DLL int XGBoosterPredictFromDMatrix(BoosterHandle handle, DMatrixHandle dmat, char const* config,

@@ -1,12 +1,15 @@
 """GPU checks of the host-side entry points around training: a QuantileDMatrix
 or DMatrix built from a batch iterator trains the same trees as one built
 from the concatenated arrays, in-place prediction equals DMatrix prediction,
-and a round slice predicts like an iteration range."""
+a round slice predicts like an iteration range, and custom objectives
+(XGBoosterTrainOneIter / XGBoosterBoostOneIter) train through the same
+kernels."""
 import numpy as np
 import pytest
 
 import xgboost as xgb
 from test_ingest_cpu import Batches, _parts
+from xgboost import core
 
 pytestmark = pytest.mark.gpu
 
@@ -54,3 +57,67 @@ def test_inplace_predict_and_slices_match_dmatrix_prediction():
     np.testing.assert_array_equal(b[:3].predict(dm), b.predict(dm, iteration_range=(0, 3)))
     np.testing.assert_array_equal(b[2:5].predict(dm, output_margin=True) - 0.0,
                                   b.predict(dm, output_margin=True, iteration_range=(2, 5)))
+
+
+def _squared_error(pred, dtrain):
+    y = dtrain.get_label()
+    w = dtrain.get_weight()
+    g = (pred - y).astype(np.float32)
+    h = np.ones_like(g)
+    if len(w):
+        g, h = (g * w).astype(np.float32), w.astype(np.float32)
+    return g, h
+
+
+@pytest.mark.parametrize("weighted", [False, True])
+def test_custom_squared_error_trains_the_builtin_model(weighted):
+    """Gradients from Python equal to the built-in ones give the same model
+    bytes: the quantised histograms, splits and leaves do not depend on
+    where the gradients came from (the built-in unweighted round counts rows
+    instead of summing unit Hessians, with the same exact sums)."""
+    rng = np.random.default_rng(13)
+    X = rng.normal(size=(6000, 6)).astype(np.float32)
+    X[rng.random(X.shape) < 0.1] = np.nan
+    y = (np.nan_to_num(X[:, 1]) * 2 + rng.normal(size=6000)).astype(np.float32)
+    w = rng.random(6000).astype(np.float32) if weighted else None
+    params = dict(PARAMS, base_score=0.5)
+    want = xgb.train(params, xgb.DMatrix(X, label=y, weight=w), 5)
+    got = xgb.train(params, xgb.DMatrix(X, label=y, weight=w), 5, obj=_squared_error)
+    assert bytes(got.save_raw("json")) == bytes(want.save_raw("json"))
+    # The flat legacy entry point trains the same round.
+    d = xgb.DMatrix(X, label=y, weight=w)
+    b = xgb.Booster(params, [d])
+    for i in range(5):
+        g, h = _squared_error(b.predict(d, output_margin=True, training=True), d)
+        assert core._LIB.XGBoosterBoostOneIter(
+            b.handle, d.handle, g.ctypes.data_as(core.ctypes.POINTER(core.ctypes.c_float)),
+            h.ctypes.data_as(core.ctypes.POINTER(core.ctypes.c_float)), core.c_bst_ulong(g.size)) == 0
+    assert bytes(b.save_raw("json")) == bytes(want.save_raw("json"))
+
+
+def test_custom_softmax_objective_learns_and_continues_from_a_model():
+    rng = np.random.default_rng(14)
+    n, k = 3000, 3
+    X = rng.normal(size=(n, 4)).astype(np.float32)
+    y = np.argmax(X[:, :k] + 0.3 * rng.normal(size=(n, k)), axis=1).astype(np.float32)
+
+    def softmax_obj(pred, dtrain):
+        labels = dtrain.get_label().astype(int)
+        p = np.exp(pred - pred.max(axis=1, keepdims=True))
+        p /= p.sum(axis=1, keepdims=True)
+        onehot = np.eye(k, dtype=np.float32)[labels]
+        g = (p - onehot).astype(np.float32)
+        h = np.maximum(2.0 * p * (1.0 - p), 1e-6).astype(np.float32)
+        return g, h
+
+    params = {"objective": "multi:softprob", "num_class": k, "tree_method": "hist", "device": "cuda",
+              "max_depth": 4, "eta": 0.3}
+    d = xgb.DMatrix(X, label=y)
+    b = xgb.train(params, d, 8, obj=softmax_obj)
+    fresh = xgb.DMatrix(X)
+    margin = b.predict(fresh, output_margin=True)
+    assert margin.shape == (n, k)
+    assert np.mean(np.argmax(margin, axis=1) == y) > 0.7
+    more = xgb.train(params, d, 2, obj=softmax_obj, xgb_model=b)
+    assert more.num_boosted_rounds() == 10 and b.num_boosted_rounds() == 8
+    np.testing.assert_array_equal(more[:8].predict(fresh, output_margin=True), margin)

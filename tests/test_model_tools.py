@@ -271,3 +271,24 @@ def test_sklearn_feature_importances(tmp_path):
     reg.n_features_in_ = 3
     imp = reg.feature_importances_
     np.testing.assert_allclose(imp, np.array([1.0, 0.5, 2.5]) / 4.0, rtol=1e-6)
+
+
+def test_custom_gradients_are_checked_before_any_device_work():
+    from xgboost import core
+    b = _booster(_model("reg:squarederror", "[0.5]"))
+    d = xgb.DMatrix(np.zeros((4, 3), np.float32), label=np.zeros(4, np.float32))
+    with pytest.raises(ValueError, match="shape mismatch"):
+        b.boost(d, 0, np.zeros(4), np.zeros(3))
+    with pytest.raises(xgb.XGBoostError, match="one row per training sample"):
+        b.boost(d, 0, np.zeros(5), np.ones(5))
+    with pytest.raises(xgb.XGBoostError, match="shape"):
+        b.boost(d, 0, np.zeros((4, 2)), np.ones((4, 2)))
+    with pytest.raises(xgb.XGBoostError, match="finite"):
+        b.boost(d, 0, np.array([0, np.nan, 0, 0]), np.ones(4))
+    with pytest.raises(xgb.XGBoostError, match="finite"):
+        b.boost(d, 0, np.zeros(4), np.array([1, 1, np.inf, 1]))
+    g = np.zeros(3, np.float32)
+    assert core._LIB.XGBoosterBoostOneIter(
+        b.handle, d.handle, g.ctypes.data_as(core.ctypes.POINTER(core.ctypes.c_float)),
+        g.ctypes.data_as(core.ctypes.POINTER(core.ctypes.c_float)), core.c_bst_ulong(3)) == -1
+    assert b"shape" in core._LIB.XGBGetLastError()

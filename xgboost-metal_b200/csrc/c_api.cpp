@@ -630,6 +630,34 @@ XGB_DLL int XGBoosterUpdateOneIter(BoosterHandle handle, int iter, DMatrixHandle
   return guarded([&] { booster(handle).update(dmat(dtrain), iter); });
 }
 
+// One round from a custom objective's gradients and Hessians: two
+// __array_interface__ documents of shape (rows,) or (rows, groups), any
+// numeric dtype (src/c_api.cpp:485-487 in the reference).
+XGB_DLL int XGBoosterTrainOneIter(BoosterHandle handle, DMatrixHandle dtrain, int iter, char const* grad,
+                                  char const* hess) {
+  return guarded([&] {
+    (void)iter;
+    require(grad != nullptr && hess != nullptr, "Null gradient or Hessian.");
+    const ArrayView ga = parse_array(grad), ha = parse_array(hess);
+    require(ga.shape == ha.shape, "Gradient and Hessian must have the same shape.");
+    require(ga.shape.size() == 1 || ga.shape.size() == 2, "Gradient must be one or two dimensional.");
+    uint64_t gr, gc, hr, hc;
+    const std::vector<float> g = to_floats(ga, gr, gc), h = to_floats(ha, hr, hc);
+    auto& d = dmat(dtrain);
+    require(gr == d->rows, "Gradient and Hessian must have one row per training sample.");
+    booster(handle).update_custom(d, g.data(), h.data(), g.size());
+  });
+}
+
+// Legacy form: flat float arrays of `len` values (src/c_api.cpp:495-497).
+XGB_DLL int XGBoosterBoostOneIter(BoosterHandle handle, DMatrixHandle dtrain, float* grad, float* hess,
+                                  bst_ulong len) {
+  return guarded([&] {
+    require(len == 0 || (grad != nullptr && hess != nullptr), "Null gradient or Hessian.");
+    booster(handle).update_custom(dmat(dtrain), grad, hess, size_t(len));
+  });
+}
+
 namespace {
 // Prediction config: {"type": 0 value | 1 margin, "iteration_begin",
 // "iteration_end", "training", "strict_shape"} (src/c_api.cpp:507 in the

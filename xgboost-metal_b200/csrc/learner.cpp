@@ -246,6 +246,10 @@ struct Booster::TrainState {
   unsigned long long* host_level_rows[2] = {};       // pinned [groups][kMaxDepth]
   uint32_t* host_level_nodes[2] = {};                // pinned [groups][kMaxDepth]
   cudaEvent_t copied[2] = {};                        // the set's copies are complete
+  // Squared error without weights: every Hessian is 1 and the histograms
+  // count rows instead of summing Hessians. Baked into the histogram
+  // configuration and the captured graphs.
+  bool unit_hessian = false;
   int pending = -1;        // set of a launched round not yet turned into trees
   bool pending_captured = false;
   uint32_t parity = 0;
@@ -391,13 +395,16 @@ void Booster::configure() {
   if (state_) state_.reset();  // parameters are baked into captured graphs
 }
 
-void Booster::initialize(DMatrix& d) {
+void Booster::initialize(DMatrix& d, bool custom) {
   require(d.cols > 0, "Data must contain at least one feature.");
   num_feature_ = d.cols;
   base_score_.assign(groups_, 0.5f);
   const auto bs = params_.find("base_score");
   if (bs != params_.end()) {
     base_score_.assign(groups_, std::stof(bs->second));
+  } else if (custom) {
+    // A custom objective starts from 0.5: the intercept is only estimated
+    // for built-in objectives (src/learner.cpp:300-333 in the reference).
   } else {
     d.upload_info(stream_);
     // The intercept is a fixed-order sum over the rows of every rank: with
@@ -464,28 +471,36 @@ void Booster::initialize(DMatrix& d) {
       base_score_[k] = sw > 0 ? float(sy / sw) : (objective_ == kSquaredError && total == 0 ? 0.0f : 0.5f);
     }
   }
-  // Scores to margins (src/objectives.cpp:17-31; the multiclass intercept of
-  // kernels/boost.metal:404-420).
-  base_margin_ = base_score_;
-  if ((objective_ == kSoftprob || objective_ == kSoftmax) && bs == params_.end()) {
-    float mean = 0;
-    for (uint32_t j = 0; j < groups_; ++j) mean += std::log(std::max(base_score_[j], 1.0e-6f));
-    for (uint32_t k = 0; k < groups_; ++k)
-      base_margin_[k] = std::log(std::max(base_score_[k], 1.0e-6f)) - mean / float(groups_);
-    base_score_ = base_margin_;
-  } else if (objective_ == kLogistic) {
-    for (uint32_t k = 0; k < groups_; ++k) {
-      require(base_score_[k] >= 0 && base_score_[k] <= 1, "base_score must be in [0,1] for logistic loss.");
-      const float v = std::min(std::max(base_score_[k], 1.0e-6f), 1.0f - 1.0e-6f);
-      base_margin_[k] = -std::log(1.0f / v - 1.0f);
-    }
-  }
+  base_margin_ = score_margins(base_score_);
+  if ((objective_ == kSoftprob || objective_ == kSoftmax) && bs == params_.end()) base_score_ = base_margin_;
   initialized_ = true;
 }
 
-Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp) {
+// Scores to margins (src/objectives.cpp:17-31; the multiclass intercept of
+// kernels/boost.metal:404-420): logit for logistic loss, centred logs for
+// multiclass scores that were not given as base_score, identity otherwise.
+std::vector<float> Booster::score_margins(const std::vector<float>& scores) const {
+  std::vector<float> m = scores;
+  const size_t G = scores.size();
+  if ((objective_ == kSoftprob || objective_ == kSoftmax) && !params_.count("base_score")) {
+    float mean = 0;
+    for (size_t j = 0; j < G; ++j) mean += std::log(std::max(scores[j], 1.0e-6f));
+    for (size_t k = 0; k < G; ++k) m[k] = std::log(std::max(scores[k], 1.0e-6f)) - mean / float(G);
+  } else if (objective_ == kLogistic) {
+    for (size_t k = 0; k < G; ++k) {
+      require(scores[k] >= 0 && scores[k] <= 1, "base_score must be in [0,1] for logistic loss.");
+      const float v = std::min(std::max(scores[k], 1.0e-6f), 1.0f - 1.0e-6f);
+      m[k] = -std::log(1.0f / v - 1.0f);
+    }
+  }
+  return m;
+}
+
+Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp, bool custom) {
   DMatrix& d = *dp;
-  if (state_ && state_->d == &d && !state_->owner.expired()) return *state_;
+  const bool unit_hessian = !custom && objective_ == kSquaredError && d.weights.empty();
+  if (state_ && state_->d == &d && !state_->owner.expired() && state_->unit_hessian == unit_hessian)
+    return *state_;
   if (state_) {
     finish_pending();
     XGBB_CUDA(cudaStreamSynchronize(stream_));
@@ -497,6 +512,7 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp) {
   ts->rows = d.rows;
   ts->groups = groups_;
   ts->rows_total = d.rows;
+  ts->unit_hessian = unit_hessian;
   if (Comm::get().active()) {
     DeviceBuffer n(8);
     XGBB_CUDA(cudaMemcpyAsync(n.get(), &ts->rows_total, 8, cudaMemcpyHostToDevice, stream_));
@@ -589,7 +605,7 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp) {
   ws.level_rows = ts->level_rows.as<unsigned long long>();
   ws.level_nodes = ts->level_nodes.as<uint32_t>();
   ws.limbs_root = ts->limbs_root.as<int4>();
-  ts->hc = hist_config(e, objective_ == kSquaredError && d.weights.empty());
+  ts->hc = hist_config(e, ts->unit_hessian);
   // One graph per group and round parity: the two differ only in the
   // profiling events they record, so a round's events are read after the
   // next round has been enqueued.
@@ -677,7 +693,7 @@ void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s, b
   tl.margins = ts.margins.as<float>();
   tl.groups = ts.groups;
   tl.group = g;
-  tl.unit_hessian = objective_ == kSquaredError && d.weights.empty();
+  tl.unit_hessian = ts.unit_hessian;
   tl.feature_group = ts.hc.feature_group;
   tl.min_limbs = uint32_t(integer(params_, "cuda_hist_limbs", 0));
   tl.hist_smem = ts.hc.smem;
@@ -738,7 +754,7 @@ static void copy_tree_out(const TreeWorkspace& ws, uint32_t capacity, uint32_t g
                             cudaMemcpyDeviceToHost, s));
 }
 
-void Booster::run_round(TrainState& ts) {
+void Booster::run_round(TrainState& ts, const CustomGradients* custom) {
   // With collectives on the stream, the previous round must have completed
   // before new NCCL calls are enqueued: an enqueue behind a collective that
   // can no longer complete (a rank failed or left) could block inside NCCL,
@@ -754,8 +770,18 @@ void Booster::run_round(TrainState& ts) {
   // Exact gradient masses are summed over ranks, so every rank derives the
   // same power-of-two scales as a single GPU holding all rows would.
   XGBB_CUDA(cudaMemsetAsync(ts.mass.get(), 0, mass_bytes(G), stream_));
-  launch_gradients(objective_, ts.margins.as<float>(), d.d_labels.as<float>(),
-                   d.d_weights.as<float>(), n, G, spw_, pairs, mass, stream_);
+  if (custom) {
+    // Caller-supplied pairs and their largest magnitudes, as the gradient
+    // kernel would have written them. The copies leave pageable memory
+    // before cudaMemcpyAsync returns.
+    if (n) XGBB_CUDA(cudaMemcpyAsync(pairs, custom->pairs.data(), size_t(n) * G * sizeof(float2),
+                                     cudaMemcpyHostToDevice, stream_));
+    XGBB_CUDA(cudaMemcpyAsync(mass.max_bits, custom->max_bits.data(), size_t(2) * G * sizeof(uint32_t),
+                              cudaMemcpyHostToDevice, stream_));
+  } else {
+    launch_gradients(objective_, ts.margins.as<float>(), d.d_labels.as<float>(),
+                     d.d_weights.as<float>(), n, G, spw_, pairs, mass, stream_);
+  }
   comm.max_u32(mass.max_bits, 2 * G, stream_);
   launch_mass_window(pairs, n, G, mass, stream_);
   if (comm.active()) {
@@ -834,7 +860,7 @@ void Booster::finish_round(TrainState& ts) {
     const uint32_t D = tp_.max_depth;
     const Ellpack& e = d.ell;
     const double node_bytes = double(hist_node_bytes(e));
-    const bool unit_h = objective_ == kSquaredError && d.weights.empty();
+    const bool unit_h = ts.unit_hessian;
     const uint32_t min_limbs = uint32_t(integer(params_, "cuda_hist_limbs", 0));
     for (uint32_t g = 0; g < G; ++g) {
       // Per row the histogram reads its codes, its gradient values (the
@@ -879,6 +905,38 @@ void Booster::update(const std::shared_ptr<DMatrix>& d, int) {
   run_round(ts);
 }
 
+void Booster::update_custom(const std::shared_ptr<DMatrix>& d, const float* grad, const float* hess,
+                            size_t count) {
+  configure();
+  const uint32_t n = d->rows, G = groups_;
+  require(count == size_t(n) * G, "Gradient and Hessian must have shape (n_samples, n_targets).");
+  require(count == 0 || (grad != nullptr && hess != nullptr), "Null gradient or Hessian.");
+  // The reference's custom_pairs (src/learner.cpp:728-740): finite values, kept
+  // as given (trees accept negative Hessians).
+  CustomGradients cg;
+  cg.pairs.resize(count);
+  cg.max_bits.assign(size_t(2) * G, 0);
+  for (uint32_t r = 0; r < n; ++r)
+    for (uint32_t k = 0; k < G; ++k) {
+      const float g = grad[size_t(r) * G + k], h = hess[size_t(r) * G + k];
+      require(std::isfinite(g) && std::isfinite(h), "Custom gradients and Hessians must be finite.");
+      cg.pairs[size_t(k) * n + r] = make_float2(g, h);
+      uint32_t bg, bh;
+      std::memcpy(&bg, &g, 4);
+      std::memcpy(&bh, &h, 4);
+      cg.max_bits[2 * k] = std::max(cg.max_bits[2 * k], bg & 0x7fffffffu);
+      cg.max_bits[2 * k + 1] = std::max(cg.max_bits[2 * k + 1], bh & 0x7fffffffu);
+    }
+  gpu();
+  d->upload_info(stream_);
+  if (!initialized_) initialize(*d, true);
+  require(d->cols == num_feature_, "Number of columns does not match the trained model.");
+  if (!d->quantised() || d->max_bin != max_bin_)
+    d->quantise(max_bin_, nullptr, stream_, int(integer(params_, "nthread", 0)));
+  TrainState& ts = train_state(d, true);
+  run_round(ts, &cg);
+}
+
 void Booster::sync() {
   if (stream_) wait_stream("the booster's work");
   finish_pending();
@@ -919,7 +977,13 @@ std::vector<float> Booster::predict(const std::shared_ptr<DMatrix>& dp, bool out
   require(!initialized_ || d.cols == num_feature_ || d.rows == 0, "Feature shape mismatch.");
   if (end == 0 || end > rounds_) end = rounds_;
   std::vector<float> out(size_t(d.rows) * G);
-  std::vector<float> base = initialized_ ? base_margin_ : std::vector<float>(G, 0.5f);
+  // Before the first round: the margins of base_score (0.5 unless given) that
+  // the first round starts from.
+  std::vector<float> base = base_margin_;
+  if (!initialized_) {
+    const auto bs = params_.find("base_score");
+    base = score_margins(std::vector<float>(G, bs != params_.end() ? std::stof(bs->second) : 0.5f));
+  }
   if (d.rows) {
     DeviceBuffer dout(out.size() * 4), dbase(G * 4);
     XGBB_CUDA(cudaMemcpyAsync(dbase.get(), base.data(), G * 4, cudaMemcpyHostToDevice, stream_));

@@ -109,6 +109,9 @@ class Booster {
   void set_param(const std::string& key, const std::string& value);
   std::string get_param(const std::string& key, const std::string& def) const;
   void update(const std::shared_ptr<DMatrix>& d, int iteration);
+  // One round from caller-supplied gradients and Hessians, `count` values
+  // each in row-major [rows][groups] order (a custom objective).
+  void update_custom(const std::shared_ptr<DMatrix>& d, const float* grad, const float* hess, size_t count);
   // Returns values [rows][groups] (margins if output_margin).
   std::vector<float> predict(const std::shared_ptr<DMatrix>& d, bool output_margin,
                              uint32_t iter_begin, uint32_t iter_end, bool training,
@@ -141,9 +144,15 @@ class Booster {
  private:
   struct TrainState;
   void configure();
-  void initialize(DMatrix& d);
-  TrainState& train_state(const std::shared_ptr<DMatrix>& d);
-  void run_round(TrainState& ts);
+  // Gradient pairs of a custom objective in the device layout [groups][rows],
+  // and per group the largest |g| and |h| bit patterns.
+  struct CustomGradients {
+    std::vector<float2> pairs;
+    std::vector<uint32_t> max_bits;
+  };
+  void initialize(DMatrix& d, bool custom = false);
+  TrainState& train_state(const std::shared_ptr<DMatrix>& d, bool custom = false);
+  void run_round(TrainState& ts, const CustomGradients* custom = nullptr);
   void finish_round(TrainState& ts);
   void gpu();  // makes the booster's device current; fails without a GPU
   void wait_stream(const char* what);
@@ -151,6 +160,7 @@ class Booster {
                             uint32_t parity);
   void materialize();
   Json model_param_json() const;
+  std::vector<float> score_margins(const std::vector<float>& scores) const;
   Json objective_json() const;
 
   std::map<std::string, std::string> params_;

@@ -330,6 +330,14 @@ class Booster:
         if cache:
             self.feature_names = cache[0].feature_names
             self.feature_types = cache[0].feature_types
+        if isinstance(model_file, Booster):
+            # Model and configuration of another booster, as pickling copies them.
+            buf = model_file.__getstate__()["handle"]
+            _check_call(_LIB.XGBoosterUnserializeFromBuffer(self.handle, ctypes.c_char_p(buf),
+                                                            c_bst_ulong(len(buf))))
+        elif model_file is not None:
+            self.load_model(model_file)
+        # Parameters given here override those of a loaded model, as upstream.
         params = params or {}
         if isinstance(params, dict):
             items = list(params.items())
@@ -339,8 +347,6 @@ class Booster:
             if k == "eval_metric":
                 continue
             self.set_param(k, v)
-        if model_file is not None:
-            self.load_model(model_file)
 
     def __del__(self):
         if _LIB is not None and getattr(self, "handle", None) is not None and self.handle.value:
@@ -399,9 +405,28 @@ class Booster:
             _check_call(_LIB.XGBoosterSetParam(self.handle, _c_str(str(k)), _c_str(str(v))))
 
     def update(self, dtrain, iteration, fobj=None):
-        if fobj is not None:
-            raise XGBoostError("Custom objectives are not implemented by the CUDA backend yet.")
-        _check_call(_LIB.XGBoosterUpdateOneIter(self.handle, ctypes.c_int(iteration), dtrain.handle))
+        """One boosting round; with `fobj(margins, dtrain) -> (grad, hess)` the
+        round trains on a custom objective's gradients."""
+        if fobj is None:
+            _check_call(_LIB.XGBoosterUpdateOneIter(self.handle, ctypes.c_int(iteration),
+                                                    dtrain.handle))
+            return
+        pred = self.predict(dtrain, output_margin=True, training=True)
+        grad, hess = fobj(pred, dtrain)
+        self.boost(dtrain, iteration, grad, hess)
+
+    def boost(self, dtrain, iteration, grad, hess):
+        """One round from gradients and Hessians of shape (rows,) or
+        (rows, groups) (XGBoosterTrainOneIter)."""
+        g = np.ascontiguousarray(np.asarray(grad, dtype=np.float32))
+        h = np.ascontiguousarray(np.asarray(hess, dtype=np.float32))
+        if g.shape != h.shape:
+            raise ValueError("grad / hess shape mismatch: %s / %s" % (g.shape, h.shape))
+        if g.ndim == 2 and g.shape[1] == 1:
+            g, h = g.reshape(-1), h.reshape(-1)
+        _check_call(_LIB.XGBoosterTrainOneIter(self.handle, dtrain.handle, ctypes.c_int(iteration),
+                                               _c_str(_array_interface(g)),
+                                               _c_str(_array_interface(h))))
 
     def num_boosted_rounds(self):
         out = ctypes.c_int()

@@ -36,19 +36,17 @@ def _default_metric(params):
 def train(params, dtrain, num_boost_round=10, *, evals=None, obj=None, maximize=None,
           early_stopping_rounds=None, evals_result=None, verbose_eval=True, xgb_model=None,
           callbacks=None, custom_metric=None):
-    if obj is not None:
-        raise XGBoostError("Custom objectives are not implemented by the CUDA backend yet.")
-    if xgb_model is not None:
-        raise XGBoostError("Continued training from a saved model is not implemented yet.")
     params = dict(params or {})
     metrics = params.pop("eval_metric", None)
     if isinstance(metrics, str):
         metrics = [metrics]
     evals = list(evals or [])
-    bst = Booster(params, [dtrain] + [d for d, _ in evals])
+    # xgb_model (a Booster, a model file or its bytes) is trained on: the new
+    # rounds are appended to its trees.
+    bst = Booster(params, [dtrain] + [d for d, _ in evals], model_file=xgb_model)
     history = {}
     for i in range(int(num_boost_round)):
-        bst.update(dtrain, i)
+        bst.update(dtrain, i, fobj=obj)
         if evals:
             names = metrics or [_default_metric(params)]
             parts = []
