@@ -43,6 +43,11 @@ XGB_DLL int XGBBQuantizeHost(const float* X, bst_ulong rows, bst_ulong cols, uin
  * GPU. */
 XGB_DLL int XGBBSketchHost(const float* X, bst_ulong rows, bst_ulong cols, const float* weights,
                            uint32_t max_bin, int threads, float* cuts, uint32_t* counts, float* minima);
+/* One evaluation metric of transformed predictions [rows][groups] (the
+ * metric side of XGBoosterEvalOneIter, src/metrics.cpp:8-158); weights may
+ * be NULL. Needs no GPU. */
+XGB_DLL int XGBBMetricHost(char const* name, const float* pred, bst_ulong rows, uint32_t groups,
+                           const float* labels, const float* weights, int multiclass, double* out);
 /* Gradient pairs [groups][rows][2] and power-of-two scales [groups][2]: the
  * reference's gradients + gradient_partial_sums + gradient_scales
  * (kernels/boost.metal:553-601, kernels/gradient_quantization.metal.h:1-67). */

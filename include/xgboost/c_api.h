@@ -128,6 +128,12 @@ XGB_DLL int XGBoosterSetParams(BoosterHandle handle, char const* config);
 XGB_DLL int XGBoosterGetNumFeature(BoosterHandle handle, bst_ulong* out);
 /* include/xgboost/c_api.h:1095 (src/c_api.cpp:484): one boosting round on the GPU. */
 XGB_DLL int XGBoosterUpdateOneIter(BoosterHandle handle, int iter, DMatrixHandle dtrain);
+/* include/xgboost/c_api.h:1134 (src/c_api.cpp:498-500, src/learner.cpp:1025-1048):
+ * "[iter]\t<name>-<metric>:<value>" over the given matrices for every
+ * eval_metric (rmse, mae, rmsle, mape, logloss, error[@t], merror, mlogloss,
+ * auc), or the objective's default metric. */
+XGB_DLL int XGBoosterEvalOneIter(BoosterHandle handle, int iter, DMatrixHandle dmats[], const char* evnames[],
+                                 bst_ulong len, const char** out_result);
 /* include/xgboost/c_api.h:1121 (src/c_api.cpp:485-487): one round from a custom
  * objective; grad and hess are __array_interface__ JSON of shape (rows,) or
  * (rows, groups), finite. Without base_score the intercept is 0.5. */

@@ -121,3 +121,33 @@ def test_custom_softmax_objective_learns_and_continues_from_a_model():
     more = xgb.train(params, d, 2, obj=softmax_obj, xgb_model=b)
     assert more.num_boosted_rounds() == 10 and b.num_boosted_rounds() == 8
     np.testing.assert_array_equal(more[:8].predict(fresh, output_margin=True), margin)
+
+
+def test_native_evaluation_and_early_stopping():
+    rng = np.random.default_rng(15)
+    X = rng.normal(size=(4000, 5)).astype(np.float32)
+    y = (X[:, 0] > 0).astype(np.float32)
+    Xv = rng.normal(size=(1500, 5)).astype(np.float32)
+    yv = (Xv[:, 0] > 0).astype(np.float32)
+    d, dv = xgb.DMatrix(X, label=y), xgb.DMatrix(Xv, label=yv)
+    params = {"objective": "binary:logistic", "tree_method": "hist", "device": "cuda", "max_depth": 3,
+              "eval_metric": ["logloss", "auc", "error"]}
+    hist = {}
+    b = xgb.train(params, d, 4, evals=[(d, "train"), (dv, "valid")], evals_result=hist, verbose_eval=False)
+    assert sorted(hist) == ["train", "valid"] and sorted(hist["valid"]) == ["auc", "error", "logloss"]
+    assert all(len(v) == 4 for v in hist["valid"].values())
+    p = b.predict(dv)
+    ll = float(np.mean(-yv * np.log(np.maximum(p, 1e-16)) - (1 - yv) * np.log(np.maximum(1 - p, 1e-16))))
+    assert hist["valid"]["logloss"][-1] == pytest.approx(ll, rel=1e-5)
+    assert hist["valid"]["error"][-1] == pytest.approx(float(np.mean((p > 0.5) != (yv > 0.5))), abs=1e-9)
+    line = b.eval(dv, "v", 7)
+    assert line.startswith("[7]\tv-logloss:") and "\tv-auc:" in line
+    # Pure-noise labels: the validation loss stops improving quickly.
+    noise = xgb.DMatrix(X, label=rng.random(4000).astype(np.float32))
+    vnoise = xgb.DMatrix(Xv, label=rng.random(1500).astype(np.float32))
+    es = xgb.train({"tree_method": "hist", "device": "cuda", "max_depth": 6, "eta": 1.0}, noise, 50,
+                   evals=[(vnoise, "valid")], early_stopping_rounds=2, verbose_eval=False)
+    assert es.num_boosted_rounds() < 50
+    assert es.num_boosted_rounds() == es.best_iteration + 1 + 2
+    best_line = es[: es.best_iteration + 1].eval(vnoise, "valid")
+    assert float(best_line.rsplit(":", 1)[1]) == pytest.approx(es.best_score, rel=1e-9)

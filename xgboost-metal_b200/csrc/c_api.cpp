@@ -17,6 +17,7 @@
 #include "comm.h"
 #include "json.h"
 #include "learner.h"
+#include "metrics.h"
 #include "model_dump.h"
 #include "sketch.h"
 #include "xgb_b200.h"
@@ -626,6 +627,21 @@ XGB_DLL int XGBoosterGetNumFeature(BoosterHandle handle, bst_ulong* out) {
   return guarded([&] { *out = booster(handle).num_feature(); });
 }
 
+XGB_DLL int XGBoosterEvalOneIter(BoosterHandle handle, int iter, DMatrixHandle dmats[], const char* evnames[],
+                                 bst_ulong len, const char** out_result) {
+  return guarded([&] {
+    std::vector<DMatrixPtr> data;
+    std::vector<std::string> names;
+    for (bst_ulong i = 0; i < len; ++i) {
+      data.push_back(dmat(dmats[i]));
+      require(evnames && evnames[i], "Null evaluation name.");
+      names.emplace_back(evnames[i]);
+    }
+    results.str = booster(handle).evaluate(iter, data, names);
+    *out_result = results.str.c_str();
+  });
+}
+
 XGB_DLL int XGBoosterUpdateOneIter(BoosterHandle handle, int iter, DMatrixHandle dtrain) {
   return guarded([&] { booster(handle).update(dmat(dtrain), iter); });
 }
@@ -1123,6 +1139,16 @@ XGB_DLL int XGBBQuantizeHost(const float* X, bst_ulong rows, bst_ulong cols, uin
 }
 
 // Test entry: the host quantile sketch on its own (no device needed).
+XGB_DLL int XGBBMetricHost(char const* name, const float* pred, bst_ulong rows, uint32_t groups,
+                           const float* labels, const float* weights, int multiclass, double* out) {
+  return guarded([&] {
+    require(name != nullptr && out != nullptr, "Null argument.");
+    require(rows == 0 || (pred != nullptr && labels != nullptr), "Null predictions or labels.");
+    require(rows < (1ull << 32) && groups >= 1, "Invalid shape.");
+    *out = xgbb::eval_metric(name, pred, uint32_t(rows), groups, labels, weights, multiclass != 0);
+  });
+}
+
 XGB_DLL int XGBBSketchHost(const float* X, bst_ulong rows, bst_ulong cols, const float* weights,
                            uint32_t max_bin, int threads, float* cuts, uint32_t* counts, float* minima) {
   return guarded([&] {

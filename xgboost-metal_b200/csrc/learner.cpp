@@ -13,6 +13,7 @@
 
 #include "comm.h"
 #include "json.h"
+#include "metrics.h"
 #include "sketch.h"
 
 namespace xgbb {
@@ -311,8 +312,71 @@ void Booster::set_param(const std::string& key, const std::string& value) {
       {"eta", "learning_rate"}, {"lambda", "reg_lambda"}, {"alpha", "reg_alpha"},
       {"gamma", "min_split_loss"}};
   auto it = alias.find(key);
+  if (key == "eval_metric") {
+    // Each setting adds a metric to the list (upstream Learner::SetParam).
+    std::string& list = params_["eval_metric"];
+    size_t b = 0;
+    bool present = false;
+    while (b <= list.size() && !list.empty()) {
+      size_t e = list.find(',', b);
+      if (e == std::string::npos) e = list.size();
+      present = present || list.compare(b, e - b, value) == 0;
+      b = e + 1;
+    }
+    if (!present && !value.empty()) list += (list.empty() ? "" : ",") + value;
+    return;
+  }
   params_[it == alias.end() ? key : it->second] = value;
   configured_ = false;
+}
+
+// "[iteration]\t<name>-<metric>:<value>..." for every matrix and metric (the
+// reference's Learner::evaluate, src/learner.cpp:1025-1048).
+std::string Booster::evaluate(int iteration, const std::vector<std::shared_ptr<DMatrix>>& data,
+                              const std::vector<std::string>& names) {
+  configure();
+  require(data.empty() || initialized_, "Model is not yet initialized (not fitted).");
+  std::vector<std::string> metrics;
+  const std::string list = get_param("eval_metric", "");
+  for (size_t b = 0; b < list.size();) {
+    size_t e = list.find(',', b);
+    if (e == std::string::npos) e = list.size();
+    if (e > b) metrics.push_back(list.substr(b, e - b));
+    b = e + 1;
+  }
+  const std::string disable = get_param("disable_default_eval_metric", "0");
+  if (metrics.empty() && (disable.empty() || std::stod(disable) == 0))
+    metrics.push_back(default_metric(get_param("objective", "reg:squarederror")));
+  const bool multiclass = objective_ == kSoftprob || objective_ == kSoftmax;
+  std::string out = "[" + std::to_string(iteration) + "]";
+  for (size_t i = 0; i < data.size(); ++i) {
+    DMatrix& d = *data[i];
+    std::vector<uint64_t> shape;
+    std::vector<float> pred;
+    if (objective_ == kSoftmax) {
+      // Metrics read class probabilities, not the predicted classes.
+      pred = predict(data[i], true, 0, 0, false, shape);
+      for (uint32_t r = 0; r < d.rows; ++r) {
+        float* row = pred.data() + size_t(r) * groups_;
+        const float mx = *std::max_element(row, row + groups_);
+        double sum = 0;
+        for (uint32_t k = 0; k < groups_; ++k) sum += std::exp(double(row[k] - mx));
+        for (uint32_t k = 0; k < groups_; ++k) row[k] = float(std::exp(double(row[k] - mx)) / sum);
+      }
+    } else {
+      pred = predict(data[i], false, 0, 0, false, shape);
+    }
+    for (const std::string& m : metrics) {
+      require(d.labels.size() == d.rows, "Evaluation data requires labels.");
+      require(d.weights.empty() || d.weights.size() == d.rows, "Evaluation weights must have one entry per row.");
+      const double v = eval_metric(m, pred.data(), d.rows, groups_, d.labels.data(),
+                                   d.weights.empty() ? nullptr : d.weights.data(), multiclass);
+      char buf[64];
+      std::snprintf(buf, sizeof buf, "%.10g", v);
+      out += "\t" + names[i] + "-" + m + ":" + buf;
+    }
+  }
+  return out;
 }
 
 std::string Booster::get_param(const std::string& key, const std::string& def) const {

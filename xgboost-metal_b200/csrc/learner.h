@@ -125,6 +125,9 @@ class Booster {
   void finish_pending();
   std::string save_json();
   void load_json(const std::string& text);
+  // Evaluation line of XGBoosterEvalOneIter.
+  std::string evaluate(int iteration, const std::vector<std::shared_ptr<DMatrix>>& data,
+                       const std::vector<std::string>& names);
   // Training configuration (upstream layout) and its inverse.
   std::string config_json();
   void load_config(const std::string& text);

@@ -344,7 +344,9 @@ class Booster:
         else:
             items = list(params)
         for k, v in items:
-            if k == "eval_metric":
+            if k == "eval_metric" and isinstance(v, (list, tuple)):
+                for m in v:  # each setting adds one metric
+                    self.set_param(k, m)
                 continue
             self.set_param(k, v)
 
@@ -498,6 +500,44 @@ class Booster:
         finally:
             if proxy is not None:
                 _LIB.XGDMatrixFree(proxy)
+
+    # -- evaluation (python-package/xgboost/core.py eval_set / eval) ---------
+    def eval_set(self, evals, iteration=0, feval=None, output_margin=True):
+        """"[iteration]\tname-metric:value..." for every (DMatrix, name) pair
+        (XGBoosterEvalOneIter), plus feval(predictions, dmatrix) -> (name,
+        value) or a list of them."""
+        for d, name in evals:
+            if not isinstance(d, DMatrix) or not isinstance(name, str):
+                raise TypeError("evals must be a list of (DMatrix, str) pairs")
+        dmats = (ctypes.c_void_p * len(evals))(*[d.handle.value for d, _ in evals])
+        names = (ctypes.c_char_p * len(evals))(*[n.encode() for _, n in evals])
+        msg = ctypes.c_char_p()
+        _check_call(_LIB.XGBoosterEvalOneIter(self.handle, ctypes.c_int(iteration), dmats, names,
+                                              c_bst_ulong(len(evals)), ctypes.byref(msg)))
+        res = msg.value.decode()
+        if feval is not None:
+            for d, evname in evals:
+                ret = feval(self.predict(d, training=False, output_margin=output_margin), d)
+                for name, val in (ret if isinstance(ret, list) else [ret]):
+                    res += "\t%s-%s:%f" % (evname, name, val)
+        return res
+
+    def eval(self, data, name="eval", iteration=0):
+        return self.eval_set([(data, name)], iteration)
+
+    @property
+    def best_iteration(self):
+        v = self.attr("best_iteration")
+        if v is None:
+            raise AttributeError("`best_iteration` is only defined when early stopping is used.")
+        return int(v)
+
+    @property
+    def best_score(self):
+        v = self.attr("best_score")
+        if v is None:
+            raise AttributeError("`best_score` is only defined when early stopping is used.")
+        return float(v)
 
     def attr(self, key):
         out = ctypes.c_char_p()

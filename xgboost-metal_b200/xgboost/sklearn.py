@@ -101,7 +101,7 @@ class XGBModel:
                 self.n_classes_ = meta["n_classes_"]
             self._Booster.set_attr(scikit_learn=None)
 
-    def _fit(self, X, y, sample_weight, eval_set, verbose, params):
+    def _fit(self, X, y, sample_weight, eval_set, verbose, params, xgb_model=None):
         dtrain = DMatrix(X, y, weight=sample_weight,
                          missing=np.nan if self.missing is None else self.missing)
         evals = []
@@ -111,16 +111,35 @@ class XGBModel:
         if self.eval_metric is not None:
             params["eval_metric"] = self.eval_metric
         self._Booster = train(params, dtrain, self.n_estimators, evals=evals,
-                              evals_result=self.evals_result_, verbose_eval=bool(verbose))
+                              evals_result=self.evals_result_, verbose_eval=verbose,
+                              early_stopping_rounds=self.early_stopping_rounds,
+                              xgb_model=xgb_model.get_booster() if isinstance(xgb_model, XGBModel)
+                              else xgb_model)
         self.n_features_in_ = dtrain.num_col()
         return self
+
+    def _iteration_range(self, iteration_range):
+        """All rounds, or up to the best one after early stopping
+        (python-package/xgboost/sklearn.py _get_iteration_range)."""
+        if iteration_range is not None and tuple(iteration_range) != (0, 0):
+            return tuple(iteration_range)
+        best = self.get_booster().attr("best_iteration")
+        return (0, int(best) + 1) if best is not None else (0, 0)
+
+    @property
+    def best_iteration(self):
+        return self.get_booster().best_iteration
+
+    @property
+    def best_score(self):
+        return self.get_booster().best_score
 
     def predict(self, X, output_margin=False, validate_features=True, base_margin=None,
                 iteration_range=None):
         dm = DMatrix(X, missing=np.nan if self.missing is None else self.missing,
                      base_margin=base_margin)
         return self.get_booster().predict(dm, output_margin=output_margin,
-                                          iteration_range=iteration_range or (0, 0))
+                                          iteration_range=self._iteration_range(iteration_range))
 
 
 class XGBRegressor(XGBModel):
@@ -130,7 +149,7 @@ class XGBRegressor(XGBModel):
     def fit(self, X, y, *, sample_weight=None, base_margin=None, eval_set=None, verbose=True,
             xgb_model=None, sample_weight_eval_set=None, base_margin_eval_set=None,
             feature_weights=None):
-        return self._fit(X, y, sample_weight, eval_set, verbose, self.get_xgb_params())
+        return self._fit(X, y, sample_weight, eval_set, verbose, self.get_xgb_params(), xgb_model)
 
 
 class XGBClassifier(XGBModel):
@@ -151,7 +170,7 @@ class XGBClassifier(XGBModel):
             params["num_class"] = self.n_classes_
         eval_set = [(ex, np.searchsorted(self.classes_, np.asarray(ey)).astype(np.float32))
                     for ex, ey in (eval_set or [])]
-        return self._fit(X, encoded, sample_weight, eval_set, verbose, params)
+        return self._fit(X, encoded, sample_weight, eval_set, verbose, params, xgb_model)
 
     def predict_proba(self, X, validate_features=True, base_margin=None, iteration_range=None):
         p = super().predict(X, base_margin=base_margin, iteration_range=iteration_range)
