@@ -13,9 +13,11 @@
 
 #ifdef __cplusplus
 #define XGB_EXTERN_C extern "C"
+#include <cstddef>
 #include <cstdint>
 #else
 #define XGB_EXTERN_C
+#include <stddef.h>
 #include <stdint.h>
 #endif
 
@@ -26,6 +28,23 @@ typedef void* DMatrixHandle;
 typedef void* BoosterHandle;
 /* include/xgboost/c_api.h:371-474: the caller's batch iterator. */
 typedef void* DataIterHandle;
+/* include/xgboost/c_api.h:373-420: the JVM packages' batch iterator. */
+typedef void* DataHolderHandle;
+typedef struct {
+  size_t size;      /* rows in the batch */
+  size_t columns;   /* columns of the batch */
+  int64_t* offset;  /* size + 1 row offsets */
+  float* label;     /* size labels, or NULL */
+  float* weight;    /* size weights, or NULL */
+  int* index;       /* feature indices */
+  float* value;     /* feature values */
+} XGBoostBatchCSR;
+typedef int XGBCallbackSetData(DataHolderHandle handle, XGBoostBatchCSR batch);
+typedef int XGBCallbackDataIterNext(DataIterHandle data_handle, XGBCallbackSetData* set_function,
+                                    DataHolderHandle set_function_handle);
+/* include/xgboost/c_api.h:57, 1671 */
+typedef void* CategoriesHandle;
+typedef void* TrackerHandle;
 typedef int XGDMatrixCallbackNext(DataIterHandle iter);
 typedef void DataIterResetCallback(DataIterHandle handle);
 
@@ -94,6 +113,79 @@ XGB_DLL int XGDMatrixCreateFromBufferDescriptor(XGBufferDescriptor const* desc, 
 /* include/xgboost/c_api.h:1881: fields as XGDMatrixSetInfoFromInterface. */
 XGB_DLL int XGDMatrixSetInfoFromBufferDescriptor(DMatrixHandle handle, char const* field,
                                                  XGBufferDescriptor const* desc);
+/* include/xgboost/c_api.h:254 (src/c_api.cpp:201): CSC; nrow 0 = from indices. */
+XGB_DLL int XGDMatrixCreateFromCSC(char const* indptr, char const* indices, char const* data, bst_ulong nrow,
+                                   char const* config, DMatrixHandle* out);
+/* include/xgboost/c_api.h:260 */
+XGB_DLL int XGDMatrixCreateFromCOO(char const* row_idx, char const* col_idx, char const* data, bst_ulong nrow,
+                                   bst_ulong ncol, char const* config, DMatrixHandle* out);
+/* include/xgboost/c_api.h:205: a JSON list of column array interfaces. */
+XGB_DLL int XGDMatrixCreateFromColumnar(char const* data, char const* config, DMatrixHandle* out);
+/* include/xgboost/c_api.h:1879 */
+XGB_DLL int XGDMatrixCreateFromColumnarBuffers(XGBufferDescriptor const* columns, bst_ulong ncol, float missing,
+                                               DMatrixHandle* out);
+/* include/xgboost/c_api.h:285 */
+XGB_DLL int XGDMatrixCreateFromMat_omp(const float* data, bst_ulong nrow, bst_ulong ncol, float missing,
+                                       DMatrixHandle* out, int nthread);
+/* include/xgboost/c_api.h:314, 300: device arrays, copied to the host. */
+XGB_DLL int XGDMatrixCreateFromCudaArrayInterface(char const* data, char const* config, DMatrixHandle* out);
+XGB_DLL int XGDMatrixCreateFromCudaColumnar(char const* data, char const* config, DMatrixHandle* out);
+/* include/xgboost/c_api.h:1883 (src/c_api.cpp:872-930): a 2-D DLPack tensor on the
+ * host or a CUDA device; its deleter runs before the call returns. */
+XGB_DLL int XGDMatrixCreateFromDLPack(void* dl_managed_tensor, int is_versioned, float missing,
+                                      DMatrixHandle* out);
+/* include/xgboost/c_api.h:1885 (src/c_api.cpp:930-983): an Arrow C-data struct of
+ * primitive columns (or one column); schema and array are released. */
+XGB_DLL int XGDMatrixCreateFromArrow(void const* arrow_schema, void const* arrow_array, float missing,
+                                     DMatrixHandle* out);
+/* include/xgboost/c_api.h:431: CSR batches from the legacy iterator. */
+XGB_DLL int XGDMatrixCreateFromDataIter(DataIterHandle data_handle, XGBCallbackDataIterNext* callback,
+                                        const char* cache_info, float missing, DMatrixHandle* out);
+/* include/xgboost/c_api.h:149 (src/c_api.cpp:364-438): {"uri": "path?format=csv"
+ * (label_column=K) or "path?format=libsvm"}. */
+XGB_DLL int XGDMatrixCreateFromURI(char const* config, DMatrixHandle* out);
+/* include/xgboost/c_api.h:681: not implemented (returns -1). */
+XGB_DLL int XGDMatrixSaveBinary(DMatrixHandle handle, const char* fname, int silent);
+/* include/xgboost/c_api.h:849: type 1 f32, 2 f64, 3 u32, 4 u64. */
+XGB_DLL int XGDMatrixSetDenseInfo(DMatrixHandle handle, const char* field, void const* data, bst_ulong size,
+                                  int type);
+/* include/xgboost/c_api.h:710 */
+XGB_DLL int XGDMatrixSetUIntInfo(DMatrixHandle handle, const char* field, const unsigned* array, bst_ulong len);
+/* include/xgboost/c_api.h:892: "group_ptr", always empty. */
+XGB_DLL int XGDMatrixGetUIntInfo(const DMatrixHandle handle, const char* field, bst_ulong* out_len,
+                                 const unsigned** out_dptr);
+/* include/xgboost/c_api.h:868: array interface of the matrix's own metadata. */
+XGB_DLL int XGDMatrixGetInfoRef(DMatrixHandle handle, char const* field, char const** out_array);
+/* include/xgboost/c_api.h:739, 777: "feature_name" / "feature_type". */
+XGB_DLL int XGDMatrixSetStrFeatureInfo(DMatrixHandle handle, const char* field, const char** features,
+                                       const bst_ulong size);
+XGB_DLL int XGDMatrixGetStrFeatureInfo(DMatrixHandle handle, const char* field, bst_ulong* size,
+                                       const char*** out_features);
+/* include/xgboost/c_api.h:929 */
+XGB_DLL int XGDMatrixDataSplitMode(DMatrixHandle handle, bst_ulong* out);
+/* include/xgboost/c_api.h:1897 */
+XGB_DLL int XGDMatrixWasZeroCopied(DMatrixHandle handle, int* out);
+/* include/xgboost/c_api.h:951 */
+XGB_DLL int XGDMatrixGetDataAsCSR(DMatrixHandle const handle, char const* config, bst_ulong* out_indptr,
+                                  unsigned* out_indices, float* out_data);
+/* include/xgboost/c_api.h:969: per feature -inf then its cuts (array interfaces). */
+XGB_DLL int XGDMatrixGetQuantileCut(DMatrixHandle const handle, char const* config, char const** out_indptr,
+                                    char const** out_data);
+/* include/xgboost/c_api.h:648, 659 */
+XGB_DLL int XGDMatrixSliceDMatrix(DMatrixHandle handle, const int* idxset, bst_ulong len, DMatrixHandle* out);
+XGB_DLL int XGDMatrixSliceDMatrixEx(DMatrixHandle handle, const int* idxset, bst_ulong len, DMatrixHandle* out,
+                                    int allow_groups);
+/* include/xgboost/c_api.h:1894 (src/c_api.cpp:1017-1117): nfold train/test pairs. */
+XGB_DLL int XGDMatrixBuildCVFolds(DMatrixHandle handle, int nfold, unsigned seed, int shuffle, int stratified,
+                                  DMatrixHandle* out_train, DMatrixHandle* out_test);
+/* include/xgboost/c_api.h:810-842: numerical splits only, so the handle is NULL. */
+XGB_DLL int XGDMatrixGetCategories(DMatrixHandle handle, char const* config, CategoriesHandle* out);
+XGB_DLL int XGDMatrixGetCategoriesExportToArrow(DMatrixHandle handle, char const* config, CategoriesHandle* out,
+                                                char const** export_out);
+XGB_DLL int XGBoosterGetCategories(BoosterHandle handle, char const* config, CategoriesHandle* out);
+XGB_DLL int XGBoosterGetCategoriesExportToArrow(BoosterHandle handle, char const* config, CategoriesHandle* out,
+                                                char const** export_out);
+XGB_DLL int XGBCategoriesFree(CategoriesHandle handle);
 /* include/xgboost/c_api.h:460: the batch holder filled by an iterator's next(). */
 XGB_DLL int XGProxyDMatrixCreate(DMatrixHandle* out);
 /* include/xgboost/c_api.h:622 */
@@ -101,6 +193,10 @@ XGB_DLL int XGProxyDMatrixSetDataDense(DMatrixHandle handle, char const* data);
 /* include/xgboost/c_api.h:635 */
 XGB_DLL int XGProxyDMatrixSetDataCSR(DMatrixHandle handle, char const* indptr, char const* indices,
                                      char const* data, bst_ulong ncol);
+/* include/xgboost/c_api.h:601, 591, 611 */
+XGB_DLL int XGProxyDMatrixSetDataColumnar(DMatrixHandle handle, char const* data);
+XGB_DLL int XGProxyDMatrixSetDataCudaArrayInterface(DMatrixHandle handle, const char* data);
+XGB_DLL int XGProxyDMatrixSetDataCudaColumnar(DMatrixHandle handle, const char* data);
 /* include/xgboost/c_api.h:499 (src/c_api.cpp:140-157, 222-224): batches
  * concatenated on the host; config {"missing"}. */
 XGB_DLL int XGDMatrixCreateFromCallback(DataIterHandle iter, DMatrixHandle proxy,
@@ -112,6 +208,11 @@ XGB_DLL int XGDMatrixCreateFromCallback(DataIterHandle iter, DMatrixHandle proxy
 XGB_DLL int XGQuantileDMatrixCreateFromCallback(DataIterHandle iter, DMatrixHandle proxy, DataIterHandle ref,
                                                 DataIterResetCallback* reset, XGDMatrixCallbackNext* next,
                                                 char const* config, DMatrixHandle* out);
+/* include/xgboost/c_api.h:576: in host memory, as the callback QuantileDMatrix. */
+XGB_DLL int XGExtMemQuantileDMatrixCreateFromCallback(DataIterHandle iter, DMatrixHandle proxy,
+                                                      DataIterHandle ref, DataIterResetCallback* reset,
+                                                      XGDMatrixCallbackNext* next, char const* config,
+                                                      DMatrixHandle* out);
 
 /* --- Booster -------------------------------------------------------------- */
 /* include/xgboost/c_api.h:996 (src/c_api.cpp:442-452) */
@@ -159,6 +260,32 @@ XGB_DLL int XGBoosterPredict(BoosterHandle handle, DMatrixHandle dmat, int optio
 XGB_DLL int XGBoosterPredictFromDense(BoosterHandle handle, char const* values, char const* config,
                                       DMatrixHandle m, bst_ulong const** out_shape, bst_ulong* out_dim,
                                       const float** out_result);
+/* include/xgboost/c_api.h:1289, 1261, 1313, 1337, 1887: in-place prediction from
+ * CSR, columnar, CUDA and buffer-descriptor inputs (config as PredictFromDense). */
+XGB_DLL int XGBoosterPredictFromCSR(BoosterHandle handle, char const* indptr, char const* indices,
+                                    char const* values, bst_ulong ncol, char const* config, DMatrixHandle m,
+                                    bst_ulong const** out_shape, bst_ulong* out_dim, const float** out_result);
+XGB_DLL int XGBoosterPredictFromColumnar(BoosterHandle handle, char const* values, char const* config,
+                                         DMatrixHandle m, bst_ulong const** out_shape, bst_ulong* out_dim,
+                                         const float** out_result);
+XGB_DLL int XGBoosterPredictFromCudaArray(BoosterHandle handle, char const* values, char const* config,
+                                          DMatrixHandle proxy, bst_ulong const** out_shape, bst_ulong* out_dim,
+                                          const float** out_result);
+XGB_DLL int XGBoosterPredictFromCudaColumnar(BoosterHandle handle, char const* data, char const* config,
+                                             DMatrixHandle proxy, bst_ulong const** out_shape, bst_ulong* out_dim,
+                                             const float** out_result);
+XGB_DLL int XGBoosterPredictFromBufferDescriptor(BoosterHandle handle, XGBufferDescriptor const* desc,
+                                                 char const* config, DMatrixHandle proxy,
+                                                 bst_ulong const** out_shape, bst_ulong* out_dim,
+                                                 float const** out_result);
+/* include/xgboost/c_api.h:1891 (src/c_api.cpp:1000-1016): into the caller's buffer. */
+XGB_DLL int XGBoosterPredictToBuffer(BoosterHandle handle, DMatrixHandle dmat, char const* config,
+                                     float* out_buffer, bst_ulong out_capacity, bst_ulong const** out_shape,
+                                     bst_ulong* out_dim);
+/* include/metalgb/c_api.h:17: vector-leaf trees are not grown (returns -1). */
+XGB_DLL int XGBoosterTrainOneIterWithSplitGrad(BoosterHandle handle, DMatrixHandle dtrain, int iter,
+                                               char const* grad, char const* hess, char const* value_grad,
+                                               char const* value_hess);
 /* include/xgboost/c_api.h:1020: releases the training state; the model stays. */
 XGB_DLL int XGBoosterReset(BoosterHandle handle);
 /* include/xgboost/c_api.h:1035 (src/c_api.cpp:503-506): rounds begin, begin+step,
@@ -216,6 +343,22 @@ XGB_DLL int XGBoosterGetStrFeatureInfo(BoosterHandle handle, const char* field, 
                                        const char*** out_features);
 
 /* --- collective ----------------------------------------------------------- */
+/* include/xgboost/c_api.h:1798-1858: host buffers over the NCCL communicator;
+ * no-ops on one rank. */
+XGB_DLL int XGCommunicatorIsDistributed(void);
+XGB_DLL int XGCommunicatorPrint(char const* message);
+XGB_DLL int XGCommunicatorGetProcessorName(const char** name_str);
+XGB_DLL int XGCommunicatorBroadcast(void* send_receive_buffer, size_t size, int root);
+XGB_DLL int XGCommunicatorAllreduce(void* send_receive_buffer, size_t count, int data_type, int op);
+/* include/metalgb/c_api.h:20: aborts this rank's communicator. */
+XGB_DLL int XGCommunicatorSignalError(void);
+/* include/xgboost/c_api.h:1697-1742: ranks bootstrap NCCL from a shared unique id
+ * instead; these return -1 with that explanation. */
+XGB_DLL int XGTrackerCreate(char const* config, TrackerHandle* handle);
+XGB_DLL int XGTrackerWorkerArgs(TrackerHandle handle, char const** args);
+XGB_DLL int XGTrackerRun(TrackerHandle handle, char const* config);
+XGB_DLL int XGTrackerWaitFor(TrackerHandle handle, char const* config);
+XGB_DLL int XGTrackerFree(TrackerHandle handle);
 /* include/xgboost/c_api.h:1768 (a stub in the reference, src/c_api.cpp:600-614):
  * config {"rank", "world_size", "device", "nccl_unique_id"}; world_size > 1
  * shards rows over one NCCL communicator per process. */

@@ -151,3 +151,63 @@ def test_native_evaluation_and_early_stopping():
     assert es.num_boosted_rounds() == es.best_iteration + 1 + 2
     best_line = es[: es.best_iteration + 1].eval(vnoise, "valid")
     assert float(best_line.rsplit(":", 1)[1]) == pytest.approx(es.best_score, rel=1e-9)
+
+
+def test_device_inputs_prediction_variants_and_cut_export():
+    import ctypes
+    import json as _json
+
+    import torch
+    rng = np.random.default_rng(16)
+    X = rng.normal(size=(3000, 4)).astype(np.float32)
+    X[rng.random(X.shape) < 0.1] = np.nan
+    y = (np.nan_to_num(X[:, 0]) + 0.1 * rng.normal(size=3000)).astype(np.float32)
+    b = xgb.train(PARAMS, xgb.DMatrix(X, label=y), 4)
+    want = b.predict(xgb.DMatrix(X))
+    L = core._LIB
+    shape = ctypes.POINTER(core.c_bst_ulong)()
+    dims = core.c_bst_ulong()
+    res = ctypes.POINTER(ctypes.c_float)()
+
+    def out():
+        n = int(np.prod([shape[i] for i in range(dims.value)]))
+        return np.ctypeslib.as_array(res, (n,)).copy()
+    cfg = _json.dumps({"type": 0, "training": False, "iteration_begin": 0, "iteration_end": 0,
+                       "strict_shape": False, "missing": None}).encode()
+    # A CUDA tensor through the CUDA array interface, as a matrix and in place.
+    t = torch.from_numpy(X).cuda()
+    cai = _json.dumps(dict(t.__cuda_array_interface__, data=[t.data_ptr(), False])).encode()
+    h = ctypes.c_void_p()
+    core._check_call(L.XGDMatrixCreateFromCudaArrayInterface(cai, b"{}", ctypes.byref(h)))
+    dm = xgb.DMatrix.__new__(xgb.DMatrix)
+    dm.handle = h
+    np.testing.assert_array_equal(b.predict(dm), want)
+    core._check_call(L.XGBoosterPredictFromCudaArray(b.handle, cai, cfg, None, ctypes.byref(shape),
+                                                     ctypes.byref(dims), ctypes.byref(res)))
+    np.testing.assert_array_equal(out(), want)
+    # Columnar host input.
+    cols = [np.ascontiguousarray(X[:, c]) for c in range(4)]
+    col_json = _json.dumps([_json.loads(core._array_interface(c)) for c in cols]).encode()
+    core._check_call(L.XGBoosterPredictFromColumnar(b.handle, col_json, cfg, None, ctypes.byref(shape),
+                                                    ctypes.byref(dims), ctypes.byref(res)))
+    np.testing.assert_array_equal(out(), want)
+    # Into the caller's buffer.
+    buf = np.zeros(3000, np.float32)
+    dx = xgb.DMatrix(X)
+    core._check_call(L.XGBoosterPredictToBuffer(b.handle, dx.handle, cfg,
+                                                buf.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
+                                                core.c_bst_ulong(3000), ctypes.byref(shape), ctypes.byref(dims)))
+    np.testing.assert_array_equal(buf, want)
+    # Cuts of a quantised matrix: per feature -inf, then increasing cut values.
+    q = xgb.QuantileDMatrix(X, label=y, max_bin=16)
+    ip, vals = ctypes.c_char_p(), ctypes.c_char_p()
+    core._check_call(L.XGDMatrixGetQuantileCut(q.handle, b"{}", ctypes.byref(ip), ctypes.byref(vals)))
+    ip_ai, v_ai = _json.loads(ip.value.decode()), _json.loads(vals.value.decode())
+    indptr = np.ctypeslib.as_array(ctypes.cast(ip_ai["data"][0], ctypes.POINTER(ctypes.c_uint64)), (5,)).copy()
+    values = np.ctypeslib.as_array(ctypes.cast(v_ai["data"][0], ctypes.POINTER(ctypes.c_float)),
+                                   (int(indptr[-1]),)).copy()
+    assert indptr[0] == 0 and np.all(np.diff(indptr) >= 2) and np.all(np.diff(indptr) <= 17)
+    for f in range(4):
+        seg = values[indptr[f]:indptr[f + 1]]
+        assert seg[0] == -np.inf and np.all(np.diff(seg[1:]) > 0)
+        assert seg[-1] > np.nanmax(X[:, f])

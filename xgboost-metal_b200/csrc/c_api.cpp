@@ -34,6 +34,11 @@ using xgbb::require;
 void (*log_callback)(const char*) = nullptr;
 }  // namespace
 
+void xgbb::capi::log_message(const char* text) {
+  if (log_callback) log_callback(text);
+  else std::fprintf(stderr, "%s\n", text);
+}
+
 // ---------------------------------------------------------------------------
 // Library
 // ---------------------------------------------------------------------------
@@ -111,22 +116,9 @@ XGB_DLL int XGDMatrixCreateFromMat(const float* data, bst_ulong nrow, bst_ulong 
 XGB_DLL int XGDMatrixCreateFromCSR(char const* indptr, char const* indices, char const* data,
                                    bst_ulong ncol, char const* config, DMatrixHandle* out) {
   return guarded([&] {
-    ArrayView p = parse_array(indptr), i = parse_array(indices), v = parse_array(data);
-    uint64_t pr, pc, ir, ic, vr, vc;
-    auto ptr = to_floats(p, pr, pc);
-    auto idx = to_floats(i, ir, ic);
-    auto val = to_floats(v, vr, vc);
-    require(pr >= 1, "CSR indptr must have at least one entry.");
-    const uint64_t rows = pr - 1;
-    uint64_t cols = ncol;
-    for (float c : idx) cols = std::max<uint64_t>(cols, uint64_t(c) + 1);
-    std::vector<float> dense(size_t(rows) * cols, NAN);
-    const float missing = config_missing(config);
-    for (uint64_t r = 0; r < rows; ++r)
-      for (uint64_t k = uint64_t(ptr[r]); k < uint64_t(ptr[r + 1]); ++k) {
-        const float x = val[k];
-        dense[size_t(r) * cols + uint64_t(idx[k])] = (std::isnan(missing) ? false : x == missing) ? NAN : x;
-      }
+    require(out != nullptr, "Null output handle.");
+    uint64_t rows, cols;
+    auto dense = csr_dense(indptr, indices, data, ncol, config_missing(config), rows, cols);
     *out = new_dmatrix(std::move(dense), rows, cols, NAN);
   });
 }
@@ -223,6 +215,7 @@ void replace_proxy_data(DMatrixHandle proxy, DMatrixHandle fresh) {
   value->labels = std::move(slot->labels);
   value->weights = std::move(slot->weights);
   value->base_margin = std::move(slot->base_margin);
+  value->feature_info = std::move(slot->feature_info);
   ++value->generation;
   slot = std::move(value);
 }
@@ -235,6 +228,7 @@ DMatrixPtr from_iterator(DataIterHandle iter, DMatrixHandle proxy, DataIterReset
   uint64_t rows = 0, cols = 0;
   bool first = true;
   int has_labels = -1, has_weights = -1, has_margins = -1;
+  std::map<std::string, std::vector<std::string>> feature_info;
   reset(iter);
   while (true) {
     const int status = next(iter);
@@ -255,6 +249,7 @@ DMatrixPtr from_iterator(DataIterHandle iter, DMatrixHandle proxy, DataIterReset
     append(labels, has_labels, b.labels, "labels");
     append(weights, has_weights, b.weights, "weights");
     append(margins, has_margins, b.base_margin, "base margins");
+    feature_info = b.feature_info;
     values.insert(values.end(), b.host, b.host + size_t(b.rows) * b.cols);
     rows += b.rows;
     first = false;
@@ -265,6 +260,7 @@ DMatrixPtr from_iterator(DataIterHandle iter, DMatrixHandle proxy, DataIterReset
   if (!labels.empty()) set_info(*out, "label", std::move(labels));
   if (!weights.empty()) set_info(*out, "weight", std::move(weights));
   if (!margins.empty()) set_info(*out, "base_margin", std::move(margins));
+  out->feature_info = std::move(feature_info);
   return out;
 }
 }  // namespace
@@ -289,12 +285,48 @@ XGB_DLL int XGProxyDMatrixSetDataCSR(DMatrixHandle handle, char const* indptr, c
   });
 }
 
+// include/xgboost/c_api.h:601
+XGB_DLL int XGProxyDMatrixSetDataColumnar(DMatrixHandle handle, char const* data) {
+  return guarded([&] {
+    uint64_t rows, cols;
+    auto v = columnar_dense(data, rows, cols);
+    replace_proxy_data(handle, new_dmatrix(std::move(v), rows, cols, NAN));
+  });
+}
+
+// include/xgboost/c_api.h:591: device batches are copied to the host.
+XGB_DLL int XGProxyDMatrixSetDataCudaArrayInterface(DMatrixHandle handle, const char* data) {
+  return guarded([&] {
+    uint64_t rows, cols;
+    auto v = cuda_dense_values(data, rows, cols);
+    replace_proxy_data(handle, new_dmatrix(std::move(v), rows, cols, NAN));
+  });
+}
+
+// include/xgboost/c_api.h:611
+XGB_DLL int XGProxyDMatrixSetDataCudaColumnar(DMatrixHandle handle, const char* data) {
+  return guarded([&] {
+    uint64_t rows, cols;
+    auto v = cuda_columnar_values(data, rows, cols);
+    replace_proxy_data(handle, new_dmatrix(std::move(v), rows, cols, NAN));
+  });
+}
+
 XGB_DLL int XGDMatrixCreateFromCallback(DataIterHandle iter, DMatrixHandle proxy, DataIterResetCallback* reset,
                                         XGDMatrixCallbackNext* next, char const* config, DMatrixHandle* out) {
   return guarded([&] {
     require(out != nullptr, "Null output handle.");
     *out = new DMatrixPtr(from_iterator(iter, proxy, reset, next, config));
   });
+}
+
+// include/xgboost/c_api.h:576: external memory is not paged here; the
+// batches are concatenated in host memory as for a QuantileDMatrix.
+XGB_DLL int XGExtMemQuantileDMatrixCreateFromCallback(DataIterHandle iter, DMatrixHandle proxy,
+                                                      DataIterHandle ref, DataIterResetCallback* reset,
+                                                      XGDMatrixCallbackNext* next, char const* config,
+                                                      DMatrixHandle* out) {
+  return XGQuantileDMatrixCreateFromCallback(iter, proxy, ref, reset, next, config, out);
 }
 
 // The batches are concatenated, then quantised on the GPU with `ref`'s cuts
@@ -319,6 +351,7 @@ XGB_DLL int XGQuantileDMatrixCreateFromCallback(DataIterHandle iter, DMatrixHand
     xgbb::DMatrix* r = ref ? dmat(ref).get() : nullptr;
     if (r && !r->quantised()) r->quantise(bins, nullptr, nullptr, 0);
     m->quantise(bins, r, nullptr, 0);
+    m->quantile = true;
     XGBB_CUDA(cudaStreamSynchronize(nullptr));
     *out = new DMatrixPtr(std::move(m));
   });
@@ -439,6 +472,20 @@ XGB_DLL int XGBoosterPredictFromDMatrix(BoosterHandle handle, DMatrixHandle dm, 
   return guarded([&] { predict_output(booster(handle), dmat(dm), config, out_shape, out_dim, out_result); });
 }
 
+namespace {
+// In-place prediction: a temporary matrix of `values`, with base margins from
+// the proxy `m` when given (the reference's copy_proxy_metadata).
+void predict_values(BoosterHandle handle, std::vector<float>&& values, uint64_t rows, uint64_t cols,
+                    float missing, const char* config, DMatrixHandle m, bst_ulong const** out_shape,
+                    bst_ulong* out_dim, const float** out_result) {
+  auto* handle_d = static_cast<DMatrixPtr*>(new_dmatrix(std::move(values), rows, cols, missing));
+  DMatrixPtr d = std::move(*handle_d);
+  delete handle_d;
+  if (m) d->base_margin = dmat(m)->base_margin;
+  predict_output(booster(handle), d, config, out_shape, out_dim, out_result);
+}
+}  // namespace
+
 // In-place prediction from a dense __array_interface__ (src/c_api.cpp:510-512
 // in the reference): config adds "missing"; base margins come from the proxy
 // `m` when it is given.
@@ -451,11 +498,98 @@ XGB_DLL int XGBoosterPredictFromDense(BoosterHandle handle, char const* values, 
     require(a.shape.size() == 2, "Dense input must be 2-dimensional.");
     uint64_t rows, cols;
     auto v = to_floats(a, rows, cols);
-    auto* handle_d = static_cast<DMatrixPtr*>(new_dmatrix(std::move(v), rows, cols, config_missing(config)));
-    DMatrixPtr d = std::move(*handle_d);
-    delete handle_d;
-    if (m) d->base_margin = dmat(m)->base_margin;
-    predict_output(booster(handle), d, config, out_shape, out_dim, out_result);
+    predict_values(handle, std::move(v), rows, cols, config_missing(config), config, m, out_shape, out_dim,
+                   out_result);
+  });
+}
+
+// include/xgboost/c_api.h:1289 (src/c_api.cpp:516-518).
+XGB_DLL int XGBoosterPredictFromCSR(BoosterHandle handle, char const* indptr, char const* indices,
+                                    char const* values, bst_ulong ncol, char const* config, DMatrixHandle m,
+                                    bst_ulong const** out_shape, bst_ulong* out_dim, const float** out_result) {
+  return guarded([&] {
+    uint64_t rows, cols;
+    auto v = csr_dense(indptr, indices, values, ncol, config_missing(config), rows, cols);
+    predict_values(handle, std::move(v), rows, cols, NAN, config, m, out_shape, out_dim, out_result);
+  });
+}
+
+// include/xgboost/c_api.h:1261 (src/c_api.cpp:513-515).
+XGB_DLL int XGBoosterPredictFromColumnar(BoosterHandle handle, char const* values, char const* config,
+                                         DMatrixHandle m, bst_ulong const** out_shape, bst_ulong* out_dim,
+                                         const float** out_result) {
+  return guarded([&] {
+    uint64_t rows, cols;
+    auto v = columnar_dense(values, rows, cols);
+    predict_values(handle, std::move(v), rows, cols, config_missing(config), config, m, out_shape, out_dim,
+                   out_result);
+  });
+}
+
+// include/xgboost/c_api.h:1313, 1337: device inputs are copied to the host.
+XGB_DLL int XGBoosterPredictFromCudaArray(BoosterHandle handle, char const* values, char const* config,
+                                          DMatrixHandle proxy, bst_ulong const** out_shape, bst_ulong* out_dim,
+                                          const float** out_result) {
+  return guarded([&] {
+    uint64_t rows, cols;
+    auto v = cuda_dense_values(values, rows, cols);
+    predict_values(handle, std::move(v), rows, cols, config_missing(config), config, proxy, out_shape, out_dim,
+                   out_result);
+  });
+}
+
+XGB_DLL int XGBoosterPredictFromCudaColumnar(BoosterHandle handle, char const* data, char const* config,
+                                             DMatrixHandle proxy, bst_ulong const** out_shape, bst_ulong* out_dim,
+                                             const float** out_result) {
+  return guarded([&] {
+    uint64_t rows, cols;
+    auto v = cuda_columnar_values(data, rows, cols);
+    predict_values(handle, std::move(v), rows, cols, config_missing(config), config, proxy, out_shape, out_dim,
+                   out_result);
+  });
+}
+
+// include/xgboost/c_api.h:1887: a 2-D buffer descriptor; config as
+// XGBoosterPredictFromDMatrix plus "missing".
+XGB_DLL int XGBoosterPredictFromBufferDescriptor(BoosterHandle handle, XGBufferDescriptor const* desc,
+                                                 char const* config, DMatrixHandle proxy,
+                                                 bst_ulong const** out_shape, bst_ulong* out_dim,
+                                                 float const** out_result) {
+  return guarded([&] {
+    const DescriptorView v = view_descriptor(desc, true);
+    predict_values(handle, descriptor_floats(v), v.rows, v.cols, config_missing(config), config, proxy, out_shape,
+                   out_dim, out_result);
+  });
+}
+
+// include/xgboost/c_api.h:1891 (src/c_api.cpp:1000-1016): predictions of a
+// matrix written into the caller's buffer of out_capacity floats.
+XGB_DLL int XGBoosterPredictToBuffer(BoosterHandle handle, DMatrixHandle dm, char const* config, float* out_buffer,
+                                     bst_ulong out_capacity, bst_ulong const** out_shape, bst_ulong* out_dim) {
+  return guarded([&] {
+    const float* values = nullptr;
+    predict_output(booster(handle), dmat(dm), config, out_shape, out_dim, &values);
+    bst_ulong elems = 1;
+    for (bst_ulong i = 0; i < *out_dim; ++i) elems *= (*out_shape)[i];
+    require(elems <= out_capacity, "Output buffer capacity (" + std::to_string(out_capacity) +
+                                       ") is smaller than prediction size (" + std::to_string(elems) + ").");
+    if (elems > 0) {
+      require(out_buffer != nullptr, "Null output buffer for nonempty prediction.");
+      std::memcpy(out_buffer, values, elems * sizeof(float));
+    }
+  });
+}
+
+// Split and value gradients train vector-leaf trees (multi_strategy =
+// multi_output_tree), which this build does not grow.
+XGB_DLL int XGBoosterTrainOneIterWithSplitGrad(BoosterHandle handle, DMatrixHandle dtrain, int iter,
+                                               char const* grad, char const* hess, char const* value_grad,
+                                               char const* value_hess) {
+  (void)dtrain, (void)iter, (void)grad, (void)hess, (void)value_grad, (void)value_hess;
+  return guarded([&] {
+    booster(handle);
+    throw Error("Reduced gradients need multi_strategy='multi_output_tree', which the CUDA backend does "
+                "not implement.");
   });
 }
 
@@ -798,6 +932,7 @@ XGB_DLL int XGDMatrixQuantise(DMatrixHandle handle, int max_bin, DMatrixHandle r
     auto& d = *dmat(handle);
     const xgbb::DMatrix* r = ref ? dmat(ref).get() : nullptr;
     d.quantise(uint32_t(max_bin), r, nullptr, 0);
+    d.quantile = true;
     XGBB_CUDA(cudaStreamSynchronize(nullptr));
   });
 }

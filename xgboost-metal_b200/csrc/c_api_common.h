@@ -45,6 +45,9 @@ DMatrixPtr& dmat(DMatrixHandle h);
 Booster& booster(BoosterHandle h);
 void ensure_device();
 
+// A message to the log callback of XGBRegisterLogCallback, else stderr.
+void log_message(const char* text);
+
 // Strings handed out through `results` (valid until the next call).
 void string_output(std::vector<std::string> strings, bst_ulong* len, char const*** out);
 
@@ -89,5 +92,14 @@ struct DescriptorView {
 DescriptorView view_descriptor(const XGBufferDescriptor* d, bool two_d);
 bool descriptor_c_contiguous_f32(const DescriptorView& v);
 std::vector<float> descriptor_floats(const DescriptorView& v);
+
+// Dense row-major values from other layouts (c_api_data.cpp): CSR triplets,
+// a list of column array interfaces, and CUDA array interfaces (copied to the
+// host).
+std::vector<float> csr_dense(const char* indptr, const char* indices, const char* data, uint64_t ncol,
+                             float missing, uint64_t& rows, uint64_t& cols);
+std::vector<float> columnar_dense(const char* data, uint64_t& rows, uint64_t& cols);
+std::vector<float> cuda_dense_values(const char* data, uint64_t& rows, uint64_t& cols);
+std::vector<float> cuda_columnar_values(const char* data, uint64_t& rows, uint64_t& cols);
 
 }  // namespace xgbb::capi

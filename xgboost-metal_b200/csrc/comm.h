@@ -46,6 +46,9 @@ class Comm {
   void wait_device(const char* what);
   void set_timeout(double seconds);
   bool failed() const { return failed_; }
+  // Aborts the communicator on this rank (XGCommunicatorSignalError): the
+  // other ranks' pending and next collectives fail within their time limit.
+  void signal_error() { abort_detached(); }
 
  private:
   void settle(const char* what);

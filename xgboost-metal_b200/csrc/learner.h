@@ -69,6 +69,10 @@ class DMatrix {
   bool validated = false;
   std::vector<float> labels, weights, base_margin;
   bool has_missing = false;
+  // "feature_name" / "feature_type" lists (empty = unnamed).
+  std::map<std::string, std::vector<std::string>> feature_info;
+  // Quantised at construction (QuantileDMatrix): no row slices.
+  bool quantile = false;
 
   // Quantised form.
   std::shared_ptr<Cuts> cuts;
