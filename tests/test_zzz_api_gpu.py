@@ -211,3 +211,31 @@ def test_device_inputs_prediction_variants_and_cut_export():
         seg = values[indptr[f]:indptr[f + 1]]
         assert seg[0] == -np.inf and np.all(np.diff(seg[1:]) > 0)
         assert seg[-1] > np.nanmax(X[:, f])
+
+
+def test_cross_validation_and_training_callbacks(tmp_path):
+    import json as _json
+
+    from xgboost import training
+    rng = np.random.default_rng(17)
+    X = rng.normal(size=(2400, 5)).astype(np.float32)
+    y = (X[:, 0] - 2 * X[:, 3] + 0.3 * rng.normal(size=2400)).astype(np.float32)
+    d = xgb.DMatrix(X, label=y)
+    res = xgb.cv(PARAMS, d, 5, nfold=3, metrics=["mae"], seed=3, as_pandas=False)
+    assert sorted(res) == ["test-mae-mean", "test-mae-std", "train-mae-mean", "train-mae-std"]
+    assert all(len(v) == 5 for v in res.values())
+    # The same folds trained one by one give the reported test mean.
+    packs = training._make_folds(d, 3, PARAMS, 3, False, True, None, ["mae"])
+    maes = []
+    for p in packs:
+        b = xgb.train(PARAMS, p.dtrain, 5)
+        maes.append(float(np.mean(np.abs(b.predict(p.dtest) - p.dtest.get_label()))))
+    assert res["test-mae-mean"][-1] == pytest.approx(np.mean(maes), rel=1e-5)
+    assert res["test-mae-std"][-1] == pytest.approx(np.std(maes), rel=1e-4, abs=1e-7)
+    # Callbacks: a learning-rate schedule and checkpoints.
+    sched = xgb.callback.LearningRateScheduler([0.3, 0.2, 0.1])
+    ckpt = xgb.callback.TrainingCheckPoint(tmp_path, interval=1)
+    b = xgb.train(PARAMS, d, 3, evals=[(d, "train")], callbacks=[sched, ckpt], verbose_eval=False)
+    ttp = _json.loads(b.save_config())["learner"]["gradient_booster"]["tree_train_param"]
+    assert float(ttp["learning_rate"]) == pytest.approx(0.1)
+    assert sorted(p.name for p in tmp_path.iterdir()) == ["model_1.json", "model_2.json"]

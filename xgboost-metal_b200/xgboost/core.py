@@ -83,6 +83,24 @@ def _to_2d_float(data):
     return arr
 
 
+def _set_str_info(fn, handle, field, values):
+    """Feature names or types through Set*StrFeatureInfo (None clears them)."""
+    if values is None:
+        _check_call(fn(handle, _c_str(field), None, c_bst_ulong(0)))
+        return
+    values = [str(v) for v in values]
+    arr = (ctypes.c_char_p * len(values))(*[v.encode() for v in values])
+    _check_call(fn(handle, _c_str(field), arr, c_bst_ulong(len(values))))
+
+
+def _get_str_info(fn, handle, field):
+    length = c_bst_ulong()
+    sarr = ctypes.POINTER(ctypes.c_char_p)()
+    _check_call(fn(handle, _c_str(field), ctypes.byref(length), ctypes.byref(sarr)))
+    values = [sarr[i].decode() for i in range(length.value)]
+    return values if values else None
+
+
 _NEXT_CALLBACK = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p)
 _RESET_CALLBACK = ctypes.CFUNCTYPE(None, ctypes.c_void_p)
 
@@ -159,6 +177,9 @@ class DataIter:
             self._feature_names = [str(c) for c in data.columns]
         if feature_types is not None:
             self._feature_types = list(feature_types)
+        for field, values in (("feature_name", self._feature_names), ("feature_type", self._feature_types)):
+            if values is not None:
+                _set_str_info(_LIB.XGDMatrixSetStrFeatureInfo, proxy, field, values)
         self._batch = keep
 
     def _next_wrapper(self, _this):
@@ -239,6 +260,96 @@ class DMatrix:
         if _LIB is not None and getattr(self, "handle", None) is not None and self.handle.value:
             _LIB.XGDMatrixFree(self.handle)
             self.handle = None
+
+    @classmethod
+    def _from_handle(cls, handle):
+        d = cls.__new__(cls)
+        d.handle = handle if isinstance(handle, ctypes.c_void_p) else ctypes.c_void_p(handle)
+        return d
+
+    # Feature names and types are kept by the native matrix, so slices, folds
+    # and boosters created from it see them (python-package/xgboost/core.py
+    # DMatrix.feature_names).
+    @property
+    def feature_names(self):
+        return _get_str_info(_LIB.XGDMatrixGetStrFeatureInfo, self.handle, "feature_name")
+
+    @feature_names.setter
+    def feature_names(self, names):
+        if names is not None:
+            names = list(names)
+            if len(names) != len(set(names)):
+                raise ValueError("feature_names must be unique")
+        _set_str_info(_LIB.XGDMatrixSetStrFeatureInfo, self.handle, "feature_name", names)
+
+    @property
+    def feature_types(self):
+        return _get_str_info(_LIB.XGDMatrixGetStrFeatureInfo, self.handle, "feature_type")
+
+    @feature_types.setter
+    def feature_types(self, types):
+        if isinstance(types, str):
+            types = [types] * self.num_col()
+        _set_str_info(_LIB.XGDMatrixSetStrFeatureInfo, self.handle, "feature_type", types)
+
+    def slice(self, rindex, allow_groups=False):
+        """The rows `rindex` as a new DMatrix (labels, weights, margins and
+        feature names follow)."""
+        idx = np.ascontiguousarray(np.asarray(rindex, dtype=np.int32).reshape(-1))
+        handle = ctypes.c_void_p()
+        _check_call(_LIB.XGDMatrixSliceDMatrixEx(self.handle, idx.ctypes.data_as(ctypes.POINTER(ctypes.c_int)),
+                                                 c_bst_ulong(idx.size), ctypes.byref(handle),
+                                                 ctypes.c_int(int(allow_groups))))
+        return DMatrix._from_handle(handle)
+
+    def get_data(self):
+        """The present entries as a scipy CSR matrix."""
+        from scipy.sparse import csr_matrix
+        rows, cols, nnz = self.num_row(), self.num_col(), self.num_nonmissing()
+        indptr = np.zeros(rows + 1, np.uint64)
+        indices = np.zeros(max(nnz, 1), np.uint32)
+        data = np.zeros(max(nnz, 1), np.float32)
+        _check_call(_LIB.XGDMatrixGetDataAsCSR(self.handle, _c_str("{}"),
+                                               indptr.ctypes.data_as(ctypes.POINTER(c_bst_ulong)),
+                                               indices.ctypes.data_as(ctypes.POINTER(ctypes.c_uint)),
+                                               data.ctypes.data_as(ctypes.POINTER(ctypes.c_float))))
+        return csr_matrix((data[:nnz], indices[:nnz], indptr), shape=(rows, cols))
+
+    def get_quantile_cut(self):
+        """(indptr, values) of the histogram cuts: per feature -inf and then
+        its cut values."""
+        ip, vals = ctypes.c_char_p(), ctypes.c_char_p()
+        _check_call(_LIB.XGDMatrixGetQuantileCut(self.handle, _c_str("{}"), ctypes.byref(ip),
+                                                 ctypes.byref(vals)))
+        ip_ai, v_ai = json.loads(ip.value.decode()), json.loads(vals.value.decode())
+        indptr = np.ctypeslib.as_array(ctypes.cast(ip_ai["data"][0], ctypes.POINTER(c_bst_ulong)),
+                                       (ip_ai["shape"][0],)).copy()
+        n = v_ai["shape"][0]
+        values = np.ctypeslib.as_array(ctypes.cast(v_ai["data"][0], ctypes.POINTER(ctypes.c_float)),
+                                       (n,)).copy() if n else np.zeros(0, np.float32)
+        return indptr, values
+
+    def save_binary(self, fname, silent=True):
+        _check_call(_LIB.XGDMatrixSaveBinary(self.handle, _c_str(os.fspath(fname)), ctypes.c_int(silent)))
+
+    def set_info(self, *, label=None, weight=None, base_margin=None, feature_names=None,
+                 feature_types=None, **kwargs):
+        if label is not None:
+            self.set_label(label)
+        if weight is not None:
+            self.set_weight(weight)
+        if base_margin is not None:
+            self.set_base_margin(base_margin)
+        if feature_names is not None:
+            self.feature_names = feature_names
+        if feature_types is not None:
+            self.feature_types = feature_types
+        unknown = [k for k, v in kwargs.items() if v is not None]
+        if unknown:
+            raise XGBoostError("Unsupported metadata: %s" % ", ".join(unknown))
+
+    def get_base_margin(self):
+        return self.get_float_info("base_margin")
 
     def _set_float(self, field, values):
         v = np.ascontiguousarray(np.asarray(values, dtype=np.float32).reshape(-1))
