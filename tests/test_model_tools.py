@@ -292,3 +292,40 @@ def test_custom_gradients_are_checked_before_any_device_work():
         b.handle, d.handle, g.ctypes.data_as(core.ctypes.POINTER(core.ctypes.c_float)),
         g.ctypes.data_as(core.ctypes.POINTER(core.ctypes.c_float)), core.c_bst_ulong(3)) == -1
     assert b"shape" in core._LIB.XGBGetLastError()
+
+
+def test_concurrent_calls_on_one_booster_are_serialised():
+    """Every C call holds the booster's lock (the reference's per-booster
+    mutex): threads mutating attributes while others save and dump never see
+    a torn model."""
+    import threading
+    b = _booster(_three_rounds())
+    want = b.get_dump()
+    errors = []
+
+    def writer(k):
+        try:
+            for i in range(200):
+                b.set_attr(**{"k%d" % k: str(i)})
+                b.set_param("max_depth", 3 + (i % 3))
+        except Exception as e:  # noqa: BLE001
+            errors.append(e)
+
+    def reader():
+        try:
+            for _ in range(100):
+                assert b.get_dump() == want
+                doc = json.loads(bytes(b.save_raw("json")).decode())
+                assert len(doc["learner"]["gradient_booster"]["model"]["trees"]) == 3
+                json.loads(b.save_config())
+        except Exception as e:  # noqa: BLE001
+            errors.append(e)
+
+    threads = [threading.Thread(target=writer, args=(k,)) for k in range(3)]
+    threads += [threading.Thread(target=reader) for _ in range(3)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors
+    assert b.attr("k2") == "199"

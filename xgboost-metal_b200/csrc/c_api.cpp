@@ -369,7 +369,13 @@ XGB_DLL int XGBoosterCreate(const DMatrixHandle dmats[], bst_ulong len, BoosterH
 }
 
 XGB_DLL int XGBoosterFree(BoosterHandle handle) {
-  return guarded([&] { delete &booster(handle); });
+  return guarded([&] {
+    require(handle != nullptr, "Booster handle is null.");
+    auto* b = static_cast<xgbb::Booster*>(handle);
+    // Wait for calls in flight on other threads, then free it unlocked.
+    { std::lock_guard<std::recursive_mutex> wait(b->mutex()); }
+    delete b;
+  });
 }
 
 XGB_DLL int XGBoosterSetParam(BoosterHandle handle, const char* name, const char* value) {

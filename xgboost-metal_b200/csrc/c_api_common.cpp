@@ -16,9 +16,13 @@ DMatrixPtr& dmat(DMatrixHandle h) {
   require(h != nullptr, "DMatrix handle is null.");
   return *static_cast<DMatrixPtr*>(h);
 }
+thread_local std::vector<std::unique_lock<std::recursive_mutex>> held_locks;
+
 xgbb::Booster& booster(BoosterHandle h) {
   require(h != nullptr, "Booster handle is null.");
-  return *static_cast<xgbb::Booster*>(h);
+  auto* b = static_cast<xgbb::Booster*>(h);
+  held_locks.emplace_back(b->mutex());
+  return *b;
 }
 
 void ensure_device() {

@@ -7,6 +7,7 @@
 #include <cstdint>
 #include <exception>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -26,9 +27,18 @@ struct Results {
 };
 extern thread_local Results results;
 extern thread_local std::string last_error;
+// Booster locks taken during the current C call (booster() takes them;
+// guarded() releases them when the call returns).
+extern thread_local std::vector<std::unique_lock<std::recursive_mutex>> held_locks;
 
 template <class F>
 int guarded(F&& f) noexcept {
+  struct Release {
+    size_t n;
+    ~Release() {
+      while (held_locks.size() > n) held_locks.pop_back();
+    }
+  } release{held_locks.size()};
   try {
     f();
     return 0;
@@ -42,6 +52,7 @@ int guarded(F&& f) noexcept {
 
 using DMatrixPtr = std::shared_ptr<DMatrix>;
 DMatrixPtr& dmat(DMatrixHandle h);
+// The booster of a handle, locked until the enclosing guarded() call returns.
 Booster& booster(BoosterHandle h);
 void ensure_device();
 

@@ -6,6 +6,7 @@
 #include <cstdint>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -142,6 +143,9 @@ class Booster {
   std::map<std::string, std::string> attrs;
   std::map<std::string, std::vector<std::string>> feature_info;
   Profile profile;
+  // Held by every C-ABI call on this booster (the reference's per-booster
+  // recursive mutex, include/metalgb/engine.hpp:201, src/c_api.cpp:37-39).
+  std::recursive_mutex& mutex() { return mutex_; }
   bool profiling = false;
   void sync();
   // CUDA events on the booster's stream, for timing whole rounds on the device.
@@ -184,6 +188,7 @@ class Booster {
   std::unique_ptr<TrainState> state_;
   std::vector<cudaEvent_t> user_events_;
   cudaEvent_t wait_event_ = nullptr;
+  std::recursive_mutex mutex_;
 };
 
 }  // namespace xgbb
