@@ -329,3 +329,14 @@ def test_concurrent_calls_on_one_booster_are_serialised():
         t.join()
     assert not errors
     assert b.attr("k2") == "199"
+
+
+def test_device_strings_are_validated():
+    b = _booster()
+    for good in ("cuda", "gpu", "cuda:0"):
+        b.set_param("device", good)
+        json.loads(b.save_config())
+    for bad, needle in (("cuda:x", "ordinal"), ("cpu", "CUDA devices only"), ("cuda:-1", "ordinal")):
+        b.set_param("device", bad)
+        with pytest.raises(xgb.XGBoostError, match=needle):
+            b.save_config()

@@ -8,6 +8,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <sstream>
 
@@ -413,6 +414,17 @@ void Booster::configure() {
   const std::string device = get_param("device", "cuda");
   require(device == "cuda" || device == "gpu" || device.rfind("cuda:", 0) == 0,
           "This build trains on CUDA devices only; device must be 'cuda', 'cuda:N' or 'gpu'.");
+  if (device.rfind("cuda:", 0) == 0) {
+    // A booster trains on the device current when it was created (one
+    // process per GPU); an explicit ordinal must name that device.
+    char* end = nullptr;
+    const long ordinal = std::strtol(device.c_str() + 5, &end, 10);
+    require(end && *end == '\0' && ordinal >= 0, "Invalid device ordinal: " + device);
+    require(!stream_ || ordinal == device_,
+            "device '" + device + "' differs from this booster's CUDA device " + std::to_string(device_) +
+                "; select the device (xgboost.core.set_device or CUDA_VISIBLE_DEVICES) before creating "
+                "the booster.");
+  }
   const std::string method = get_param("tree_method", "hist");
   require(method == "hist" || method == "auto" || method == "gpu_hist",
           "CUDA tree training requires tree_method='hist' or 'auto'.");
