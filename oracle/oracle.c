@@ -789,6 +789,208 @@ int orc_grow_tree(const uint32_t* bins, uint32_t rows, uint32_t cols, const int6
 }
 
 /* ------------------------------------------------------------------------ */
+/* The host-driven tree: a queue of evaluated leaves.                        */
+/* ------------------------------------------------------------------------ */
+
+typedef struct {
+  uint32_t id, depth;
+  uint32_t begin, count; /* range in the row array */
+  orc_split split;
+} queue_leaf;
+
+/* Queue order of src/tree.cpp:63-69: loss-guided trees pop the largest gain
+ * first; ties, and every depth-wise tree, pop the smallest node id first.
+ * Returns nonzero when a pops before b. */
+static int leaf_before(const queue_leaf* a, const queue_leaf* b, uint32_t lossguide) {
+  if (lossguide && a->split.gain != b->split.gain) return a->split.gain > b->split.gain;
+  return a->id < b->id;
+}
+
+static void heap_push(queue_leaf* h, uint32_t* n, queue_leaf v, uint32_t lossguide) {
+  uint32_t i = (*n)++;
+  h[i] = v;
+  while (i && leaf_before(&h[i], &h[(i - 1) / 2], lossguide)) {
+    queue_leaf t = h[i];
+    h[i] = h[(i - 1) / 2];
+    h[(i - 1) / 2] = t;
+    i = (i - 1) / 2;
+  }
+}
+
+static queue_leaf heap_pop(queue_leaf* h, uint32_t* n, uint32_t lossguide) {
+  queue_leaf top = h[0];
+  h[0] = h[--(*n)];
+  uint32_t i = 0;
+  for (;;) {
+    uint32_t l = 2 * i + 1, r = l + 1, m = i;
+    if (l < *n && leaf_before(&h[l], &h[m], lossguide)) m = l;
+    if (r < *n && leaf_before(&h[r], &h[m], lossguide)) m = r;
+    if (m == i) break;
+    queue_leaf t = h[i];
+    h[i] = h[m];
+    h[m] = t;
+    i = m;
+  }
+  return top;
+}
+
+/* The best split of one node over rows [begin, begin + count) of `order`. */
+static orc_split evaluate_node(const uint32_t* bins, uint32_t cols, const int64_t* q, const float* scale,
+                               const float* cuts, uint32_t stride, const uint32_t* counts,
+                               const float* minima, const orc_tree_params* tp, const uint32_t* order,
+                               uint32_t begin, uint32_t count, int root, int64_t sum_g, int64_t sum_h) {
+  size_t per_node = (size_t)cols * (stride + 1) * 2;
+  int64_t* hist = (int64_t*)calloc(per_node, sizeof(int64_t));
+  orc_split* cand = (orc_split*)malloc((size_t)cols * sizeof(orc_split));
+  int64_t sums[2] = {sum_g, sum_h};
+  orc_split best;
+  orc_histogram(bins, cols, stride, q, order + begin, count, hist);
+  orc_evaluate_splits(hist, 1, cols, stride, scale, cuts, counts, minima, tp->reg_lambda, tp->reg_alpha,
+                      tp->min_child_weight, tp->max_delta_step, root ? 0u : 1u, sums, cand);
+  orc_select_splits(cand, 1, cols, scale, tp->reg_lambda, tp->reg_alpha, tp->max_delta_step, &best);
+  free(hist);
+  free(cand);
+  return best;
+}
+
+/* [ours, restating src/tree.cpp:291-349 and 1031-1120] Host-driven growth.
+ * The root is evaluated and queued; each pass pops a batch (one leaf when
+ * loss-guided, else up to 256 leaves of one depth in node-id order), keeping
+ * the leaves whose split is usable (feature >= 0, gain > 1e-6, gain >=
+ * min_split_loss, depth < max_depth, fewer than max_leaves leaves so far,
+ * counting the root as one); the first empty batch ends the tree. Applying
+ * a leaf numbers its children in pop order; while depth + 1 < max_depth and
+ * the leaf count allows, the children are partitioned, evaluated and queued
+ * when their gain exceeds 1e-6. max_depth 0 means unlimited. Node fields
+ * follow the level-synchronous grower (cover = the evaluated total Hessian,
+ * the applied parent Hessian once split). */
+int orc_grow_tree_queue(const uint32_t* bins, uint32_t rows, uint32_t cols, const int64_t* q,
+                        const float* scale, const float* cuts, uint32_t stride, const uint32_t* counts,
+                        const float* minima, const orc_tree_params* tp, uint32_t lossguide,
+                        uint32_t max_leaves, orc_node* nodes, uint32_t capacity, float* row_leaf) {
+  const uint32_t max_depth = tp->max_depth;
+  uint32_t* order = (uint32_t*)malloc(((size_t)rows + 1) * sizeof(uint32_t));
+  uint32_t* scratch = (uint32_t*)malloc(((size_t)rows + 1) * sizeof(uint32_t));
+  queue_leaf* heap = (queue_leaf*)malloc(((size_t)capacity + 1) * sizeof(queue_leaf));
+  queue_leaf* batch = (queue_leaf*)malloc(256 * sizeof(queue_leaf));
+  queue_leaf* kids = (queue_leaf*)malloc(512 * sizeof(queue_leaf));
+  uint32_t nheap = 0, size = 1, leaves = 1;
+  int result = 0;
+  for (uint32_t r = 0; r < rows; ++r) order[r] = r;
+  if (capacity < 1) {
+    result = -1;
+    goto done;
+  }
+  {
+    queue_leaf root = {0, 0, 0, rows, evaluate_node(bins, cols, q, scale, cuts, stride, counts, minima, tp,
+                                                    order, 0, rows, 1, 0, 0)};
+    memset(&nodes[0], 0, sizeof(orc_node));
+    nodes[0].left = nodes[0].right = nodes[0].feature = nodes[0].parent = -1;
+    nodes[0].split_bin = 0;
+    nodes[0].cover = root.split.total_h;
+    nodes[0].leaf = root.split.parent_weight * tp->eta;
+    heap_push(heap, &nheap, root, lossguide);
+  }
+  for (;;) {
+    /* pop */
+    uint32_t nb = 0;
+    if (!nheap) break;
+    uint32_t depth = heap[0].depth;
+    do {
+      queue_leaf leaf = heap_pop(heap, &nheap, lossguide);
+      if (leaf.split.feature >= 0 && leaf.split.gain > 1.0e-6f && leaf.split.gain >= tp->min_split_loss &&
+          (!max_depth || leaf.depth < max_depth) && (!max_leaves || leaves < max_leaves)) {
+        ++leaves;
+        batch[nb++] = leaf;
+      }
+      if (lossguide) break;
+    } while (nheap && heap[0].depth == depth && nb < 256);
+    if (!nb) break;
+    /* apply */
+    uint32_t nk = 0;
+    for (uint32_t i = 0; i < nb; ++i) {
+      const queue_leaf* leaf = &batch[i];
+      const orc_split* sp = &leaf->split;
+      if (size + 2 > capacity) {
+        result = -1;
+        goto done;
+      }
+      uint32_t left = size;
+      size += 2;
+      orc_node* nd = &nodes[leaf->id];
+      nd->left = (int32_t)left;
+      nd->right = (int32_t)left + 1;
+      nd->feature = sp->feature;
+      nd->threshold = sp->threshold;
+      nd->default_left = sp->default_left;
+      nd->gain = sp->gain;
+      nd->cover = sp->applied_parent_hessian;
+      uint32_t f = (uint32_t)sp->feature;
+      int32_t k = -1;
+      for (uint32_t b = 0; b < counts[f]; ++b)
+        if (f32_bits(cuts[(size_t)f * stride + b]) == f32_bits(sp->threshold)) k = (int32_t)b;
+      nd->split_bin = k;
+      for (int c = 0; c < 2; ++c) {
+        orc_node* n = &nodes[left + c];
+        memset(n, 0, sizeof *n);
+        n->left = n->right = n->feature = -1;
+        n->parent = (int32_t)leaf->id;
+        n->leaf = (c ? sp->right_weight : sp->left_weight) * tp->eta;
+        n->cover = c ? sp->right_h : sp->left_h;
+      }
+      if ((!max_depth || leaf->depth + 1 < max_depth) && (!max_leaves || leaves < max_leaves)) {
+        /* stable partition of this leaf's rows */
+        uint32_t* rows_in = order + leaf->begin;
+        uint32_t nl = 0, nr = 0;
+        for (uint32_t j = 0; j < leaf->count; ++j) {
+          uint32_t b = bins[(size_t)rows_in[j] * cols + f];
+          int go_left = b == ORC_MISSING ? (int)sp->default_left : (int32_t)b <= k;
+          if (go_left) rows_in[nl++] = rows_in[j];
+          else scratch[nr++] = rows_in[j];
+        }
+        memcpy(rows_in + nl, scratch, nr * sizeof(uint32_t));
+        /* Each child carries its parent's split until it is evaluated. */
+        queue_leaf l = {left, leaf->depth + 1, leaf->begin, nl, *sp};
+        queue_leaf r = {left + 1, leaf->depth + 1, leaf->begin + nl, nr, *sp};
+        kids[nk] = l;
+        kids[nk + 1] = r;
+        nk += 2;
+      }
+    }
+    /* evaluate the children of this batch */
+    for (uint32_t i = 0; i < nk; ++i) {
+      const orc_split parent = kids[i].split;
+      const int right = (i & 1) != 0;
+      kids[i].split = evaluate_node(bins, cols, q, scale, cuts, stride, counts, minima, tp, order,
+                                    kids[i].begin, kids[i].count, 0,
+                                    right ? parent.right_sum_g : parent.left_sum_g,
+                                    right ? parent.right_sum_h : parent.left_sum_h);
+      nodes[kids[i].id].cover = kids[i].split.total_h;
+      if (kids[i].split.gain > 1.0e-6f) heap_push(heap, &nheap, kids[i], lossguide);
+    }
+  }
+  result = (int)size;
+  if (row_leaf) {
+    for (uint32_t r = 0; r < rows; ++r) {
+      int32_t n = 0;
+      while (nodes[n].left >= 0) {
+        uint32_t b = bins[(size_t)r * cols + (uint32_t)nodes[n].feature];
+        int go_left = b == ORC_MISSING ? (int)nodes[n].default_left : (int32_t)b <= nodes[n].split_bin;
+        n = go_left ? nodes[n].left : nodes[n].right;
+      }
+      row_leaf[r] = nodes[n].leaf;
+    }
+  }
+done:
+  free(order);
+  free(scratch);
+  free(heap);
+  free(batch);
+  free(kids);
+  return result;
+}
+
+/* ------------------------------------------------------------------------ */
 /* Base score and the boosting loop.                                         */
 /* ------------------------------------------------------------------------ */
 

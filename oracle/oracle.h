@@ -83,6 +83,16 @@ int orc_grow_tree(const uint32_t* bins, uint32_t rows, uint32_t cols, const int6
                   const uint32_t* counts, const float* minima, const orc_tree_params* tp,
                   orc_node* nodes, uint32_t capacity, float* row_leaf);
 
+/* The host-driven grower (the reference's fallback driver for loss-guided
+ * trees, max_leaves and depth > 10): depth-wise batches of at most 256
+ * leaves in node-id order, or one leaf at a time by largest gain when
+ * `lossguide`; max_leaves 0 and max_depth 0 mean unlimited. Returns the node
+ * count or a negative value on error. */
+int orc_grow_tree_queue(const uint32_t* bins, uint32_t rows, uint32_t cols, const int64_t* q,
+                        const float* scale, const float* cuts, uint32_t stride, const uint32_t* counts,
+                        const float* minima, const orc_tree_params* tp, uint32_t lossguide,
+                        uint32_t max_leaves, orc_node* nodes, uint32_t capacity, float* row_leaf);
+
 void orc_base_score(int objective, const float* labels, const float* weights, uint32_t rows,
                     uint32_t groups, float scale_pos_weight, float* score, float* margin);
 

@@ -163,6 +163,27 @@ class Checker:
         return nodes[:n], leaf
 
 
+def grow_tree_queue(bins, q, scale, cuts, counts, minima, params, lossguide=False, max_leaves=0,
+                    capacity=None):
+    """The oracle's host-driven grower (queue of leaves; max_depth 0 =
+    unlimited): (nodes, per-row leaf values)."""
+    lib = ctypes.CDLL(os.path.join(ORACLE_DIR, "liboracle.so"))
+    fn = lib.orc_grow_tree_queue
+    fn.restype = ctypes.c_int
+    rows, cols = bins.shape
+    cap = capacity or max(2 * rows + 1, 3)
+    nodes = np.zeros(cap, NODE_DTYPE)
+    leaf = np.zeros(rows, np.float32)
+    tp = _TreeParams(params["max_depth"], params["eta"], params["reg_lambda"], params["reg_alpha"],
+                     params["min_child_weight"], params["max_delta_step"], params["min_split_loss"])
+    n = fn(_ptr(np.ascontiguousarray(bins, np.uint32)), _U32(rows), _U32(cols),
+           _ptr(np.ascontiguousarray(q, np.int64)), _ptr(np.ascontiguousarray(scale, np.float32)),
+           _ptr(cuts), _U32(cuts.shape[1]), _ptr(counts), _ptr(minima), ctypes.byref(tp),
+           _U32(int(lossguide)), _U32(max_leaves), _ptr(nodes), _U32(cap), _ptr(leaf))
+    assert n > 0, n
+    return nodes[:n], leaf
+
+
 def oracle():
     return Checker("oracle")
 
