@@ -1082,7 +1082,13 @@ int64_t orc_train(const float* X, uint32_t rows, uint32_t cols, const float* lab
     for (uint32_t k = 0; k < groups; ++k) margins[(size_t)r * groups + k] = base[k];
   uint64_t used = 0;
   int64_t result = 0;
-  uint32_t tree_cap = (2u << p->tree.max_depth) - 1;
+  /* The host-driven grower for loss-guided trees, leaf budgets and depths
+   * the level-synchronous driver does not take (src/tree.cpp:366-385). */
+  const int queue = p->lossguide || p->max_leaves || p->tree.max_depth == 0 || p->tree.max_depth > 10;
+  uint64_t tree_cap64 = 2ull * rows + 1;
+  if (p->tree.max_depth && p->tree.max_depth < 31 && ((2ull << p->tree.max_depth) - 1) < tree_cap64)
+    tree_cap64 = (2ull << p->tree.max_depth) - 1;
+  uint32_t tree_cap = (uint32_t)tree_cap64;
   for (uint32_t round = 0; round < p->rounds && !result; ++round) {
     orc_gradients(p->objective, margins, labels, weights, rows, groups, p->scale_pos_weight, pairs);
     /* All trees of a round use the gradients of the round's start; the
@@ -1100,8 +1106,10 @@ int64_t orc_train(const float* X, uint32_t rows, uint32_t cols, const float* lab
         result = -100;
         break;
       }
-      int n = orc_grow_tree(bins, rows, cols, q, scale, cuts, stride, counts, minima, &p->tree,
-                            nodes + used, tree_cap, leaf);
+      int n = queue ? orc_grow_tree_queue(bins, rows, cols, q, scale, cuts, stride, counts, minima, &p->tree,
+                                          p->lossguide, p->max_leaves, nodes + used, tree_cap, leaf)
+                    : orc_grow_tree(bins, rows, cols, q, scale, cuts, stride, counts, minima, &p->tree,
+                                    nodes + used, tree_cap, leaf);
       if (n < 0) {
         result = n;
         break;

@@ -108,6 +108,9 @@ typedef struct {
   int has_base_score;
   float base_score;
   orc_tree_params tree;
+  /* grow_policy="lossguide" and max_leaves (0 = no limit); either, or a
+   * max_depth of 0 or above 10, selects the host-driven grower. */
+  uint32_t lossguide, max_leaves;
 } orc_train_params;
 
 int64_t orc_train(const float* X, uint32_t rows, uint32_t cols, const float* labels,

@@ -209,7 +209,8 @@ class _TrainParams(ctypes.Structure):
     _fields_ = [("objective", ctypes.c_int), ("num_class", ctypes.c_uint32),
                 ("max_bin", ctypes.c_uint32), ("rounds", ctypes.c_uint32),
                 ("scale_pos_weight", ctypes.c_float), ("has_base_score", ctypes.c_int),
-                ("base_score", ctypes.c_float), ("tree", _TreeParams)]
+                ("base_score", ctypes.c_float), ("tree", _TreeParams),
+                ("lossguide", ctypes.c_uint32), ("max_leaves", ctypes.c_uint32)]
 
 
 OBJECTIVES = {"reg:squarederror": 0, "binary:logistic": 1, "multi:softprob": 3}
@@ -237,8 +238,13 @@ def oracle_train(X, y, params, rounds, weights=None):
                       float(p.get("base_score", 0.0)),
                       _TreeParams(int(p["max_depth"]), float(p["eta"]), float(p["reg_lambda"]),
                                   float(p["reg_alpha"]), float(p["min_child_weight"]),
-                                  float(p["max_delta_step"]), float(p["min_split_loss"])))
-    cap = rounds * groups * ((2 << int(p["max_depth"])) - 1)
+                                  float(p["max_delta_step"]), float(p["min_split_loss"])),
+                      int(p.get("grow_policy", "depthwise") == "lossguide"), int(p.get("max_leaves", 0)))
+    depth = int(p["max_depth"])
+    tree_cap = 2 * rows + 1
+    if 0 < depth < 31:
+        tree_cap = min(tree_cap, (2 << depth) - 1)
+    cap = rounds * groups * tree_cap
     nodes = np.zeros(cap, NODE_DTYPE)
     sizes = np.zeros(rounds * groups, np.uint32)
     margins = np.zeros((rows, groups), np.float32)

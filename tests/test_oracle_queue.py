@@ -99,3 +99,21 @@ def test_max_leaves_caps_the_tree(lossguide):
         split = small["left"] >= 0
         assert np.array_equal(small["feature"][split], large["feature"][: len(small)][split])
         assert np.array_equal(small["gain"][split], large["gain"][: len(small)][split])
+
+
+def test_whole_run_training_with_the_host_driven_grower():
+    rng = np.random.default_rng(11)
+    X = rng.normal(size=(2500, 5)).astype(np.float32)
+    X[rng.random(X.shape) < 0.05] = np.nan
+    y = (np.nan_to_num(X[:, 0]) + np.nan_to_num(X[:, 1]) ** 2 > 0.5).astype(np.float32)
+    base = {"objective": "binary:logistic", "max_depth": 5, "max_bin": 64}
+    depthwise, m_d, _ = C.oracle_train(X, y, base, 4)
+    lossguide, m_l, _ = C.oracle_train(X, y, dict(base, grow_policy="lossguide"), 4)
+    # Without a leaf budget the loss-guided trees are the depth-wise trees
+    # numbered in another order, so the margins agree bit for bit.
+    assert [_canonical(t) for t in lossguide] == [_canonical(t) for t in depthwise]
+    assert m_l.tobytes() == m_d.tobytes()
+    capped, _, _ = C.oracle_train(X, y, dict(base, grow_policy="lossguide", max_depth=0, max_leaves=7), 4)
+    assert all(np.sum(t["left"] < 0) <= 7 for t in capped)
+    deep, _, _ = C.oracle_train(X, y, dict(base, max_depth=12, min_child_weight=0.0), 2)
+    assert max(_depths(t).max() for t in deep) > 10
