@@ -1,0 +1,37 @@
+"""The package surface of the reference's python-package/xgboost/__init__.py
+(no GPU): global configuration through the library, and the entry points
+that exist for import compatibility with explicit errors."""
+import pytest
+
+import xgboost as xgb
+
+
+def test_global_config_round_trip_and_context():
+    assert xgb.get_config() == {"nthread": 0, "use_rmm": False, "verbosity": 1}
+    with xgb.config_context(verbosity=0, nthread=4):
+        assert xgb.get_config()["verbosity"] == 0 and xgb.get_config()["nthread"] == 4
+    assert xgb.get_config() == {"nthread": 0, "use_rmm": False, "verbosity": 1}
+    xgb.set_config(verbosity=2, nthread=None)
+    assert xgb.get_config()["verbosity"] == 2
+    xgb.set_config(verbosity=1)
+    for bad, needle in (({"verbosity": 4}, "verbosity"), ({"use_rmm": True}, "RMM"),
+                        ({"colour": 1}, "Unknown global parameter")):
+        with pytest.raises(xgb.XGBoostError, match=needle):
+            xgb.set_config(**bad)
+
+
+def test_reference_package_names_exist():
+    import xgboost
+    for name in ("DMatrix", "QuantileDMatrix", "ExtMemQuantileDMatrix", "Booster", "DataIter", "train",
+                 "cv", "build_info", "plot_importance", "plot_tree", "to_graphviz", "set_config",
+                 "get_config", "config_context", "XGBModel", "XGBClassifier", "XGBRegressor",
+                 "XGBRanker", "XGBRFClassifier", "XGBRFRegressor", "collective", "RabitTracker"):
+        assert hasattr(xgboost, name), name
+    with pytest.raises(xgb.XGBoostError, match="Ranking"):
+        xgb.XGBRanker().fit([[0.0]], [0.0])
+    with pytest.raises(xgb.XGBoostError, match="Random forests"):
+        xgb.XGBRFRegressor().fit([[0.0]], [0.0])
+    with pytest.raises(xgb.XGBoostError, match="unique_id"):
+        xgb.RabitTracker(2)
+    with pytest.raises(TypeError):
+        xgb.ExtMemQuantileDMatrix([[1.0]])

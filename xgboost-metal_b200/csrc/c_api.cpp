@@ -67,13 +67,47 @@ XGB_DLL int XGBuildInfo(char const** out) {
   });
 }
 
+namespace {
+// Global parameters, per thread as in the reference (src/c_api.cpp:18-29,
+// 179-189): verbosity in [0, 3], use_rmm (no RMM allocator here), nthread.
+struct GlobalConfig {
+  int verbosity = 1;
+  bool use_rmm = false;
+  long long nthread = 0;
+};
+thread_local GlobalConfig global_config;
+}  // namespace
+
 XGB_DLL int XGBSetGlobalConfig(char const* config) {
-  return guarded([&] { (void)Json::parse(config ? config : "{}"); });
+  return guarded([&] {
+    const Json c = Json::parse(config && *config ? config : "{}");
+    require(c.kind == Json::Object, "The global configuration must be a JSON object.");
+    GlobalConfig next = global_config;
+    for (auto& kv : c.obj) {
+      const std::string& key = kv.first;
+      const Json& v = kv.second;
+      if (key == "verbosity") {
+        require(v.kind == Json::Number && v.num == std::floor(v.num) && v.num >= 0 && v.num <= 3,
+                "verbosity must be in [0, 3].");
+        next.verbosity = int(v.num);
+      } else if (key == "use_rmm") {
+        require(!v.truthy(), "RMM is not used by this build; device memory comes from cudaMalloc.");
+        next.use_rmm = false;
+      } else if (key == "nthread") {
+        require(v.kind == Json::Number && v.num >= 0, "nthread must be a nonnegative integer.");
+        next.nthread = (long long)v.num;
+      } else {
+        throw Error("Unknown global parameter: " + key);
+      }
+    }
+    global_config = next;
+  });
 }
 
 XGB_DLL int XGBGetGlobalConfig(char const** out) {
   return guarded([&] {
-    results.str = "{\"verbosity\":1,\"use_rmm\":false,\"nthread\":0}";
+    results.str = "{\"nthread\":" + std::to_string(global_config.nthread) + ",\"use_rmm\":false,\"verbosity\":" +
+                  std::to_string(global_config.verbosity) + "}";
     *out = results.str.c_str();
   });
 }

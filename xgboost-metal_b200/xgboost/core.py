@@ -13,7 +13,8 @@ import os
 
 import numpy as np
 
-__all__ = ["DMatrix", "QuantileDMatrix", "DataIter", "Booster", "XGBoostError", "build_info"]
+__all__ = ["DMatrix", "QuantileDMatrix", "ExtMemQuantileDMatrix", "DataIter", "Booster", "XGBoostError",
+           "build_info"]
 
 
 class XGBoostError(ValueError):
@@ -426,6 +427,27 @@ class QuantileDMatrix(DMatrix):
                          group=group, qid=qid)
         _check_call(_LIB.XGDMatrixQuantise(self.handle, ctypes.c_int(self.max_bin),
                                            ref.handle if ref is not None else None))
+
+
+class ExtMemQuantileDMatrix(QuantileDMatrix):
+    """QuantileDMatrix from a DataIter for data that is streamed in batches
+    (python-package/xgboost/core.py ExtMemQuantileDMatrix). The batches are
+    concatenated in host memory (XGExtMemQuantileDMatrixCreateFromCallback);
+    nothing is paged to disk."""
+
+    def __init__(self, data, *, missing=None, nthread=None, max_bin=None, ref=None,
+                 enable_categorical=False, max_quantile_batches=None, cache_host_ratio=None):
+        if not isinstance(data, DataIter):
+            raise TypeError("ExtMemQuantileDMatrix takes a DataIter.")
+        self.max_bin = 256 if max_bin is None else int(max_bin)
+        miss = np.nan if missing is None else float(missing)
+        config = {"missing": None if np.isnan(miss) else miss, "nthread": nthread or 0,
+                  "max_bin": self.max_bin}
+        self.handle = data._create(config, ref.handle if ref is not None else None, quantile=True)
+        if data._feature_names is not None:
+            self.feature_names = data._feature_names
+        if data._feature_types is not None:
+            self.feature_types = data._feature_types
 
 
 class Booster:

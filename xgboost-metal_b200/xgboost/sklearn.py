@@ -7,7 +7,7 @@ import numpy as np
 from .core import Booster, DMatrix, XGBoostError
 from .training import train
 
-__all__ = ["XGBModel", "XGBRegressor", "XGBClassifier"]
+__all__ = ["XGBModel", "XGBRegressor", "XGBClassifier", "XGBRanker", "XGBRFRegressor", "XGBRFClassifier"]
 
 _PARAM_NAMES = (
     "max_depth", "max_leaves", "max_bin", "grow_policy", "learning_rate", "verbosity",
@@ -185,3 +185,31 @@ class XGBClassifier(XGBModel):
                                    iteration_range=iteration_range)
         p = self.predict_proba(X, base_margin=base_margin, iteration_range=iteration_range)
         return self.classes_[np.argmax(p, axis=1)]
+
+
+class XGBRanker(XGBModel):
+    """Learning to rank needs query groups and ranking objectives, which the
+    CUDA backend does not train; fit raises."""
+
+    def __init__(self, *, objective="rank:ndcg", **kwargs):
+        super().__init__(objective=objective, **kwargs)
+
+    def fit(self, X, y, *args, **kwargs):
+        raise XGBoostError("Ranking objectives and query groups are not implemented by the CUDA backend.")
+
+
+class XGBRFRegressor(XGBRegressor):
+    """Random forests need num_parallel_tree > 1 with row and column
+    sampling, which the CUDA backend does not train; fit raises."""
+
+    def fit(self, X, y, *args, **kwargs):
+        raise XGBoostError("Random forests (num_parallel_tree > 1, subsample, colsample_*) are not "
+                           "implemented by the CUDA backend.")
+
+
+class XGBRFClassifier(XGBClassifier):
+    """See XGBRFRegressor."""
+
+    def fit(self, X, y, *args, **kwargs):
+        raise XGBoostError("Random forests (num_parallel_tree > 1, subsample, colsample_*) are not "
+                           "implemented by the CUDA backend.")
