@@ -35,3 +35,22 @@ def test_reference_package_names_exist():
         xgb.RabitTracker(2)
     with pytest.raises(TypeError):
         xgb.ExtMemQuantileDMatrix([[1.0]])
+
+
+def test_dataframe_names_flow_into_matrices_slices_and_boosters():
+    pd = pytest.importorskip("pandas")
+    import numpy as np
+    df = pd.DataFrame({"age": [1.0, 2.0, np.nan], "size": [3.0, 4.0, 5.0]})
+    d = xgb.DMatrix(df, label=[0.0, 1.0, 0.0])
+    assert d.feature_names == ["age", "size"]
+    assert d.slice([2, 0]).feature_names == ["age", "size"]
+    b = xgb.Booster({}, [d])
+    assert b.feature_names == ["age", "size"]
+    d.feature_types = "q"
+    assert d.feature_types == ["q", "q"]
+    with pytest.raises(ValueError, match="unique"):
+        d.feature_names = ["a", "a"]
+    d.feature_names = None
+    assert d.feature_names is None
+    csr = d.get_data()
+    assert csr.shape == (3, 2) and csr.nnz == 5
