@@ -54,3 +54,22 @@ def test_dataframe_names_flow_into_matrices_slices_and_boosters():
     assert d.feature_names is None
     csr = d.get_data()
     assert csr.shape == (3, 2) and csr.nnz == 5
+
+
+def test_feature_validation_and_split_value_histogram():
+    import json
+
+    import numpy as np
+    from test_model_io import _model
+    b = xgb.Booster()
+    b.load_model(bytearray(json.dumps(_model()).encode()))
+    b.feature_names = ["a", "b", "c"]
+    d = xgb.DMatrix(np.zeros((2, 3), np.float32), feature_names=["a", "x", "c"])
+    with pytest.raises(ValueError, match="feature_names mismatch"):
+        b.predict(d)
+    with pytest.raises(ValueError, match="did not contain feature names"):
+        b.predict(xgb.DMatrix(np.zeros((2, 3), np.float32)))
+    # One threshold per feature: numpy's single bin spans value +- 0.5, and
+    # rows carry each bin's right edge.
+    assert b.get_split_value_histogram("c", as_pandas=False).tolist() == [[0.75, 1.0]]
+    assert b.get_split_value_histogram("a", as_pandas=False).tolist() == [[-1.0, 1.0]]

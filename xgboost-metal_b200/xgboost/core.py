@@ -539,9 +539,60 @@ class Booster:
                 v = int(v)
             _check_call(_LIB.XGBoosterSetParam(self.handle, _c_str(str(k)), _c_str(str(v))))
 
+    def _validate_features(self, feature_names):
+        """Raises ValueError when the data's feature names differ from the
+        model's (python-package/xgboost/core.py Booster._validate_features)."""
+        mine = self.feature_names
+        if mine is None:
+            return
+        if feature_names is None:
+            raise ValueError("data did not contain feature names, but the following fields are expected: "
+                             + ", ".join(mine))
+        if list(mine) != list(feature_names):
+            msg = "feature_names mismatch: {0} {1}".format(mine, feature_names)
+            dat_missing = set(mine) - set(feature_names)
+            my_missing = set(feature_names) - set(mine)
+            if dat_missing:
+                msg += "\nexpected " + ", ".join(str(s) for s in dat_missing) + " in input data"
+            if my_missing:
+                msg += "\ntraining data did not have the following fields: " + ", ".join(str(s) for s in my_missing)
+            raise ValueError(msg)
+
+    def get_split_value_histogram(self, feature, fmap="", bins=None, as_pandas=True):
+        """Histogram of the thresholds the model splits `feature` at: rows of
+        (SplitValue, Count) for the non-empty bins."""
+        import re
+        names = self.feature_names
+        if names is not None and feature in names:
+            types = self.feature_types
+            if types is not None and types[names.index(feature)] == "c":
+                raise ValueError("Split value histogram doesn't support categorical split.")
+        pattern = re.compile(r"\[{0}<([\d.Ee+-]+)\]".format(re.escape(str(feature))))
+        values = [float(x) for tree in self.get_dump(fmap=fmap) for x in pattern.findall(tree)]
+        n_unique = len(np.unique(values))
+        nbins = max(min(n_unique, bins) if bins is not None else n_unique, 1)
+        counts, edges = np.histogram(values, bins=nbins)
+        stacked = np.column_stack((edges[1:], counts))
+        stacked = stacked[stacked[:, 1] > 0]
+        if as_pandas:
+            try:
+                from pandas import DataFrame
+                return DataFrame(stacked, columns=["SplitValue", "Count"])
+            except ImportError:
+                pass
+        return stacked
+
     def update(self, dtrain, iteration, fobj=None):
         """One boosting round; with `fobj(margins, dtrain) -> (grad, hess)` the
         round trains on a custom objective's gradients."""
+        if self.feature_names is None and dtrain.num_row():
+            names, types = dtrain.feature_names, dtrain.feature_types
+            if names is not None:
+                self.feature_names = names
+            if types is not None:
+                self.feature_types = types
+        else:
+            self._validate_features(dtrain.feature_names)
         if fobj is None:
             _check_call(_LIB.XGBoosterUpdateOneIter(self.handle, ctypes.c_int(iteration),
                                                     dtrain.handle))
@@ -578,6 +629,8 @@ class Booster:
                 training=False, iteration_range=(0, 0), strict_shape=False):
         if pred_leaf or pred_contribs or pred_interactions:
             raise XGBoostError("Leaf and contribution predictions are not implemented by the CUDA backend.")
+        if validate_features:
+            self._validate_features(data.feature_names)
         config = json.dumps({"type": 1 if output_margin else 0, "training": bool(training),
                              "iteration_begin": int(iteration_range[0]),
                              "iteration_end": int(iteration_range[1]),
