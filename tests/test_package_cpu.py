@@ -73,3 +73,13 @@ def test_feature_validation_and_split_value_histogram():
     # rows carry each bin's right edge.
     assert b.get_split_value_histogram("c", as_pandas=False).tolist() == [[0.75, 1.0]]
     assert b.get_split_value_histogram("a", as_pandas=False).tolist() == [[-1.0, 1.0]]
+
+
+def test_estimators_are_scikit_learn_estimators():
+    base = pytest.importorskip("sklearn.base")
+    r = xgb.XGBRegressor(max_depth=3, learning_rate=0.1, eval_metric="mae")
+    c = base.clone(r)
+    assert c.get_params()["max_depth"] == 3 and c.get_params()["eval_metric"] == "mae"
+    assert base.is_regressor(r) and base.is_classifier(xgb.XGBClassifier())
+    assert c.set_params(max_depth=5).max_depth == 5
+    assert "XGBRegressor(" in repr(r)

@@ -9,6 +9,17 @@ from .training import train
 
 __all__ = ["XGBModel", "XGBRegressor", "XGBClassifier", "XGBRanker", "XGBRFRegressor", "XGBRFClassifier"]
 
+# With scikit-learn present the estimators take its mixins (score(), the
+# estimator type tags), as upstream's do.
+try:
+    from sklearn.base import BaseEstimator as _Base
+    from sklearn.base import ClassifierMixin as _ClassifierBase
+    from sklearn.base import RegressorMixin as _RegressorBase
+except ImportError:  # pragma: no cover - scikit-learn is optional
+    _Base = object
+    _ClassifierBase = object
+    _RegressorBase = object
+
 _PARAM_NAMES = (
     "max_depth", "max_leaves", "max_bin", "grow_policy", "learning_rate", "verbosity",
     "objective", "booster", "tree_method", "n_jobs", "gamma", "min_child_weight",
@@ -20,7 +31,7 @@ _PARAM_NAMES = (
     "multi_strategy", "eval_metric", "early_stopping_rounds", "callbacks")
 
 
-class XGBModel:
+class XGBModel(_Base):
     def __init__(self, *, n_estimators=100, objective=None, **kwargs):
         self.n_estimators = n_estimators
         self.objective = objective
@@ -142,7 +153,7 @@ class XGBModel:
                                           iteration_range=self._iteration_range(iteration_range))
 
 
-class XGBRegressor(XGBModel):
+class XGBRegressor(_RegressorBase, XGBModel):
     def __init__(self, *, objective="reg:squarederror", **kwargs):
         super().__init__(objective=objective, **kwargs)
 
@@ -152,7 +163,7 @@ class XGBRegressor(XGBModel):
         return self._fit(X, y, sample_weight, eval_set, verbose, self.get_xgb_params(), xgb_model)
 
 
-class XGBClassifier(XGBModel):
+class XGBClassifier(_ClassifierBase, XGBModel):
     def __init__(self, *, objective="binary:logistic", **kwargs):
         super().__init__(objective=objective, **kwargs)
 
