@@ -112,12 +112,22 @@ class XGBModel(_Base):
                 self.n_classes_ = meta["n_classes_"]
             self._Booster.set_attr(scikit_learn=None)
 
-    def _fit(self, X, y, sample_weight, eval_set, verbose, params, xgb_model=None):
-        dtrain = DMatrix(X, y, weight=sample_weight,
-                         missing=np.nan if self.missing is None else self.missing)
+    def _fit(self, X, y, sample_weight, eval_set, verbose, params, xgb_model=None, base_margin=None,
+             sample_weight_eval_set=None, base_margin_eval_set=None):
+        missing = np.nan if self.missing is None else self.missing
+        dtrain = DMatrix(X, y, weight=sample_weight, base_margin=base_margin, missing=missing,
+                         feature_types=self.feature_types)
         evals = []
-        for i, (ex, ey) in enumerate(eval_set or []):
-            evals.append((DMatrix(ex, ey), "validation_%d" % i))
+        eval_set = list(eval_set or [])
+        for name, extra in (("sample_weight_eval_set", sample_weight_eval_set),
+                            ("base_margin_eval_set", base_margin_eval_set)):
+            if extra is not None and len(extra) != len(eval_set):
+                raise ValueError("%s must have one entry per eval_set pair" % name)
+        for i, (ex, ey) in enumerate(eval_set):
+            w = sample_weight_eval_set[i] if sample_weight_eval_set is not None else None
+            m = base_margin_eval_set[i] if base_margin_eval_set is not None else None
+            evals.append((DMatrix(ex, ey, weight=w, base_margin=m, missing=missing,
+                                  feature_types=self.feature_types), "validation_%d" % i))
         self.evals_result_ = {}
         if self.eval_metric is not None:
             params["eval_metric"] = self.eval_metric
@@ -127,6 +137,8 @@ class XGBModel(_Base):
                               xgb_model=xgb_model.get_booster() if isinstance(xgb_model, XGBModel)
                               else xgb_model)
         self.n_features_in_ = dtrain.num_col()
+        if hasattr(X, "columns"):
+            self.feature_names_in_ = np.asarray([str(c) for c in X.columns], dtype=object)
         return self
 
     def _iteration_range(self, iteration_range):
@@ -160,7 +172,8 @@ class XGBRegressor(_RegressorBase, XGBModel):
     def fit(self, X, y, *, sample_weight=None, base_margin=None, eval_set=None, verbose=True,
             xgb_model=None, sample_weight_eval_set=None, base_margin_eval_set=None,
             feature_weights=None):
-        return self._fit(X, y, sample_weight, eval_set, verbose, self.get_xgb_params(), xgb_model)
+        return self._fit(X, y, sample_weight, eval_set, verbose, self.get_xgb_params(), xgb_model,
+                         base_margin, sample_weight_eval_set, base_margin_eval_set)
 
 
 class XGBClassifier(_ClassifierBase, XGBModel):
@@ -181,7 +194,8 @@ class XGBClassifier(_ClassifierBase, XGBModel):
             params["num_class"] = self.n_classes_
         eval_set = [(ex, np.searchsorted(self.classes_, np.asarray(ey)).astype(np.float32))
                     for ex, ey in (eval_set or [])]
-        return self._fit(X, encoded, sample_weight, eval_set, verbose, params, xgb_model)
+        return self._fit(X, encoded, sample_weight, eval_set, verbose, params, xgb_model,
+                         base_margin, sample_weight_eval_set, base_margin_eval_set)
 
     def predict_proba(self, X, validate_features=True, base_margin=None, iteration_range=None):
         p = super().predict(X, base_margin=base_margin, iteration_range=iteration_range)
