@@ -653,6 +653,12 @@ class Booster:
         input goes through a DMatrix."""
         if predict_type not in ("value", "margin"):
             raise XGBoostError("predict_type must be 'value' or 'margin'.")
+        if validate_features:
+            if hasattr(data, "columns"):
+                self._validate_features([str(c) for c in data.columns])
+            shape = getattr(data, "shape", None)
+            if shape is not None and len(shape) == 2 and shape[1] != self.num_features():
+                raise ValueError("Feature shape mismatch, expected: %d, got %d" % (self.num_features(), shape[1]))
         if _is_scipy_csr(data):
             dm = DMatrix(data, missing=missing, base_margin=base_margin)
             return self.predict(dm, output_margin=predict_type == "margin",

@@ -161,8 +161,13 @@ class XGBModel(_Base):
                 iteration_range=None):
         dm = DMatrix(X, missing=np.nan if self.missing is None else self.missing,
                      base_margin=base_margin)
-        return self.get_booster().predict(dm, output_margin=output_margin,
-                                          iteration_range=self._iteration_range(iteration_range))
+        # As upstream's in-place prediction: names are checked for data
+        # frames, only the width for plain arrays.
+        b = self.get_booster()
+        if validate_features and not hasattr(X, "columns") and dm.num_col() != b.num_features():
+            raise ValueError("Feature shape mismatch, expected: %d, got %d" % (b.num_features(), dm.num_col()))
+        return b.predict(dm, output_margin=output_margin, validate_features=validate_features and
+                         hasattr(X, "columns"), iteration_range=self._iteration_range(iteration_range))
 
 
 class XGBRegressor(_RegressorBase, XGBModel):
