@@ -239,3 +239,31 @@ def test_cross_validation_and_training_callbacks(tmp_path):
     ttp = _json.loads(b.save_config())["learner"]["gradient_booster"]["tree_train_param"]
     assert float(ttp["learning_rate"]) == pytest.approx(0.1)
     assert sorted(p.name for p in tmp_path.iterdir()) == ["model_1.json", "model_2.json"]
+
+
+def test_leaf_prediction_matches_a_host_walk_of_the_model():
+    import json as _json
+    rng = np.random.default_rng(18)
+    X = rng.normal(size=(1500, 4)).astype(np.float32)
+    X[rng.random(X.shape) < 0.1] = np.nan
+    params = {"objective": "multi:softprob", "num_class": 3, "tree_method": "hist", "device": "cuda",
+              "max_depth": 4}
+    yk = (np.nan_to_num(X[:, 0]) > 0).astype(np.float32) + (np.nan_to_num(X[:, 1]) > 0.5)
+    b = xgb.train(params, xgb.DMatrix(X, label=yk), 3)
+    d = xgb.DMatrix(X)
+    leaves = b.predict(d, pred_leaf=True)
+    assert leaves.shape == (1500, 9)
+    trees = _json.loads(bytes(b.save_raw("json")).decode())["learner"]["gradient_booster"]["model"]["trees"]
+    want = np.zeros((1500, 9), np.float32)
+    for t, tree in enumerate(trees):
+        for r in range(1500):
+            n = 0
+            while tree["left_children"][n] >= 0:
+                v = X[r, tree["split_indices"][n]]
+                go_left = bool(tree["default_left"][n]) if np.isnan(v) else v < np.float32(tree["split_conditions"][n])
+                n = tree["left_children"][n] if go_left else tree["right_children"][n]
+            want[r, t] = n
+    np.testing.assert_array_equal(leaves, want)
+    strict = b.predict(d, pred_leaf=True, strict_shape=True, iteration_range=(1, 3))
+    assert strict.shape == (1500, 2, 3, 1)
+    np.testing.assert_array_equal(strict.reshape(1500, 6), want[:, 3:])

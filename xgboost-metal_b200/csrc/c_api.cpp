@@ -480,7 +480,7 @@ XGB_DLL int XGBoosterBoostOneIter(BoosterHandle handle, DMatrixHandle dtrain, fl
 }
 
 namespace {
-// Prediction config: {"type": 0 value | 1 margin, "iteration_begin",
+// Prediction config: {"type": 0 value | 1 margin | 6 leaf ids, "iteration_begin",
 // "iteration_end", "training", "strict_shape"} (src/c_api.cpp:507 in the
 // reference).
 void predict_output(xgbb::Booster& bst, const DMatrixPtr& d, const char* config, bst_ulong const** out_shape,
@@ -488,7 +488,8 @@ void predict_output(xgbb::Booster& bst, const DMatrixPtr& d, const char* config,
   Json c = Json::parse(config && *config ? config : "{}");
   int type = 0;
   if (auto* t = c.find("type")) type = int(t->num);
-  require(type == 0 || type == 1, "Only value (type 0) and margin (type 1) predictions are implemented.");
+  require(type == 0 || type == 1 || type == 6,
+          "Only value (type 0), margin (type 1) and leaf (type 6) predictions are implemented.");
   uint32_t begin = 0, end = 0;
   if (auto* b = c.find("iteration_begin")) begin = uint32_t(b->num);
   if (auto* e = c.find("iteration_end")) end = uint32_t(e->num);
@@ -497,8 +498,12 @@ void predict_output(xgbb::Booster& bst, const DMatrixPtr& d, const char* config,
   bool strict = false;
   if (auto* s = c.find("strict_shape")) strict = s->truthy();
   std::vector<uint64_t> shape;
-  results.floats = bst.predict(d, type == 1, begin, end, training, shape);
-  if (strict && shape.size() == 1) shape.push_back(1);
+  if (type == 6) {
+    results.floats = bst.predict_leaf(d, begin, end, strict, shape);
+  } else {
+    results.floats = bst.predict(d, type == 1, begin, end, training, shape);
+    if (strict && shape.size() == 1) shape.push_back(1);
+  }
   results.shape.assign(shape.begin(), shape.end());
   *out_shape = results.shape.data();
   *out_dim = results.shape.size();

@@ -1102,6 +1102,42 @@ std::vector<float> Booster::predict(const std::shared_ptr<DMatrix>& dp, bool out
   return out;
 }
 
+// Leaf node ids of rounds [begin, end) (the reference's pred_leaf,
+// src/learner.cpp:533-553): [rows][trees], or [rows][rounds][groups][1] when
+// strict, [rows] for a single tree.
+std::vector<float> Booster::predict_leaf(const std::shared_ptr<DMatrix>& dp, uint32_t begin, uint32_t end,
+                                         bool strict, std::vector<uint64_t>& shape) {
+  gpu();
+  configure();
+  finish_pending();
+  DMatrix& d = *dp;
+  require(!initialized_ || d.cols == num_feature_ || d.rows == 0, "Feature shape mismatch.");
+  const uint32_t G = std::max<uint32_t>(groups_, 1);
+  if (end == 0 || end > rounds_) end = rounds_;
+  if (begin > end) begin = end;
+  std::vector<DevNode> all;
+  std::vector<uint32_t> tb;
+  for (size_t t = size_t(begin) * G; t < size_t(end) * G && t < trees_.size(); ++t) {
+    tb.push_back(uint32_t(all.size()));
+    all.insert(all.end(), trees_[t].nodes.begin(), trees_[t].nodes.end());
+  }
+  const uint32_t trees = uint32_t(tb.size());
+  std::vector<float> out(size_t(d.rows) * trees);
+  if (d.rows && trees) {
+    DeviceBuffer dn(all.size() * sizeof(DevNode)), db(tb.size() * 4), dout(out.size() * 4);
+    XGBB_CUDA(cudaMemcpyAsync(dn.get(), all.data(), all.size() * sizeof(DevNode), cudaMemcpyHostToDevice, stream_));
+    XGBB_CUDA(cudaMemcpyAsync(db.get(), tb.data(), tb.size() * 4, cudaMemcpyHostToDevice, stream_));
+    launch_leaf_index(d.device_data(stream_), d.rows, d.cols, dn.as<DevNode>(), db.as<uint32_t>(), trees,
+                      dout.as<float>(), stream_);
+    XGBB_CUDA(cudaMemcpyAsync(out.data(), dout.get(), out.size() * 4, cudaMemcpyDeviceToHost, stream_));
+    XGBB_CUDA(cudaStreamSynchronize(stream_));
+  }
+  if (strict) shape = {d.rows, end - begin, G, 1};
+  else if (trees == 1) shape = {d.rows};
+  else shape = {d.rows, trees};
+  return out;
+}
+
 // ---------------------------------------------------------------------------
 // Model files: upstream XGBoost's JSON model schema (the one the reference
 // writes, src/model.cpp:28-78, and reads, src/model.cpp:79-240): per tree the

@@ -121,6 +121,10 @@ class Booster {
   std::vector<float> predict(const std::shared_ptr<DMatrix>& d, bool output_margin,
                              uint32_t iter_begin, uint32_t iter_end, bool training,
                              std::vector<uint64_t>& shape);
+  // Node id (as float) of the leaf each row reaches in each tree of rounds
+  // [begin, end): [rows][trees] (strict: [rows][rounds][groups][1]).
+  std::vector<float> predict_leaf(const std::shared_ptr<DMatrix>& d, uint32_t begin, uint32_t end, bool strict,
+                                  std::vector<uint64_t>& shape);
   uint32_t boosted_rounds() const { return rounds_; }
   uint32_t num_feature() const { return num_feature_; }
   uint32_t groups() const { return groups_; }

@@ -1794,6 +1794,26 @@ __global__ void predict_kernel(const float* __restrict__ X, uint32_t rows, uint3
   }
 }
 
+// The leaf each row reaches in each tree, as the node id in float32:
+// out[row][tree] (pred_leaf; the reference's predict_leaf kernel).
+__global__ void leaf_index_kernel(const float* __restrict__ X, uint32_t rows, uint32_t cols,
+                                  const DevNode* __restrict__ nodes, const uint32_t* tree_begin,
+                                  uint32_t trees, float* out) {
+  for (uint32_t t = blockIdx.y; t < trees; t += gridDim.y) {
+    const DevNode* tn = nodes + tree_begin[t];
+    for (uint32_t r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
+      const float* x = X + size_t(r) * cols;
+      int32_t n = 0;
+      while (tn[n].left >= 0) {
+        const float v = x[tn[n].feature];
+        const bool left = isnan(v) ? tn[n].default_left != 0u : v < tn[n].threshold;
+        n = left ? tn[n].left : tn[n].right;
+      }
+      out[size_t(r) * trees + t] = float(n);
+    }
+  }
+}
+
 // Output transforms (kernels/boost.metal:1855-1885) with det_expf.
 __global__ void transform_kernel(int objective, float* v, uint32_t rows, uint32_t groups) {
   for (uint32_t r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
@@ -2207,6 +2227,14 @@ void launch_predict(const float* X, uint32_t rows, uint32_t cols, const DevNode*
   if (!rows) return;
   predict_kernel<<<grid_for(rows, 128), 128, 0, stream>>>(X, rows, cols, nodes, tree_begin,
                                                          tree_group, trees, base, groups, out);
+  XGBB_CUDA(cudaGetLastError());
+}
+
+void launch_leaf_index(const float* X, uint32_t rows, uint32_t cols, const DevNode* nodes,
+                       const uint32_t* tree_begin, uint32_t trees, float* out, cudaStream_t stream) {
+  if (!rows || !trees) return;
+  dim3 grid(grid_for(rows, 128), std::min<uint32_t>(trees, 65535u));
+  leaf_index_kernel<<<grid, 128, 0, stream>>>(X, rows, cols, nodes, tree_begin, trees, out);
   XGBB_CUDA(cudaGetLastError());
 }
 

@@ -170,6 +170,9 @@ inline uint32_t max_slots_at(uint32_t depth) { return 1u << depth; }
 void launch_predict(const float* X, uint32_t rows, uint32_t cols, const DevNode* nodes,
                     const uint32_t* tree_begin, const uint32_t* tree_group, uint32_t trees,
                     const float* base_margin, uint32_t groups, float* out, cudaStream_t stream);
+// Node id (float) of the leaf each row reaches in each tree: out[rows][trees].
+void launch_leaf_index(const float* X, uint32_t rows, uint32_t cols, const DevNode* nodes,
+                       const uint32_t* tree_begin, uint32_t trees, float* out, cudaStream_t stream);
 void launch_transform(int objective, float* values, uint32_t rows, uint32_t groups,
                       cudaStream_t stream);
 

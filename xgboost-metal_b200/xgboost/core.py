@@ -627,11 +627,11 @@ class Booster:
     def predict(self, data, output_margin=False, pred_leaf=False, pred_contribs=False,
                 approx_contribs=False, pred_interactions=False, validate_features=True,
                 training=False, iteration_range=(0, 0), strict_shape=False):
-        if pred_leaf or pred_contribs or pred_interactions:
-            raise XGBoostError("Leaf and contribution predictions are not implemented by the CUDA backend.")
+        if pred_contribs or pred_interactions:
+            raise XGBoostError("Contribution predictions are not implemented by the CUDA backend.")
         if validate_features:
             self._validate_features(data.feature_names)
-        config = json.dumps({"type": 1 if output_margin else 0, "training": bool(training),
+        config = json.dumps({"type": 6 if pred_leaf else (1 if output_margin else 0), "training": bool(training),
                              "iteration_begin": int(iteration_range[0]),
                              "iteration_end": int(iteration_range[1]),
                              "strict_shape": bool(strict_shape)})
