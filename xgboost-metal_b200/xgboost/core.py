@@ -43,7 +43,7 @@ c_bst_ulong = ctypes.c_uint64
 
 def _check_call(ret):
     if ret != 0:
-        raise XGBoostError(_LIB.XGBGetLastError().decode())
+        raise XGBoostError(_LIB.XGBGetLastError().decode("utf-8", "replace"))
 
 
 def _c_str(s):
