@@ -83,3 +83,16 @@ def test_estimators_are_scikit_learn_estimators():
     assert base.is_regressor(r) and base.is_classifier(xgb.XGBClassifier())
     assert c.set_params(max_depth=5).max_depth == 5
     assert "XGBRegressor(" in repr(r)
+
+
+def test_dmatrix_from_text_files(tmp_path):
+    import numpy as np
+    p = tmp_path / "d.csv"
+    p.write_text("0,1.5,2\n1,,3\n")
+    d = xgb.DMatrix(str(p) + "?format=csv&label_column=0")
+    assert (d.num_row(), d.num_col()) == (2, 2)
+    np.testing.assert_array_equal(d.get_label(), [0, 1])
+    s = tmp_path / "d.svm"
+    s.write_text("1 0:1 2:3\n0 1:2\n")
+    d = xgb.DMatrix(str(s) + "?format=libsvm", feature_names=["a", "b", "c"])
+    assert d.feature_names == ["a", "b", "c"] and d.num_nonmissing() == 3

@@ -230,6 +230,21 @@ class DMatrix:
                 data._feature_names
             self.feature_types = feature_types if feature_types is not None else data._feature_types
             return
+        if isinstance(data, (str, os.PathLike)):
+            # A text file: "path?format=csv" (label_column=K) or
+            # "path?format=libsvm" (XGDMatrixCreateFromURI).
+            uri = os.fspath(data)
+            _check_call(_LIB.XGDMatrixCreateFromURI(_c_str(json.dumps({"uri": uri, "silent": int(silent)})),
+                                                    ctypes.byref(self.handle)))
+            if feature_names is not None:
+                self.feature_names = feature_names
+            if feature_types is not None:
+                self.feature_types = feature_types
+            for setter, values in ((self.set_label, label), (self.set_weight, weight),
+                                   (self.set_base_margin, base_margin)):
+                if values is not None:
+                    setter(values)
+            return
         if _is_scipy_csr(data):
             csr = data
             _check_call(_LIB.XGDMatrixCreateFromCSR(
