@@ -240,7 +240,7 @@ def test_single_rank_collective_and_trackers(capfd):
     core._check_call(L.XGCommunicatorGetProcessorName(ctypes.byref(name)))
     assert name.value.decode() == socket.gethostname()
     core._check_call(L.XGCommunicatorPrint(b"hello from the communicator"))
-    assert "hello from the communicator" in capfd.readouterr().err
+    assert "hello from the communicator" in capfd.readouterr().out
     assert L.XGTrackerCreate(b"{}", ctypes.byref(ctypes.c_void_p())) == -1
     assert b"NCCL" in L.XGBGetLastError()
     assert L.XGTrackerFree(None) == 0

@@ -30,9 +30,30 @@ def _lib_path():
     return path
 
 
+_VERSION = (3, 5, 0)
+_LOG_CALLBACK = ctypes.CFUNCTYPE(None, ctypes.c_char_p)
+
+
+def _log(msg):
+    print(msg.decode("utf-8", "replace"), flush=True)
+
+
 def _load_lib():
+    """Loads the library, routes its log messages to stdout and checks that
+    it is the version this package belongs to (python-package/xgboost/
+    _c_api.py:90-174 in the reference)."""
     lib = ctypes.CDLL(_lib_path())
     lib.XGBGetLastError.restype = ctypes.c_char_p
+    lib.callback = _LOG_CALLBACK(_log)
+    if lib.XGBRegisterLogCallback(lib.callback) != 0:
+        raise XGBoostError(lib.XGBGetLastError().decode("utf-8", "replace"))
+    major, minor, patch = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    lib.XGBoostVersion(ctypes.byref(major), ctypes.byref(minor), ctypes.byref(patch))
+    libver = (major.value, minor.value, patch.value)
+    if libver != _VERSION:
+        raise ValueError("Mismatched version between the Python package (%s) and the native shared object "
+                         "(%s) loaded from %s." % (".".join(map(str, _VERSION)), ".".join(map(str, libver)),
+                                                   _lib_path()))
     return lib
 
 
