@@ -48,6 +48,15 @@ XGB_DLL int XGBBSketchHost(const float* X, bst_ulong rows, bst_ulong cols, const
  * be NULL. Needs no GPU. */
 XGB_DLL int XGBBMetricHost(char const* name, const float* pred, bst_ulong rows, uint32_t groups,
                            const float* labels, const float* weights, int multiclass, double* out);
+/* No counterpart in the reference, which evaluates in one process. The
+ * rank-additive form of a mean-type metric (every metric but auc) used when
+ * rows are sharded over workers: sums[0] = sum of weight x per-row term,
+ * sums[1] = sum of weights over `rows`; XGBBMetricFromSums turns the sums of
+ * all workers into the metric (a square root for rmse and rmsle). AUC is
+ * refused: it needs all rows. */
+XGB_DLL int XGBBMetricSumsHost(char const* name, const float* pred, bst_ulong rows, uint32_t groups,
+                               const float* labels, const float* weights, int multiclass, double* sums);
+XGB_DLL int XGBBMetricFromSums(char const* name, double loss_sum, double weight_sum, double* out);
 /* Gradient pairs [groups][rows][2] and power-of-two scales [groups][2]: the
  * reference's gradients + gradient_partial_sums + gradient_scales
  * (kernels/boost.metal:553-601, kernels/gradient_quantization.metal.h:1-67). */

@@ -116,3 +116,62 @@ def test_eval_metric_settings_accumulate_in_the_config():
     c = xgb.Booster()
     c.load_config(b.save_config())
     assert json.loads(c.save_config())["learner"]["metrics"] == cfg["learner"]["metrics"]
+
+
+def _sums(name, pred, labels, weights=None, multiclass=False):
+    pred = np.ascontiguousarray(pred, np.float32)
+    labels = np.ascontiguousarray(labels, np.float32)
+    groups = pred.shape[1] if pred.ndim == 2 else 1
+    w = None if weights is None else np.ascontiguousarray(weights, np.float32)
+    out = (ctypes.c_double * 2)()
+    fp = ctypes.POINTER(ctypes.c_float)
+    ret = core._LIB.XGBBMetricSumsHost(name.encode(), pred.ctypes.data_as(fp), core.c_bst_ulong(len(labels)),
+                                       ctypes.c_uint32(groups), labels.ctypes.data_as(fp),
+                                       None if w is None else w.ctypes.data_as(fp), ctypes.c_int(int(multiclass)),
+                                       out)
+    if ret != 0:
+        raise xgb.XGBoostError(core._LIB.XGBGetLastError().decode())
+    return out[0], out[1]
+
+
+def _from_sums(name, loss, weight):
+    out = ctypes.c_double()
+    ret = core._LIB.XGBBMetricFromSums(name.encode(), ctypes.c_double(loss), ctypes.c_double(weight),
+                                       ctypes.byref(out))
+    if ret != 0:
+        raise xgb.XGBoostError(core._LIB.XGBGetLastError().decode())
+    return out.value
+
+
+@pytest.mark.parametrize("name", ["rmse", "mae", "rmsle", "logloss", "error", "error@0.3", "mape"])
+def test_row_shards_sum_to_the_whole_matrix_metric(data, name):
+    # Row-sharded evaluation adds every shard's (weighted loss, weight) and
+    # finishes once: the metric of all rows, whatever the split.
+    p, y, w = data
+    y = y + 0.5 if name in ("mape", "rmsle") else y
+    whole = metric(name, p, y, w)
+    for cuts in ([1000], [1, 700, 1999], [0, 2000]):
+        parts = np.split(np.arange(len(y)), cuts)
+        sums = [_sums(name, p[i], y[i], w[i]) for i in parts]
+        got = _from_sums(name, sum(s[0] for s in sums), sum(s[1] for s in sums))
+        assert got == pytest.approx(whole, rel=1e-12)
+
+
+def test_row_shards_of_multiclass_metrics(data):
+    rng = np.random.default_rng(4)
+    probs = rng.random((900, 5)).astype(np.float32)
+    probs /= probs.sum(1, keepdims=True)
+    labels = rng.integers(0, 5, 900).astype(np.float32)
+    for name in ("merror", "mlogloss"):
+        whole = metric(name, probs, labels, multiclass=True)
+        a = _sums(name, probs[:300], labels[:300], multiclass=True)
+        b = _sums(name, probs[300:], labels[300:], multiclass=True)
+        assert _from_sums(name, a[0] + b[0], a[1] + b[1]) == pytest.approx(whole, rel=1e-12)
+
+
+def test_auc_is_not_a_row_sum(data):
+    p, y, _ = data
+    with pytest.raises(xgb.XGBoostError, match="not a sum over rows"):
+        _sums("auc", p, y)
+    with pytest.raises(xgb.XGBoostError, match="has not been implemented"):
+        _from_sums("ndcg", 1.0, 1.0)

@@ -1053,6 +1053,25 @@ XGB_DLL int XGBBMetricHost(char const* name, const float* pred, bst_ulong rows, 
   });
 }
 
+XGB_DLL int XGBBMetricSumsHost(char const* name, const float* pred, bst_ulong rows, uint32_t groups,
+                               const float* labels, const float* weights, int multiclass, double* sums) {
+  return guarded([&] {
+    require(name != nullptr && sums != nullptr, "Null argument.");
+    require(rows == 0 || (pred != nullptr && labels != nullptr), "Null predictions or labels.");
+    require(rows < (1ull << 32) && groups >= 1, "Invalid shape.");
+    require(!xgbb::metric_needs_all_rows(name), std::string(name) + " is not a sum over rows.");
+    xgbb::metric_sums(name, pred, uint32_t(rows), groups, labels, weights, multiclass != 0, &sums[0], &sums[1]);
+  });
+}
+
+XGB_DLL int XGBBMetricFromSums(char const* name, double loss_sum, double weight_sum, double* out) {
+  return guarded([&] {
+    require(name != nullptr && out != nullptr, "Null argument.");
+    require(!xgbb::metric_needs_all_rows(name), std::string(name) + " is not a sum over rows.");
+    *out = xgbb::metric_from_sums(name, loss_sum, weight_sum);
+  });
+}
+
 XGB_DLL int XGBBSketchHost(const float* X, bst_ulong rows, bst_ulong cols, const float* weights,
                            uint32_t max_bin, int threads, float* cuts, uint32_t* counts, float* minima) {
   return guarded([&] {

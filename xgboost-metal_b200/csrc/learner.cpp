@@ -367,17 +367,104 @@ std::string Booster::evaluate(int iteration, const std::vector<std::shared_ptr<D
     } else {
       pred = predict(data[i], false, 0, 0, false, shape);
     }
-    for (const std::string& m : metrics) {
-      require(d.labels.size() == d.rows, "Evaluation data requires labels.");
-      require(d.weights.empty() || d.weights.size() == d.rows, "Evaluation weights must have one entry per row.");
-      const double v = eval_metric(m, pred.data(), d.rows, groups_, d.labels.data(),
-                                   d.weights.empty() ? nullptr : d.weights.data(), multiclass);
+    require(metrics.empty() || d.labels.size() == d.rows, "Evaluation data requires labels.");
+    require(d.weights.empty() || d.weights.size() == d.rows, "Evaluation weights must have one entry per row.");
+    const float* weights = d.weights.empty() ? nullptr : d.weights.data();
+    std::vector<double> values(metrics.size());
+    if (!Comm::get().active()) {
+      for (size_t j = 0; j < metrics.size(); ++j)
+        values[j] = eval_metric(metrics[j], pred.data(), d.rows, groups_, d.labels.data(), weights, multiclass);
+    } else {
+      evaluate_across_ranks(metrics, pred, d, multiclass, values);
+    }
+    for (size_t j = 0; j < metrics.size(); ++j) {
       char buf[64];
-      std::snprintf(buf, sizeof buf, "%.10g", v);
-      out += "\t" + names[i] + "-" + m + ":" + buf;
+      std::snprintf(buf, sizeof buf, "%.10g", values[j]);
+      out += "\t" + names[i] + "-" + metrics[j] + ":" + buf;
     }
   }
   return out;
+}
+
+// Row-sharded evaluation: every rank holds some rows of the matrix, and each
+// metric is the metric of all ranks' rows, so that every rank reports the
+// same score and early stopping ends training on the same round everywhere.
+// The reference evaluates in one process (src/metrics.cpp); this is the
+// row-sharded form of the same metrics. Mean-type metrics add up (weighted loss, weight) pairs over the ranks; AUC
+// sorts all rows, so its predictions, labels and weights are gathered first.
+void Booster::evaluate_across_ranks(const std::vector<std::string>& metrics, const std::vector<float>& pred,
+                                    const DMatrix& d, bool multiclass, std::vector<double>& values) {
+  Comm& comm = Comm::get();
+  const uint32_t world = uint32_t(comm.world());
+  const float* weights = d.weights.empty() ? nullptr : d.weights.data();
+  std::vector<double> sums(2 * metrics.size(), 0.0);
+  bool gather = false;
+  for (size_t j = 0; j < metrics.size(); ++j) {
+    if (metric_needs_all_rows(metrics[j])) {
+      gather = true;
+      continue;
+    }
+    metric_sums(metrics[j], pred.data(), d.rows, groups_, d.labels.data(), weights, multiclass, &sums[2 * j],
+                &sums[2 * j + 1]);
+  }
+  if (!sums.empty()) {
+    DeviceBuffer buf(sums.size() * 8);
+    XGBB_CUDA(cudaMemcpyAsync(buf.get(), sums.data(), sums.size() * 8, cudaMemcpyHostToDevice, stream_));
+    comm.sum_f64(buf.get(), sums.size(), stream_);
+    XGBB_CUDA(cudaMemcpyAsync(sums.data(), buf.get(), sums.size() * 8, cudaMemcpyDeviceToHost, stream_));
+    wait_stream("an evaluation sum");
+  }
+  for (size_t j = 0; j < metrics.size(); ++j)
+    if (!metric_needs_all_rows(metrics[j])) values[j] = metric_from_sums(metrics[j], sums[2 * j], sums[2 * j + 1]);
+  if (!gather) return;
+  // Row counts and weight presence of every rank, then each rank's rows
+  // padded to the largest count: [world][max_rows] slots.
+  std::vector<uint64_t> mine = {d.rows, weights ? 1u : 0u}, counts(2 * size_t(world));
+  {
+    DeviceBuffer send(16), recv(16 * size_t(world));
+    XGBB_CUDA(cudaMemcpyAsync(send.get(), mine.data(), 16, cudaMemcpyHostToDevice, stream_));
+    comm.all_gather(send.get(), recv.get(), 16, stream_);
+    XGBB_CUDA(cudaMemcpyAsync(counts.data(), recv.get(), counts.size() * 8, cudaMemcpyDeviceToHost, stream_));
+    wait_stream("evaluation row counts");
+  }
+  uint64_t widest = 0, total = 0;
+  bool any_weights = false;
+  for (uint32_t r = 0; r < world; ++r) {
+    widest = std::max(widest, counts[2 * r]);
+    total += counts[2 * r];
+    any_weights = any_weights || counts[2 * r + 1];
+  }
+  require(total <= UINT32_MAX, "Evaluation data has too many rows across workers.");
+  // One record per row: groups predictions, the label and the weight.
+  const size_t width = size_t(groups_) + 2;
+  std::vector<float> local(size_t(widest) * width, 0.0f), all(local.size() * world);
+  for (uint32_t r = 0; r < d.rows; ++r) {
+    std::copy(pred.data() + size_t(r) * groups_, pred.data() + size_t(r + 1) * groups_, &local[r * width]);
+    local[r * width + groups_] = d.labels[r];
+    local[r * width + groups_ + 1] = weights ? weights[r] : 1.0f;
+  }
+  if (!local.empty()) {
+    DeviceBuffer send(local.size() * 4), recv(all.size() * 4);
+    XGBB_CUDA(cudaMemcpyAsync(send.get(), local.data(), local.size() * 4, cudaMemcpyHostToDevice, stream_));
+    comm.all_gather(send.get(), recv.get(), local.size() * 4, stream_);
+    XGBB_CUDA(cudaMemcpyAsync(all.data(), recv.get(), all.size() * 4, cudaMemcpyDeviceToHost, stream_));
+    wait_stream("evaluation rows");
+  }
+  std::vector<float> p, l, w;
+  p.reserve(size_t(total) * groups_);
+  l.reserve(total);
+  w.reserve(total);
+  for (uint32_t r = 0; r < world; ++r)
+    for (uint64_t k = 0; k < counts[2 * r]; ++k) {
+      const float* rec = &all[(size_t(r) * widest + k) * width];
+      p.insert(p.end(), rec, rec + groups_);
+      l.push_back(rec[groups_]);
+      w.push_back(rec[groups_ + 1]);
+    }
+  for (size_t j = 0; j < metrics.size(); ++j)
+    if (metric_needs_all_rows(metrics[j]))
+      values[j] = eval_metric(metrics[j], p.data(), uint32_t(total), groups_, l.data(),
+                              any_weights ? w.data() : nullptr, multiclass);
 }
 
 std::string Booster::get_param(const std::string& key, const std::string& def) const {

@@ -171,6 +171,8 @@ class Booster {
   void finish_round(TrainState& ts);
   void gpu();  // makes the booster's device current; fails without a GPU
   void wait_stream(const char* what);
+  void evaluate_across_ranks(const std::vector<std::string>& metrics, const std::vector<float>& pred,
+                             const DMatrix& d, bool multiclass, std::vector<double>& values);
   void record_tree_launches(TrainState& ts, uint32_t group, cudaStream_t stream, bool capturing,
                             uint32_t parity);
   void materialize();

@@ -54,12 +54,18 @@ std::string default_metric(const std::string& objective) {
   return "rmse";
 }
 
+bool metric_needs_all_rows(const std::string& name) { return name.substr(0, name.find('@')) == "auc"; }
+
 double eval_metric(const std::string& name, const float* pred, uint32_t rows, uint32_t groups,
                    const float* labels, const float* weights, bool multiclass) {
   const size_t at = name.find('@');
   const std::string base = name.substr(0, at);
-  const std::string param = at == std::string::npos ? "" : name.substr(at + 1);
-  if (base == "auc") {
+  if (base != "auc") {
+    double loss_sum = 0, weight_sum = 0;
+    metric_sums(name, pred, rows, groups, labels, weights, multiclass, &loss_sum, &weight_sum);
+    return metric_from_sums(name, loss_sum, weight_sum);
+  }
+  {
     if (rows == 0) return kNaN;
     if (!multiclass) {
       for (uint32_t r = 0; r < rows; ++r)
@@ -82,10 +88,30 @@ double eval_metric(const std::string& name, const float* pred, uint32_t rows, ui
     }
     return total > 0 ? sum / total : kNaN;
   }
+}
+
+namespace {
+int metric_type(const std::string& base) {
   static const char* const kNames[] = {"rmse", "mae", "rmsle", "logloss", "merror", "mlogloss", "error", "mape"};
-  int type = -1;
   for (int i = 0; i < 8; ++i)
-    if (base == kNames[i]) type = i;
+    if (base == kNames[i]) return i;
+  return -1;
+}
+}  // namespace
+
+double metric_from_sums(const std::string& name, double loss_sum, double weight_sum) {
+  const int type = metric_type(name.substr(0, name.find('@')));
+  require(type >= 0, "Metric has not been implemented yet: " + name);
+  const double mean = weight_sum > 0 ? loss_sum / weight_sum : kNaN;
+  return type == 0 || type == 2 ? std::sqrt(mean) : mean;
+}
+
+void metric_sums(const std::string& name, const float* pred, uint32_t rows, uint32_t groups, const float* labels,
+                 const float* weights, bool multiclass, double* loss_out, double* weight_out) {
+  const size_t at = name.find('@');
+  const std::string base = name.substr(0, at);
+  const std::string param = at == std::string::npos ? "" : name.substr(at + 1);
+  const int type = metric_type(base);
   require(type >= 0, "Metric has not been implemented yet: " + name);
   const bool per_row = type == 4 || type == 5;
   if (per_row || multiclass)
@@ -127,8 +153,8 @@ double eval_metric(const std::string& name, const float* pred, uint32_t rows, ui
     loss_sum += double(w * loss);
     weight_sum += double(w);
   }
-  const double mean = weight_sum > 0 ? loss_sum / weight_sum : kNaN;
-  return type == 0 || type == 2 ? std::sqrt(mean) : mean;
+  *loss_out = loss_sum;
+  *weight_out = weight_sum;
 }
 
 }  // namespace xgbb

@@ -14,6 +14,14 @@ namespace xgbb {
 double eval_metric(const std::string& name, const float* pred, uint32_t rows, uint32_t groups,
                    const float* labels, const float* weights, bool multiclass);
 
+// The weighted sum of per-row terms and the weight sum of a mean-type metric
+// (every metric but auc), and the metric from them: rows split over ranks
+// give the metric of all rows once both sums are added up.
+bool metric_needs_all_rows(const std::string& name);
+void metric_sums(const std::string& name, const float* pred, uint32_t rows, uint32_t groups, const float* labels,
+                 const float* weights, bool multiclass, double* loss_sum, double* weight_sum);
+double metric_from_sums(const std::string& name, double loss_sum, double weight_sum);
+
 // The metric an objective is evaluated with when none is set
 // (src/learner.cpp:1012-1024 in the reference).
 std::string default_metric(const std::string& objective);
