@@ -68,7 +68,10 @@ def train(X, y, params, rounds, weights=None):
     rows, cols = X.shape
     groups = int(params.get("num_class", 1)) if params.get("objective", "").startswith("multi") else 1
     depth = int(params.get("max_depth", 6))
-    cap = rounds * groups * ((2 << depth) - 1)
+    tree_cap = 2 * rows + 1
+    if 0 < depth < 31:
+        tree_cap = min(tree_cap, (2 << depth) - 1)
+    cap = rounds * groups * tree_cap
     nodes = np.zeros(cap, DEVNODE_DTYPE)
     sizes = np.zeros(rounds * groups, np.uint32)
     margins = np.zeros((rows, groups), np.float32)

@@ -13,6 +13,7 @@
 #include <sstream>
 
 #include "comm.h"
+#include "grower.h"
 #include "json.h"
 #include "metrics.h"
 #include "sketch.h"
@@ -228,6 +229,13 @@ void DMatrix::quantise(uint32_t mb, const DMatrix* ref, cudaStream_t stream, int
 // ---------------------------------------------------------------------------
 // Training state for one matrix.
 // ---------------------------------------------------------------------------
+// Pinned upload words of a host-driven tree: an evaluation's segments and
+// tile offsets (3 * kMaxFrontier + 1), or a partition's items, tile offsets
+// and cursors (8 * kQueueBatch + 1).
+constexpr size_t kQueueUpWords = 3 * size_t(kMaxFrontier) + 1 > 8 * size_t(kQueueBatch) + 1
+                                     ? 3 * size_t(kMaxFrontier) + 1
+                                     : 8 * size_t(kQueueBatch) + 1;
+
 struct Booster::TrainState {
   std::weak_ptr<DMatrix> owner;
   DMatrix* d = nullptr;
@@ -257,7 +265,22 @@ struct Booster::TrainState {
   uint32_t parity = 0;
   uint32_t capacity = 0;
   std::vector<cudaEvent_t> events;  // profiling: [groups][levels][2]
+  // Host-driven trees (loss-guided, leaf budgets, depth > 10): row order and
+  // its partition scratch, node histograms and candidates of one batch, the
+  // batch descriptors, and pinned landing buffers for the host's reads.
+  DeviceBuffer q_order, q_scratch, q_built, q_cand, q_keys, q_sums, q_seg, q_items, q_cursor, q_best, q_nodes;
+  uint32_t q_slots = 0;
+  NodeBest* q_best_host = nullptr;   // pinned [kMaxFrontier]
+  uint32_t* q_cursor_host = nullptr; // pinned [2 * kQueueBatch]
+  uint32_t* q_up_host = nullptr;     // pinned upload staging
+  long long* q_sums_host = nullptr;  // pinned [2 * kMaxFrontier]
+  cudaEvent_t q_done = nullptr;
   ~TrainState() {
+    if (q_best_host) cudaFreeHost(q_best_host);
+    if (q_cursor_host) cudaFreeHost(q_cursor_host);
+    if (q_up_host) cudaFreeHost(q_up_host);
+    if (q_sums_host) cudaFreeHost(q_sums_host);
+    if (q_done) cudaEventDestroy(q_done);
     for (auto g : graphs)
       if (g) cudaGraphExecDestroy(g);
     for (auto e : events) cudaEventDestroy(e);
@@ -516,19 +539,28 @@ void Booster::configure() {
   require(method == "hist" || method == "auto" || method == "gpu_hist",
           "CUDA tree training requires tree_method='hist' or 'auto'.");
   require(get_param("booster", "gbtree") == "gbtree", "Only the gbtree booster is implemented.");
-  require(get_param("grow_policy", "depthwise") == "depthwise", "Only grow_policy='depthwise' is implemented.");
+  const std::string policy = get_param("grow_policy", "depthwise");
+  require(policy == "depthwise" || policy == "lossguide", "grow_policy must be depthwise or lossguide.");
   require(number(params_, "subsample", 1) == 1.0f, "subsample < 1 is not implemented by the CUDA backend.");
   for (auto k : {"colsample_bytree", "colsample_bylevel", "colsample_bynode"})
     require(number(params_, k, 1) == 1.0f, std::string(k) + " < 1 is not implemented by the CUDA backend.");
   require(integer(params_, "num_parallel_tree", 1) == 1, "num_parallel_tree > 1 is not implemented.");
-  require(integer(params_, "max_leaves", 0) == 0, "max_leaves is not implemented.");
   for (auto k : {"monotone_constraints", "interaction_constraints"}) {
     auto v = get_param(k, "");
     require(v.empty() || v == "()" || v == "[]", std::string(k) + " are not implemented.");
   }
-  tp_.max_depth = uint32_t(integer(params_, "max_depth", 6));
-  require(tp_.max_depth >= 1 && tp_.max_depth <= kMaxDepth,
-          "max_depth must be in [1, 10] for the CUDA depthwise driver.");
+  // The reference's limits (src/learner.cpp:258-260). Loss-guided trees,
+  // leaf budgets and depths the level-synchronous device driver does not
+  // cover (0 = unlimited, or above 10) grow host-driven (src/tree.cpp:376-384).
+  const long max_depth = integer(params_, "max_depth", 6), max_leaves = integer(params_, "max_leaves", 0);
+  require(max_depth >= 0 && max_leaves >= 0, "max_depth and max_leaves must be nonnegative.");
+  require(max_depth <= 30 || max_leaves, "max_depth must not exceed 30 unless max_leaves is constrained.");
+  require(max_leaves <= (long(INT32_MAX) + 1) / 2, "max_leaves exceeds the tree node index range.");
+  require(max_depth || max_leaves, "max_depth and max_leaves cannot both be unconstrained.");
+  tp_.max_depth = uint32_t(std::min<long>(max_depth, INT32_MAX));
+  lossguide_ = policy == "lossguide";
+  max_leaves_ = uint32_t(max_leaves);
+  host_driven_ = lossguide_ || max_leaves_ || tp_.max_depth == 0 || tp_.max_depth > kMaxDepth;
   tp_.eta = number(params_, "learning_rate", 0.3f);
   tp_.reg_lambda = number(params_, "reg_lambda", 1.0f);
   tp_.reg_alpha = number(params_, "reg_alpha", 0.0f);
@@ -683,8 +715,29 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp, bo
     XGBB_CUDA(cudaMemcpyAsync(&ts->rows_total, n.get(), 8, cudaMemcpyDeviceToHost, stream_));
     XGBB_CUDA(cudaStreamSynchronize(stream_));
   }
-  const uint32_t n = d.rows, G = groups_, C = d.cols, D = tp_.max_depth;
+  // Host-driven trees use the level-synchronous buffers of a one-level tree
+  // only (for the common round setup) and their own below.
+  const uint32_t n = d.rows, G = groups_, C = d.cols, D = host_driven_ ? 1u : tp_.max_depth;
   const Ellpack& e = d.ell;
+  if (host_driven_) {
+    require(e.bins <= kMaxBins, "host-driven trees support at most 256 bins per feature");
+    ts->q_slots = lossguide_ ? 2u : kMaxFrontier;
+    ts->q_order.resize(std::max<size_t>(n, 1) * 4);
+    ts->q_scratch.resize(std::max<size_t>(n, 1) * 4);
+    ts->q_built.resize(size_t(C) * ts->q_slots * (e.bins + 1) * sizeof(longlong2));
+    ts->q_cand.resize(size_t(ts->q_slots) * C * sizeof(DevSplit));
+    ts->q_keys.resize(kMaxFrontier * 8);
+    ts->q_sums.resize(kMaxFrontier * 16);
+    ts->q_seg.resize((3 * size_t(kMaxFrontier) + 1) * 4);
+    ts->q_items.resize((6 * size_t(kQueueBatch) + 1) * 4);
+    ts->q_cursor.resize(2 * size_t(kQueueBatch) * 4);
+    ts->q_best.resize(kMaxFrontier * sizeof(NodeBest));
+    XGBB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ts->q_best_host), kMaxFrontier * sizeof(NodeBest)));
+    XGBB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ts->q_cursor_host), 2 * size_t(kQueueBatch) * 4));
+    XGBB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ts->q_up_host), kQueueUpWords * 4));
+    XGBB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ts->q_sums_host), 2 * size_t(kMaxFrontier) * 8));
+    XGBB_CUDA(cudaEventCreateWithFlags(&ts->q_done, cudaEventDisableTiming));
+  }
   ts->margins.resize(std::max<size_t>(size_t(n) * G, 1) * 4);
   ts->pairs.resize(std::max<size_t>(size_t(n) * G, 1) * 8);
   ts->mass.resize(mass_bytes(G));
@@ -835,6 +888,126 @@ bool staged_round(const unsigned int* max_bits, const float2* scales, uint32_t g
   };
   return two_limbs(bits[0], scale.x) && (unit_h || two_limbs(bits[1], scale.y));
 }
+
+// Device buffers of one group's host-driven tree (owned by the training
+// state).
+struct QueueDevice {
+  Ellpack e;
+  TreeParams tp;
+  const float2* pairs;  // this group's gradient pairs by row id
+  const float2* scale;  // this group's scales (device)
+  uint32_t* order;      // row order: each node owns a segment
+  uint32_t* scratch;
+  longlong2* built;     // [cols][slots][bins + 1]
+  DevSplit* cand;       // [slots][cols]
+  unsigned long long* keys;
+  long long* sums;      // [slots][2]
+  DriverState* state;
+  uint32_t* seg;        // [slots][2] segments, then [slots + 1] tile offsets
+  uint32_t* items;      // [kQueueBatch][5] partition items, then [kQueueBatch + 1] tile offsets
+  uint32_t* cursor;     // [kQueueBatch][2]
+  NodeBest* best;       // [kMaxFrontier]
+  NodeBest* best_host;  // pinned [kMaxFrontier]
+  uint32_t* cursor_host;  // pinned [kQueueBatch][2]
+  // Pinned staging of the uploads: a pageable copy would wait for the
+  // stream's earlier collectives outside the communicator's time limit.
+  uint32_t* up_host;      // pinned [kQueueUpWords]
+  long long* sums_host;   // pinned [kMaxFrontier][2]
+  uint32_t slots;       // node capacity of one evaluation
+  cudaEvent_t done;
+  cudaStream_t stream;
+  int hist_blocks, eval_blocks, part_blocks;
+};
+
+// The GPU backend of host-driven trees: node histograms (queue_hist_kernel),
+// summed over ranks when the rows are sharded so that every rank takes the
+// same decisions, split evaluation (eval_kernel), and row partitions; the
+// host waits once per evaluation and once per partition.
+class DeviceGrower final : public GrowerBackend {
+ public:
+  explicit DeviceGrower(const QueueDevice& q) : q_(q) {}
+
+  void evaluate(const std::vector<Segment>& nodes, bool root, const std::vector<long long>& sums,
+                std::vector<DevSplit>& out) override {
+    const uint32_t n = uint32_t(nodes.size());
+    require(n >= 1 && n <= q_.slots, "host-driven tree batch exceeds its buffers");
+    uint32_t* up = q_.up_host;
+    uint32_t tiles = 0;
+    for (uint32_t s = 0; s < n; ++s) {
+      up[2 * s] = nodes[s].begin;
+      up[2 * s + 1] = nodes[s].count;
+      up[2 * size_t(n) + s] = tiles;
+      tiles += (nodes[s].count + kQueueTileRows - 1) / kQueueTileRows;
+    }
+    up[3 * size_t(n)] = tiles;
+    XGBB_CUDA(cudaMemcpyAsync(q_.seg, up, (3 * size_t(n) + 1) * 4, cudaMemcpyHostToDevice, q_.stream));
+    if (!root) {
+      require(sums.size() == 2 * size_t(n), "host-driven tree node sums missing");
+      std::copy(sums.begin(), sums.end(), q_.sums_host);
+      XGBB_CUDA(cudaMemcpyAsync(q_.sums, q_.sums_host, sums.size() * 8, cudaMemcpyHostToDevice, q_.stream));
+    }
+    launch_queue_hist(q_.e, q_.order, q_.pairs, q_.scale, q_.seg, q_.seg + 2 * size_t(n), n, tiles, q_.built,
+                      q_.hist_blocks, q_.stream);
+    Comm::get().sum_u64(q_.built, size_t(q_.e.cols) * n * (q_.e.bins + 1) * 2, q_.stream);
+    queue_evaluate(q_.e, q_.tp, q_.scale, q_.state, n, root, q_.built, q_.sums, q_.cand, q_.keys, q_.best,
+                   q_.eval_blocks, q_.stream);
+    XGBB_CUDA(cudaMemcpyAsync(q_.best_host, q_.best, size_t(n) * sizeof(NodeBest), cudaMemcpyDeviceToHost,
+                              q_.stream));
+    XGBB_CUDA(cudaEventRecord(q_.done, q_.stream));
+    Comm::get().wait(q_.done, "a host-driven tree's split evaluation");
+    out.resize(n);
+    for (uint32_t s = 0; s < n; ++s) {
+      out[s] = q_.best_host[s].split;
+      if (!q_.best_host[s].key) {
+        out[s] = DevSplit{};
+        out[s].feature = -1;
+        out[s].split_bin = -1;
+        out[s].gain = -INFINITY;
+      }
+    }
+  }
+
+  void partition(const std::vector<PartitionItem>& items, std::vector<uint32_t>& left) override {
+    const uint32_t m = uint32_t(items.size());
+    require(m <= kQueueBatch, "host-driven tree batch exceeds its buffers");
+    left.assign(m, 0);
+    if (!m) return;
+    uint32_t* up = q_.up_host;
+    uint32_t* cursor = q_.up_host + 6 * size_t(m) + 1;
+    uint32_t tiles = 0;
+    for (uint32_t i = 0; i < m; ++i) {
+      const PartitionItem& it = items[i];
+      require(it.feature >= 0 && uint32_t(it.feature) < q_.e.cols, "host-driven tree split feature out of range");
+      uint32_t* d = &up[5 * size_t(i)];
+      d[0] = it.begin;
+      d[1] = it.count;
+      d[2] = uint32_t(it.feature);
+      d[3] = uint32_t(it.split_bin);
+      d[4] = it.default_left;
+      up[5 * size_t(m) + i] = tiles;
+      tiles += (it.count + kQueuePartRows - 1) / kQueuePartRows;
+      cursor[2 * i] = it.begin;
+      cursor[2 * i + 1] = it.begin + it.count;
+    }
+    up[6 * size_t(m)] = tiles;
+    XGBB_CUDA(cudaMemcpyAsync(q_.items, up, (6 * size_t(m) + 1) * 4, cudaMemcpyHostToDevice, q_.stream));
+    XGBB_CUDA(cudaMemcpyAsync(q_.cursor, cursor, 2 * size_t(m) * 4, cudaMemcpyHostToDevice, q_.stream));
+    launch_queue_partition(q_.e, q_.order, q_.scratch, q_.items, q_.items + 5 * size_t(m), m, tiles, q_.cursor,
+                           q_.part_blocks, q_.stream);
+    XGBB_CUDA(cudaMemcpyAsync(q_.cursor_host, q_.cursor, 2 * size_t(m) * 4, cudaMemcpyDeviceToHost, q_.stream));
+    XGBB_CUDA(cudaEventRecord(q_.done, q_.stream));
+    Comm::get().wait(q_.done, "a host-driven tree's row partition");
+    for (uint32_t i = 0; i < m; ++i) {
+      const uint32_t l = q_.cursor_host[2 * i], r = q_.cursor_host[2 * i + 1];
+      require(l == r && l >= items[i].begin && l - items[i].begin <= items[i].count,
+              "host-driven tree partition lost rows");
+      left[i] = l - items[i].begin;
+    }
+  }
+
+ private:
+  QueueDevice q_;
+};
 }  // namespace
 
 void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s, bool capturing,
@@ -956,6 +1129,10 @@ void Booster::run_round(TrainState& ts, const CustomGradients* custom) {
   launch_mass_exact(pairs, n, G, mass, stream_);
   comm.sum_u64(mass.exact, 20 * size_t(G), stream_);
   launch_scales_exact(G, mass, ts.scales.as<float2>(), stream_);
+  if (host_driven_) {
+    grow_host_driven(ts);
+    return;
+  }
   const bool use_graph = integer(params_, "cuda_graph", 1) != 0;
   bool captured = false;
   const uint32_t b = ts.parity;
@@ -995,6 +1172,73 @@ void Booster::run_round(TrainState& ts, const CustomGradients* custom) {
   finish_round(ts);
   ts.pending = int(b);
   ts.pending_captured = captured;
+}
+
+// One round of host-driven trees (grower.cpp), one per group, each grown to
+// completion before the next; the margins take each tree's leaves on the
+// device.
+void Booster::grow_host_driven(TrainState& ts) {
+  DMatrix& d = *ts.d;
+  const uint32_t n = ts.rows, G = ts.groups;
+  // The scales follow the round's collectives on the stream: wait for them
+  // within the communicator's limit, then read.
+  wait_stream("a training round's gradient scales");
+  std::vector<float2> scales(G);
+  XGBB_CUDA(cudaMemcpyAsync(scales.data(), ts.scales.get(), G * sizeof(float2), cudaMemcpyDeviceToHost, stream_));
+  XGBB_CUDA(cudaStreamSynchronize(stream_));
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device_);
+  QueueDevice q{};
+  q.e = d.ell;
+  q.tp = tp_;
+  q.order = ts.q_order.as<uint32_t>();
+  q.scratch = ts.q_scratch.as<uint32_t>();
+  q.built = ts.q_built.as<longlong2>();
+  q.cand = ts.q_cand.as<DevSplit>();
+  q.keys = ts.q_keys.as<unsigned long long>();
+  q.sums = ts.q_sums.as<long long>();
+  q.state = ts.state.as<DriverState>();
+  q.seg = ts.q_seg.as<uint32_t>();
+  q.items = ts.q_items.as<uint32_t>();
+  q.cursor = ts.q_cursor.as<uint32_t>();
+  q.best = ts.q_best.as<NodeBest>();
+  q.best_host = ts.q_best_host;
+  q.cursor_host = ts.q_cursor_host;
+  q.up_host = ts.q_up_host;
+  q.sums_host = ts.q_sums_host;
+  q.slots = ts.q_slots;
+  q.done = ts.q_done;
+  q.stream = stream_;
+  q.hist_blocks = sms * 8;
+  q.eval_blocks = sms * 8;
+  q.part_blocks = sms * 8;
+  GrowerParams gp;
+  gp.tree = tp_;
+  gp.lossguide = lossguide_;
+  gp.max_leaves = max_leaves_;
+  std::vector<HostTree> grown(G);
+  for (uint32_t g = 0; g < G; ++g) {
+    q.pairs = ts.pairs.as<float2>() + size_t(g) * n;
+    q.scale = ts.scales.as<float2>() + g;
+    gp.scale_g = scales[g].x;
+    gp.scale_h = scales[g].y;
+    launch_queue_iota(q.order, n, stream_);
+    DeviceGrower backend(q);
+    HostTree& t = grown[g];
+    t.group = g;
+    t.nodes = grow_tree_host_driven(backend, n, gp);
+    // The previous group's margin update has completed (the growth above
+    // waited on the stream), so the node buffer may be reallocated.
+    ts.q_nodes.resize(t.nodes.size() * sizeof(DevNode));
+    XGBB_CUDA(cudaMemcpyAsync(ts.q_nodes.get(), t.nodes.data(), t.nodes.size() * sizeof(DevNode),
+                              cudaMemcpyHostToDevice, stream_));
+    launch_queue_margins(d.ell, ts.q_nodes.as<DevNode>(), uint32_t(t.nodes.size()), ts.margins.as<float>(), G, g,
+                         stream_);
+  }
+  wait_stream("a host-driven round's margin update");
+  for (HostTree& t : grown) trees_.push_back(std::move(t));
+  ++rounds_;
+  ts.margin_rounds = rounds_;
 }
 
 // Turns the pending round's host copies into trees (and profile figures).

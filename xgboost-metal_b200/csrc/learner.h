@@ -173,6 +173,7 @@ class Booster {
   void wait_stream(const char* what);
   void evaluate_across_ranks(const std::vector<std::string>& metrics, const std::vector<float>& pred,
                              const DMatrix& d, bool multiclass, std::vector<double>& values);
+  void grow_host_driven(TrainState& ts);
   void record_tree_launches(TrainState& ts, uint32_t group, cudaStream_t stream, bool capturing,
                             uint32_t parity);
   void materialize();
@@ -186,6 +187,10 @@ class Booster {
   int objective_ = kSquaredError;
   uint32_t groups_ = 1, num_feature_ = 0, rounds_ = 0, max_bin_ = 256;
   TreeParams tp_{};
+  // Trees the level-synchronous device driver does not grow (loss-guided,
+  // leaf budgets, depth 0 or above 10) grow host-driven (grower.h).
+  bool host_driven_ = false, lossguide_ = false;
+  uint32_t max_leaves_ = 0;
   float spw_ = 1.0f;
   std::vector<float> base_score_, base_margin_;
   std::vector<HostTree> trees_;

@@ -1121,6 +1121,9 @@ struct EvalArgs {
   DevSplit* cand;
   unsigned long long* keys;
   bool write_bank;
+  // Host-driven trees: `built` holds every node's own histogram,
+  // [cols][pair_stride = slots][bins + 1], with no sibling subtraction.
+  bool direct;
 };
 
 struct Candidate {
@@ -1155,6 +1158,8 @@ __global__ void __launch_bounds__(256) eval_kernel(EvalArgs a) {
     const longlong2* pptr = nullptr;
     if (a.depth == 0) {
       bptr = a.built + size_t(f) * B1;
+    } else if (a.direct) {
+      bptr = a.built + (size_t(f) * a.pair_stride + slot) * B1;
     } else {
       const uint32_t p = slot >> 1;
       const uint32_t built_side = a.built_left[p] ? 0u : 1u;
@@ -1484,6 +1489,8 @@ __global__ void __launch_bounds__(1024) control_kernel(ControlArgs a) {
 // the best candidate of each slot (key + record) is gathered from all ranks
 // and the overall best written where control_kernel reads it, so every rank
 // selects the same split as one GPU evaluating every feature would.
+__global__ void set_frontier_kernel(DriverState* state, uint32_t frontier) { state->frontier = frontier; }
+
 struct BestRecord {
   unsigned long long key;
   DevSplit split;
@@ -2110,6 +2117,7 @@ void tree_level_eval(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t dep
   a.cand = ws.cand;
   a.keys = ws.keys[depth & 1];
   a.write_bank = depth + 1 < tl.params.max_depth;
+  a.direct = false;
   eval_kernel<<<tl.eval_blocks, 256, 0, stream>>>(a);
   XGBB_CUDA(cudaGetLastError());
 }
@@ -2129,6 +2137,37 @@ void tree_level_merge_best(const TreeWorkspace& ws, const TreeLaunch& tl, uint32
 }
 
 size_t best_record_bytes() { return sizeof(BestRecord); }
+static_assert(sizeof(BestRecord) == sizeof(NodeBest) && alignof(BestRecord) == alignof(NodeBest),
+              "NodeBest mirrors BestRecord");
+
+void queue_evaluate(const Ellpack& e, const TreeParams& tp, const float2* scale, DriverState* state,
+                    uint32_t slots, bool root, const longlong2* built, const long long* sums, DevSplit* cand,
+                    unsigned long long* keys, NodeBest* best, int blocks, cudaStream_t stream) {
+  // The node count eval_kernel reads (set by a kernel: a host copy would wait
+  // for the stream's earlier collectives).
+  set_frontier_kernel<<<1, 1, 0, stream>>>(state, slots);
+  XGBB_CUDA(cudaGetLastError());
+  XGBB_CUDA(cudaMemsetAsync(keys, 0, kMaxFrontier * sizeof(unsigned long long), stream));
+  EvalArgs a{};
+  a.e = e;
+  a.m = split_math(tp);
+  a.scale = scale;
+  a.state = state;
+  a.depth = root ? 0u : 1u;
+  a.built = built;
+  a.pair_stride = slots;
+  a.f_lo = 0;
+  a.f_hi = e.cols;
+  a.sums = sums;
+  a.cand = cand;
+  a.keys = keys;
+  a.write_bank = false;
+  a.direct = true;
+  eval_kernel<<<blocks, 256, 0, stream>>>(a);
+  XGBB_CUDA(cudaGetLastError());
+  pack_best_kernel<<<1, 512, 0, stream>>>(keys, cand, e.cols, reinterpret_cast<BestRecord*>(best));
+  XGBB_CUDA(cudaGetLastError());
+}
 
 void tree_level_control(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t depth,
                         cudaStream_t stream) {

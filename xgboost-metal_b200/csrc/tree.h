@@ -167,6 +167,40 @@ inline size_t hist_node_bytes(const Ellpack& e, uint32_t cols_pad) {
 inline uint32_t max_pairs_at(uint32_t depth) { return depth ? (1u << (depth - 1)) : 1u; }
 inline uint32_t max_slots_at(uint32_t depth) { return 1u << depth; }
 
+// Host-driven trees (grower.cpp): each node's split from its own histogram.
+// The best candidate of each node, as gathered for the host.
+struct NodeBest {
+  unsigned long long key;  // 0 when the node had no candidate
+  DevSplit split;
+};
+// Evaluates `slots` nodes (<= kMaxFrontier) whose histograms are in `built`
+// ([cols][slots][bins + 1]): the root (totals from its histogram) or children
+// whose exact totals are sums[slot][2]. Writes best[kMaxFrontier].
+void queue_evaluate(const Ellpack& e, const TreeParams& tp, const float2* scale, DriverState* state,
+                    uint32_t slots, bool root, const longlong2* built, const long long* sums, DevSplit* cand,
+                    unsigned long long* keys, NodeBest* best, int blocks, cudaStream_t stream);
+// Row order of a host-driven tree: 0, 1, ..., rows - 1.
+void launch_queue_iota(uint32_t* rows, uint32_t n, cudaStream_t stream);
+// Histograms of `slots` nodes: node s owns order[seg[2s] .. seg[2s] + seg[2s+1]);
+// tiles[s] is the exclusive scan of the nodes' tile counts (kQueueTileRows
+// rows per tile), tiles[slots] the total. `built` is cleared first.
+constexpr uint32_t kQueueTileRows = 2048;
+void launch_queue_hist(const Ellpack& e, const uint32_t* order, const float2* pairs, const float2* scale,
+                       const uint32_t* seg, const uint32_t* tiles, uint32_t slots, uint32_t total_tiles,
+                       longlong2* built, int blocks, cudaStream_t stream);
+// Splits the segment of each item between its children: items[i] = (begin,
+// count, feature, split_bin, default_left); cursor[i] = (begin, begin +
+// count) on entry, (begin + left rows, begin + left rows) on exit. `scratch`
+// has as many rows as `order`.
+constexpr uint32_t kQueuePartRows = 1024;
+void launch_queue_partition(const Ellpack& e, uint32_t* order, uint32_t* scratch, const uint32_t* items,
+                            const uint32_t* tiles, uint32_t nitems, uint32_t total_tiles, uint32_t* cursor,
+                            int blocks, cudaStream_t stream);
+// margins[row][group] += the leaf each row reaches in `nodes`, walking the
+// quantised codes.
+void launch_queue_margins(const Ellpack& e, const DevNode* nodes, uint32_t node_count, float* margins,
+                          uint32_t groups, uint32_t group, cudaStream_t stream);
+
 void launch_predict(const float* X, uint32_t rows, uint32_t cols, const DevNode* nodes,
                     const uint32_t* tree_begin, const uint32_t* tree_group, uint32_t trees,
                     const float* base_margin, uint32_t groups, float* out, cudaStream_t stream);
