@@ -53,6 +53,9 @@ def leave_after_two_rounds(params, shard, rank, world):
     os._exit(1)
 
 
+HOST_DRIVEN = {"grow_policy": "lossguide", "max_depth": 0, "max_leaves": 24}
+
+
 def main():
     import faulthandler
     faulthandler.dump_traceback_later(int(os.environ.get("XGBB_WORKER_TIMEOUT", "240")), exit=True)
@@ -78,9 +81,20 @@ def main():
     if mode == "leave":
         leave_after_two_rounds(params, shard, rank, world)
         return
-    bst = xgb.train(params, shard, 6)
+    evals_result = {}
+    if mode == "hostdriven":
+        # Loss-guided trees under a leaf budget, evaluated on every rank's
+        # shard: the scores cover all ranks' rows.
+        params.update(HOST_DRIVEN)
+        metrics = ["rmse", "mae"] if objective == "reg:squarederror" else ["logloss", "error", "auc"]
+        params["eval_metric"] = metrics
+        bst = xgb.train(params, shard, 6, evals=[(shard, "train")], evals_result=evals_result)
+    else:
+        bst = xgb.train(params, shard, 6)
     margins = bst.predict(xgb.DMatrix(X), output_margin=True)
     np.save(os.path.join(out_dir, "margins_%d.npy" % rank), margins)
+    with open(os.path.join(out_dir, "evals_%d.json" % rank), "w") as f:
+        json.dump(evals_result, f)
     xgb.collective.finalize()
     dist.barrier()
     dist.destroy_process_group()
