@@ -43,6 +43,12 @@ XGB_DLL int XGBBQuantizeHost(const float* X, bst_ulong rows, bst_ulong cols, uin
  * GPU. */
 XGB_DLL int XGBBSketchHost(const float* X, bst_ulong rows, bst_ulong cols, const float* weights,
                            uint32_t max_bin, int threads, float* cuts, uint32_t* counts, float* minima);
+/* The same cuts computed on the GPU (the reference's sketch kernels,
+ * kernels/quantile.metal.h:19-400, driven as in src/quantile.cpp:22-213):
+ * X [rows][cols] and weights (or NULL) are host arrays copied to the device;
+ * results land in the host arrays as for XGBBSketchHost, bit for bit. */
+XGB_DLL int XGBBSketchDevice(const float* X, bst_ulong rows, bst_ulong cols, const float* weights,
+                             uint32_t max_bin, float* cuts, uint32_t* counts, float* minima);
 /* One evaluation metric of transformed predictions [rows][groups] (the
  * metric side of XGBoosterEvalOneIter, src/metrics.cpp:8-158); weights may
  * be NULL. Needs no GPU. */

@@ -88,6 +88,20 @@ def train(X, y, params, rounds, weights=None):
     return trees, margins
 
 
+def sketch_device(X, max_bin, weights=None):
+    """The GPU sketch (XGBBSketchDevice): cuts, counts, minima."""
+    X = np.ascontiguousarray(X, np.float32)
+    rows, cols = X.shape
+    stride = max(1, min(max_bin, rows))
+    cuts = np.zeros((cols, stride), np.float32)
+    counts = np.zeros(cols, np.uint32)
+    minima = np.zeros(cols, np.float32)
+    w = None if weights is None else np.ascontiguousarray(weights, np.float32)
+    check(lib().XGBBSketchDevice(_ptr(X), ctypes.c_uint64(rows), ctypes.c_uint64(cols), _ptr(w),
+                                 ctypes.c_uint32(max_bin), _ptr(cuts), _ptr(counts), _ptr(minima)))
+    return cuts, counts, minima
+
+
 def sketch(X, max_bin, weights=None, threads=0):
     """The product's host sketch (no GPU): cuts, counts, minima."""
     X = np.ascontiguousarray(X, np.float32)

@@ -1072,6 +1072,33 @@ XGB_DLL int XGBBMetricFromSums(char const* name, double loss_sum, double weight_
   });
 }
 
+XGB_DLL int XGBBSketchDevice(const float* X, bst_ulong rows, bst_ulong cols, const float* weights,
+                             uint32_t max_bin, float* cuts, uint32_t* counts, float* minima) {
+  return guarded([&] {
+    ensure_device();
+    require(rows < (1ull << 32) && cols < (1ull << 32), "Matrix too large.");
+    require(max_bin >= 2, "max_bin must be at least 2.");
+    require(rows == 0 || cols == 0 || X != nullptr, "Null matrix.");
+    xgbb::DeviceBuffer dx(std::max<size_t>(size_t(rows) * cols * 4, 4)), dw;
+    if (rows && cols) XGBB_CUDA(cudaMemcpy(dx.get(), X, size_t(rows) * cols * 4, cudaMemcpyHostToDevice));
+    if (weights) {
+      dw.resize(std::max<size_t>(size_t(rows) * 4, 4));
+      if (rows) XGBB_CUDA(cudaMemcpy(dw.get(), weights, size_t(rows) * 4, cudaMemcpyHostToDevice));
+    }
+    cudaStream_t s;
+    XGBB_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    try {
+      xgbb::sketch_cuts_device(dx.as<float>(), uint32_t(rows), uint32_t(cols), weights ? dw.as<float>() : nullptr,
+                               max_bin, cuts, counts, minima, s);
+    } catch (...) {
+      cudaStreamSynchronize(s);
+      cudaStreamDestroy(s);
+      throw;
+    }
+    cudaStreamDestroy(s);
+  });
+}
+
 XGB_DLL int XGBBSketchHost(const float* X, bst_ulong rows, bst_ulong cols, const float* weights,
                            uint32_t max_bin, int threads, float* cuts, uint32_t* counts, float* minima) {
   return guarded([&] {

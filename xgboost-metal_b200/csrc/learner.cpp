@@ -218,8 +218,22 @@ void DMatrix::quantise(uint32_t mb, const DMatrix* ref, cudaStream_t stream, int
     c->values.assign(size_t(cols) * c->stride, 0.0f);
     c->counts.assign(cols, 0);
     c->minima.assign(cols, -INFINITY);
-    sketch_cuts(host, rows, cols, weights.empty() ? nullptr : weights.data(), mb,
-                c->values.data(), c->counts.data(), c->minima.data(), threads);
+    // XGBB_SKETCH=device computes the cuts on the GPU (the same cuts, bit for
+    // bit); the host sketch is the default.
+    const char* where = std::getenv("XGBB_SKETCH");
+    if (where && std::strcmp(where, "device") == 0 && rows && cols) {
+      const float* X = device_data(stream);
+      DeviceBuffer w;
+      if (!weights.empty()) {
+        w.resize(weights.size() * 4);
+        XGBB_CUDA(cudaMemcpyAsync(w.get(), weights.data(), weights.size() * 4, cudaMemcpyHostToDevice, stream));
+      }
+      sketch_cuts_device(X, rows, cols, w.as<float>(), mb, c->values.data(), c->counts.data(), c->minima.data(),
+                         stream);
+    } else {
+      sketch_cuts(host, rows, cols, weights.empty() ? nullptr : weights.data(), mb, c->values.data(),
+                  c->counts.data(), c->minima.data(), threads);
+    }
     c->upload();
   }
   max_bin = mb;

@@ -17,6 +17,8 @@
 // they are compared exactly against the checker in the tests.
 #include "sketch.h"
 
+#include "sketch_par.h"
+
 #include <algorithm>
 #include <atomic>
 #include <cmath>
@@ -27,34 +29,16 @@
 namespace xgbb {
 namespace {
 
-struct Run {
-  float v, w;
-};
-struct Entry {
-  float rmin, rmax, wmin, value;
-};
-
-uint32_t budget_for(uint32_t bins, uint32_t count) {
-  if (!count) return 1;
-  const double epsilon = 1.0 / double(std::min(bins, count));
-  for (uint32_t level = 1; level < 32; ++level) {
-    uint64_t limit = uint64_t(std::ceil(level / (epsilon / 2.0))) + 1;
-    limit = std::min<uint64_t>(limit, count);
-    if ((uint64_t{1} << level) * limit >= count) return uint32_t(limit);
-  }
-  return count;
-}
+using sketch::budget_for;
+using sketch::Entry;
+using sketch::Run;
 
 // Stable sort of runs by value: an LSD radix sort on order-preserving keys
 // (the sign bit flipped for positives, all bits for negatives), which orders
 // every non-NaN float as `<` does (-0 never occurs: it is read as +0) and
 // keeps equal values in their input order, as std::stable_sort would. Passes
 // in which every key has the same digit are skipped.
-inline uint32_t order_key(float v) {
-  uint32_t b;
-  std::memcpy(&b, &v, 4);
-  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-}
+using sketch::order_key;
 void sort_runs(Run* a, size_t n, std::vector<Run>& tmp, std::vector<uint32_t>& keys,
                std::vector<uint32_t>& keys_tmp) {
   if (n < 2) return;
@@ -80,100 +64,6 @@ void sort_runs(Run* a, size_t n, std::vector<Run>& tmp, std::vector<uint32_t>& k
     std::swap(ks, kd);
   }
   if (src != a) std::copy(src, src + n, a);
-}
-
-inline float lower_next(const Entry& e) { return e.rmin + e.wmin; }
-inline float upper_prev(const Entry& e) { return e.rmax - e.wmin; }
-
-uint32_t prune(Entry* e, uint32_t size, uint32_t capacity) {
-  if (size <= capacity) return size;
-  if (capacity == 0) return 0;
-  if (capacity == 1) return 1;
-  const float begin = e[0].rmax, range = e[size - 1].rmin - begin;
-  const uint32_t n = capacity - 1;
-  uint32_t count = 1, i = 1, last = 0;
-  const Entry tail = e[size - 1];
-  Entry left = e[1], right = e[2];
-  for (uint32_t k = 1; k < n; ++k) {
-    const float rank = 2.0f * (float(k) * range / float(n) + begin);
-    while (i < size - 1 && rank >= right.rmax + right.rmin) {
-      ++i;
-      left = right;
-      if (i < size - 1) right = e[i + 1];
-    }
-    if (i == size - 1) break;
-    if (rank < lower_next(left) + upper_prev(right)) {
-      if (i != last) {
-        e[count++] = left;
-        last = i;
-      }
-    } else if (i + 1 != last) {
-      e[count++] = right;
-      last = i + 1;
-    }
-  }
-  if (last != size - 1) e[count++] = tail;
-  return count;
-}
-
-uint32_t combine(Entry* cur, uint32_t n, const Entry* other, uint32_t m, Entry* scratch) {
-  if (!m) return n;
-  if (!n) {
-    std::copy(other, other + m, cur);
-    return m;
-  }
-  uint32_t a = 0, b = 0, count = 0;
-  float prev_a = 0, prev_b = 0;
-  while (a < n && b < m) {
-    const Entry x = cur[a], y = other[b];
-    Entry r;
-    if (x.value == y.value) {
-      r = {x.rmin + y.rmin, x.rmax + y.rmax, x.wmin + y.wmin, x.value};
-      prev_a = lower_next(x);
-      prev_b = lower_next(y);
-      ++a;
-      ++b;
-    } else if (x.value < y.value) {
-      r = {x.rmin + prev_b, x.rmax + upper_prev(y), x.wmin, x.value};
-      prev_a = lower_next(x);
-      ++a;
-    } else {
-      r = {y.rmin + prev_a, y.rmax + upper_prev(x), y.wmin, y.value};
-      prev_b = lower_next(y);
-      ++b;
-    }
-    scratch[count++] = r;
-  }
-  const float tail_a = cur[n - 1].rmax, tail_b = other[m - 1].rmax;
-  while (a < n) {
-    Entry x = cur[a++];
-    x.rmin = x.rmin + prev_b;
-    x.rmax = x.rmax + tail_b;
-    scratch[count++] = x;
-  }
-  while (b < m) {
-    Entry y = other[b++];
-    y.rmin = y.rmin + prev_a;
-    y.rmax = y.rmax + tail_a;
-    scratch[count++] = y;
-  }
-  float prev_min = 0, prev_max = 0;
-  for (uint32_t i = 0; i < count; ++i) {
-    Entry e = scratch[i];
-    if (e.rmin < prev_min) e.rmin = prev_min;
-    else prev_min = e.rmin;
-    if (e.rmax < prev_max) e.rmax = prev_max;
-    if (e.rmax < lower_next(e)) e.rmax = lower_next(e);
-    prev_max = e.rmax;
-    cur[i] = e;
-  }
-  return count;
-}
-
-uint64_t bits64(double v) {
-  uint64_t b;
-  std::memcpy(&b, &v, 8);
-  return b;
 }
 
 // One feature's cuts from its column `col` (contiguous, `rows` values).
@@ -215,6 +105,8 @@ void one_feature(const float* col, uint32_t rows, const float* weights, uint32_t
   uint32_t counts[64] = {0};
   std::vector<Run> sort_tmp;
   std::vector<uint32_t> sort_keys, sort_keys_tmp;
+  const auto prune = sketch::prune_serial;
+  const auto combine = sketch::combine_serial;
   for (uint32_t batch = 0; batch < nbatch; ++batch) {
     const uint64_t begin = batch * capacity;
     const uint32_t size = uint32_t(std::min<uint64_t>(capacity, nruns - begin));
@@ -251,46 +143,7 @@ void one_feature(const float* col, uint32_t rows, const float* weights, uint32_t
     n = prune(current.data(), n, std::max(budget, limit));
   }
   const uint32_t size = prune(current.data(), n, budget);
-  uint32_t count = 0;
-  if (!size) {
-    out[0] = 1e-5f;
-    *count_out = 1;
-    return;
-  }
-  const Entry* e = current.data();
-  if (size <= max_bin) {
-    float last = e[0].value;
-    for (uint32_t i = 1; i < size; ++i)
-      if (last < e[i].value) {
-        out[count++] = e[i].value;
-        last = e[i].value;
-      }
-  } else {
-    float last = e[0].value;
-    uint32_t next = 1, cursor = 0;
-    const double total = double(e[size - 1].rmax);
-    for (uint32_t i = 1; i < max_bin; ++i) {
-      const uint64_t rank = bits64(double(i) * total / double(max_bin) * 2.0);
-      while (cursor < size - 2 && rank >= bits64(double(e[cursor + 1].rmin + e[cursor + 1].rmax)))
-        ++cursor;
-      const float boundary = lower_next(e[cursor]) + upper_prev(e[cursor + 1]);
-      float value = e[cursor + ((std::isnan(boundary) || rank >= bits64(double(boundary))) ? 1 : 0)].value;
-      if (value <= last) {
-        while (next < size && e[next].value <= last) ++next;
-        if (next == size) break;
-        value = e[next].value;
-      } else if (next < size && e[next].value <= value) {
-        do {
-          ++next;
-        } while (next < size && e[next].value <= value);
-      }
-      out[count++] = value;
-      last = value;
-    }
-  }
-  const float tail = e[size - 1].value;
-  out[count++] = tail + (std::fabs(tail) + 1e-5f);
-  *count_out = count;
+  *count_out = sketch::select_cuts(current.data(), size, max_bin, out);
 }
 
 }  // namespace

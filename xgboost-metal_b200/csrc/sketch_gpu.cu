@@ -1,0 +1,338 @@
+// Quantile cuts on the GPU: the data-parallel sketch of sketch_par.h run with
+// one thread block per task.
+//
+//   sketch_runs_kernel    one block per feature: the feature's runs in row
+//                         order, a chunk of rows at a time
+//                         (kernels/quantile.metal.h:19-140)
+//   sketch_batch_kernel   one block per batch of 2 * limit runs: sorted,
+//                         summarised and pruned (:216-240, :192-214)
+//   sketch_reduce_kernel  one block per feature: the batch summaries
+//                         combined and pruned level by level, then the cuts
+//                         (:266-400)
+//
+// Features are processed in groups sized to the free device memory; each
+// group's runs and summaries take about 16 bytes per row and feature.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "common.h"
+#include "sketch.h"
+#include "sketch_par.h"
+
+namespace xgbb {
+namespace {
+
+using namespace sketch;
+
+constexpr int kSketchThreads = 1024;
+constexpr uint32_t kChunkRows = 4096;
+
+template <class Op>
+struct Identity;
+template <>
+struct Identity<Add32> {
+  static __device__ uint32_t get() { return 0u; }
+};
+template <>
+struct Identity<SatAdd24> {
+  static __device__ uint32_t get() { return 0u; }
+};
+template <>
+struct Identity<MaxU32> {
+  static __device__ uint32_t get() { return 0u; }
+};
+template <>
+struct Identity<KeepMax> {
+  static __device__ float get() { return -INFINITY; }
+};
+
+// Block executor: loop bodies strided over the block's threads with a
+// barrier after each loop; scans over arrays by contiguous per-thread chunks
+// and a warp-shuffle scan of the chunk totals (the combining operations are
+// associative, and each is applied left to right).
+struct DeviceExec {
+  __device__ void note(SerialPath) {}
+
+  template <class F>
+  __device__ void for_each(uint32_t n, F&& f) {
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) f(i);
+    __syncthreads();
+  }
+
+  // Exclusive block scan of one value per thread; *total gets the fold of all.
+  template <class T, class Op>
+  __device__ T block_scan(T x, Op op, T* total) {
+    __shared__ unsigned long long warp_buf[32];
+    T* warp_tot = reinterpret_cast<T*>(warp_buf);
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = (blockDim.x + 31) >> 5;
+    T v = x;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const T o = __shfl_up_sync(0xffffffffu, v, d);
+      if (lane >= uint32_t(d)) v = op(o, v);
+    }
+    if (lane == 31) warp_tot[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+      T w = lane < nwarps ? warp_tot[lane] : Identity<Op>::get();
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const T o = __shfl_up_sync(0xffffffffu, w, d);
+        if (lane >= uint32_t(d)) w = op(o, w);
+      }
+      warp_tot[lane] = w;
+    }
+    __syncthreads();
+    const T before_warp = warp ? warp_tot[warp - 1] : Identity<Op>::get();
+    const T prev_lane = __shfl_up_sync(0xffffffffu, v, 1);
+    const T excl = lane ? op(before_warp, prev_lane) : before_warp;
+    *total = warp_tot[nwarps - 1];
+    __syncthreads();
+    return excl;
+  }
+
+  template <class T, class Op>
+  __device__ T scan_exclusive(T* a, uint32_t n, Op op) {
+    const uint32_t chunk = (n + blockDim.x - 1) / blockDim.x;
+    const uint32_t lo = min(n, threadIdx.x * chunk), hi = min(n, lo + chunk);
+    T acc = Identity<Op>::get();
+    for (uint32_t i = lo; i < hi; ++i) acc = op(acc, a[i]);
+    T total;
+    T run = block_scan(acc, op, &total);
+    for (uint32_t i = lo; i < hi; ++i) {
+      const T x = a[i];
+      a[i] = run;
+      run = op(run, x);
+    }
+    __syncthreads();
+    return total;
+  }
+
+  template <class T, class Op>
+  __device__ void scan_inclusive(T* a, uint32_t n, T init, Op op) {
+    const uint32_t chunk = (n + blockDim.x - 1) / blockDim.x;
+    const uint32_t lo = min(n, threadIdx.x * chunk), hi = min(n, lo + chunk);
+    T acc = Identity<Op>::get();
+    for (uint32_t i = lo; i < hi; ++i) acc = op(acc, a[i]);
+    T total;
+    T run = op(init, block_scan(acc, op, &total));
+    for (uint32_t i = lo; i < hi; ++i) a[i] = run = op(run, a[i]);
+    __syncthreads();
+  }
+};
+
+// Runs of feature f0 + blockIdx.x into runs[blockIdx.x * rows ...];
+// stats[blockIdx.x] = (runs, elements, nonmissing).
+__global__ void __launch_bounds__(kSketchThreads) sketch_runs_kernel(const float* __restrict__ X, uint32_t rows,
+                                                                     uint32_t cols, const float* __restrict__ weights,
+                                                                     uint32_t f0, Run* runs, uint32_t* stats) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ RunCarry carry;
+  __shared__ float last_w;
+  float* sv = reinterpret_cast<float*>(smem);
+  ChunkWork c{sv,
+              sv + kChunkRows,
+              reinterpret_cast<uint32_t*>(sv + 2 * kChunkRows),
+              reinterpret_cast<uint32_t*>(sv + 3 * kChunkRows),
+              reinterpret_cast<uint32_t*>(sv + 4 * kChunkRows),
+              reinterpret_cast<uint32_t*>(sv + 5 * kChunkRows),
+              reinterpret_cast<uint32_t*>(sv + 6 * kChunkRows),
+              &last_w};
+  const uint32_t f = f0 + blockIdx.x;
+  Run* out = runs + size_t(blockIdx.x) * rows;
+  if (threadIdx.x == 0) carry = RunCarry{0, 0, 0, 0, 0.0f, 0.0f};
+  __syncthreads();
+  DeviceExec ex;
+  for (uint32_t r0 = 0; r0 < rows; r0 += kChunkRows) {
+    const uint32_t n = min(kChunkRows, rows - r0);
+    runs_chunk(
+        ex,
+        [&](uint32_t i, float& v, float& w) {
+          v = X[size_t(r0 + i) * cols + f];
+          w = weights ? weights[r0 + i] : 1.0f;
+        },
+        n, weights == nullptr, carry, out, c);
+  }
+  if (threadIdx.x == 0) {
+    stats[3 * blockIdx.x] = carry.runs;
+    stats[3 * blockIdx.x + 1] = carry.elements;
+    stats[3 * blockIdx.x + 2] = carry.nonmissing;
+  }
+}
+
+// One batch: runs[run_begin, run_begin + size) of a feature, summarised into
+// `limit` entries at summaries[summary_at].
+struct BatchTask {
+  unsigned long long run_begin, summary_at;
+  uint32_t size, limit, size_slot, pad;
+};
+
+__global__ void __launch_bounds__(kSketchThreads) sketch_batch_kernel(const Run* runs, const BatchTask* tasks,
+                                                                      uint32_t ntasks, Entry* summaries,
+                                                                      uint32_t* sizes, unsigned char* scratch,
+                                                                      size_t scratch_stride, uint32_t cap) {
+  unsigned char* base = scratch + size_t(blockIdx.x) * scratch_stride;
+  const uint32_t p = pow2_ceil(cap);
+  BatchWork bw;
+  bw.keys = reinterpret_cast<unsigned long long*>(base);
+  bw.sorted = reinterpret_cast<Run*>(bw.keys + p);
+  bw.entries = reinterpret_cast<Entry*>(bw.sorted + cap);
+  bw.w.u = reinterpret_cast<uint32_t*>(bw.entries + cap);
+  bw.w.v = bw.w.u + cap + 2;
+  bw.w.f = reinterpret_cast<float*>(bw.w.v + cap + 2);
+  DeviceExec ex;
+  for (uint32_t t = blockIdx.x; t < ntasks; t += gridDim.x) {
+    const BatchTask task = tasks[t];
+    const uint32_t n = summarize_par(ex, runs + task.run_begin, task.size, task.limit, bw.keys, bw.sorted, bw.entries,
+                                     summaries + task.summary_at, bw.w);
+    if (threadIdx.x == 0) sizes[task.size_slot] = n;
+    __syncthreads();
+  }
+}
+
+struct ReduceTask {
+  unsigned long long summary_at, work_at;
+  uint32_t first_size, nbatch, limit, budget, levels, feature;
+};
+
+__global__ void __launch_bounds__(kSketchThreads) sketch_reduce_kernel(const Entry* summaries, const uint32_t* sizes,
+                                                                       const ReduceTask* tasks, unsigned char* work,
+                                                                       uint32_t max_bin, uint32_t stride, float* cuts,
+                                                                       uint32_t* counts) {
+  const ReduceTask t = tasks[blockIdx.x];
+  const uint32_t big = 2 * max(t.limit, t.budget) + 2;
+  unsigned char* base = work + t.work_at;
+  ReduceWork r;
+  r.resident = reinterpret_cast<Entry*>(base);
+  r.a = r.resident + size_t(t.limit) * t.levels;
+  r.b = r.a + big;
+  r.scratch = r.b + big;
+  r.w.u = reinterpret_cast<uint32_t*>(r.scratch + big);
+  r.w.v = r.w.u + big;
+  r.w.f = reinterpret_cast<float*>(r.w.v + big);
+  r.counts = reinterpret_cast<uint32_t*>(r.w.f + big);
+  r.size = r.counts + t.levels;
+  DeviceExec ex;
+  const uint32_t n = reduce_feature(ex, summaries + t.summary_at, sizes + t.first_size, t.nbatch, t.limit, t.budget,
+                                    t.levels, max_bin, r, cuts + size_t(t.feature) * stride);
+  if (threadIdx.x == 0) counts[t.feature] = n;
+}
+
+size_t reduce_work_bytes(uint32_t limit, uint32_t budget, uint32_t levels) {
+  const size_t big = 2 * size_t(std::max(limit, budget)) + 2;
+  const size_t bytes = (size_t(limit) * levels + 3 * big) * sizeof(Entry) + 3 * big * 4 + (size_t(levels) + 1) * 4;
+  return (bytes + 255) / 256 * 256;
+}
+
+struct Device {
+  void* p = nullptr;
+  size_t n = 0;
+  void need(size_t bytes) {
+    if (bytes <= n) return;
+    if (p) cudaFree(p);
+    p = nullptr;
+    n = 0;
+    XGBB_CUDA(cudaMalloc(&p, std::max<size_t>(bytes, 256)));
+    n = std::max<size_t>(bytes, 256);
+  }
+  ~Device() {
+    if (p) cudaFree(p);
+  }
+  template <class T>
+  T* as() const {
+    return static_cast<T*>(p);
+  }
+};
+
+}  // namespace
+
+void sketch_cuts_device(const float* X, uint32_t rows, uint32_t cols, const float* weights, uint32_t max_bin,
+                        float* cuts, uint32_t* counts, float* minima, cudaStream_t stream) {
+  const uint32_t stride = cut_stride(rows, max_bin);
+  std::fill(cuts, cuts + size_t(cols) * stride, 0.0f);
+  std::fill(counts, counts + cols, 0u);
+  std::fill(minima, minima + cols, -INFINITY);
+  if (!cols) return;
+  const size_t runs_smem = 7 * size_t(kChunkRows) * 4;
+  XGBB_CUDA(cudaFuncSetAttribute(sketch_runs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(runs_smem)));
+  int sms = 148, dev = 0;
+  XGBB_CUDA(cudaGetDevice(&dev));
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // Features per group: runs and batch summaries take about 16 bytes per row
+  // and feature; keep them within a quarter of the free memory.
+  size_t free_b = 0, total_b = 0;
+  XGBB_CUDA(cudaMemGetInfo(&free_b, &total_b));
+  const size_t per_feature = std::max<size_t>(size_t(rows) * 16, 1);
+  const uint32_t group = uint32_t(std::max<size_t>(1, std::min<size_t>(cols, free_b / 4 / per_feature)));
+  Device d_cuts, d_counts, d_runs, d_stats, d_summaries, d_sizes, d_tasks, d_scratch, d_rtasks, d_work;
+  d_cuts.need(size_t(cols) * stride * 4);
+  d_counts.need(size_t(cols) * 4);
+  XGBB_CUDA(cudaMemsetAsync(d_cuts.p, 0, size_t(cols) * stride * 4, stream));
+  std::vector<uint32_t> stats;
+  for (uint32_t f0 = 0; f0 < cols; f0 += group) {
+    const uint32_t nf = std::min(group, cols - f0);
+    d_runs.need(size_t(nf) * std::max(rows, 1u) * sizeof(Run));
+    d_stats.need(size_t(nf) * 3 * 4);
+    sketch_runs_kernel<<<nf, kSketchThreads, runs_smem, stream>>>(X, rows, cols, weights, f0, d_runs.as<Run>(),
+                                                                   d_stats.as<uint32_t>());
+    XGBB_CUDA(cudaGetLastError());
+    stats.assign(size_t(nf) * 3, 0);
+    XGBB_CUDA(cudaMemcpyAsync(stats.data(), d_stats.p, stats.size() * 4, cudaMemcpyDeviceToHost, stream));
+    XGBB_CUDA(cudaStreamSynchronize(stream));
+    // Plans: batch tasks, summary slots and reduction work per feature.
+    std::vector<BatchTask> tasks;
+    std::vector<ReduceTask> rtasks;
+    uint64_t summary_at = 0, work_at = 0;
+    uint32_t cap = 2, sizes_n = 0;
+    for (uint32_t j = 0; j < nf; ++j) {
+      const FeaturePlan p = plan_feature(max_bin, stats[3 * j], stats[3 * j + 1], stats[3 * j + 2]);
+      ReduceTask rt{summary_at, work_at, sizes_n, p.nbatch, p.limit, p.budget, p.levels, f0 + j};
+      for (uint32_t k = 0; k < p.nbatch; ++k) {
+        const uint64_t begin = uint64_t(k) * p.capacity;
+        const uint32_t size = uint32_t(std::min<uint64_t>(p.capacity, p.runs - begin));
+        tasks.push_back(BatchTask{uint64_t(j) * rows + begin, summary_at + uint64_t(k) * p.limit, size, p.limit,
+                                  sizes_n + k, 0});
+        cap = std::max(cap, size);
+      }
+      summary_at += uint64_t(std::max(p.nbatch, 1u)) * p.limit;
+      sizes_n += std::max(p.nbatch, 1u);
+      work_at += reduce_work_bytes(p.limit, p.budget, p.levels);
+      rtasks.push_back(rt);
+    }
+    d_summaries.need(size_t(summary_at) * sizeof(Entry));
+    d_sizes.need(size_t(sizes_n) * 4);
+    d_work.need(size_t(work_at));
+    if (!tasks.empty()) {
+      const uint32_t p2 = pow2_ceil(cap);
+      size_t scratch_stride = size_t(p2) * 8 + size_t(cap) * (sizeof(Run) + sizeof(Entry)) + 3 * (size_t(cap) + 2) * 4;
+      scratch_stride = (scratch_stride + 255) / 256 * 256;
+      const uint32_t grid = uint32_t(std::min<size_t>(tasks.size(), size_t(sms) * 2));
+      d_scratch.need(scratch_stride * grid);
+      d_tasks.need(tasks.size() * sizeof(BatchTask));
+      XGBB_CUDA(cudaMemcpyAsync(d_tasks.p, tasks.data(), tasks.size() * sizeof(BatchTask), cudaMemcpyHostToDevice,
+                                stream));
+      sketch_batch_kernel<<<grid, kSketchThreads, 0, stream>>>(d_runs.as<Run>(), d_tasks.as<BatchTask>(),
+                                                              uint32_t(tasks.size()), d_summaries.as<Entry>(),
+                                                              d_sizes.as<uint32_t>(), d_scratch.as<unsigned char>(),
+                                                              scratch_stride, cap);
+      XGBB_CUDA(cudaGetLastError());
+    }
+    d_rtasks.need(rtasks.size() * sizeof(ReduceTask));
+    XGBB_CUDA(cudaMemcpyAsync(d_rtasks.p, rtasks.data(), rtasks.size() * sizeof(ReduceTask), cudaMemcpyHostToDevice,
+                              stream));
+    sketch_reduce_kernel<<<nf, kSketchThreads, 0, stream>>>(d_summaries.as<Entry>(), d_sizes.as<uint32_t>(),
+                                                            d_rtasks.as<ReduceTask>(), d_work.as<unsigned char>(),
+                                                            max_bin, stride, d_cuts.as<float>(),
+                                                            d_counts.as<uint32_t>());
+    XGBB_CUDA(cudaGetLastError());
+    // The next group reuses the buffers.
+    XGBB_CUDA(cudaStreamSynchronize(stream));
+  }
+  XGBB_CUDA(cudaMemcpyAsync(cuts, d_cuts.p, size_t(cols) * stride * 4, cudaMemcpyDeviceToHost, stream));
+  XGBB_CUDA(cudaMemcpyAsync(counts, d_counts.p, size_t(cols) * 4, cudaMemcpyDeviceToHost, stream));
+  XGBB_CUDA(cudaStreamSynchronize(stream));
+}
+
+}  // namespace xgbb
