@@ -8,6 +8,7 @@
 
 #include "sketch_par.h"
 
+using namespace xgbb;
 using namespace xgbb::sketch;
 
 namespace {
@@ -76,6 +77,6 @@ extern "C" int sketch_harness(const float* X, uint32_t rows, uint32_t cols, cons
                                rw, cuts + size_t(f) * stride);
     minima[f] = -INFINITY;
   }
-  for (int k = 0; k < 3; ++k) serial[k] = ex.serial[k];
+  for (int k = 0; k < 3; ++k) serial[k] = ex.notes[k];
   return 0;
 }

@@ -1,0 +1,165 @@
+// Executors for block-structured algorithms: the same algorithm code runs as
+// a CUDA thread block (DeviceExec: each loop strided over the block's threads
+// with a barrier after it, block-wide scans, device atomics) and serially on
+// the host (HostExec), which is how the tests check the kernels' index and
+// scan logic on the CPU against the oracle.
+//
+// Contract for algorithm code: every executor call is reached by all threads
+// of the block (control flow depends only on values every thread reads after
+// a barrier), and a loop body touches no location another index of the same
+// loop writes, except through the atomic helpers.
+#pragma once
+#include <cmath>
+#include <cstdint>
+
+#if defined(__CUDACC__)
+#define XGBB_HD __host__ __device__
+#else
+#define XGBB_HD
+#endif
+
+namespace xgbb {
+
+// Associative combining operations with their identities.
+struct Add32 {
+  XGBB_HD uint32_t operator()(uint32_t a, uint32_t b) const { return a + b; }
+  XGBB_HD static uint32_t identity() { return 0u; }
+};
+struct MaxU32 {
+  XGBB_HD uint32_t operator()(uint32_t a, uint32_t b) const { return a > b ? a : b; }
+  XGBB_HD static uint32_t identity() { return 0u; }
+};
+// Addition saturating above 2^24 (associative on non-negative integers).
+struct SatAdd24 {
+  XGBB_HD uint32_t operator()(uint32_t a, uint32_t b) const {
+    const uint32_t s = a + b;
+    return (s > (1u << 24) + 1 || s < a) ? (1u << 24) + 1 : s;
+  }
+  XGBB_HD static uint32_t identity() { return 0u; }
+};
+// Right-biased maximum: b unless b < a. Associative, and a left fold of it
+// from `init` is the serial clamp `if (x < prev) x = prev; prev = x`.
+struct KeepMax {
+  XGBB_HD float operator()(float a, float b) const { return b < a ? a : b; }
+  XGBB_HD static float identity() { return -INFINITY; }
+};
+
+// Serial executor. `notes` counts algorithm-specific events (hand-overs to
+// serial forms) for the tests.
+struct HostExec {
+  uint64_t notes[8] = {};
+  void note(uint32_t kind) { ++notes[kind & 7]; }
+  template <class F>
+  void for_each(uint32_t n, F&& f) {
+    for (uint32_t i = 0; i < n; ++i) f(i);
+  }
+  template <class T, class Op>
+  T scan_exclusive(T* a, uint32_t n, Op op) {
+    T acc = Op::identity();
+    for (uint32_t i = 0; i < n; ++i) {
+      const T x = a[i];
+      a[i] = acc;
+      acc = op(acc, x);
+    }
+    return acc;
+  }
+  template <class T, class Op>
+  void scan_inclusive(T* a, uint32_t n, T init, Op op) {
+    T acc = init;
+    for (uint32_t i = 0; i < n; ++i) a[i] = acc = op(acc, a[i]);
+  }
+  void add_u64(unsigned long long* p, unsigned long long v) { *p += v; }
+  uint32_t add_u32(uint32_t* p, uint32_t v) {
+    const uint32_t old = *p;
+    *p = old + v;
+    return old;
+  }
+  uint32_t sub_u32(uint32_t* p, uint32_t v) {
+    const uint32_t old = *p;
+    *p = old - v;
+    return old;
+  }
+};
+
+#if defined(__CUDACC__)
+// Block executor: loop bodies strided over the block's threads with a
+// barrier after each loop; scans over arrays by contiguous per-thread chunks
+// and a warp-shuffle scan of the chunk totals, each operation applied left to
+// right.
+struct DeviceExec {
+  __device__ void note(uint32_t) {}
+
+  template <class F>
+  __device__ void for_each(uint32_t n, F&& f) {
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) f(i);
+    __syncthreads();
+  }
+
+  // Exclusive block scan of one value per thread; *total gets the fold of all.
+  template <class T, class Op>
+  __device__ T block_scan(T x, Op op, T* total) {
+    __shared__ unsigned long long warp_buf[32];
+    T* warp_tot = reinterpret_cast<T*>(warp_buf);
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = (blockDim.x + 31) >> 5;
+    T v = x;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const T o = __shfl_up_sync(0xffffffffu, v, d);
+      if (lane >= uint32_t(d)) v = op(o, v);
+    }
+    if (lane == 31) warp_tot[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+      T w = lane < nwarps ? warp_tot[lane] : Op::identity();
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const T o = __shfl_up_sync(0xffffffffu, w, d);
+        if (lane >= uint32_t(d)) w = op(o, w);
+      }
+      warp_tot[lane] = w;
+    }
+    __syncthreads();
+    const T before_warp = warp ? warp_tot[warp - 1] : Op::identity();
+    const T prev_lane = __shfl_up_sync(0xffffffffu, v, 1);
+    const T excl = lane ? op(before_warp, prev_lane) : before_warp;
+    *total = warp_tot[nwarps - 1];
+    __syncthreads();
+    return excl;
+  }
+
+  template <class T, class Op>
+  __device__ T scan_exclusive(T* a, uint32_t n, Op op) {
+    const uint32_t chunk = (n + blockDim.x - 1) / blockDim.x;
+    const uint32_t lo = min(n, threadIdx.x * chunk), hi = min(n, lo + chunk);
+    T acc = Op::identity();
+    for (uint32_t i = lo; i < hi; ++i) acc = op(acc, a[i]);
+    T total;
+    T run = block_scan(acc, op, &total);
+    for (uint32_t i = lo; i < hi; ++i) {
+      const T x = a[i];
+      a[i] = run;
+      run = op(run, x);
+    }
+    __syncthreads();
+    return total;
+  }
+
+  template <class T, class Op>
+  __device__ void scan_inclusive(T* a, uint32_t n, T init, Op op) {
+    const uint32_t chunk = (n + blockDim.x - 1) / blockDim.x;
+    const uint32_t lo = min(n, threadIdx.x * chunk), hi = min(n, lo + chunk);
+    T acc = Op::identity();
+    for (uint32_t i = lo; i < hi; ++i) acc = op(acc, a[i]);
+    T total;
+    T run = op(init, block_scan(acc, op, &total));
+    for (uint32_t i = lo; i < hi; ++i) a[i] = run = op(run, a[i]);
+    __syncthreads();
+  }
+
+  __device__ void add_u64(unsigned long long* p, unsigned long long v) { atomicAdd(p, v); }
+  __device__ uint32_t add_u32(uint32_t* p, uint32_t v) { return atomicAdd(p, v); }
+  __device__ uint32_t sub_u32(uint32_t* p, uint32_t v) { return atomicSub(p, v); }
+};
+#endif
+
+}  // namespace xgbb

@@ -18,6 +18,7 @@
 #include <vector>
 
 #include "common.h"
+#include "exec.h"
 #include "sketch.h"
 #include "sketch_par.h"
 
@@ -28,100 +29,6 @@ using namespace sketch;
 
 constexpr int kSketchThreads = 1024;
 constexpr uint32_t kChunkRows = 4096;
-
-template <class Op>
-struct Identity;
-template <>
-struct Identity<Add32> {
-  static __device__ uint32_t get() { return 0u; }
-};
-template <>
-struct Identity<SatAdd24> {
-  static __device__ uint32_t get() { return 0u; }
-};
-template <>
-struct Identity<MaxU32> {
-  static __device__ uint32_t get() { return 0u; }
-};
-template <>
-struct Identity<KeepMax> {
-  static __device__ float get() { return -INFINITY; }
-};
-
-// Block executor: loop bodies strided over the block's threads with a
-// barrier after each loop; scans over arrays by contiguous per-thread chunks
-// and a warp-shuffle scan of the chunk totals (the combining operations are
-// associative, and each is applied left to right).
-struct DeviceExec {
-  __device__ void note(SerialPath) {}
-
-  template <class F>
-  __device__ void for_each(uint32_t n, F&& f) {
-    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) f(i);
-    __syncthreads();
-  }
-
-  // Exclusive block scan of one value per thread; *total gets the fold of all.
-  template <class T, class Op>
-  __device__ T block_scan(T x, Op op, T* total) {
-    __shared__ unsigned long long warp_buf[32];
-    T* warp_tot = reinterpret_cast<T*>(warp_buf);
-    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = (blockDim.x + 31) >> 5;
-    T v = x;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const T o = __shfl_up_sync(0xffffffffu, v, d);
-      if (lane >= uint32_t(d)) v = op(o, v);
-    }
-    if (lane == 31) warp_tot[warp] = v;
-    __syncthreads();
-    if (warp == 0) {
-      T w = lane < nwarps ? warp_tot[lane] : Identity<Op>::get();
-#pragma unroll
-      for (int d = 1; d < 32; d <<= 1) {
-        const T o = __shfl_up_sync(0xffffffffu, w, d);
-        if (lane >= uint32_t(d)) w = op(o, w);
-      }
-      warp_tot[lane] = w;
-    }
-    __syncthreads();
-    const T before_warp = warp ? warp_tot[warp - 1] : Identity<Op>::get();
-    const T prev_lane = __shfl_up_sync(0xffffffffu, v, 1);
-    const T excl = lane ? op(before_warp, prev_lane) : before_warp;
-    *total = warp_tot[nwarps - 1];
-    __syncthreads();
-    return excl;
-  }
-
-  template <class T, class Op>
-  __device__ T scan_exclusive(T* a, uint32_t n, Op op) {
-    const uint32_t chunk = (n + blockDim.x - 1) / blockDim.x;
-    const uint32_t lo = min(n, threadIdx.x * chunk), hi = min(n, lo + chunk);
-    T acc = Identity<Op>::get();
-    for (uint32_t i = lo; i < hi; ++i) acc = op(acc, a[i]);
-    T total;
-    T run = block_scan(acc, op, &total);
-    for (uint32_t i = lo; i < hi; ++i) {
-      const T x = a[i];
-      a[i] = run;
-      run = op(run, x);
-    }
-    __syncthreads();
-    return total;
-  }
-
-  template <class T, class Op>
-  __device__ void scan_inclusive(T* a, uint32_t n, T init, Op op) {
-    const uint32_t chunk = (n + blockDim.x - 1) / blockDim.x;
-    const uint32_t lo = min(n, threadIdx.x * chunk), hi = min(n, lo + chunk);
-    T acc = Identity<Op>::get();
-    for (uint32_t i = lo; i < hi; ++i) acc = op(acc, a[i]);
-    T total;
-    T run = op(init, block_scan(acc, op, &total));
-    for (uint32_t i = lo; i < hi; ++i) a[i] = run = op(run, a[i]);
-    __syncthreads();
-  }
-};
 
 // Runs of feature f0 + blockIdx.x into runs[blockIdx.x * rows ...];
 // stats[blockIdx.x] = (runs, elements, nonmissing).

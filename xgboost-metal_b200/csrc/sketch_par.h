@@ -27,11 +27,7 @@
 #include <cstdint>
 #include <cstring>
 
-#if defined(__CUDACC__)
-#define XGBB_HD __host__ __device__
-#else
-#define XGBB_HD
-#endif
+#include "exec.h"
 
 namespace xgbb {
 namespace sketch {
@@ -219,25 +215,6 @@ XGBB_HD inline uint32_t select_cuts(const Entry* e, uint32_t size, uint32_t max_
 // Where a data-parallel form hands over to the serial definition (counted
 // by the test executor).
 enum SerialPath : uint32_t { kPruneSerial = 0, kCombineSerial = 1, kPrefixSerial = 2 };
-
-// Right-biased maximum: b unless b < a. Associative, and a left fold of it
-// from `init` is the serial clamp `if (x < prev) x = prev; prev = x`.
-struct KeepMax {
-  XGBB_HD float operator()(float a, float b) const { return b < a ? a : b; }
-};
-struct Add32 {
-  XGBB_HD uint32_t operator()(uint32_t a, uint32_t b) const { return a + b; }
-};
-struct MaxU32 {
-  XGBB_HD uint32_t operator()(uint32_t a, uint32_t b) const { return a > b ? a : b; }
-};
-// Addition saturating above 2^24 (associative on non-negative integers).
-struct SatAdd24 {
-  XGBB_HD uint32_t operator()(uint32_t a, uint32_t b) const {
-    const uint32_t s = a + b;
-    return (s > (1u << 24) + 1 || s < a) ? (1u << 24) + 1 : s;
-  }
-};
 
 // First index j in [lo, hi) with key(j) > x (hi when none), for
 // non-decreasing keys.
@@ -668,31 +645,6 @@ struct BatchWork {
   Run* sorted;               // [capacity]
   Entry* entries;            // [capacity]
   Work w;                    // capacity + 2 words each
-};
-
-// A plain executor: each loop runs serially, each barrier is a no-op.
-struct HostExec {
-  uint64_t serial[3] = {0, 0, 0};
-  void note(SerialPath p) { ++serial[p]; }
-  template <class F>
-  void for_each(uint32_t n, F&& f) {
-    for (uint32_t i = 0; i < n; ++i) f(i);
-  }
-  template <class T, class Op>
-  T scan_exclusive(T* a, uint32_t n, Op op) {
-    T acc = T(0);
-    for (uint32_t i = 0; i < n; ++i) {
-      const T x = a[i];
-      a[i] = acc;
-      acc = op(acc, x);
-    }
-    return acc;
-  }
-  template <class T, class Op>
-  void scan_inclusive(T* a, uint32_t n, T init, Op op) {
-    T acc = init;
-    for (uint32_t i = 0; i < n; ++i) a[i] = acc = op(acc, a[i]);
-  }
 };
 
 }  // namespace sketch
