@@ -31,6 +31,39 @@ struct EmuBackend : GrowerBackend {
   orc_tree_params tp;
   std::vector<uint32_t> order, scratch;
   uint64_t hist_mismatches = 0, evaluations = 0;
+  // Sparse rows (used when `sparse`): row_ptr [rows + 1], entries.
+  bool sparse = false;
+  std::vector<unsigned long long> row_ptr;
+  std::vector<uint32_t> entries;
+
+  template <class CodeT>
+  void make_sparse_rows() {
+    row_ptr.assign(size_t(e.rows) + 1, 0);
+    for (uint32_t r = 0; r < e.rows; ++r) row_ptr[r + 1] = row_ptr[r] + csr_row_count<CodeT>(e, r);
+    entries.assign(std::max<size_t>(row_ptr[e.rows], 1), 0);
+    for (uint32_t r = 0; r < e.rows; ++r) csr_row_fill<CodeT>(e, r, row_ptr[r], entries.data());
+  }
+
+  void build_sparse(const std::vector<Segment>& nodes, std::vector<longlong2>& built) {
+    const uint32_t n = uint32_t(nodes.size()), C = e.cols, B1 = e.bins + 1;
+    std::vector<uint32_t> seg(2 * n), tiles(n + 1);
+    uint32_t total = 0;
+    for (uint32_t s = 0; s < n; ++s) {
+      seg[2 * s] = nodes[s].begin;
+      seg[2 * s + 1] = nodes[s].count;
+      tiles[s] = total;
+      total += (nodes[s].count + kQueueTileRows - 1) / kQueueTileRows;
+    }
+    tiles[n] = total;
+    built.assign(size_t(C) * n * B1, longlong2{0, 0});
+    std::vector<unsigned long long> totals(2 * size_t(n), 0), tot(2);
+    HostExec ex;
+    for (uint32_t t = 0; t < total; ++t)
+      queue_hist_csr_tile(ex, e.bins, C, row_ptr.data(), entries.data(), order.data(), pairs, sc, seg.data(),
+                          tiles.data(), n, t, tot.data(), totals.data(), built.data());
+    for (uint32_t f = 0; f < C; ++f)
+      for (uint32_t s = 0; s < n; ++s) queue_fill_missing(e.bins, n, totals.data(), built.data(), f, s);
+  }
 
   template <class CodeT>
   void build(const std::vector<Segment>& nodes, std::vector<longlong2>& built) {
@@ -57,7 +90,8 @@ struct EmuBackend : GrowerBackend {
                 std::vector<DevSplit>& out) override {
     const uint32_t n = uint32_t(nodes.size()), C = e.cols, B = e.bins, B1 = B + 1;
     std::vector<longlong2> built;
-    if (e.bytes_per_code == 1) build<uint8_t>(nodes, built);
+    if (sparse) build_sparse(nodes, built);
+    else if (e.bytes_per_code == 1) build<uint8_t>(nodes, built);
     else build<uint16_t>(nodes, built);
     out.assign(n, DevSplit{});
     std::vector<int64_t> hist(size_t(C) * B1 * 2), want(hist.size());
@@ -144,13 +178,14 @@ struct EmuBackend : GrowerBackend {
 
 // ELLPACK codes are built from the oracle bins with the library's layout
 // rules (uint8 when every feature's codes, missing included, fit 256
-// symbols; `wide` forces uint16). margins[rows] start at `base` and receive
+// symbols; `wide` forces uint16); `sparse` builds the node histograms from
+// the rows' present codes. margins[rows] start at `base` and receive
 // the tree's leaves through the margin walk. stats[0] = histogram mismatches
 // against the oracle, stats[1] = evaluated nodes. Returns the node count.
 extern "C" int queue_harness(const uint32_t* bins, uint32_t rows, uint32_t cols, const int64_t* q, const float* pairs,
                              const float* scale, const float* cuts, uint32_t stride, const uint32_t* counts,
                              const float* minima, const orc_tree_params* tp, uint32_t lossguide, uint32_t max_leaves,
-                             int wide, float base, DevNode* nodes, uint32_t capacity, float* margins,
+                             int wide, int sparse, float base, DevNode* nodes, uint32_t capacity, float* margins,
                              uint64_t* stats) {
   try {
     uint32_t max_count = 0;
@@ -189,6 +224,11 @@ extern "C" int queue_harness(const uint32_t* bins, uint32_t rows, uint32_t cols,
     be.counts = counts;
     be.minima = minima;
     be.tp = *tp;
+    be.sparse = sparse != 0;
+    if (be.sparse) {
+      if (narrow) be.make_sparse_rows<uint8_t>();
+      else be.make_sparse_rows<uint16_t>();
+    }
     be.order.resize(rows);
     be.scratch.resize(rows);
     for (uint32_t r = 0; r < rows; ++r) be.order[r] = r;

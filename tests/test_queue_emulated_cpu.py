@@ -1,5 +1,6 @@
 """Host-driven trees with the GPU backend's block functions
-(csrc/queue_par.h: node histograms, row partitions, the margin walk) run on
+(csrc/queue_par.h: node histograms dense or from sparse rows, row
+partitions, the margin walk) run on
 the CPU by the serial executor (csrc/exec.h HostExec), split evaluation by
 the oracle: every histogram equals the oracle's for the same rows, and the
 trees and margins equal the oracle's host-driven grower. Covers uint8 and
@@ -50,7 +51,7 @@ def _inputs(seed, rows=6000, cols=6, max_bin=32, nan=0.1):
     return bins, q, pairs, scale, cuts, counts, minima
 
 
-def _run(lib, inputs, params, lossguide=False, max_leaves=0, wide=False):
+def _run(lib, inputs, params, lossguide=False, max_leaves=0, wide=False, sparse=False):
     bins, q, pairs, scale, cuts, counts, minima = inputs
     rows, cols = bins.shape
     cap = 2 * rows + 1
@@ -67,16 +68,17 @@ def _run(lib, inputs, params, lossguide=False, max_leaves=0, wide=False):
     scale = np.ascontiguousarray(scale, np.float32)
     n = lib.queue_harness(p(bins), u32(rows), u32(cols), p(q), p(pairs), p(scale), p(cuts), u32(cuts.shape[1]),
                           p(counts), p(minima), ctypes.byref(tp), u32(int(lossguide)), u32(max_leaves),
-                          ctypes.c_int(int(wide)), ctypes.c_float(0.25), p(nodes), u32(cap), p(margins), p(stats))
+                          ctypes.c_int(int(wide)), ctypes.c_int(int(sparse)), ctypes.c_float(0.25), p(nodes),
+                          u32(cap), p(margins), p(stats))
     assert n > 0, n
     return nodes[:n], margins, stats
 
 
-def _check(lib, inputs, params, lossguide=False, max_leaves=0, wide=False):
+def _check(lib, inputs, params, lossguide=False, max_leaves=0, wide=False, sparse=False):
     bins, q, pairs, scale, cuts, counts, minima = inputs
     want, leaf = C.grow_tree_queue(bins, q, scale, cuts, counts, minima, params, lossguide=lossguide,
                                    max_leaves=max_leaves)
-    got, margins, stats = _run(lib, inputs, params, lossguide, max_leaves, wide)
+    got, margins, stats = _run(lib, inputs, params, lossguide, max_leaves, wide, sparse)
     assert stats[0] == 0 and stats[1] > 0, stats
     assert len(got) == len(want)
     for f in ("left", "right", "feature", "parent"):
@@ -117,3 +119,18 @@ def test_missing_code_conventions(harness):
 def test_wide_batches_and_regularisation(harness):
     inputs = _inputs(6, rows=30000, cols=5, max_bin=64, nan=0.02)
     _check(harness, inputs, dict(BASE, max_depth=11, min_child_weight=0.0, reg_alpha=0.3, max_delta_step=0.5))
+
+
+@pytest.mark.parametrize("wide", [False, True])
+def test_sparse_row_histograms(harness, wide):
+    # Mostly missing values: each node histogram from the rows' present codes
+    # and its missing bin from the node total.
+    inputs = _inputs(7, rows=12000, cols=20, max_bin=64, nan=0.9)
+    _check(harness, inputs, dict(BASE, max_depth=9), sparse=True, wide=wide)
+    _check(harness, inputs, dict(BASE, max_depth=0), lossguide=True, max_leaves=25, sparse=True, wide=wide)
+
+
+def test_sparse_rows_without_missing_values(harness):
+    # Every code present (uint8 with 256 bins and no missing value).
+    inputs = _inputs(8, rows=6000, cols=3, max_bin=256, nan=0.0)
+    _check(harness, inputs, dict(BASE, max_depth=12), sparse=True)

@@ -93,3 +93,14 @@ def test_python_api_predictions_follow_the_training_margins():
         raw = bst.save_raw("json")
         again = xgb.Booster(model_file=bytearray(raw))
         np.testing.assert_array_equal(bits(again.predict(xgb.DMatrix(X))), bits(bst.predict(xgb.DMatrix(X))))
+
+
+def test_sparse_row_histograms():
+    # cuda_sparse_hist=1: node histograms from each row's present values,
+    # missing bins from the node totals; the trees are the oracle's.
+    X, y = _data(20000, 30, 0.9, 38)
+    _run(X, y, dict(max_depth=6, cuda_sparse_hist=1, max_bin=64), 3)
+    _run(X, y, dict(grow_policy="lossguide", max_depth=0, max_leaves=40, cuda_sparse_hist=1), 2)
+    rng = np.random.default_rng(6)
+    Xc = rng.normal(size=(8000, 5)).astype(np.float32)  # no missing values
+    _run(Xc, Xc[:, 0] * 2 + Xc[:, 1], dict(max_depth=5, cuda_sparse_hist=1), 2)

@@ -25,6 +25,10 @@ struct Add32 {
   XGBB_HD uint32_t operator()(uint32_t a, uint32_t b) const { return a + b; }
   XGBB_HD static uint32_t identity() { return 0u; }
 };
+struct Add64 {
+  XGBB_HD unsigned long long operator()(unsigned long long a, unsigned long long b) const { return a + b; }
+  XGBB_HD static unsigned long long identity() { return 0ull; }
+};
 struct MaxU32 {
   XGBB_HD uint32_t operator()(uint32_t a, uint32_t b) const { return a > b ? a : b; }
   XGBB_HD static uint32_t identity() { return 0u; }

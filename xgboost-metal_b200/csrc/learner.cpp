@@ -185,6 +185,9 @@ void DMatrix::set_cuts(std::shared_ptr<Cuts> c, cudaStream_t stream) {
     }
   }
   ell.codes = codes.get();
+  sparse_ready = false;
+  sparse_ptr.release();
+  sparse_entries.release();
   // A feature-major copy lets the partition read a node's split feature from
   // a dense column; it is made when it leaves a quarter of the device free.
   codes_fm.release();
@@ -200,6 +203,18 @@ void DMatrix::set_cuts(std::shared_ptr<Cuts> c, cudaStream_t stream) {
     }
   }
   cuts = std::move(c);
+}
+
+void DMatrix::build_sparse_rows(cudaStream_t stream) {
+  if (sparse_ready) return;
+  sparse_ptr.resize((size_t(rows) + 1) * 8);
+  DeviceBuffer tile_sums((size_t(rows) / 4096 + 1) * 8);
+  const uint64_t nnz =
+      queue_csr_row_ptr(ell, sparse_ptr.as<unsigned long long>(), tile_sums.as<unsigned long long>(), stream);
+  sparse_entries.resize(std::max<size_t>(nnz, 1) * 4);
+  queue_csr_fill(ell, sparse_ptr.as<unsigned long long>(), sparse_entries.as<uint32_t>(), stream);
+  XGBB_CUDA(cudaStreamSynchronize(stream));
+  sparse_ready = true;
 }
 
 void DMatrix::quantise(uint32_t mb, const DMatrix* ref, cudaStream_t stream, int threads) {
@@ -282,7 +297,8 @@ struct Booster::TrainState {
   // Host-driven trees (loss-guided, leaf budgets, depth > 10): row order and
   // its partition scratch, node histograms and candidates of one batch, the
   // batch descriptors, and pinned landing buffers for the host's reads.
-  DeviceBuffer q_order, q_scratch, q_built, q_cand, q_keys, q_sums, q_seg, q_items, q_cursor, q_best, q_nodes;
+  DeviceBuffer q_order, q_scratch, q_built, q_cand, q_keys, q_sums, q_seg, q_items, q_cursor, q_best, q_nodes,
+      q_totals;
   uint32_t q_slots = 0;
   NodeBest* q_best_host = nullptr;   // pinned [kMaxFrontier]
   uint32_t* q_cursor_host = nullptr; // pinned [2 * kQueueBatch]
@@ -574,7 +590,11 @@ void Booster::configure() {
   tp_.max_depth = uint32_t(std::min<long>(max_depth, INT32_MAX));
   lossguide_ = policy == "lossguide";
   max_leaves_ = uint32_t(max_leaves);
-  host_driven_ = lossguide_ || max_leaves_ || tp_.max_depth == 0 || tp_.max_depth > kMaxDepth;
+  // cuda_sparse_hist=1: node histograms from each row's present values (the
+  // reference's CSR histograms, kernels/histogram_csr.metal.h), on the
+  // host-driven path; the trees are the same.
+  sparse_hist_ = integer(params_, "cuda_sparse_hist", 0) != 0;
+  host_driven_ = lossguide_ || max_leaves_ || tp_.max_depth == 0 || tp_.max_depth > kMaxDepth || sparse_hist_;
   tp_.eta = number(params_, "learning_rate", 0.3f);
   tp_.reg_lambda = number(params_, "reg_lambda", 1.0f);
   tp_.reg_alpha = number(params_, "reg_alpha", 0.0f);
@@ -746,6 +766,8 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp, bo
     ts->q_items.resize((6 * size_t(kQueueBatch) + 1) * 4);
     ts->q_cursor.resize(2 * size_t(kQueueBatch) * 4);
     ts->q_best.resize(kMaxFrontier * sizeof(NodeBest));
+    ts->q_totals.resize(size_t(ts->q_slots) * 16);
+    if (sparse_hist_) d.build_sparse_rows(stream_);
     XGBB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ts->q_best_host), kMaxFrontier * sizeof(NodeBest)));
     XGBB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ts->q_cursor_host), 2 * size_t(kQueueBatch) * 4));
     XGBB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ts->q_up_host), kQueueUpWords * 4));
@@ -928,6 +950,10 @@ struct QueueDevice {
   uint32_t* up_host;      // pinned [kQueueUpWords]
   long long* sums_host;   // pinned [kMaxFrontier][2]
   uint32_t slots;       // node capacity of one evaluation
+  // Sparse rows (null for dense histograms) and per-node totals.
+  const unsigned long long* sparse_ptr;
+  const uint32_t* sparse_entries;
+  unsigned long long* node_totals;  // [slots][2]
   cudaEvent_t done;
   cudaStream_t stream;
   int hist_blocks, eval_blocks, part_blocks;
@@ -960,8 +986,12 @@ class DeviceGrower final : public GrowerBackend {
       std::copy(sums.begin(), sums.end(), q_.sums_host);
       XGBB_CUDA(cudaMemcpyAsync(q_.sums, q_.sums_host, sums.size() * 8, cudaMemcpyHostToDevice, q_.stream));
     }
-    launch_queue_hist(q_.e, q_.order, q_.pairs, q_.scale, q_.seg, q_.seg + 2 * size_t(n), n, tiles, q_.built,
-                      q_.hist_blocks, q_.stream);
+    if (q_.sparse_ptr)
+      launch_queue_hist_csr(q_.e, q_.sparse_ptr, q_.sparse_entries, q_.order, q_.pairs, q_.scale, q_.seg,
+                            q_.seg + 2 * size_t(n), n, tiles, q_.node_totals, q_.built, q_.hist_blocks, q_.stream);
+    else
+      launch_queue_hist(q_.e, q_.order, q_.pairs, q_.scale, q_.seg, q_.seg + 2 * size_t(n), n, tiles, q_.built,
+                        q_.hist_blocks, q_.stream);
     Comm::get().sum_u64(q_.built, size_t(q_.e.cols) * n * (q_.e.bins + 1) * 2, q_.stream);
     queue_evaluate(q_.e, q_.tp, q_.scale, q_.state, n, root, q_.built, q_.sums, q_.cand, q_.keys, q_.best,
                    q_.eval_blocks, q_.stream);
@@ -1221,6 +1251,9 @@ void Booster::grow_host_driven(TrainState& ts) {
   q.up_host = ts.q_up_host;
   q.sums_host = ts.q_sums_host;
   q.slots = ts.q_slots;
+  q.sparse_ptr = sparse_hist_ ? d.sparse_ptr.as<unsigned long long>() : nullptr;
+  q.sparse_entries = sparse_hist_ ? d.sparse_entries.as<uint32_t>() : nullptr;
+  q.node_totals = ts.q_totals.as<unsigned long long>();
   q.done = ts.q_done;
   q.stream = stream_;
   q.hist_blocks = sms * 8;

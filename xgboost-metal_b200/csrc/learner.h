@@ -84,6 +84,11 @@ class DMatrix {
   bool quantised() const { return bool(cuts) && (codes || rows == 0); }
   void quantise(uint32_t max_bin, const DMatrix* ref, cudaStream_t stream, int threads);
   void set_cuts(std::shared_ptr<Cuts> c, cudaStream_t stream);
+  // Sparse rows of the codes (present codes only, feature << 16 | code),
+  // made on first use for sparse node histograms.
+  DeviceBuffer sparse_ptr, sparse_entries;
+  bool sparse_ready = false;
+  void build_sparse_rows(cudaStream_t stream);
 
   // Device copies on demand.
   DeviceBuffer d_data, d_labels, d_weights;
@@ -189,7 +194,7 @@ class Booster {
   TreeParams tp_{};
   // Trees the level-synchronous device driver does not grow (loss-guided,
   // leaf budgets, depth 0 or above 10) grow host-driven (grower.h).
-  bool host_driven_ = false, lossguide_ = false;
+  bool host_driven_ = false, lossguide_ = false, sparse_hist_ = false;
   uint32_t max_leaves_ = 0;
   float spw_ = 1.0f;
   std::vector<float> base_score_, base_margin_;

@@ -137,6 +137,81 @@ XGBB_HD void queue_partition_tile(Ex& ex, const Ellpack& e, const uint32_t* orde
   });
 }
 
+// ---------------------------------------------------------------------------
+// Sparse rows (kernels/histogram_csr.metal.h:22-152 in the reference): each
+// row's present codes as (feature << 16 | code) entries in feature order,
+// row_ptr[r] .. row_ptr[r + 1]. A node histogram then costs work in
+// proportion to the present values; each node's exact total is summed
+// alongside, and its missing bin is the total minus the present bins.
+// ---------------------------------------------------------------------------
+template <class CodeT>
+XGBB_HD inline uint32_t csr_row_count(const Ellpack& e, uint32_t r) {
+  uint32_t n = 0;
+  for (uint32_t f = 0; f < e.cols; ++f) n += code_at<CodeT>(e, r, f) != e.missing;
+  return n;
+}
+
+template <class CodeT>
+XGBB_HD inline void csr_row_fill(const Ellpack& e, uint32_t r, unsigned long long at, uint32_t* entries) {
+  for (uint32_t f = 0; f < e.cols; ++f) {
+    const uint32_t code = code_at<CodeT>(e, r, f);
+    if (code != e.missing) entries[at++] = (f << 16) | code;
+  }
+}
+
+// Tile t of the sparse histograms of `slots` nodes (segments and tiles as
+// for queue_hist_item): every present entry of the tile's rows is added to
+// built[feature][slot][code]; tot[2] (block scratch) collects the rows'
+// exact (g, h) sums, added to node_totals[slot][2] once per tile.
+template <class Ex>
+XGBB_HD void queue_hist_csr_tile(Ex& ex, uint32_t bins, uint32_t cols, const unsigned long long* row_ptr,
+                                 const uint32_t* entries, const uint32_t* order, const float2* pairs, float2 sc,
+                                 const uint32_t* seg, const uint32_t* tiles, uint32_t slots, uint32_t t,
+                                 unsigned long long* tot, unsigned long long* node_totals, longlong2* built) {
+  const uint32_t B1 = bins + 1;
+  const uint32_t s = owner_of(tiles, slots, t);
+  const uint32_t begin = seg[2 * s] + (t - tiles[s]) * kQueueTileRows;
+  const uint32_t seg_end = seg[2 * s] + seg[2 * s + 1];
+  const uint32_t end = seg_end < begin + kQueueTileRows ? seg_end : begin + kQueueTileRows;
+  ex.for_each(1, [&](uint32_t) {
+    tot[0] = 0;
+    tot[1] = 0;
+  });
+  ex.for_each(end - begin, [&](uint32_t i) {
+    const uint32_t row = order[begin + i];
+    const float2 p = pairs[row];
+    const unsigned long long qg = (unsigned long long)quantize_value(p.x, sc.x);
+    const unsigned long long qh = (unsigned long long)quantize_value(p.y, sc.y);
+    ex.add_u64(&tot[0], qg);
+    ex.add_u64(&tot[1], qh);
+    for (unsigned long long k = row_ptr[row]; k < row_ptr[row + 1]; ++k) {
+      const uint32_t f = entries[k] >> 16, code = entries[k] & 0xffffu;
+      if (f >= cols || code >= bins) continue;
+      longlong2* dst = built + (size_t(f) * slots + s) * B1 + code;
+      ex.add_u64(reinterpret_cast<unsigned long long*>(&dst->x), qg);
+      ex.add_u64(reinterpret_cast<unsigned long long*>(&dst->y), qh);
+    }
+  });
+  ex.for_each(1, [&](uint32_t) {
+    ex.add_u64(&node_totals[2 * s], tot[0]);
+    ex.add_u64(&node_totals[2 * s + 1], tot[1]);
+  });
+}
+
+// The missing bin of (feature f, slot s): the node total minus the present
+// bins, mod 2^64.
+XGBB_HD inline void queue_fill_missing(uint32_t bins, uint32_t slots, const unsigned long long* node_totals,
+                                       longlong2* built, uint32_t f, uint32_t s) {
+  longlong2* h = built + (size_t(f) * slots + s) * (bins + 1);
+  unsigned long long g = node_totals[2 * s], hh = node_totals[2 * s + 1];
+  for (uint32_t b = 0; b < bins; ++b) {
+    g -= (unsigned long long)h[b].x;
+    hh -= (unsigned long long)h[b].y;
+  }
+  h[bins].x = (long long)g;
+  h[bins].y = (long long)hh;
+}
+
 // margins[row][group] += the leaf `row` reaches in `nodes`, walking its
 // codes (at most node_count steps).
 template <class CodeT>

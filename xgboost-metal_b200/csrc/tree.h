@@ -196,6 +196,18 @@ constexpr uint32_t kQueuePartRows = 1024;
 void launch_queue_partition(const Ellpack& e, uint32_t* order, uint32_t* scratch, const uint32_t* items,
                             const uint32_t* tiles, uint32_t nitems, uint32_t total_tiles, uint32_t* cursor,
                             int blocks, cudaStream_t stream);
+// Sparse rows of the ELLPACK codes: row_ptr [rows + 1] (returns the entry
+// count after a stream synchronisation; tile_sums holds one word per 4096
+// rows), then entries [nnz] = feature << 16 | code in feature order.
+uint64_t queue_csr_row_ptr(const Ellpack& e, unsigned long long* row_ptr, unsigned long long* tile_sums,
+                           cudaStream_t stream);
+void queue_csr_fill(const Ellpack& e, const unsigned long long* row_ptr, uint32_t* entries, cudaStream_t stream);
+// Node histograms from the sparse rows: work per present value; each node's
+// missing bin is its total (node_totals [slots][2]) minus its present bins.
+void launch_queue_hist_csr(const Ellpack& e, const unsigned long long* row_ptr, const uint32_t* entries,
+                           const uint32_t* order, const float2* pairs, const float2* scale, const uint32_t* seg,
+                           const uint32_t* tiles, uint32_t slots, uint32_t total_tiles,
+                           unsigned long long* node_totals, longlong2* built, int blocks, cudaStream_t stream);
 // margins[row][group] += the leaf each row reaches in `nodes`, walking the
 // quantised codes.
 void launch_queue_margins(const Ellpack& e, const DevNode* nodes, uint32_t node_count, float* margins,
