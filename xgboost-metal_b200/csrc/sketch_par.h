@@ -108,7 +108,9 @@ XGBB_HD inline uint32_t prune_serial(Entry* e, uint32_t size, uint32_t capacity)
 }
 
 // Merges `other` (m entries) into `cur` (n entries, room for n + m); scratch
-// holds n + m entries. Returns the merged size.
+// holds n + m entries. Returns the merged size. Each merged entry's ranks are
+// clamped to be non-decreasing as it is produced: rmin to the running rmin,
+// rmax to the running rmax and to rmin + wmin.
 XGBB_HD inline uint32_t combine_serial(Entry* cur, uint32_t n, const Entry* other, uint32_t m, Entry* scratch) {
   if (!m) return n;
   if (!n) {
@@ -116,50 +118,43 @@ XGBB_HD inline uint32_t combine_serial(Entry* cur, uint32_t n, const Entry* othe
     return m;
   }
   uint32_t a = 0, b = 0, count = 0;
-  float prev_a = 0, prev_b = 0;
-  while (a < n && b < m) {
-    const Entry x = cur[a], y = other[b];
-    Entry r;
-    if (x.value == y.value) {
-      r = {x.rmin + y.rmin, x.rmax + y.rmax, x.wmin + y.wmin, x.value};
-      prev_a = lower_next(x);
-      prev_b = lower_next(y);
-      ++a;
-      ++b;
-    } else if (x.value < y.value) {
-      r = {x.rmin + prev_b, x.rmax + upper_prev(y), x.wmin, x.value};
-      prev_a = lower_next(x);
-      ++a;
-    } else {
-      r = {y.rmin + prev_a, y.rmax + upper_prev(x), y.wmin, y.value};
-      prev_b = lower_next(y);
-      ++b;
-    }
-    scratch[count++] = r;
-  }
-  const float tail_a = cur[n - 1].rmax, tail_b = other[m - 1].rmax;
-  while (a < n) {
-    Entry x = cur[a++];
-    x.rmin = x.rmin + prev_b;
-    x.rmax = x.rmax + tail_b;
-    scratch[count++] = x;
-  }
-  while (b < m) {
-    Entry y = other[b++];
-    y.rmin = y.rmin + prev_a;
-    y.rmax = y.rmax + tail_a;
-    scratch[count++] = y;
-  }
-  float prev_min = 0, prev_max = 0;
-  for (uint32_t i = 0; i < count; ++i) {
-    Entry e = scratch[i];
+  float prev_a = 0, prev_b = 0, prev_min = 0, prev_max = 0;
+  auto emit = [&](Entry e) {
     if (e.rmin < prev_min) e.rmin = prev_min;
     else prev_min = e.rmin;
     if (e.rmax < prev_max) e.rmax = prev_max;
     if (e.rmax < lower_next(e)) e.rmax = lower_next(e);
     prev_max = e.rmax;
-    cur[i] = e;
+    scratch[count++] = e;
+  };
+  while (a < n && b < m) {
+    const Entry x = cur[a], y = other[b];
+    if (x.value == y.value) {
+      emit({x.rmin + y.rmin, x.rmax + y.rmax, x.wmin + y.wmin, x.value});
+      prev_a = lower_next(x);
+      prev_b = lower_next(y);
+      ++a;
+      ++b;
+    } else if (x.value < y.value) {
+      emit({x.rmin + prev_b, x.rmax + upper_prev(y), x.wmin, x.value});
+      prev_a = lower_next(x);
+      ++a;
+    } else {
+      emit({y.rmin + prev_a, y.rmax + upper_prev(x), y.wmin, y.value});
+      prev_b = lower_next(y);
+      ++b;
+    }
   }
+  const float tail_a = cur[n - 1].rmax, tail_b = other[m - 1].rmax;
+  while (a < n) {
+    const Entry x = cur[a++];
+    emit({x.rmin + prev_b, x.rmax + tail_b, x.wmin, x.value});
+  }
+  while (b < m) {
+    const Entry y = other[b++];
+    emit({y.rmin + prev_a, y.rmax + tail_a, y.wmin, y.value});
+  }
+  for (uint32_t i = 0; i < count; ++i) cur[i] = scratch[i];
   return count;
 }
 
