@@ -36,34 +36,52 @@ using sketch::Run;
 // Stable sort of runs by value: an LSD radix sort on order-preserving keys
 // (the sign bit flipped for positives, all bits for negatives), which orders
 // every non-NaN float as `<` does (-0 never occurs: it is read as +0) and
-// keeps equal values in their input order, as std::stable_sort would. Passes
-// in which every key has the same digit are skipped.
-using sketch::order_key;
-void sort_runs(Run* a, size_t n, std::vector<Run>& tmp, std::vector<uint32_t>& keys,
-               std::vector<uint32_t>& keys_tmp) {
+// keeps equal values in their input order, as std::stable_sort would. Each
+// run travels as one 64-bit word, key above weight; the three digit
+// histograms (11, 11 and 10 bits) come from one counting pass, and a pass in
+// which every key has the same digit is skipped.
+inline float key_value(uint32_t k) {
+  const uint32_t b = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  float v;
+  std::memcpy(&v, &b, 4);
+  return v;
+}
+void sort_runs(Run* a, size_t n, std::vector<uint64_t>& buf, std::vector<uint64_t>& tmp) {
   if (n < 2) return;
+  buf.resize(n);
   tmp.resize(n);
-  keys.resize(n);
-  keys_tmp.resize(n);
-  for (size_t i = 0; i < n; ++i) keys[i] = order_key(a[i].v);
-  Run* src = a;
-  Run* dst = tmp.data();
-  uint32_t* ks = keys.data();
-  uint32_t* kd = keys_tmp.data();
-  for (int shift = 0; shift < 32; shift += 8) {
-    uint32_t hist[257] = {0};
-    for (size_t i = 0; i < n; ++i) ++hist[((ks[i] >> shift) & 0xffu) + 1];
-    if (hist[((ks[0] >> shift) & 0xffu) + 1] == n) continue;  // one digit: order unchanged
-    for (int d = 0; d < 256; ++d) hist[d + 1] += hist[d];
-    for (size_t i = 0; i < n; ++i) {
-      const uint32_t pos = hist[(ks[i] >> shift) & 0xffu]++;
-      dst[pos] = src[i];
-      kd[pos] = ks[i];
-    }
-    std::swap(src, dst);
-    std::swap(ks, kd);
+  static constexpr int kShift[3] = {0, 11, 22};
+  static constexpr uint32_t kMask[3] = {0x7ffu, 0x7ffu, 0x3ffu};
+  uint32_t hist[3][2048] = {};
+  for (size_t i = 0; i < n; ++i) {
+    const uint32_t k = sketch::order_key(a[i].v);
+    buf[i] = (uint64_t(k) << 32) | sketch::float_bits(a[i].w);
+    ++hist[0][k & 0x7ffu];
+    ++hist[1][(k >> 11) & 0x7ffu];
+    ++hist[2][k >> 22];
   }
-  if (src != a) std::copy(src, src + n, a);
+  uint64_t* src = buf.data();
+  uint64_t* dst = tmp.data();
+  for (int p = 0; p < 3; ++p) {
+    uint32_t* h = hist[p];
+    const int shift = 32 + kShift[p];
+    const uint32_t mask = kMask[p];
+    if (h[(src[0] >> shift) & mask] == n) continue;  // one digit: order unchanged
+    uint32_t sum = 0;
+    for (uint32_t d = 0; d <= mask; ++d) {
+      const uint32_t c = h[d];
+      h[d] = sum;
+      sum += c;
+    }
+    for (size_t i = 0; i < n; ++i) dst[h[(src[i] >> shift) & mask]++] = src[i];
+    std::swap(src, dst);
+  }
+  for (size_t i = 0; i < n; ++i) {
+    const uint32_t wb = uint32_t(src[i]);
+    float w;
+    std::memcpy(&w, &wb, 4);
+    a[i] = Run{key_value(uint32_t(src[i] >> 32)), w};
+  }
 }
 
 // One feature's cuts from its column `col` (contiguous, `rows` values).
@@ -103,15 +121,14 @@ void one_feature(const float* col, uint32_t rows, const float* weights, uint32_t
   std::vector<Entry> resident(size_t(limit) * levels), current(2 * size_t(limit) + 1),
       scratch(2 * size_t(limit) + 1), summary(capacity + 1);
   uint32_t counts[64] = {0};
-  std::vector<Run> sort_tmp;
-  std::vector<uint32_t> sort_keys, sort_keys_tmp;
+  std::vector<uint64_t> sort_buf, sort_tmp;
   const auto prune = sketch::prune_serial;
   const auto combine = sketch::combine_serial;
   for (uint32_t batch = 0; batch < nbatch; ++batch) {
     const uint64_t begin = batch * capacity;
     const uint32_t size = uint32_t(std::min<uint64_t>(capacity, nruns - begin));
     Run* src = runs.data() + begin;
-    sort_runs(src, size, sort_tmp, sort_keys, sort_keys_tmp);
+    sort_runs(src, size, sort_buf, sort_tmp);
     uint32_t n = 0;
     float total = 0;
     for (uint32_t i = 0; i < size;) {
