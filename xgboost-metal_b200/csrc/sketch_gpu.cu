@@ -69,26 +69,11 @@ __global__ void __launch_bounds__(kSketchThreads) sketch_runs_kernel(const float
   }
 }
 
-// One batch: runs[run_begin, run_begin + size) of a feature, summarised into
-// `limit` entries at summaries[summary_at].
-struct BatchTask {
-  unsigned long long run_begin, summary_at;
-  uint32_t size, limit, size_slot, pad;
-};
-
 __global__ void __launch_bounds__(kSketchThreads) sketch_batch_kernel(const Run* runs, const BatchTask* tasks,
                                                                       uint32_t ntasks, Entry* summaries,
                                                                       uint32_t* sizes, unsigned char* scratch,
                                                                       size_t scratch_stride, uint32_t cap) {
-  unsigned char* base = scratch + size_t(blockIdx.x) * scratch_stride;
-  const uint32_t p = pow2_ceil(cap);
-  BatchWork bw;
-  bw.keys = reinterpret_cast<unsigned long long*>(base);
-  bw.sorted = reinterpret_cast<Run*>(bw.keys + p);
-  bw.entries = reinterpret_cast<Entry*>(bw.sorted + cap);
-  bw.w.u = reinterpret_cast<uint32_t*>(bw.entries + cap);
-  bw.w.v = bw.w.u + cap + 2;
-  bw.w.f = reinterpret_cast<float*>(bw.w.v + cap + 2);
+  const BatchWork bw = batch_work_at(scratch + size_t(blockIdx.x) * scratch_stride, cap);
   DeviceExec ex;
   for (uint32_t t = blockIdx.x; t < ntasks; t += gridDim.x) {
     const BatchTask task = tasks[t];
@@ -99,38 +84,16 @@ __global__ void __launch_bounds__(kSketchThreads) sketch_batch_kernel(const Run*
   }
 }
 
-struct ReduceTask {
-  unsigned long long summary_at, work_at;
-  uint32_t first_size, nbatch, limit, budget, levels, feature;
-};
-
 __global__ void __launch_bounds__(kSketchThreads) sketch_reduce_kernel(const Entry* summaries, const uint32_t* sizes,
                                                                        const ReduceTask* tasks, unsigned char* work,
                                                                        uint32_t max_bin, uint32_t stride, float* cuts,
                                                                        uint32_t* counts) {
   const ReduceTask t = tasks[blockIdx.x];
-  const uint32_t big = 2 * max(t.limit, t.budget) + 2;
-  unsigned char* base = work + t.work_at;
-  ReduceWork r;
-  r.resident = reinterpret_cast<Entry*>(base);
-  r.a = r.resident + size_t(t.limit) * t.levels;
-  r.b = r.a + big;
-  r.scratch = r.b + big;
-  r.w.u = reinterpret_cast<uint32_t*>(r.scratch + big);
-  r.w.v = r.w.u + big;
-  r.w.f = reinterpret_cast<float*>(r.w.v + big);
-  r.counts = reinterpret_cast<uint32_t*>(r.w.f + big);
-  r.size = r.counts + t.levels;
+  const ReduceWork r = reduce_work_at(work + t.work_at, t.limit, t.budget, t.levels);
   DeviceExec ex;
   const uint32_t n = reduce_feature(ex, summaries + t.summary_at, sizes + t.first_size, t.nbatch, t.limit, t.budget,
                                     t.levels, max_bin, r, cuts + size_t(t.feature) * stride);
   if (threadIdx.x == 0) counts[t.feature] = n;
-}
-
-size_t reduce_work_bytes(uint32_t limit, uint32_t budget, uint32_t levels) {
-  const size_t big = 2 * size_t(std::max(limit, budget)) + 2;
-  const size_t bytes = (size_t(limit) * levels + 3 * big) * sizeof(Entry) + 3 * big * 4 + (size_t(levels) + 1) * 4;
-  return (bytes + 255) / 256 * 256;
 }
 
 struct Device {
@@ -188,33 +151,16 @@ void sketch_cuts_device(const float* X, uint32_t rows, uint32_t cols, const floa
     stats.assign(size_t(nf) * 3, 0);
     XGBB_CUDA(cudaMemcpyAsync(stats.data(), d_stats.p, stats.size() * 4, cudaMemcpyDeviceToHost, stream));
     XGBB_CUDA(cudaStreamSynchronize(stream));
-    // Plans: batch tasks, summary slots and reduction work per feature.
-    std::vector<BatchTask> tasks;
-    std::vector<ReduceTask> rtasks;
-    uint64_t summary_at = 0, work_at = 0;
-    uint32_t cap = 2, sizes_n = 0;
-    for (uint32_t j = 0; j < nf; ++j) {
-      const FeaturePlan p = plan_feature(max_bin, stats[3 * j], stats[3 * j + 1], stats[3 * j + 2]);
-      ReduceTask rt{summary_at, work_at, sizes_n, p.nbatch, p.limit, p.budget, p.levels, f0 + j};
-      for (uint32_t k = 0; k < p.nbatch; ++k) {
-        const uint64_t begin = uint64_t(k) * p.capacity;
-        const uint32_t size = uint32_t(std::min<uint64_t>(p.capacity, p.runs - begin));
-        tasks.push_back(BatchTask{uint64_t(j) * rows + begin, summary_at + uint64_t(k) * p.limit, size, p.limit,
-                                  sizes_n + k, 0});
-        cap = std::max(cap, size);
-      }
-      summary_at += uint64_t(std::max(p.nbatch, 1u)) * p.limit;
-      sizes_n += std::max(p.nbatch, 1u);
-      work_at += reduce_work_bytes(p.limit, p.budget, p.levels);
-      rtasks.push_back(rt);
-    }
+    const GroupPlan plan = plan_group(stats.data(), nf, f0, rows, max_bin);
+    const std::vector<BatchTask>& tasks = plan.tasks;
+    const std::vector<ReduceTask>& rtasks = plan.reduce;
+    const uint64_t summary_at = plan.summary_entries, work_at = plan.work_bytes;
+    const uint32_t cap = plan.cap, sizes_n = plan.sizes;
     d_summaries.need(size_t(summary_at) * sizeof(Entry));
     d_sizes.need(size_t(sizes_n) * 4);
     d_work.need(size_t(work_at));
     if (!tasks.empty()) {
-      const uint32_t p2 = pow2_ceil(cap);
-      size_t scratch_stride = size_t(p2) * 8 + size_t(cap) * (sizeof(Run) + sizeof(Entry)) + 3 * (size_t(cap) + 2) * 4;
-      scratch_stride = (scratch_stride + 255) / 256 * 256;
+      const size_t scratch_stride = batch_scratch_bytes(cap);
       const uint32_t grid = uint32_t(std::min<size_t>(tasks.size(), size_t(sms) * 2));
       d_scratch.need(scratch_stride * grid);
       d_tasks.need(tasks.size() * sizeof(BatchTask));

@@ -26,6 +26,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <vector>
 
 #include "exec.h"
 
@@ -641,6 +642,90 @@ struct BatchWork {
   Entry* entries;            // [capacity]
   Work w;                    // capacity + 2 words each
 };
+
+// ---------------------------------------------------------------------------
+// The GPU sketch's plan for a group of features and the layouts of its
+// scratch (sketch_gpu.cu), shared with the tests.
+// ---------------------------------------------------------------------------
+
+// One batch: runs[run_begin, run_begin + size) of a feature, summarised into
+// `limit` entries at summaries[summary_at]; its size lands in sizes[size_slot].
+struct BatchTask {
+  unsigned long long run_begin, summary_at;
+  uint32_t size, limit, size_slot, pad;
+};
+// One feature's reduction: its batch summaries from summaries[summary_at]
+// (sizes from sizes[first_size]) and its work area at work + work_at.
+struct ReduceTask {
+  unsigned long long summary_at, work_at;
+  uint32_t first_size, nbatch, limit, budget, levels, feature;
+};
+
+inline size_t reduce_work_bytes(uint32_t limit, uint32_t budget, uint32_t levels) {
+  const size_t big = 2 * size_t(limit > budget ? limit : budget) + 2;
+  const size_t bytes = (size_t(limit) * levels + 3 * big) * sizeof(Entry) + 3 * big * 4 + (size_t(levels) + 1) * 4;
+  return (bytes + 255) / 256 * 256;
+}
+
+XGBB_HD inline ReduceWork reduce_work_at(unsigned char* base, uint32_t limit, uint32_t budget, uint32_t levels) {
+  const uint32_t big = 2 * (limit > budget ? limit : budget) + 2;
+  ReduceWork r;
+  r.resident = reinterpret_cast<Entry*>(base);
+  r.a = r.resident + size_t(limit) * levels;
+  r.b = r.a + big;
+  r.scratch = r.b + big;
+  r.w.u = reinterpret_cast<uint32_t*>(r.scratch + big);
+  r.w.v = r.w.u + big;
+  r.w.f = reinterpret_cast<float*>(r.w.v + big);
+  r.counts = reinterpret_cast<uint32_t*>(r.w.f + big);
+  r.size = r.counts + levels;
+  return r;
+}
+
+// Bytes of one batch's scratch for batches of at most `cap` runs.
+inline size_t batch_scratch_bytes(uint32_t cap) {
+  const size_t bytes = size_t(pow2_ceil(cap)) * 8 + size_t(cap) * (sizeof(Run) + sizeof(Entry)) + 3 * (size_t(cap) + 2) * 4;
+  return (bytes + 255) / 256 * 256;
+}
+
+XGBB_HD inline BatchWork batch_work_at(unsigned char* base, uint32_t cap) {
+  BatchWork bw;
+  bw.keys = reinterpret_cast<unsigned long long*>(base);
+  bw.sorted = reinterpret_cast<Run*>(bw.keys + pow2_ceil(cap));
+  bw.entries = reinterpret_cast<Entry*>(bw.sorted + cap);
+  bw.w.u = reinterpret_cast<uint32_t*>(bw.entries + cap);
+  bw.w.v = bw.w.u + cap + 2;
+  bw.w.f = reinterpret_cast<float*>(bw.w.v + cap + 2);
+  return bw;
+}
+
+// Tasks of `nf` features (feature f0 + j has its runs at runs[j * rows]) from
+// their (runs, elements, nonmissing) statistics.
+struct GroupPlan {
+  std::vector<BatchTask> tasks;
+  std::vector<ReduceTask> reduce;
+  uint64_t summary_entries = 0, work_bytes = 0;
+  uint32_t sizes = 0, cap = 2;
+};
+inline GroupPlan plan_group(const uint32_t* stats, uint32_t nf, uint32_t f0, uint32_t rows, uint32_t max_bin) {
+  GroupPlan g;
+  for (uint32_t j = 0; j < nf; ++j) {
+    const FeaturePlan p = plan_feature(max_bin, stats[3 * j], stats[3 * j + 1], stats[3 * j + 2]);
+    g.reduce.push_back(ReduceTask{g.summary_entries, g.work_bytes, g.sizes, p.nbatch, p.limit, p.budget, p.levels,
+                                  f0 + j});
+    for (uint32_t k = 0; k < p.nbatch; ++k) {
+      const uint64_t begin = uint64_t(k) * p.capacity;
+      const uint32_t size = uint32_t(p.runs - begin < p.capacity ? p.runs - begin : p.capacity);
+      g.tasks.push_back(BatchTask{uint64_t(j) * rows + begin, g.summary_entries + uint64_t(k) * p.limit, size,
+                                  p.limit, g.sizes + k, 0});
+      if (size > g.cap) g.cap = size;
+    }
+    g.summary_entries += uint64_t(p.nbatch > 1 ? p.nbatch : 1u) * p.limit;
+    g.sizes += p.nbatch > 1 ? p.nbatch : 1u;
+    g.work_bytes += reduce_work_bytes(p.limit, p.budget, p.levels);
+  }
+  return g;
+}
 
 }  // namespace sketch
 }  // namespace xgbb
