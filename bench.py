@@ -220,6 +220,14 @@ class Dist:
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
 
+    def gather_bytes(self, data):
+        """Every rank's bytes on rank 0, in rank order (None elsewhere)."""
+        if not self.pg:
+            return [data]
+        box = [None] * self.world if self.rank == 0 else None
+        self.pg.gather_object(data, box, dst=0)
+        return box
+
     def bcast(self, obj):
         if not self.pg:
             return obj
@@ -236,12 +244,32 @@ def shard(rows, rank, world):
     return rows * rank // world, rows * (rank + 1) // world
 
 
+def parity_digest(bst, dtrain, dist, next_round):
+    """SHA-256 of every tree of the booster (node arrays of the model JSON)
+    and of the root level's int64 (g, h) histogram words of one more round,
+    the feature ranges of all ranks joined in rank order. Both are the same
+    at every GPU count when training is bit-exact."""
+    import hashlib
+
+    import product as P
+    trees = json.loads(bst.save_raw("json"))["learner"]["gradient_booster"]["model"]["trees"]
+    model = hashlib.sha256(json.dumps(trees, sort_keys=True).encode()).hexdigest()
+    P.capture_level_histograms(bst, 0)
+    bst.update(dtrain, next_round)
+    meta, hist, _ = P.level_histograms(bst)
+    parts = dist.gather_bytes(np.ascontiguousarray(hist).tobytes())
+    return {"model_sha256": model, "trees": len(trees),
+            "root_hist_sha256": hashlib.sha256(b"".join(parts)).hexdigest() if parts else None,
+            "root_hist_words": int(hist.size) * dist.world if parts else None,
+            "note": "trees after warm-up + timed rounds; root histogram of the round after them"}
+
+
 def launches_per_round(depth, groups):
-    # gradients, window, scales, exact, exact scales; per tree: init, root
-    # limbs, 5 per level (three-limb and staged histogram kernels, one of
-    # which exits at once; evaluation, control, partition), 2 per non-last
-    # level (counts, plan).
-    return 5 + groups * (2 + 5 * depth + 2 * (depth - 1))
+    # gradients, window, scales, exact, exact scales; per tree: init, 5 per
+    # level (three-limb and staged histogram kernels, one of which exits at
+    # once; evaluation, control, partition), 2 per non-last level (counts,
+    # plan).
+    return 5 + groups * (1 + 5 * depth + 2 * (depth - 1))
 
 
 # ---------------------------------------------------------------------------
@@ -450,6 +478,7 @@ def main():
         core.synchronize()
     dev_ms = dist.max(dev_ms)
     prof = bst.cuda_profile()
+    parity = parity_digest(bst, dtrain, dist, W + K)
     value = dev_ms * 100.0 / K
 
     peak, peak_kind = measured_peak()
@@ -458,7 +487,7 @@ def main():
     roofline = {"bound": "hbm", "achieved": round(hist_gbs, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(hist_gbs / peak, 4), "peak_kind": peak_kind,
                 "traffic": traffic["dram_bytes_per_launch"] if traffic else None,
-                "kernel": "hist_kernel",
+                "kernel": "hist2_kernel",
                 "algorithmic_bytes_per_launch": prof["hist_bytes"] / max(prof["hist_launches"], 1),
                 "avg_launch_ms": prof["hist_ms"] / max(prof["hist_launches"], 1),
                 "launches": prof["hist_launches"],
@@ -494,6 +523,7 @@ def main():
                 "h2d_bytes_per_step": int(x_bytes / K), "d2h_bytes_per_step": node_table,
                 "note": "xgb.train(QuantileDMatrix/DMatrix from pinned host arrays) for K rounds, "
                         "wall clock, max over ranks; H2D of the matrix amortised over K rounds"},
+        "parity": parity,
         "gpu_launches": launches_per_round(spec["max_depth"], groups) * K,
         "clocks": clocks.summary(),
     }

@@ -25,6 +25,18 @@ XGB_DLL int XGDMatrixQuantise(DMatrixHandle handle, int max_bin, DMatrixHandle r
 XGB_DLL int XGBoosterGetCudaProfile(BoosterHandle handle, char const** out);
 /* Clears the counters of XGBoosterGetCudaProfile. */
 XGB_DLL int XGBoosterResetCudaProfile(BoosterHandle handle);
+/* Asks the next boosting round to keep the built int64 histograms of level
+ * `depth` (0 = root) of its first tree; -1 cancels. That tree runs without
+ * its CUDA graph. The words kept are the ones the reference's histogram
+ * kernels write (kernels/boost.metal:700-733, histogram_missing.metal.h:13-60):
+ * one (g, h) pair per (built node, feature, bin), bin B the missing bin. */
+XGB_DLL int XGBoosterCaptureLevelHistograms(BoosterHandle handle, int depth);
+/* The captured level: meta = JSON {"depth", "pairs", "f_lo", "f_hi", "bins1"};
+ * hist = [pairs][f_hi - f_lo][bins1][2] int64 (this rank's features, summed
+ * over every rank's rows); node_ids[pairs] = the node each histogram belongs
+ * to. Valid until the next call on this thread. */
+XGB_DLL int XGBoosterGetLevelHistograms(BoosterHandle handle, char const** meta, int64_t const** hist,
+                                        uint32_t const** node_ids);
 /* Records CUDA event `slot` (0..63) on the booster's stream, and the device
  * time between two recorded events; used to time whole rounds. */
 XGB_DLL int XGBoosterRecordEvent(BoosterHandle handle, int slot);
@@ -86,7 +98,9 @@ XGB_DLL int XGBBGradientsHost(int objective, const float* margins, const float* 
  * Calls that can overlap on one device (different streams or unordered host
  * threads) race on the shared array; calls on one stream are safe. The first
  * call on each device looks up the array's address (cudaGetSymbolAddress) and
- * should come before any stream capture on that device. */
+ * should come before any stream capture on that device; after a device reset
+ * (cudaDeviceReset) the first call looks it up again in the new context, and
+ * that call too should come before any capture. */
 XGB_DLL int XGBBGradientsDeviceNoAlloc(int objective, const float* margins, const float* labels,
                                        const float* weights, bst_ulong rows, uint32_t groups,
                                        float scale_pos_weight, float* pairs, float* scales,

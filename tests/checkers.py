@@ -272,3 +272,28 @@ def oracle_gradients(objective, margins, labels, weights=None, scale_pos_weight=
                       _ptr(None if weights is None else np.ascontiguousarray(weights, np.float32)),
                       _U32(rows), _U32(groups), _F(scale_pos_weight), _ptr(pairs))
     return pairs
+
+
+def oracle_histogram(bins, q, rows, stride):
+    """orc_histogram: exact int64 (g, h) sums [cols][stride + 1][2] of the rows
+    `rows` (uint32 ids) of the row-major bins, the missing bin last."""
+    bins = np.ascontiguousarray(bins, np.uint32)
+    q = np.ascontiguousarray(q, np.int64)
+    rows = np.ascontiguousarray(rows, np.uint32)
+    cols = bins.shape[1]
+    hist = np.zeros((cols, stride + 1, 2), np.int64)
+    oracle()._l.lib.orc_histogram(_ptr(bins), _U32(cols), _U32(stride), _ptr(q), _ptr(rows),
+                                  _U32(len(rows)), _ptr(hist))
+    return hist
+
+
+def oracle_base_margin(objective, labels, weights=None, groups=1, scale_pos_weight=1.0):
+    """orc_base_score: the intercept as margins [groups]."""
+    labels = np.ascontiguousarray(labels, np.float32)
+    score = np.zeros(groups, np.float32)
+    margin = np.zeros(groups, np.float32)
+    oracle()._l.lib.orc_base_score(ctypes.c_int(OBJECTIVES[objective]), _ptr(labels),
+                                   _ptr(None if weights is None else np.ascontiguousarray(weights, np.float32)),
+                                   _U32(len(labels)), _U32(groups), _F(scale_pos_weight), _ptr(score),
+                                   _ptr(margin))
+    return margin

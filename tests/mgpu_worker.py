@@ -1,6 +1,7 @@
 """One rank of the row-sharded training check (launched by test_multi_gpu.py
-under torch.distributed.run, one process per GPU): trains on its contiguous
-row shard with cuts from the full matrix and writes the full-matrix margins."""
+under torch.distributed.run, one process per GPU): quantises and trains on its
+contiguous row shard only (the cuts cover every rank's rows) and writes the
+full-matrix margins."""
 import json
 import os
 import sys
@@ -73,8 +74,12 @@ def main():
                         timeout=15.0 if mode == "leave" else None)
     X, y = data(objective, cols)
     lo, hi = len(y) * rank // world, len(y) * (rank + 1) // world
-    ref = xgb.QuantileDMatrix(X, max_bin=64)
-    shard = xgb.QuantileDMatrix(X[lo:hi], label=y[lo:hi], ref=ref, max_bin=64)
+    # Every rank quantises only its own rows: the cuts come from the rows of
+    # all ranks (assembled over NCCL), so they equal the single-GPU cuts.
+    if mode == "lazy":
+        shard = xgb.DMatrix(X[lo:hi], label=y[lo:hi])
+    else:
+        shard = xgb.QuantileDMatrix(X[lo:hi], label=y[lo:hi], max_bin=64)
     params = {"objective": objective, "max_depth": 6, "eta": 0.3, "max_bin": 64,
               "device": "cuda", "tree_method": "hist",
               "cuda_graph": int(os.environ.get("XGBB_WORKER_GRAPH", "1"))}

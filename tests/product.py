@@ -115,3 +115,26 @@ def sketch(X, max_bin, weights=None, threads=0):
                                ctypes.c_uint32(max_bin), ctypes.c_int(threads), _ptr(cuts),
                                _ptr(counts), _ptr(minima)))
     return cuts, counts, minima
+
+
+def capture_level_histograms(booster, depth):
+    """Ask the booster's next round to keep the built histograms of level
+    `depth` of its first tree (XGBoosterCaptureLevelHistograms)."""
+    check(lib().XGBoosterCaptureLevelHistograms(booster.handle, ctypes.c_int(depth)))
+
+
+def level_histograms(booster):
+    """The captured level: (meta dict, hist int64 [pairs][features][bins + 1][2],
+    node id of each built histogram)."""
+    meta = ctypes.c_char_p()
+    hist = ctypes.POINTER(ctypes.c_int64)()
+    ids = ctypes.POINTER(ctypes.c_uint32)()
+    check(lib().XGBoosterGetLevelHistograms(booster.handle, ctypes.byref(meta), ctypes.byref(hist),
+                                            ctypes.byref(ids)))
+    m = json.loads(meta.value.decode())
+    nf = m["f_hi"] - m["f_lo"]
+    n = m["pairs"] * nf * m["bins1"] * 2
+    h = np.ctypeslib.as_array(hist, shape=(n,)).copy() if n else np.zeros(0, np.int64)
+    node_ids = (np.ctypeslib.as_array(ids, shape=(m["pairs"],)).copy() if m["pairs"]
+                else np.zeros(0, np.uint32))
+    return m, h.reshape(m["pairs"], nf, m["bins1"], 2), node_ids

@@ -221,3 +221,46 @@ def test_two_limb_unit_hessian_u8_matches_oracle():
     trees_p, margins_p = P.train(X, y, {k: v for k, v in params.items() if k != "num_class"}, 3)
     assert_same_trees(trees_p, trees_o)
     np.testing.assert_array_equal(bits(margins_p), bits(margins_o))
+
+
+def _c3_like(rows, cols, classes, seed):
+    """Integer-valued images in the manner of BASELINE's c3: per class a
+    pattern P[k] of uniform(0, 255) intensities; a cell is zero where its
+    class pattern plus per-row noise falls below the class's 80th percentile
+    (so classes overlap and trees grow), else clip(Poisson(P[k]), 0, 255);
+    balanced shuffled classes."""
+    rng = np.random.default_rng(seed)
+    P = rng.uniform(0, 255, size=(classes, cols)).astype(np.float32)
+    thr = np.quantile(P, 0.8, axis=1, keepdims=True)
+    y = rng.permutation(np.arange(rows) % classes)
+    X = np.clip(rng.poisson(P[y]), 0, 255).astype(np.float32)
+    X[P[y] + rng.normal(0, 60, size=X.shape) < thr[y]] = 0.0
+    return X, y.astype(np.float32)
+
+
+def test_c3_shape_softprob_784_features_10_classes_matches_oracle():
+    """BASELINE's c3 shape: 784 features (25 feature groups of 32, the last
+    partial), 10 classes (10 trees per round), ~80 % exact zeros, integer
+    values with at most 256 distinct values per feature (exact cuts, uint8
+    codes, no missing bin)."""
+    X, y = _c3_like(24000, 784, 10, seed=31)
+    assert (X == 0).mean() > 0.75
+    params = C.train_params(dict(objective="multi:softprob", num_class=10, max_depth=6, eta=0.3))
+    trees_o, margins_o, _ = C.oracle_train(X, y, params, 2)
+    trees_p, margins_p = P.train(X, y, params, 2)
+    assert len(trees_p) == 20
+    assert_same_trees(trees_p, trees_o)
+    np.testing.assert_array_equal(bits(margins_p), bits(margins_o))
+
+
+def test_c4_width_logistic_128_features_matches_oracle():
+    """BASELINE's c4 row format at 128 features: 256 bins plus missing
+    (uint16 codes), 5 % NaN, binary:logistic, depth 10, 2 rounds."""
+    X, _ = _data(60000, 128, 0.05, seed=33)
+    rng = np.random.default_rng(34)
+    y = (rng.random(60000) < 0.35).astype(np.float32)
+    params = C.train_params(dict(objective="binary:logistic", max_depth=10, eta=0.1))
+    trees_o, margins_o, _ = C.oracle_train(X, y, params, 2)
+    trees_p, margins_p = P.train(X, y, {k: v for k, v in params.items() if k != "num_class"}, 2)
+    assert_same_trees(trees_p, trees_o)
+    np.testing.assert_array_equal(bits(margins_p), bits(margins_o))

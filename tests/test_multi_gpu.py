@@ -24,17 +24,22 @@ def gpu_count():
 
 
 @pytest.mark.skipif(gpu_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("objective,cols", [("reg:squarederror", 12), ("binary:logistic", 13)])
-def test_two_ranks_match_the_oracle(tmp_path, objective, cols):
-    """13 features over 2 ranks: the padded feature of the reduce-scatter
-    layout and an uneven split of the split search."""
+@pytest.mark.parametrize("objective,cols,mode,port", [("reg:squarederror", 12, "train", 29533),
+                                                      ("binary:logistic", 13, "train", 29541),
+                                                      ("binary:logistic", 12, "lazy", 29543)])
+def test_two_ranks_match_the_oracle(tmp_path, objective, cols, mode, port):
+    """Each rank holds and quantises only its rows; the cuts of all ranks'
+    rows are computed on every GPU, so the model equals the single-GPU model.
+    13 features over 2 ranks: the padded feature of the reduce-scatter
+    layout and an uneven split of the split search. "lazy": a plain DMatrix
+    quantised at the first round, also over all ranks' rows."""
     sys.path.insert(0, HERE)
     import mgpu_worker
     # One node: NCCL's bootstrap sockets on loopback, no NVLink multicast.
     env = dict(os.environ, MASTER_ADDR="127.0.0.1", NCCL_NVLS_ENABLE="0", NCCL_SOCKET_IFNAME="lo")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr=127.0.0.1", "--master-port=29533",
-           os.path.join(HERE, "mgpu_worker.py"), str(tmp_path), objective, str(cols)]
+           "--master-addr=127.0.0.1", "--master-port=%d" % port,
+           os.path.join(HERE, "mgpu_worker.py"), str(tmp_path), objective, str(cols), mode]
     proc = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=420)
     assert proc.returncode == 0, proc.stderr[-3000:]
     X, y = mgpu_worker.data(objective, cols)

@@ -1008,6 +1008,31 @@ XGB_DLL int XGBoosterEventElapsed(BoosterHandle handle, int a, int b, float* ms)
   return guarded([&] { *ms = booster(handle).elapsed_ms(a, b); });
 }
 
+XGB_DLL int XGBoosterCaptureLevelHistograms(BoosterHandle handle, int depth) {
+  return guarded([&] {
+    auto& b = booster(handle);
+    xgbb::require(depth >= -1 && depth < int(xgbb::kMaxDepth), "capture depth out of range");
+    b.capture = xgbb::Booster::LevelCapture{};
+    b.capture.depth = depth;
+  });
+}
+
+XGB_DLL int XGBoosterGetLevelHistograms(BoosterHandle handle, char const** meta, int64_t const** hist,
+                                        uint32_t const** node_ids) {
+  return guarded([&] {
+    auto& b = booster(handle);
+    b.sync();
+    const auto& c = b.capture;
+    xgbb::require(c.ready, "no level histograms were captured (request one, then train a round)");
+    results.str = "{\"depth\":" + std::to_string(c.depth) + ",\"pairs\":" + std::to_string(c.pairs) +
+                  ",\"f_lo\":" + std::to_string(c.f_lo) + ",\"f_hi\":" + std::to_string(c.f_hi) +
+                  ",\"bins1\":" + std::to_string(c.bins1) + "}";
+    *meta = results.str.c_str();
+    *hist = reinterpret_cast<const int64_t*>(c.hist.data());
+    *node_ids = c.node_ids.data();
+  });
+}
+
 XGB_DLL int XGBoosterResetCudaProfile(BoosterHandle handle) {
   return guarded([&] {
     booster(handle).finish_pending();  // a pending round belongs to the counts being cleared

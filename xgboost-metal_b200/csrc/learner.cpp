@@ -217,14 +217,84 @@ void DMatrix::build_sparse_rows(cudaStream_t stream) {
   sparse_ready = true;
 }
 
+namespace {
+// Cuts of the rows of every rank of a row-sharded job, identical on every
+// rank and bit for bit the cuts one GPU holding all rows would compute. Each
+// rank's rows (and weights, 1 where a rank has none) are assembled in rank
+// order on every GPU with one NCCL broadcast per rank, and the GPU sketch
+// runs over all of them; NVLink moves the whole matrix in a few tens of
+// milliseconds, and the assembled copy is freed afterwards.
+void sketch_all_ranks(DMatrix& d, uint32_t mb, Cuts& c, cudaStream_t stream) {
+  Comm& comm = Comm::get();
+  const int world = comm.world(), rank = comm.rank();
+  // Row counts and weight flags of every rank.
+  DeviceBuffer mine(16), all(size_t(world) * 16);
+  const uint64_t info[2] = {d.rows, d.weights.empty() ? 0u : 1u};
+  XGBB_CUDA(cudaMemcpyAsync(mine.get(), info, 16, cudaMemcpyHostToDevice, stream));
+  comm.all_gather(mine.get(), all.get(), 16, stream);
+  std::vector<uint64_t> got(size_t(world) * 2);
+  XGBB_CUDA(cudaMemcpyAsync(got.data(), all.get(), got.size() * 8, cudaMemcpyDeviceToHost, stream));
+  cudaEvent_t ev;
+  XGBB_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+  XGBB_CUDA(cudaEventRecord(ev, stream));
+  comm.wait(ev, "the row counts of every rank");
+  std::vector<uint64_t> off(size_t(world) + 1, 0);
+  bool weighted = false;
+  for (int r = 0; r < world; ++r) {
+    off[r + 1] = off[r] + got[2 * r];
+    weighted = weighted || got[2 * r + 1];
+  }
+  const uint64_t total = off[world];
+  require(total <= 0xffffffffull, "more than 2^32 - 1 rows over all ranks");
+  c.stride = cut_stride(uint32_t(total), mb);
+  c.values.assign(size_t(d.cols) * c.stride, 0.0f);
+  const size_t row_bytes = size_t(d.cols) * sizeof(float);
+  DeviceBuffer X(std::max<size_t>(total * row_bytes, 16)), W;
+  if (d.rows) {
+    XGBB_CUDA(cudaMemcpyAsync(X.as<char>() + off[rank] * row_bytes, d.device_data(stream), d.rows * row_bytes,
+                              cudaMemcpyDeviceToDevice, stream));
+  }
+  if (weighted) {
+    W.resize(std::max<size_t>(total * 4, 16));
+    std::vector<float> w = d.weights.empty() ? std::vector<float>(d.rows, 1.0f) : d.weights;
+    if (d.rows)
+      XGBB_CUDA(cudaMemcpyAsync(W.as<float>() + off[rank], w.data(), d.rows * 4, cudaMemcpyHostToDevice, stream));
+    XGBB_CUDA(cudaStreamSynchronize(stream));  // `w` leaves scope
+  }
+  for (int r = 0; r < world; ++r) {
+    const uint64_t n = off[r + 1] - off[r];
+    if (!n) continue;
+    comm.broadcast(X.as<char>() + off[r] * row_bytes, n * row_bytes, r, stream);
+    if (weighted) comm.broadcast(W.as<float>() + off[r], n * 4, r, stream);
+  }
+  XGBB_CUDA(cudaEventRecord(ev, stream));
+  comm.wait(ev, "the rows of every rank");
+  cudaEventDestroy(ev);
+  if (total && d.cols)
+    sketch_cuts_device(X.as<float>(), uint32_t(total), d.cols, weighted ? W.as<float>() : nullptr, mb,
+                       c.values.data(), c.counts.data(), c.minima.data(), stream);
+}
+}  // namespace
+
 void DMatrix::quantise(uint32_t mb, const DMatrix* ref, cudaStream_t stream, int threads) {
   if (quantised() && max_bin == mb) return;
   require(mb >= 2, "max_bin must be at least 2.");
   require(mb <= kMaxBins, "max_bin above 256 is not supported by the CUDA histogram kernels.");
   std::shared_ptr<Cuts> c;
+  const bool uploaded = bool(d_data);
   if (ref) {
     require(ref->cuts && ref->max_bin == mb, "Quantile reference does not match max_bin.");
     c = ref->cuts;
+  } else if (Comm::get().active()) {
+    // Rows are split over the ranks of a multi-GPU job (every rank quantises
+    // its matrix together): the cuts cover all ranks' rows.
+    c = std::make_shared<Cuts>();
+    c->cols = cols;
+    c->max_bin = mb;
+    c->counts.assign(cols, 0);
+    c->minima.assign(cols, -INFINITY);
+    sketch_all_ranks(*this, mb, *c, stream);
+    c->upload();
   } else {
     c = std::make_shared<Cuts>();
     c->cols = cols;
@@ -233,10 +303,20 @@ void DMatrix::quantise(uint32_t mb, const DMatrix* ref, cudaStream_t stream, int
     c->values.assign(size_t(cols) * c->stride, 0.0f);
     c->counts.assign(cols, 0);
     c->minima.assign(cols, -INFINITY);
-    // XGBB_SKETCH=device computes the cuts on the GPU (the same cuts, bit for
-    // bit); the host sketch is the default.
+    // The GPU sketch (the same cuts, bit for bit) takes matrices of 2^26
+    // values or more when the device holds the matrix plus its runs; the
+    // host sketch takes smaller ones. XGBB_SKETCH=host|device overrides.
     const char* where = std::getenv("XGBB_SKETCH");
-    if (where && std::strcmp(where, "device") == 0 && rows && cols) {
+    bool on_device = false;
+    if (rows && cols) {
+      size_t free_b = 0, total_b = 0;
+      const size_t need = size_t(rows) * cols * sizeof(float) + size_t(rows) * 32 + (1ull << 30);
+      on_device = uint64_t(rows) * cols >= (1ull << 26) && cudaMemGetInfo(&free_b, &total_b) == cudaSuccess &&
+                  need <= free_b;
+      if (where && std::strcmp(where, "device") == 0) on_device = true;
+      if (where && std::strcmp(where, "host") == 0) on_device = false;
+    }
+    if (on_device) {
       const float* X = device_data(stream);
       DeviceBuffer w;
       if (!weights.empty()) {
@@ -253,6 +333,12 @@ void DMatrix::quantise(uint32_t mb, const DMatrix* ref, cudaStream_t stream, int
   }
   max_bin = mb;
   set_cuts(std::move(c), stream);
+  // The raw matrix was uploaded only for the sketch; predictions upload it
+  // again on demand.
+  if (!uploaded && d_data) {
+    XGBB_CUDA(cudaStreamSynchronize(stream));
+    d_data.release();
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -274,7 +360,7 @@ struct Booster::TrainState {
   uint32_t cols_pad = 0;
   DeviceBuffer state, ids[2], sums[2], seg_begin[2], seg_count[2], parent_slot, built_left,
       tile_offset, ptile_offset, cursor_l, cursor_r, counts_local, counts_global, mode, slot_leaf,
-      keys[2], cand, nodes, built, bank[2], rows_buf[2], level_rows, level_nodes, ord[2], limbs_root;
+      keys[2], cand, nodes, built, bank[2], rows_buf[2], level_rows, level_nodes, ord[2];
   TreeWorkspace ws{};
   HistConfig hc{};
   std::vector<cudaGraphExec_t> graphs;
@@ -786,9 +872,8 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp, bo
     ts->seg_count[i].resize(kMaxFrontier * 4);
     ts->keys[i].resize(kMaxFrontier * 8);
     ts->rows_buf[i].resize(std::max<size_t>(n, 1) * 4);
-    ts->ord[i].resize(std::max<size_t>(n, 1) * 16);
+    ts->ord[i].resize(std::max<size_t>(n, 1) * sizeof(float2));
   }
-  ts->limbs_root.resize(std::max<size_t>(n, 1) * 16);
   ts->parent_slot.resize(kMaxFrontier * 4);
   ts->built_left.resize(kMaxFrontier * 4);
   ts->tile_offset.resize((kMaxFrontier + 1) * 4);
@@ -838,7 +923,7 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp, bo
     ws.keys[i] = ts->keys[i].as<unsigned long long>();
     ws.bank[i] = ts->bank[i].as<longlong2>();
     ws.rows[i] = ts->rows_buf[i].as<uint32_t>();
-    ws.ord[i] = ts->ord[i].get();
+    ws.ord[i] = ts->ord[i].as<float2>();
   }
   ws.parent_slot = ts->parent_slot.as<uint32_t>();
   ws.built_left = ts->built_left.as<uint32_t>();
@@ -856,7 +941,6 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp, bo
   ws.node_capacity = ts->capacity;
   ws.level_rows = ts->level_rows.as<unsigned long long>();
   ws.level_nodes = ts->level_nodes.as<uint32_t>();
-  ws.limbs_root = ts->limbs_root.as<int4>();
   ts->hc = hist_config(e, ts->unit_hessian);
   // One graph per group and round parity: the two differ only in the
   // profiling events they record, so a round's events are read after the
@@ -903,28 +987,6 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp, bo
 }
 
 namespace {
-// The device's choice of histogram kernel for group g's tree, restated on the
-// host for the profile: two limbs when every |q| of the round has at most 42
-// bits (the staged kernel), three otherwise.
-bool staged_round(const unsigned int* max_bits, const float2* scales, uint32_t g, const Ellpack& e,
-                  bool unit_h, uint32_t min_limbs) {
-  if (e.bins + 1 > 257 || min_limbs >= 3) return false;
-  unsigned int bits[2];
-  float2 scale;
-  XGBB_CUDA(cudaMemcpy(bits, max_bits + 2 * g, sizeof bits, cudaMemcpyDeviceToHost));
-  XGBB_CUDA(cudaMemcpy(&scale, scales + g, sizeof scale, cudaMemcpyDeviceToHost));
-  auto two_limbs = [](unsigned int b, float sc) {
-    float mv;
-    const unsigned int m = b & 0x7fffffffu;
-    std::memcpy(&mv, &m, 4);
-    const long long q = std::llrint(mv * sc);
-    const unsigned long long a = (unsigned long long)(q < 0 ? -q : q);
-    const int bl = a ? 64 - __builtin_clzll(a) : 0;
-    return bl <= 42;
-  };
-  return two_limbs(bits[0], scale.x) && (unit_h || two_limbs(bits[1], scale.y));
-}
-
 // Device buffers of one group's host-driven tree (owned by the training
 // state).
 struct QueueDevice {
@@ -1099,6 +1161,7 @@ void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s, b
     if (profiling) mark(ts.events[((size_t(parity) * ts.groups + g) * D + depth) * 2 + 1]);
     // Sum the built histograms over ranks, each rank receiving its features.
     comm.reduce_scatter_u64(ws.built, size_t(per_rank) * max_pairs_at(depth) * (d.ell.bins + 1) * 2, s);
+    if (!capturing && g == 0 && capture.depth == int(depth) && !capture.ready) capture_level(ts, depth, tl);
     tree_level_eval(ws, tl, depth, s);
     if (comm.active()) {
       tree_level_pack_best(ws, tl, depth, ts.best_mine.get(), s);
@@ -1117,6 +1180,40 @@ void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s, b
       tree_level_plan(ws, tl, depth + 1, s);
     }
   }
+}
+
+// Copies this level's built histograms (after the sum over ranks) and the
+// nodes they belong to into `capture`. The built layout is feature-major,
+// [cols_pad][pair_stride][B + 1]; the capture is node-major.
+void Booster::capture_level(TrainState& ts, uint32_t depth, const TreeLaunch& tl) {
+  wait_stream("a level-histogram capture");
+  const TreeWorkspace& ws = ts.ws;
+  DriverState st{};
+  XGBB_CUDA(cudaMemcpy(&st, ws.state, sizeof st, cudaMemcpyDeviceToHost));
+  const uint32_t pairs = st.frontier ? (depth ? st.pairs : 1u) : 0u;
+  const uint32_t stride = max_pairs_at(depth), B1 = ts.d->ell.bins + 1, nf = tl.f_hi - tl.f_lo;
+  std::vector<long long> built(size_t(nf) * stride * B1 * 2);
+  if (!built.empty())
+    XGBB_CUDA(cudaMemcpy(built.data(), ws.built + size_t(tl.f_lo) * stride * B1, built.size() * 8,
+                         cudaMemcpyDeviceToHost));
+  std::vector<uint32_t> ids(size_t(2) * std::max(pairs, 1u)), left(std::max(pairs, 1u));
+  if (pairs) {
+    XGBB_CUDA(cudaMemcpy(ids.data(), ws.ids[depth & 1], ids.size() * 4, cudaMemcpyDeviceToHost));
+    XGBB_CUDA(cudaMemcpy(left.data(), ws.built_left, left.size() * 4, cudaMemcpyDeviceToHost));
+  }
+  capture.pairs = pairs;
+  capture.f_lo = tl.f_lo;
+  capture.f_hi = tl.f_hi;
+  capture.bins1 = B1;
+  capture.node_ids.assign(pairs, 0);
+  capture.hist.assign(size_t(pairs) * nf * B1 * 2, 0);
+  for (uint32_t p = 0; p < pairs; ++p) {
+    capture.node_ids[p] = depth ? ids[2 * p + (left[p] ? 0 : 1)] : ids[0];
+    for (uint32_t f = 0; f < nf; ++f)
+      std::memcpy(&capture.hist[(size_t(p) * nf + f) * B1 * 2], &built[(size_t(f) * stride + p) * B1 * 2],
+                  size_t(B1) * 16);
+  }
+  capture.ready = true;
 }
 
 // Group g's tree (node table, driver state, level statistics) into host set
@@ -1181,7 +1278,10 @@ void Booster::run_round(TrainState& ts, const CustomGradients* custom) {
   bool captured = false;
   const uint32_t b = ts.parity;
   for (uint32_t g = 0; g < G; ++g) {
-    if (use_graph) {
+    // A level capture reads the histograms between two launches, so that
+    // tree runs without its graph (the same launches, issued one by one).
+    const bool capture_here = g == 0 && capture.depth >= 0 && !capture.ready;
+    if (use_graph && !capture_here) {
       cudaGraphExec_t& exec = ts.graphs[size_t(g) * 2 + b];
       if (!exec) {
         // Kernel attributes are set on first use, outside any capture.
@@ -1314,15 +1414,11 @@ void Booster::finish_round(TrainState& ts) {
     const uint32_t D = tp_.max_depth;
     const Ellpack& e = d.ell;
     const double node_bytes = double(hist_node_bytes(e));
-    const bool unit_h = ts.unit_hessian;
-    const uint32_t min_limbs = uint32_t(integer(params_, "cuda_hist_limbs", 0));
     for (uint32_t g = 0; g < G; ++g) {
-      // Per row the histogram reads its codes, its gradient values (the
-      // int64-exact two-limb values, 16 bytes, on the staged path; the float
-      // pair, 8 bytes, on the three-limb path) and below the root its row id.
-      const bool staged = staged_round(mass_view(ts.mass.get(), ts.groups).max_bits,
-                                       ts.scales.as<float2>(), g, e, unit_h, min_limbs);
-      const double row_bytes = double(e.cols) * e.bytes_per_code + (staged ? 16.0 : 8.0);
+      // Per row the histogram reads its codes, its float gradient pair (8
+      // bytes, from which either kernel forms the exact integer values) and
+      // below the root its row id.
+      const double row_bytes = double(e.cols) * e.bytes_per_code + 8.0;
       for (uint32_t depth = 0; depth < D; ++depth) {
         float ms = 0;
         const size_t e = ((size_t(b) * G + g) * D + depth) * 2;

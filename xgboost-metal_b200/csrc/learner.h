@@ -156,6 +156,19 @@ class Booster {
   // recursive mutex, include/metalgb/engine.hpp:201, src/c_api.cpp:37-39).
   std::recursive_mutex& mutex() { return mutex_; }
   bool profiling = false;
+  // Built histograms of one level of the first tree of the next round, for
+  // checking them word for word. `depth` >= 0 requests a capture; the round
+  // that takes it runs that tree without a CUDA graph. `hist` holds
+  // [pairs][f_hi - f_lo][bins1][2] int64 words: the exact sums of this rank's
+  // feature range over the rows of every rank (the whole histogram on one
+  // GPU); node_ids[p] is the node whose histogram pair p built.
+  struct LevelCapture {
+    int depth = -1;
+    bool ready = false;
+    uint32_t pairs = 0, f_lo = 0, f_hi = 0, bins1 = 0;
+    std::vector<long long> hist;
+    std::vector<uint32_t> node_ids;
+  } capture;
   void sync();
   // CUDA events on the booster's stream, for timing whole rounds on the device.
   void record_event(int slot);
@@ -181,6 +194,7 @@ class Booster {
   void grow_host_driven(TrainState& ts);
   void record_tree_launches(TrainState& ts, uint32_t group, cudaStream_t stream, bool capturing,
                             uint32_t parity);
+  void capture_level(TrainState& ts, uint32_t depth, const TreeLaunch& tl);
   void materialize();
   Json model_param_json() const;
   std::vector<float> score_margins(const std::vector<float>& scores) const;

@@ -19,7 +19,10 @@
 //
 // Set-up: the first call on each device looks the scratch address up with
 // cudaGetSymbolAddress (which may load this library's device code); make that
-// first call before any stream capture on that device.
+// first call before any stream capture on that device. The address is kept
+// with the id of the device context it was found in; after a device reset
+// the next call finds the new context and looks the address up again, so
+// that call too belongs outside any capture.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -40,14 +43,51 @@ namespace xgbb {
 namespace {
 static_assert(kScratchBytes == kNoAllocMaxGroups * 2 * (4 + 4 + 16 + 32 + 80), "scratch size");
 
+// Id of the calling thread's current context (cuCtxGetId: unique for the
+// life of the process), or 0 when there is none or it cannot be read. The
+// driver calls are reached through the runtime's entry-point lookup, so the
+// library links no driver library.
+unsigned long long current_context_id() {
+  using GetCurrent = int (*)(void**);
+  using GetId = int (*)(void*, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrent>(f);
+    f = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(f);
+    cudaGetLastError();
+  });
+  void* ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current && get_id && get_current(&ctx) == 0 && ctx && get_id(ctx, &id) == 0) return id;
+  return 0;
+}
+
+// The array's device address in the current context. It is looked up once
+// per device and kept with the id of the context it belongs to; a device
+// reset (cudaDeviceReset) ends that context, and the next one maps the array
+// afresh, so a different (or unreadable) context id means a new lookup.
 void* scratch_address() {
   static std::mutex mu;
   static void* addr[kMaxDevices] = {};
+  static unsigned long long ctx[kMaxDevices] = {};
   int dev = 0;
   XGBB_CUDA(cudaGetDevice(&dev));
   require(dev >= 0 && dev < kMaxDevices, "device ordinal out of range for the gradient scratch");
   std::lock_guard<std::mutex> lock(mu);
-  if (!addr[dev]) XGBB_CUDA(cudaGetSymbolAddress(&addr[dev], g_gradient_scratch));
+  const unsigned long long id = current_context_id();
+  if (!addr[dev] || id == 0 || id != ctx[dev]) {
+    XGBB_CUDA(cudaGetSymbolAddress(&addr[dev], g_gradient_scratch));
+    ctx[dev] = current_context_id();  // the lookup made the device's context current
+  }
   return addr[dev];
 }
 }  // namespace

@@ -5,8 +5,8 @@
 //   gradient_kernel      kernels/boost.metal:553-601
 //   mass_*/scales        kernels/gradient_quantization.metal.h:1-67
 //   hist_kernel          kernels/boost.metal:700-733, histogram_missing.metal.h
-//   hist2_kernel         the same sums, staged two-limb form (limbs_kernel
-//                        forms each row's values once per tree)
+//   hist2_kernel         the same sums, staged two-limb form (each row's
+//                        values formed once per 32 features)
 //   eval_kernel          kernels/boost.metal:902-1005 (+ subtraction :780-794);
 //                        pack_best / merge_best select across ranks
 //   transpose_codes_kernel, narrow_codes_kernel: layouts of the same codes
@@ -411,8 +411,7 @@ __global__ void fill_margins_kernel(float* margins, const float* base, uint32_t 
 // ---------------------------------------------------------------------------
 struct HistArgs {
   Ellpack e;
-  const float2* pairs;   // gradient pairs in the order of the level's row list (three-limb kernel)
-  const int4* limbs;     // balanced two-limb values in that order (staged kernel)
+  const float2* pairs;   // gradient pairs in the order of the level's row list
   const float2* scale;
   const unsigned int* max_bits;  // largest |g| and |h| bits of this group (float bits)
   const uint32_t* rows;
@@ -679,16 +678,27 @@ __device__ __forceinline__ void hist_body(const HistArgs& a, int* smem, const Dr
 // ---------------------------------------------------------------------------
 // Staged two-limb histogram (every |q| of the round has at most 2L bits).
 //
-// Same ownership as hist_body (one CTA per SM, lane = feature, tile-ordered
-// items), with 16 warps. The global reads leave the critical path: each warp
-// copies the 32-feature code slice and the precomputed limbs of each of its
-// 32-row steps into one of two shared-memory stage buffers with cp.async, one
-// step ahead of the step it accumulates, and loads the row ids one step
-// ahead of the copies. The inner loop is one shared load of the code, one
-// broadcast load of the row's limbs and 3-4 shared atomics at compile-time
-// plane offsets. The carries out of limb 1 stay in registers (each thread
-// owns fixed words of the planes), so normalisation and flush touch only
-// shared memory and registers.
+// One CTA per SM over tile-ordered (feature group, pair, tile) items, as
+// hist_body, with 16 warps. Each warp copies the 32-feature code slices and
+// the precomputed limbs of its next 32 rows into one of two shared-memory
+// stage buffers with cp.async, one step ahead of the step it accumulates, and
+// loads the row ids one step ahead of the copies.
+//
+// Accumulation: lane r owns row r of the step. It keeps the row's limbs in
+// registers and reads the row's codes with 16-byte loads, so each shared
+// load feeds 8 (uint16) or 16 (uint8) features. At step f (0..31) lane r
+// adds to feature f ^ r: the 32 atomics of one instruction then touch 32
+// different features, which the [slot][32 features] plane layout puts in
+// 32 different banks. The stage stores row r's 16-byte chunk c at position
+// c ^ swz(r) (swz = (r >> 1) & 3 for uint16, (r >> 2) & 1 for uint8), so the
+// 8 lanes of each quarter-warp load phase read 8 different bank groups, and
+// each lane permutes its loaded codes in registers (position e holds element
+// e ^ r) so that the code of feature f ^ r sits at a fixed position for
+// step f. Per row and 32 features this costs 4 (3 with unit hessians)
+// shared atomics plus 0.5 (uint16) or 0.25 (uint8) shared loads; the carries
+// out of limb 1 stay in registers (each thread owns fixed words of the
+// planes), so normalisation and flush touch only shared memory and
+// registers.
 constexpr uint32_t kSlots = 257;                       // bins 0..255 + missing slot (<= 256)
 constexpr uint32_t kPlaneWords = kSlots * kHistLanes;  // ints per plane
 constexpr uint32_t kH2Warps = 16;
@@ -702,7 +712,7 @@ static_assert(kPlaneWords % 2 == 0, "planes hold whole word pairs");
 template <typename CodeT>
 struct __align__(16) HistStage {
   CodeT codes[kStageRows][kHistLanes];
-  int4 limbs[kStageRows];
+  float2 pairs[kStageRows];
 };
 
 template <typename CodeT, bool kUnitH>
@@ -713,6 +723,9 @@ constexpr size_t hist2_smem() {
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(dst), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template <int N>
@@ -725,6 +738,36 @@ __device__ __forceinline__ void cp_async_wait() {
 // the planes is separated from the adds by a CTA barrier.
 __device__ __forceinline__ void red_shared(uint32_t addr, int v) {
   asm volatile("red.shared.add.s32 [%0], %1;\n" ::"r"(addr), "r"(v));
+}
+
+// Stage position of chunk c (16 bytes) of staged row r; see hist2_kernel.
+template <typename CodeT>
+__device__ __forceinline__ uint32_t stage_chunk(uint32_t r, uint32_t c) {
+  return sizeof(CodeT) == 2 ? (c ^ ((r >> 1) & 3u)) : (c ^ ((r >> 2) & 1u));
+}
+__device__ __forceinline__ uint32_t pick(uint32_t a, uint32_t b, bool p) { return p ? b : a; }
+// Reorders 16 bytes of codes in registers so that position e holds element
+// e ^ x: uint16 codes (8 per quad, x < 8) or uint8 codes (16 per quad, x < 16).
+template <typename CodeT>
+__device__ __forceinline__ void xor_permute(uint32_t (&a)[4], uint32_t x) {
+  uint32_t s, p1, p2;
+  if (sizeof(CodeT) == 2) {
+    s = (x & 1u) ? 0x1032u : 0x3210u;  // swap the halves of each word
+    p1 = x & 2u;
+    p2 = x & 4u;
+  } else {
+    s = (x & 2u) ? ((x & 1u) ? 0x0123u : 0x1032u) : ((x & 1u) ? 0x2301u : 0x3210u);
+    p1 = x & 4u;
+    p2 = x & 8u;
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) a[i] = __byte_perm(a[i], 0, s);
+  const uint32_t t0 = pick(a[0], a[1], p1), t1 = pick(a[1], a[0], p1);
+  const uint32_t t2 = pick(a[2], a[3], p1), t3 = pick(a[3], a[2], p1);
+  a[0] = pick(t0, t2, p2);
+  a[2] = pick(t2, t0, p2);
+  a[1] = pick(t1, t3, p2);
+  a[3] = pick(t3, t1, p2);
 }
 
 // Limb plans of a round; the staged kernel takes the rounds whose values all
@@ -766,16 +809,6 @@ __device__ __forceinline__ int4 row_limbs(float2 gp, float2 sc, uint32_t Lg, uin
   return v;
 }
 
-// Limbs of every row (row order) for the root level of a staged round.
-__global__ void limbs_kernel(const float2* __restrict__ pairs, uint32_t rows, const float2* scale,
-                             const unsigned int* max_bits, uint32_t min_limbs, bool staged, bool unit_h,
-                             int4* __restrict__ out) {
-  LimbPlan pg, ph;
-  if (!plan_round(scale, max_bits, min_limbs, staged, unit_h, pg, ph)) return;
-  const float2 sc = *scale;
-  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < rows; i += gridDim.x * blockDim.x)
-    out[i] = row_limbs(__ldg(pairs + i), sc, pg.L, ph.L, unit_h);
-}
 
 // One step of one warp: up to kStageRows rows of one item, packed into three
 // registers (group < 2^22, pair < 2^10, rows of the CTA <= kStepRows).
@@ -941,15 +974,14 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
       const uint32_t r = pass * kRowsPerPass + lane / kParts;
       const uint32_t rid = kRoot ? s.row0 + r : __shfl_sync(0xffffffffu, id, r);
       if (r < s.n() && part < chunks)
-        cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(&dst.codes[r][0])) + part * 16,
+        cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(&dst.codes[r][0])) +
+                       stage_chunk<CodeT>(r, part) * 16,
                    codes + size_t(rid) * row_bytes + col_bytes);
     }
-    // Limb slots past n up to the next multiple of 8 are read by the
-    // unrolled loop: they hold zeros, so their stale codes add nothing.
+    // Lanes past n add zeros (their pairs are not read), so the stale codes
+    // of their stage rows add nothing; every stale code is a valid slot.
     if (lane < s.n())
-      cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(&dst.limbs[lane])), a.limbs + s.row0 + lane);
-    else if (lane < ((s.n() + 7) & ~7u))
-      dst.limbs[lane] = make_int4(0, 0, 0, 0);
+      cp_async8(static_cast<uint32_t>(__cvta_generic_to_shared(&dst.pairs[lane])), a.pairs + s.row0 + lane);
   };
   auto load_ids = [&](const HistStep& s) -> uint32_t {
     if (kRoot) return 0u;
@@ -1044,7 +1076,7 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
   uint32_t buf = 0;
   int64_t cur_group = -1, cur_pair = -1;
   uint32_t since = 0;
-  const uint32_t plane0 = static_cast<uint32_t>(__cvta_generic_to_shared(smem)) + lane * 4;
+  const uint32_t pbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
 
   while (s0.valid()) {
     if (int64_t(s0.group()) != cur_group || int64_t(s0.pair()) != cur_pair) {
@@ -1064,15 +1096,33 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
     issue(s1, id, buf ^ 1);
     cp_async_commit();
     id = load_ids(s2);
-    HistStage<CodeT>& st0 = stage[buf];
-    const uint32_t nr = (s0.n() + 7) & ~7u;
-    const CodeT* cc = &st0.codes[0][lane];
-    for (uint32_t j0 = 0; j0 < nr; j0 += 8) {
+    if (s0.n()) {
+      HistStage<CodeT>& st0 = stage[buf];
+      // Lane = row: its two-limb values, formed once for 32 features; lanes
+      // past n add zeros.
+      const int4 q = lane < s0.n() ? row_limbs(st0.pairs[lane], sc, Lg, Lh, kUnitH) : make_int4(0, 0, 0, 0);
+      constexpr uint32_t kQuads = kSlice / 16;
+      constexpr uint32_t kPerQuad = 16 / sizeof(CodeT);
+      uint32_t quad[kQuads][4];
+      const unsigned char* row = reinterpret_cast<const unsigned char*>(&st0.codes[lane][0]);
 #pragma unroll
-      for (uint32_t u = 0; u < 8; ++u) {
-        const uint32_t code = cc[(j0 + u) * kHistLanes];
-        const int4 q = st0.limbs[j0 + u];
-        const uint32_t addr = plane0 + code * (kHistLanes * 4);
+      for (uint32_t k = 0; k < kQuads; ++k) {
+        // Quad k holds features kPerQuad * (k ^ hi) + e ^ lo after the
+        // permutation, hi/lo the chunk and in-chunk bits of the lane.
+        const uint32_t c = k ^ (lane / kPerQuad);
+        const uint4 v = *reinterpret_cast<const uint4*>(row + stage_chunk<CodeT>(lane, c) * 16);
+        quad[k][0] = v.x;
+        quad[k][1] = v.y;
+        quad[k][2] = v.z;
+        quad[k][3] = v.w;
+        xor_permute<CodeT>(quad[k], lane % kPerQuad);
+      }
+      const uint32_t lane4 = lane * 4;
+#pragma unroll
+      for (uint32_t f = 0; f < kHistLanes; ++f) {
+        const uint32_t w = quad[f / kPerQuad][(f % kPerQuad) * sizeof(CodeT) / 4];
+        const uint32_t code = sizeof(CodeT) == 2 ? (w >> (16 * (f & 1))) & 0xffffu : (w >> (8 * (f & 3))) & 0xffu;
+        const uint32_t addr = pbase + code * (kHistLanes * 4) + (lane4 ^ (4 * f));
         red_shared(addr, q.x);
         red_shared(addr + kPlaneBytes, q.y);
         red_shared(addr + 2 * kPlaneBytes, q.z);
@@ -1539,14 +1589,8 @@ struct PartArgs {
   const float* slot_leaf;
   const uint32_t* rows;
   uint32_t* rows_next;
-  const float2* pairs;       // gradient pairs in the order of `rows` (three-limb rounds)
+  const float2* pairs;       // gradient pairs in the order of `rows`
   float2* pairs_next;        // ... and of `rows_next`
-  const int4* limbs;         // two-limb values in the order of `rows` (staged rounds)
-  int4* limbs_next;          // ... and of `rows_next`
-  const float2* scale;       // the round's limb plan (as the histogram kernels make it)
-  const unsigned int* max_bits;
-  uint32_t min_limbs;
-  bool staged, unit_h;
   uint32_t* cursor_l;
   uint32_t* cursor_r;
   float* margins;
@@ -1575,8 +1619,6 @@ __global__ void __launch_bounds__(kPartThreads) partition_kernel(PartArgs a) {
   const uint32_t lt_mask = (1u << lane) - 1u;
   const CodeT* __restrict__ codes = static_cast<const CodeT*>(a.e.codes);
   const CodeT* __restrict__ fm = static_cast<const CodeT*>(a.e.codes_fm);
-  LimbPlan pg, ph;
-  const bool two_limb = plan_round(a.scale, a.max_bits, a.min_limbs, a.staged, a.unit_h, pg, ph);
   for (uint32_t t = blockIdx.x; t < ptiles; t += gridDim.x) {
     uint32_t lo = 0, hi = n;
     while (hi - lo > 1) {
@@ -1662,8 +1704,7 @@ __global__ void __launch_bounds__(kPartThreads) partition_kernel(PartArgs a) {
         const uint32_t pos = left ? lpos + __popc(bl & lt_mask) : rpos + __popc(br & lt_mask);
         a.rows_next[pos] = rows[k];
         const uint32_t src = begin + w0 + k * 32 + lane;
-        if (two_limb) a.limbs_next[pos] = __ldg(a.limbs + src);
-        else a.pairs_next[pos] = __ldg(a.pairs + src);
+        a.pairs_next[pos] = __ldg(a.pairs + src);
       }
       lpos += __popc(bl);
       rpos += __popc(br);
@@ -2041,13 +2082,6 @@ void tree_init(const TreeWorkspace& ws, const TreeLaunch& tl, cudaStream_t strea
                                         ws.built_left, ws.keys[0], ws.nodes, ws.level_rows,
                                         ws.level_nodes);
   XGBB_CUDA(cudaGetLastError());
-  if (tl.ell.bins + 1 <= kSlots && tl.ell.rows) {
-    // Root limbs for a staged round (the kernel exits when the round needs
-    // three limbs).
-    limbs_kernel<<<grid_for(tl.ell.rows, 256, 148 * 8), 256, 0, stream>>>(
-        tl.pairs, tl.ell.rows, tl.scale, tl.max_bits, tl.min_limbs, true, tl.unit_hessian, ws.limbs_root);
-    XGBB_CUDA(cudaGetLastError());
-  }
 }
 
 void tree_level_hist(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t depth,
@@ -2056,8 +2090,7 @@ void tree_level_hist(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t dep
   XGBB_CUDA(cudaMemsetAsync(ws.built, 0, bytes, stream));
   HistArgs a;
   a.e = tl.ell;
-  a.pairs = depth == 0 ? tl.pairs : static_cast<const float2*>(ws.ord[depth & 1]);
-  a.limbs = depth == 0 ? ws.limbs_root : static_cast<const int4*>(ws.ord[depth & 1]);
+  a.pairs = depth == 0 ? tl.pairs : ws.ord[depth & 1];
   a.scale = tl.scale;
   a.rows = ws.rows[depth & 1];
   a.state = ws.state;
@@ -2213,15 +2246,8 @@ void tree_level_partition(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_
   a.slot_leaf = ws.slot_leaf;
   a.rows = ws.rows[depth & 1];
   a.rows_next = ws.rows[(depth + 1) & 1];
-  a.pairs = depth == 0 ? tl.pairs : static_cast<const float2*>(ws.ord[depth & 1]);
-  a.pairs_next = static_cast<float2*>(ws.ord[(depth + 1) & 1]);
-  a.limbs = depth == 0 ? ws.limbs_root : static_cast<const int4*>(ws.ord[depth & 1]);
-  a.limbs_next = static_cast<int4*>(ws.ord[(depth + 1) & 1]);
-  a.scale = tl.scale;
-  a.max_bits = tl.max_bits;
-  a.min_limbs = tl.min_limbs;
-  a.staged = tl.ell.bins + 1 <= kSlots;
-  a.unit_h = tl.unit_hessian;
+  a.pairs = depth == 0 ? tl.pairs : ws.ord[depth & 1];
+  a.pairs_next = ws.ord[(depth + 1) & 1];
   a.cursor_l = ws.cursor_l;
   a.cursor_r = ws.cursor_r;
   a.margins = tl.margins;

@@ -67,9 +67,7 @@ struct TreeWorkspace {
   longlong2* built;          // [pairs][cols][bins + 1]
   longlong2* bank[2];        // [slots][cols][bins + 1]
   uint32_t* rows[2];         // row ids per level (level 0 uses the identity)
-  void* ord[2];              // per row of rows[] (level >= 1): float2 gradient pair
-                             // (three-limb rounds) or int4 limbs (staged rounds)
-  int4* limbs_root;          // int4 limbs in row order (level 0 of staged rounds)
+  float2* ord[2];            // per row of rows[] (level >= 1): its gradient pair
   uint32_t node_capacity;
   unsigned long long* level_rows;  // [kMaxDepth] rows in built nodes per level
   uint32_t* level_nodes;           // [kMaxDepth] built nodes per level
