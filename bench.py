@@ -273,109 +273,180 @@ def launches_per_round(depth, groups):
 
 
 # ---------------------------------------------------------------------------
-# CPU baselines
+# CPU baselines: the reference's own functions on the host (oracle/_ref)
 # ---------------------------------------------------------------------------
-def _fit_to_full(samples, full_rows):
-    """Per-round seconds at `full_rows` from (rows, seconds) samples: a + b*rows
-    by least squares (the split search is a per-node cost, the histograms and
-    partitions a per-row cost)."""
-    r = np.array([s[0] for s in samples], np.float64)
-    t = np.array([s[1] for s in samples], np.float64)
-    if len(set(r.tolist())) == 1:
-        return float(t.mean()) * full_rows / r[0]
-    b, a = np.polyfit(r, t, 1)
-    return float(a + b * full_rows)
-
-
-def _sample_sizes(wl):
+def cpu_sample_rows(wl):
+    """Rows the CPU legs time: the whole matrix when it is small (c0-c2), a
+    leading 2M-row sample of c4 (c3: 200k rows of 784 features x 10
+    classes), so that a timed round takes seconds."""
     spec = WORKLOADS[wl]
-    rows = spec["rows"]
-    if rows <= 300_000:
-        return [rows]
-    if spec["cols"] * spec.get("num_class", 1) > 1000:
-        return [4_000, 16_000]   # wide multi-class rows: keep the CPU sample to seconds
-    return [25_000, 100_000]
+    if spec["rows"] <= 300_000:
+        return spec["rows"]
+    return 200_000 if spec["cols"] * spec.get("num_class", 1) > 1000 else 2_000_000
 
 
-def cpu_oracle_baseline(wl, device):
-    """The single-threaded oracle on bounded samples: per-round cost as the
-    difference of 2-round and 0-round runs, fitted over two sample sizes and
-    evaluated at the workload's rows."""
+class ReferencePath:
+    """One boosting round of the reference's own CPU path on a fixed sample:
+    its gradients kernel, gradient scales and quantisation, then its split
+    evaluation, selection, tree driver and predict functions over its
+    feature-major uint16 bins, building the smaller child of each node pair
+    and subtracting the sibling as its level loop does, on every host thread
+    (oracle/_ref/libxgbref.so, compiled from the reference's sources). The
+    cuts and bins come from the reference's own sketch and quantize kernel
+    (the DMatrix step, not timed)."""
+
+    def __init__(self, wl, rows, device):
+        import checkers as C
+        self.C = C
+        self.r = C.reference()
+        spec = WORKLOADS[wl]
+        self.spec, self.rows = spec, rows
+        X, self.y = gen_rows(wl, 0, rows, device, pin=False)
+        self.cuts, self.counts, self.minima = self.r.sketch_cuts(X, 256)
+        self.fm = C.reference_quantize_fm(X, self.cuts, self.counts)
+        del X
+        self.groups = groups_of(wl)
+        self.margins = np.zeros((rows, self.groups), np.float32)
+        self.tp = dict(max_depth=spec["max_depth"], eta=spec["eta"], reg_lambda=1.0, reg_alpha=0.0,
+                       min_child_weight=1.0, max_delta_step=0.0, min_split_loss=0.0)
+
+    def round(self):
+        """Seconds of one boosting round (wall clock)."""
+        C = self.C
+        t = time.perf_counter()
+        pairs = C.reference_gradients(self.spec["objective"], self.margins, self.y)
+        scale = self.r.gradient_scales(pairs)
+        q = self.r.quantize_gradients(pairs, scale)
+        for g in range(self.groups):   # one tree per class
+            _, leaf = C.reference_grow_tree_fm(self.fm, q[:, g, :], scale[g], self.cuts, self.counts,
+                                               self.minima, self.tp)
+            self.margins[:, g] += leaf
+        return time.perf_counter() - t
+
+
+def cpu_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count()
+
+
+def _full_rows_model(wl, device, measured):
+    """A labelled estimate of the reference path at the workload's full row
+    count: per-round seconds t = a + b * rows fitted through a second,
+    half-size sample (the per-node split search is the constant part, the
+    histograms and partitions grow with rows), evaluated at the full rows."""
     import checkers as C
     spec = WORKLOADS[wl]
-    extra = {"num_class": spec["num_class"]} if "num_class" in spec else {}
-    p = C.train_params(dict(objective=spec["objective"], max_depth=spec["max_depth"],
-                            eta=spec["eta"], **extra))
-    samples = []
-    for rows in _sample_sizes(wl):
-        X, y = gen_rows(wl, 0, rows, device, pin=False)
-        t = time.perf_counter()
-        C.oracle_train(X, y, p, 0)
-        t0 = time.perf_counter() - t
-        t = time.perf_counter()
-        C.oracle_train(X, y, p, 2)
-        t2 = time.perf_counter() - t
-        samples.append((rows, max(t2 - t0, 1e-9) / 2))
-    per_round = _fit_to_full(samples, spec["rows"])
-    value = per_round * 1000 * 100
-    return {"value": round(value, 1), "unit": UNIT, "cores": 1, "kind": "port",
-            "sample": "oracle (single-threaded C): per-round seconds %s on the first rows, "
-                      "linear fit in rows evaluated at %d rows, x100 rounds"
-                      % (", ".join("%d rows %.3fs" % s for s in samples), spec["rows"])}
+    rows2, t2 = measured
+    if rows2 >= spec["rows"] or not C.have_reference():
+        return None
+    half = ReferencePath(wl, rows2 // 2, device)
+    half.round()
+    t1 = min(half.round(), half.round())
+    b = (t2 - t1) / (rows2 - rows2 // 2)
+    a = t1 - b * (rows2 // 2)
+    return {"ms_per_100_rounds": round((a + b * spec["rows"]) * 1e5, 1), "rows": spec["rows"],
+            "model": "t = a + b*rows through %d rows (%.3f s) and %d rows (%.3f s) per round"
+                     % (rows2 // 2, t1, rows2, t2), "kind": "extrapolated"}
+
+
+def cpu_baseline_leg(wl, device):
+    """cpu_baseline: the reference path on the sample, warm-up round then the
+    best of three timed rounds (about 10-30 s of CPU work)."""
+    import checkers as C
+    if not C.have_reference():
+        return None
+    rows = cpu_sample_rows(wl)
+    ref = ReferencePath(wl, rows, device)
+    ref.round()
+    per_round = min(ref.round() for _ in range(3))
+    out = {"value": round(per_round * 1e5, 1), "unit": UNIT, "cores": cpu_cores(), "kind": "reference",
+           "rows": rows,
+           "sample": "the reference's CPU path (oracle/_ref: its gradients, scales, split evaluation, "
+                     "selection, tree driver and predict functions over its feature-major uint16 bins, "
+                     "smaller child built, sibling subtracted) on the first %d rows of %s, best of 3 "
+                     "rounds after 1 warm-up, x100 rounds; measured, not scaled to %d rows"
+                     % (rows, wl, WORKLOADS[wl]["rows"])}
+    model = _full_rows_model(wl, device, (rows, per_round))
+    if model:
+        out["full_rows_estimate"] = model
+    return out
 
 
 def reference_arm(args, wl, device):
-    """The reference's own serial split/driver/predict functions (oracle/_ref,
-    every host thread), one boosting round per step on bounded samples
-    (alternating two sizes), fitted in rows to the workload."""
+    """--impl reference: every step one boosting round of the reference's CPU
+    path (ReferencePath) on the sample, all host threads; value and
+    ms_per_step are what the steps measured."""
     import checkers as C
     spec = WORKLOADS[wl]
-    kind = "reference" if C.have_reference() else "port"
-    chk = C.reference() if kind == "reference" else C.oracle()
-    o = C.oracle()
-    sizes = _sample_sizes(wl) if spec["rows"] <= 300_000 else (
-        [2_000, 8_000] if spec["cols"] * spec.get("num_class", 1) > 1000 else [10_000, 40_000])
-    setups = []
-    for rows in sizes:
-        X, y = gen_rows(wl, 0, rows, device, pin=False)
-        cuts, counts, minima = o.sketch_cuts(X, 256)
-        setups.append(dict(rows=rows, y=y, bins=o.quantize(X, cuts, counts), cuts=cuts,
-                           counts=counts, minima=minima,
-                           margins=np.zeros((rows, groups_of(wl)), np.float32)))
-    tp = dict(max_depth=spec["max_depth"], eta=spec["eta"], reg_lambda=1.0, reg_alpha=0.0,
-              min_child_weight=1.0, max_delta_step=0.0, min_split_loss=0.0)
-    samples = []
-    for step in range(args.warmup + args.steps):
-        st = setups[step % len(setups)]
-        t = time.perf_counter()
-        pairs = C.oracle_gradients(spec["objective"], st["margins"], st["y"])
-        scale = chk.gradient_scales(pairs)
-        q_all = chk.quantize_gradients(pairs, scale)
-        for grp in range(groups_of(wl)):   # one tree per class
-            _, leaf = chk.grow_tree(st["bins"], q_all[:, grp, :], scale[grp], st["cuts"], st["counts"],
-                                    st["minima"], tp)
-            st["margins"][:, grp] += leaf
-        if step >= args.warmup:
-            samples.append((st["rows"], time.perf_counter() - t))
-    per_round = _fit_to_full(samples, spec["rows"])
-    value = per_round * 1000 * 100
-    cores = os.cpu_count() if kind == "reference" else 1
-    sample = ("%s, one round per step on the first %s rows (%d timed steps, means %s), linear "
-              "fit in rows evaluated at %d rows, x100 rounds"
-              % ("reference kernel functions compiled for the host (oracle/_ref)" if kind == "reference"
-                 else "oracle port", "/".join(str(x) for x in sizes), args.steps,
-                 ", ".join("%.3fs" % np.mean([t for r, t in samples if r == x]) for x in sizes),
-                 spec["rows"]))
+    if not C.have_reference():
+        return {"impl": "reference", "unavailable": "oracle/_ref/libxgbref.so (the reference's functions "
+                "compiled for the host) was not built"}
+    rows = cpu_sample_rows(wl)
+    ref = ReferencePath(wl, rows, device)
+    for _ in range(args.warmup):
+        ref.round()
+    times = [ref.round() for _ in range(args.steps)]
+    per_round = float(np.mean(times))
+    value = per_round * 1e5
+    sample = ("the reference's CPU path (oracle/_ref) on the first %d of %s's %d rows, one round per "
+              "step, %d timed steps after %d warm-up, %d host threads; measured on the sample"
+              % (rows, wl, spec["rows"], args.steps, args.warmup, cpu_cores()))
     return {"impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": UNIT,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(value / 100, 3), "higher_is_better": False, "scaling": "strong",
+            "ms_per_step": round(per_round * 1000, 3), "higher_is_better": False, "scaling": "strong",
             "vs_baseline": None, "dtype": "int64", "data": "synthetic",
-            "config": {"workload": wl, "rows": spec["rows"], "cols": spec["cols"],
+            "config": {"workload": wl, "rows": rows, "sample_of_rows": spec["rows"], "cols": spec["cols"],
                        "max_depth": spec["max_depth"], "objective": spec["objective"]},
-            "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": cores, "kind": kind,
+            "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": cpu_cores(), "kind": "reference",
                              "sample": sample},
             "e2e": {"value": round(value, 1), "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
+
+
+def c2_comparison(xgb, core, device, rounds=100, ref_rounds=3):
+    """BASELINE's c2 workload (262,144 x 64, depth 8, 100 rounds), where
+    north_star asks for 10x over the host CPU, measured in full on both
+    sides: this library end to end (DMatrix from pinned host arrays, lazy
+    quantisation inside train, as the reference's protocol times it) and on
+    the device, and the reference's CPU path on every host thread over all
+    262,144 rows."""
+    wl = "c2"
+    spec = WORKLOADS[wl]
+    Xh, yh = gen_rows(wl, 0, spec["rows"], device)
+    params = params_for(wl)
+    core.synchronize()
+    t0 = time.perf_counter()
+    bst = xgb.train(params, xgb.DMatrix(Xh, label=yh), rounds)
+    core.synchronize()
+    e2e_ms = (time.perf_counter() - t0) * 1000 * 100.0 / rounds
+    del bst
+    d = xgb.DMatrix(Xh, label=yh)
+    bst = xgb.Booster(params, [d])
+    for i in range(3):
+        bst.update(d, i)
+    core.synchronize()
+    bst.record_event(0)
+    for i in range(rounds):
+        bst.update(d, 3 + i)
+    bst.record_event(1)
+    dev_ms = bst.event_elapsed(0, 1) * 100.0 / rounds
+    core.synchronize()
+    out = {"workload": "c2", "rows": spec["rows"], "cols": spec["cols"], "max_depth": spec["max_depth"],
+           "rounds": rounds, "e2e_ms_per_100_rounds": round(e2e_ms, 2),
+           "device_ms_per_100_rounds": round(dev_ms, 2)}
+    import checkers as C
+    if C.have_reference():
+        ref = ReferencePath(wl, spec["rows"], device)
+        ref.round()
+        t = float(np.mean([ref.round() for _ in range(ref_rounds)]))
+        out.update({"reference_cpu_ms_per_100_rounds": round(t * 1e5, 1), "reference_cpu_cores": cpu_cores(),
+                    "reference_cpu_rounds_timed": ref_rounds,
+                    "speedup_e2e": round(t * 1e5 / e2e_ms, 1), "speedup_device": round(t * 1e5 / dev_ms, 1),
+                    "reference": "the reference's CPU path (oracle/_ref) on all rows; stock XGBoost CPU hist "
+                                 "is not installable here"})
+    return out
 
 
 def measured_peak():
@@ -438,27 +509,30 @@ def main():
     begin, end = shard(spec["rows"], dist.rank, dist.world)
     t = time.perf_counter()
     Xh, yh = gen_rows(wl, begin, end, device)
-    sample = min(spec["rows"], CHUNK)
-    if wl == "c4":
-        Xs, _ = gen_rows(wl, 0, sample, device, pin=False)
-        ref = xgb.QuantileDMatrix(Xs, max_bin=256)
     log("rank %d: rows [%d, %d) generated in %.1fs" % (dist.rank, begin, end, time.perf_counter() - t))
     params = params_for(wl)
     K, W = args.steps, args.warmup
     groups = groups_of(wl)
 
-    # End to end: host buffers in, quantisation (H2D + binning) and K rounds
-    # through the public API; every round reads its trees back to the host.
+    # End to end through the public API from pinned host arrays: ingest (the
+    # H2D copy, the quantile sketch of every row -- over all ranks' rows, on
+    # every GPU, when sharded -- and binning; a plain DMatrix does this lazily
+    # in the first round), then K rounds, each reading its trees back.
     dist.barrier()
     core.synchronize()
     t0 = time.perf_counter()
-    if wl == "c4":
-        dtrain = xgb.QuantileDMatrix(Xh, label=yh, ref=ref, max_bin=256)
+    if wl in ("c4", "c3"):
+        dtrain = xgb.QuantileDMatrix(Xh, label=yh, max_bin=256)
     else:
         dtrain = xgb.DMatrix(Xh, label=yh)
+    core.synchronize()
+    t1 = time.perf_counter()
     bst = xgb.train(params, dtrain, K)
     core.synchronize()
-    e2e_ms = dist.max((time.perf_counter() - t0) * 1000)
+    t2 = time.perf_counter()
+    e2e_ms = dist.max((t2 - t0) * 1000)
+    ingest_ms = dist.max((t1 - t0) * 1000)
+    rounds_ms = dist.max((t2 - t1) * 1000)
     del bst
 
     # Device-resident: a fresh booster on the quantised matrix, W warm-up
@@ -495,9 +569,11 @@ def main():
                 "per_level_ms_mrows": [[round(ms / K, 3), round(rows / K / 1e6, 3)]
                                        for ms, rows, _ in prof.get("levels", []) if rows]}
 
-    cpu = None
+    cpu, c2 = None, None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_oracle_baseline(wl, device)
+        cpu = cpu_baseline_leg(wl, device)
+        if wl == "c4" and not args.rows:
+            c2 = c2_comparison(xgb, core, device)
 
     bytes_per_code = 2 if (spec["nan"] > 0) else 1
     x_bytes = Xh.nbytes + yh.nbytes
@@ -513,17 +589,19 @@ def main():
                    "max_bin": 256, "eta": spec["eta"], "nan_fraction": spec["nan"],
                    "bins": "uint%d ELLPACK" % (8 * bytes_per_code),
                    "parallelism": "row-shard dp%d" % dist.world,
-                   "cuts": ("from the first %d rows (QuantileDMatrix ref), identical on every rank"
-                            % sample) if wl == "c4" else "sketch of the full matrix",
+                   "cuts": "sketch of every row (GPU sketch; over all ranks' rows when sharded)",
                    "l2": "inputs larger than L2 (quantised matrix %.1f GB)"
                          % (spec["rows"] * spec["cols"] * bytes_per_code / 1e9)},
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_ms * 100.0 / K, 3), "unit": UNIT,
                 "h2d_bytes_per_step": int(x_bytes / K), "d2h_bytes_per_step": node_table,
-                "note": "xgb.train(QuantileDMatrix/DMatrix from pinned host arrays) for K rounds, "
-                        "wall clock, max over ranks; H2D of the matrix amortised over K rounds"},
+                "ingest_ms": round(ingest_ms, 1), "per_round_ms": round(rounds_ms / K, 3), "rounds": K,
+                "note": "QuantileDMatrix (c3, c4) or DMatrix from pinned host arrays, then xgb.train for "
+                        "K rounds; wall clock, max over ranks. ingest = H2D + sketch of all rows + "
+                        "binning; the ingest is amortised over K rounds in value"},
         "parity": parity,
+        "c2": c2,
         "gpu_launches": launches_per_round(spec["max_depth"], groups) * K,
         "clocks": clocks.summary(),
     }

@@ -144,11 +144,12 @@ extern "C" {
 int xgbref_sketch_cuts(const float* X, uint32_t rows, uint32_t cols, const float* weights,
                        uint32_t max_bin, float* cuts, uint32_t* counts, float* minima) {
   u32 hist_bins = std::max(1u, std::min(max_bin, rows));
-  for (u32 f = 0; f < cols; ++f) {
+  // Features are independent (one summary per feature): one task each.
+  parallel_for(cols, [&](u32 f) {
     std::fill(cuts + std::size_t(f) * hist_bins, cuts + std::size_t(f + 1) * hist_bins, 0.0f);
     feature_cuts(X, rows, cols, f, weights, max_bin, hist_bins, cuts + std::size_t(f) * hist_bins,
                  counts + f, minima + f);
-  }
+  });
   return int(hist_bins);
 }
 
@@ -170,6 +171,36 @@ void xgbref_quantize(const float* X, uint32_t rows, uint32_t cols, const float* 
       bins_out[std::size_t(r) * cols + c] =
           wide ? storage[fm] : load_bin(bins16, fm, cut_stride);
     }
+}
+
+// The reference's own feature-major uint16 bins (bins[f * rows + row],
+// 0xffff = missing; Matrix::quantize, src/data.cpp:1210-1306) via the
+// quantize kernel, rows in parallel. Only for cut strides up to 65534.
+void xgbref_quantize_fm(const float* X, uint32_t rows, uint32_t cols, const float* cuts,
+                        uint32_t cut_stride, const uint32_t* counts, uint16_t* fm_out) {
+  MatrixParams p{rows, cols, rows, cut_stride, cut_stride};
+  std::vector<uchar> categorical(cols, 0);
+  atomic_uint missing = 0;
+  const u32 chunk = 4096;
+  parallel_for((rows + chunk - 1) / chunk, [&](u32 t) {
+    for (u32 r = t * chunk; r < std::min(rows, (t + 1) * chunk); ++r)
+      for (u32 c = 0; c < cols; ++c)
+        quantize<>(X, cuts, counts, reinterpret_cast<ushort*>(fm_out), categorical.data(), &missing, p,
+                   uint2(r, c));
+  });
+}
+
+// Gradient pairs [rows][groups] from the reference's gradients kernel
+// (kernels/boost.metal:553-601), rows in parallel.
+void xgbref_gradients(int objective, const float* margins, const float* labels, const float* weights,
+                      uint32_t rows, uint32_t groups, float scale_pos_weight, float* pairs) {
+  GradientParams p{rows, groups, 1, uint(objective), weights ? 1u : 0u, 0, 0, 0, scale_pos_weight, 1, 0, 0};
+  const u32 chunk = 4096;
+  parallel_for((rows + chunk - 1) / chunk, [&](u32 t) {
+    for (u32 r = t * chunk; r < std::min(rows, (t + 1) * chunk); ++r)
+      for (u32 g = 0; g < groups; ++g)
+        gradients<>(margins, labels, weights, reinterpret_cast<Pair*>(pairs), p, uint2(r, g));
+  });
 }
 
 // Per-group power-of-two scales (float pairs: g-scale, h-scale). The exact
@@ -400,6 +431,168 @@ int xgbref_grow_tree(const uint32_t* bins, uint32_t rows, uint32_t cols, const i
       predict<>(row.data(), tree.data(), &meta, &base, &zero, row_leaf + r, &no_categories, nullptr,
                 nullptr, nullptr, pp, uint2(0, 0));
     }
+  }
+  return int(count);
+}
+
+// The same tree over the reference's feature-major uint16 bins (as
+// xgbref_quantize_fm writes them), built the way the reference's level loop
+// builds it: at each level only the smaller child of every node pair gets a
+// histogram (a tie builds the left one; plan_histograms,
+// kernels/boost.metal:661-698) and its sibling is the parent minus it
+// (subtract_histograms, :780-794). Histograms are built per (node, feature)
+// task over all host threads; partitions per node pair and the margin
+// increments per row block run in parallel as well. Splits, selection, the
+// driver and prediction are the reference's functions as in xgbref_grow_tree.
+int xgbref_grow_tree_fm(const uint16_t* fm, uint32_t rows, uint32_t cols, const int64_t* q,
+                        const float* scale, const float* cuts, uint32_t cut_stride,
+                        const uint32_t* counts, const float* minima, uint32_t max_depth, float eta,
+                        float reg_lambda, float reg_alpha, float min_child_weight, float max_delta_step,
+                        float min_split_loss, RefNode* out_nodes, uint32_t node_capacity,
+                        float* row_leaf) {
+  const u32 B = cut_stride;
+  if (B > 65534) return -1;
+  const std::size_t per_node = std::size_t(cols) * (B + 1) * 2;
+  TreeDriverParams tp{};
+  tp.split.cols = cols; tp.split.bins = B;
+  tp.split.reg_lambda = reg_lambda; tp.split.reg_alpha = reg_alpha;
+  tp.split.min_child_weight = min_child_weight; tp.split.max_delta_step = max_delta_step;
+  tp.partition.rows = rows;
+  tp.max_depth = max_depth;
+  u32 capacity = (max_depth >= 31) ? 0xffffffffu : ((2u << max_depth) - 1);
+  tp.node_capacity = capacity;
+  tp.min_gain = min_split_loss;
+  TreeDriverState state{1, 1, 0, 0};
+  std::vector<Split> history(capacity);
+  std::vector<uint> flags(capacity, 0);
+  std::vector<uint> ids{0};
+  std::vector<IntPair> sums{IntPair{0, 0}};
+  std::vector<std::vector<u32>> segments(1);
+  segments[0].resize(rows);
+  for (u32 r = 0; r < rows; ++r) segments[0][r] = r;
+  auto bin_of = [&](u32 r, u32 f) -> u32 { return load_bin(fm, std::size_t(f) * rows + r, B); };
+  auto decoded = [&](u32 r, u32 f) -> float {
+    u32 b = bin_of(r, f);
+    if (b == 0xffffffffu) return NAN;
+    return b ? cuts[std::size_t(f) * B + b - 1] : -INFINITY;
+  };
+  std::vector<int64_t> prev;     // the previous level's histograms [nodes][cols][B + 1][2]
+  std::vector<uint> parent_hist;  // previous-level slot of each pair's parent
+  for (u32 depth = 0; depth < max_depth && state.frontier_count; ++depth) {
+    u32 nodes = state.frontier_count;
+    std::vector<int64_t> hist(std::size_t(nodes) * per_node, 0);
+    std::vector<u32> seg_count(nodes), seg_offset(nodes), built;
+    u32 offset = 0;
+    for (u32 s = 0; s < nodes; ++s) {
+      seg_count[s] = u32(segments[s].size());
+      seg_offset[s] = offset;
+      offset += seg_count[s];
+    }
+    if (depth == 0) built.push_back(0);
+    else
+      for (u32 s = 0; s + 1 < nodes; s += 2) built.push_back(seg_count[s] <= seg_count[s + 1] ? s : s + 1);
+    parallel_for(u32(built.size()) * cols, [&](u32 i) {
+      const u32 s = built[i / cols], f = i % cols;
+      int64_t* h = hist.data() + std::size_t(s) * per_node + std::size_t(f) * (B + 1) * 2;
+      const uint16_t* col = fm + std::size_t(f) * rows;
+      for (u32 r : segments[s]) {
+        u32 b = col[r];
+        b = b == 65535 ? B : b;
+        h[2 * b] = int64_t(uint64_t(h[2 * b]) + uint64_t(q[std::size_t(r) * 2]));
+        h[2 * b + 1] = int64_t(uint64_t(h[2 * b + 1]) + uint64_t(q[std::size_t(r) * 2 + 1]));
+      }
+    });
+    if (depth) {
+      parallel_for(u32(built.size()) * cols, [&](u32 i) {
+        const u32 pair = i / cols, f = i % cols, small = built[pair], other = small ^ 1u;
+        const int64_t* par = prev.data() + std::size_t(parent_hist[pair]) * per_node + std::size_t(f) * (B + 1) * 2;
+        const int64_t* got = hist.data() + std::size_t(small) * per_node + std::size_t(f) * (B + 1) * 2;
+        int64_t* out = hist.data() + std::size_t(other) * per_node + std::size_t(f) * (B + 1) * 2;
+        for (u32 k = 0; k < (B + 1) * 2; ++k) out[k] = int64_t(uint64_t(par[k]) - uint64_t(got[k]));
+      });
+    }
+    std::vector<Split> candidates(std::size_t(nodes) * cols), best(nodes);
+    xgbref_evaluate_splits(hist.data(), nodes, cols, B, scale, cuts, counts, minima, reg_lambda,
+                           reg_alpha, min_child_weight, max_delta_step, depth != 0,
+                           reinterpret_cast<const int64_t*>(sums.data()), candidates.data());
+    xgbref_select_splits(candidates.data(), nodes, cols, scale, reg_lambda, reg_alpha,
+                         max_delta_step, best.data());
+    std::vector<uint> next_ids(2 * nodes), selected_counts(nodes), selected_offsets(nodes);
+    parent_hist.assign(nodes, 0);
+    std::vector<IntPair> next_sums(2 * nodes);
+    std::vector<Split> selected(nodes);
+    std::vector<int2> children(nodes);
+    tree_driver_apply<>(&state, ids.data(), best.data(), seg_count.data(), seg_offset.data(),
+                        history.data(), flags.data(), next_ids.data(), next_sums.data(),
+                        selected.data(), selected_counts.data(), selected_offsets.data(),
+                        children.data(), parent_hist.data(), tp, 0u);
+    if (state.error) return -1;
+    u32 next = state.frontier_count;
+    std::vector<std::vector<u32>> next_segments(next);
+    parallel_for(next / 2, [&](u32 s) {
+      u32 slot = parent_hist[s];
+      const Split& sp = selected[s];
+      for (u32 r : segments[slot]) {
+        bool left = split_left(decoded(r, u32(sp.feature)), sp.threshold, sp.default_left, 0, 0, 0,
+                               nullptr);
+        next_segments[2 * s + (left ? 0 : 1)].push_back(r);
+      }
+    });
+    ids.assign(next_ids.begin(), next_ids.begin() + next);
+    sums.assign(next_sums.begin(), next_sums.begin() + next);
+    segments = std::move(next_segments);
+    prev = std::move(hist);
+  }
+  // Host replay (src/tree.cpp:1663-1717), scalar numeric leaves only.
+  u32 count = state.node_count;
+  if (count > node_capacity) return -1;
+  std::vector<Node> tree(1);
+  std::vector<u32> split_bin(1, 0);
+  for (u32 id = 0; id < count; ++id) {
+    if (id >= tree.size()) return -1;
+    uint status = flags[id];
+    if (!(status & kTreeDriverEvaluated)) continue;
+    const Split& split = history[id];
+    tree[id].cover = split.total_h;
+    if (!id) tree[0].leaf = split.parent_weight * eta;
+    if (!(status & kTreeDriverExpanded)) continue;
+    int left = int(tree.size());
+    tree[id].left = left; tree[id].right = left + 1; tree[id].feature = split.feature;
+    tree[id].threshold = split.threshold; tree[id].default_left = split.default_left;
+    tree[id].gain = split.gain;
+    tree[id].cover = split.applied_parent_hessian;
+    u32 f = u32(split.feature);
+    int k = -1;
+    for (u32 b = 0; b < counts[f]; ++b)
+      if (as_type<uint>(cuts[std::size_t(f) * B + b]) == as_type<uint>(split.threshold)) k = int(b);
+    split_bin[id] = u32(k);
+    Node l, r;
+    l.parent = int(id); r.parent = int(id);
+    l.leaf = split.left_weight * eta; l.cover = split.left_h;
+    r.leaf = split.right_weight * eta; r.cover = split.right_h;
+    tree.push_back(l); tree.push_back(r);
+    split_bin.push_back(0); split_bin.push_back(0);
+  }
+  if (tree.size() != count) return -1;
+  for (u32 i = 0; i < count; ++i) {
+    const Node& n = tree[i];
+    out_nodes[i] = RefNode{n.left, n.right, n.feature, n.parent, n.threshold, n.leaf, n.cover, n.gain,
+                           n.default_left, split_bin[i]};
+  }
+  if (row_leaf) {
+    TreeMeta meta{0, count, 0, 0, 0, 1, 0};
+    PredictParams pp{1, cols, 1, 1, 0, 1, 0, 0, 1, 1, 0, 0, 0};
+    const u32 chunk = 4096;
+    parallel_for((rows + chunk - 1) / chunk, [&](u32 t) {
+      std::vector<float> row(cols);
+      float zero = 0, base = 0;
+      uint no_categories = 0;
+      for (u32 r = t * chunk; r < std::min(rows, (t + 1) * chunk); ++r) {
+        for (u32 f = 0; f < cols; ++f) row[f] = decoded(r, f);
+        predict<>(row.data(), tree.data(), &meta, &base, &zero, row_leaf + r, &no_categories, nullptr,
+                  nullptr, nullptr, pp, uint2(0, 0));
+      }
+    });
   }
   return int(count);
 }

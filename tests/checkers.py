@@ -297,3 +297,45 @@ def oracle_base_margin(objective, labels, weights=None, groups=1, scale_pos_weig
                                    _U32(len(labels)), _U32(groups), _F(scale_pos_weight), _ptr(score),
                                    _ptr(margin))
     return margin
+
+
+# --- the reference's own CPU path for the bench's reference arm ---------------
+
+def reference_quantize_fm(X, cuts, counts):
+    """Feature-major uint16 bins [cols][rows] (0xffff = missing) from the
+    reference's quantize kernel (xgbref_quantize_fm)."""
+    X = np.ascontiguousarray(X, np.float32)
+    rows, cols = X.shape
+    out = np.zeros((cols, rows), np.uint16)
+    reference()._l.fn("quantize_fm")(_ptr(X), _U32(rows), _U32(cols), _ptr(cuts), _U32(cuts.shape[1]),
+                                     _ptr(counts), _ptr(out))
+    return out
+
+
+def reference_gradients(objective, margins, labels, weights=None, scale_pos_weight=1.0):
+    """Gradient pairs [rows][groups][2] from the reference's gradients kernel."""
+    margins = np.ascontiguousarray(margins, np.float32)
+    rows, groups = margins.shape
+    pairs = np.zeros((rows, groups, 2), np.float32)
+    reference()._l.fn("gradients")(ctypes.c_int(OBJECTIVES[objective]), _ptr(margins),
+                                   _ptr(np.ascontiguousarray(labels, np.float32)),
+                                   _ptr(None if weights is None else np.ascontiguousarray(weights, np.float32)),
+                                   _U32(rows), _U32(groups), _F(scale_pos_weight), _ptr(pairs))
+    return pairs
+
+
+def reference_grow_tree_fm(fm, q, scale, cuts, counts, minima, params):
+    """xgbref_grow_tree_fm: (nodes, per-row leaf values) over feature-major
+    uint16 bins, smaller child built and sibling subtracted per level."""
+    cols, rows = fm.shape
+    cap = (2 << params["max_depth"]) - 1
+    nodes = np.zeros(cap, NODE_DTYPE)
+    leaf = np.zeros(rows, np.float32)
+    n = reference()._l.fn("grow_tree_fm", ctypes.c_int)(
+        _ptr(np.ascontiguousarray(fm, np.uint16)), _U32(rows), _U32(cols),
+        _ptr(np.ascontiguousarray(q, np.int64)), _ptr(np.ascontiguousarray(scale, np.float32)),
+        _ptr(cuts), _U32(cuts.shape[1]), _ptr(counts), _ptr(minima), _U32(params["max_depth"]),
+        _F(params["eta"]), _F(params["reg_lambda"]), _F(params["reg_alpha"]), _F(params["min_child_weight"]),
+        _F(params["max_delta_step"]), _F(params["min_split_loss"]), _ptr(nodes), _U32(cap), _ptr(leaf))
+    assert n > 0, n
+    return nodes[:n], leaf

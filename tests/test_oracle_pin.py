@@ -147,3 +147,44 @@ def test_det_exp_is_correctly_rounded_on_a_grid():
     got = np.array([f(float(x)) for x in xs], np.float32)
     want = np.exp(xs.astype(np.float64)).astype(np.float32)
     assert np.array_equal(got, want)
+
+
+@pytest.mark.skipif(not C.have_reference(), reason="reference harness not built")
+@pytest.mark.parametrize("seed", [0, 1])
+def test_reference_cpu_path_matches_its_serial_form(seed):
+    """The bench's reference arm runs the reference's functions on all host
+    threads over its feature-major uint16 bins, building the smaller child of
+    each pair and subtracting the sibling. Its trees and leaf values equal the
+    serial harness's (every node built) and the oracle's, bit for bit, and
+    the reference's gradients kernel equals the oracle's restatement."""
+    o, r = C.oracle(), C.reference()
+    rng = np.random.default_rng(300 + seed)
+    rows, cols = [6000, 9000][seed], 7
+    X = rng.normal(size=(rows, cols)).astype(np.float32)
+    X[rng.random(X.shape) < 0.1 * seed] = np.nan
+    cuts, counts, minima = r.sketch_cuts(X, 64)
+    bins = r.quantize(X, cuts, counts)
+    fm = C.reference_quantize_fm(X, cuts, counts)
+    want_fm = np.where(bins == C.MISSING, 0xFFFF, bins).T.astype(np.uint16)
+    np.testing.assert_array_equal(fm, want_fm)
+    objective = ["reg:squarederror", "binary:logistic"][seed]
+    y = (rng.random(rows) < 0.4).astype(np.float32) if seed else rng.normal(size=rows).astype(np.float32)
+    margins = (rng.normal(size=(rows, 1)) * 0.5).astype(np.float32)
+    pairs = C.reference_gradients(objective, margins, y)
+    want = C.oracle_gradients(objective, margins, y)
+    if objective == "reg:squarederror":
+        np.testing.assert_array_equal(_bits(pairs), _bits(want))
+    else:
+        # The harness's sigmoid takes the host libm's exp, the oracle's the
+        # deterministic det_expf: a few values differ by an ulp or two.
+        assert np.abs(_bits(pairs).astype(np.int64) - _bits(want).astype(np.int64)).max() <= 2
+    scale = r.gradient_scales(pairs)[0]
+    q = r.quantize_gradients(pairs, scale[None])[:, 0, :]
+    tp = dict(max_depth=[6, 8][seed], eta=0.3, reg_lambda=1.0, reg_alpha=0.0,
+              min_child_weight=1.0, max_delta_step=0.0, min_split_loss=0.0)
+    nf, lf = C.reference_grow_tree_fm(fm, q, scale, cuts, counts, minima, tp)
+    ns, ls = r.grow_tree(bins, q, scale, cuts, counts, minima, tp)
+    no, lo = o.grow_tree(bins, q, scale, cuts, counts, minima, tp)
+    assert nf.tobytes() == ns.tobytes() == no.tobytes()
+    np.testing.assert_array_equal(_bits(lf), _bits(ls))
+    np.testing.assert_array_equal(_bits(lf), _bits(lo))
