@@ -1140,8 +1140,7 @@ void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s, b
   tl.min_limbs = uint32_t(integer(params_, "cuda_hist_limbs", 0));
   tl.hist_smem = ts.hc.smem;
   tl.hist_threads = ts.hc.threads;
-  int sms = 148;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device_);
+  const int sms = device_sms();
   tl.hist_blocks = sms;
   tl.eval_blocks = sms * 8;
   tl.part_blocks = sms * 8;
@@ -1330,8 +1329,7 @@ void Booster::grow_host_driven(TrainState& ts) {
   std::vector<float2> scales(G);
   XGBB_CUDA(cudaMemcpyAsync(scales.data(), ts.scales.get(), G * sizeof(float2), cudaMemcpyDeviceToHost, stream_));
   XGBB_CUDA(cudaStreamSynchronize(stream_));
-  int sms = 148;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device_);
+  const int sms = device_sms();
   QueueDevice q{};
   q.e = d.ell;
   q.tp = tp_;

@@ -131,8 +131,8 @@ __global__ void queue_fill_missing_kernel(uint32_t bins, uint32_t cols, uint32_t
 }
 
 int grid_for(uint64_t work, int threads) {
-  const uint64_t g = (work + threads - 1) / threads;
-  return int(g < 1 ? 1 : (g > 148 * 16 ? 148 * 16 : g));
+  const uint64_t g = (work + threads - 1) / threads, cap = uint64_t(device_sms()) * 16;
+  return int(g < 1 ? 1 : (g > cap ? cap : g));
 }
 
 }  // namespace

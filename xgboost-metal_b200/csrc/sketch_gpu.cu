@@ -21,6 +21,7 @@
 #include "exec.h"
 #include "sketch.h"
 #include "sketch_par.h"
+#include "tree.h"
 
 namespace xgbb {
 namespace {
@@ -127,9 +128,7 @@ void sketch_cuts_device(const float* X, uint32_t rows, uint32_t cols, const floa
   if (!cols) return;
   const size_t runs_smem = 7 * size_t(kChunkRows) * 4;
   XGBB_CUDA(cudaFuncSetAttribute(sketch_runs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(runs_smem)));
-  int sms = 148, dev = 0;
-  XGBB_CUDA(cudaGetDevice(&dev));
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int sms = device_sms();
   // Features per group: runs and batch summaries take about 16 bytes per row
   // and feature; keep them within a quarter of the free memory.
   size_t free_b = 0, total_b = 0;

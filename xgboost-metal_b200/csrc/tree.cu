@@ -1906,12 +1906,27 @@ __global__ void limbs_to_window_kernel(MassAccum m, uint32_t n) {
   m.window[2 * i + 1] = w[2] | (w[3] << 32);
 }
 
-int grid_for(uint64_t work, int threads, int cap = 148 * 16) {
+// Blocks for `work` items at `threads` per block, at most `per_sm` blocks per
+// streaming multiprocessor of the device.
+int grid_for(uint64_t work, int threads, int per_sm = 16) {
   const uint64_t blocks = (work + threads - 1) / threads;
-  return int(std::max<uint64_t>(1, std::min<uint64_t>(blocks, uint64_t(cap))));
+  return int(std::max<uint64_t>(1, std::min<uint64_t>(blocks, uint64_t(device_sms()) * per_sm)));
 }
 
 }  // namespace
+
+int device_sms() {
+  constexpr int kDevices = 64;
+  static int cache[kDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kDevices) return 148;
+  if (!cache[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
 
 // ---------------------------------------------------------------------------
 // Launchers.
@@ -1942,7 +1957,7 @@ void launch_transpose_codes(const void* codes, uint32_t rows, uint32_t cols, uin
                             uint32_t bytes_per_code, void* fm, cudaStream_t stream) {
   const uint64_t tiles = uint64_t((rows + 63) / 64) * ((cols + 63) / 64);
   if (!tiles) return;
-  const int blocks = grid_for(tiles, 1, 148 * 16);
+  const int blocks = grid_for(tiles, 1, 16);
   if (bytes_per_code == 1)
     transpose_codes_kernel<uint8_t><<<blocks, 256, 0, stream>>>(
         static_cast<const uint8_t*>(codes), rows, cols, stride, static_cast<uint8_t*>(fm));
@@ -1957,7 +1972,7 @@ void launch_quantize(const float* X, uint32_t rows, uint32_t cols, const float* 
                      uint32_t bytes_per_code, uint32_t missing, cudaStream_t stream) {
   const uint64_t total = uint64_t(rows) * stride;
   if (!total) return;
-  const int threads = 256, blocks = grid_for(total, threads, 148 * 32);
+  const int threads = 256, blocks = grid_for(total, threads, 32);
   if (bytes_per_code == 1)
     quantize_kernel<uint8_t><<<blocks, threads, 0, stream>>>(
         X, rows, cols, cuts, counts, bins, static_cast<uint8_t*>(codes), stride, missing);
@@ -1971,7 +1986,7 @@ void launch_narrow_codes(const void* src, uint32_t rows, uint32_t cols, uint32_t
                          uint32_t pad, void* dst, cudaStream_t stream) {
   const uint64_t total = uint64_t(rows) * s8;
   if (!total) return;
-  narrow_codes_kernel<<<grid_for(total, 256, 148 * 16), 256, 0, stream>>>(
+  narrow_codes_kernel<<<grid_for(total, 256, 16), 256, 0, stream>>>(
       static_cast<const uint16_t*>(src), rows, cols, s16, s8, uint8_t(pad), static_cast<uint8_t*>(dst));
   XGBB_CUDA(cudaGetLastError());
 }
@@ -1979,7 +1994,7 @@ void launch_narrow_codes(const void* src, uint32_t rows, uint32_t cols, uint32_t
 void launch_validate(const float* X, uint64_t n, unsigned int* flags, cudaStream_t stream) {
   if (!n) return;
   const bool aligned = (reinterpret_cast<uintptr_t>(X) & 15) == 0;
-  validate_kernel<<<grid_for(n / 4 + 1, 256, 148 * 8), 256, 0, stream>>>(
+  validate_kernel<<<grid_for(n / 4 + 1, 256, 8), 256, 0, stream>>>(
       aligned ? reinterpret_cast<const float4*>(X) : nullptr, X, n, flags);
   XGBB_CUDA(cudaGetLastError());
 }
@@ -1989,7 +2004,7 @@ void launch_gradients(int objective, const float* margins, const float* labels,
                       float2* pairs, MassAccum mass, cudaStream_t stream) {
   if (!rows) return;
   const int threads = 256;
-  dim3 grid(grid_for(rows, threads, 148 * 4), groups);
+  dim3 grid(grid_for(rows, threads, 4), groups);
   gradient_kernel<<<grid, threads, 0, stream>>>(objective, margins, labels, weights, rows, groups,
                                                 spw, pairs, mass);
   XGBB_CUDA(cudaGetLastError());
@@ -1999,7 +2014,7 @@ void launch_mass_window(const float2* pairs, uint32_t rows, uint32_t groups, Mas
                         cudaStream_t stream) {
   if (!rows) return;
   const int threads = 256;
-  dim3 grid(grid_for(rows, threads, 148 * 4), groups);
+  dim3 grid(grid_for(rows, threads, 4), groups);
   mass_window_kernel<<<grid, threads, 0, stream>>>(pairs, rows, mass);
   XGBB_CUDA(cudaGetLastError());
 }
@@ -2014,7 +2029,7 @@ void launch_mass_exact(const float2* pairs, uint32_t rows, uint32_t groups, Mass
                        cudaStream_t stream) {
   if (!rows) return;
   const int threads = 256;
-  dim3 grid(grid_for(rows, threads, 148 * 4), groups);
+  dim3 grid(grid_for(rows, threads, 4), groups);
   mass_exact_kernel<<<grid, threads, 0, stream>>>(pairs, rows, mass);
   XGBB_CUDA(cudaGetLastError());
 }

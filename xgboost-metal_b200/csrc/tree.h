@@ -90,6 +90,9 @@ struct TreeLaunch {
   uint32_t f_lo, f_hi;       // features whose splits this rank evaluates
 };
 
+// Streaming multiprocessors of the current device (queried once per device).
+int device_sms();
+
 // Launch helpers (tree.cu). All are asynchronous on `stream`.
 void launch_narrow_codes(const void* src, uint32_t rows, uint32_t cols, uint32_t s16, uint32_t s8,
                          uint32_t pad, void* dst, cudaStream_t stream);
