@@ -27,7 +27,7 @@ def harness(tmp_path_factory):
     return lib
 
 
-def _parallel(lib, X, max_bin, weights=None, chunk=64):
+def _parallel(lib, X, max_bin, weights=None, chunk=64, segments=1, tree=0):
     X = np.ascontiguousarray(X, np.float32)
     rows, cols = X.shape
     stride = max(1, min(max_bin, rows))
@@ -37,22 +37,29 @@ def _parallel(lib, X, max_bin, weights=None, chunk=64):
     w = None if weights is None else np.ascontiguousarray(weights, np.float32)
     p = lambda a: None if a is None else a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
     u32 = ctypes.c_uint32
-    serial = np.zeros(3, np.uint64)
-    assert lib.sketch_harness(p(X), u32(rows), u32(cols), p(w), u32(max_bin), u32(chunk), p(cuts), p(counts),
-                              p(minima), p(serial)) == 0
+    serial = np.zeros(5, np.uint64)
+    assert lib.sketch_harness(p(X), u32(rows), u32(cols), p(w), u32(max_bin), u32(chunk), u32(segments), u32(tree),
+                              p(cuts), p(counts), p(minima), p(serial)) == 0
     return cuts, counts, minima, serial
+
+
+# (segments, tree): the single pass with the level-by-level reduction, and the
+# GPU's forms: rows in segments linked afterwards, and the merge tree.
+MODES = [(1, 0), (3, 1), (7, 1)]
 
 
 def _same(lib, X, max_bin, weights=None, chunk=64, serial_prefix=False):
     want = P.sketch(X, max_bin, weights)
-    got = _parallel(lib, X, max_bin, weights, chunk)
-    np.testing.assert_array_equal(got[1], want[1])
-    np.testing.assert_array_equal(got[0].view(np.uint32), want[0].view(np.uint32))
-    np.testing.assert_array_equal(got[2].view(np.uint32), want[2].view(np.uint32))
-    # The data-parallel prune and combine ran throughout; batch prefix sums
-    # are serial only for non-integer weights.
-    assert got[3][0] == 0 and got[3][1] == 0, got[3]
-    assert (got[3][2] > 0) == serial_prefix, got[3]
+    for segments, tree in MODES:
+        got = _parallel(lib, X, max_bin, weights, chunk, segments, tree)
+        msg = "segments %d tree %d" % (segments, tree)
+        np.testing.assert_array_equal(got[1], want[1], err_msg=msg)
+        np.testing.assert_array_equal(got[0].view(np.uint32), want[0].view(np.uint32), err_msg=msg)
+        np.testing.assert_array_equal(got[2].view(np.uint32), want[2].view(np.uint32), err_msg=msg)
+        # The data-parallel prune and combine ran throughout; batch prefix sums
+        # are serial only for non-integer weights.
+        assert got[3][0] == 0 and got[3][1] == 0, (msg, got[3])
+        assert (got[3][2] > 0) == serial_prefix, (msg, got[3])
     return want
 
 
@@ -112,3 +119,38 @@ def test_few_rows(harness):
         X = rng.normal(size=(rows, 3)).astype(np.float32)
         X[0, 0] = np.nan
         _same(harness, X, 256, chunk=2)
+
+
+def test_merge_tree_takes_distinct_values_and_hands_ties_to_the_serial_reduction(harness):
+    """Continuous features over many batches reduce through the merge tree
+    (every merge of two summaries overflows the limit); a feature with few
+    distinct values does not, and takes the level-by-level reduction. Both
+    give the host sketch's cuts."""
+    rng = np.random.default_rng(5)
+    X = rng.normal(size=(60000, 3)).astype(np.float32)
+    X[:, 2] = rng.integers(0, 20, 60000)
+    X[rng.random(X.shape) < 0.05] = np.nan
+    want = P.sketch(X, 8)
+    got = _parallel(harness, X, 8, chunk=512, segments=5, tree=1)
+    np.testing.assert_array_equal(got[1], want[1])
+    np.testing.assert_array_equal(got[0].view(np.uint32), want[0].view(np.uint32))
+    assert got[3][3] == 2 and got[3][4] == 1, got[3]
+
+
+def test_segments_link_runs_spanning_many_segments(harness):
+    """A run that spans whole segments, with unit and with float weights (the
+    weighted continuation is summed row by row as the single pass does)."""
+    rng = np.random.default_rng(6)
+    n = 9000
+    X = np.zeros((n, 3), np.float32)
+    X[:, 0] = np.repeat(rng.normal(size=9), 1000)      # runs of 1000 rows
+    X[:, 1] = np.where(np.arange(n) < 7000, 1.5, 2.5)  # one run over most segments
+    X[:, 2] = rng.normal(size=n)
+    X[rng.random(n) < 0.2, 1] = np.nan                 # the long run skips missing rows
+    w = (rng.random(n) * 2).astype(np.float32)
+    for weights in (None, w):
+        want = P.sketch(X, 16, weights)
+        for segments in (2, 9, 40):
+            got = _parallel(harness, X, 16, weights, chunk=128, segments=segments, tree=1)
+            np.testing.assert_array_equal(got[1], want[1])
+            np.testing.assert_array_equal(got[0].view(np.uint32), want[0].view(np.uint32))

@@ -223,23 +223,28 @@ XGBB_HD inline uint32_t upper_bound_by(uint32_t lo, uint32_t hi, float x, Key ke
   }
   return lo;
 }
-// First index j in [0, n) with e[j].value >= x.
-XGBB_HD inline uint32_t lower_bound_value(const Entry* e, uint32_t n, float x) {
-  uint32_t lo = 0, hi = n;
-  while (lo < hi) {
-    const uint32_t mid = lo + (hi - lo) / 2;
-    if (e[mid].value < x) lo = mid + 1;
-    else hi = mid;
-  }
-  return lo;
-}
 
-// Scratch of the parallel operations on up to `cap` entries.
+// Scratch of the parallel operations on up to `cap` entries. `fa` and `fb`
+// hold the keys the binary searches probe (rank sums, entry values); the
+// kernels place them in shared memory.
 struct Work {
   uint32_t* u;  // [cap + 1] per-index words
   uint32_t* v;  // [cap + 1]
   float* f;     // [cap + 1]
+  float* fa;    // [cap + 1]
+  float* fb;    // [cap + 1]
 };
+
+// First index j in [0, n) with v[j] >= x.
+XGBB_HD inline uint32_t lower_bound_f(const float* v, uint32_t n, float x) {
+  uint32_t lo = 0, hi = n;
+  while (lo < hi) {
+    const uint32_t mid = lo + (hi - lo) / 2;
+    if (v[mid] < x) lo = mid + 1;
+    else hi = mid;
+  }
+  return lo;
+}
 
 // prune_serial(in, size, capacity) written to `out` (may not alias `in`).
 template <class Ex>
@@ -254,9 +259,11 @@ XGBB_HD uint32_t prune_par(Ex& ex, const Entry* in, uint32_t size, uint32_t capa
   // The binary searches need non-decreasing rank sums s_j = rmax + rmin
   // (j >= 2) and query ranks (range >= 0); otherwise run the serial form.
   uint32_t* bad = w.v;
+  float* sums = w.fa;  // s_j, probed by the searches below
   ex.for_each(1, [&](uint32_t) { bad[0] = !(range >= 0.0f); });
   ex.for_each(size, [&](uint32_t j) {
     const float s = in[j].rmax + in[j].rmin;
+    sums[j] = s;
     if (s != s || (j >= 3 && s < in[j - 1].rmax + in[j - 1].rmin)) bad[0] = 1;
   });
   if (bad[0]) {
@@ -274,7 +281,7 @@ XGBB_HD uint32_t prune_par(Ex& ex, const Entry* in, uint32_t size, uint32_t capa
       return;
     }
     const float rank = 2.0f * (float(k) * range / float(n) + begin);
-    const uint32_t j = upper_bound_by(2, size, rank, [&](uint32_t t) { return in[t].rmax + in[t].rmin; });
+    const uint32_t j = upper_bound_by(2, size, rank, [&](uint32_t t) { return sums[t]; });
     const uint32_t i = j - 1;  // in [1, size - 1]
     if (i == size - 1) {
       chosen[k] = size;
@@ -336,17 +343,24 @@ XGBB_HD uint32_t combine_par(Ex& ex, const Entry* cur, uint32_t n, const Entry* 
     ex.for_each(1, [&](uint32_t) { result[0] = combine_serial(out, n, other, m, scratch); });
     return result[0];
   }
+  // The values both sides' searches probe.
+  float* va = w.fa;
+  float* vb = w.fb;
+  ex.for_each(n + m, [&](uint32_t i) {
+    if (i < n) va[i] = cur[i].value;
+    else vb[i - n] = other[i - n].value;
+  });
   // Matches: cur[a] equals other[lower_bound(a)].
   uint32_t* match_a = w.u;      // [n] 1 when cur[a] has an equal in other
   uint32_t* match_b = w.u + n;  // [m]
   ex.for_each(n + m, [&](uint32_t i) {
     if (i < n) {
-      const uint32_t b = lower_bound_value(other, m, cur[i].value);
-      match_a[i] = b < m && other[b].value == cur[i].value;
+      const uint32_t b = lower_bound_f(vb, m, va[i]);
+      match_a[i] = b < m && vb[b] == va[i];
     } else {
       const uint32_t b = i - n;
-      const uint32_t a = lower_bound_value(cur, n, other[b].value);
-      match_b[b] = a < n && cur[a].value == other[b].value;
+      const uint32_t a = lower_bound_f(va, n, vb[b]);
+      match_b[b] = a < n && va[a] == vb[b];
     }
   });
   ex.scan_exclusive(match_a, n, Add32{});
@@ -357,9 +371,9 @@ XGBB_HD uint32_t combine_par(Ex& ex, const Entry* cur, uint32_t n, const Entry* 
     if (i < n) {
       const uint32_t a = i;
       const Entry x = cur[a];
-      const uint32_t b = lower_bound_value(other, m, x.value);
+      const uint32_t b = lower_bound_f(vb, m, x.value);
       const uint32_t at = a + b - match_a[a];
-      if (b < m && other[b].value == x.value) {
+      if (b < m && vb[b] == x.value) {
         const Entry y = other[b];
         scratch[at] = {x.rmin + y.rmin, x.rmax + y.rmax, x.wmin + y.wmin, x.value};
       } else {
@@ -370,8 +384,8 @@ XGBB_HD uint32_t combine_par(Ex& ex, const Entry* cur, uint32_t n, const Entry* 
     } else {
       const uint32_t b = i - n;
       const Entry y = other[b];
-      const uint32_t a = lower_bound_value(cur, n, y.value);
-      if (a < n && cur[a].value == y.value) return;  // written by its match
+      const uint32_t a = lower_bound_f(va, n, y.value);
+      if (a < n && va[a] == y.value) return;  // written by its match
       const uint32_t at = b + a - match_b[b];
       const float prev_a = a ? lower_next(cur[a - 1]) : 0.0f;
       const float up = a < n ? upper_prev(cur[a]) : tail_a;
@@ -486,6 +500,17 @@ XGBB_HD uint32_t summarize_par(Ex& ex, const Run* runs, uint32_t size, uint32_t 
 struct RunCarry {
   uint32_t has_prev, runs, elements, nonmissing;
   float prev, w;  // value and weight so far of the last run
+  float first;    // value of the first used row (set with has_prev)
+};
+
+// How runs_chunk writes a chunk's runs: `write` false only counts them (the
+// first pass over a segment of rows); run indices below `own_from` belong to
+// an earlier segment, and a weight for such a run goes to *cont_w instead.
+struct RunOut {
+  Run* runs;
+  bool write;
+  uint32_t own_from;
+  float* cont_w;
 };
 
 // Per-row scratch of a chunk of up to `cap` rows.
@@ -503,8 +528,9 @@ struct ChunkWork {
 // `load(i)` gives the (value, weight) of row i of the chunk; runs go to
 // runs[carry.runs ...]; `carry` is updated for the next chunk.
 template <class Ex, class Load>
-XGBB_HD void runs_chunk(Ex& ex, Load load, uint32_t n, bool unit, RunCarry& carry, Run* runs, ChunkWork c) {
+XGBB_HD void runs_chunk(Ex& ex, Load load, uint32_t n, bool unit, RunCarry& carry, RunOut out, ChunkWork c) {
   if (!n) return;
+  Run* runs = out.runs;
   ex.for_each(n, [&](uint32_t i) {
     float v, w;
     load(i, v, w);
@@ -552,11 +578,23 @@ XGBB_HD void runs_chunk(Ex& ex, Load load, uint32_t n, bool unit, RunCarry& carr
       acc = unit ? fminf(acc + 1.0f, 16777216.0f) : acc + c.w[j];
     }
     const uint32_t run = c.start[i] ? runs0 + c.rank[i] : runs0 - 1;
-    if (c.start[i]) runs[run].v = c.v[i];
-    runs[run].w = acc;
+    if (out.write) {
+      if (run < out.own_from) {
+        out.cont_w[0] = acc;
+      } else {
+        if (c.start[i]) runs[run].v = c.v[i];
+        runs[run].w = acc;
+      }
+    }
     if (j == n) c.last_w[0] = acc;
   });
   const uint32_t last = c.last[n - 1];
+  if (!has_prev && last) {
+    // The first used row of the chunk is the first of the rows so far.
+    ex.for_each(n, [&](uint32_t i) {
+      if (c.valid[i] && (i == 0 || c.last[i - 1] == 0)) carry.first = c.v[i];
+    });
+  }
   ex.for_each(1, [&](uint32_t) {
     carry.nonmissing += nonmissing;
     carry.elements += used;
@@ -567,6 +605,79 @@ XGBB_HD void runs_chunk(Ex& ex, Load load, uint32_t n, bool unit, RunCarry& carr
       carry.w = c.last_w[0];
     }
   });
+}
+
+template <class Ex, class Load>
+XGBB_HD void runs_chunk(Ex& ex, Load load, uint32_t n, bool unit, RunCarry& carry, Run* runs, ChunkWork c) {
+  runs_chunk(ex, load, n, unit, carry, RunOut{runs, true, 0u, nullptr}, c);
+}
+
+// ---------------------------------------------------------------------------
+// A feature's runs from segments of rows processed at the same time. Pass 1
+// counts each segment's runs from an empty carry (runs_chunk with write
+// false), keeping its RunCarry. link_segments then walks the segments in
+// order: it gives each segment the carry the single pass would reach at its
+// first row (the run count so far, the last used value and the weight of the
+// run still open there) and notes which segments continue the previous
+// segment's last run. Pass 2 writes every segment's runs from that carry; a
+// continuing run's weight lands in cont_w, and finish_links stores those
+// weights in segment order, so a run spanning several segments keeps the
+// weight of its last segment. The runs are those of the single pass.
+//
+// A continuation's weight is min(prev + count, 2^24) with unit weights. With
+// weights, a segment whose used rows all continue the previous run passes on
+// a float sum that the single pass forms row by row, so link_segments forms
+// it the same way from the segment's rows (`load_w(s, k, v, w)`: row k of
+// segment s; `rows_of(s)`: its row count).
+// ---------------------------------------------------------------------------
+struct SegmentLink {
+  RunCarry in;    // the carry at the segment's first row
+  uint32_t cont;  // 1 when the segment's first run continues the previous one
+  float cont_w;   // that run's weight after this segment (written by pass 2)
+};
+
+template <class LoadW, class RowsOf>
+XGBB_HD void link_segments(const RunCarry* pass1, uint32_t nseg, bool unit, SegmentLink* link, LoadW load_w,
+                           RowsOf rows_of, uint32_t* stats) {
+  RunCarry cur{0, 0, 0, 0, 0.0f, 0.0f, 0.0f};
+  for (uint32_t s = 0; s < nseg; ++s) {
+    const RunCarry& p = pass1[s];
+    link[s].in = cur;
+    link[s].cont = 0;
+    link[s].cont_w = 0.0f;
+    cur.elements += p.elements;
+    cur.nonmissing += p.nonmissing;
+    if (!p.has_prev) continue;  // no used row: the open run carries over
+    const bool cont = cur.has_prev && p.first == cur.prev;
+    link[s].cont = cont;
+    cur.runs += p.runs - (cont ? 1u : 0u);
+    if (cont && p.runs == 1) {
+      // Every used row of the segment extends the open run.
+      if (unit) {
+        cur.w = fminf(cur.w + p.w, 16777216.0f);
+      } else {
+        float acc = cur.w;
+        for (uint32_t k = 0, n = rows_of(s); k < n; ++k) {
+          float v, w;
+          load_w(s, k, v, w);
+          if (v == v && (float_bits(w) & 0x7fffffffu) != 0) acc = acc + w;
+        }
+        cur.w = acc;
+      }
+    } else {
+      cur.w = p.w;
+    }
+    cur.has_prev = 1;
+    cur.prev = p.prev;
+  }
+  stats[0] = cur.runs;
+  stats[1] = cur.elements;
+  stats[2] = cur.nonmissing;
+}
+
+XGBB_HD inline void finish_links(const SegmentLink* link, uint32_t nseg, Run* runs) {
+  for (uint32_t s = 0; s < nseg; ++s)
+    if (link[s].cont) runs[link[s].in.runs - 1].w = link[s].cont_w;
 }
 
 // ---------------------------------------------------------------------------
@@ -582,6 +693,26 @@ struct ReduceWork {
   Work w;            // 2 * limit + 2 words each
   uint32_t* size;    // [1]
 };
+
+// The end of a feature's reduction: the resident summary of every level
+// (`resident(level, count)`, count 0 when the level holds none) merged from
+// the lowest level up, each merge pruned to max(budget, limit), then pruned
+// to `budget` and turned into cuts; returns the cut count.
+template <class Ex, class Resident>
+XGBB_HD uint32_t finish_reduce(Ex& ex, uint32_t levels, uint32_t limit, uint32_t budget, uint32_t max_bin,
+                               ReduceWork r, Resident resident, float* cuts) {
+  uint32_t n = 0;
+  const uint32_t keep = budget > limit ? budget : limit;
+  for (uint32_t level = 0; level < levels; ++level) {
+    uint32_t m = 0;
+    const Entry* res = resident(level, m);
+    n = combine_par(ex, r.a, n, res, m, r.b, r.scratch, r.w);
+    n = prune_par(ex, r.b, n, keep, r.a, r.w);
+  }
+  n = prune_par(ex, r.a, n, budget, r.b, r.w);
+  ex.for_each(1, [&](uint32_t) { r.size[0] = select_cuts(r.b, n, max_bin, cuts); });
+  return r.size[0];
+}
 
 // summaries[k * limit ...] holds batch k's sizes[k] entries. Writes at most
 // max_bin cuts to `cuts` and returns their count.
@@ -607,15 +738,13 @@ XGBB_HD uint32_t reduce_feature(Ex& ex, const Entry* summaries, const uint32_t* 
     ex.for_each(n, [&](uint32_t i) { dst[i] = r.a[i]; });
     ex.for_each(1, [&](uint32_t) { r.counts[level] = n; });
   }
-  uint32_t n = 0;
-  const uint32_t keep = budget > limit ? budget : limit;
-  for (uint32_t level = 0; level < levels; ++level) {
-    n = combine_par(ex, r.a, n, r.resident + size_t(level) * limit, r.counts[level], r.b, r.scratch, r.w);
-    n = prune_par(ex, r.b, n, keep, r.a, r.w);
-  }
-  n = prune_par(ex, r.a, n, budget, r.b, r.w);
-  ex.for_each(1, [&](uint32_t) { r.size[0] = select_cuts(r.b, n, max_bin, cuts); });
-  return r.size[0];
+  return finish_reduce(
+      ex, levels, limit, budget, max_bin, r,
+      [&](uint32_t level, uint32_t& count) {
+        count = r.counts[level];
+        return static_cast<const Entry*>(r.resident + size_t(level) * limit);
+      },
+      cuts);
 }
 
 // Batches and levels of one feature (src/quantile.cpp:98-127): batches of
@@ -661,14 +790,19 @@ struct ReduceTask {
   uint32_t first_size, nbatch, limit, budget, levels, feature;
 };
 
+// Entries of the largest summary a reduction step holds.
+XGBB_HD inline uint32_t reduce_big(uint32_t limit, uint32_t budget) {
+  return 2 * (limit > budget ? limit : budget) + 2;
+}
+
 inline size_t reduce_work_bytes(uint32_t limit, uint32_t budget, uint32_t levels) {
-  const size_t big = 2 * size_t(limit > budget ? limit : budget) + 2;
-  const size_t bytes = (size_t(limit) * levels + 3 * big) * sizeof(Entry) + 3 * big * 4 + (size_t(levels) + 1) * 4;
+  const size_t big = reduce_big(limit, budget);
+  const size_t bytes = (size_t(limit) * levels + 3 * big) * sizeof(Entry) + 5 * big * 4 + (size_t(levels) + 1) * 4;
   return (bytes + 255) / 256 * 256;
 }
 
 XGBB_HD inline ReduceWork reduce_work_at(unsigned char* base, uint32_t limit, uint32_t budget, uint32_t levels) {
-  const uint32_t big = 2 * (limit > budget ? limit : budget) + 2;
+  const uint32_t big = reduce_big(limit, budget);
   ReduceWork r;
   r.resident = reinterpret_cast<Entry*>(base);
   r.a = r.resident + size_t(limit) * levels;
@@ -677,14 +811,16 @@ XGBB_HD inline ReduceWork reduce_work_at(unsigned char* base, uint32_t limit, ui
   r.w.u = reinterpret_cast<uint32_t*>(r.scratch + big);
   r.w.v = r.w.u + big;
   r.w.f = reinterpret_cast<float*>(r.w.v + big);
-  r.counts = reinterpret_cast<uint32_t*>(r.w.f + big);
+  r.w.fa = r.w.f + big;
+  r.w.fb = r.w.fa + big;
+  r.counts = reinterpret_cast<uint32_t*>(r.w.fb + big);
   r.size = r.counts + levels;
   return r;
 }
 
 // Bytes of one batch's scratch for batches of at most `cap` runs.
 inline size_t batch_scratch_bytes(uint32_t cap) {
-  const size_t bytes = size_t(pow2_ceil(cap)) * 8 + size_t(cap) * (sizeof(Run) + sizeof(Entry)) + 3 * (size_t(cap) + 2) * 4;
+  const size_t bytes = size_t(pow2_ceil(cap)) * 8 + size_t(cap) * (sizeof(Run) + sizeof(Entry)) + 5 * (size_t(cap) + 2) * 4;
   return (bytes + 255) / 256 * 256;
 }
 
@@ -696,6 +832,8 @@ XGBB_HD inline BatchWork batch_work_at(unsigned char* base, uint32_t cap) {
   bw.w.u = reinterpret_cast<uint32_t*>(bw.entries + cap);
   bw.w.v = bw.w.u + cap + 2;
   bw.w.f = reinterpret_cast<float*>(bw.w.v + cap + 2);
+  bw.w.fa = bw.w.f + cap + 2;
+  bw.w.fb = bw.w.fa + cap + 2;
   return bw;
 }
 
@@ -725,6 +863,127 @@ inline GroupPlan plan_group(const uint32_t* stats, uint32_t nf, uint32_t f0, uin
     g.work_bytes += reduce_work_bytes(p.limit, p.budget, p.levels);
   }
   return g;
+}
+
+// ---------------------------------------------------------------------------
+// The reduction as a tree of merges. reduce_feature inserts batch summaries
+// one by one: each is merged with the summary held at level 0, the result
+// (pruned to `limit`) with the one held at level 1, and so on, a binary
+// counter. Whenever every such merge yields more than `limit` entries, node
+// i of level l + 1 is prune(combine(node 2i + 1, node 2i), limit) over the
+// nodes of level l (node 2i + 1 the newer), the nodes left over at odd
+// counts are the summaries the counter holds at the end, and finish_reduce
+// over them gives the same cuts. All merges of a level run at once, across
+// features. A merge that yields `limit` entries or fewer marks its feature
+// irregular (the counter would have kept that result at its level); such a
+// feature takes reduce_feature instead, whose steps are then cheap.
+// ---------------------------------------------------------------------------
+struct MergeTask {
+  unsigned long long older_at, newer_at, out_at;  // entry offsets
+  uint32_t older_size, newer_size, out_size;       // size slots
+  uint32_t limit, local;                           // local: feature index within the group
+};
+struct FinishRes {
+  unsigned long long at;
+  uint32_t size_slot, present;
+};
+struct FinishTask {
+  uint32_t feature, local, limit, budget, levels, res_begin;
+  unsigned long long work_at;
+};
+struct TreePlan {
+  std::vector<std::vector<MergeTask>> levels;  // the merges of level 1, 2, ...
+  std::vector<FinishTask> finish;
+  std::vector<FinishRes> res;
+  uint64_t entries = 0;  // summary entries including the tree's nodes
+  uint32_t sizes = 0;    // size slots including the tree's nodes
+};
+
+inline TreePlan plan_tree(const GroupPlan& g) {
+  TreePlan t;
+  t.entries = g.summary_entries;
+  t.sizes = g.sizes;
+  for (uint32_t j = 0; j < g.reduce.size(); ++j) {
+    const ReduceTask& rt = g.reduce[j];
+    struct Node {
+      unsigned long long at;
+      uint32_t slot;
+    };
+    std::vector<Node> prev;
+    for (uint32_t k = 0; k < rt.nbatch; ++k)
+      prev.push_back({rt.summary_at + uint64_t(k) * rt.limit, rt.first_size + k});
+    std::vector<FinishRes> res(rt.levels, FinishRes{0, 0, 0});
+    uint32_t level = 0;
+    while (prev.size() >= 2) {
+      if (prev.size() & 1) res[level] = FinishRes{prev.back().at, prev.back().slot, 1};
+      if (t.levels.size() <= level) t.levels.resize(level + 1);
+      std::vector<Node> cur;
+      for (size_t i = 0; i + 1 < prev.size(); i += 2) {
+        const Node out{t.entries, t.sizes};
+        t.entries += rt.limit;
+        t.sizes += 1;
+        t.levels[level].push_back(MergeTask{prev[i].at, prev[i + 1].at, out.at, prev[i].slot, prev[i + 1].slot,
+                                            out.slot, rt.limit, j});
+        cur.push_back(out);
+      }
+      prev.swap(cur);
+      ++level;
+    }
+    if (prev.size() == 1) res[level] = FinishRes{prev[0].at, prev[0].slot, 1};
+    t.finish.push_back(FinishTask{rt.feature, j, rt.limit, rt.budget, rt.levels, uint32_t(t.res.size()), rt.work_at});
+    t.res.insert(t.res.end(), res.begin(), res.end());
+  }
+  return t;
+}
+
+// Scratch of one merge: the merged summary, the combine's unclamped
+// entries, and the per-index words (the searched keys come separately).
+struct MergeWork {
+  Entry* merged;
+  Entry* scratch;
+  Work w;
+};
+inline size_t merge_scratch_bytes(uint32_t big) {
+  return (size_t(big) * 2 * sizeof(Entry) + size_t(big) * 5 * 4 + 255) / 256 * 256;
+}
+XGBB_HD inline MergeWork merge_work_at(unsigned char* base, uint32_t big) {
+  MergeWork m;
+  m.merged = reinterpret_cast<Entry*>(base);
+  m.scratch = m.merged + big;
+  m.w.u = reinterpret_cast<uint32_t*>(m.scratch + big);
+  m.w.v = m.w.u + big;
+  m.w.f = reinterpret_cast<float*>(m.w.v + big);
+  m.w.fa = m.w.f + big;
+  m.w.fb = m.w.fa + big;
+  return m;
+}
+
+// One tree merge; sets irregular[task.local] when the combine keeps `limit`
+// entries or fewer.
+template <class Ex>
+XGBB_HD void merge_node(Ex& ex, const MergeTask& t, Entry* entries, uint32_t* sizes, uint32_t* irregular,
+                        MergeWork m) {
+  const uint32_t n = combine_par(ex, entries + t.newer_at, sizes[t.newer_size], entries + t.older_at,
+                                 sizes[t.older_size], m.merged, m.scratch, m.w);
+  const uint32_t kept = prune_par(ex, m.merged, n, t.limit, entries + t.out_at, m.w);
+  ex.for_each(1, [&](uint32_t) {
+    sizes[t.out_size] = kept;
+    if (n <= t.limit) irregular[t.local] = 1;
+  });
+}
+
+// A regular feature's cuts from the tree's left-over nodes.
+template <class Ex>
+XGBB_HD uint32_t finish_tree(Ex& ex, const FinishTask& t, const FinishRes* res, const Entry* entries,
+                             const uint32_t* sizes, uint32_t max_bin, ReduceWork r, float* cuts) {
+  return finish_reduce(
+      ex, t.levels, t.limit, t.budget, max_bin, r,
+      [&](uint32_t level, uint32_t& count) {
+        const FinishRes& x = res[t.res_begin + level];
+        count = x.present ? sizes[x.size_slot] : 0u;
+        return entries + x.at;
+      },
+      cuts);
 }
 
 }  // namespace sketch
