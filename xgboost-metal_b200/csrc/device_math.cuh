@@ -74,12 +74,4 @@ __device__ __forceinline__ bool valid_hessian(double H, const SplitMath& m) {
   return H > 0.0 && H >= m.min_child;
 }
 
-// Order-preserving map of a float gain to uint32 (-0 folded onto +0), so that
-// a 64-bit max over (gain << 32 | ~feature) picks the largest gain and, among
-// equal gains, the smallest feature.
-__device__ __forceinline__ uint32_t gain_key(float g) {
-  uint32_t b = __float_as_uint(g == 0.0f ? 0.0f : g);
-  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-}
-
 }  // namespace xgbb

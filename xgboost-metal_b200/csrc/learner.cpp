@@ -17,6 +17,7 @@
 #include "json.h"
 #include "metrics.h"
 #include "sketch.h"
+#include "split_select.h"
 
 namespace xgbb {
 
@@ -893,7 +894,8 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp, bo
   // the features padded to a multiple of the ranks so that a reduce-scatter
   // hands every rank whole features.
   const uint32_t world = uint32_t(Comm::get().world());
-  ts->cols_pad = (C + world - 1) / world * world;
+  uint32_t lo, hi;
+  rank_features(C, world, uint32_t(Comm::get().rank()), &ts->cols_pad, &lo, &hi);
   ts->built.resize(size_t(max_pairs_at(D - 1)) * hist_node_bytes(e, ts->cols_pad));
   if (world > 1) {
     ts->best_mine.resize(size_t(kMaxFrontier) * best_record_bytes());
@@ -1149,10 +1151,8 @@ void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s, b
   // Each rank evaluates the splits of its own feature range; one GPU evaluates
   // them all.
   const uint32_t world = uint32_t(comm.world()), rank = uint32_t(comm.rank());
-  tl.cols_pad = ts.cols_pad;
-  const uint32_t per_rank = ts.cols_pad / world;
-  tl.f_lo = std::min(rank * per_rank, d.ell.cols);
-  tl.f_hi = std::min((rank + 1) * per_rank, d.ell.cols);
+  rank_features(d.ell.cols, world, rank, &tl.cols_pad, &tl.f_lo, &tl.f_hi);
+  const uint32_t per_rank = tl.cols_pad / world;
   tree_init(ws, tl, s);
   for (uint32_t depth = 0; depth < D; ++depth) {
     if (profiling) mark(ts.events[((size_t(parity) * ts.groups + g) * D + depth) * 2]);

@@ -19,6 +19,7 @@
 #include <algorithm>
 
 #include "device_math.cuh"
+#include "split_select.h"
 #include "tree.h"
 
 namespace xgbb {
@@ -1385,9 +1386,7 @@ __global__ void __launch_bounds__(256) eval_kernel(EvalArgs a) {
         r.left_g = r.left_hs = r.right_g = r.right_hs = 0;
       }
       a.cand[size_t(slot) * C + f] = r;
-      const unsigned long long key =
-          ((unsigned long long)gain_key(r.gain) << 32) | (0xffffffffu - f);
-      atomicMax(a.keys + slot, key);
+      atomicMax(a.keys + slot, split_key(r.gain, f));
     }
   }
 }
@@ -1551,7 +1550,7 @@ __global__ void pack_best_kernel(const unsigned long long* keys, const DevSplit*
   for (uint32_t s = threadIdx.x; s < kMaxFrontier; s += blockDim.x) {
     BestRecord r;
     r.key = keys[s];
-    const uint32_t f = 0xffffffffu - uint32_t(r.key & 0xffffffffu);
+    const uint32_t f = key_feature(r.key);
     if (r.key && f < cols) r.split = cand[size_t(s) * cols + f];
     else r = BestRecord{};
     out[s] = r;
@@ -1562,17 +1561,11 @@ __global__ void merge_best_kernel(const DriverState* state, const BestRecord* al
                                   uint32_t cols, unsigned long long* keys, DevSplit* cand) {
   const uint32_t n = state->frontier;
   for (uint32_t s = threadIdx.x; s < n; s += blockDim.x) {
-    uint32_t best = 0;
-    unsigned long long key = all[s].key;
-    for (uint32_t r = 1; r < ranks; ++r) {
-      const unsigned long long k = all[size_t(r) * kMaxFrontier + s].key;
-      if (k > key) {
-        key = k;
-        best = r;
-      }
-    }
+    unsigned long long key;
+    const uint32_t best =
+        merge_rank_keys(ranks, [&](uint32_t r) { return all[size_t(r) * kMaxFrontier + s].key; }, &key);
     keys[s] = key;
-    const uint32_t f = 0xffffffffu - uint32_t(key & 0xffffffffu);
+    const uint32_t f = key_feature(key);
     if (key && f < cols) cand[size_t(s) * cols + f] = all[size_t(best) * kMaxFrontier + s].split;
   }
 }
