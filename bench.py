@@ -469,6 +469,25 @@ def ncu_traffic(wl):
 
 
 # ---------------------------------------------------------------------------
+def probe_shared_pipe():
+    """SM cycles per warp-level shared instruction for each probe variant, at
+    16 and 32 warps per SM: the throughput figures behind the histogram
+    kernels' limb scheme."""
+    import ctypes
+    import xgboost as xgb  # noqa: F401
+    from xgboost import core
+    names = {0: "red.shared.add.s32 x4", 1: "red.shared.add.s32 x1", 2: "st.shared.b32 x4",
+             3: "atom.shared.add.u64 x2"}
+    out = {"probe": "shared_pipe", "unit": "SM cycles per warp instruction", "variants": {}}
+    for v, name in names.items():
+        for warps in (16, 32):
+            c = ctypes.c_double()
+            core._check_call(core._LIB.XGBBProbeSharedPipe(ctypes.c_int(v), ctypes.c_uint32(warps),
+                                                           ctypes.c_uint32(2000), ctypes.byref(c)))
+            out["variants"]["%s, %d warps" % (name, warps)] = round(c.value, 3)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -479,7 +498,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--rows", type=int, default=0,
                     help="override the row count (small profiling cases only; not a bench line)")
+    ap.add_argument("--probe", action="store_true",
+                    help="measure the shared-memory pipe (XGBBProbeSharedPipe) instead of training")
     args = ap.parse_args()
+    if args.probe:
+        print(json.dumps(probe_shared_pipe()), flush=True)
+        return
     assert args.warmup >= 3, "at least 3 warm-up rounds"
     dist = Dist()
     wl = args.workload

@@ -61,6 +61,13 @@ XGB_DLL int XGBBSketchHost(const float* X, bst_ulong rows, bst_ulong cols, const
  * results land in the host arrays as for XGBBSketchHost, bit for bit. */
 XGB_DLL int XGBBSketchDevice(const float* X, bst_ulong rows, bst_ulong cols, const float* weights,
                              uint32_t max_bin, float* cuts, uint32_t* counts, float* minima);
+/* No counterpart in the reference (a measurement of this hardware): SM
+ * cycles per warp-level shared-memory instruction when `warps` warps of one
+ * block per SM each run `iters` passes of 32 feature steps with the histogram
+ * kernels' conflict-free addressing. variant 0: red.shared.add.s32, 4 per
+ * code; 1: red.shared.add.s32, 1 per code; 2: st.shared.b32, 4 per code;
+ * 3: atom.shared.add.u64, 2 per code. */
+XGB_DLL int XGBBProbeSharedPipe(int variant, uint32_t warps, uint32_t iters, double* cycles);
 /* One evaluation metric of transformed predictions [rows][groups] (the
  * metric side of XGBoosterEvalOneIter, src/metrics.cpp:8-158); weights may
  * be NULL. Needs no GPU. */

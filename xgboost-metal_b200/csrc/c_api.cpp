@@ -989,7 +989,8 @@ XGB_DLL int XGBoosterGetCudaProfile(BoosterHandle handle, char const** out) {
     results.str = "{\"hist_ms\":" + std::to_string(p.hist_ms) +
                   ",\"hist_bytes\":" + std::to_string(p.hist_bytes) +
                   ",\"hist_launches\":" + std::to_string(p.hist_launches) +
-                  ",\"rounds\":" + std::to_string(p.rounds) + ",\"levels\":[";
+                  ",\"rounds\":" + std::to_string(p.rounds) + ",\"csr\":" + (p.csr ? "true" : "false") +
+                  ",\"levels\":[";
     for (uint32_t d = 0; d < xgbb::kMaxDepth; ++d) {
       if (d) results.str += ",";
       results.str += "[" + std::to_string(p.level_ms[d]) + "," + std::to_string(p.level_rows[d]) + "," +
@@ -1121,6 +1122,16 @@ XGB_DLL int XGBBSketchDevice(const float* X, bst_ulong rows, bst_ulong cols, con
       throw;
     }
     cudaStreamDestroy(s);
+  });
+}
+
+// Measurement entry: SM cycles per warp-level shared instruction of a probe
+// variant (probe.cu), for sizing the histogram kernels' limb scheme.
+XGB_DLL int XGBBProbeSharedPipe(int variant, uint32_t warps, uint32_t iters, double* cycles) {
+  return guarded([&] {
+    ensure_device();
+    xgbb::require(cycles != nullptr, "Null output.");
+    *cycles = xgbb::probe_shared_pipe(variant, warps, iters);
   });
 }
 

@@ -212,6 +212,7 @@ void DMatrix::build_sparse_rows(cudaStream_t stream) {
   DeviceBuffer tile_sums((size_t(rows) / 4096 + 1) * 8);
   const uint64_t nnz =
       queue_csr_row_ptr(ell, sparse_ptr.as<unsigned long long>(), tile_sums.as<unsigned long long>(), stream);
+  sparse_nnz = nnz;
   sparse_entries.resize(std::max<size_t>(nnz, 1) * 4);
   queue_csr_fill(ell, sparse_ptr.as<unsigned long long>(), sparse_entries.as<uint32_t>(), stream);
   XGBB_CUDA(cudaStreamSynchronize(stream));
@@ -386,6 +387,9 @@ struct Booster::TrainState {
   // batch descriptors, and pinned landing buffers for the host's reads.
   DeviceBuffer q_order, q_scratch, q_built, q_cand, q_keys, q_sums, q_seg, q_items, q_cursor, q_best, q_nodes,
       q_totals;
+  // Level histograms from the rows' present codes (sparse matrices).
+  bool csr = false;
+  DeviceBuffer csr_totals;
   uint32_t q_slots = 0;
   NodeBest* q_best_host = nullptr;   // pinned [kMaxFrontier]
   uint32_t* q_cursor_host = nullptr; // pinned [2 * kQueueBatch]
@@ -861,6 +865,22 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp, bo
     XGBB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ts->q_sums_host), 2 * size_t(kMaxFrontier) * 8));
     XGBB_CUDA(cudaEventCreateWithFlags(&ts->q_done, cudaEventDisableTiming));
   }
+  // Sparse matrices build the level histograms from the rows' present codes
+  // when at most a quarter of the cells hold a value (cuda_csr_hist: -1
+  // decides so, 0 never, 1 always); the results are the same.
+  const long csr_mode = integer(params_, "cuda_csr_hist", -1);
+  if (!host_driven_ && csr_mode != 0 && (csr_mode == 1 || d.has_missing) && C <= 0x10000u && n) {
+    d.build_sparse_rows(stream_);
+    const double density = double(d.sparse_nnz) / (double(n) * C);
+    ts->csr = csr_mode == 1 || density <= 0.25;
+    if (ts->csr) {
+      ts->csr_totals.resize(size_t(kMaxFrontier) * 16);
+    } else {
+      d.sparse_ptr.release();
+      d.sparse_entries.release();
+      d.sparse_ready = false;
+    }
+  }
   ts->margins.resize(std::max<size_t>(size_t(n) * G, 1) * 4);
   ts->pairs.resize(std::max<size_t>(size_t(n) * G, 1) * 8);
   ts->mass.resize(mass_bytes(G));
@@ -1152,6 +1172,11 @@ void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s, b
   // them all.
   const uint32_t world = uint32_t(comm.world()), rank = uint32_t(comm.rank());
   rank_features(d.ell.cols, world, rank, &tl.cols_pad, &tl.f_lo, &tl.f_hi);
+  if (ts.csr) {
+    tl.csr_ptr = d.sparse_ptr.as<unsigned long long>();
+    tl.csr_entries = d.sparse_entries.as<uint32_t>();
+    tl.csr_totals = ts.csr_totals.as<unsigned long long>();
+  }
   const uint32_t per_rank = tl.cols_pad / world;
   tree_init(ws, tl, s);
   for (uint32_t depth = 0; depth < D; ++depth) {
@@ -1308,6 +1333,7 @@ void Booster::run_round(TrainState& ts, const CustomGradients* custom) {
                   ts.host_level_nodes[b], stream_);
   }
   XGBB_CUDA(cudaEventRecord(ts.copied[b], stream_));
+  profile.csr = ts.csr;
   ++rounds_;
   ts.margin_rounds = rounds_;
   ts.parity ^= 1u;

@@ -87,6 +87,7 @@ class DMatrix {
   // Sparse rows of the codes (present codes only, feature << 16 | code),
   // made on first use for sparse node histograms.
   DeviceBuffer sparse_ptr, sparse_entries;
+  uint64_t sparse_nnz = 0;
   bool sparse_ready = false;
   void build_sparse_rows(cudaStream_t stream);
 
@@ -105,6 +106,7 @@ struct HostTree {
 };
 
 struct Profile {
+  bool csr = false;  // the level histograms came from the rows' present codes
   double hist_ms = 0, total_ms = 0;
   double hist_bytes = 0;
   uint64_t hist_launches = 0, kernel_launches = 0, rounds = 0;

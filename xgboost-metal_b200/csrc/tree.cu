@@ -73,11 +73,27 @@ __device__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* total) {
 // ---------------------------------------------------------------------------
 // Binning.
 // ---------------------------------------------------------------------------
+// With `staged`, every feature's cuts and counts are first copied into
+// shared memory (cols * bins + cols words), so the binary searches of a
+// row's features, which touch as many cut arrays as the row has features,
+// read shared memory instead of thrashing L1.
 template <typename CodeT>
 __global__ void quantize_kernel(const float* __restrict__ X, uint32_t rows, uint32_t cols,
-                                const float* __restrict__ cuts, const uint32_t* __restrict__ counts,
+                                const float* __restrict__ cuts_g, const uint32_t* __restrict__ counts_g,
                                 uint32_t bins, CodeT* __restrict__ codes, uint32_t stride,
-                                uint32_t missing) {
+                                uint32_t missing, bool staged) {
+  extern __shared__ float staged_cuts[];
+  const float* cuts = cuts_g;
+  const uint32_t* counts = counts_g;
+  if (staged) {
+    const uint32_t n = cols * bins;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) staged_cuts[i] = cuts_g[i];
+    uint32_t* sc = reinterpret_cast<uint32_t*>(staged_cuts + n);
+    for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) sc[i] = counts_g[i];
+    __syncthreads();
+    cuts = staged_cuts;
+    counts = sc;
+  }
   const uint64_t total = uint64_t(rows) * stride;
   for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < total;
        i += uint64_t(gridDim.x) * blockDim.x) {
@@ -91,7 +107,7 @@ __global__ void quantize_kernel(const float* __restrict__ X, uint32_t rows, uint
         uint32_t lo = 0, hi = count;
         while (lo < hi) {
           const uint32_t mid = (lo + hi) >> 1;
-          if (v >= __ldg(fc + mid)) lo = mid + 1;
+          if (v >= fc[mid]) lo = mid + 1;
           else hi = mid;
         }
         code = lo < count - 1 ? lo : count - 1;
@@ -1636,26 +1652,38 @@ __global__ void __launch_bounds__(kPartThreads) partition_kernel(PartArgs a) {
       rows[k] = valid ? (a.root ? begin + i : a.rows[begin + i]) : 0u;
       valid_bits |= uint32_t(valid) << k;
     }
+    // All of a lane's split codes are loaded before any is used, and all of
+    // its margins before any is stored, so the random reads of a deep level
+    // are in flight together.
+    uint32_t code[kPartIter];
 #pragma unroll
     for (uint32_t k = 0; k < kPartIter; ++k) {
-      if (!((valid_bits >> k) & 1u)) continue;
-      const uint32_t row = rows[k];
-      if (md == 0) {
-        float* m = a.margins + size_t(row) * a.groups + a.group;
-        *m = __fadd_rn(*m, leaf_l);
-        continue;
-      }
-      const uint32_t code = fm ? fm[size_t(node.feature) * a.e.rows + row]
-                               : codes[size_t(row) * a.e.stride + uint32_t(node.feature)];
-      const bool left = code == a.e.missing ? node.default_left != 0u : int32_t(code) <= node.split_bin;
-      if (md == 2) {
-        float* m = a.margins + size_t(row) * a.groups + a.group;
-        *m = __fadd_rn(*m, left ? leaf_l : leaf_r);
-      } else {
-        left_bits |= uint32_t(left) << k;
-      }
+      code[k] = 0;
+      if (md != 0 && ((valid_bits >> k) & 1u))
+        code[k] = fm ? fm[size_t(node.feature) * a.e.rows + rows[k]]
+                     : codes[size_t(rows[k]) * a.e.stride + uint32_t(node.feature)];
     }
-    if (md != 1) continue;  // uniform across the block
+#pragma unroll
+    for (uint32_t k = 0; k < kPartIter; ++k) {
+      const bool left = code[k] == a.e.missing ? node.default_left != 0u : int32_t(code[k]) <= node.split_bin;
+      left_bits |= uint32_t(left) << k;
+    }
+    if (md != 1) {
+      // A stopping node adds its leaf to every row's margin; a split at the
+      // last level adds the child's leaf.
+      float* m[kPartIter];
+      float v[kPartIter];
+#pragma unroll
+      for (uint32_t k = 0; k < kPartIter; ++k) {
+        m[k] = a.margins + size_t(rows[k]) * a.groups + a.group;
+        v[k] = ((valid_bits >> k) & 1u) ? *m[k] : 0.0f;
+      }
+#pragma unroll
+      for (uint32_t k = 0; k < kPartIter; ++k)
+        if ((valid_bits >> k) & 1u)
+          *m[k] = __fadd_rn(v[k], md == 0 ? leaf_l : (((left_bits >> k) & 1u) ? leaf_l : leaf_r));
+      continue;  // uniform across the block
+    }
     // Per-warp totals, then warp offsets within the tile and the tile's
     // positions in the two child blocks.
     uint32_t nl = 0, nr = 0;
@@ -1965,13 +1993,28 @@ void launch_quantize(const float* X, uint32_t rows, uint32_t cols, const float* 
                      uint32_t bytes_per_code, uint32_t missing, cudaStream_t stream) {
   const uint64_t total = uint64_t(rows) * stride;
   if (!total) return;
-  const int threads = 256, blocks = grid_for(total, threads, 32);
+  constexpr size_t kStagedMax = 160 * 1024;
+  const size_t smem = (size_t(cols) * bins + cols) * 4;
+  const bool staged = smem <= kStagedMax;
+  static bool configured = false;
+  if (!configured) {
+    XGBB_CUDA(cudaFuncSetAttribute(quantize_kernel<uint8_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   int(kStagedMax)));
+    XGBB_CUDA(cudaFuncSetAttribute(quantize_kernel<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   int(kStagedMax)));
+    configured = true;
+  }
+  // Staged: one 1024-thread block per SM walks the values; otherwise many
+  // small blocks.
+  const int threads = staged ? 1024 : 256;
+  const int blocks = staged ? int(std::min<uint64_t>(device_sms(), (total + threads - 1) / threads))
+                            : grid_for(total, threads, 32);
   if (bytes_per_code == 1)
-    quantize_kernel<uint8_t><<<blocks, threads, 0, stream>>>(
-        X, rows, cols, cuts, counts, bins, static_cast<uint8_t*>(codes), stride, missing);
+    quantize_kernel<uint8_t><<<blocks, threads, staged ? smem : 0, stream>>>(
+        X, rows, cols, cuts, counts, bins, static_cast<uint8_t*>(codes), stride, missing, staged);
   else
-    quantize_kernel<uint16_t><<<blocks, threads, 0, stream>>>(
-        X, rows, cols, cuts, counts, bins, static_cast<uint16_t*>(codes), stride, missing);
+    quantize_kernel<uint16_t><<<blocks, threads, staged ? smem : 0, stream>>>(
+        X, rows, cols, cuts, counts, bins, static_cast<uint16_t*>(codes), stride, missing, staged);
   XGBB_CUDA(cudaGetLastError());
 }
 
@@ -2092,10 +2135,144 @@ void tree_init(const TreeWorkspace& ws, const TreeLaunch& tl, cudaStream_t strea
   XGBB_CUDA(cudaGetLastError());
 }
 
+namespace {
+// Histograms of the built children from each row's present codes, for a
+// sparse matrix (the reference's histogram_csr_accumulate,
+// kernels/histogram_csr.metal.h:22-114): blocks take tiles of built rows;
+// every present (feature, code) of a row adds the row's exact (g, h) with
+// 64-bit global atomics, and each tile adds its rows' (g, h) sums to its
+// node's totals. csr_missing_kernel then sets each built node's missing bin
+// to the node total minus its present bins, mod 2^64
+// (histogram_csr_finalize_missing, :117-152). Both are linear in the rows,
+// so on several GPUs each rank's local histograms still sum to the global
+// ones in the reduce-scatter.
+struct CsrLevelArgs {
+  const unsigned long long* row_ptr;  // [rows + 1]
+  const uint32_t* entries;            // feature << 16 | code, present codes only
+  const float2* pairs;                // this group's gradient pairs in row order
+  const float2* scale;
+  const uint32_t* rows;
+  const DriverState* state;
+  const uint32_t* tile_offset;
+  const uint32_t* built_left;
+  const uint32_t* seg_begin;
+  const uint32_t* seg_count;
+  longlong2* built;                   // [cols_pad][pair_stride][bins + 1]
+  unsigned long long* totals;         // [pairs][2]
+  uint32_t pair_stride, bins, cols;
+  bool root;
+};
+constexpr int kCsrThreads = 256;
+
+__global__ void __launch_bounds__(kCsrThreads) csr_level_hist_kernel(CsrLevelArgs a) {
+  __shared__ unsigned long long tot[2];
+  const DriverState st = *a.state;
+  if (!st.frontier || !st.total_tiles) return;
+  const uint32_t npairs = a.root ? 1u : st.pairs;
+  const float2 sc = *a.scale;
+  const uint32_t B1 = a.bins + 1;
+  for (uint32_t t = blockIdx.x; t < st.total_tiles; t += gridDim.x) {
+    uint32_t pair = 0;
+    if (!a.root) {
+      uint32_t lo = 0, hi = npairs;
+      while (hi - lo > 1) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (a.tile_offset[mid] <= t) lo = mid;
+        else hi = mid;
+      }
+      pair = lo;
+    }
+    const uint32_t slot = a.root ? 0u : 2u * pair + (a.built_left[pair] ? 0u : 1u);
+    const uint32_t seg0 = a.seg_begin[slot], segn = a.seg_count[slot];
+    const uint32_t begin = seg0 + (t - a.tile_offset[pair]) * kTileRows;
+    const uint32_t cnt = min(kTileRows, seg0 + segn - begin);
+    if (threadIdx.x < 2) tot[threadIdx.x] = 0;
+    __syncthreads();
+    unsigned long long sg = 0, sh = 0;
+    for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) {
+      const uint32_t row = a.root ? begin + i : a.rows[begin + i];
+      const float2 p = a.pairs[row];
+      const unsigned long long qg = (unsigned long long)__float2ll_rn(__fmul_rn(p.x, sc.x));
+      const unsigned long long qh = (unsigned long long)__float2ll_rn(__fmul_rn(p.y, sc.y));
+      sg += qg;
+      sh += qh;
+      for (unsigned long long k = a.row_ptr[row], e = a.row_ptr[row + 1]; k < e; ++k) {
+        const uint32_t x = a.entries[k], f = x >> 16, code = x & 0xffffu;
+        if (f >= a.cols || code >= a.bins) continue;
+        longlong2* dst = a.built + (size_t(f) * a.pair_stride + pair) * B1 + code;
+        atomicAdd(reinterpret_cast<unsigned long long*>(&dst->x), qg);
+        atomicAdd(reinterpret_cast<unsigned long long*>(&dst->y), qh);
+      }
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) {
+      sg += __shfl_down_sync(0xffffffffu, sg, d);
+      sh += __shfl_down_sync(0xffffffffu, sh, d);
+    }
+    if ((threadIdx.x & 31) == 0) {
+      atomicAdd(&tot[0], sg);
+      atomicAdd(&tot[1], sh);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      atomicAdd(&a.totals[2 * pair], tot[0]);
+      atomicAdd(&a.totals[2 * pair + 1], tot[1]);
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void csr_missing_kernel(const DriverState* state, bool root, longlong2* built,
+                                   const unsigned long long* totals, uint32_t pair_stride, uint32_t bins,
+                                   uint32_t cols) {
+  const DriverState st = *state;
+  if (!st.frontier || !st.total_tiles) return;
+  const uint32_t npairs = root ? 1u : st.pairs;
+  const uint64_t n = uint64_t(cols) * npairs;
+  for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < n; i += uint64_t(gridDim.x) * blockDim.x) {
+    const uint32_t f = uint32_t(i / npairs), p = uint32_t(i % npairs);
+    longlong2* h = built + (size_t(f) * pair_stride + p) * (bins + 1);
+    unsigned long long g = totals[2 * p], hh = totals[2 * p + 1];
+    for (uint32_t b = 0; b < bins; ++b) {
+      g -= (unsigned long long)h[b].x;
+      hh -= (unsigned long long)h[b].y;
+    }
+    h[bins].x = (long long)g;
+    h[bins].y = (long long)hh;
+  }
+}
+}  // namespace
+
 void tree_level_hist(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t depth,
                      cudaStream_t stream) {
   const size_t bytes = size_t(max_pairs_at(depth)) * hist_node_bytes(tl.ell, tl.cols_pad);
   XGBB_CUDA(cudaMemsetAsync(ws.built, 0, bytes, stream));
+  if (tl.csr_ptr) {
+    XGBB_CUDA(cudaMemsetAsync(tl.csr_totals, 0, size_t(max_pairs_at(depth)) * 16, stream));
+    CsrLevelArgs c;
+    c.row_ptr = tl.csr_ptr;
+    c.entries = tl.csr_entries;
+    c.pairs = tl.pairs;
+    c.scale = tl.scale;
+    c.rows = ws.rows[depth & 1];
+    c.state = ws.state;
+    c.tile_offset = ws.tile_offset;
+    c.built_left = ws.built_left;
+    c.seg_begin = ws.seg_begin[depth & 1];
+    c.seg_count = ws.seg_count[depth & 1];
+    c.built = ws.built;
+    c.totals = tl.csr_totals;
+    c.pair_stride = max_pairs_at(depth);
+    c.bins = tl.ell.bins;
+    c.cols = tl.ell.cols;
+    c.root = depth == 0;
+    csr_level_hist_kernel<<<device_sms() * 8, kCsrThreads, 0, stream>>>(c);
+    XGBB_CUDA(cudaGetLastError());
+    csr_missing_kernel<<<grid_for(uint64_t(tl.ell.cols) * c.pair_stride, 256), 256, 0, stream>>>(
+        ws.state, c.root, ws.built, tl.csr_totals, c.pair_stride, tl.ell.bins, tl.ell.cols);
+    XGBB_CUDA(cudaGetLastError());
+    return;
+  }
   HistArgs a;
   a.e = tl.ell;
   a.pairs = depth == 0 ? tl.pairs : ws.ord[depth & 1];

@@ -88,10 +88,19 @@ struct TreeLaunch {
   size_t hist_smem;
   uint32_t cols_pad;         // features in the built layout (a multiple of the ranks)
   uint32_t f_lo, f_hi;       // features whose splits this rank evaluates
+  // Sparse matrices: the rows' present codes (row pointers and
+  // feature << 16 | code entries) and the built nodes' totals [pairs][2];
+  // csr_ptr null builds histograms from the dense codes.
+  const unsigned long long* csr_ptr = nullptr;
+  const uint32_t* csr_entries = nullptr;
+  unsigned long long* csr_totals = nullptr;
 };
 
 // Streaming multiprocessors of the current device (queried once per device).
 int device_sms();
+// SM cycles per warp-level shared-memory instruction of one probe variant
+// (probe.cu) on the current device.
+double probe_shared_pipe(int variant, uint32_t warps, uint32_t iters);
 
 // Launch helpers (tree.cu). All are asynchronous on `stream`.
 void launch_narrow_codes(const void* src, uint32_t rows, uint32_t cols, uint32_t s16, uint32_t s8,
