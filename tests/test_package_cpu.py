@@ -25,14 +25,12 @@ def test_reference_package_names_exist():
     for name in ("DMatrix", "QuantileDMatrix", "ExtMemQuantileDMatrix", "Booster", "DataIter", "train",
                  "cv", "build_info", "plot_importance", "plot_tree", "to_graphviz", "set_config",
                  "get_config", "config_context", "XGBModel", "XGBClassifier", "XGBRegressor",
-                 "XGBRanker", "XGBRFClassifier", "XGBRFRegressor", "collective", "RabitTracker"):
+                 "XGBRanker", "XGBRFClassifier", "XGBRFRegressor", "collective"):
         assert hasattr(xgboost, name), name
     with pytest.raises(xgb.XGBoostError, match="Ranking"):
         xgb.XGBRanker().fit([[0.0]], [0.0])
     with pytest.raises(xgb.XGBoostError, match="Random forests"):
         xgb.XGBRFRegressor().fit([[0.0]], [0.0])
-    with pytest.raises(xgb.XGBoostError, match="unique_id"):
-        xgb.RabitTracker(2)
     with pytest.raises(TypeError):
         xgb.ExtMemQuantileDMatrix([[1.0]])
 

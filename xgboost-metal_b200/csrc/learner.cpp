@@ -115,9 +115,14 @@ void DMatrix::set_cuts(std::shared_ptr<Cuts> c, cudaStream_t stream) {
   if (!decided) narrow = false;
   code_layout(ell, cols, B, max_count, narrow);
   codes.resize(std::max<size_t>(size_t(rows) * ell.stride * ell.bytes_per_code, 16));
+  // The binning kernels count the NaN cells, which decides later whether the
+  // level histograms come from the rows' present codes.
+  DeviceBuffer d_missing(8);
+  unsigned long long h_missing = 0;
+  XGBB_CUDA(cudaMemsetAsync(d_missing.get(), 0, 8, stream));
   if (rows && d_data) {
     launch_quantize(d_data.as<float>(), rows, cols, ell.cuts, ell.counts, ell.bins, codes.get(), ell.stride,
-                    ell.bytes_per_code, ell.missing, stream);
+                    ell.bytes_per_code, ell.missing, d_missing.as<unsigned long long>(), stream);
   } else if (rows) {
     // Stream the host matrix through two staging buffers: the copy of one
     // chunk overlaps the validation and quantisation of the other, and the
@@ -153,7 +158,7 @@ void DMatrix::set_cuts(std::shared_ptr<Cuts> c, cudaStream_t stream) {
         launch_validate(stage[b].as<float>(), uint64_t(n) * cols, flags.as<unsigned int>(), stream);
       launch_quantize(stage[b].as<float>(), n, cols, ell.cuts, ell.counts, ell.bins,
                       static_cast<char*>(codes.get()) + size_t(r0) * code_row, ell.stride,
-                      ell.bytes_per_code, ell.missing, stream);
+                      ell.bytes_per_code, ell.missing, d_missing.as<unsigned long long>(), stream);
       XGBB_CUDA(cudaEventRecord(consumed[b], stream));
     }
     unsigned int h[2] = {0, 0};
@@ -185,6 +190,9 @@ void DMatrix::set_cuts(std::shared_ptr<Cuts> c, cudaStream_t stream) {
       ell = n8;
     }
   }
+  XGBB_CUDA(cudaMemcpyAsync(&h_missing, d_missing.get(), 8, cudaMemcpyDeviceToHost, stream));
+  XGBB_CUDA(cudaStreamSynchronize(stream));
+  missing_cells = h_missing;
   ell.codes = codes.get();
   sparse_ready = false;
   sparse_ptr.release();
@@ -870,15 +878,11 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp, bo
   // decides so, 0 never, 1 always); the results are the same.
   const long csr_mode = integer(params_, "cuda_csr_hist", -1);
   if (!host_driven_ && csr_mode != 0 && (csr_mode == 1 || d.has_missing) && C <= 0x10000u && n) {
-    d.build_sparse_rows(stream_);
-    const double density = double(d.sparse_nnz) / (double(n) * C);
+    const double density = 1.0 - double(d.missing_cells) / (double(n) * C);
     ts->csr = csr_mode == 1 || density <= 0.25;
     if (ts->csr) {
+      d.build_sparse_rows(stream_);
       ts->csr_totals.resize(size_t(kMaxFrontier) * 16);
-    } else {
-      d.sparse_ptr.release();
-      d.sparse_entries.release();
-      d.sparse_ready = false;
     }
   }
   ts->margins.resize(std::max<size_t>(size_t(n) * G, 1) * 4);

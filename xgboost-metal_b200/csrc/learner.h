@@ -88,6 +88,7 @@ class DMatrix {
   // made on first use for sparse node histograms.
   DeviceBuffer sparse_ptr, sparse_entries;
   uint64_t sparse_nnz = 0;
+  uint64_t missing_cells = 0;  // NaN values among the rows, counted while binning
   bool sparse_ready = false;
   void build_sparse_rows(cudaStream_t stream);
 

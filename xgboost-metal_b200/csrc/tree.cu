@@ -81,7 +81,7 @@ template <typename CodeT>
 __global__ void quantize_kernel(const float* __restrict__ X, uint32_t rows, uint32_t cols,
                                 const float* __restrict__ cuts_g, const uint32_t* __restrict__ counts_g,
                                 uint32_t bins, CodeT* __restrict__ codes, uint32_t stride,
-                                uint32_t missing, bool staged) {
+                                uint32_t missing, bool staged, unsigned long long* missing_cells) {
   extern __shared__ float staged_cuts[];
   const float* cuts = cuts_g;
   const uint32_t* counts = counts_g;
@@ -95,6 +95,7 @@ __global__ void quantize_kernel(const float* __restrict__ X, uint32_t rows, uint
     counts = sc;
   }
   const uint64_t total = uint64_t(rows) * stride;
+  uint32_t absent = 0;  // cells of this thread without a value
   for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < total;
        i += uint64_t(gridDim.x) * blockDim.x) {
     const uint32_t r = uint32_t(i / stride), c = uint32_t(i % stride);
@@ -102,6 +103,7 @@ __global__ void quantize_kernel(const float* __restrict__ X, uint32_t rows, uint
     if (c < cols) {
       const float v = X[size_t(r) * cols + c];
       const uint32_t count = counts[c];
+      absent += isnan(v) ? 1u : 0u;
       if (!isnan(v) && count) {
         const float* fc = cuts + size_t(c) * bins;
         uint32_t lo = 0, hi = count;
@@ -115,6 +117,8 @@ __global__ void quantize_kernel(const float* __restrict__ X, uint32_t rows, uint
     }
     codes[i] = CodeT(code);
   }
+  const uint32_t warp_absent = __reduce_add_sync(0xffffffffu, absent);
+  if (missing_cells && (threadIdx.x & 31) == 0 && warp_absent) atomicAdd(missing_cells, warp_absent);
 }
 
 // Feature-major copy of the codes, [cols][rows], for the partition: the rows
@@ -756,6 +760,11 @@ __device__ __forceinline__ void cp_async_wait() {
 __device__ __forceinline__ void red_shared(uint32_t addr, int v) {
   asm volatile("red.shared.add.s32 [%0], %1;\n" ::"r"(addr), "r"(v));
 }
+// The same at a constant offset from addr (an immediate of the instruction).
+template <uint32_t kOff>
+__device__ __forceinline__ void red_shared_at(uint32_t addr, int v) {
+  asm volatile("red.shared.add.s32 [%0+%2], %1;\n" ::"r"(addr), "r"(v), "n"(kOff));
+}
 
 // Stage position of chunk c (16 bytes) of staged row r; see hist2_kernel.
 template <typename CodeT>
@@ -1141,9 +1150,9 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
         const uint32_t code = sizeof(CodeT) == 2 ? (w >> (16 * (f & 1))) & 0xffffu : (w >> (8 * (f & 3))) & 0xffu;
         const uint32_t addr = pbase + code * (kHistLanes * 4) + (lane4 ^ (4 * f));
         red_shared(addr, q.x);
-        red_shared(addr + kPlaneBytes, q.y);
-        red_shared(addr + 2 * kPlaneBytes, q.z);
-        if (!kUnitH) red_shared(addr + 3 * kPlaneBytes, q.w);
+        red_shared_at<kPlaneBytes>(addr, q.y);
+        red_shared_at<2 * kPlaneBytes>(addr, q.z);
+        if (!kUnitH) red_shared_at<3 * kPlaneBytes>(addr, q.w);
       }
     }
     __syncwarp();
@@ -1990,7 +1999,8 @@ void launch_transpose_codes(const void* codes, uint32_t rows, uint32_t cols, uin
 
 void launch_quantize(const float* X, uint32_t rows, uint32_t cols, const float* cuts,
                      const uint32_t* counts, uint32_t bins, void* codes, uint32_t stride,
-                     uint32_t bytes_per_code, uint32_t missing, cudaStream_t stream) {
+                     uint32_t bytes_per_code, uint32_t missing, unsigned long long* missing_cells,
+                     cudaStream_t stream) {
   const uint64_t total = uint64_t(rows) * stride;
   if (!total) return;
   constexpr size_t kStagedMax = 160 * 1024;
@@ -2011,10 +2021,10 @@ void launch_quantize(const float* X, uint32_t rows, uint32_t cols, const float* 
                             : grid_for(total, threads, 32);
   if (bytes_per_code == 1)
     quantize_kernel<uint8_t><<<blocks, threads, staged ? smem : 0, stream>>>(
-        X, rows, cols, cuts, counts, bins, static_cast<uint8_t*>(codes), stride, missing, staged);
+        X, rows, cols, cuts, counts, bins, static_cast<uint8_t*>(codes), stride, missing, staged, missing_cells);
   else
     quantize_kernel<uint16_t><<<blocks, threads, staged ? smem : 0, stream>>>(
-        X, rows, cols, cuts, counts, bins, static_cast<uint16_t*>(codes), stride, missing, staged);
+        X, rows, cols, cuts, counts, bins, static_cast<uint16_t*>(codes), stride, missing, staged, missing_cells);
   XGBB_CUDA(cudaGetLastError());
 }
 

@@ -107,9 +107,11 @@ void launch_narrow_codes(const void* src, uint32_t rows, uint32_t cols, uint32_t
                          uint32_t pad, void* dst, cudaStream_t stream);
 void launch_transpose_codes(const void* codes, uint32_t rows, uint32_t cols, uint32_t stride,
                             uint32_t bytes_per_code, void* fm, cudaStream_t stream);
+// missing_cells (or null) gains the number of NaN values among the rows.
 void launch_quantize(const float* X, uint32_t rows, uint32_t cols, const float* cuts,
                      const uint32_t* counts, uint32_t bins, void* codes, uint32_t stride,
-                     uint32_t bytes_per_code, uint32_t missing, cudaStream_t stream);
+                     uint32_t bytes_per_code, uint32_t missing, unsigned long long* missing_cells,
+                     cudaStream_t stream);
 // flags[0] |= any NaN, flags[1] |= any infinity over n values.
 void launch_validate(const float* X, uint64_t n, unsigned int* flags, cudaStream_t stream);
 void launch_gradients(int objective, const float* margins, const float* labels,

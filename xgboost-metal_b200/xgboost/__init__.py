@@ -7,7 +7,6 @@ from .core import (Booster, DataIter, DMatrix, ExtMemQuantileDMatrix, QuantileDM
                    build_info, synchronize)
 from .plotting import plot_importance, plot_tree, to_graphviz
 from .sklearn import XGBClassifier, XGBModel, XGBRanker, XGBRegressor, XGBRFClassifier, XGBRFRegressor
-from .tracker import RabitTracker
 from .training import cv, train
 
 __version__ = "3.5.0-dev"
@@ -15,4 +14,4 @@ __version__ = "3.5.0-dev"
 __all__ = ["Booster", "DataIter", "DMatrix", "QuantileDMatrix", "ExtMemQuantileDMatrix", "XGBoostError",
            "XGBModel", "XGBRegressor", "XGBClassifier", "XGBRanker", "XGBRFRegressor", "XGBRFClassifier",
            "train", "cv", "build_info", "callback", "collective", "synchronize", "set_config", "get_config",
-           "config_context", "plot_importance", "plot_tree", "to_graphviz", "RabitTracker"]
+           "config_context", "plot_importance", "plot_tree", "to_graphviz"]
