@@ -457,6 +457,29 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
+def phase_breakdown(xgb, core, params, dtrain, dist, rounds=3):
+    """Milliseconds per round of each phase of the tree levels (histogram,
+    reduce-scatter over ranks, split search, best-split gather, partition,
+    child counts), from CUDA events around each launch group
+    (cuda_profile=2), max over ranks; measured after the timed region on a
+    fresh booster, so the extra events do not touch `value`."""
+    bst = xgb.Booster(dict(params, cuda_profile=2), [dtrain])
+    for i in range(2):
+        bst.update(dtrain, i)
+    core.synchronize()
+    bst.reset_cuda_profile()
+    for i in range(rounds):
+        bst.update(dtrain, 2 + i)
+    prof = bst.cuda_profile()
+    out = {k: round(dist.max(v) / rounds, 3) for k, v in prof["phases"].items()}
+    levels = [[round(dist.max(v) / rounds, 3) for v in row] for row in prof["level_phases"]]
+    del bst
+    return {"ms_per_round": out, "per_level_ms": [r for r in levels if any(r)],
+            "columns": list(prof["phases"].keys()), "rounds": rounds,
+            "note": "CUDA events around each phase on the booster's stream (cuda_profile=2) on a "
+                    "fresh booster after the timed region; max over ranks"}
+
+
 def ncu_traffic(wl):
     """Per-launch DRAM bytes of the histogram kernel from the committed ncu
     summary, scaled to one average launch of this workload, or None."""
@@ -578,6 +601,8 @@ def main():
     prof = bst.cuda_profile()
     parity = parity_digest(bst, dtrain, dist, W + K)
     value = dev_ms * 100.0 / K
+    del bst
+    phases = phase_breakdown(xgb, core, params, dtrain, dist)
 
     peak, peak_kind = measured_peak()
     hist_gbs = prof["hist_bytes"] / prof["hist_ms"] / 1e6 if prof["hist_ms"] > 0 else 0.0
@@ -625,6 +650,7 @@ def main():
                         "K rounds; wall clock, max over ranks. ingest = H2D + sketch of all rows + "
                         "binning; the ingest is amortised over K rounds in value"},
         "parity": parity,
+        "phases": phases,
         "c2": c2,
         "gpu_launches": launches_per_round(spec["max_depth"], groups) * K,
         "clocks": clocks.summary(),

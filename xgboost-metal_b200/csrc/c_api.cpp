@@ -996,6 +996,19 @@ XGB_DLL int XGBoosterGetCudaProfile(BoosterHandle handle, char const** out) {
       results.str += "[" + std::to_string(p.level_ms[d]) + "," + std::to_string(p.level_rows[d]) + "," +
                      std::to_string(p.level_nodes[d]) + "]";
     }
+    // cuda_profile=2: milliseconds per phase, in total and per level.
+    static const char* const kNames[xgbb::kPhases] = {"hist", "reduce_scatter", "eval", "best_gather",
+                                                      "partition", "counts"};
+    results.str += "],\"phases\":{";
+    for (uint32_t k = 0; k < xgbb::kPhases; ++k)
+      results.str += std::string(k ? "," : "") + "\"" + kNames[k] + "\":" + std::to_string(p.phase_ms[k]);
+    results.str += "},\"level_phases\":[";
+    for (uint32_t d = 0; d < xgbb::kMaxDepth; ++d) {
+      results.str += d ? ",[" : "[";
+      for (uint32_t k = 0; k < xgbb::kPhases; ++k)
+        results.str += std::string(k ? "," : "") + std::to_string(p.level_phase_ms[d][k]);
+      results.str += "]";
+    }
     results.str += "]}";
     *out = results.str.c_str();
   });

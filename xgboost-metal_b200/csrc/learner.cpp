@@ -389,7 +389,7 @@ struct Booster::TrainState {
   bool pending_captured = false;
   uint32_t parity = 0;
   uint32_t capacity = 0;
-  std::vector<cudaEvent_t> events;  // profiling: [groups][levels][2]
+  std::vector<cudaEvent_t> events;  // profiling: [parity][groups][levels][phase marks]
   // Host-driven trees (loss-guided, leaf budgets, depth > 10): row order and
   // its partition scratch, node histograms and candidates of one batch, the
   // batch descriptors, and pinned landing buffers for the host's reads.
@@ -718,7 +718,8 @@ void Booster::configure() {
   } else {
     groups_ = 1;
   }
-  profiling = integer(params_, "cuda_profile", 0) != 0;
+  profile_level = int(integer(params_, "cuda_profile", 0));
+  profiling = profile_level != 0;
   configured_ = true;
   if (state_) state_.reset();  // parameters are baked into captured graphs
 }
@@ -973,7 +974,7 @@ Booster::TrainState& Booster::train_state(const std::shared_ptr<DMatrix>& dp, bo
   // next round has been enqueued.
   ts->graphs.assign(size_t(G) * 2, nullptr);
   if (profiling) {
-    ts->events.resize(size_t(2) * G * D * 2);
+    ts->events.resize(size_t(2) * G * D * (kPhases + 1));
     for (auto& ev : ts->events) XGBB_CUDA(cudaEventCreate(&ev));
   }
   // Margins start from the base margins plus every tree already in the model.
@@ -1182,22 +1183,32 @@ void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s, b
     tl.csr_totals = ts.csr_totals.as<unsigned long long>();
   }
   const uint32_t per_rank = tl.cols_pad / world;
+  // Phase marks of a level: mark k opens phase k and closes phase k - 1.
+  // cuda_profile=1 records the histogram's two marks only.
+  auto phase = [&](uint32_t depth, uint32_t k) {
+    if (!profiling || (profile_level < 2 && k > kPhaseHist + 1)) return;
+    mark(ts.events[(((size_t(parity) * ts.groups + g) * D + depth) * (kPhases + 1)) + k]);
+  };
   tree_init(ws, tl, s);
   for (uint32_t depth = 0; depth < D; ++depth) {
-    if (profiling) mark(ts.events[((size_t(parity) * ts.groups + g) * D + depth) * 2]);
+    phase(depth, kPhaseHist);
     tree_level_hist(ws, tl, depth, s);
-    if (profiling) mark(ts.events[((size_t(parity) * ts.groups + g) * D + depth) * 2 + 1]);
+    phase(depth, kPhaseReduce);
     // Sum the built histograms over ranks, each rank receiving its features.
     comm.reduce_scatter_u64(ws.built, size_t(per_rank) * max_pairs_at(depth) * (d.ell.bins + 1) * 2, s);
     if (!capturing && g == 0 && capture.depth == int(depth) && !capture.ready) capture_level(ts, depth, tl);
+    phase(depth, kPhaseEval);
     tree_level_eval(ws, tl, depth, s);
+    phase(depth, kPhaseGather);
     if (comm.active()) {
       tree_level_pack_best(ws, tl, depth, ts.best_mine.get(), s);
       comm.all_gather(ts.best_mine.get(), ts.best_all.get(), size_t(kMaxFrontier) * best_record_bytes(), s);
       tree_level_merge_best(ws, tl, depth, ts.best_all.get(), world, s);
     }
+    phase(depth, kPhasePartition);
     tree_level_control(ws, tl, depth, s);
     tree_level_partition(ws, tl, depth, s);
+    phase(depth, kPhaseCounts);
     if (depth + 1 < D) {
       tree_level_counts(ws, depth, s);
       if (comm.active()) {
@@ -1207,6 +1218,7 @@ void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s, b
       }
       tree_level_plan(ws, tl, depth + 1, s);
     }
+    phase(depth, kPhases);
   }
 }
 
@@ -1449,10 +1461,18 @@ void Booster::finish_round(TrainState& ts) {
       const double row_bytes = double(e.cols) * e.bytes_per_code + 8.0;
       for (uint32_t depth = 0; depth < D; ++depth) {
         float ms = 0;
-        const size_t e = ((size_t(b) * G + g) * D + depth) * 2;
+        const size_t e = ((size_t(b) * G + g) * D + depth) * (kPhases + 1);
         XGBB_CUDA(cudaEventElapsedTime(&ms, ts.events[e], ts.events[e + 1]));
         const double rows = double(ts.host_level_rows[b][size_t(g) * kMaxDepth + depth]);
         const double nodes = double(ts.host_level_nodes[b][size_t(g) * kMaxDepth + depth]);
+        if (profile_level >= 2) {
+          for (uint32_t k = 0; k < kPhases; ++k) {
+            float pm = 0;
+            XGBB_CUDA(cudaEventElapsedTime(&pm, ts.events[e + k], ts.events[e + k + 1]));
+            profile.phase_ms[k] += pm;
+            profile.level_phase_ms[depth][k] += pm;
+          }
+        }
         if (nodes == 0) continue;
         profile.hist_ms += ms;
         profile.hist_bytes += rows * (row_bytes + (depth ? 4.0 : 0.0)) + nodes * node_bytes;

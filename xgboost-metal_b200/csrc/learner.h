@@ -106,8 +106,21 @@ struct HostTree {
   uint32_t group = 0;
 };
 
+// Phases of a tree level timed with cuda_profile=2 (CUDA events around each
+// launch group on the booster's stream).
+enum : uint32_t {
+  kPhaseHist = 0,       // histogram kernels
+  kPhaseReduce,         // reduce-scatter of the built histograms over ranks
+  kPhaseEval,           // subtraction, prefix scan and split gain
+  kPhaseGather,         // best-split records gathered over ranks and merged
+  kPhasePartition,      // control (expansion rule) and row partition
+  kPhaseCounts,         // child counts, their sum over ranks, the next plan
+  kPhases
+};
 struct Profile {
   bool csr = false;  // the level histograms came from the rows' present codes
+  double phase_ms[kPhases] = {};
+  double level_phase_ms[kMaxDepth][kPhases] = {};
   double hist_ms = 0, total_ms = 0;
   double hist_bytes = 0;
   uint64_t hist_launches = 0, kernel_launches = 0, rounds = 0;
@@ -159,6 +172,7 @@ class Booster {
   // recursive mutex, include/metalgb/engine.hpp:201, src/c_api.cpp:37-39).
   std::recursive_mutex& mutex() { return mutex_; }
   bool profiling = false;
+  int profile_level = 0;  // cuda_profile: 1 histogram events, 2 every phase
   // Built histograms of one level of the first tree of the next round, for
   // checking them word for word. `depth` >= 0 requests a capture; the round
   // that takes it runs that tree without a CUDA graph. `hist` holds
