@@ -727,7 +727,11 @@ constexpr uint32_t kH2Threads = kH2Warps * 32;
 constexpr uint32_t kStageRows = 32;                    // rows per warp per step
 constexpr uint32_t kStepRows = kStageRows * kH2Warps;  // rows per CTA per step
 constexpr uint32_t kStageBufs = 2;                     // one step of copies in flight
-constexpr uint32_t kOwn2 = (kPlaneWords / 2 + kH2Threads - 1) / kH2Threads;  // word pairs per thread
+constexpr uint32_t kOwn4 = (kPlaneWords / 4 + kH2Threads - 1) / kH2Threads;  // word quads per thread
+// A normalisation carries only words above this magnitude; the rows between
+// two normalisations are limited so that a word left below it cannot
+// overflow (see hist2_kernel).
+constexpr int kCarryAbove = 1 << 26;
 static_assert(kPlaneWords % 2 == 0, "planes hold whole word pairs");
 
 template <typename CodeT>
@@ -961,12 +965,15 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
   const float2 sc = *a.scale;
   const long long qh_unit = __float2ll_rn(sc.y);
   // Limbs are balanced: l0 in [-2^(L-1), 2^(L-1)), l1 = (q - l0) / 2^L, so
-  // |l1| <= 2^(L-1) as well when |q| < 2^(2L-1). A word starts below 2^L
-  // after a carry and may take `norm_rows` more rows before int32 overflows.
+  // |l1| <= 2^(L-1) as well when |q| < 2^(2L-1): a row adds at most
+  // 2^per_row_bits to a word.
   const uint32_t Lmax = kUnitH ? Lg : (Lg > Lh ? Lg : Lh);
   const uint32_t per_row_bits =
       (pg.bits + 1 <= 2 * Lg && (kUnitH || ph.bits + 1 <= 2 * Lh)) ? Lmax - 1 : Lmax;
-  const uint32_t norm_rows = uint32_t((0x7fffffffull - (1ull << Lmax)) >> per_row_bits);
+  // A normalisation leaves every word at most kCarryAbove in magnitude (a
+  // carried word restarts in [0, 2^L)), so `norm_rows` more rows keep it
+  // inside int32.
+  const uint32_t norm_rows = uint32_t((0x7fffffffull - uint64_t(kCarryAbove)) >> per_row_bits);
   const unsigned char* codes = static_cast<const unsigned char*>(a.e.codes);
   const size_t row_bytes = size_t(a.e.stride) * sizeof(CodeT);
   const uint32_t miss_slot = a.e.missing;
@@ -979,10 +986,10 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
   }
   __syncthreads();
 
-  // Carries out of limb 1 of the word pairs tid + k * kH2Threads.
-  int2 tg[kOwn2], th[kOwn2];
+  // Carries out of limb 1 of the word quads tid + k * kH2Threads.
+  int4 tg[kOwn4], th[kOwn4];
 #pragma unroll
-  for (uint32_t k = 0; k < kOwn2; ++k) tg[k] = th[k] = make_int2(0, 0);
+  for (uint32_t k = 0; k < kOwn4; ++k) tg[k] = th[k] = make_int4(0, 0, 0, 0);
 
   // Copies of one step's code slices and gradient pairs into stage buffer
   // `buf`; `id` holds the row id of lane j's row (non-root).
@@ -1013,26 +1020,41 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
     if (kRoot) return 0u;
     return lane < s.n() ? __ldg(a.rows + s.row0 + lane) : 0u;
   };
-  auto carry1 = [](int& x0, int& x1, int& top, uint32_t L) {
-    const int c0 = x0 >> L;  // arithmetic shift: floor division by 2^L
-    x0 -= c0 * (1 << L);
-    x1 += c0;
-    const int c1 = x1 >> L;
-    x1 -= c1 * (1 << L);
-    top += c1;
+  // Carries of one word pair (limb 0, limb 1) whose magnitude passed
+  // kCarryAbove: a floor carry from limb 0 into limb 1, and from limb 1 into
+  // the register limb `top`. Returns whether a word changed.
+  auto carry1 = [](int& x0, int& x1, int& top, uint32_t L) -> bool {
+    bool changed = false;
+    if (abs(x0) > kCarryAbove) {
+      const int c0 = x0 >> L;  // arithmetic shift: floor division by 2^L
+      x0 -= c0 * (1 << L);
+      x1 += c0;
+      changed = true;
+    }
+    if (abs(x1) > kCarryAbove) {
+      const int c1 = x1 >> L;
+      x1 -= c1 * (1 << L);
+      top += c1;
+      changed = true;
+    }
+    return changed;
   };
-  auto carry = [&](int* p0, int* p1, int2& top, uint32_t L) {
-    int2 x0 = *reinterpret_cast<int2*>(p0), x1 = *reinterpret_cast<int2*>(p1);
-    carry1(x0.x, x1.x, top.x, L);
-    carry1(x0.y, x1.y, top.y, L);
-    *reinterpret_cast<int2*>(p0) = x0;
-    *reinterpret_cast<int2*>(p1) = x1;
+  auto carry = [&](int* p0, int* p1, int4& top, uint32_t L) {
+    int4 x0 = *reinterpret_cast<int4*>(p0), x1 = *reinterpret_cast<int4*>(p1);
+    bool changed = carry1(x0.x, x1.x, top.x, L);
+    changed |= carry1(x0.y, x1.y, top.y, L);
+    changed |= carry1(x0.z, x1.z, top.z, L);
+    changed |= carry1(x0.w, x1.w, top.w, L);
+    if (changed) {
+      *reinterpret_cast<int4*>(p0) = x0;
+      *reinterpret_cast<int4*>(p1) = x1;
+    }
   };
   auto normalise = [&]() {
     __syncthreads();
 #pragma unroll
-    for (uint32_t k = 0; k < kOwn2; ++k) {
-      const uint32_t i = 2 * (threadIdx.x + k * kH2Threads);
+    for (uint32_t k = 0; k < kOwn4; ++k) {
+      const uint32_t i = 4 * (threadIdx.x + k * kH2Threads);
       if (i < words) {
         carry(smem + i, smem + kPlaneWords + i, tg[k], Lg);
         if (!kUnitH) carry(smem + 2 * kPlaneWords + i, smem + 3 * kPlaneWords + i, th[k], Lh);
@@ -1048,13 +1070,15 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
     int* p2 = smem + 2 * kPlaneWords;
     int* p3 = smem + 3 * kPlaneWords;
 #pragma unroll
-    for (uint32_t k = 0; k < kOwn2; ++k) {
-      const uint32_t i0 = 2 * (threadIdx.x + k * kH2Threads);
+    for (uint32_t k = 0; k < kOwn4; ++k) {
+      const uint32_t i0 = 4 * (threadIdx.x + k * kH2Threads);
       if (i0 < words) {
+        const int tgs[4] = {tg[k].x, tg[k].y, tg[k].z, tg[k].w};
+        const int ths[4] = {th[k].x, th[k].y, th[k].z, th[k].w};
 #pragma unroll
-        for (uint32_t e = 0; e < 2; ++e) {
+        for (uint32_t e = 0; e < 4; ++e) {
           const uint32_t i = i0 + e;
-          const int topg = e ? tg[k].y : tg[k].x, toph = e ? th[k].y : th[k].x;
+          const int topg = tgs[e], toph = ths[e];
           const uint32_t slot = i / kHistLanes, f = f0 + (i % kHistLanes);
           const uint32_t bin = slot == miss_slot ? B : slot;
           const long long g = (long long)((unsigned long long)(long long)p0[i] +
@@ -1077,13 +1101,13 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
             atomicAdd(reinterpret_cast<unsigned long long*>(&dst->y), (unsigned long long)h);
           }
         }
-        *reinterpret_cast<int2*>(p0 + i0) = make_int2(0, 0);
-        *reinterpret_cast<int2*>(p1 + i0) = make_int2(0, 0);
-        *reinterpret_cast<int2*>(p2 + i0) = make_int2(0, 0);
-        if (!kUnitH) *reinterpret_cast<int2*>(p3 + i0) = make_int2(0, 0);
+        *reinterpret_cast<int4*>(p0 + i0) = make_int4(0, 0, 0, 0);
+        *reinterpret_cast<int4*>(p1 + i0) = make_int4(0, 0, 0, 0);
+        *reinterpret_cast<int4*>(p2 + i0) = make_int4(0, 0, 0, 0);
+        if (!kUnitH) *reinterpret_cast<int4*>(p3 + i0) = make_int4(0, 0, 0, 0);
       }
-      tg[k] = make_int2(0, 0);
-      th[k] = make_int2(0, 0);
+      tg[k] = make_int4(0, 0, 0, 0);
+      th[k] = make_int4(0, 0, 0, 0);
     }
     __syncthreads();
   };
