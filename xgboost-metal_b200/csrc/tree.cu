@@ -17,6 +17,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstddef>
 
 #include "device_math.cuh"
 #include "split_select.h"
@@ -859,6 +860,7 @@ struct HistCursor {
   uint64_t it, end;
   uint32_t k;        // step within the item
   uint32_t group, pair, begin, cnt;
+  uint32_t tile;     // tile of `it` within its feature group
   uint32_t total_tiles;
   uint32_t t_lo, t_hi;   // tiles of `pair`: [t_lo, t_hi)
   uint32_t seg0, segn;   // rows of the built child of `pair`
@@ -881,6 +883,7 @@ struct HistCursor {
   __device__ __forceinline__ void resolve(const HistArgs& a, uint32_t npairs) {
     group = uint32_t(it / total_tiles);
     const uint32_t t = uint32_t(it % total_tiles);
+    tile = t;
     pair = 0;
     if (!kRoot) {
       uint32_t lo = 0, hi = npairs;
@@ -920,8 +923,8 @@ struct HistCursor {
     }
     k = 0;
     if (++it >= end) return;
-    const uint32_t g = uint32_t(it / total_tiles), t = uint32_t(it % total_tiles);
-    if (g != group) {
+    const uint32_t t = ++tile;
+    if (t == total_tiles) {  // next feature group
       resolve(a, npairs);
       return;
     }
@@ -993,28 +996,36 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
 
   // Copies of one step's code slices and gradient pairs into stage buffer
   // `buf`; `id` holds the row id of lane j's row (non-root).
+  // Per lane: which 16-byte part of a row's slice it copies, and where each
+  // pass's piece lands in a stage buffer (fixed for the kernel).
+  constexpr uint32_t kParts = kSlice / 16;  // 4 (u16) or 2 (u8)
+  constexpr uint32_t kRowsPerPass = 32 / kParts;
+  constexpr uint32_t kPasses = kStageRows / kRowsPerPass;
+  const uint32_t part = lane % kParts;
+  const uint32_t stage0 = static_cast<uint32_t>(__cvta_generic_to_shared(stage));
+  uint32_t piece_at[kPasses];
+#pragma unroll
+  for (uint32_t pass = 0; pass < kPasses; ++pass) {
+    const uint32_t r = pass * kRowsPerPass + lane / kParts;
+    piece_at[pass] = r * kSlice + stage_chunk<CodeT>(r, part) * 16;
+  }
+  const uint32_t pair_at = static_cast<uint32_t>(offsetof(HistStage<CodeT>, pairs)) + lane * 8;
+  const unsigned char* const codes_part = codes + part * 16;
   auto issue = [&](const HistStep& s, uint32_t id, uint32_t buf) {
     if (!s.n()) return;
-    HistStage<CodeT>& dst = stage[buf];
+    const uint32_t dst = stage0 + buf * uint32_t(sizeof(HistStage<CodeT>));
     const uint32_t fvalid = min(kHistLanes, C - s.group() * kHistLanes);
     const uint32_t chunks = (fvalid * sizeof(CodeT) + 15) / 16;  // 16-byte pieces of the slice
-    constexpr uint32_t kParts = kSlice / 16;                      // 4 (u16) or 2 (u8)
-    constexpr uint32_t kRowsPerPass = 32 / kParts;
-    const uint32_t part = lane % kParts;
-    const size_t col_bytes = size_t(s.group()) * kSlice + part * 16;
+    const unsigned char* const src = codes_part + size_t(s.group()) * kSlice;
 #pragma unroll
-    for (uint32_t pass = 0; pass < kStageRows / kRowsPerPass; ++pass) {
+    for (uint32_t pass = 0; pass < kPasses; ++pass) {
       const uint32_t r = pass * kRowsPerPass + lane / kParts;
       const uint32_t rid = kRoot ? s.row0 + r : __shfl_sync(0xffffffffu, id, r);
-      if (r < s.n() && part < chunks)
-        cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(&dst.codes[r][0])) +
-                       stage_chunk<CodeT>(r, part) * 16,
-                   codes + size_t(rid) * row_bytes + col_bytes);
+      if (r < s.n() && part < chunks) cp_async16(dst + piece_at[pass], src + size_t(rid) * row_bytes);
     }
     // Lanes past n add zeros (their pairs are not read), so the stale codes
     // of their stage rows add nothing; every stale code is a valid slot.
-    if (lane < s.n())
-      cp_async8(static_cast<uint32_t>(__cvta_generic_to_shared(&dst.pairs[lane])), a.pairs + s.row0 + lane);
+    if (lane < s.n()) cp_async8(dst + pair_at, a.pairs + s.row0 + lane);
   };
   auto load_ids = [&](const HistStep& s) -> uint32_t {
     if (kRoot) return 0u;
@@ -1129,6 +1140,13 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
   const uint32_t pbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
 
   while (s0.valid()) {
+    cp_async_wait<0>();  // this step's copies
+    __syncwarp();
+    // The next step's copies go out before any flush or normalisation, so
+    // that memory stays busy while every warp of the CTA carries or flushes.
+    issue(s1, id, buf ^ 1);
+    cp_async_commit();
+    id = load_ids(s2);
     if (int64_t(s0.group()) != cur_group || int64_t(s0.pair()) != cur_pair) {
       if (cur_group >= 0) {
         flush(uint32_t(cur_group), uint32_t(cur_pair));
@@ -1141,11 +1159,6 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
       normalise();
       since = 0;
     }
-    cp_async_wait<0>();  // this step's copies
-    __syncwarp();
-    issue(s1, id, buf ^ 1);
-    cp_async_commit();
-    id = load_ids(s2);
     if (s0.n()) {
       HistStage<CodeT>& st0 = stage[buf];
       // Lane = row: its two-limb values, formed once for 32 features; lanes
@@ -1764,6 +1777,93 @@ __global__ void __launch_bounds__(kPartThreads) partition_kernel(PartArgs a) {
       rpos += __popc(br);
     }
     __syncthreads();
+  }
+}
+
+// Loads of streamed data that should leave L2 first (evict-first policy).
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ uint32_t ld_stream_u32(const uint32_t* p, uint64_t pol) {
+  uint32_t v;
+  asm volatile("ld.global.nc.L2::cache_hint.u32 %0, [%1], %2;\n" : "=r"(v) : "l"(p), "l"(pol));
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_stream_code(const uint16_t* p, uint64_t pol) {
+  unsigned short v;
+  asm volatile("ld.global.nc.L2::cache_hint.u16 %0, [%1], %2;\n" : "=h"(v) : "l"(p), "l"(pol));
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_stream_code(const uint8_t* p, uint64_t pol) {
+  unsigned short v;
+  asm volatile("ld.global.nc.L2::cache_hint.u8 %0, [%1], %2;\n" : "=h"(v) : "l"(p), "l"(pol));
+  return v;
+}
+
+// The last level: every frontier node stops (its leaf goes to all its rows)
+// or splits into two leaves, and no row moves. Only margins change, at
+// random row ids, so the level runs in passes over ranges of row ids: each
+// pass walks the whole row list but reads and writes only the margins of
+// rows in [row_lo, row_hi), which then stay in L2 across the pass (the row
+// ids and split codes stream through with an evict-first policy). The
+// result is the partition kernel's: margin += leaf, one add per row.
+template <typename CodeT>
+__global__ void __launch_bounds__(kPartThreads) leaf_margin_kernel(PartArgs a, uint32_t row_lo, uint32_t row_hi) {
+  const DriverState st = *a.state;
+  if (!st.frontier || st.error) return;
+  const uint32_t n = st.frontier, ptiles = st.pad0;
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const CodeT* __restrict__ codes = static_cast<const CodeT*>(a.e.codes);
+  const CodeT* __restrict__ fm = static_cast<const CodeT*>(a.e.codes_fm);
+  const uint64_t pol = evict_first_policy();
+  for (uint32_t t = blockIdx.x; t < ptiles; t += gridDim.x) {
+    uint32_t lo = 0, hi = n;
+    while (hi - lo > 1) {
+      const uint32_t mid = (lo + hi) >> 1;
+      if (a.ptile_offset[mid] <= t) lo = mid;
+      else hi = mid;
+    }
+    const uint32_t s = lo;
+    const uint32_t seg0 = a.seg_begin[s], segn = a.seg_count[s];
+    const uint32_t begin = seg0 + (t - a.ptile_offset[s]) * kTileRows;
+    const uint32_t cnt = min(kTileRows, seg0 + segn - begin);
+    const uint32_t md = a.mode[s];
+    const DevNode node = a.nodes[a.ids[s]];
+    const float leaf_l = a.slot_leaf[2 * s], leaf_r = a.slot_leaf[2 * s + 1];
+    const uint32_t w0 = warp * (kTileRows / kPartWarps);
+    uint32_t rows[kPartIter], take = 0;
+#pragma unroll
+    for (uint32_t k = 0; k < kPartIter; ++k) {
+      const uint32_t i = w0 + k * 32 + lane;
+      rows[k] = 0;
+      if (i < cnt) {
+        rows[k] = a.root ? begin + i : ld_stream_u32(a.rows + begin + i, pol);
+        take |= uint32_t(rows[k] >= row_lo && rows[k] < row_hi) << k;
+      }
+    }
+    uint32_t code[kPartIter];
+#pragma unroll
+    for (uint32_t k = 0; k < kPartIter; ++k) {
+      code[k] = 0;
+      if (md != 0 && ((take >> k) & 1u))
+        code[k] = fm ? ld_stream_code(fm + size_t(node.feature) * a.e.rows + rows[k], pol)
+                     : ld_stream_code(codes + size_t(rows[k]) * a.e.stride + uint32_t(node.feature), pol);
+    }
+    float* m[kPartIter];
+    float v[kPartIter];
+#pragma unroll
+    for (uint32_t k = 0; k < kPartIter; ++k) {
+      m[k] = a.margins + size_t(rows[k]) * a.groups + a.group;
+      v[k] = ((take >> k) & 1u) ? *m[k] : 0.0f;
+    }
+#pragma unroll
+    for (uint32_t k = 0; k < kPartIter; ++k) {
+      if (!((take >> k) & 1u)) continue;
+      const bool left = code[k] == a.e.missing ? node.default_left != 0u : int32_t(code[k]) <= node.split_bin;
+      *m[k] = __fadd_rn(v[k], md == 0 ? leaf_l : (left ? leaf_l : leaf_r));
+    }
   }
 }
 
@@ -2473,6 +2573,23 @@ void tree_level_partition(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_
   a.groups = tl.groups;
   a.group = tl.group;
   a.root = depth == 0;
+  if (depth + 1 >= tl.params.max_depth) {
+    // Last level: margins only, in passes whose margins fit well inside L2.
+    constexpr uint64_t kPassBytes = 48ull << 20;
+    const uint64_t bytes = uint64_t(tl.ell.rows) * 4 * std::min<uint32_t>(tl.groups, 8);
+    const uint32_t passes = uint32_t(std::max<uint64_t>(1, (bytes + kPassBytes - 1) / kPassBytes));
+    const uint32_t span = uint32_t((uint64_t(tl.ell.rows) + passes - 1) / passes);
+    for (uint32_t p = 0; p < passes; ++p) {
+      const uint32_t lo = uint32_t(std::min<uint64_t>(uint64_t(p) * span, tl.ell.rows));
+      const uint32_t hi = p + 1 == passes ? 0xffffffffu : uint32_t(std::min<uint64_t>(uint64_t(p + 1) * span, tl.ell.rows));
+      if (tl.ell.bytes_per_code == 1)
+        leaf_margin_kernel<uint8_t><<<tl.part_blocks, kPartThreads, 0, stream>>>(a, lo, hi);
+      else
+        leaf_margin_kernel<uint16_t><<<tl.part_blocks, kPartThreads, 0, stream>>>(a, lo, hi);
+      XGBB_CUDA(cudaGetLastError());
+    }
+    return;
+  }
   if (tl.ell.bytes_per_code == 1)
     partition_kernel<uint8_t><<<tl.part_blocks, kPartThreads, 0, stream>>>(a);
   else
