@@ -68,6 +68,6 @@ struct DriverState {
   uint32_t node_count, frontier, depth, error;
   uint32_t pairs, total_tiles, pad0, pad1;
 };
-enum : uint32_t { kErrCapacity = 1, kErrNode = 2 };
+enum : uint32_t { kErrCapacity = 1, kErrNode = 2, kErrLayout = 4 };
 
 }  // namespace xgbb

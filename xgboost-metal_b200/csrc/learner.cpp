@@ -1439,6 +1439,7 @@ void Booster::finish_round(TrainState& ts) {
   const uint32_t G = ts.groups;
   for (uint32_t g = 0; g < G; ++g) {
     const DriverState st = ts.host_state[b][g];
+    require(!(st.error & kErrLayout), "Histogram kernel: shared memory is not 128-byte aligned.");
     require(!st.error, "GPU tree driver produced an invalid tree.");
     require(st.node_count >= 1 && st.node_count <= ts.capacity, "GPU tree driver node count out of range.");
     HostTree t;

@@ -944,11 +944,15 @@ struct HistCursor {
 
 template <typename CodeT, bool kUnitH, bool kRoot>
 __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
-  extern __shared__ __align__(16) int smem[];
+  extern __shared__ __align__(128) int smem[];
   const DriverState st = *a.state;
   if (!st.frontier || !st.total_tiles) return;
   LimbPlan pg, ph;
   if (!plan_round(a, kUnitH, pg, ph)) return;  // the three-limb kernel builds this level
+  if (static_cast<uint32_t>(__cvta_generic_to_shared(smem)) & 127u) {
+    if (threadIdx.x == 0) atomicOr(&const_cast<DriverState*>(a.state)->error, kErrLayout);
+    return;
+  }
   const uint32_t Lg = pg.L, Lh = ph.L;
   constexpr uint32_t kPlanes = kUnitH ? 3 : 4;  // g0, g1, h0 | count, h1
   constexpr uint32_t kPlaneBytes = kPlaneWords * sizeof(int);
@@ -1138,6 +1142,10 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
   int64_t cur_group = -1, cur_pair = -1;
   uint32_t since = 0;
   const uint32_t pbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  // With the planes on a 128-byte boundary, code * 128 + pbase has zero low
+  // seven bits, so the lane term is or-ed in once and the feature term is a
+  // constant XOR: word code * 32 + (lane ^ f) of the plane.
+  const uint32_t tbase = pbase + (lane << 2);
 
   while (s0.valid()) {
     cp_async_wait<0>();  // this step's copies
@@ -1180,12 +1188,11 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
         quad[k][3] = v.w;
         xor_permute<CodeT>(quad[k], lane % kPerQuad);
       }
-      const uint32_t lane4 = lane * 4;
 #pragma unroll
       for (uint32_t f = 0; f < kHistLanes; ++f) {
         const uint32_t w = quad[f / kPerQuad][(f % kPerQuad) * sizeof(CodeT) / 4];
         const uint32_t code = sizeof(CodeT) == 2 ? (w >> (16 * (f & 1))) & 0xffffu : (w >> (8 * (f & 3))) & 0xffu;
-        const uint32_t addr = pbase + code * (kHistLanes * 4) + (lane4 ^ (4 * f));
+        const uint32_t addr = (code * (kHistLanes * 4) + tbase) ^ (4 * f);
         red_shared(addr, q.x);
         red_shared_at<kPlaneBytes>(addr, q.y);
         red_shared_at<2 * kPlaneBytes>(addr, q.z);
@@ -1206,7 +1213,7 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
 
 template <typename CodeT, bool kUnitH, bool kRoot>
 __global__ void __launch_bounds__(1024, 1) hist_kernel(HistArgs a) {
-  extern __shared__ __align__(16) int smem[];
+  extern __shared__ __align__(128) int smem[];
   const DriverState st = *a.state;
   if (!st.frontier || !st.total_tiles) return;
   LimbPlan pg, ph;
@@ -2575,7 +2582,7 @@ void tree_level_partition(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_
   a.root = depth == 0;
   if (depth + 1 >= tl.params.max_depth) {
     // Last level: margins only, in passes whose margins fit well inside L2.
-    constexpr uint64_t kPassBytes = 48ull << 20;
+    constexpr uint64_t kPassBytes = 96ull << 20;
     const uint64_t bytes = uint64_t(tl.ell.rows) * 4 * std::min<uint32_t>(tl.groups, 8);
     const uint32_t passes = uint32_t(std::max<uint64_t>(1, (bytes + kPassBytes - 1) / kPassBytes));
     const uint32_t span = uint32_t((uint64_t(tl.ell.rows) + passes - 1) / passes);
