@@ -95,10 +95,15 @@ extern "C" int sketch_harness(const float* X, uint32_t rows, uint32_t cols, cons
   std::vector<Entry> summaries(std::max<uint64_t>(tree ? tp.entries : plan.summary_entries, 1));
   std::vector<uint32_t> sizes(std::max(tree ? tp.sizes : plan.sizes, 1u));
   std::vector<unsigned char> scratch(batch_scratch_bytes(plan.cap)), work(std::max<uint64_t>(plan.work_bytes, 1));
+  // Every other batch takes the radix form of the sort (the GPU kernel's
+  // path), the others the bitonic form: both must give the host sketch's cuts.
+  std::vector<unsigned char> radix(radix_sort_bytes(plan.cap, 32));
+  size_t task_index = 0;
   for (const BatchTask& t : plan.tasks) {
     const BatchWork bw = batch_work_at(scratch.data(), plan.cap);
     sizes[t.size_slot] = summarize_par(ex, runs.data() + t.run_begin, t.size, t.limit, bw.keys, bw.sorted, bw.entries,
-                                       summaries.data() + t.summary_at, bw.w);
+                                       summaries.data() + t.summary_at, bw.w,
+                                       (task_index++ & 1) ? radix.data() : nullptr);
   }
   std::vector<uint32_t> irregular(std::max<size_t>(plan.reduce.size(), 1), tree ? 0u : 1u);
   if (tree) {

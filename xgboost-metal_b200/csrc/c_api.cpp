@@ -973,12 +973,15 @@ XGB_DLL int XGBBSynchronize(void) {
 
 XGB_DLL int XGDMatrixQuantise(DMatrixHandle handle, int max_bin, DMatrixHandle ref) {
   return guarded([&] {
+    xgbb::Trace trace("XGDMatrixQuantise");
     ensure_device();
+    trace.mark("device", nullptr);
     auto& d = *dmat(handle);
     const xgbb::DMatrix* r = ref ? dmat(ref).get() : nullptr;
     d.quantise(uint32_t(max_bin), r, nullptr, 0);
     d.quantile = true;
     XGBB_CUDA(cudaStreamSynchronize(nullptr));
+    trace.mark("quantise", nullptr);
   });
 }
 

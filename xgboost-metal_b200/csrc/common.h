@@ -2,7 +2,10 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <chrono>
 #include <cstdint>
+#include <cstdio>
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
@@ -17,11 +20,48 @@ struct Error : std::runtime_error {
 inline void require(bool ok, const std::string& message) {
   if (!ok) throw Error(message);
 }
+// The same for a literal message, which then costs nothing until a check
+// fails (checks run once per element of large arrays).
+inline void require(bool ok, const char* message) {
+  if (!ok) throw Error(message);
+}
 
 inline void cuda_check(cudaError_t e, const char* what) {
   if (e != cudaSuccess) throw Error(std::string(what) + ": " + cudaGetErrorString(e));
 }
 #define XGBB_CUDA(call) ::xgbb::cuda_check((call), #call)
+
+// Phase timing of host-driven work for diagnosis: with XGBB_TRACE=1 each
+// mark waits for `stream` and prints the wall time since the previous mark
+// to stderr; otherwise marks cost nothing.
+class Trace {
+ public:
+  explicit Trace(const char* scope) : scope_(scope), on_(enabled()) {
+    if (on_) t_ = now();
+  }
+  void mark(const char* what, cudaStream_t stream) {
+    if (!on_) return;
+    cudaStreamSynchronize(stream);
+    const double t = now();
+    std::fprintf(stderr, "[xgbb trace] %s: %s %.1f ms\n", scope_, what, (t - t_) * 1e3);
+    t_ = t;
+  }
+
+ private:
+  static bool enabled() {
+    static const bool on = [] {
+      const char* v = std::getenv("XGBB_TRACE");
+      return v && v[0] == '1';
+    }();
+    return on;
+  }
+  static double now() {
+    return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+  }
+  const char* scope_;
+  bool on_;
+  double t_ = 0;
+};
 
 constexpr uint32_t kMaxDepth = 10;         // device driver limit (src/tree.cpp:376-384)
 constexpr uint32_t kMaxBins = 256;         // bins per feature, missing bin excluded

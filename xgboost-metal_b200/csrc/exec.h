@@ -11,6 +11,7 @@
 #pragma once
 #include <cmath>
 #include <cstdint>
+#include <vector>
 
 #if defined(__CUDACC__)
 #define XGBB_HD __host__ __device__
@@ -72,6 +73,21 @@ struct HostExec {
     T acc = init;
     for (uint32_t i = 0; i < n; ++i) a[i] = acc = op(acc, a[i]);
   }
+  // order[i] = index of the i-th smallest of key[0, n), ties in index order
+  // (the device's radix sort gives the same order). The other pointers are
+  // the device form's scratch and go unused here.
+  void stable_order(uint32_t* key, uint16_t* order, uint32_t n, uint32_t*, uint16_t*, uint32_t*) {
+    std::vector<uint32_t> idx(n), tmp(n);
+    for (uint32_t i = 0; i < n; ++i) idx[i] = i;
+    for (uint32_t shift = 0; shift < 32; shift += 8) {  // LSD counting sort, stable
+      uint32_t count[257] = {};
+      for (uint32_t i = 0; i < n; ++i) ++count[((key[idx[i]] >> shift) & 255u) + 1];
+      for (uint32_t d = 0; d < 256; ++d) count[d + 1] += count[d];
+      for (uint32_t i = 0; i < n; ++i) tmp[count[(key[idx[i]] >> shift) & 255u]++] = idx[i];
+      idx.swap(tmp);
+    }
+    for (uint32_t i = 0; i < n; ++i) order[i] = uint16_t(idx[i]);
+  }
   void add_u64(unsigned long long* p, unsigned long long v) { *p += v; }
   uint32_t add_u32(uint32_t* p, uint32_t v) {
     const uint32_t old = *p;
@@ -129,6 +145,60 @@ struct DeviceExec {
     *total = warp_tot[nwarps - 1];
     __syncthreads();
     return excl;
+  }
+
+  // Stable radix sort (8-bit digits, four passes) of n < 65536 32-bit keys:
+  // order[i] = index of the i-th smallest, ties in index order. key, order
+  // and key2, order2 (n entries each) are shared scratch, cnt holds
+  // 256 * (warps + 1) counters. Warp w ranks the elements of its contiguous
+  // segment row by row, lanes with equal digits found by __match_any_sync,
+  // and the offsets are scanned digit-major then warp, so equal keys keep
+  // their input order. key is left permuted.
+  __device__ void stable_order(uint32_t* key, uint16_t* order, uint32_t n, uint32_t* key2, uint16_t* order2,
+                               uint32_t* cnt) {
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const uint32_t stride = nw + 1;  // counter of (digit d, warp w): cnt[d * stride + w]
+    const uint32_t seg = (n + nw - 1) / nw;
+    const uint32_t lo = min(n, warp * seg), hi = min(n, lo + seg);
+    const uint32_t lt = (1u << lane) - 1u;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) order[i] = uint16_t(i);
+    uint32_t *ka = key, *kb = key2;
+    uint16_t *oa = order, *ob = order2;
+    for (uint32_t shift = 0; shift < 32; shift += 8) {
+      for (uint32_t i = threadIdx.x; i < 256 * stride; i += blockDim.x) cnt[i] = 0;
+      __syncthreads();
+      for (uint32_t base = lo; base < hi; base += 32) {
+        const uint32_t e = base + lane;
+        const bool valid = e < hi;
+        const uint32_t d = valid ? (ka[e] >> shift) & 255u : 256u + lane;
+        const uint32_t m = __match_any_sync(0xffffffffu, d);
+        if (valid && (m & lt) == 0) cnt[d * stride + warp] += __popc(m);
+        __syncwarp();
+      }
+      __syncthreads();
+      scan_exclusive(cnt, 256 * stride, Add32{});
+      for (uint32_t base = lo; base < hi; base += 32) {
+        const uint32_t e = base + lane;
+        const bool valid = e < hi;
+        const uint32_t d = valid ? (ka[e] >> shift) & 255u : 256u + lane;
+        const uint32_t m = __match_any_sync(0xffffffffu, d);
+        if (valid) {
+          const uint32_t pos = cnt[d * stride + warp] + __popc(m & lt);
+          kb[pos] = ka[e];
+          ob[pos] = oa[e];
+        }
+        __syncwarp();
+        if (valid && (m & lt) == 0) cnt[d * stride + warp] += __popc(m);
+        __syncwarp();
+      }
+      __syncthreads();
+      uint32_t* tk = ka;
+      ka = kb;
+      kb = tk;
+      uint16_t* to = oa;
+      oa = ob;
+      ob = to;
+    }
   }
 
   template <class T, class Op>

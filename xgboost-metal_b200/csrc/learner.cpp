@@ -292,6 +292,7 @@ void DMatrix::quantise(uint32_t mb, const DMatrix* ref, cudaStream_t stream, int
   require(mb <= kMaxBins, "max_bin above 256 is not supported by the CUDA histogram kernels.");
   std::shared_ptr<Cuts> c;
   const bool uploaded = bool(d_data);
+  Trace trace("quantise");
   if (ref) {
     require(ref->cuts && ref->max_bin == mb, "Quantile reference does not match max_bin.");
     c = ref->cuts;
@@ -328,6 +329,7 @@ void DMatrix::quantise(uint32_t mb, const DMatrix* ref, cudaStream_t stream, int
     }
     if (on_device) {
       const float* X = device_data(stream);
+      trace.mark("upload and validate", stream);
       DeviceBuffer w;
       if (!weights.empty()) {
         w.resize(weights.size() * 4);
@@ -342,12 +344,15 @@ void DMatrix::quantise(uint32_t mb, const DMatrix* ref, cudaStream_t stream, int
     c->upload();
   }
   max_bin = mb;
+  trace.mark("cuts", stream);
   set_cuts(std::move(c), stream);
+  trace.mark("binning and feature-major copy", stream);
   // The raw matrix was uploaded only for the sketch; predictions upload it
   // again on demand.
   if (!uploaded && d_data) {
     XGBB_CUDA(cudaStreamSynchronize(stream));
     d_data.release();
+    trace.mark("release of the uploaded matrix", stream);
   }
 }
 

@@ -108,12 +108,13 @@ __global__ void sketch_links_kernel(uint32_t rows, uint32_t nf, uint32_t nseg, c
 
 // With `in_shared`, the sort keys live in shared memory (pow2_ceil(cap)
 // words) and, once sorted, the same space holds the rank sums the prune
-// searches.
+// searches. With `radix` as well, the sort is the block radix sort, whose
+// scratch takes the same space.
 __global__ void __launch_bounds__(kSketchThreads) sketch_batch_kernel(const Run* runs, const BatchTask* tasks,
                                                                       uint32_t ntasks, Entry* summaries,
                                                                       uint32_t* sizes, unsigned char* scratch,
                                                                       size_t scratch_stride, uint32_t cap,
-                                                                      bool in_shared) {
+                                                                      bool in_shared, bool radix) {
   extern __shared__ __align__(16) unsigned char fast[];
   BatchWork bw = batch_work_at(scratch + size_t(blockIdx.x) * scratch_stride, cap);
   if (in_shared) {
@@ -124,7 +125,7 @@ __global__ void __launch_bounds__(kSketchThreads) sketch_batch_kernel(const Run*
   for (uint32_t t = blockIdx.x; t < ntasks; t += gridDim.x) {
     const BatchTask task = tasks[t];
     const uint32_t n = summarize_par(ex, runs + task.run_begin, task.size, task.limit, bw.keys, bw.sorted, bw.entries,
-                                     summaries + task.summary_at, bw.w);
+                                     summaries + task.summary_at, bw.w, radix ? fast : nullptr);
     if (threadIdx.x == 0) sizes[task.size_slot] = n;
     __syncthreads();
   }
@@ -236,9 +237,11 @@ void sketch_cuts_device(const float* X, uint32_t rows, uint32_t cols, const floa
   d_counts.need(size_t(cols) * 4);
   XGBB_CUDA(cudaMemsetAsync(d_cuts.p, 0, size_t(cols) * stride * 4, stream));
   std::vector<uint32_t> stats;
+  Trace trace("sketch");
   for (uint32_t f0 = 0; f0 < cols; f0 += group) {
     const uint32_t nf = std::min(group, cols - f0);
     d_runs.need(size_t(nf) * std::max(rows, 1u) * sizeof(Run));
+    trace.mark("group scratch", stream);
     d_stats.need(size_t(nf) * 3 * 4);
     // Segments of whole chunks, about 4 blocks per SM in all.
     const uint32_t chunks = std::max(1u, (rows + kRunsChunk - 1) / kRunsChunk);
@@ -265,8 +268,10 @@ void sketch_cuts_device(const float* X, uint32_t rows, uint32_t cols, const floa
     stats.assign(size_t(nf) * 3, 0);
     XGBB_CUDA(cudaMemcpyAsync(stats.data(), d_stats.p, stats.size() * 4, cudaMemcpyDeviceToHost, stream));
     XGBB_CUDA(cudaStreamSynchronize(stream));
+    trace.mark("runs", stream);
     const GroupPlan plan = plan_group(stats.data(), nf, f0, rows, max_bin);
     const TreePlan tree = plan_tree(plan);
+    trace.mark("plan", stream);
     const std::vector<BatchTask>& tasks = plan.tasks;
     const std::vector<ReduceTask>& rtasks = plan.reduce;
     const uint32_t cap = plan.cap;
@@ -279,16 +284,20 @@ void sketch_cuts_device(const float* X, uint32_t rows, uint32_t cols, const floa
       const size_t scratch_stride = batch_scratch_bytes(cap);
       const size_t keys_bytes = size_t(pow2_ceil(cap)) * 8;
       const bool in_shared = keys_bytes <= kSketchSmem;
+      const size_t radix_bytes = radix_sort_bytes(cap, kSketchThreads / 32);
+      const bool radix = in_shared && radix_bytes <= kSketchSmem && cap < 65536;
+      const size_t batch_smem = radix ? std::max(keys_bytes, radix_bytes) : in_shared ? keys_bytes : 0;
       const uint32_t grid = uint32_t(std::min<size_t>(tasks.size(), size_t(sms) * (in_shared ? 1 : 2)));
       d_scratch.need(scratch_stride * grid);
       d_tasks.need(tasks.size() * sizeof(BatchTask));
       XGBB_CUDA(cudaMemcpyAsync(d_tasks.p, tasks.data(), tasks.size() * sizeof(BatchTask), cudaMemcpyHostToDevice,
                                 stream));
-      sketch_batch_kernel<<<grid, kSketchThreads, in_shared ? keys_bytes : 0, stream>>>(
+      sketch_batch_kernel<<<grid, kSketchThreads, batch_smem, stream>>>(
           d_runs.as<Run>(), d_tasks.as<BatchTask>(), uint32_t(tasks.size()), d_summaries.as<Entry>(),
-          d_sizes.as<uint32_t>(), d_scratch.as<unsigned char>(), scratch_stride, cap, in_shared);
+          d_sizes.as<uint32_t>(), d_scratch.as<unsigned char>(), scratch_stride, cap, in_shared, radix);
       XGBB_CUDA(cudaGetLastError());
     }
+    trace.mark("batch summaries", stream);
     uint32_t big = 2;
     for (const ReduceTask& rt : rtasks) big = std::max(big, reduce_big(rt.limit, rt.budget));
     const size_t fast_bytes = size_t(2) * big * sizeof(float);
@@ -320,6 +329,7 @@ void sketch_cuts_device(const float* X, uint32_t rows, uint32_t cols, const floa
         XGBB_CUDA(cudaGetLastError());
       }
     }
+    trace.mark("merge tree", stream);
     d_ftasks.need(tree.finish.size() * sizeof(FinishTask));
     d_res.need(std::max<size_t>(tree.res.size(), 1) * sizeof(FinishRes));
     XGBB_CUDA(cudaMemcpyAsync(d_ftasks.p, tree.finish.data(), tree.finish.size() * sizeof(FinishTask),
@@ -341,10 +351,12 @@ void sketch_cuts_device(const float* X, uint32_t rows, uint32_t cols, const floa
     XGBB_CUDA(cudaGetLastError());
     // The next group reuses the buffers.
     XGBB_CUDA(cudaStreamSynchronize(stream));
+    trace.mark("finish and reduce", stream);
   }
   XGBB_CUDA(cudaMemcpyAsync(cuts, d_cuts.p, size_t(cols) * stride * 4, cudaMemcpyDeviceToHost, stream));
   XGBB_CUDA(cudaMemcpyAsync(counts, d_counts.p, size_t(cols) * 4, cudaMemcpyDeviceToHost, stream));
   XGBB_CUDA(cudaStreamSynchronize(stream));
+  trace.mark("cuts to the host", stream);
 }
 
 }  // namespace xgbb

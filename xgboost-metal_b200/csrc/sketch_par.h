@@ -418,28 +418,45 @@ XGBB_HD inline uint32_t pow2_ceil(uint32_t x) {
   return p;
 }
 
+// Scratch of the radix form of the sort: two key and two 16-bit order
+// arrays of `size` entries, then 256 * (warps + 1) counters.
+XGBB_HD inline size_t radix_sort_bytes(uint32_t size, uint32_t warps) {
+  return size_t(size) * 12 + size_t(256) * (warps + 1) * 4;
+}
+
 template <class Ex>
 XGBB_HD uint32_t summarize_par(Ex& ex, const Run* runs, uint32_t size, uint32_t limit, unsigned long long* keys,
-                               Run* sorted, Entry* entries, Entry* out, Work w) {
+                               Run* sorted, Entry* entries, Entry* out, Work w, unsigned char* radix = nullptr) {
   if (!size) return 0;
-  const uint32_t p = pow2_ceil(size);
-  ex.for_each(p, [&](uint32_t i) {
-    keys[i] = i < size ? ((unsigned long long)order_key(runs[i].v) << 32) | i : ~0ull;
-  });
-  // Bitonic sort, ascending; keys are distinct, so the order is the stable
-  // order by value.
-  for (uint32_t k = 2; k <= p; k <<= 1)
-    for (uint32_t j = k >> 1; j > 0; j >>= 1)
-      ex.for_each(p / 2, [&](uint32_t t) {
-        const uint32_t i = 2 * j * (t / j) + t % j, l = i + j;  // pair (i, l), i < l
-        const bool up = (i & k) == 0;
-        const unsigned long long a = keys[i], b = keys[l];
-        if ((a > b) == up) {
-          keys[i] = b;
-          keys[l] = a;
-        }
-      });
-  ex.for_each(size, [&](uint32_t i) { sorted[i] = runs[uint32_t(keys[i] & 0xffffffffu)]; });
+  if (radix && size < 65536) {
+    // Stable radix sort of the order-preserving value keys.
+    uint32_t* k32 = reinterpret_cast<uint32_t*>(radix);
+    uint16_t* o16 = reinterpret_cast<uint16_t*>(k32 + 2 * size);
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(radix + size_t(size) * 12);
+    ex.for_each(size, [&](uint32_t i) { k32[i] = order_key(runs[i].v); });
+    ex.stable_order(k32, o16, size, k32 + size, o16 + size, cnt);
+    ex.for_each(size, [&](uint32_t i) { sorted[i] = runs[o16[i]]; });
+  } else {
+    const uint32_t p = pow2_ceil(size);
+    ex.for_each(p, [&](uint32_t i) {
+      keys[i] = i < size ? ((unsigned long long)order_key(runs[i].v) << 32) | i : ~0ull;
+    });
+    // Bitonic sort, ascending; keys are distinct, so the order is the stable
+    // order by value.
+    for (uint32_t k = 2; k <= p; k <<= 1)
+      for (uint32_t j = k >> 1; j > 0; j >>= 1)
+        ex.for_each(p / 2, [&](uint32_t t) {
+          // Pair (i, l), i < l: 2j * (t / j) + t % j, with j a power of two.
+          const uint32_t i = ((t & ~(j - 1)) << 1) | (t & (j - 1)), l = i + j;
+          const bool up = (i & k) == 0;
+          const unsigned long long a = keys[i], b = keys[l];
+          if ((a > b) == up) {
+            keys[i] = b;
+            keys[l] = a;
+          }
+        });
+    ex.for_each(size, [&](uint32_t i) { sorted[i] = runs[uint32_t(keys[i] & 0xffffffffu)]; });
+  }
   // Groups of equal values: head flags, group ids, weights summed in order.
   uint32_t* head = w.u;
   ex.for_each(size, [&](uint32_t i) { head[i] = (i == 0 || !(sorted[i].v == sorted[i - 1].v)) ? 1u : 0u; });
