@@ -821,21 +821,38 @@ __device__ __forceinline__ bool plan_round(const HistArgs& a, bool unit_h, LimbP
   return plan_round(a.scale, a.max_bits, a.min_limbs, a.staged, unit_h, pg, ph);
 }
 
-// Balanced two-limb split of q: l0 in [-2^(L-1), 2^(L-1)), l1 = (q - l0) / 2^L.
-__device__ __forceinline__ void split_balanced(long long q, uint32_t L, int& l0, int& l1) {
-  const long long half = 1ll << (L - 1);
-  l0 = int(((q + half) & ((1ll << L) - 1)) - half);
-  l1 = int((q - l0) >> L);  // exact: q - l0 is a multiple of 2^L
+// A two-limb split of q = rint(v * s) in float arithmetic on the FMA pipe,
+// which the histogram kernel leaves mostly idle: l1 = rint(q * 2^-L) and
+// l0 = q - l1 * 2^L. Every step is exact: q is an integer-valued float (s is
+// a power of two), scaling by 2^-L and rounding to an integer are exact, and
+// |l0| <= 2^(L-1) makes the fused multiply-add exact. So l0 + l1 * 2^L = q,
+// with |l0| <= 2^(L-1) and |l1| <= 2^(bits - L): the bounds the staged
+// kernel's normalisation interval assumes. (Ties give l0 = +2^(L-1), which
+// the balanced integer split avoids; only the sum reaches the histogram.)
+struct LimbSplit {
+  float two_l, inv_two_l;  // 2^L, 2^-L
+  __device__ __forceinline__ void operator()(float v, float s, int& l0, int& l1) const {
+    const float q = rintf(__fmul_rn(v, s));
+    const float hi = rintf(__fmul_rn(q, inv_two_l));
+    l1 = __float2int_rn(hi);
+    l0 = __float2int_rn(__fmaf_rn(-hi, two_l, q));
+  }
+};
+
+__device__ __forceinline__ LimbSplit limb_split(uint32_t L) {
+  return LimbSplit{__int_as_float(int(127 + L) << 23), __int_as_float(int(127 - L) << 23)};
 }
+
 // (g0, g1, h0, h1) of one row, or (g0, g1, 1, 0) with unit hessians.
-__device__ __forceinline__ int4 row_limbs(float2 gp, float2 sc, uint32_t Lg, uint32_t Lh, bool unit_h) {
+__device__ __forceinline__ int4 row_limbs(float2 gp, float2 sc, const LimbSplit& sg, const LimbSplit& sh,
+                                          bool unit_h) {
   int4 v;
-  split_balanced(__float2ll_rn(__fmul_rn(gp.x, sc.x)), Lg, v.x, v.y);
+  sg(gp.x, sc.x, v.x, v.y);
   if (unit_h) {
     v.z = 1;
     v.w = 0;
   } else {
-    split_balanced(__float2ll_rn(__fmul_rn(gp.y, sc.y)), Lh, v.z, v.w);
+    sh(gp.y, sc.y, v.z, v.w);
   }
   return v;
 }
@@ -954,6 +971,7 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
     return;
   }
   const uint32_t Lg = pg.L, Lh = ph.L;
+  const LimbSplit split_g = limb_split(Lg), split_h = limb_split(Lh);
   constexpr uint32_t kPlanes = kUnitH ? 3 : 4;  // g0, g1, h0 | count, h1
   constexpr uint32_t kPlaneBytes = kPlaneWords * sizeof(int);
   constexpr uint32_t kSlice = kHistLanes * sizeof(CodeT);  // bytes of a row's group slice
@@ -971,9 +989,8 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
   HistStage<CodeT>* stage = reinterpret_cast<HistStage<CodeT>*>(smem + kPlanes * kPlaneWords) + warp * kStageBufs;
   const float2 sc = *a.scale;
   const long long qh_unit = __float2ll_rn(sc.y);
-  // Limbs are balanced: l0 in [-2^(L-1), 2^(L-1)), l1 = (q - l0) / 2^L, so
-  // |l1| <= 2^(L-1) as well when |q| < 2^(2L-1): a row adds at most
-  // 2^per_row_bits to a word.
+  // Limbs (LimbSplit): |l0| <= 2^(L-1), and |l1| <= 2^(L-1) as well when
+  // |q| < 2^(2L-1): a row adds at most 2^per_row_bits to a word.
   const uint32_t Lmax = kUnitH ? Lg : (Lg > Lh ? Lg : Lh);
   const uint32_t per_row_bits =
       (pg.bits + 1 <= 2 * Lg && (kUnitH || ph.bits + 1 <= 2 * Lh)) ? Lmax - 1 : Lmax;
@@ -1171,7 +1188,7 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
       HistStage<CodeT>& st0 = stage[buf];
       // Lane = row: its two-limb values, formed once for 32 features; lanes
       // past n add zeros.
-      const int4 q = lane < s0.n() ? row_limbs(st0.pairs[lane], sc, Lg, Lh, kUnitH) : make_int4(0, 0, 0, 0);
+      const int4 q = lane < s0.n() ? row_limbs(st0.pairs[lane], sc, split_g, split_h, kUnitH) : make_int4(0, 0, 0, 0);
       constexpr uint32_t kQuads = kSlice / 16;
       constexpr uint32_t kPerQuad = 16 / sizeof(CodeT);
       uint32_t quad[kQuads][4];
