@@ -314,7 +314,7 @@ void DMatrix::quantise(uint32_t mb, const DMatrix* ref, cudaStream_t stream, int
     c->values.assign(size_t(cols) * c->stride, 0.0f);
     c->counts.assign(cols, 0);
     c->minima.assign(cols, -INFINITY);
-    // The GPU sketch (the same cuts, bit for bit) takes matrices of 2^26
+    // The GPU sketch (the same cuts, bit for bit) takes matrices of 2^24
     // values or more when the device holds the matrix plus its runs; the
     // host sketch takes smaller ones. XGBB_SKETCH=host|device overrides.
     const char* where = std::getenv("XGBB_SKETCH");
@@ -322,7 +322,7 @@ void DMatrix::quantise(uint32_t mb, const DMatrix* ref, cudaStream_t stream, int
     if (rows && cols) {
       size_t free_b = 0, total_b = 0;
       const size_t need = size_t(rows) * cols * sizeof(float) + size_t(rows) * 32 + (1ull << 30);
-      on_device = uint64_t(rows) * cols >= (1ull << 26) && cudaMemGetInfo(&free_b, &total_b) == cudaSuccess &&
+      on_device = uint64_t(rows) * cols >= (1ull << 24) && cudaMemGetInfo(&free_b, &total_b) == cudaSuccess &&
                   need <= free_b;
       if (where && std::strcmp(where, "device") == 0) on_device = true;
       if (where && std::strcmp(where, "host") == 0) on_device = false;
