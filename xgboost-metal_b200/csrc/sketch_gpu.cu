@@ -37,7 +37,7 @@ using namespace sketch;
 constexpr int kSketchThreads = 1024;
 // Shared memory for the batch sort keys and for the searched keys of merges
 // (a larger need falls back to the global scratch).
-constexpr size_t kSketchSmem = 200 * 1024;
+constexpr size_t kSketchSmem = 220 * 1024;
 
 // Runs of every feature of the group, rows split into gridDim.y segments of
 // seg_rows rows processed at the same time. Pass 1 (pass2 false): each
@@ -114,12 +114,22 @@ __global__ void __launch_bounds__(kSketchThreads) sketch_batch_kernel(const Run*
                                                                       uint32_t ntasks, Entry* summaries,
                                                                       uint32_t* sizes, unsigned char* scratch,
                                                                       size_t scratch_stride, uint32_t cap,
-                                                                      bool in_shared, bool radix) {
+                                                                      bool in_shared, bool radix, bool work_shared) {
   extern __shared__ __align__(16) unsigned char fast[];
   BatchWork bw = batch_work_at(scratch + size_t(blockIdx.x) * scratch_stride, cap);
   if (in_shared) {
     bw.keys = reinterpret_cast<unsigned long long*>(fast);
     bw.w.fa = reinterpret_cast<float*>(fast);
+  }
+  if (work_shared) {
+    // The summary's per-index words (head flags, group weights, rank sums,
+    // the prune's choices) in shared memory too: they are first written
+    // after the radix sort, whose scratch they then overwrite.
+    uint32_t* wb = reinterpret_cast<uint32_t*>(fast);
+    bw.w.u = wb;
+    bw.w.v = wb + cap + 2;
+    bw.w.f = reinterpret_cast<float*>(bw.w.v + cap + 2);
+    bw.w.fa = bw.w.f + cap + 2;
   }
   DeviceExec ex;
   for (uint32_t t = blockIdx.x; t < ntasks; t += gridDim.x) {
@@ -286,7 +296,10 @@ void sketch_cuts_device(const float* X, uint32_t rows, uint32_t cols, const floa
       const bool in_shared = keys_bytes <= kSketchSmem;
       const size_t radix_bytes = radix_sort_bytes(cap, kSketchThreads / 32);
       const bool radix = in_shared && radix_bytes <= kSketchSmem && cap < 65536;
-      const size_t batch_smem = radix ? std::max(keys_bytes, radix_bytes) : in_shared ? keys_bytes : 0;
+      const size_t work_bytes = size_t(4) * (cap + 2) * 4;
+      const bool work_shared = radix && work_bytes <= kSketchSmem;
+      const size_t batch_smem = radix ? std::max({keys_bytes, radix_bytes, work_shared ? work_bytes : size_t(0)})
+                                      : in_shared ? keys_bytes : 0;
       const uint32_t grid = uint32_t(std::min<size_t>(tasks.size(), size_t(sms) * (in_shared ? 1 : 2)));
       d_scratch.need(scratch_stride * grid);
       d_tasks.need(tasks.size() * sizeof(BatchTask));
@@ -294,7 +307,8 @@ void sketch_cuts_device(const float* X, uint32_t rows, uint32_t cols, const floa
                                 stream));
       sketch_batch_kernel<<<grid, kSketchThreads, batch_smem, stream>>>(
           d_runs.as<Run>(), d_tasks.as<BatchTask>(), uint32_t(tasks.size()), d_summaries.as<Entry>(),
-          d_sizes.as<uint32_t>(), d_scratch.as<unsigned char>(), scratch_stride, cap, in_shared, radix);
+          d_sizes.as<uint32_t>(), d_scratch.as<unsigned char>(), scratch_stride, cap, in_shared, radix,
+          work_shared);
       XGBB_CUDA(cudaGetLastError());
     }
     trace.mark("batch summaries", stream);
