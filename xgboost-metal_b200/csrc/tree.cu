@@ -1277,7 +1277,7 @@ struct Candidate {
 // forward candidates (missing right) and, when the node has missing rows,
 // backward candidates (missing left), each scored in binary64 with the
 // reference's rounding points; the best candidate by (gain, scan order).
-__global__ void __launch_bounds__(256) eval_kernel(EvalArgs a) {
+__global__ void __launch_bounds__(256, 2) eval_kernel(EvalArgs a) {
   const uint32_t lane = threadIdx.x & 31;
   const uint32_t nslots = a.state->frontier;
   const uint32_t C = a.e.cols, B = a.e.bins, B1 = B + 1;
