@@ -1,0 +1,46 @@
+"""The staged histogram kernel forms each row's two limbs in float arithmetic
+(tree.cu, LimbSplit): q = rint(v * s) with s a power of two, l1 = rint(q *
+2^-L), l0 = q - l1 * 2^L in one fused multiply-add. These checks restate that
+arithmetic in float32 and confirm the facts the kernel's exactness and its
+normalisation interval rest on, for every limb width the kernel uses and
+values up to its widest (2L bits): every step is exact, l0 + l1 * 2^L = q,
+|l0| <= 2^(L-1), and |l1| <= 2^(bits-L)."""
+import numpy as np
+import pytest
+
+
+def _split(q32, L):
+    inv = np.float32(2.0 ** -L)
+    two = np.float32(2.0 ** L)
+    scaled = (q32 * inv).astype(np.float32)
+    hi = np.rint(scaled).astype(np.float32)
+    # The fused multiply-add's exact value; it is representable (|l0| < 2^24),
+    # so the single rounding of the FMA leaves it unchanged.
+    l0 = q32.astype(np.float64) - hi.astype(np.float64) * float(two)
+    return scaled, hi, l0
+
+
+@pytest.mark.parametrize("L", [17, 18, 19, 20, 21])
+def test_float_limb_split_is_exact_and_bounded(L):
+    rng = np.random.default_rng(L)
+    for bits in range(1, 2 * L + 1):
+        mag = rng.integers(0, 1 << bits, 20000, dtype=np.int64)
+        sign = rng.choice(np.array([-1, 1], dtype=np.int64), mag.size)
+        # rint(v * s) of a float v and a power-of-two s: an integer-valued float.
+        q32 = (mag * sign).astype(np.float32)
+        scaled, hi, l0 = _split(q32, L)
+        q = q32.astype(np.float64)
+        assert np.array_equal(scaled.astype(np.float64), q * 2.0 ** -L)  # exact scaling
+        assert np.all(np.abs(l0) <= 2.0 ** (L - 1))
+        assert np.all(np.abs(l0) < 2.0 ** 24)
+        assert np.all(np.abs(hi) <= max(1.0, 2.0 ** (bits - L)))
+        assert np.array_equal(l0 + hi.astype(np.float64) * 2.0 ** L, q)
+
+
+def test_ties_round_to_even_and_stay_in_bounds():
+    L = 19
+    half = 2 ** (L - 1)
+    q32 = np.array([half, -half, 3 * half, -3 * half, 5 * half], dtype=np.float32)
+    _, hi, l0 = _split(q32, L)
+    assert np.all(np.abs(l0) <= half)
+    assert np.array_equal(l0 + hi.astype(np.float64) * 2.0 ** L, q32.astype(np.float64))
