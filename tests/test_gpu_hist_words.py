@@ -119,9 +119,16 @@ def test_c4_width_histogram_words_match_oracle():
 
 
 @pytest.mark.parametrize("case", ["unit_hessian_13_features", "weighted_u8_40_features",
-                                  "three_limb_small"])
+                                  "weighted_u8_40_features_unstaged", "three_limb_small",
+                                  "three_limb_small_unstaged"])
 def test_level_histogram_words_match_oracle(case):
+    """The weighted uint8 and three_limb_small cases have values wider than
+    42 bits, which the staged three-limb kernel builds; their `_unstaged`
+    forms (cuda_hist_staged3=0) build the same levels with the unstaged
+    three-limb kernel."""
     import xgboost as xgb
+    unstaged = case.endswith("_unstaged")
+    case = case.replace("_unstaged", "")
     rng = np.random.default_rng({"unit_hessian_13_features": 1, "weighted_u8_40_features": 2,
                                  "three_limb_small": 3}[case])
     if case == "unit_hessian_13_features":
@@ -147,5 +154,9 @@ def test_level_histogram_words_match_oracle(case):
     dtrain = xgb.DMatrix(X, label=y, weight=w)
     params = {"objective": objective, "max_depth": 8, "eta": 0.3, "max_bin": max_bin,
               "tree_method": "hist", "device": "cuda"}
+    if objective != "reg:squarederror" or weighted:
+        assert int(np.abs(q).max()).bit_length() > 42  # three-limb values
+    if unstaged:
+        params["cuda_hist_staged3"] = 0
     for depth in depths:
         _check_level(xgb, dtrain, params, X, bins, q, cuts.shape[1], depth)

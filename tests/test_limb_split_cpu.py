@@ -44,3 +44,47 @@ def test_ties_round_to_even_and_stay_in_bounds():
     _, hi, l0 = _split(q32, L)
     assert np.all(np.abs(l0) <= half)
     assert np.array_equal(l0 + hi.astype(np.float64) * 2.0 ** L, q32.astype(np.float64))
+
+
+def _split3(q32, L):
+    """The three-limb split (tree.cu, LimbSplit3) in float32, each fused
+    multiply-add taken at its exact value (representable, so the FMA's one
+    rounding leaves it unchanged; checked below)."""
+    top = np.rint((q32 * np.float32(2.0 ** (-2 * L))).astype(np.float32)).astype(np.float32)
+    r = q32.astype(np.float64) - top.astype(np.float64) * 2.0 ** (2 * L)
+    r32 = r.astype(np.float32)
+    assert np.array_equal(r32.astype(np.float64), r)  # the first FMA is exact
+    mid = np.rint((r32 * np.float32(2.0 ** -L)).astype(np.float32)).astype(np.float32)
+    l0 = r - mid.astype(np.float64) * 2.0 ** L
+    assert np.array_equal(l0.astype(np.float32).astype(np.float64), l0)  # and the second
+    return l0, mid.astype(np.float64), top.astype(np.float64)
+
+
+@pytest.mark.parametrize("L", [12, 15, 17, 21])
+def test_float_three_limb_split_is_exact_and_bounded(L):
+    rng = np.random.default_rng(100 + L)
+    for bits in range(1, min(3 * L - 1, 63) + 1):
+        mag = rng.integers(0, 1 << min(bits, 62), 20000, dtype=np.int64)
+        if bits == 63:
+            mag = mag * 2 + 1
+        sign = rng.choice(np.array([-1, 1], dtype=np.int64), mag.size)
+        q32 = (mag.astype(np.float64) * sign).astype(np.float32)  # a float q: <= 24 significant bits
+        l0, l1, l2 = _split3(q32, L)
+        assert np.all(np.abs(l0) <= 2.0 ** (L - 1)) and np.all(np.abs(l1) <= 2.0 ** (L - 1))
+        assert np.all(np.abs(l2) <= max(1.0, 2.0 ** (bits - 2 * L)))
+        total = l0 + l1 * 2.0 ** L + l2 * 2.0 ** (2 * L)  # exact in binary64 for these magnitudes
+        exact = [int(a) + int(b) * 2 ** L + int(c) * 2 ** (2 * L) for a, b, c in zip(l0[:200], l1[:200], l2[:200])]
+        assert exact == [int(v) for v in q32[:200].astype(np.float64)]
+        assert np.array_equal(total, q32.astype(np.float64))
+
+
+def test_three_limb_width_rule():
+    """limb3_width: L = ceil((bits + 1) / 3), within [12, 21], so that every
+    limb of a bits-wide value stays within 2^(L-1) below 63 bits."""
+    for bits in range(0, 64):
+        L = min(max((bits + 3) // 3, 12), 21)
+        if bits < 63:
+            assert bits - 2 * L <= L - 1
+        # the normalisation interval covers a whole 12-warp CTA step (384 rows)
+        per_row = max(L - 1, bits - 2 * L)
+        assert ((2 ** 31 - 1 - 2 ** 26) >> per_row) >= 384

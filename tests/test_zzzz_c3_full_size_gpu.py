@@ -1,11 +1,14 @@
 """The c3 shape at its full size: 1M rows x 784 features, integer values
-0..255 with 80 % exact zeros, 10 balanced classes, multi:softprob,
-max_depth 6, 256 bins (uint16 codes: 256 bins plus the missing bin).
+0..254 with 80 % exact zeros, 10 balanced classes, multi:softprob,
+max_depth 6, max_bin 256. Each feature has 255 bins, so the codes are uint8
+(255 bins plus the missing code); the cut stride stays max_bin, so the
+built histograms have 257 bins, the missing one last.
 
 784 features are 24.5 groups of 32, so the last histogram feature group is
 half full, and every round grows 10 trees. The values are drawn so that each
-feature takes every integer 0..255: the bins are the values themselves. The
-checks:
+feature takes every integer 0..254: the bins are the values themselves. At
+1M rows the first round's quantised gradients are 44 bits wide, so the
+staged three-limb histogram kernel builds these levels. The checks:
 
 - class 0's root and its deepest built level (5) match `orc_histogram` word
   for word on features of the first, a middle and the half-full last feature
@@ -25,6 +28,7 @@ from test_gpu_hist_words import _node_of_rows, _oracle_q, _tree_arrays
 pytestmark = pytest.mark.gpu
 
 ROWS, COLS, CLASSES, ZEROS = 1_000_000, 784, 10, 0.8
+NBINS = 255  # distinct values per feature
 SEL = (0, 17, 31, 32, 400, 767, 768, 775, 783)
 
 
@@ -38,7 +42,7 @@ def _data():
     step = 1 << 18
     for i in range(0, ROWS, step):
         n = min(step, ROWS - i)
-        c = torch.randint(1, 256, (n, COLS), generator=g, device="cuda", dtype=torch.int32)
+        c = torch.randint(1, NBINS, (n, COLS), generator=g, device="cuda", dtype=torch.int32)
         c.masked_fill_(torch.rand((n, COLS), generator=g, device="cuda") < ZEROS, 0)
         torch.from_numpy(X[i:i + n]).copy_(c.float())
         torch.from_numpy(bins[i:i + n].view(np.int32)).copy_(c.index_select(1, sel))
@@ -54,6 +58,7 @@ def c3_full():
     import xgboost as xgb
     X, bins, y = _data()
     q = np.ascontiguousarray(_oracle_q("multi:softprob", y, None, CLASSES))
+    assert int(np.abs(q).max()).bit_length() > 42
     dtrain = xgb.DMatrix(X, label=y)
     params = {"objective": "multi:softprob", "num_class": CLASSES, "max_depth": 6, "eta": 0.3,
               "max_bin": 256, "tree_method": "hist", "device": "cuda"}

@@ -1170,6 +1170,9 @@ void Booster::record_tree_launches(TrainState& ts, uint32_t g, cudaStream_t s, b
   tl.unit_hessian = ts.unit_hessian;
   tl.feature_group = ts.hc.feature_group;
   tl.min_limbs = uint32_t(integer(params_, "cuda_hist_limbs", 0));
+  // cuda_hist_staged3=0 keeps three-limb rounds on the unstaged kernel
+  // (tuning and cross-checks; results are identical).
+  tl.staged3 = integer(params_, "cuda_hist_staged3", 1) != 0;
   tl.hist_smem = ts.hc.smem;
   tl.hist_threads = ts.hc.threads;
   const int sms = device_sms();

@@ -445,6 +445,7 @@ struct HistArgs {
   longlong2* built;      // [cols_pad][pair_stride][bins + 1]
   uint32_t pair_stride;  // pairs of this level in the built layout
   bool staged;         // the staged two-limb kernel may take this level (bins + 1 <= 257)
+  bool staged3;        // the staged three-limb kernel takes the levels the two-limb one leaves
   uint32_t ngroups;
   uint32_t min_limbs;  // 3 forces three-limb accumulation (tuning; results unchanged)
 };
@@ -725,10 +726,12 @@ constexpr uint32_t kSlots = 257;                       // bins 0..255 + missing 
 constexpr uint32_t kPlaneWords = kSlots * kHistLanes;  // ints per plane
 constexpr uint32_t kH2Warps = 16;
 constexpr uint32_t kH2Threads = kH2Warps * 32;
+// The three-limb form keeps six planes (197 KB), so its CTA has 12 warps and
+// takes uint8 codes only: their stage buffers then fit beside the planes.
+constexpr uint32_t kH3Warps = 12;
 constexpr uint32_t kStageRows = 32;                    // rows per warp per step
 constexpr uint32_t kStepRows = kStageRows * kH2Warps;  // rows per CTA per step
 constexpr uint32_t kStageBufs = 2;                     // one step of copies in flight
-constexpr uint32_t kOwn4 = (kPlaneWords / 4 + kH2Threads - 1) / kH2Threads;  // word quads per thread
 // A normalisation carries only words above this magnitude; the rows between
 // two normalisations are limited so that a word left below it cannot
 // overflow (see hist2_kernel).
@@ -741,11 +744,20 @@ struct __align__(16) HistStage {
   float2 pairs[kStageRows];
 };
 
-template <typename CodeT, bool kUnitH>
-constexpr size_t hist2_smem() {
-  return size_t(kUnitH ? 3 : 4) * kPlaneWords * sizeof(int) +
-         size_t(kH2Warps) * kStageBufs * sizeof(HistStage<CodeT>);
+// Limb planes of the staged kernel: g0 g1 h0 h1 (g0 g1 count with unit
+// hessians) for two limbs, g0 g1 g2 h0 h1 h2 for three.
+template <bool kUnitH, uint32_t kLimbs>
+constexpr uint32_t staged_planes() {
+  return kLimbs == 3 ? 6u : (kUnitH ? 3u : 4u);
 }
+
+template <typename CodeT, bool kUnitH, uint32_t kLimbs = 2, uint32_t kWarps = kH2Warps>
+constexpr size_t hist2_smem() {
+  return size_t(staged_planes<kUnitH, kLimbs>()) * kPlaneWords * sizeof(int) +
+         size_t(kWarps) * kStageBufs * sizeof(HistStage<CodeT>);
+}
+static_assert(hist2_smem<uint16_t, false>() <= 227 * 1024 && hist2_smem<uint8_t, false, 3, kH3Warps>() <= 227 * 1024,
+              "staged histogram shared memory");
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
@@ -857,6 +869,40 @@ __device__ __forceinline__ int4 row_limbs(float2 gp, float2 sc, const LimbSplit&
   return v;
 }
 
+// The three-limb split of q = rint(v * s), in the same float arithmetic:
+// l2 = rint(q * 2^-2L), r = q - l2 * 2^2L, l1 = rint(r * 2^-L),
+// l0 = r - l1 * 2^L. Each step is exact. If |q| <= 2^(2L-1), l2 = 0 and r = q.
+// Otherwise ulp(q) >= 2^(2L-24) divides both q and l2 * 2^2L, and
+// |r| <= 2^(2L-1), so r has at most 24 significant bits; the same holds one
+// level down for l0. So l0 + l1 * 2^L + l2 * 2^2L = q, with |l0|, |l1| <=
+// 2^(L-1) and |l2| <= 2^(bits - 2L).
+struct LimbSplit3 {
+  float two_l, inv_two_l, two_2l, inv_two_2l;  // 2^L, 2^-L, 2^2L, 2^-2L
+  __device__ __forceinline__ void operator()(float v, float s, int& l0, int& l1, int& l2) const {
+    const float q = rintf(__fmul_rn(v, s));
+    const float top = rintf(__fmul_rn(q, inv_two_2l));
+    const float r = __fmaf_rn(-top, two_2l, q);
+    const float mid = rintf(__fmul_rn(r, inv_two_l));
+    l2 = __float2int_rn(top);
+    l1 = __float2int_rn(mid);
+    l0 = __float2int_rn(__fmaf_rn(-mid, two_l, r));
+  }
+};
+
+__device__ __forceinline__ LimbSplit3 limb_split3(uint32_t L) {
+  return LimbSplit3{__int_as_float(int(127 + L) << 23), __int_as_float(int(127 - L) << 23),
+                    __int_as_float(int(127 + 2 * L) << 23), __int_as_float(int(127 - 2 * L) << 23)};
+}
+
+// Limb width of the staged three-limb kernel for values of `bits` bits:
+// L = ceil((bits + 1) / 3), so that |l2| <= 2^(L-1) as well, and at least 12
+// (the register limb above l2 then holds any sum below 2^63 in int32), at
+// most 21.
+__device__ __forceinline__ uint32_t limb3_width(uint32_t bits) {
+  const uint32_t L = (bits + 3) / 3;
+  return L < 12 ? 12u : (L > 21 ? 21u : L);
+}
+
 
 // One step of one warp: up to kStageRows rows of one item, packed into three
 // registers (group < 2^22, pair < 2^10, rows of the CTA <= kStepRows).
@@ -872,7 +918,7 @@ struct HistStep {
 };
 static_assert(kMaxFrontier / 2 <= 0x400u && kStepRows <= 0xffffu && kStageRows <= 0xffu, "HistStep packing");
 
-template <bool kRoot>
+template <bool kRoot, uint32_t kStep = kStepRows>
 struct HistCursor {
   uint64_t it, end;
   uint32_t k;        // step within the item
@@ -922,8 +968,8 @@ struct HistCursor {
     HistStep s;
     const bool valid = it < end;
     s.gp = group << 10 | pair;
-    const uint32_t off = k * kStepRows;
-    const uint32_t cta_rows = valid ? min(kStepRows, cnt - off) : 0u;
+    const uint32_t off = k * kStep;
+    const uint32_t cta_rows = valid ? min(kStep, cnt - off) : 0u;
     const uint32_t w0 = off + warp * kStageRows;
     const uint32_t n = (valid && w0 < cnt) ? min(kStageRows, cnt - w0) : 0u;
     s.meta = uint32_t(valid) << 31 | cta_rows << 8 | n;
@@ -934,7 +980,7 @@ struct HistCursor {
   // order), so only a change of feature group needs the full lookup.
   __device__ __forceinline__ void advance(const HistArgs& a, uint32_t npairs) {
     if (it >= end) return;
-    if ((k + 1) * kStepRows < cnt) {
+    if ((k + 1) * kStep < cnt) {
       ++k;
       return;
     }
@@ -959,27 +1005,36 @@ struct HistCursor {
   }
 };
 
-template <typename CodeT, bool kUnitH, bool kRoot>
-__global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
+template <typename CodeT, bool kUnitH, bool kRoot, uint32_t kLimbs = 2, uint32_t kWarps = kH2Warps>
+__global__ void __launch_bounds__(kWarps * 32, 1) hist2_kernel(HistArgs a) {
+  static_assert(kLimbs == 2 || (kLimbs == 3 && !kUnitH && sizeof(CodeT) == 1), "staged limb forms");
+  constexpr uint32_t kThreads = kWarps * 32;
+  constexpr uint32_t kStep = kStageRows * kWarps;                          // rows per CTA per step
+  constexpr uint32_t kOwn4 = (kPlaneWords / 4 + kThreads - 1) / kThreads;  // word quads per thread
   extern __shared__ __align__(128) int smem[];
   const DriverState st = *a.state;
   if (!st.frontier || !st.total_tiles) return;
   LimbPlan pg, ph;
-  if (!plan_round(a, kUnitH, pg, ph)) return;  // the three-limb kernel builds this level
+  // Two limbs when every value of the round fits them; otherwise the
+  // three-limb form, staged here or the unstaged three-limb kernel.
+  const bool two = plan_round(a, kUnitH, pg, ph);
+  if (kLimbs == 2 ? !two : (two || !a.staged3)) return;
   if (static_cast<uint32_t>(__cvta_generic_to_shared(smem)) & 127u) {
     if (threadIdx.x == 0) atomicOr(&const_cast<DriverState*>(a.state)->error, kErrLayout);
     return;
   }
-  const uint32_t Lg = pg.L, Lh = ph.L;
+  const uint32_t Lg = kLimbs == 3 ? limb3_width(pg.bits) : pg.L;
+  const uint32_t Lh = kLimbs == 3 ? limb3_width(ph.bits) : ph.L;
   const LimbSplit split_g = limb_split(Lg), split_h = limb_split(Lh);
-  constexpr uint32_t kPlanes = kUnitH ? 3 : 4;  // g0, g1, h0 | count, h1
+  const LimbSplit3 split3_g = limb_split3(Lg), split3_h = limb_split3(Lh);
+  constexpr uint32_t kPlanes = staged_planes<kUnitH, kLimbs>();
   constexpr uint32_t kPlaneBytes = kPlaneWords * sizeof(int);
   constexpr uint32_t kSlice = kHistLanes * sizeof(CodeT);  // bytes of a row's group slice
   const uint32_t B = a.e.bins, B1 = B + 1, C = a.e.cols;
   const uint32_t words = B1 * kHistLanes;
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t npairs = kRoot ? 1u : st.pairs;
-  HistCursor<kRoot> cur;
+  HistCursor<kRoot, kStep> cur;
   hist_item_range(st.total_tiles, a.ngroups, cur.it, cur.end);
   cur.k = 0;
   cur.total_tiles = st.total_tiles;
@@ -990,10 +1045,18 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
   const float2 sc = *a.scale;
   const long long qh_unit = __float2ll_rn(sc.y);
   // Limbs (LimbSplit): |l0| <= 2^(L-1), and |l1| <= 2^(L-1) as well when
-  // |q| < 2^(2L-1): a row adds at most 2^per_row_bits to a word.
+  // |q| < 2^(2L-1): a row adds at most 2^per_row_bits to a word. Three limbs
+  // (LimbSplit3): |l0|, |l1| <= 2^(L-1) and |l2| <= 2^(bits-2L).
   const uint32_t Lmax = kUnitH ? Lg : (Lg > Lh ? Lg : Lh);
-  const uint32_t per_row_bits =
-      (pg.bits + 1 <= 2 * Lg && (kUnitH || ph.bits + 1 <= 2 * Lh)) ? Lmax - 1 : Lmax;
+  uint32_t per_row_bits;
+  if (kLimbs == 3) {
+    const uint32_t tg_bits = pg.bits > 2 * Lg ? pg.bits - 2 * Lg : 0u;
+    const uint32_t th_bits = ph.bits > 2 * Lh ? ph.bits - 2 * Lh : 0u;
+    const uint32_t top_bits = tg_bits > th_bits ? tg_bits : th_bits;
+    per_row_bits = top_bits > Lmax - 1 ? top_bits : Lmax - 1;
+  } else {
+    per_row_bits = (pg.bits + 1 <= 2 * Lg && (kUnitH || ph.bits + 1 <= 2 * Lh)) ? Lmax - 1 : Lmax;
+  }
   // A normalisation leaves every word at most kCarryAbove in magnitude (a
   // carried word restarts in [0, 2^L)), so `norm_rows` more rows keep it
   // inside int32.
@@ -1005,12 +1068,13 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
   for (uint32_t i = threadIdx.x; i < kPlanes * kPlaneWords; i += blockDim.x) smem[i] = 0;
   {
     int* sz = reinterpret_cast<int*>(stage - warp * kStageBufs);
-    const uint32_t n = kH2Warps * kStageBufs * sizeof(HistStage<CodeT>) / sizeof(int);
+    const uint32_t n = kWarps * kStageBufs * sizeof(HistStage<CodeT>) / sizeof(int);
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) sz[i] = 0;
   }
   __syncthreads();
 
-  // Carries out of limb 1 of the word quads tid + k * kH2Threads.
+  // Carries out of the top shared limb (limb 1, or limb 2 with three limbs)
+  // of the word quads tid + k * kThreads.
   int4 tg[kOwn4], th[kOwn4];
 #pragma unroll
   for (uint32_t k = 0; k < kOwn4; ++k) tg[k] = th[k] = make_int4(0, 0, 0, 0);
@@ -1052,13 +1116,21 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
     if (kRoot) return 0u;
     return lane < s.n() ? __ldg(a.rows + s.row0 + lane) : 0u;
   };
-  // Carries of one word pair (limb 0, limb 1) whose magnitude passed
-  // kCarryAbove: a floor carry from limb 0 into limb 1, and from limb 1 into
-  // the register limb `top`. Returns whether a word changed.
+  // Carries of the limbs of one word whose magnitude passed kCarryAbove: a
+  // floor carry from limb 0 into limb 1, from limb 1 into limb 2 (three
+  // limbs), and from the top shared limb into the register limb `top`. Each
+  // limb is checked after its carry in. Returns whether a word changed.
+  auto carry_up = [](int& x, int& next, uint32_t L) -> bool {
+    if (abs(x) <= kCarryAbove) return false;
+    const int c = x >> L;  // arithmetic shift: floor division by 2^L
+    x -= c * (1 << L);
+    next += c;
+    return true;
+  };
   auto carry1 = [](int& x0, int& x1, int& top, uint32_t L) -> bool {
     bool changed = false;
     if (abs(x0) > kCarryAbove) {
-      const int c0 = x0 >> L;  // arithmetic shift: floor division by 2^L
+      const int c0 = x0 >> L;
       x0 -= c0 * (1 << L);
       x1 += c0;
       changed = true;
@@ -1082,50 +1154,80 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
       *reinterpret_cast<int4*>(p1) = x1;
     }
   };
+  auto carry3 = [&](int* p0, int* p1, int* p2, int4& top, uint32_t L) {
+    int4 x0 = *reinterpret_cast<int4*>(p0), x1 = *reinterpret_cast<int4*>(p1),
+         x2 = *reinterpret_cast<int4*>(p2);
+    bool changed = carry_up(x0.x, x1.x, L) | carry_up(x0.y, x1.y, L) | carry_up(x0.z, x1.z, L) |
+                   carry_up(x0.w, x1.w, L);
+    changed |= carry1(x1.x, x2.x, top.x, L);
+    changed |= carry1(x1.y, x2.y, top.y, L);
+    changed |= carry1(x1.z, x2.z, top.z, L);
+    changed |= carry1(x1.w, x2.w, top.w, L);
+    if (changed) {
+      *reinterpret_cast<int4*>(p0) = x0;
+      *reinterpret_cast<int4*>(p1) = x1;
+      *reinterpret_cast<int4*>(p2) = x2;
+    }
+  };
   auto normalise = [&]() {
     __syncthreads();
 #pragma unroll
     for (uint32_t k = 0; k < kOwn4; ++k) {
-      const uint32_t i = 4 * (threadIdx.x + k * kH2Threads);
+      const uint32_t i = 4 * (threadIdx.x + k * kThreads);
       if (i < words) {
-        carry(smem + i, smem + kPlaneWords + i, tg[k], Lg);
-        if (!kUnitH) carry(smem + 2 * kPlaneWords + i, smem + 3 * kPlaneWords + i, th[k], Lh);
+        if (kLimbs == 3) {
+          carry3(smem + i, smem + kPlaneWords + i, smem + 2 * kPlaneWords + i, tg[k], Lg);
+          carry3(smem + 3 * kPlaneWords + i, smem + 4 * kPlaneWords + i, smem + 5 * kPlaneWords + i, th[k], Lh);
+        } else {
+          carry(smem + i, smem + kPlaneWords + i, tg[k], Lg);
+          if (!kUnitH) carry(smem + 2 * kPlaneWords + i, smem + 3 * kPlaneWords + i, th[k], Lh);
+        }
       }
     }
     __syncthreads();
   };
+  // Three limbs: l0 + l1 * 2^L + l2 * 2^2L + top * 2^3L, modulo 2^64.
+  auto combine = [](const int* p, int top, uint32_t L) -> long long {
+    return (long long)((unsigned long long)(long long)p[0] +
+                       ((unsigned long long)(long long)p[kPlaneWords] << L) +
+                       ((unsigned long long)(long long)p[2 * kPlaneWords] << (2 * L)) +
+                       ((unsigned long long)(long long)top << (3 * L)));
+  };
   auto flush = [&](uint32_t group, uint32_t pair) {
     __syncthreads();
     const uint32_t f0 = group * kHistLanes;
-    int* p0 = smem;
-    int* p1 = smem + kPlaneWords;
-    int* p2 = smem + 2 * kPlaneWords;
-    int* p3 = smem + 3 * kPlaneWords;
+    int* const ph0 = smem + (kLimbs == 3 ? 3 : 2) * kPlaneWords;  // h0, or the counts
 #pragma unroll
     for (uint32_t k = 0; k < kOwn4; ++k) {
-      const uint32_t i0 = 4 * (threadIdx.x + k * kH2Threads);
+      const uint32_t i0 = 4 * (threadIdx.x + k * kThreads);
       if (i0 < words) {
         const int tgs[4] = {tg[k].x, tg[k].y, tg[k].z, tg[k].w};
         const int ths[4] = {th[k].x, th[k].y, th[k].z, th[k].w};
 #pragma unroll
         for (uint32_t e = 0; e < 4; ++e) {
           const uint32_t i = i0 + e;
-          const int topg = tgs[e], toph = ths[e];
           const uint32_t slot = i / kHistLanes, f = f0 + (i % kHistLanes);
           const uint32_t bin = slot == miss_slot ? B : slot;
-          const long long g = (long long)((unsigned long long)(long long)p0[i] +
-                                          ((unsigned long long)(long long)p1[i] << Lg) +
-                                          ((unsigned long long)(long long)topg << (2 * Lg)));
-          long long h;
+          long long g, h;
           bool any;
-          if (kUnitH) {
-            h = (long long)((unsigned long long)(unsigned)p2[i] * (unsigned long long)qh_unit);
-            any = g != 0 || p2[i] != 0;
-          } else {
-            h = (long long)((unsigned long long)(long long)p2[i] +
-                            ((unsigned long long)(long long)p3[i] << Lh) +
-                            ((unsigned long long)(long long)toph << (2 * Lh)));
+          if constexpr (kLimbs == 3) {
+            g = combine(smem + i, tgs[e], Lg);
+            h = combine(ph0 + i, ths[e], Lh);
             any = g != 0 || h != 0;
+          } else {
+            const int topg = tgs[e], toph = ths[e];
+            g = (long long)((unsigned long long)(long long)smem[i] +
+                            ((unsigned long long)(long long)smem[kPlaneWords + i] << Lg) +
+                            ((unsigned long long)(long long)topg << (2 * Lg)));
+            if (kUnitH) {
+              h = (long long)((unsigned long long)(unsigned)ph0[i] * (unsigned long long)qh_unit);
+              any = g != 0 || ph0[i] != 0;
+            } else {
+              h = (long long)((unsigned long long)(long long)ph0[i] +
+                              ((unsigned long long)(long long)ph0[kPlaneWords + i] << Lh) +
+                              ((unsigned long long)(long long)toph << (2 * Lh)));
+              any = g != 0 || h != 0;
+            }
           }
           if (any && f < C) {
             longlong2* dst = a.built + (size_t(f) * a.pair_stride + pair) * B1 + bin;
@@ -1133,10 +1235,14 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
             atomicAdd(reinterpret_cast<unsigned long long*>(&dst->y), (unsigned long long)h);
           }
         }
-        *reinterpret_cast<int4*>(p0 + i0) = make_int4(0, 0, 0, 0);
-        *reinterpret_cast<int4*>(p1 + i0) = make_int4(0, 0, 0, 0);
-        *reinterpret_cast<int4*>(p2 + i0) = make_int4(0, 0, 0, 0);
-        if (!kUnitH) *reinterpret_cast<int4*>(p3 + i0) = make_int4(0, 0, 0, 0);
+        *reinterpret_cast<int4*>(smem + i0) = make_int4(0, 0, 0, 0);
+        *reinterpret_cast<int4*>(smem + kPlaneWords + i0) = make_int4(0, 0, 0, 0);
+        *reinterpret_cast<int4*>(smem + 2 * kPlaneWords + i0) = make_int4(0, 0, 0, 0);
+        if (kPlanes > 3) *reinterpret_cast<int4*>(smem + 3 * kPlaneWords + i0) = make_int4(0, 0, 0, 0);
+        if (kPlanes > 4) {
+          *reinterpret_cast<int4*>(smem + 4 * kPlaneWords + i0) = make_int4(0, 0, 0, 0);
+          *reinterpret_cast<int4*>(smem + 5 * kPlaneWords + i0) = make_int4(0, 0, 0, 0);
+        }
       }
       tg[k] = make_int4(0, 0, 0, 0);
       th[k] = make_int4(0, 0, 0, 0);
@@ -1186,9 +1292,20 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
     }
     if (s0.n()) {
       HistStage<CodeT>& st0 = stage[buf];
-      // Lane = row: its two-limb values, formed once for 32 features; lanes
-      // past n add zeros.
-      const int4 q = lane < s0.n() ? row_limbs(st0.pairs[lane], sc, split_g, split_h, kUnitH) : make_int4(0, 0, 0, 0);
+      // Lane = row: its limbs, formed once for 32 features; lanes past n add
+      // zeros. Three limbs: (g0, g1, h0, h1) in q and (g2, h2) in q3.
+      int2 q3 = make_int2(0, 0);
+      int4 q;
+      if constexpr (kLimbs == 3) {
+        q = make_int4(0, 0, 0, 0);
+        if (lane < s0.n()) {
+          const float2 gp = st0.pairs[lane];
+          split3_g(gp.x, sc.x, q.x, q.y, q3.x);
+          split3_h(gp.y, sc.y, q.z, q.w, q3.y);
+        }
+      } else {
+        q = lane < s0.n() ? row_limbs(st0.pairs[lane], sc, split_g, split_h, kUnitH) : make_int4(0, 0, 0, 0);
+      }
       constexpr uint32_t kQuads = kSlice / 16;
       constexpr uint32_t kPerQuad = 16 / sizeof(CodeT);
       uint32_t quad[kQuads][4];
@@ -1210,10 +1327,19 @@ __global__ void __launch_bounds__(kH2Threads, 1) hist2_kernel(HistArgs a) {
         const uint32_t w = quad[f / kPerQuad][(f % kPerQuad) * sizeof(CodeT) / 4];
         const uint32_t code = sizeof(CodeT) == 2 ? (w >> (16 * (f & 1))) & 0xffffu : (w >> (8 * (f & 3))) & 0xffu;
         const uint32_t addr = (code * (kHistLanes * 4) + tbase) ^ (4 * f);
-        red_shared(addr, q.x);
-        red_shared_at<kPlaneBytes>(addr, q.y);
-        red_shared_at<2 * kPlaneBytes>(addr, q.z);
-        if (!kUnitH) red_shared_at<3 * kPlaneBytes>(addr, q.w);
+        if (kLimbs == 3) {
+          red_shared(addr, q.x);
+          red_shared_at<kPlaneBytes>(addr, q.y);
+          red_shared_at<2 * kPlaneBytes>(addr, q3.x);
+          red_shared_at<3 * kPlaneBytes>(addr, q.z);
+          red_shared_at<4 * kPlaneBytes>(addr, q.w);
+          red_shared_at<5 * kPlaneBytes>(addr, q3.y);
+        } else {
+          red_shared(addr, q.x);
+          red_shared_at<kPlaneBytes>(addr, q.y);
+          red_shared_at<2 * kPlaneBytes>(addr, q.z);
+          if (!kUnitH) red_shared_at<3 * kPlaneBytes>(addr, q.w);
+        }
       }
     }
     __syncwarp();
@@ -1234,7 +1360,9 @@ __global__ void __launch_bounds__(1024, 1) hist_kernel(HistArgs a) {
   const DriverState st = *a.state;
   if (!st.frontier || !st.total_tiles) return;
   LimbPlan pg, ph;
-  if (plan_round(a, kUnitH, pg, ph)) return;  // the staged kernel builds this level
+  // The staged kernels build this level: the two-limb one when the round's
+  // values fit two limbs, else the three-limb one where it applies.
+  if (plan_round(a, kUnitH, pg, ph) || a.staged3) return;
   if (pg.n == 2 && ph.n == 2) hist_body<CodeT, kUnitH, kRoot, 2, 2>(a, smem, st, pg.L, ph.L);
   else if (pg.n == 2) hist_body<CodeT, kUnitH, kRoot, 2, 3>(a, smem, st, pg.L, ph.L);
   else if (ph.n == 2) hist_body<CodeT, kUnitH, kRoot, 3, 2>(a, smem, st, pg.L, ph.L);
@@ -2282,6 +2410,20 @@ void launch_hist_t(const HistArgs& args, int blocks, int threads, size_t smem, c
     }
     staged<<<blocks, kH2Threads, smem2, stream>>>(args);
   }
+  if constexpr (sizeof(CodeT) == 1 && !kUnit) {
+    if (args.staged3) {
+      // The staged three-limb kernel takes the rounds the two-limb one leaves
+      // (the unstaged three-limb kernel above then exits at once).
+      auto staged3 = hist2_kernel<CodeT, false, kRoot, 3, kH3Warps>;
+      constexpr size_t smem3 = hist2_smem<CodeT, false, 3, kH3Warps>();
+      static bool configured3 = false;
+      if (!configured3) {
+        XGBB_CUDA(cudaFuncSetAttribute(staged3, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem3)));
+        configured3 = true;
+      }
+      staged3<<<blocks, kH3Warps * 32, smem3, stream>>>(args);
+    }
+  }
 }
 }  // namespace
 
@@ -2444,6 +2586,7 @@ void tree_level_hist(const TreeWorkspace& ws, const TreeLaunch& tl, uint32_t dep
   a.built = ws.built;
   a.pair_stride = max_pairs_at(depth);
   a.staged = tl.ell.bins + 1 <= kSlots;
+  a.staged3 = a.staged && tl.staged3 && tl.ell.bytes_per_code == 1 && !tl.unit_hessian;
   a.max_bits = tl.max_bits;
   a.min_limbs = tl.min_limbs;
   a.ngroups = (tl.ell.cols + kHistLanes - 1) / kHistLanes;

@@ -85,6 +85,7 @@ struct TreeLaunch {
   int hist_blocks, hist_threads, eval_blocks, part_blocks;
   uint32_t feature_group;    // features per histogram CTA
   uint32_t min_limbs;        // 3 forces three-limb histogram accumulation
+  bool staged3 = true;       // uint8 rounds of three-limb values take the staged three-limb kernel
   size_t hist_smem;
   uint32_t cols_pad;         // features in the built layout (a multiple of the ranks)
   uint32_t f_lo, f_hi;       // features whose splits this rank evaluates
