@@ -1,10 +1,12 @@
-"""The staged histogram kernel forms each row's two limbs in float arithmetic
+"""The staged histogram kernels form each row's limbs in float arithmetic
 (tree.cu, LimbSplit): q = rint(v * s) with s a power of two, l1 = rint(q *
-2^-L), l0 = q - l1 * 2^L in one fused multiply-add. These checks restate that
-arithmetic in float32 and confirm the facts the kernel's exactness and its
-normalisation interval rest on, for every limb width the kernel uses and
-values up to its widest (2L bits): every step is exact, l0 + l1 * 2^L = q,
-|l0| <= 2^(L-1), and |l1| <= 2^(bits-L)."""
+2^-L), l0 = q - l1 * 2^L in one fused multiply-add; the three-limb form
+(LimbSplit3) first takes l2 = rint(q * 2^-2L) and splits the remainder the
+same way. These checks restate that arithmetic in float32 and confirm the
+facts the kernels' exactness and their normalisation intervals rest on, for
+every limb width they use and values up to the widest each takes: every step
+is exact, the limbs sum to q, |l0| (and |l1| with three limbs) <= 2^(L-1),
+and the top limb <= 2^(bits - L) (two limbs) or 2^(bits - 2L) (three)."""
 import numpy as np
 import pytest
 

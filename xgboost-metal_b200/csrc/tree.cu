@@ -6,7 +6,8 @@
 //   mass_*/scales        kernels/gradient_quantization.metal.h:1-67
 //   hist_kernel          kernels/boost.metal:700-733, histogram_missing.metal.h
 //   hist2_kernel         the same sums, staged two-limb form (each row's
-//                        values formed once per 32 features)
+//                        values formed once per 32 features), and a staged
+//                        three-limb form for uint8 rounds of wider values
 //   eval_kernel          kernels/boost.metal:902-1005 (+ subtraction :780-794);
 //                        pack_best / merge_best select across ranks
 //   transpose_codes_kernel, narrow_codes_kernel: layouts of the same codes
@@ -699,10 +700,12 @@ __device__ __forceinline__ void hist_body(const HistArgs& a, int* smem, const Dr
 }
 
 // ---------------------------------------------------------------------------
-// Staged two-limb histogram (every |q| of the round has at most 2L bits).
+// Staged histogram: two limbs (every |q| of the round has at most 2L bits),
+// or three limbs for uint8 codes with real hessians (wider values).
 //
 // One CTA per SM over tile-ordered (feature group, pair, tile) items, as
-// hist_body, with 16 warps. Each warp copies the 32-feature code slices and
+// hist_body, with 16 warps (12 for three limbs, whose six limb planes leave
+// room for fewer stage buffers). Each warp copies the 32-feature code slices and
 // the precomputed limbs of its next 32 rows into one of two shared-memory
 // stage buffers with cp.async, one step ahead of the step it accumulates, and
 // loads the row ids one step ahead of the copies.
