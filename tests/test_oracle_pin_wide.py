@@ -121,3 +121,30 @@ def test_reference_softmax_gradients_agree_with_the_oracle():
     diff = np.abs(got.astype(np.float64) - want.astype(np.float64))
     assert diff.max() <= 2.0 ** -24
     assert (diff == 0).mean() > 0.7
+
+
+def test_reference_level_loop_at_c4_width_matches_its_serial_form():
+    """The bench's reference arm (the reference's functions over its
+    feature-major uint16 bins, the smaller child of each pair built and its
+    sibling subtracted, on all host threads) grows the same depth-10 tree as
+    the reference's serial form and the oracle at c4's width."""
+    o, r = C.oracle(), C.reference()
+    rng = np.random.default_rng(4404)
+    rows, cols = 16_000, 128
+    X = rng.normal(size=(rows, cols)).astype(np.float32)
+    X[rng.random(X.shape) < 0.05] = np.nan
+    y = (rng.random(rows) < 0.4).astype(np.float32)
+    cuts, counts, minima = r.sketch_cuts(X, 256)
+    bins = r.quantize(X, cuts, counts)
+    fm = C.reference_quantize_fm(X, cuts, counts)
+    pairs = C.oracle_gradients("binary:logistic", np.zeros((rows, 1), np.float32), y)
+    scale = r.gradient_scales(pairs)[0]
+    q = r.quantize_gradients(pairs, scale[None])[:, 0, :]
+    tp = _tree_params(10, 0.1)
+    nf, lf = C.reference_grow_tree_fm(fm, q, scale, cuts, counts, minima, tp)
+    ns, ls = r.grow_tree(bins, q, scale, cuts, counts, minima, tp)
+    no, lo = o.grow_tree(bins, q, scale, cuts, counts, minima, tp)
+    assert len(no) > 100
+    assert nf.tobytes() == ns.tobytes() == no.tobytes()
+    np.testing.assert_array_equal(_bits(lf), _bits(ls))
+    np.testing.assert_array_equal(_bits(np.float32(0) + lo), _bits(ls))
