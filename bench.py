@@ -244,6 +244,67 @@ def shard(rows, rank, world):
     return rows * rank // world, rows * (rank + 1) // world
 
 
+# The reference's benchmark records the SHA-256 of its input rows and labels
+# with every run (benchmarks/controlled_comparison.py:107-108). A 25.6 GB
+# matrix takes too long to hash serially, and a shard's hash depends on the
+# GPU count, so the digest here is a hash of block hashes: SHA-256 of each
+# block of rows (X bytes then y bytes), then SHA-256 over the block digests
+# in row order. Blocks divide every shard of 1, 2, 4 and 8 ranks, so every
+# GPU count gives the same digest for the same rows.
+DIGEST_BLOCK_ROWS = 250_000
+
+
+def digest_block_rows(rows):
+    """Rows per digest block: the largest divisor of rows/8 that is at most
+    DIGEST_BLOCK_ROWS when 8 divides the rows (so blocks tile the shards of
+    1, 2, 4 and 8 ranks), else the whole matrix."""
+    if rows % 8:
+        return rows
+    eighth = rows // 8
+    for d in range(min(eighth, DIGEST_BLOCK_ROWS), 0, -1):
+        if eighth % d == 0:
+            return d
+    return eighth
+
+
+def block_digests(Xh, yh, block, threads):
+    """SHA-256 of each `block` rows of (Xh, yh), in row order, hashed on
+    `threads` host threads (hashlib releases the GIL on large buffers)."""
+    import hashlib
+    from concurrent.futures import ThreadPoolExecutor
+    assert Xh.shape[0] == yh.shape[0] and Xh.shape[0] % block == 0, "blocks must tile the rows"
+    X2 = np.ascontiguousarray(Xh)
+    y2 = np.ascontiguousarray(yh)
+
+    def one(b):
+        h = hashlib.sha256(memoryview(X2[b * block:(b + 1) * block]).cast("B"))
+        h.update(memoryview(y2[b * block:(b + 1) * block]).cast("B"))
+        return h.digest()
+
+    with ThreadPoolExecutor(max_workers=max(1, threads)) as pool:
+        return list(pool.map(one, range(Xh.shape[0] // block)))
+
+
+def data_digest(Xh, yh, rows, dist):
+    """{input_sha256, blocks, block_rows} over all ranks' rows, on rank 0
+    (None elsewhere); outside every timed region."""
+    import hashlib
+    block = digest_block_rows(rows)
+    if Xh.shape[0] % block:
+        block = Xh.shape[0] if dist.world == 1 else 0
+    mine = b"".join(block_digests(Xh, yh, block, cpu_cores() // dist.world)) if block else b"?"
+    parts = dist.gather_bytes(mine)
+    if parts is None:
+        return None
+    if any(p == b"?" for p in parts):
+        return {"input_sha256": None, "note": "the shards do not divide into equal digest blocks"}
+    joined = b"".join(parts)
+    return {"input_sha256": hashlib.sha256(joined).hexdigest(), "blocks": len(joined) // 32,
+            "block_rows": block,
+            "note": "SHA-256 over the SHA-256 of each block of rows (float32 X bytes, then float32 "
+                    "labels), blocks in row order; the same at every GPU count"}
+
+
 def parity_digest(bst, dtrain, dist, next_round):
     """SHA-256 of every tree of the booster (node arrays of the model JSON)
     and of the root level's int64 (g, h) histogram words of one more round,
@@ -557,6 +618,9 @@ def main():
     t = time.perf_counter()
     Xh, yh = gen_rows(wl, begin, end, device)
     log("rank %d: rows [%d, %d) generated in %.1fs" % (dist.rank, begin, end, time.perf_counter() - t))
+    t = time.perf_counter()
+    digest = data_digest(Xh, yh, spec["rows"], dist)
+    log("rank %d: data digest in %.1fs" % (dist.rank, time.perf_counter() - t))
     params = params_for(wl)
     K, W = args.steps, args.warmup
     groups = groups_of(wl)
@@ -667,6 +731,7 @@ def main():
                         "K rounds; wall clock, max over ranks. ingest = H2D + sketch of all rows + "
                         "binning; the ingest is amortised over K rounds in value"},
         "parity": parity,
+        "data_digest": digest,
         "phases": phases,
         "c2": c2,
         "gpu_launches": launches_per_round(spec["max_depth"], groups) * K,

@@ -1,0 +1,104 @@
+"""The bench line's data digest: a hash of the SHA-256 of each block of rows
+(X bytes, then labels), blocks in row order, that every GPU count must give
+alike for the same rows. Checked here on the CPU with the bench's own
+functions: the block size tiles the shards of 1, 2, 4 and 8 ranks at every
+workload's row count, the digest of a whole matrix equals the one gathered
+from its shards over two and four gloo ranks (the bench's own Dist class),
+and one changed value changes it."""
+import hashlib
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+import bench  # noqa: E402
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _matrix(rows, cols=6, seed=11):
+    rng = np.random.default_rng(seed)
+    X = rng.normal(size=(rows, cols)).astype(np.float32)
+    X[rng.random(X.shape) < 0.05] = np.nan
+    return X, rng.normal(size=rows).astype(np.float32)
+
+
+class _OneRank:
+    rank, world = 0, 1
+
+    def gather_bytes(self, data):
+        return [data]
+
+
+@pytest.mark.parametrize("wl", sorted(bench.WORKLOADS))
+def test_blocks_tile_every_shard(wl):
+    rows = bench.WORKLOADS[wl]["rows"]
+    block = bench.digest_block_rows(rows)
+    assert 0 < block <= bench.DIGEST_BLOCK_ROWS
+    for world in (1, 2, 4, 8):
+        for rank in range(world):
+            lo, hi = bench.shard(rows, rank, world)
+            assert lo % block == 0 and (hi - lo) % block == 0, (wl, world, rank)
+
+
+def test_one_rank_digest_is_a_hash_of_block_hashes():
+    X, y = _matrix(4000)
+    block = bench.digest_block_rows(4000)
+    assert block == 500
+    want = b"".join(hashlib.sha256(X[b:b + block].tobytes() + y[b:b + block].tobytes()).digest()
+                    for b in range(0, 4000, block))
+    got = bench.data_digest(X, y, 4000, _OneRank())
+    assert got["input_sha256"] == hashlib.sha256(want).hexdigest()
+    assert got["blocks"] == 8 and got["block_rows"] == 500
+    X2 = X.copy()
+    X2[3999, 5] = np.float32(1.5)
+    assert bench.data_digest(X2, y, 4000, _OneRank())["input_sha256"] != got["input_sha256"]
+
+
+def test_rows_that_eight_does_not_divide_hash_as_one_block():
+    X, y = _matrix(1001)
+    assert bench.digest_block_rows(1001) == 1001
+    got = bench.data_digest(X, y, 1001, _OneRank())
+    assert got["blocks"] == 1
+    assert got["input_sha256"] == hashlib.sha256(
+        hashlib.sha256(X.tobytes() + y.tobytes()).digest()).hexdigest()
+
+
+def _rank(rank, world, port, rows, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    d = bench.Dist()
+    X, y = _matrix(rows)
+    lo, hi = bench.shard(rows, rank, world)
+    got = bench.data_digest(np.ascontiguousarray(X[lo:hi]), np.ascontiguousarray(y[lo:hi]), rows, d)
+    if rank == 0:
+        out["digest"] = got["input_sha256"]
+        out["blocks"] = got["blocks"]
+    else:
+        out["other"] = got
+    d.close()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_gloo_ranks_give_the_one_rank_digest(world):
+    rows = 8 * 700
+    X, y = _matrix(rows)
+    want = bench.data_digest(X, y, rows, _OneRank())
+    out = mp.Manager().dict()
+    mp.spawn(_rank, args=(world, _free_port(), rows, out), nprocs=world, join=True)
+    assert out["digest"] == want["input_sha256"]
+    assert out["blocks"] == want["blocks"] == 8
+    assert out["other"] is None
