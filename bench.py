@@ -392,6 +392,24 @@ def cpu_cores():
         return os.cpu_count()
 
 
+def cpu_model():
+    """The host CPU's model name and logical CPU count, recorded beside the
+    CPU timings (the reference's benchmark records the platform with each
+    run)."""
+    name = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    name = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    import platform
+    return {"model": name or platform.processor() or platform.machine(), "logical_cpus": os.cpu_count(),
+            "usable_cpus": cpu_cores()}
+
+
 def _full_rows_model(wl, device, measured):
     """A labelled estimate of the reference path at the workload's full row
     count: per-round seconds t = a + b * rows fitted through a second,
@@ -423,6 +441,7 @@ def cpu_baseline_leg(wl, device):
     ref.round()
     per_round = min(ref.round() for _ in range(3))
     out = {"value": round(per_round * 1e5, 1), "unit": UNIT, "cores": cpu_cores(), "kind": "reference",
+           "cpu": cpu_model(),
            "rows": rows,
            "sample": "the reference's CPU path (oracle/_ref: its gradients, scales, split evaluation, "
                      "selection, tree driver and predict functions over its feature-major uint16 bins, "
@@ -461,6 +480,7 @@ def reference_arm(args, wl, device):
             "config": {"workload": wl, "rows": rows, "sample_of_rows": spec["rows"], "cols": spec["cols"],
                        "max_depth": spec["max_depth"], "objective": spec["objective"]},
             "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": cpu_cores(), "kind": "reference",
+                             "cpu": cpu_model(),
                              "sample": sample},
             "e2e": {"value": round(value, 1), "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}

@@ -4,7 +4,8 @@ alike for the same rows. Checked here on the CPU with the bench's own
 functions: the block size tiles the shards of 1, 2, 4 and 8 ranks at every
 workload's row count, the digest of a whole matrix equals the one gathered
 from its shards over two and four gloo ranks (the bench's own Dist class),
-and one changed value changes it."""
+and one changed value changes it. Also the CPU record that goes beside the
+CPU timings."""
 import hashlib
 import os
 import socket
@@ -102,3 +103,9 @@ def test_gloo_ranks_give_the_one_rank_digest(world):
     assert out["digest"] == want["input_sha256"]
     assert out["blocks"] == want["blocks"] == 8
     assert out["other"] is None
+
+
+def test_cpu_record_names_the_host():
+    got = bench.cpu_model()
+    assert isinstance(got["model"], str) and got["model"]
+    assert got["logical_cpus"] >= got["usable_cpus"] == bench.cpu_cores() >= 1
