@@ -1084,7 +1084,9 @@ XGB_DLL int XGBBQuantizeHost(const float* X, bst_ulong rows, bst_ulong cols, uin
   });
 }
 
-// Test entry: the host quantile sketch on its own (no device needed).
+// Test entries: an evaluation metric over host predictions, its per-row
+// (loss, weight) sums, and the metric from sums gathered over workers (no
+// device needed).
 XGB_DLL int XGBBMetricHost(char const* name, const float* pred, bst_ulong rows, uint32_t groups,
                            const float* labels, const float* weights, int multiclass, double* out) {
   return guarded([&] {
@@ -1114,6 +1116,9 @@ XGB_DLL int XGBBMetricFromSums(char const* name, double loss_sum, double weight_
   });
 }
 
+// Test entry: the quantile sketch on the GPU (sketch_gpu.cu) over a host
+// matrix copied in; cuts [cols][min(max_bin, rows)], counts and minima as
+// XGBBSketchHost returns them.
 XGB_DLL int XGBBSketchDevice(const float* X, bst_ulong rows, bst_ulong cols, const float* weights,
                              uint32_t max_bin, float* cuts, uint32_t* counts, float* minima) {
   return guarded([&] {
@@ -1151,6 +1156,7 @@ XGB_DLL int XGBBProbeSharedPipe(int variant, uint32_t warps, uint32_t iters, dou
   });
 }
 
+// Test entry: the host quantile sketch on its own (no device needed).
 XGB_DLL int XGBBSketchHost(const float* X, bst_ulong rows, bst_ulong cols, const float* weights,
                            uint32_t max_bin, int threads, float* cuts, uint32_t* counts, float* minima) {
   return guarded([&] {
