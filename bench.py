@@ -325,12 +325,29 @@ def parity_digest(bst, dtrain, dist, next_round):
             "note": "trees after warm-up + timed rounds; root histogram of the round after them"}
 
 
-def launches_per_round(depth, groups):
-    # gradients, window, scales, exact, exact scales; per tree: init, 5 per
-    # level (three-limb and staged histogram kernels, one of which exits at
-    # once; evaluation, control, partition), 2 per non-last level (counts,
-    # plan).
-    return 5 + groups * (1 + 5 * depth + 2 * (depth - 1))
+def launches_per_round(spec, world, rows_local):
+    """This library's kernel launches in one device-driven round of
+    workload `spec` on `world` ranks holding `rows_local` rows each.
+
+    Per round: gradients, mass window, scales, exact mass, exact scales, and
+    with several ranks the mass limbs' two conversions around their sum.
+    Per tree: init; per level the histogram launches (the unstaged
+    three-limb kernel and the staged two-limb one, one of which exits at
+    once, plus the staged three-limb one for uint8 codes with real
+    hessians), evaluation and control, and with several ranks the best-split
+    pack and merge; per level but the last, partition, child counts and the
+    next level's plan; at the last level one margin pass per 96 MiB of the
+    rank's margins (tree.cu, tree_level_partition)."""
+    depth = spec["max_depth"]
+    groups = int(spec.get("num_class", 1))
+    codes8 = spec["nan"] == 0  # 256 bins: uint8 codes only without missing values
+    unit_h = spec["objective"] == "reg:squarederror"
+    hist = 2 + (1 if codes8 and not unit_h else 0)
+    margin_bytes = rows_local * 4 * min(groups, 8)
+    passes = max(1, -(-margin_bytes // (96 << 20)))
+    sharded = world > 1
+    per_tree = 1 + depth * (hist + 2 + 2 * sharded) + 3 * (depth - 1) + passes
+    return 5 + 2 * sharded + groups * per_tree
 
 
 # ---------------------------------------------------------------------------
@@ -754,7 +771,7 @@ def main():
         "data_digest": digest,
         "phases": phases,
         "c2": c2,
-        "gpu_launches": launches_per_round(spec["max_depth"], groups) * K,
+        "gpu_launches": launches_per_round(spec, dist.world, end - begin) * K,
         "clocks": clocks.summary(),
     }
     if dist.rank == 0:

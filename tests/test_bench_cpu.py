@@ -1,11 +1,15 @@
-"""The bench line's data digest: a hash of the SHA-256 of each block of rows
-(X bytes, then labels), blocks in row order, that every GPU count must give
-alike for the same rows. Checked here on the CPU with the bench's own
-functions: the block size tiles the shards of 1, 2, 4 and 8 ranks at every
+"""Host-side parts of the bench line, checked on the CPU with bench.py's own
+functions.
+
+The data digest: a hash of the SHA-256 of each block of rows (X bytes, then
+labels), blocks in row order, that every GPU count must give alike for the
+same rows. The block size tiles the shards of 1, 2, 4 and 8 ranks at every
 workload's row count, the digest of a whole matrix equals the one gathered
 from its shards over two and four gloo ranks (the bench's own Dist class),
-and one changed value changes it. Also the CPU record that goes beside the
-CPU timings."""
+and one changed value changes it.
+
+The kernel launch count (`gpu_launches`) against the committed launch list
+of the c4 bench, and the CPU record that goes beside the CPU timings."""
 import hashlib
 import os
 import socket
@@ -109,3 +113,19 @@ def test_cpu_record_names_the_host():
     got = bench.cpu_model()
     assert isinstance(got["model"], str) and got["model"]
     assert got["logical_cpus"] >= got["usable_cpus"] == bench.cpu_cores() >= 1
+
+
+def test_launch_count_matches_the_committed_c4_launch_list():
+    """profiles/launches_c4_bench.md lists 1,131 launches of this library's
+    kernels over 15 c4 rounds on one GPU, 3 of them base_chunk_kernel and 3
+    fill_margins_kernel (one each per booster's first round): 75 per round,
+    the last level's margins in two passes over 50M rows."""
+    W = bench.WORKLOADS
+    assert bench.launches_per_round(W["c4"], 1, 50_000_000) == (1131 - 3 - 3) // 15 == 75
+    # Sharded: two mass-limb conversions per round, pack and merge per level,
+    # and one margin pass once a rank's margins fit in 96 MiB.
+    assert bench.launches_per_round(W["c4"], 2, 25_000_000) == 75 + 2 + 20 - 1
+    assert bench.launches_per_round(W["c4"], 8, 6_250_000) == 96
+    # uint8 codes with real hessians add the staged three-limb launch per level.
+    c3 = bench.launches_per_round(W["c3"], 1, 1_000_000)
+    assert c3 == 5 + 10 * (1 + 6 * 5 + 3 * 5 + 1)
