@@ -1,0 +1,98 @@
+"""Pins the oracle against the reference's own serial kernel functions
+(oracle/_ref) on the missing-value edge families the reference's own tests
+exercise (tests/test_histogram_missing.py:11-20, 63-80 of the reference):
+mostly-missing rows with explicit zeros, rows that are entirely missing, a
+column that is entirely missing and a partial last feature group; row
+counts around the SIMD width and the histogram tile (1, 31-33, 255-257,
+2049); a matrix with no value at all; and dense data with no missing value.
+Each case runs three squared-error rounds at depth 4 (base margin 0) and
+compares cuts, bins, gradient scales, quantised gradients, node tables and
+per-row leaf values bit for bit."""
+import numpy as np
+import pytest
+
+import checkers as C
+
+pytestmark = pytest.mark.skipif(not C.have_reference(),
+                                reason="reference harness not built (no reference checkout)")
+
+TREE = dict(max_depth=4, eta=0.3, reg_lambda=1.0, reg_alpha=0.0, min_child_weight=1.0,
+            max_delta_step=0.0, min_split_loss=0.0)
+
+
+def _bits(a):
+    return np.ascontiguousarray(a).view(np.uint32 if a.dtype == np.float32 else a.dtype)
+
+
+def _sparse_rows(rows, density=0.05, seed=7315):
+    """7 features, about `density` of the cells present; a label from a few
+    of the features before masking; explicit zeros in feature 0 every 17th
+    row; every 29th row entirely missing; the last feature never present."""
+    rng = np.random.default_rng(seed)
+    X = rng.normal(size=(rows, 7)).astype(np.float32)
+    y = (X[:, 0] - X[:, 1] * X[:, 2] + X[:, 3] ** 2).astype(np.float32)
+    X[rng.random(X.shape) >= density] = np.nan
+    X[1::17, 0] = 0.0
+    X[::29] = np.nan
+    X[:, -1] = np.nan
+    return X, y
+
+
+def _pin(X, y, max_bin, rounds=3):
+    o, r = C.oracle(), C.reference()
+    co, cr = o.sketch_cuts(X, max_bin), r.sketch_cuts(X, max_bin)
+    for a, b in zip(co, cr):
+        np.testing.assert_array_equal(_bits(a), _bits(b))
+    bins = o.quantize(X, co[0], co[1])
+    np.testing.assert_array_equal(bins, r.quantize(X, cr[0], cr[1]))
+    margins = np.zeros((len(y), 1), np.float32)
+    nodes = 0
+    for _ in range(rounds):
+        pairs = C.oracle_gradients("reg:squarederror", margins, y)
+        np.testing.assert_array_equal(_bits(pairs), _bits(C.reference_gradients("reg:squarederror", margins, y)))
+        scale = o.gradient_scales(pairs)
+        np.testing.assert_array_equal(_bits(scale), _bits(r.gradient_scales(pairs)))
+        q = o.quantize_gradients(pairs, scale)
+        np.testing.assert_array_equal(q, r.quantize_gradients(pairs, scale))
+        no, lo = o.grow_tree(bins, q[:, 0, :], scale[0], co[0], co[1], co[2], TREE)
+        nr, lr = r.grow_tree(bins, q[:, 0, :], scale[0], co[0], co[1], co[2], TREE)
+        assert no.tobytes() == nr.tobytes()
+        # The harness reports a row's leaf as 0 + leaf (the reference's
+        # predict kernel), which reads a -0.0 leaf as +0.0.
+        np.testing.assert_array_equal(_bits(np.float32(0) + lo), _bits(lr))
+        margins[:, 0] += lo
+        nodes += len(no)
+    return nodes, bins
+
+
+@pytest.mark.parametrize("max_bin", [16, 256])
+def test_mostly_missing_rows_with_explicit_zeros(max_bin):
+    X, y = _sparse_rows(769)
+    nodes, bins = _pin(X, y, max_bin)
+    assert (bins == C.MISSING).mean() > 0.9
+    assert (bins[:, -1] == C.MISSING).all() and (bins[::29] == C.MISSING).all()
+    assert nodes > 3
+
+
+@pytest.mark.parametrize("rows", [1, 31, 32, 33, 255, 256, 257, 2049])
+def test_partial_simd_groups_and_tiles(rows):
+    X, y = _sparse_rows(rows)
+    if rows == 1:
+        X.fill(np.nan)
+    _pin(X, y, 16, rounds=1)
+
+
+def test_matrix_without_any_value():
+    X = np.full((529, 7), np.nan, np.float32)
+    y = np.linspace(-1, 1, len(X), dtype=np.float32)
+    nodes, bins = _pin(X, y, 16, rounds=2)
+    assert (bins == C.MISSING).all()
+    assert nodes == 2  # one leaf per round
+
+
+def test_dense_ramp_without_missing_values():
+    X = np.arange(257 * 7, dtype=np.float32).reshape(-1, 7) / 100
+    y = (X[:, 0] > 3).astype(np.float32)
+    nodes, bins = _pin(X, y, 256, rounds=2)
+    assert not (bins == C.MISSING).any()
+    assert nodes > 2
