@@ -96,3 +96,96 @@ def test_dense_ramp_without_missing_values():
     nodes, bins = _pin(X, y, 256, rounds=2)
     assert not (bins == C.MISSING).any()
     assert nodes > 2
+
+
+def _tree_family(case, rows=513):
+    """The depth-wise tree families of the reference's own tests
+    (tests/test_gpu_tree.py:36-80 of the reference), restated: 7 N(0, 1)
+    features and a label from four of them, then one change per case."""
+    rng = np.random.default_rng(82171)
+    X = rng.normal(size=(rows, 7)).astype(np.float32)
+    y = (X[:, 0] - X[:, 1] * X[:, 2] + X[:, 3] ** 2).astype(np.float32)
+    w = None
+    objective, groups = "reg:squarederror", 1
+    if case == "missing":
+        X[::7, 0] = np.nan
+        X[::11, 3] = np.nan
+        X[:, 6] = np.nan
+    elif case == "ties":   # four values, every feature a copy of the first
+        X[:, 0] = np.arange(rows) % 4
+        X[:, 1:] = X[:, :1]
+        y = (X[:, 0] >= 2).astype(np.float32)
+    elif case == "constant":
+        y.fill(0)
+    elif case == "weighted":   # weights in (0.01, 3), every 13th row weight 0
+        w = rng.uniform(0.01, 3, rows).astype(np.float32)
+        w[::13] = 0
+    elif case == "multiclass":
+        y = np.argmax(X[:, :3], axis=1).astype(np.float32)
+        objective, groups = "multi:softprob", 3
+    elif case == "subnormal_features":
+        tiny = np.nextafter(np.float32(0), np.float32(1))
+        X[:, 0] = np.resize(np.asarray([-4 * tiny, -tiny, -0.0, 0.0, tiny, 4 * tiny], np.float32), rows)
+        y = (np.arange(rows) % 6 >= 3).astype(np.float32)
+    return X, y, w, objective, groups
+
+
+def _zeros_as_positive(a):
+    return np.where(a == 0, np.float32(0), a).astype(a.dtype)
+
+
+def _thresholds_as_positive(nodes):
+    out = nodes.copy()
+    out["threshold"] = _zeros_as_positive(out["threshold"])
+    return out
+
+
+@pytest.mark.parametrize("case", ["regression", "missing", "ties", "constant", "weighted", "multiclass",
+                                  "subnormal_features"])
+def test_reference_tree_families(case):
+    """max_bin 32, depth 4, three rounds (one tree per class), base margin 0:
+    weighted cuts and gradients where the case has weights; the oracle's
+    gradient pairs feed both growers (softmax probabilities may round
+    differently through the host libm's exp). Each side grows from its own
+    cuts. The one deliberate difference: the oracle (and the library) reads
+    -0.0 as +0.0 in the sketch, while the reference keeps the sign of the
+    first zero of a run, so where a column holds signed zeros a cut, and a
+    threshold at that cut, may be -0.0 in the reference and +0.0 here. The
+    two compare equal, so the bins, the splits and the leaf values are the
+    same; every other bit is compared as is."""
+    o, r = C.oracle(), C.reference()
+    X, y, w, objective, groups = _tree_family(case)
+    co, cr = o.sketch_cuts(X, 32, w), r.sketch_cuts(X, 32, w)
+    np.testing.assert_array_equal(co[1], cr[1])
+    np.testing.assert_array_equal(_bits(co[2]), _bits(cr[2]))
+    signed_zero = (co[0] == 0) & (_bits(co[0]) != _bits(cr[0]))
+    assert (case == "subnormal_features") or not signed_zero.any()
+    assert not (_bits(co[0]) != _bits(cr[0]))[~signed_zero].any()
+    assert (_bits(co[0])[signed_zero] == 0).all()
+    bins = o.quantize(X, co[0], co[1])
+    np.testing.assert_array_equal(bins, r.quantize(X, cr[0], cr[1]))
+    margins = np.zeros((len(y), groups), np.float32)
+    nodes = 0
+    for _ in range(3):
+        pairs = C.oracle_gradients(objective, margins, y, w)
+        if objective == "reg:squarederror":
+            np.testing.assert_array_equal(_bits(pairs), _bits(C.reference_gradients(objective, margins, y, w)))
+        scales = o.gradient_scales(pairs)
+        np.testing.assert_array_equal(_bits(scales), _bits(r.gradient_scales(pairs)))
+        q = o.quantize_gradients(pairs, scales)
+        np.testing.assert_array_equal(q, r.quantize_gradients(pairs, scales))
+        for g in range(groups):
+            no, lo = o.grow_tree(bins, q[:, g, :], scales[g], co[0], co[1], co[2], TREE)
+            nr, lr = r.grow_tree(bins, q[:, g, :], scales[g], cr[0], cr[1], cr[2], TREE)
+            assert len(no) == len(nr), (case, g)
+            if signed_zero.any():
+                assert _thresholds_as_positive(no).tobytes() == _thresholds_as_positive(nr).tobytes(), (case, g)
+            else:
+                assert no.tobytes() == nr.tobytes(), (case, g)
+            np.testing.assert_array_equal(_bits(np.float32(0) + lo), _bits(lr))
+            margins[:, g] += lo
+            nodes += len(no)
+    if case == "constant":
+        assert nodes == 3
+    else:
+        assert nodes > 3 * groups
