@@ -189,3 +189,48 @@ def test_reference_tree_families(case):
         assert nodes == 3
     else:
         assert nodes > 3 * groups
+
+
+@pytest.mark.parametrize("bins", [2, 31, 32, 33, 127, 256])
+@pytest.mark.parametrize("custom", [False, True])
+def test_regularised_split_scan_families(bins, custom):
+    """The split-scan family of the reference's tests
+    (tests/test_split_scan.py:8-31 of the reference), restated for the
+    depth-wise path: values on a 1/64 grid (many ties), feature 1 a copy of
+    feature 0, missing values in three features, alpha 0.17, lambda 0.4,
+    max_delta_step 1, min_child_weight 0.5, eta 0.2; and with `custom` the
+    caller's fixed gradients in quarters and hessians of 1.25 or -0.5."""
+    o, r = C.oracle(), C.reference()
+    rng = np.random.default_rng(833)
+    X = rng.integers(-200, 201, (1025, 7)).astype(np.float32) / 64
+    X[:, 1] = X[:, 0]
+    y = (1.2 * X[:, 0] - X[:, 3] ** 2 + X[:, 5]).astype(np.float32)
+    X[::11, 2] = np.nan
+    X[::13, 4] = np.nan
+    X[::17, 6] = np.nan
+    tp = dict(max_depth=4, eta=0.2, reg_lambda=0.4, reg_alpha=0.17, min_child_weight=0.5,
+              max_delta_step=1.0, min_split_loss=0.0)
+    co, cr = o.sketch_cuts(X, bins), r.sketch_cuts(X, bins)
+    for a, b in zip(co, cr):
+        np.testing.assert_array_equal(_bits(a), _bits(b))
+    bins_ = o.quantize(X, co[0], co[1])
+    np.testing.assert_array_equal(bins_, r.quantize(X, cr[0], cr[1]))
+    row = np.arange(len(X))
+    margins = np.zeros((len(X), 1), np.float32)
+    nodes = 0
+    for _ in range(3):
+        if custom:
+            pairs = np.stack([((row % 7 - 3) / 4), np.where(row % 5, 1.25, -0.5)], 1).astype(np.float32)[:, None, :]
+        else:
+            pairs = C.oracle_gradients("reg:squarederror", margins, y)
+        scale = o.gradient_scales(pairs)
+        np.testing.assert_array_equal(_bits(scale), _bits(r.gradient_scales(pairs)))
+        q = o.quantize_gradients(pairs, scale)
+        np.testing.assert_array_equal(q, r.quantize_gradients(pairs, scale))
+        no, lo = o.grow_tree(bins_, q[:, 0, :], scale[0], co[0], co[1], co[2], tp)
+        nr, lr = r.grow_tree(bins_, q[:, 0, :], scale[0], cr[0], cr[1], cr[2], tp)
+        assert no.tobytes() == nr.tobytes()
+        np.testing.assert_array_equal(_bits(np.float32(0) + lo), _bits(lr))
+        margins[:, 0] += lo
+        nodes += len(no)
+    assert nodes >= 3
