@@ -134,3 +134,60 @@ def test_sparse_rows_without_missing_values(harness):
     # Every code present (uint8 with 256 bins and no missing value).
     inputs = _inputs(8, rows=6000, cols=3, max_bin=256, nan=0.0)
     _check(harness, inputs, dict(BASE, max_depth=12), sparse=True)
+
+
+def _inputs_from(X, pairs, max_bin):
+    o = C.oracle()
+    cuts, counts, minima = o.sketch_cuts(X, max_bin)
+    bins = o.quantize(X, cuts, counts)
+    pairs = np.ascontiguousarray(pairs, np.float32)
+    scale = o.gradient_scales(pairs[:, None, :])[0]
+    q = o.quantize_gradients(pairs[:, None, :], scale[None])[:, 0, :]
+    return bins, q, pairs, scale, cuts, counts, minima
+
+
+@pytest.mark.parametrize("max_bin", [2, 33, 256])
+@pytest.mark.parametrize("lossguide", [False, True])
+def test_reference_split_scan_family(harness, max_bin, lossguide):
+    """The split-scan family of the reference's tests
+    (tests/test_split_scan.py:8-31 of the reference): values on a 1/64 grid,
+    feature 1 a copy of feature 0, missing values in three features, the
+    caller's gradients in quarters and hessians of 1.25 or -0.5, alpha 0.17,
+    lambda 0.4, max_delta_step 1, min_child_weight 0.5; depth 4, or
+    loss-guided with at most 15 leaves."""
+    rng = np.random.default_rng(833)
+    X = rng.integers(-200, 201, (1025, 7)).astype(np.float32) / 64
+    X[:, 1] = X[:, 0]
+    X[::11, 2] = np.nan
+    X[::13, 4] = np.nan
+    X[::17, 6] = np.nan
+    row = np.arange(len(X))
+    pairs = np.stack([(row % 7 - 3) / 4, np.where(row % 5, 1.25, -0.5)], 1)
+    params = dict(BASE, eta=0.2, reg_lambda=0.4, reg_alpha=0.17, min_child_weight=0.5, max_delta_step=1.0,
+                  max_depth=0 if lossguide else 4)
+    got = _check(harness, _inputs_from(X, pairs, max_bin), params, lossguide=lossguide,
+                 max_leaves=15 if lossguide else 0)
+    assert len(got) > 3
+    assert not (got["feature"] == 1).any()  # ties with feature 0 go to the smaller feature
+
+
+@pytest.mark.parametrize("sparse", [False, True])
+@pytest.mark.parametrize("lossguide", [False, True])
+def test_reference_missing_family(harness, sparse, lossguide):
+    """The missing-value family of the reference's tests
+    (tests/test_histogram_missing.py:11-20 of the reference): about 95 % of
+    the cells missing, explicit zeros in feature 0, every 29th row and the
+    last feature entirely missing; node histograms dense or from the rows'
+    present codes."""
+    rng = np.random.default_rng(7315)
+    X = rng.normal(size=(2049, 7)).astype(np.float32)
+    y = X[:, 0] - X[:, 1] * X[:, 2] + X[:, 3] ** 2
+    X[rng.random(X.shape) >= 0.05] = np.nan
+    X[1::17, 0] = 0.0
+    X[::29] = np.nan
+    X[:, -1] = np.nan
+    pairs = np.stack([-y, np.ones(len(y))], 1)
+    params = dict(BASE, max_depth=0 if lossguide else 4)
+    got = _check(harness, _inputs_from(X, pairs, 16), params, lossguide=lossguide,
+                 max_leaves=12 if lossguide else 0, sparse=sparse)
+    assert len(got) > 3
