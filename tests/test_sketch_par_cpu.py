@@ -154,3 +154,26 @@ def test_segments_link_runs_spanning_many_segments(harness):
             got = _parallel(harness, X, 16, weights, chunk=128, segments=segments, tree=1)
             np.testing.assert_array_equal(got[1], want[1])
             np.testing.assert_array_equal(got[0].view(np.uint32), want[0].view(np.uint32))
+
+
+@pytest.mark.skipif(not __import__("checkers").have_reference(), reason="reference harness not built")
+@pytest.mark.parametrize("family", range(18))
+def test_reference_cut_families_against_the_reference_kernels(harness, family):
+    """The weight and value families of the reference's own cut tests
+    (tests/test_quantiles.py:9-20 of the reference; restated in
+    test_oracle_pin_sketch.py) through the GPU sketch's data-parallel
+    functions, in every mode the kernels use, against the reference's own
+    sketch kernels compiled for the host: cuts, counts and minima bit for
+    bit."""
+    import checkers as C
+    import test_oracle_pin_sketch as F
+    rows, bins, kind = F.FAMILIES[family]
+    X, w = F._family(rows, kind)
+    weights = None if kind == "unit" else w
+    want = C.reference().sketch_cuts(X, bins, weights)
+    for segments, tree in MODES:
+        got = _parallel(harness, X, bins, weights, 1024, segments, tree)
+        msg = "%s: segments %d tree %d" % (kind, segments, tree)
+        np.testing.assert_array_equal(got[1], want[1], err_msg=msg)
+        np.testing.assert_array_equal(got[0].view(np.uint32), want[0].view(np.uint32), err_msg=msg)
+        np.testing.assert_array_equal(got[2].view(np.uint32), want[2].view(np.uint32), err_msg=msg)
