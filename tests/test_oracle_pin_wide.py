@@ -148,3 +148,18 @@ def test_reference_level_loop_at_c4_width_matches_its_serial_form():
     assert nf.tobytes() == ns.tobytes() == no.tobytes()
     np.testing.assert_array_equal(_bits(lf), _bits(ls))
     np.testing.assert_array_equal(_bits(np.float32(0) + lo), _bits(ls))
+
+
+def test_c2_full_size_matches_reference():
+    """c2 at its full size, the north_star's 10x configuration: 262,144 rows
+    of 64 N(0, 1) features, a linear label with noise, squared error, 256
+    bins, depth 8, two rounds (trees of up to 511 nodes). The GPU tests hold
+    the CUDA path to the oracle at this size (test_c2_full_size_matches_oracle);
+    this holds the oracle to the reference."""
+    rng = np.random.default_rng(1337)
+    X = rng.normal(size=(262_144, 64)).astype(np.float32)
+    w = np.random.default_rng(1338).normal(size=64)
+    y = (X @ w + 0.1 * rng.normal(size=len(X))).astype(np.float32)
+    cuts, bins = _same_cuts(X, 256)
+    nodes = _boost("reg:squarederror", bins, cuts, y, 1, _tree_params(8, 0.3), 2)
+    assert nodes > 800
