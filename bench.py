@@ -373,10 +373,11 @@ class ReferencePath:
     cuts and bins come from the reference's own sketch and quantize kernel
     (the DMatrix step, not timed)."""
 
-    def __init__(self, wl, rows, device):
+    def __init__(self, wl, rows, device, keep_trees=False):
         import checkers as C
         self.C = C
         self.r = C.reference()
+        self.trees = [] if keep_trees else None
         spec = WORKLOADS[wl]
         self.spec, self.rows = spec, rows
         X, self.y = gen_rows(wl, 0, rows, device, pin=False)
@@ -396,10 +397,41 @@ class ReferencePath:
         scale = self.r.gradient_scales(pairs)
         q = self.r.quantize_gradients(pairs, scale)
         for g in range(self.groups):   # one tree per class
-            _, leaf = C.reference_grow_tree_fm(self.fm, q[:, g, :], scale[g], self.cuts, self.counts,
-                                               self.minima, self.tp)
+            nodes, leaf = C.reference_grow_tree_fm(self.fm, q[:, g, :], scale[g], self.cuts, self.counts,
+                                                   self.minima, self.tp)
             self.margins[:, g] += leaf
+            if self.trees is not None:
+                self.trees.append(nodes)
         return time.perf_counter() - t
+
+
+def compare_trees(got, want):
+    """The first difference between two lists of node tables (this
+    library's 48-byte records or the reference path's 40-byte ones, by field
+    name), or None: structure, features, leaf values and covers bit for bit,
+    and at split nodes the thresholds, gains, default directions and split
+    bins."""
+    def bits(a):
+        return np.ascontiguousarray(a).view(np.uint32)
+    if len(got) != len(want):
+        return "%d trees against %d" % (len(got), len(want))
+    for t, (g, w) in enumerate(zip(got, want)):
+        if len(g) != len(w):
+            return "tree %d: %d nodes against %d" % (t, len(g), len(w))
+        for f in ("left", "right", "parent", "feature"):
+            if not np.array_equal(g[f], w[f]):
+                return "tree %d: %s" % (t, f)
+        for f in ("leaf", "cover"):
+            if not np.array_equal(bits(g[f]), bits(w[f])):
+                return "tree %d: %s" % (t, f)
+        split = w["left"] >= 0
+        for f in ("threshold", "gain"):
+            if not np.array_equal(bits(g[f][split]), bits(w[f][split])):
+                return "tree %d: %s" % (t, f)
+        for f in ("default_left", "split_bin"):
+            if not np.array_equal(g[f][split].astype(np.int64), w[f][split].astype(np.int64)):
+                return "tree %d: %s" % (t, f)
+    return None
 
 
 def cpu_cores():
@@ -536,15 +568,35 @@ def c2_comparison(xgb, core, device, rounds=100, ref_rounds=3):
            "device_ms_per_100_rounds": round(dev_ms, 2)}
     import checkers as C
     if C.have_reference():
-        ref = ReferencePath(wl, spec["rows"], device)
+        ref = ReferencePath(wl, spec["rows"], device, keep_trees=True)
         ref.round()
         t = float(np.mean([ref.round() for _ in range(ref_rounds)]))
+        out["reference_parity"] = c2_reference_parity(ref, Xh, yh, params, ref_rounds + 1)
         out.update({"reference_cpu_ms_per_100_rounds": round(t * 1e5, 1), "reference_cpu_cores": cpu_cores(),
                     "reference_cpu_rounds_timed": ref_rounds,
                     "speedup_e2e": round(t * 1e5 / e2e_ms, 1), "speedup_device": round(t * 1e5 / dev_ms, 1),
                     "reference": "the reference's CPU path (oracle/_ref) on all rows; stock XGBoost CPU hist "
                                  "is not installable here"})
     return out
+
+
+def c2_reference_parity(ref, Xh, yh, params, rounds):
+    """This library's c2 trees against the reference path's (`ref`, which
+    has just grown `rounds` rounds from margin 0 over all of c2's rows with
+    the reference's own functions): the same rounds through the library's
+    training entry point with base_score 0, compared node for node. A
+    failure here is recorded, never raised: the bench line still prints."""
+    try:
+        import product as P
+        p = {k: v for k, v in params.items() if k not in ("device", "tree_method", "seed")}
+        trees, _ = P.train(Xh, yh, dict(p, base_score=0.0), rounds)
+        diff = compare_trees(trees, ref.trees)
+        return {"rounds": rounds, "trees": len(trees), "nodes": int(sum(len(t) for t in trees)),
+                "identical": diff is None, "first_difference": diff,
+                "note": "this library's trees (XGBBTrainHost, base_score 0) against the reference's own "
+                        "CPU path over all 262,144 rows, node for node"}
+    except Exception as e:  # noqa: BLE001 -- recorded in the line instead
+        return {"rounds": rounds, "identical": None, "error": "%s: %s" % (type(e).__name__, e)}
 
 
 def measured_peak():

@@ -129,3 +129,40 @@ def test_launch_count_matches_the_committed_c4_launch_list():
     # uint8 codes with real hessians add the staged three-limb launch per level.
     c3 = bench.launches_per_round(W["c3"], 1, 1_000_000)
     assert c3 == 5 + 10 * (1 + 6 * 5 + 3 * 5 + 1)
+
+
+@pytest.mark.skipif(not __import__("checkers").have_reference(), reason="reference harness not built")
+def test_tree_comparison_of_the_c2_reference_parity_check():
+    """compare_trees, which the bench's c2 leg uses to hold this library's
+    trees to the reference path's: equal tables give None, across the two
+    record layouts (the library's 48-byte records, the reference harness's
+    40-byte ones); a changed threshold, leaf bit or node count is named."""
+    import checkers as C
+    import product as P
+    o, r = C.oracle(), C.reference()
+    rng = np.random.default_rng(21)
+    X = rng.normal(size=(3000, 5)).astype(np.float32)
+    y = (X[:, 0] - X[:, 1] ** 2).astype(np.float32)
+    cuts, counts, minima = r.sketch_cuts(X, 64)
+    bins = r.quantize(X, cuts, counts)
+    pairs = C.oracle_gradients("reg:squarederror", np.zeros((3000, 1), np.float32), y)
+    s = r.gradient_scales(pairs)
+    q = r.quantize_gradients(pairs, s)
+    tp = dict(max_depth=5, eta=0.3, reg_lambda=1.0, reg_alpha=0.0, min_child_weight=1.0, max_delta_step=0.0,
+              min_split_loss=0.0)
+    want = [r.grow_tree(bins, q[:, 0, :], s[0], cuts, counts, minima, tp)[0]]
+    dev = np.zeros(len(want[0]), P.DEVNODE_DTYPE)
+    for f in C.NODE_DTYPE.names:
+        dev[f] = want[0][f]
+    assert bench.compare_trees([dev], want) is None
+    assert bench.compare_trees([o.grow_tree(bins, q[:, 0, :], s[0], cuts, counts, minima, tp)[0]], want) is None
+    changed = dev.copy()
+    split = np.nonzero(changed["left"] >= 0)[0][1]
+    changed["threshold"][split] = np.nextafter(changed["threshold"][split], np.float32(np.inf))
+    assert bench.compare_trees([changed], want) == "tree 0: threshold"
+    changed = dev.copy()
+    leaf = np.nonzero(changed["left"] < 0)[0][0]
+    changed["leaf"][leaf] = -changed["leaf"][leaf]
+    assert bench.compare_trees([changed], want) == "tree 0: leaf"
+    assert bench.compare_trees([dev[:-1]], want).startswith("tree 0: ")
+    assert bench.compare_trees([], want) == "0 trees against 1"
