@@ -486,7 +486,9 @@ def cpu_baseline_leg(wl, device):
     if not C.have_reference():
         return None
     rows = cpu_sample_rows(wl)
-    ref = ReferencePath(wl, rows, device)
+    spec = WORKLOADS[wl]
+    check = spec["objective"] == "binary:logistic"
+    ref = ReferencePath(wl, rows, device, keep_trees=check)
     ref.round()
     per_round = min(ref.round() for _ in range(3))
     out = {"value": round(per_round * 1e5, 1), "unit": UNIT, "cores": cpu_cores(), "kind": "reference",
@@ -497,6 +499,14 @@ def cpu_baseline_leg(wl, device):
                      "smaller child built, sibling subtracted) on the first %d rows of %s, best of 3 "
                      "rounds after 1 warm-up, x100 rounds; measured, not scaled to %d rows"
                      % (rows, wl, WORKLOADS[wl]["rows"])}
+    if check:
+        # The first round only: from margin 0 both sides take sigmoid(0) = 0.5
+        # exactly; later rounds go through the reference harness's libm exp,
+        # which can differ by an ulp from this library's deterministic one.
+        Xs, ys = gen_rows(wl, 0, rows, device, pin=False)
+        out["reference_parity"] = reference_parity(ref, Xs, ys, params_for(wl), 1, 0.5)
+        del Xs, ys
+    del ref
     model = _full_rows_model(wl, device, (rows, per_round))
     if model:
         out["full_rows_estimate"] = model
@@ -571,7 +581,7 @@ def c2_comparison(xgb, core, device, rounds=100, ref_rounds=3):
         ref = ReferencePath(wl, spec["rows"], device, keep_trees=True)
         ref.round()
         t = float(np.mean([ref.round() for _ in range(ref_rounds)]))
-        out["reference_parity"] = c2_reference_parity(ref, Xh, yh, params, ref_rounds + 1)
+        out["reference_parity"] = reference_parity(ref, Xh, yh, params, ref_rounds + 1, 0.0)
         out.update({"reference_cpu_ms_per_100_rounds": round(t * 1e5, 1), "reference_cpu_cores": cpu_cores(),
                     "reference_cpu_rounds_timed": ref_rounds,
                     "speedup_e2e": round(t * 1e5 / e2e_ms, 1), "speedup_device": round(t * 1e5 / dev_ms, 1),
@@ -580,21 +590,23 @@ def c2_comparison(xgb, core, device, rounds=100, ref_rounds=3):
     return out
 
 
-def c2_reference_parity(ref, Xh, yh, params, rounds):
-    """This library's c2 trees against the reference path's (`ref`, which
-    has just grown `rounds` rounds from margin 0 over all of c2's rows with
-    the reference's own functions): the same rounds through the library's
-    training entry point with base_score 0, compared node for node. A
-    failure here is recorded, never raised: the bench line still prints."""
+def reference_parity(ref, Xh, yh, params, rounds, base_score):
+    """This library's trees against the first `rounds` rounds the reference
+    path `ref` has grown from margin 0 with the reference's own functions
+    over the same rows (Xh, yh): the same rounds through the library's
+    training entry point, with the base_score whose margin is 0, compared
+    node for node. A failure here is recorded, never raised: the bench line
+    still prints."""
     try:
         import product as P
         p = {k: v for k, v in params.items() if k not in ("device", "tree_method", "seed")}
-        trees, _ = P.train(Xh, yh, dict(p, base_score=0.0), rounds)
-        diff = compare_trees(trees, ref.trees)
-        return {"rounds": rounds, "trees": len(trees), "nodes": int(sum(len(t) for t in trees)),
-                "identical": diff is None, "first_difference": diff,
-                "note": "this library's trees (XGBBTrainHost, base_score 0) against the reference's own "
-                        "CPU path over all 262,144 rows, node for node"}
+        trees, _ = P.train(Xh, yh, dict(p, base_score=base_score), rounds)
+        want = ref.trees[:len(trees)]
+        diff = compare_trees(trees, want)
+        return {"rounds": rounds, "rows": int(Xh.shape[0]), "trees": len(trees),
+                "nodes": int(sum(len(t) for t in trees)), "identical": diff is None, "first_difference": diff,
+                "note": "this library's trees (XGBBTrainHost, margin 0 at the start) against the "
+                        "reference's own CPU path on the same rows, node for node"}
     except Exception as e:  # noqa: BLE001 -- recorded in the line instead
         return {"rounds": rounds, "identical": None, "error": "%s: %s" % (type(e).__name__, e)}
 

@@ -132,9 +132,9 @@ def test_launch_count_matches_the_committed_c4_launch_list():
 
 
 @pytest.mark.skipif(not __import__("checkers").have_reference(), reason="reference harness not built")
-def test_tree_comparison_of_the_c2_reference_parity_check():
-    """compare_trees, which the bench's c2 leg uses to hold this library's
-    trees to the reference path's: equal tables give None, across the two
+def test_tree_comparison_of_the_reference_parity_checks():
+    """compare_trees, which the bench's c2 and c4 CPU legs use to hold this
+    library's trees to the reference path's: equal tables give None, across the two
     record layouts (the library's 48-byte records, the reference harness's
     40-byte ones); a changed threshold, leaf bit or node count is named."""
     import checkers as C
@@ -166,3 +166,14 @@ def test_tree_comparison_of_the_c2_reference_parity_check():
     assert bench.compare_trees([changed], want) == "tree 0: leaf"
     assert bench.compare_trees([dev[:-1]], want).startswith("tree 0: ")
     assert bench.compare_trees([], want) == "0 trees against 1"
+
+
+@pytest.mark.skipif(__import__("torch").cuda.is_available(), reason="needs a machine without a GPU")
+def test_reference_parity_failure_is_recorded_not_raised():
+    """Without a GPU the library refuses to train; the check records that in
+    the bench line instead of raising."""
+    class _Ref:
+        trees = []
+    X = np.zeros((10, 3), np.float32)
+    got = bench.reference_parity(_Ref(), X, np.zeros(10, np.float32), bench.params_for("c2"), 4, 0.0)
+    assert got["identical"] is None and "error" in got
