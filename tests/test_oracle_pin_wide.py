@@ -163,3 +163,19 @@ def test_c2_full_size_matches_reference():
     cuts, bins = _same_cuts(X, 256)
     nodes = _boost("reg:squarederror", bins, cuts, y, 1, _tree_params(8, 0.3), 2)
     assert nodes > 800
+
+
+@pytest.mark.parametrize("nan", [0.0, 0.15])
+def test_c0_and_c1_full_size_match_reference(nan):
+    """c0 and c1 at their full size: 100,000 rows of 32 N(0, 1) features, a
+    linear label with noise computed before masking, 15 % NaN for c1;
+    squared error, 256 bins, depth 6, eta 0.3, three rounds."""
+    rng = np.random.default_rng(1337)
+    X = rng.normal(size=(100_000, 32)).astype(np.float32)
+    w = np.random.default_rng(1338).normal(size=32)
+    y = (X @ w + 0.1 * rng.normal(size=len(X))).astype(np.float32)
+    if nan:
+        X[rng.random(X.shape) < nan] = np.nan
+    cuts, bins = _same_cuts(X, 256)
+    nodes = _boost("reg:squarederror", bins, cuts, y, 1, _tree_params(6, 0.3), 3)
+    assert nodes > 300
