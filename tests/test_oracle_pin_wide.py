@@ -86,14 +86,14 @@ def test_c4_width_two_rounds_match_reference():
 
 
 def test_c3_shape_two_rounds_match_reference():
-    """c3's shape at 3k rows: 784 integer-valued features in [0, 255], each
+    """c3's shape at 20k rows: 784 integer-valued features in [0, 255], each
     class's cells below the 80th percentile of its pattern held at 0, the
     rest Poisson around the pattern; 10 classes (one tree per class per
     round), depth 6, 256 bins. A fifth of the labels are redrawn at random:
     with clean labels one split separates each class and the trees stop at
     three nodes; with the noise they grow to a few dozen."""
     rng = np.random.default_rng(4402)
-    rows, cols, K = 3_000, 784, 10
+    rows, cols, K = 20_000, 784, 10
     P = rng.uniform(0, 255, size=(K, cols)).astype(np.float32)
     keep = P >= np.quantile(P, 0.8, axis=1, keepdims=True)
     labels = rng.permutation(np.arange(rows) % K)
